@@ -1,0 +1,319 @@
+#!/usr/bin/env python
+"""Benchmark: Q4_K GEMV achieved HBM GB/s on B200.
+
+Workload: y = W . x with W a Q4_K matrix of N=4096 rows x K=4096 columns
+(65,536 blocks, 9,437,184 bytes), x and y fp32, M=1 -- the single Q4_K GEMV
+of the headline metric, seeded as its definition says (d = fp16(|N(0,1)|*2e-3),
+dmin = fp16(|N(0,1)|*1e-3), scales/mins uniform 0..63, nibbles uniform).
+A step is one GEMV over each of COPIES distinct weight matrices (64 x 9.4 MB
+= 604 MB, more than 4x the 126 MB L2, so every step streams from HBM).  The
+COPIES launches of a step are one CUDA graph; the timed region replays it.
+
+Arms:
+  --impl swq (default): libswq on each GPU.  Under torchrun every rank runs
+      its own stream of GEMVs on its own weights (weak scaling, no data-path
+      collective); the time is the max over ranks.
+  --impl reference: the reference's own CPU code (Compute::matmul_transposed_q,
+      compiled from source into oracle/_ref; the oracle port if that is
+      absent) on all host cores, one Q4_K 4096x4096 GEMV per step.
+
+One JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (str(REPO), str(REPO / "swllm.cpp_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "Q4_K GEMV achieved HBM GB/s (% peak); decode tok/s at 1/2/4/8 B200"
+N_ROWS, K_COLS, M_ROWS = 4096, 4096, 1
+COPIES = 64
+Q4_K = 12
+BLOCK_BYTES = 144
+W_BYTES = N_ROWS * (K_COLS // 256) * BLOCK_BYTES              # 9,437,184
+ALG_BYTES = W_BYTES + 4 * K_COLS * M_ROWS + 4 * N_ROWS * M_ROWS  # 9,469,952 per GEMV
+WORKLOAD = (f"Q4_K GEMV N={N_ROWS} K={K_COLS} M={M_ROWS}, {COPIES} rotating weight copies "
+            f"({COPIES * W_BYTES / 1e6:.0f} MB)")
+# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_kernel<Q4_K,1> launch
+# from ncu (profiles/gemv_q4k_4096x4096.md); None until captured.
+NCU_TRAFFIC_PER_LAUNCH = None
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.err = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+        except Exception as e:  # pragma: no cover
+            self.err = str(e)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        if self.proc is None:
+            return {"unavailable": self.err or "nvidia-smi not started"}
+        rows = [r for r in csv.reader(io.StringIO(self.out or "")) if len(r) >= 9]
+        if not rows:
+            return {"unavailable": "no nvidia-smi samples during the timed region"}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- CPU arm
+def cpu_gemv_timing(seconds: float, max_steps: int | None = None, copies: int = 16) -> dict:
+    """The reference CPU routine on all host cores, one 4096x4096 Q4_K GEMV per
+    step, rotating over `copies` weight matrices (151 MB, beyond the LLC)."""
+    import numpy as np
+
+    import oracle
+    from swq import synth
+
+    cores = oracle.host_cores()
+    if oracle.ref_available():
+        kind = "reference"
+        oracle.ref_set_threads(cores)
+        fn = lambda w, x: oracle.ref_gemv(Q4_K, w, x, N_ROWS, K_COLS)  # noqa: E731
+    else:
+        kind = "port"
+        oracle.set_threads(cores)
+        fn = lambda w, x: oracle.gemv(Q4_K, w, x, N_ROWS, K_COLS, format_order=False)  # noqa: E731
+    ws = [synth.random_blocks(Q4_K, N_ROWS, K_COLS, seed=1000 + i) for i in range(copies)]
+    x = synth.random_activations(1, K_COLS, seed=7)[0]
+    fn(ws[0], x)  # warm-up
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        fn(ws[n % copies], x)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or (max_steps is not None and n >= max_steps):
+            break
+    gbs = n * ALG_BYTES / el / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": f"{n} Q4_K GEMVs N={N_ROWS} K={K_COLS} M=1 over {copies} weight copies, "
+                      f"{el:.1f} s, {cores} OpenMP threads", "seconds": round(el, 2), "steps": n}
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    budget = 60.0  # seconds of CPU work for the whole --steps run
+    r = cpu_gemv_timing(seconds=budget, max_steps=max(1, args.steps))
+    line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": r["steps"], "warmup": args.warmup,
+            "ms_per_step": round(1e3 * r["seconds"] / r["steps"], 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"Q4_K GEMV N={N_ROWS} K={K_COLS} M=1 (reference CPU path)",
+                       "format": "Q4_K", "N": N_ROWS, "K": K_COLS, "M": 1},
+            "cpu_baseline": {"value": r["value"], "unit": "GB/s", "cores": r["cores"], "kind": r["kind"],
+                             "sample": r["sample"]},
+            "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def run_swq(args, rank: int, world: int) -> None:
+    import numpy as np
+    import torch
+
+    import swq
+    from swq import synth
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    # Weights: COPIES distinct seeded matrices per rank, resident in HBM.
+    host_ws = [synth.random_blocks(Q4_K, N_ROWS, K_COLS, seed=10_000 * rank + i) for i in range(COPIES)]
+    d_ws = [torch.from_numpy(w.reshape(-1)).to(dev) for w in host_ws]
+    x_host = synth.random_activations(1, K_COLS, seed=5 + rank)
+    d_x = torch.from_numpy(x_host).to(dev)
+    d_ys = [torch.empty(N_ROWS, dtype=torch.float32, device=dev) for _ in range(COPIES)]
+
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+
+    def step():
+        for i in range(COPIES):
+            swq.gemv(Q4_K, d_ws[i], d_x, d_ys[i], N_ROWS, K_COLS, stream=stream)
+
+    with torch.cuda.stream(stream):
+        step()  # eager warm-up: attributes set, kernels loaded
+    swq.check(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+    stream.synchronize()
+
+    peak, peak_kind = load_peaks()
+    gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    gpu_uuid = gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}"
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_uuid) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    swq.check(stream)
+    if dist:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    launches = args.steps * COPIES
+    total_bytes = launches * ALG_BYTES * world
+    value = total_bytes / (ms * 1e-3) / 1e9
+    per_launch_s = ms * 1e-3 / launches
+    achieved = ALG_BYTES / per_launch_s / 1e9
+
+    # The host-buffer path below must reproduce the device result of the last copy.
+    y_last = d_ys[-1].cpu().numpy()
+
+    # End to end through the host-buffer API (the reference's calling
+    # convention): host x in, host y out, weights resident after first use.
+    e2e_steps = max(1, min(args.steps, 200))
+    comp = swq.Compute(device=local)
+    out = np.zeros(N_ROWS, np.float32)
+    qws = [swq.QuantWeight(w, Q4_K) for w in host_ws]
+    for i in range(COPIES):  # upload once (warm-up)
+        comp.matmul_transposed_q(out, x_host[0], qws[i], N_ROWS, K_COLS)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        for i in range(COPIES):
+            comp.matmul_transposed_q(out, x_host[0], qws[i], N_ROWS, K_COLS)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = e2e_steps * COPIES * ALG_BYTES * world / e2e_s / 1e9
+    comp.close()
+    if not np.allclose(out, y_last, rtol=1e-5, atol=1e-4):
+        raise RuntimeError("host-buffer path disagrees with the device path")
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1:
+            cpu = cpu_gemv_timing(seconds=10.0)
+            cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "format": "Q4_K", "N": N_ROWS, "K": K_COLS, "M": M_ROWS,
+                       "copies": COPIES, "bytes_per_gemv": ALG_BYTES,
+                       "l2": "inputs larger than L2 (rotating weights)",
+                       "arith": "Q4_K nibbles x 16-bit fixed-point x (dp2a, int32), fp32 scales",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                         "kernel": "swq::gemv_kernel<Q4_K,1>", "alg_bytes_per_launch": ALG_BYTES,
+                         "us_per_launch": round(per_launch_s * 1e6, 3)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": COPIES * 4 * K_COLS * M_ROWS,
+                    "d2h_bytes_per_step": COPIES * 4 * N_ROWS * M_ROWS,
+                    "api": "swq_ctx_matmul_transposed_q (host fp32 x/out, resident weights)",
+                    "steps": e2e_steps},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+    del graph
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["swq", "reference"], default="swq")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if args.warmup < 3:
+        log("warm-up raised to 3 steps (minimum)")
+        args.warmup = 3
+    run_swq(args, rank, world)
+
+
+if __name__ == "__main__":
+    main()

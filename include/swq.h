@@ -1,0 +1,145 @@
+/*
+ * swq.h -- C ABI of libswq, the sm_100a (B200) implementation of swllm.cpp's
+ * quantized-weight matmul path: GGUF block dequantization fused into GEMV
+ * (decode) and GEMM (prefill), for Q4_0, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K.
+ *
+ * Plain C: pointers, sizes and a stream handle.  Device pointers are CUDA
+ * device (or managed) memory; every call is asynchronous on `stream` and
+ * returns once the work is enqueued.  The caller owns every buffer.  Weights
+ * are the GGUF blocks exactly as stored in the file (src/gguf.h:60-118 sizes,
+ * src/tensor.h:136-432 layouts): a matrix W[N x K] is N rows of K/QK
+ * consecutive blocks, GGUF dims[0] = K, dims[1] = N (src/model.h:729-758).
+ *
+ * Type ids are the GGMLType values of src/gguf.h:18-40.
+ *
+ * Numerics (checked by the tests against the reference's own CPU code):
+ *   - swq_dequant is bit-exact with the reference's dequantize().
+ *   - swq_gemv / swq_gemm are within 1e-3 relative L2 of the reference's
+ *     fp32 result on the same inputs.
+ */
+#ifndef SWQ_H
+#define SWQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st* swq_stream_t;
+
+typedef enum swq_status {
+    SWQ_OK = 0,
+    SWQ_ERR_BAD_TYPE = 1,    /* type id not on this path */
+    SWQ_ERR_BAD_SHAPE = 2,   /* K % QK != 0, negative sizes, size limits */
+    SWQ_ERR_NULL_PTR = 3,    /* a required pointer is NULL */
+    SWQ_ERR_CUDA = 4,        /* a CUDA runtime call failed (see swq_last_error) */
+    SWQ_ERR_TIMEOUT = 5,     /* a bounded device-side wait gave up */
+    SWQ_ERR_UNSUPPORTED = 6, /* no sm_100 device, or option value not supported */
+    SWQ_ERR_BAD_ARG = 7      /* any other invalid argument */
+} swq_status;
+
+/* GGMLType ids on this path (src/gguf.h:18-40). */
+enum {
+    SWQ_TYPE_Q4_0 = 2,
+    SWQ_TYPE_Q8_0 = 8,
+    SWQ_TYPE_Q2_K = 10,
+    SWQ_TYPE_Q3_K = 11,
+    SWQ_TYPE_Q4_K = 12,
+    SWQ_TYPE_Q5_K = 13,
+    SWQ_TYPE_Q6_K = 14
+};
+
+/* Human-readable name of a status code (static storage). */
+const char* swq_status_string(swq_status s);
+
+/* Detail of the last error raised on the calling host thread ("" if none). */
+const char* swq_last_error(void);
+
+/* Bytes per block and elements per block.  Replaces ggml_type_size /
+ * ggml_block_size (src/gguf.h:60-118) for the types on this path; 0 for any
+ * other type. */
+size_t swq_type_size(int ggml_type);
+size_t swq_block_size(int ggml_type);
+
+/* Dequantize n elements of GGUF blocks to fp32, bit-exact with the reference.
+ * Replaces dequantize(const void* src, float* dst, int64_t n, GGMLType)
+ * (src/tensor.h:451).  As there, n / QK whole blocks are written and a tail of
+ * n % QK elements is left untouched; n == 0 is a no-op. */
+swq_status swq_dequant(int ggml_type, const void* blocks, float* out, int64_t n,
+                       swq_stream_t stream);
+
+/* y[N] = W[N x K] . x[K], fp32 in and out.  Replaces the per-type CPU branch
+ * and the host-dequantize CUDA branch of Compute::matmul_transposed_q
+ * (src/tensor.h:1212-1278) with one fused kernel on device-resident blocks.
+ * K must be a multiple of the block size (32 or 256). */
+swq_status swq_gemv(int ggml_type, const void* W, const float* x, float* y,
+                    int N, int K, swq_stream_t stream);
+
+/* Y[M x N] = X[M x K] . W[N x K]^T, row-major fp32 X and Y.  The reference has
+ * no batched quantized path: its prefill calls Compute::matmul_transposed_q
+ * once per token (src/main.cpp:284-287), so this equals M such calls.  Small
+ * M runs the fused GEMV kernel; larger M the tensor-core GEMM. */
+swq_status swq_gemm(int ggml_type, const void* W, const float* X, float* Y,
+                    int M, int N, int K, swq_stream_t stream);
+
+/* Options (process-wide). */
+enum {
+    /* 1: Q2_K uses the activation order of the reference's fused CPU routine
+     * cpu_matmul_transposed_q2_k (src/tensor.h:935-945), which reads
+     * x[n + l] / x[n + l + 16] for all four 2-bit planes.  0 (default): Q2_K
+     * uses the element order of dequantize_q2_k (src/tensor.h:232-265), which
+     * is the GGUF format order and what the reference's CUDA backend computes
+     * (host dequantize, then SGEMM, src/tensor.h:1219-1223). */
+    SWQ_OPT_Q2K_REFERENCE_CPU_ORDER = 1,
+    /* 1 (default): the GEMV kernel starts streaming weight blocks before the
+     * previous kernel on the stream has finished (programmatic dependent
+     * launch); weights must then not be written by the immediately preceding
+     * kernel.  Activations are always read after that kernel completes.
+     * 0: every read waits for the preceding kernel. */
+    SWQ_OPT_EARLY_WEIGHT_PREFETCH = 2,
+    /* Largest M served by the fused GEMV kernel; larger M use the GEMM. */
+    SWQ_OPT_GEMV_MAX_M = 3
+};
+swq_status swq_set_option(int option, int value);
+int swq_get_option(int option);
+
+/* Synchronize `stream`, then read and clear the device-side status word that
+ * bounded waits set on timeout.  Returns SWQ_ERR_TIMEOUT if any kernel on
+ * this device gave up a wait since the last check, SWQ_ERR_CUDA if the
+ * synchronize failed, else SWQ_OK. */
+swq_status swq_check(swq_stream_t stream);
+
+/* ---- Host-buffer entry point (the reference's calling convention) --------
+ *
+ * Mirrors Compute::matmul_transposed_q(out, x, QuantWeight{data,type}, N, K)
+ * (src/tensor.h:1212) with host fp32 `out`/`x` and a host pointer to the GGUF
+ * blocks, as Model::forward calls it (src/model.h:284-539).  The blocks are
+ * uploaded to the device once per (pointer, type, N, K) and stay resident,
+ * like the reference's GPUWeightCache keyed by host pointer
+ * (src/cuda_kernels.cu:88-127), but the key includes the shape so that a
+ * reused host address of a different matrix never aliases.  Blocks must stay
+ * unchanged while cached; swq_ctx_evict drops one entry.  Synchronous: returns
+ * when `out` holds the result. */
+typedef struct swq_ctx* swq_ctx_t;
+swq_status swq_ctx_create(int device, swq_ctx_t* ctx);
+swq_status swq_ctx_destroy(swq_ctx_t ctx);
+swq_status swq_ctx_matmul_transposed_q(swq_ctx_t ctx, float* out, const float* x,
+                                       const void* w_host, int ggml_type, int N, int K);
+/* Same for M activation rows (X: M x K, Y: M x N, host, row-major). */
+swq_status swq_ctx_matmul_q_batched(swq_ctx_t ctx, float* Y, const float* X,
+                                    const void* w_host, int ggml_type, int M, int N, int K);
+/* dequantize() with host src/dst (src/tensor.h:451). */
+swq_status swq_ctx_dequantize(swq_ctx_t ctx, const void* src_host, float* dst_host,
+                              int64_t n, int ggml_type);
+swq_status swq_ctx_evict(swq_ctx_t ctx, const void* w_host);
+/* Bytes of weight blocks currently resident for this context. */
+size_t swq_ctx_resident_bytes(swq_ctx_t ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SWQ_H */

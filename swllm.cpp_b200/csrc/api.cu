@@ -1,0 +1,437 @@
+// api.cu -- the extern "C" boundary of libswq (declared in include/swq.h).
+//
+// Argument checks, per-device properties, options, status words and the
+// host-buffer context.  All compute is in the kernels (gemv.cu, dequant.cu,
+// gemm_tc.cu); nothing here computes on the CPU.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/swq.h"
+#include "gemm_tc.h"
+#include "gemv.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+std::atomic<int> g_opt_q2k_refcpu{0};
+std::atomic<int> g_opt_early_prefetch{1};
+std::atomic<int> g_opt_gemv_max_m{8};
+
+swq_status fail(swq_status s, const std::string& msg) {
+    g_last_error = msg;
+    return s;
+}
+
+swq_status cuda_fail(cudaError_t e, const char* where) {
+    g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+    return SWQ_ERR_CUDA;
+}
+
+struct TypeInfo {
+    int qk, bb;
+};
+
+bool type_info(int t, TypeInfo* ti) {
+    switch (t) {
+        case SWQ_TYPE_Q4_0: *ti = {32, 18}; return true;
+        case SWQ_TYPE_Q8_0: *ti = {32, 34}; return true;
+        case SWQ_TYPE_Q2_K: *ti = {256, 84}; return true;
+        case SWQ_TYPE_Q3_K: *ti = {256, 110}; return true;
+        case SWQ_TYPE_Q4_K: *ti = {256, 144}; return true;
+        case SWQ_TYPE_Q5_K: *ti = {256, 176}; return true;
+        case SWQ_TYPE_Q6_K: *ti = {256, 210}; return true;
+        default: return false;
+    }
+}
+
+std::mutex g_dev_mu;
+std::map<int, swq::DeviceInfo> g_dev;
+
+swq_status current_device(swq::DeviceInfo* out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    auto it = g_dev.find(dev);
+    if (it == g_dev.end()) {
+        swq::DeviceInfo d;
+        d.device = dev;
+        if ((e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+            (e = cudaDeviceGetAttribute(&d.smem_per_block_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) !=
+                cudaSuccess ||
+            (e = cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev)) !=
+                cudaSuccess ||
+            (e = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+            (e = cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute");
+        it = g_dev.emplace(dev, d).first;
+    }
+    *out = it->second;
+    if (out->cc_major != 10)
+        return fail(SWQ_ERR_UNSUPPORTED, "libswq is built for sm_100a (B200); device " + std::to_string(dev) +
+                                             " is sm_" + std::to_string(out->cc_major) +
+                                             std::to_string(out->cc_minor));
+    return SWQ_OK;
+}
+
+// Largest activation-row group the GEMV kernel takes for this K: the per-CTA
+// activation copy must leave room for at least three weight stages.
+int gemv_group_rows(int type, int K, int max_m) {
+    const size_t budget = 120 * 1024;
+    for (int g : {8, 4, 2, 1}) {
+        if (g > max_m && g != 1) continue;
+        if (swq::gemv_smem_x_bytes(type, g, K) <= budget) return g;
+    }
+    return 0;
+}
+
+swq_status check_gemm_args(int type, const void* W, const float* X, const float* Y, int M, int N, int K,
+                           TypeInfo* ti) {
+    if (!type_info(type, ti)) return fail(SWQ_ERR_BAD_TYPE, "type " + std::to_string(type) + " is not on this path");
+    if (M < 0 || N < 0 || K < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative size");
+    if (K % ti->qk != 0)
+        return fail(SWQ_ERR_BAD_SHAPE, "K=" + std::to_string(K) + " is not a multiple of " + std::to_string(ti->qk));
+    if (M == 0 || N == 0 || K == 0) return SWQ_OK;
+    if (!W || !X || !Y) return fail(SWQ_ERR_NULL_PTR, "null W, X or Y");
+    return SWQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* swq_status_string(swq_status s) {
+    switch (s) {
+        case SWQ_OK: return "ok";
+        case SWQ_ERR_BAD_TYPE: return "bad type";
+        case SWQ_ERR_BAD_SHAPE: return "bad shape";
+        case SWQ_ERR_NULL_PTR: return "null pointer";
+        case SWQ_ERR_CUDA: return "cuda error";
+        case SWQ_ERR_TIMEOUT: return "device wait timed out";
+        case SWQ_ERR_UNSUPPORTED: return "unsupported";
+        case SWQ_ERR_BAD_ARG: return "bad argument";
+    }
+    return "unknown status";
+}
+
+const char* swq_last_error(void) { return g_last_error.c_str(); }
+
+size_t swq_type_size(int t) {
+    TypeInfo ti;
+    return type_info(t, &ti) ? static_cast<size_t>(ti.bb) : 0;
+}
+
+size_t swq_block_size(int t) {
+    TypeInfo ti;
+    return type_info(t, &ti) ? static_cast<size_t>(ti.qk) : 0;
+}
+
+swq_status swq_set_option(int option, int value) {
+    switch (option) {
+        case SWQ_OPT_Q2K_REFERENCE_CPU_ORDER:
+            if (value != 0 && value != 1) return fail(SWQ_ERR_BAD_ARG, "option value must be 0 or 1");
+            g_opt_q2k_refcpu = value;
+            return SWQ_OK;
+        case SWQ_OPT_EARLY_WEIGHT_PREFETCH:
+            if (value != 0 && value != 1) return fail(SWQ_ERR_BAD_ARG, "option value must be 0 or 1");
+            g_opt_early_prefetch = value;
+            return SWQ_OK;
+        case SWQ_OPT_GEMV_MAX_M:
+            if (value < 0 || value > 8) return fail(SWQ_ERR_BAD_ARG, "GEMV max M must be in 0..8");
+            g_opt_gemv_max_m = value;
+            return SWQ_OK;
+        default:
+            return fail(SWQ_ERR_BAD_ARG, "unknown option " + std::to_string(option));
+    }
+}
+
+int swq_get_option(int option) {
+    switch (option) {
+        case SWQ_OPT_Q2K_REFERENCE_CPU_ORDER: return g_opt_q2k_refcpu;
+        case SWQ_OPT_EARLY_WEIGHT_PREFETCH: return g_opt_early_prefetch;
+        case SWQ_OPT_GEMV_MAX_M: return g_opt_gemv_max_m;
+        default: return -1;
+    }
+}
+
+swq_status swq_dequant(int type, const void* blocks, float* out, int64_t n, swq_stream_t stream) {
+    TypeInfo ti;
+    if (!type_info(type, &ti)) return fail(SWQ_ERR_BAD_TYPE, "type " + std::to_string(type) + " is not on this path");
+    if (n < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative n");
+    const int64_t nblocks = n / ti.qk;
+    if (nblocks == 0) return SWQ_OK;
+    if (!blocks || !out) return fail(SWQ_ERR_NULL_PTR, "null blocks or out");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    cudaError_t e = swq::dequant_launch(type, blocks, out, nblocks, dev.num_sms,
+                                        reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "dequant launch");
+    return SWQ_OK;
+}
+
+swq_status swq_gemm(int type, const void* W, const float* X, float* Y, int M, int N, int K,
+                    swq_stream_t stream) {
+    TypeInfo ti;
+    swq_status st = check_gemm_args(type, W, X, Y, M, N, K, &ti);
+    if (st != SWQ_OK || M == 0 || N == 0) return st;
+    swq::DeviceInfo dev;
+    if ((st = current_device(&dev)) != SWQ_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (K == 0) {
+        cudaError_t e = cudaMemsetAsync(Y, 0, sizeof(float) * static_cast<size_t>(M) * N, s);
+        return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
+    }
+    const int max_m = g_opt_gemv_max_m;
+    if (M > max_m && swq::gemm_tc_supported(type, M, N, K)) {
+        cudaError_t e = swq::gemm_tc_launch(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms, s);
+        if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
+        return SWQ_OK;
+    }
+    const int g = gemv_group_rows(type, K, std::max(1, max_m));
+    if (g == 0) return fail(SWQ_ERR_BAD_SHAPE, "K=" + std::to_string(K) + " exceeds the GEMV activation buffer");
+    for (int m0 = 0; m0 < M; m0 += g) {
+        swq::GemvLaunch L{};
+        L.type = type;
+        L.W = W;
+        L.X = X + static_cast<size_t>(m0) * K;
+        L.Y = Y + static_cast<size_t>(m0) * N;
+        L.M = std::min(g, M - m0);
+        L.N = N;
+        L.K = K;
+        L.refcpu = g_opt_q2k_refcpu;
+        L.early = g_opt_early_prefetch;
+        L.num_sms = dev.num_sms;
+        L.smem_per_block_optin = dev.smem_per_block_optin;
+        L.smem_per_sm = dev.smem_per_sm;
+        cudaError_t e = swq::gemv_launch(L, s);
+        if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
+    }
+    return SWQ_OK;
+}
+
+swq_status swq_gemv(int type, const void* W, const float* x, float* y, int N, int K, swq_stream_t stream) {
+    return swq_gemm(type, W, x, y, 1, N, K, stream);
+}
+
+swq_status swq_check(swq_stream_t stream) {
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    unsigned a = 0, b = 0, c = 0;
+    if ((e = swq::status_fetch_gemv(&a, s)) != cudaSuccess ||
+        (e = swq::status_fetch_dequant(&b, s)) != cudaSuccess ||
+        (e = swq::status_fetch_gemm_tc(&c, s)) != cudaSuccess)
+        return cuda_fail(e, "status fetch");
+    if (a | b | c) {
+        char buf[96];
+        std::snprintf(buf, sizeof(buf), "device wait timeout (gemv=%#x dequant=%#x gemm=%#x)", a, b, c);
+        return fail(SWQ_ERR_TIMEOUT, buf);
+    }
+    return SWQ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Host-buffer context: the reference's calling convention.
+// ---------------------------------------------------------------------------
+
+struct swq_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;
+    struct Entry {
+        void* dev = nullptr;
+        size_t bytes = 0;
+        int type = 0, N = 0, K = 0;
+    };
+    std::map<const void*, std::vector<Entry>> cache;
+    size_t resident = 0;
+    // device activation/output buffers and pinned staging, grown on demand
+    float* d_x = nullptr;
+    float* d_y = nullptr;
+    size_t cap_x = 0, cap_y = 0;
+    float* h_x = nullptr;
+    float* h_y = nullptr;
+    size_t hcap_x = 0, hcap_y = 0;
+};
+
+namespace {
+
+swq_status ensure_dev(float** p, size_t* cap, size_t need) {
+    if (*cap >= need) return SWQ_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), need);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+    *cap = need;
+    return SWQ_OK;
+}
+
+swq_status ensure_host(float** p, size_t* cap, size_t need) {
+    if (*cap >= need) return SWQ_OK;
+    if (*p) cudaFreeHost(*p);
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMallocHost(reinterpret_cast<void**>(p), need);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocHost");
+    *cap = need;
+    return SWQ_OK;
+}
+
+swq_status resident_weight(swq_ctx* c, const void* w, int type, int N, int K, size_t bytes, const void** dev) {
+    auto& v = c->cache[w];
+    for (auto& en : v) {
+        if (en.type == type && en.N == N && en.K == K) {
+            *dev = en.dev;
+            return SWQ_OK;
+        }
+    }
+    swq_ctx::Entry en;
+    cudaError_t e = cudaMalloc(&en.dev, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(weights)");
+    e = cudaMemcpy(en.dev, w, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(en.dev);
+        return cuda_fail(e, "cudaMemcpy(weights)");
+    }
+    en.bytes = bytes;
+    en.type = type;
+    en.N = N;
+    en.K = K;
+    v.push_back(en);
+    c->resident += bytes;
+    *dev = en.dev;
+    return SWQ_OK;
+}
+
+}  // namespace
+
+swq_status swq_ctx_create(int device, swq_ctx_t* out) {
+    if (!out) return fail(SWQ_ERR_NULL_PTR, "null ctx out");
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    auto* c = new swq_ctx();
+    c->device = device;
+    e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "cudaStreamCreate");
+    }
+    *out = c;
+    return SWQ_OK;
+}
+
+swq_status swq_ctx_destroy(swq_ctx_t c) {
+    if (!c) return SWQ_OK;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    for (auto& kv : c->cache)
+        for (auto& en : kv.second) cudaFree(en.dev);
+    if (c->d_x) cudaFree(c->d_x);
+    if (c->d_y) cudaFree(c->d_y);
+    if (c->h_x) cudaFreeHost(c->h_x);
+    if (c->h_y) cudaFreeHost(c->h_y);
+    cudaStreamDestroy(c->stream);
+    delete c;
+    return SWQ_OK;
+}
+
+swq_status swq_ctx_matmul_q_batched(swq_ctx_t c, float* Y, const float* X, const void* w, int type, int M, int N,
+                                    int K) {
+    if (!c) return fail(SWQ_ERR_NULL_PTR, "null ctx");
+    TypeInfo ti;
+    swq_status st = check_gemm_args(type, w, X, Y, M, N, K, &ti);
+    if (st != SWQ_OK || M == 0 || N == 0) return st;
+    std::lock_guard<std::mutex> lk(c->mu);
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    const size_t wbytes = static_cast<size_t>(N) * (K / ti.qk) * ti.bb;
+    const void* dW = nullptr;
+    if (K > 0 && (st = resident_weight(c, w, type, N, K, wbytes, &dW)) != SWQ_OK) return st;
+    const size_t xb = sizeof(float) * static_cast<size_t>(M) * K, yb = sizeof(float) * static_cast<size_t>(M) * N;
+    if ((st = ensure_dev(&c->d_x, &c->cap_x, std::max<size_t>(xb, 16))) != SWQ_OK ||
+        (st = ensure_dev(&c->d_y, &c->cap_y, yb)) != SWQ_OK ||
+        (st = ensure_host(&c->h_x, &c->hcap_x, std::max<size_t>(xb, 16))) != SWQ_OK ||
+        (st = ensure_host(&c->h_y, &c->hcap_y, yb)) != SWQ_OK)
+        return st;
+    if (xb) std::memcpy(c->h_x, X, xb);
+    if (xb && (e = cudaMemcpyAsync(c->d_x, c->h_x, xb, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
+        return cuda_fail(e, "H2D x");
+    st = swq_gemm(type, dW ? dW : c->d_x, c->d_x, c->d_y, M, N, K, reinterpret_cast<swq_stream_t>(c->stream));
+    if (st != SWQ_OK) return st;
+    if ((e = cudaMemcpyAsync(c->h_y, c->d_y, yb, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
+        return cuda_fail(e, "D2H y");
+    if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    std::memcpy(Y, c->h_y, yb);
+    return SWQ_OK;
+}
+
+swq_status swq_ctx_matmul_transposed_q(swq_ctx_t c, float* out, const float* x, const void* w, int type, int N,
+                                       int K) {
+    return swq_ctx_matmul_q_batched(c, out, x, w, type, 1, N, K);
+}
+
+swq_status swq_ctx_dequantize(swq_ctx_t c, const void* src, float* dst, int64_t n, int type) {
+    if (!c) return fail(SWQ_ERR_NULL_PTR, "null ctx");
+    TypeInfo ti;
+    if (!type_info(type, &ti)) return fail(SWQ_ERR_BAD_TYPE, "type " + std::to_string(type) + " is not on this path");
+    if (n < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative n");
+    const int64_t nblocks = n / ti.qk;
+    if (nblocks == 0) return SWQ_OK;
+    if (!src || !dst) return fail(SWQ_ERR_NULL_PTR, "null src or dst");
+    std::lock_guard<std::mutex> lk(c->mu);
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    const size_t inb = static_cast<size_t>(nblocks) * ti.bb;
+    const size_t outb = sizeof(float) * static_cast<size_t>(nblocks) * ti.qk;
+    void* d_in = nullptr;
+    float* d_out = nullptr;
+    if ((e = cudaMalloc(&d_in, inb)) != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+    if ((e = cudaMalloc(reinterpret_cast<void**>(&d_out), outb)) != cudaSuccess) {
+        cudaFree(d_in);
+        return cuda_fail(e, "cudaMalloc");
+    }
+    swq_status st = SWQ_OK;
+    if ((e = cudaMemcpyAsync(d_in, src, inb, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
+        st = cuda_fail(e, "H2D blocks");
+    if (st == SWQ_OK) st = swq_dequant(type, d_in, d_out, n, reinterpret_cast<swq_stream_t>(c->stream));
+    if (st == SWQ_OK && (e = cudaMemcpyAsync(dst, d_out, outb, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
+        st = cuda_fail(e, "D2H out");
+    if (st == SWQ_OK && (e = cudaStreamSynchronize(c->stream)) != cudaSuccess) st = cuda_fail(e, "sync");
+    cudaFree(d_in);
+    cudaFree(d_out);
+    return st;
+}
+
+swq_status swq_ctx_evict(swq_ctx_t c, const void* w) {
+    if (!c) return fail(SWQ_ERR_NULL_PTR, "null ctx");
+    std::lock_guard<std::mutex> lk(c->mu);
+    auto it = c->cache.find(w);
+    if (it == c->cache.end()) return SWQ_OK;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    for (auto& en : it->second) {
+        cudaFree(en.dev);
+        c->resident -= en.bytes;
+    }
+    c->cache.erase(it);
+    return SWQ_OK;
+}
+
+size_t swq_ctx_resident_bytes(swq_ctx_t c) { return c ? c->resident : 0; }
+
+}  // extern "C"

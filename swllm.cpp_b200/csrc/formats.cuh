@@ -1,0 +1,428 @@
+// formats.cuh -- GGUF block formats on the quantized-weight path.
+//
+// For each format two views of the same block layout:
+//
+//  * dq_elem(): one element exactly as the reference dequantizer computes it
+//    (src/tensor.h:139-432), fp32 with explicit round-to-nearest mul/sub so no
+//    FMA contraction changes a bit.  Used by swq_dequant (bit-exact).
+//
+//  * unit decode for the fused GEMV: a block is split into UPB "units" of UE
+//    elements (one lane's work).  decode() turns a unit's quant bits into
+//    UE/4 words of four small non-negative integers (bytes), in "unit order";
+//    the activation row is re-laid out in the same unit order as 16-bit
+//    fixed-point values, so the dot product is a chain of dp2a instructions.
+//    Each unit has PARTS parts of PE elements that share one weight scale and
+//    one activation block scale:
+//        contribution = xs * (wd * (S - IOFF * I) - wm * I)
+//    where S = sum(q * X) over the part, I = sum(X) over the part, wd/wm the
+//    part's weight scale/min and IOFF the format's integer zero point.
+#pragma once
+
+#include "swq_device.cuh"
+
+namespace swq {
+
+// ---- helpers for the K-quant 6-bit scale field --------------------------------
+
+// get_scale_min_k4 (src/tensor.h:218-227) on the 12-byte field held as three
+// little-endian words s0 = bytes 0-3, s1 = bytes 4-7, s2 = bytes 8-11.
+__device__ __forceinline__ void scale_min_k4(int j, uint32_t s0, uint32_t s1, uint32_t s2,
+                                             uint32_t& sc, uint32_t& m) {
+    if (j < 4) {
+        sc = byte_of(s0, j) & 63u;
+        m = byte_of(s1, j) & 63u;
+    } else {
+        const int jj = j - 4;
+        sc = (byte_of(s2, jj) & 0x0Fu) | ((byte_of(s0, jj) >> 6) << 4);
+        m = (byte_of(s2, jj) >> 4) | ((byte_of(s1, jj) >> 6) << 4);
+    }
+}
+
+// Q3_K signed scales, src/tensor.h:286-304: word w (0..3) of the unpacked
+// 16 scales, each word reduced by 0x20202020 as a whole (byte borrows kept).
+__device__ __forceinline__ uint32_t q3k_scale_word(int w, uint32_t t0, uint32_t t1, uint32_t t2) {
+    const uint32_t km = 0x03030303u;
+    const uint32_t ta = (w < 2) ? t0 : t1;
+    const int sh_lo = (w & 1) ? 2 : 0;
+    const int sh_hi = 2 * w;
+    return ((((ta >> sh_lo) & km) | (((t2 >> sh_hi) & km) << 4))) - 0x20202020u;
+}
+
+__device__ __forceinline__ uint32_t ldg_u8(const uint8_t* p) { return __ldg(p); }
+__device__ __forceinline__ uint32_t ldg_u16(const uint8_t* p) {
+    return static_cast<uint32_t>(__ldg(p)) | (static_cast<uint32_t>(__ldg(p + 1)) << 8);
+}
+
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+
+template <int T>
+struct Fmt;
+
+// =============================================================================
+// Q4_0: 32 elements, 18 bytes: d (f16) @0, 16 nibble bytes @2.  src/tensor.h:139
+// =============================================================================
+template <>
+struct Fmt<Q4_0> {
+    static constexpr int QK = 32, BB = 18, UPB = 1, UE = 32, PARTS = 1, PE = 32, IOFF = 8;
+    static constexpr bool MIN = false;
+
+    __device__ static float dq_elem(const uint8_t* b, int k) {
+        const float d = half_bits_to_float(ldg_u16(b));
+        const uint32_t v = ldg_u8(b + 2 + (k & 15));
+        const int q = (k < 16) ? static_cast<int>(v & 0x0F) : static_cast<int>(v >> 4);
+        return fmul(static_cast<float>(q - 8), d);
+    }
+    // unit element e <-> block element k: identity (low nibbles 0..15, high 16..31)
+    __host__ __device__ static int xdests(int k, bool, int* c, int* e) { c[0] = 0; e[0] = k; return 1; }
+    __host__ __device__ static int part_xblock(int, int, bool) { return 0; }
+    __host__ __device__ static int part_half(int, int, bool) { return 0; }
+
+    __device__ static void decode(const uint8_t* b, int, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
+                                  float (&wm)[PARTS]) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = lds_u32_a2(b + 2 + 4 * i);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            q[i] = w[i] & 0x0F0F0F0Fu;
+            q[4 + i] = (w[i] >> 4) & 0x0F0F0F0Fu;
+        }
+        wd[0] = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b));
+        wm[0] = 0.f;
+    }
+};
+
+// =============================================================================
+// Q8_0: 32 elements, 34 bytes: d @0, 32 x int8 @2.  src/tensor.h:157
+// =============================================================================
+template <>
+struct Fmt<Q8_0> {
+    static constexpr int QK = 32, BB = 34, UPB = 1, UE = 32, PARTS = 1, PE = 32, IOFF = 0;
+    static constexpr bool MIN = false;
+
+    __device__ static float dq_elem(const uint8_t* b, int k) {
+        const float d = half_bits_to_float(ldg_u16(b));
+        const int q = static_cast<int8_t>(ldg_u8(b + 2 + k));
+        return fmul(static_cast<float>(q), d);
+    }
+    __host__ __device__ static int xdests(int k, bool, int* c, int* e) { c[0] = 0; e[0] = k; return 1; }
+    __host__ __device__ static int part_xblock(int, int, bool) { return 0; }
+    __host__ __device__ static int part_half(int, int, bool) { return 0; }
+
+    __device__ static void decode(const uint8_t* b, int, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
+                                  float (&wm)[PARTS]) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = lds_u32_a2(b + 2 + 4 * i);  // signed bytes
+        wd[0] = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b));
+        wm[0] = 0.f;
+    }
+};
+
+// =============================================================================
+// Q2_K: 256 elements, 84 bytes: scales[16] @0, qs[64] @16, d @80, dmin @82.
+// src/tensor.h:232-265.  Element 128n + 32j + 16h + l <- (qs[32n + 16h + l] >> 2j) & 3,
+// scale byte sc[8n + 2j + h] (low nibble: scale, high nibble: min).
+// Unit c = (n = c>>1, h = c&1): 64 elements, part j = the 16 elements of plane j.
+// =============================================================================
+template <>
+struct Fmt<Q2_K> {
+    static constexpr int QK = 256, BB = 84, UPB = 4, UE = 64, PARTS = 4, PE = 16, IOFF = 0;
+    static constexpr bool MIN = true;
+
+    __device__ static float dq_elem(const uint8_t* b, int k) {
+        const int n = k >> 7, r = k & 127, j = r >> 5, h = (r >> 4) & 1, l = r & 15;
+        const float d = half_bits_to_float(ldg_u16(b + 80));
+        const float dmin = half_bits_to_float(ldg_u16(b + 82));
+        const uint32_t s = ldg_u8(b + 8 * n + 2 * j + h);
+        const float dl = fmul(d, static_cast<float>(s & 0xF));
+        const float ml = fmul(dmin, static_cast<float>(s >> 4));
+        const uint32_t v = (ldg_u8(b + 16 + 32 * n + 16 * h + l) >> (2 * j)) & 3u;
+        return fsub(fmul(dl, static_cast<float>(v)), ml);
+    }
+    // Format order: unit element e = 16j + l of unit c is block element
+    // 128n + 32j + 16h + l.  Reference-CPU order (cpu_matmul_transposed_q2_k,
+    // src/tensor.h:935-945): it is block element 128n + 16h + l for every j, so
+    // elements 128n + 32..127 are never used and the others feed four planes.
+    __host__ __device__ static int xdests(int k, bool refcpu, int* c, int* e) {
+        const int n = k >> 7, r = k & 127;
+        if (!refcpu) {
+            const int j = r >> 5, h = (r >> 4) & 1, l = r & 15;
+            c[0] = 2 * n + h;
+            e[0] = 16 * j + l;
+            return 1;
+        }
+        if (r >= 32) return 0;
+        const int h = r >> 4, l = r & 15;
+        for (int j = 0; j < 4; ++j) { c[j] = 2 * n + h; e[j] = 16 * j + l; }
+        return 4;
+    }
+    __host__ __device__ static int part_xblock(int c, int j, bool refcpu) {
+        return 4 * (c >> 1) + (refcpu ? 0 : j);
+    }
+    __host__ __device__ static int part_half(int c, int j, bool refcpu) {
+        return 8 * (c >> 1) + (refcpu ? 0 : 2 * j) + (c & 1);
+    }
+
+    __device__ static void decode(const uint8_t* b, int c, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
+                                  float (&wm)[PARTS]) {
+        const int n = c >> 1, h = c & 1;
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = lds_u32_a4(b + 16 + 32 * n + 16 * h + 4 * i);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) q[4 * j + i] = (w[i] >> (2 * j)) & 0x03030303u;
+        const uint32_t s_lo = lds_u32_a4(b + 8 * n);      // sc[8n .. 8n+3]
+        const uint32_t s_hi = lds_u32_a4(b + 8 * n + 4);  // sc[8n+4 .. 8n+7]
+        const uint32_t dd = lds_u32_a4(b + 80);
+        const float d = half_bits_to_float(dd & 0xFFFFu);
+        const float dmin = half_bits_to_float(dd >> 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t s = byte_of(j < 2 ? s_lo : s_hi, 2 * (j & 1) + h);
+            wd[j] = d * static_cast<float>(s & 0xF);
+            wm[j] = dmin * static_cast<float>(s >> 4);
+        }
+    }
+};
+
+// =============================================================================
+// Q3_K: 256 elements, 110 bytes: hmask[32] @0, qs[64] @32, scales[12] @96, d @108.
+// src/tensor.h:269-326.  Element 128n + 32j + 16h + l:
+//   v = ((qs[32n + 16h + l] >> 2j) & 3) - (hmask[16h + l] bit (4n + j) ? 0 : 4),
+//   scale = scales_i8[8n + 2j + h].
+// =============================================================================
+template <>
+struct Fmt<Q3_K> {
+    static constexpr int QK = 256, BB = 110, UPB = 4, UE = 64, PARTS = 4, PE = 16, IOFF = 4;
+    static constexpr bool MIN = false;
+
+    __device__ static float dq_elem(const uint8_t* b, int k) {
+        const int n = k >> 7, r = k & 127, j = r >> 5, h = (r >> 4) & 1, l = r & 15;
+        const float d = half_bits_to_float(ldg_u16(b + 108));
+        uint32_t t[3];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+            t[i] = ldg_u16(b + 96 + 4 * i) | (ldg_u16(b + 98 + 4 * i) << 16);
+        const int idx = 8 * n + 2 * j + h;
+        const uint32_t sw = q3k_scale_word(idx >> 2, t[0], t[1], t[2]);
+        const int sc = static_cast<int8_t>(byte_of(sw, idx & 3));
+        const float dl = fmul(d, static_cast<float>(sc));
+        const int q2 = static_cast<int>((ldg_u8(b + 32 + 32 * n + 16 * h + l) >> (2 * j)) & 3u);
+        const int hb = (ldg_u8(b + 16 * h + l) >> (4 * n + j)) & 1;
+        return fmul(dl, static_cast<float>(q2 - (hb ? 0 : 4)));
+    }
+    __host__ __device__ static int xdests(int k, bool, int* c, int* e) {
+        const int n = k >> 7, r = k & 127, j = r >> 5, h = (r >> 4) & 1, l = r & 15;
+        c[0] = 2 * n + h;
+        e[0] = 16 * j + l;
+        return 1;
+    }
+    __host__ __device__ static int part_xblock(int c, int j, bool) { return 4 * (c >> 1) + j; }
+    __host__ __device__ static int part_half(int c, int j, bool) { return 8 * (c >> 1) + 2 * j + (c & 1); }
+
+    __device__ static void decode(const uint8_t* b, int c, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
+                                  float (&wm)[PARTS]) {
+        const int n = c >> 1, h = c & 1;
+        uint32_t w[4], hm[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w[i] = lds_u32_a2(b + 32 + 32 * n + 16 * h + 4 * i);
+            hm[i] = lds_u32_a2(b + 16 * h + 4 * i);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                q[4 * j + i] = ((w[i] >> (2 * j)) & 0x03030303u) |
+                               (((hm[i] >> (4 * n + j)) & 0x01010101u) << 2);
+        const uint32_t t0 = lds_u32_a2(b + 96), t1 = lds_u32_a2(b + 100), t2 = lds_u32_a2(b + 104);
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b + 108));
+        const uint32_t a_lo = q3k_scale_word(2 * n, t0, t1, t2);      // scales 8n .. 8n+3
+        const uint32_t a_hi = q3k_scale_word(2 * n + 1, t0, t1, t2);  // scales 8n+4 .. 8n+7
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int s = static_cast<int8_t>(byte_of(j < 2 ? a_lo : a_hi, 2 * (j & 1) + h));
+            wd[j] = d * static_cast<float>(s);
+            wm[j] = 0.f;
+        }
+    }
+};
+
+// =============================================================================
+// Q4_K: 256 elements, 144 bytes: d @0, dmin @2, scales[12] @4, qs[128] @16.
+// src/tensor.h:329-358.  64-group g: elements 64g + l (l<32) <- qs[32g+l] & 15
+// with (sc, m) pair 2g; elements 64g + 32 + l <- qs[32g+l] >> 4 with pair 2g+1.
+// Unit c = group g: part 0 = low nibbles, part 1 = high nibbles; unit order is
+// block order (elements 64c .. 64c+63).
+// =============================================================================
+template <>
+struct Fmt<Q4_K> {
+    static constexpr int QK = 256, BB = 144, UPB = 4, UE = 64, PARTS = 2, PE = 32, IOFF = 0;
+    static constexpr bool MIN = true;
+
+    __device__ static float dq_elem(const uint8_t* b, int k) {
+        const int g = k >> 6, r = k & 63, hi = r >> 5, l = r & 31;
+        const float d = half_bits_to_float(ldg_u16(b));
+        const float dmin = half_bits_to_float(ldg_u16(b + 2));
+        uint32_t s[3];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+            s[i] = ldg_u16(b + 4 + 4 * i) | (ldg_u16(b + 6 + 4 * i) << 16);
+        uint32_t sc, m;
+        scale_min_k4(2 * g + hi, s[0], s[1], s[2], sc, m);
+        const float d1 = fmul(d, static_cast<float>(sc));
+        const float m1 = fmul(dmin, static_cast<float>(m));
+        const uint32_t v = ldg_u8(b + 16 + 32 * g + l);
+        const uint32_t qv = hi ? (v >> 4) : (v & 0xF);
+        return fsub(fmul(d1, static_cast<float>(qv)), m1);
+    }
+    __host__ __device__ static int xdests(int k, bool, int* c, int* e) { c[0] = k >> 6; e[0] = k & 63; return 1; }
+    __host__ __device__ static int part_xblock(int c, int p, bool) { return 2 * c + p; }
+    __host__ __device__ static int part_half(int c, int p, bool) { return 2 * (2 * c + p); }
+
+    __device__ static void decode(const uint8_t* b, int c, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
+                                  float (&wm)[PARTS]) {
+        const uint4 hd = lds_u128(b);
+        const uint4 a = lds_u128(b + 16 + 32 * c);
+        const uint4 a2 = lds_u128(b + 32 + 32 * c);
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, a2.x, a2.y, a2.z, a2.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            q[i] = w[i] & 0x0F0F0F0Fu;
+            q[8 + i] = (w[i] >> 4) & 0x0F0F0F0Fu;
+        }
+        const float d = half_bits_to_float(hd.x & 0xFFFFu);
+        const float dmin = half_bits_to_float(hd.x >> 16);
+        uint32_t sc0, m0, sc1, m1;
+        scale_min_k4(2 * c, hd.y, hd.z, hd.w, sc0, m0);
+        scale_min_k4(2 * c + 1, hd.y, hd.z, hd.w, sc1, m1);
+        wd[0] = d * static_cast<float>(sc0);
+        wm[0] = dmin * static_cast<float>(m0);
+        wd[1] = d * static_cast<float>(sc1);
+        wm[1] = dmin * static_cast<float>(m1);
+    }
+};
+
+// =============================================================================
+// Q5_K: 256 elements, 176 bytes: d @0, dmin @2, scales[12] @4, qh[32] @16,
+// qs[128] @48.  src/tensor.h:361-395.  As Q4_K plus a fifth bit:
+// element 64g + l gets +16 when qh[l] bit 2g is set, 64g + 32 + l when bit 2g+1.
+// =============================================================================
+template <>
+struct Fmt<Q5_K> {
+    static constexpr int QK = 256, BB = 176, UPB = 4, UE = 64, PARTS = 2, PE = 32, IOFF = 0;
+    static constexpr bool MIN = true;
+
+    __device__ static float dq_elem(const uint8_t* b, int k) {
+        const int g = k >> 6, r = k & 63, hi = r >> 5, l = r & 31;
+        const float d = half_bits_to_float(ldg_u16(b));
+        const float dmin = half_bits_to_float(ldg_u16(b + 2));
+        uint32_t s[3];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+            s[i] = ldg_u16(b + 4 + 4 * i) | (ldg_u16(b + 6 + 4 * i) << 16);
+        uint32_t sc, m;
+        scale_min_k4(2 * g + hi, s[0], s[1], s[2], sc, m);
+        const float d1 = fmul(d, static_cast<float>(sc));
+        const float m1 = fmul(dmin, static_cast<float>(m));
+        const uint32_t v = ldg_u8(b + 48 + 32 * g + l);
+        const uint32_t hb = (ldg_u8(b + 16 + l) >> (2 * g + hi)) & 1u;
+        const uint32_t qv = (hi ? (v >> 4) : (v & 0xF)) + (hb ? 16u : 0u);
+        return fsub(fmul(d1, static_cast<float>(qv)), m1);
+    }
+    __host__ __device__ static int xdests(int k, bool, int* c, int* e) { c[0] = k >> 6; e[0] = k & 63; return 1; }
+    __host__ __device__ static int part_xblock(int c, int p, bool) { return 2 * c + p; }
+    __host__ __device__ static int part_half(int c, int p, bool) { return 2 * (2 * c + p); }
+
+    __device__ static void decode(const uint8_t* b, int c, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
+                                  float (&wm)[PARTS]) {
+        const uint4 hd = lds_u128(b);
+        const uint4 h0 = lds_u128(b + 16);
+        const uint4 h1 = lds_u128(b + 32);
+        const uint4 a = lds_u128(b + 48 + 32 * c);
+        const uint4 a2 = lds_u128(b + 64 + 32 * c);
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, a2.x, a2.y, a2.z, a2.w};
+        const uint32_t qh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            q[i] = (w[i] & 0x0F0F0F0Fu) | (((qh[i] >> (2 * c)) & 0x01010101u) << 4);
+            q[8 + i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * c + 1)) & 0x01010101u) << 4);
+        }
+        const float d = half_bits_to_float(hd.x & 0xFFFFu);
+        const float dmin = half_bits_to_float(hd.x >> 16);
+        uint32_t sc0, m0, sc1, m1;
+        scale_min_k4(2 * c, hd.y, hd.z, hd.w, sc0, m0);
+        scale_min_k4(2 * c + 1, hd.y, hd.z, hd.w, sc1, m1);
+        wd[0] = d * static_cast<float>(sc0);
+        wm[0] = dmin * static_cast<float>(m0);
+        wd[1] = d * static_cast<float>(sc1);
+        wm[1] = dmin * static_cast<float>(m1);
+    }
+};
+
+// =============================================================================
+// Q6_K: 256 elements, 210 bytes: ql[128] @0, qh[64] @128, int8 scales[16] @192,
+// d @208.  src/tensor.h:398-432.  Half n, l in 0..31, plane k in 0..3:
+//   element 128n + 32k + l, 6-bit value from ql[64n + l (+32 for k odd)]
+//   (low nibble for k<2, high for k>=2) and bits 2k..2k+1 of qh[32n + l],
+//   minus 32; scale sc[8n + l/16 + 2k].
+// Unit c = (n = c>>1, h = c&1): l = 16h .. 16h+15, part k = plane k.
+// =============================================================================
+template <>
+struct Fmt<Q6_K> {
+    static constexpr int QK = 256, BB = 210, UPB = 4, UE = 64, PARTS = 4, PE = 16, IOFF = 32;
+    static constexpr bool MIN = false;
+
+    __device__ static float dq_elem(const uint8_t* b, int k) {
+        const int n = k >> 7, r = k & 127, kk = r >> 5, l = r & 31, is = l >> 4;
+        const float d = half_bits_to_float(ldg_u16(b + 208));
+        const uint32_t lo = ldg_u8(b + 64 * n + l + ((kk & 1) ? 32 : 0));
+        const uint32_t hh = ldg_u8(b + 128 + 32 * n + l);
+        const uint32_t nib = (kk < 2) ? (lo & 0xF) : (lo >> 4);
+        const int qv = static_cast<int>(nib | (((hh >> (2 * kk)) & 3u) << 4)) - 32;
+        const int sc = static_cast<int8_t>(ldg_u8(b + 192 + 8 * n + is + 2 * kk));
+        return fmul(fmul(d, static_cast<float>(sc)), static_cast<float>(qv));
+    }
+    __host__ __device__ static int xdests(int k, bool, int* c, int* e) {
+        const int n = k >> 7, r = k & 127, kk = r >> 5, l = r & 31;
+        c[0] = 2 * n + (l >> 4);
+        e[0] = 16 * kk + (l & 15);
+        return 1;
+    }
+    __host__ __device__ static int part_xblock(int c, int k, bool) { return 4 * (c >> 1) + k; }
+    __host__ __device__ static int part_half(int c, int k, bool) { return 8 * (c >> 1) + 2 * k + (c & 1); }
+
+    __device__ static void decode(const uint8_t* b, int c, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
+                                  float (&wm)[PARTS]) {
+        const int n = c >> 1, h = c & 1;
+        uint32_t A[4], B[4], H[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            A[i] = lds_u32_a2(b + 64 * n + 16 * h + 4 * i);
+            B[i] = lds_u32_a2(b + 64 * n + 32 + 16 * h + 4 * i);
+            H[i] = lds_u32_a2(b + 128 + 32 * n + 16 * h + 4 * i);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            q[i] = (A[i] & 0x0F0F0F0Fu) | ((H[i] & 0x03030303u) << 4);
+            q[4 + i] = (B[i] & 0x0F0F0F0Fu) | (((H[i] >> 2) & 0x03030303u) << 4);
+            q[8 + i] = ((A[i] >> 4) & 0x0F0F0F0Fu) | (((H[i] >> 4) & 0x03030303u) << 4);
+            q[12 + i] = ((B[i] >> 4) & 0x0F0F0F0Fu) | (((H[i] >> 6) & 0x03030303u) << 4);
+        }
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b + 208));
+        const uint32_t s_lo = lds_u32_a2(b + 192 + 8 * n);      // sc[8n .. 8n+3]
+        const uint32_t s_hi = lds_u32_a2(b + 192 + 8 * n + 4);  // sc[8n+4 .. 8n+7]
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            // scale index 8n + h + 2k
+            const int s = static_cast<int8_t>(byte_of(k < 2 ? s_lo : s_hi, 2 * (k & 1) + h));
+            wd[k] = d * static_cast<float>(s);
+            wm[k] = 0.f;
+        }
+    }
+};
+
+}  // namespace swq

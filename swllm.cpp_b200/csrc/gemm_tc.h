@@ -1,0 +1,15 @@
+// gemm_tc.h -- tensor-core (tcgen05) dequant-GEMM for prefill-sized M.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace swq {
+
+// True when the tcgen05 GEMM serves this problem.
+bool gemm_tc_supported(int type, int M, int N, int K);
+// Y[M x N] = X[M x K] . W[N x K]^T on tensor cores.
+cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, int M, int N, int K,
+                           int refcpu, int num_sms, cudaStream_t s);
+cudaError_t status_fetch_gemm_tc(unsigned* out, cudaStream_t s);
+
+}  // namespace swq

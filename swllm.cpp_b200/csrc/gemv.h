@@ -1,0 +1,45 @@
+// gemv.h -- internal launch interface of the libswq kernels (host side).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace swq {
+
+struct DeviceInfo {
+    int device = -1;
+    int num_sms = 0;
+    int smem_per_block_optin = 0;
+    int smem_per_sm = 0;
+    int cc_major = 0, cc_minor = 0;
+};
+
+struct GemvLaunch {
+    int type;
+    const void* W;
+    const float* X;
+    float* Y;
+    int M, N, K;
+    int refcpu;  // Q2_K reference-CPU activation order
+    int early;   // weight prefetch before the programmatic dependency
+    int num_sms;
+    int smem_per_block_optin;
+    int smem_per_sm;
+};
+
+// Fused dequant + GEMV for M <= 8 activation rows.
+cudaError_t gemv_launch(const GemvLaunch& L, cudaStream_t s);
+// Shared-memory bytes of the per-CTA activation prep for padded row count MT.
+size_t gemv_smem_x_bytes(int type, int MT, int K);
+
+// Bit-exact dequantization of nblocks whole blocks.
+cudaError_t dequant_launch(int type, const void* src, float* dst, int64_t nblocks, int num_sms,
+                           cudaStream_t s);
+
+// Device status words of each translation unit (bounded-wait timeouts).
+cudaError_t status_fetch_gemv(unsigned* out, cudaStream_t s);
+cudaError_t status_fetch_dequant(unsigned* out, cudaStream_t s);
+
+}  // namespace swq

@@ -1,0 +1,23 @@
+"""swq -- B200 (sm_100a) quantized-weight matmul for swllm.cpp models.
+
+Python host side over the C ABI of ``libswq.so`` (declared in include/swq.h).
+It mirrors the reference's interface for this path (src/tensor.h):
+
+* ``QuantWeight`` (src/tensor.h:507-511), ``Compute.matmul_transposed_q``
+  (src/tensor.h:1212) and ``dequantize`` (src/tensor.h:451) with host arrays;
+* device-pointer entry points ``dequant``, ``gemv``, ``gemm`` for callers that
+  keep weights and activations resident on the GPU (torch tensors or raw
+  pointers).
+
+All arithmetic runs in the CUDA kernels of libswq.  There is no CPU fallback:
+if the library is missing or the GPU is not an sm_100 part, calls raise.
+"""
+from __future__ import annotations
+
+from .lib import (  # noqa: F401
+    Q2_K, Q3_K, Q4_0, Q4_K, Q5_K, Q6_K, Q8_0, TYPES, TYPE_NAMES,
+    OPT_EARLY_WEIGHT_PREFETCH, OPT_GEMV_MAX_M, OPT_Q2K_REFERENCE_CPU_ORDER,
+    SwqError, Status, block_size, build, check, dequant, exported_symbols, gemm, gemv,
+    get_option, header_symbols, lib, lib_path, set_option, type_size,
+)
+from .compute import Backend, Compute, QuantWeight, dequantize  # noqa: F401

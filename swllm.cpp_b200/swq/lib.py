@@ -1,0 +1,167 @@
+"""ctypes binding of libswq.so (include/swq.h)."""
+from __future__ import annotations
+
+import ctypes
+import enum
+import re
+import subprocess
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+PKG_ROOT = HERE.parent                      # swllm.cpp_b200/
+REPO_ROOT = PKG_ROOT.parent
+CSRC = PKG_ROOT / "csrc"
+HEADER = REPO_ROOT / "include" / "swq.h"
+_LIB_PATH = HERE / "libswq.so"
+
+# GGMLType ids, src/gguf.h:18-40
+Q4_0, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 2, 8, 10, 11, 12, 13, 14
+TYPES = {"Q4_0": Q4_0, "Q8_0": Q8_0, "Q2_K": Q2_K, "Q3_K": Q3_K,
+         "Q4_K": Q4_K, "Q5_K": Q5_K, "Q6_K": Q6_K}
+TYPE_NAMES = {v: k for k, v in TYPES.items()}
+
+OPT_Q2K_REFERENCE_CPU_ORDER = 1
+OPT_EARLY_WEIGHT_PREFETCH = 2
+OPT_GEMV_MAX_M = 3
+
+
+class Status(enum.IntEnum):
+    OK = 0
+    BAD_TYPE = 1
+    BAD_SHAPE = 2
+    NULL_PTR = 3
+    CUDA = 4
+    TIMEOUT = 5
+    UNSUPPORTED = 6
+    BAD_ARG = 7
+
+
+class SwqError(RuntimeError):
+    def __init__(self, status: int, detail: str):
+        self.status = Status(status)
+        super().__init__(f"swq: {self.status.name}: {detail}")
+
+
+_lib = None
+
+
+def lib_path() -> Path:
+    return _LIB_PATH
+
+
+def build(jobs: int = 8) -> Path:
+    """Compile libswq.so for sm_100a (nvcc cross-compiles without a GPU)."""
+    subprocess.run(["make", "-s", f"-j{jobs}", "-C", str(CSRC)], check=True)
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not _LIB_PATH.exists():
+        raise FileNotFoundError(f"{_LIB_PATH} is not built; run swq.build() (make -C {CSRC})")
+    L = ctypes.CDLL(str(_LIB_PATH))
+    vp, i32, i64, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
+    sig = {
+        "swq_status_string": (ctypes.c_char_p, [i32]),
+        "swq_last_error": (ctypes.c_char_p, []),
+        "swq_type_size": (sz, [i32]),
+        "swq_block_size": (sz, [i32]),
+        "swq_dequant": (i32, [i32, vp, vp, i64, vp]),
+        "swq_gemv": (i32, [i32, vp, vp, vp, i32, i32, vp]),
+        "swq_gemm": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
+        "swq_set_option": (i32, [i32, i32]),
+        "swq_get_option": (i32, [i32]),
+        "swq_check": (i32, [vp]),
+        "swq_ctx_create": (i32, [i32, ctypes.POINTER(vp)]),
+        "swq_ctx_destroy": (i32, [vp]),
+        "swq_ctx_matmul_transposed_q": (i32, [vp, vp, vp, vp, i32, i32, i32]),
+        "swq_ctx_matmul_q_batched": (i32, [vp, vp, vp, vp, i32, i32, i32, i32]),
+        "swq_ctx_dequantize": (i32, [vp, vp, vp, i64, i32]),
+        "swq_ctx_evict": (i32, [vp, vp]),
+        "swq_ctx_resident_bytes": (sz, [vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _raise(rc: int) -> None:
+    if rc != 0:
+        detail = lib().swq_last_error().decode(errors="replace")
+        raise SwqError(rc, detail)
+
+
+def header_symbols() -> list[str]:
+    """Every function declared in include/swq.h."""
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*[\w\s\*]+?\b(swq_\w+)\s*\(", text, flags=re.M)))
+
+
+def exported_symbols() -> list[str]:
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    return sorted({ln.split()[-1] for ln in out.splitlines() if ln.split() and ln.split()[-1].startswith("swq_")})
+
+
+def type_size(t: int) -> int:
+    return int(lib().swq_type_size(t))
+
+
+def block_size(t: int) -> int:
+    return int(lib().swq_block_size(t))
+
+
+def set_option(opt: int, value: int) -> None:
+    _raise(lib().swq_set_option(opt, value))
+
+
+def get_option(opt: int) -> int:
+    return int(lib().swq_get_option(opt))
+
+
+def _ptr(a) -> int:
+    """Device address of a torch tensor, or an int address as given."""
+    if a is None:
+        return 0
+    if isinstance(a, int):
+        return a
+    return int(a.data_ptr())
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                return int(torch.cuda.current_stream().cuda_stream)
+        except Exception:  # pragma: no cover
+            pass
+        return 0
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)
+
+
+def dequant(type_id: int, blocks, out, n: int, stream=None) -> None:
+    """out[:n] = dequantize(blocks) on the device, bit-exact (async)."""
+    _raise(lib().swq_dequant(type_id, _ptr(blocks), _ptr(out), n, _stream(stream)))
+
+
+def gemv(type_id: int, W, x, y, N: int, K: int, stream=None) -> None:
+    """y[N] = W[N x K] . x[K] on device buffers (async)."""
+    _raise(lib().swq_gemv(type_id, _ptr(W), _ptr(x), _ptr(y), N, K, _stream(stream)))
+
+
+def gemm(type_id: int, W, X, Y, M: int, N: int, K: int, stream=None) -> None:
+    """Y[M x N] = X[M x K] . W[N x K]^T on device buffers (async)."""
+    _raise(lib().swq_gemm(type_id, _ptr(W), _ptr(X), _ptr(Y), M, N, K, _stream(stream)))
+
+
+def check(stream=None) -> None:
+    """Synchronize and raise on a device-side wait timeout or CUDA error."""
+    _raise(lib().swq_check(_stream(stream)))

@@ -1,0 +1,92 @@
+"""The C ABI of libswq on the CPU: the library loads, exports every function
+include/swq.h declares, and rejects bad arguments with the documented status
+before touching a GPU (no compute call runs here)."""
+import ctypes
+
+import pytest
+
+import kat
+import swq
+from swq.lib import Status, lib
+
+
+def test_library_built_and_loads():
+    assert swq.lib_path().exists(), "run __graft_entry__.build() first"
+    lib()
+
+
+def test_exports_every_header_symbol():
+    declared = swq.header_symbols()
+    assert {"swq_dequant", "swq_gemv", "swq_gemm", "swq_ctx_matmul_transposed_q"} <= set(declared)
+    exported = set(swq.exported_symbols())
+    missing = [s for s in declared if s not in exported]
+    assert not missing, f"declared in include/swq.h but not exported: {missing}"
+    for s in declared:
+        getattr(lib(), s)
+
+
+def test_type_and_block_sizes():
+    for t, bb in kat.TYPE_SIZES.items():
+        assert swq.type_size(t) == bb
+        assert swq.block_size(t) == kat.BLOCK_SIZES[t]
+    for t in (0, 1, 6, 30, 37):  # F32, F16, Q5_0, BF16, F8 are not on this path
+        assert swq.type_size(t) == 0 and swq.block_size(t) == 0
+
+
+def test_status_strings():
+    L = lib()
+    for s in Status:
+        assert L.swq_status_string(int(s))
+
+
+def _rc(fn, *args):
+    return Status(fn(*args))
+
+
+def test_gemv_argument_errors():
+    L = lib()
+    assert _rc(L.swq_gemv, 0, 1, 1, 1, 4, 256, None) is Status.BAD_TYPE
+    assert _rc(L.swq_gemv, kat.Q4_K, 1, 1, 1, 4, 100, None) is Status.BAD_SHAPE
+    assert b"multiple of 256" in L.swq_last_error()
+    assert _rc(L.swq_gemv, kat.Q4_0, 1, 1, 1, 4, 48, None) is Status.BAD_SHAPE
+    assert _rc(L.swq_gemv, kat.Q4_K, None, 1, 1, 4, 256, None) is Status.NULL_PTR
+    assert _rc(L.swq_gemv, kat.Q4_K, 1, None, 1, 4, 256, None) is Status.NULL_PTR
+    assert _rc(L.swq_gemv, kat.Q4_K, 1, 1, None, 4, 256, None) is Status.NULL_PTR
+    assert _rc(L.swq_gemm, kat.Q4_K, 1, 1, 1, -1, 4, 256, None) is Status.BAD_SHAPE
+    # empty problems are a no-op, like the reference's loops over zero rows
+    assert _rc(L.swq_gemv, kat.Q4_K, None, None, None, 0, 256, None) is Status.OK
+    assert _rc(L.swq_gemm, kat.Q4_K, None, None, None, 0, 4, 256, None) is Status.OK
+
+
+def test_dequant_argument_errors():
+    L = lib()
+    assert _rc(L.swq_dequant, 1, 1, 1, 32, None) is Status.BAD_TYPE
+    assert _rc(L.swq_dequant, kat.Q8_0, 1, 1, -32, None) is Status.BAD_SHAPE
+    assert _rc(L.swq_dequant, kat.Q8_0, None, 1, 32, None) is Status.NULL_PTR
+    # fewer elements than one block: nothing to write (reference: n / QK blocks)
+    assert _rc(L.swq_dequant, kat.Q4_K, None, None, 255, None) is Status.OK
+    assert _rc(L.swq_dequant, kat.Q4_K, None, None, 0, None) is Status.OK
+
+
+def test_options():
+    assert swq.get_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER) == 0
+    assert swq.get_option(swq.OPT_EARLY_WEIGHT_PREFETCH) == 1
+    swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 1)
+    assert swq.get_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER) == 1
+    swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 0)
+    with pytest.raises(swq.SwqError) as ei:
+        swq.set_option(swq.OPT_GEMV_MAX_M, 9)
+    assert ei.value.status is Status.BAD_ARG
+    with pytest.raises(swq.SwqError):
+        swq.set_option(99, 0)
+    assert swq.get_option(99) == -1
+
+
+def test_ctx_null_handle_errors():
+    L = lib()
+    assert _rc(L.swq_ctx_matmul_transposed_q, None, 1, 1, 1, kat.Q4_K, 4, 256) is Status.NULL_PTR
+    assert _rc(L.swq_ctx_create, 0, None) is Status.NULL_PTR
+    assert _rc(L.swq_ctx_destroy, None) is Status.OK
+    assert L.swq_ctx_resident_bytes(None) == 0
+    out = ctypes.c_void_p()
+    assert isinstance(out, ctypes.c_void_p)

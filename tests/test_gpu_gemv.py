@@ -1,0 +1,212 @@
+"""Fused dequant-GEMV / small-M GEMM on the GPU against the oracle.
+
+Tolerance: relative L2 <= 1e-3 against the reference's fp32 result on the same
+seeded inputs (REL_L2_TOL).  Q2_K is compared in the element order of
+dequantize_q2_k by default, and in the reference fused-CPU order with
+SWQ_OPT_Q2K_REFERENCE_CPU_ORDER.
+"""
+import numpy as np
+import pytest
+
+import kat
+import swq
+from conftest import REL_L2_TOL, rel_l2
+from swq import synth
+
+pytestmark = pytest.mark.gpu
+
+FORMATS = ["Q4_0", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"]
+
+
+def _gemm_gpu(torch, t, blocks, X, N, K, w_offset=0):
+    M = X.shape[0]
+    flat = np.ascontiguousarray(blocks).reshape(-1)
+    d_w = torch.zeros(flat.size + 64, dtype=torch.uint8, device="cuda")
+    d_w[w_offset:w_offset + flat.size] = torch.from_numpy(flat).cuda()
+    d_x = torch.from_numpy(np.ascontiguousarray(X, dtype=np.float32)).cuda()
+    d_y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    swq.gemm(t, d_w.data_ptr() + w_offset, d_x, d_y, M, N, K)
+    swq.check()
+    return d_y.cpu().numpy()
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("M", [1, 2, 3, 8])
+def test_small_shapes(cuda, oracle_mod, fmt, M):
+    t = synth.IDS[fmt]
+    qk, _ = synth.block_geometry(t)
+    N, K = 301, 8 * qk if qk == 256 else 64 * qk
+    blocks = synth.random_blocks(t, N, K, seed=100 + t)
+    X = synth.random_activations(M, K, seed=200 + M)
+    got = _gemm_gpu(cuda, t, blocks, X, N, K)
+    want = oracle_mod.gemm(t, blocks, X, M, N, K)
+    assert rel_l2(got, want) <= REL_L2_TOL
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_llama_ffn_shape_m1(cuda, oracle_mod, fmt):
+    """N=14336, K=4096 (Llama-3-8B FFN up-projection), one activation row."""
+    t = synth.IDS[fmt]
+    N, K = 14336, 4096
+    blocks = synth.random_blocks(t, N, K, seed=300 + t)
+    X = synth.random_activations(1, K, seed=301)
+    got = _gemm_gpu(cuda, t, blocks, X, N, K)
+    want = oracle_mod.gemm(t, blocks, X, 1, N, K)
+    assert rel_l2(got, want) <= REL_L2_TOL
+    assert np.all(np.isfinite(got))
+
+
+def test_q4k_4096_square(cuda, oracle_mod):
+    t = synth.Q4_K
+    blocks = synth.random_blocks(t, 4096, 4096, seed=0)
+    X = synth.random_activations(1, 4096, seed=1)
+    got = _gemm_gpu(cuda, t, blocks, X, 4096, 4096)
+    want = oracle_mod.gemm(t, blocks, X, 1, 4096, 4096)
+    err = rel_l2(got, want)
+    assert err <= REL_L2_TOL
+    # the fixed-point activation path is far inside the tolerance
+    assert err < 1e-4
+
+
+@pytest.mark.parametrize("fmt,K", [("Q6_K", 28672), ("Q4_K", 28672), ("Q4_K", 8192), ("Q8_0", 14336)])
+def test_long_rows(cuda, oracle_mod, fmt, K):
+    t = synth.IDS[fmt]
+    N = 96
+    blocks = synth.random_blocks(t, N, K, seed=400 + t)
+    X = synth.random_activations(2, K, seed=401)
+    got = _gemm_gpu(cuda, t, blocks, X, N, K)
+    want = oracle_mod.gemm(t, blocks, X, 2, N, K)
+    assert rel_l2(got, want) <= REL_L2_TOL
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_golden_vectors(cuda, golden, fmt):
+    g = golden(fmt)
+    t, N, K = int(g["type"]), int(g["N"]), int(g["K"])
+    got = _gemm_gpu(cuda, t, g["blocks"], g["x"], N, K)
+    want = g["gemv_dq"] if fmt == "Q2_K" else g["gemv_ref"]
+    assert rel_l2(got, want) <= REL_L2_TOL
+
+
+def test_q2k_reference_cpu_order_option(cuda, golden):
+    g = golden("Q2_K")
+    t, N, K = int(g["type"]), int(g["N"]), int(g["K"])
+    swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 1)
+    try:
+        got = _gemm_gpu(cuda, t, g["blocks"], g["x"], N, K)
+    finally:
+        swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 0)
+    assert rel_l2(got, g["gemv_ref"]) <= REL_L2_TOL
+
+
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K", "Q2_K", "Q8_0"])
+def test_unaligned_weights_and_rows(cuda, oracle_mod, fmt):
+    """Base not 16-byte aligned, and rows whose byte length is not a multiple
+    of 16 (one Q6_K/Q8_0 block per row): the plain-load producer path."""
+    t = synth.IDS[fmt]
+    qk, _ = synth.block_geometry(t)
+    for N, K, off in ((37, qk, 0), (37, 3 * qk, 2), (64, 16 * qk if qk == 32 else 4 * qk, 6)):
+        blocks = synth.random_blocks(t, N, K, seed=500 + off)
+        X = synth.random_activations(3, K, seed=501)
+        got = _gemm_gpu(cuda, t, blocks, X, N, K, w_offset=off)
+        want = oracle_mod.gemm(t, blocks, X, 3, N, K)
+        assert rel_l2(got, want) <= REL_L2_TOL, (N, K, off)
+
+
+@pytest.mark.parametrize("N", [1, 7, 148, 149, 300])
+def test_row_counts_around_grid(cuda, oracle_mod, N):
+    t = synth.Q4_K
+    blocks = synth.random_blocks(t, N, 1024, seed=600 + N)
+    X = synth.random_activations(1, 1024, seed=601)
+    got = _gemm_gpu(cuda, t, blocks, X, N, 1024)
+    assert rel_l2(got, oracle_mod.gemm(t, blocks, X, 1, N, 1024)) <= REL_L2_TOL
+
+
+def test_without_early_prefetch(cuda, oracle_mod):
+    t = synth.Q5_K
+    blocks = synth.random_blocks(t, 512, 2048, seed=7)
+    X = synth.random_activations(4, 2048, seed=8)
+    swq.set_option(swq.OPT_EARLY_WEIGHT_PREFETCH, 0)
+    try:
+        got = _gemm_gpu(cuda, t, blocks, X, 512, 2048)
+    finally:
+        swq.set_option(swq.OPT_EARLY_WEIGHT_PREFETCH, 1)
+    assert rel_l2(got, oracle_mod.gemm(t, blocks, X, 4, 512, 2048)) <= REL_L2_TOL
+
+
+@pytest.mark.parametrize("M", [9, 16, 64])
+def test_larger_m(cuda, oracle_mod, M):
+    t = synth.Q4_K
+    N, K = 384, 2048
+    blocks = synth.random_blocks(t, N, K, seed=700 + M)
+    X = synth.random_activations(M, K, seed=701)
+    got = _gemm_gpu(cuda, t, blocks, X, N, K)
+    assert rel_l2(got, oracle_mod.gemm(t, blocks, X, M, N, K)) <= REL_L2_TOL
+
+
+def test_back_to_back_launches_deterministic(cuda):
+    torch = cuda
+    t = synth.Q4_K
+    N, K = 4096, 4096
+    blocks = synth.random_blocks(t, N, K, seed=9)
+    d_w = torch.from_numpy(blocks.reshape(-1)).cuda()
+    d_x = torch.from_numpy(synth.random_activations(1, K, seed=10)).cuda()
+    ys = [torch.empty(N, dtype=torch.float32, device="cuda") for _ in range(6)]
+    for y in ys:
+        swq.gemv(t, d_w, d_x, y, N, K)
+    swq.check()
+    for y in ys[1:]:
+        assert torch.equal(y, ys[0])
+
+
+def test_fused_known_answers(cuda):
+    c = kat.q8_0_2x32()
+    got = _gemm_gpu(cuda, c["type"], c["blocks"], c["x"][None, :], 2, 32)[0]
+    np.testing.assert_allclose(got, c["expect"], atol=c["tol"])
+    c = kat.q4_0_2x32()
+    for x in (c["x"], c["x_alt"]):
+        got = _gemm_gpu(cuda, c["type"], c["blocks"], x[None, :], 2, 32)[0]
+        np.testing.assert_allclose(got, [0.0, 0.0], atol=1e-4)
+    for case in kat.fused_kats():
+        x = np.ones((1, case["K"]), np.float32)
+        got = _gemm_gpu(cuda, case["type"], case["blocks"], x, case["N"], case["K"])[0]
+        import oracle
+        want = oracle.gemv(case["type"], case["blocks"], x[0], case["N"], case["K"])
+        np.testing.assert_allclose(got, want, rtol=1e-3, atol=case["tol"])
+
+
+def test_host_buffer_compute_api(cuda, oracle_mod):
+    """Compute.matmul_transposed_q with host arrays, the reference's calling
+    convention (src/tensor.h:1212): weights uploaded once and kept resident."""
+    t = synth.Q6_K
+    N, K = 1024, 4096
+    w = swq.QuantWeight(synth.random_blocks(t, N, K, seed=12), t)
+    x = synth.random_activations(1, K, seed=13)[0]
+    out = np.zeros(N, np.float32)
+    with swq.Compute() as c:
+        c.matmul_transposed_q(out, x, w, N, K)
+        assert rel_l2(out, oracle_mod.gemv(t, w.data, x, N, K)) <= REL_L2_TOL
+        resident = c.resident_bytes()
+        assert resident == synth.matrix_bytes(t, N, K)
+        x2 = synth.random_activations(1, K, seed=14)[0]
+        c.matmul_transposed_q(out, x2, w, N, K)
+        assert c.resident_bytes() == resident  # cache hit, no second upload
+        assert rel_l2(out, oracle_mod.gemv(t, w.data, x2, N, K)) <= REL_L2_TOL
+        X = synth.random_activations(5, K, seed=15)
+        Y = np.zeros((5, N), np.float32)
+        c.matmul_q_batched(Y, X, w, 5, N, K)
+        assert rel_l2(Y, oracle_mod.gemm(t, w.data, X, 5, N, K)) <= REL_L2_TOL
+        c.evict(w)
+        assert c.resident_bytes() == 0
+        dst = np.zeros(N * K, np.float32)
+        c.dequantize(w.data, dst, N * K, t)
+        want = oracle_mod.dequantize(t, w.data, N * K)
+        assert np.array_equal(dst.view(np.uint32), want.view(np.uint32))
+
+
+def test_module_dequantize_host(cuda, oracle_mod):
+    t = synth.Q3_K
+    blocks = synth.random_blocks(t, 4, 1024, seed=16)
+    dst = np.zeros(4096, np.float32)
+    swq.dequantize(blocks, dst, 4096, t)
+    assert np.array_equal(dst.view(np.uint32), oracle_mod.dequantize(t, blocks, 4096).view(np.uint32))
