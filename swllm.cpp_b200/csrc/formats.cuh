@@ -8,21 +8,26 @@
 //
 //  * unit decode for the fused GEMV: a block is split into UPB "units" of UE
 //    elements (one lane's work).  decode() turns a unit's quant bits into
-//    UE/4 words of four small non-negative integers (bytes), in "unit order";
-//    the activation row is re-laid out in the same unit order as 16-bit
-//    fixed-point values, so the dot product is a chain of dp2a instructions.
-//    Each unit has PARTS parts of PE elements that share one weight scale and
-//    one activation block scale:
-//        contribution = xs * (wd * (S - IOFF * I) - wm * I)
-//    where S = sum(q * X) over the part, I = sum(X) over the part, wd/wm the
-//    part's weight scale/min and IOFF the format's integer zero point.
+//    UE/4 words of four small integers (bytes, unsigned unless QSIGNED).  A
+//    unit has PARTS parts; part p covers the PE consecutive block elements
+//    starting at part_elem0(c, p), held in words p*WPP .. p*WPP+WPP-1 in
+//    element order, and shares one weight scale and one 32-element activation
+//    block.  A part's bytes may hold the quant value times a power of two
+//    (e.g. a high nibble left in place, x16); wd then carries the inverse
+//    factor and ioff(p) (the integer zero point) is in the same scaled units.
+//    Activations are 16-bit fixed point, so the dot product is a chain of
+//    dp2a instructions:
+//        contribution = xs * (wd * (S - ioff(p) * I) - wm * I)
+//    with S = sum(q * X) and I = sum(X) over the part.
 #pragma once
+
+#include <cuda_fp16.h>
 
 #include "swq_device.cuh"
 
 namespace swq {
 
-// ---- helpers for the K-quant 6-bit scale field --------------------------------
+// ---- helpers --------------------------------------------------------------------
 
 // get_scale_min_k4 (src/tensor.h:218-227) on the 12-byte field held as three
 // little-endian words s0 = bytes 0-3, s1 = bytes 4-7, s2 = bytes 8-11.
@@ -36,6 +41,19 @@ __device__ __forceinline__ void scale_min_k4(int j, uint32_t s0, uint32_t s1, ui
         sc = (byte_of(s2, jj) & 0x0Fu) | ((byte_of(s0, jj) >> 6) << 4);
         m = (byte_of(s2, jj) >> 4) | ((byte_of(s1, jj) >> 6) << 4);
     }
+}
+
+// The same for sub-block j = 2c + t (t = 0, 1) without a branch on c, so
+// lanes that hold different units of a block do not diverge.
+__device__ __forceinline__ void scale_min_k4_unit(int c, int t, uint32_t s0, uint32_t s1, uint32_t s2,
+                                                  uint32_t& sc, uint32_t& m) {
+    const uint32_t pos = 8u * ((2 * c + t) & 3);
+    const uint32_t a0 = __funnelshift_r(s0, 0u, pos) & 0xFFu;  // byte of s0
+    const uint32_t a1 = __funnelshift_r(s1, 0u, pos) & 0xFFu;
+    const uint32_t a2 = __funnelshift_r(s2, 0u, pos) & 0xFFu;
+    const bool hi = c >= 2;
+    sc = hi ? ((a2 & 0x0Fu) | ((a0 >> 6) << 4)) : (a0 & 63u);
+    m = hi ? ((a2 >> 4) | ((a1 >> 6) << 4)) : (a1 & 63u);
 }
 
 // Q3_K signed scales, src/tensor.h:286-304: word w (0..3) of the unpacked
@@ -56,16 +74,23 @@ __device__ __forceinline__ uint32_t ldg_u16(const uint8_t* p) {
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
 
+// Hardware fp16 -> fp32 (exact for every finite value); the GEMV's scales.
+__device__ __forceinline__ float h2f(uint32_t bits) { return __half2float(__ushort_as_half(static_cast<unsigned short>(bits))); }
+
 template <int T>
 struct Fmt;
 
 // =============================================================================
 // Q4_0: 32 elements, 18 bytes: d (f16) @0, 16 nibble bytes @2.  src/tensor.h:139
+// element j <- low nibble of byte j, element j+16 <- high nibble; value - 8.
+// One unit = the block; part 0 = elements 0..15, part 1 = 16..31 (high
+// nibbles kept in place, x16).
 // =============================================================================
 template <>
 struct Fmt<Q4_0> {
-    static constexpr int QK = 32, BB = 18, UPB = 1, UE = 32, PARTS = 1, PE = 32, IOFF = 8;
-    static constexpr bool MIN = false;
+    static constexpr int QK = 32, BB = 18, UPB = 1, UE = 32, PARTS = 2, PE = 16;
+    static constexpr bool MIN = false, QSIGNED = false;
+    __host__ __device__ static constexpr int ioff(int p) { return p == 0 ? 8 : 128; }
 
     __device__ static float dq_elem(const uint8_t* b, int k) {
         const float d = half_bits_to_float(ldg_u16(b));
@@ -73,10 +98,11 @@ struct Fmt<Q4_0> {
         const int q = (k < 16) ? static_cast<int>(v & 0x0F) : static_cast<int>(v >> 4);
         return fmul(static_cast<float>(q - 8), d);
     }
-    // unit element e <-> block element k: identity (low nibbles 0..15, high 16..31)
-    __host__ __device__ static int xdests(int k, bool, int* c, int* e) { c[0] = 0; e[0] = k; return 1; }
-    __host__ __device__ static int part_xblock(int, int, bool) { return 0; }
-    __host__ __device__ static int part_half(int, int, bool) { return 0; }
+    __host__ __device__ static int part_elem0(int, int p, bool) { return 16 * p; }
+    // 8-element item at block element kk -> (unit, part, chunk in part)
+    __host__ __device__ static int item_dest(int kk, bool, int& c, int& p, int& j) {
+        c = 0; p = kk >> 4; j = (kk >> 3) & 1; return 1;
+    }
 
     __device__ static void decode(const uint8_t* b, int, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
                                   float (&wm)[PARTS]) {
@@ -86,10 +112,12 @@ struct Fmt<Q4_0> {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             q[i] = w[i] & 0x0F0F0F0Fu;
-            q[4 + i] = (w[i] >> 4) & 0x0F0F0F0Fu;
+            q[4 + i] = w[i] & 0xF0F0F0F0u;
         }
-        wd[0] = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b));
-        wm[0] = 0.f;
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(b));
+        wd[0] = d;
+        wd[1] = d * 0.0625f;
+        wm[0] = wm[1] = 0.f;
     }
 };
 
@@ -98,23 +126,25 @@ struct Fmt<Q4_0> {
 // =============================================================================
 template <>
 struct Fmt<Q8_0> {
-    static constexpr int QK = 32, BB = 34, UPB = 1, UE = 32, PARTS = 1, PE = 32, IOFF = 0;
-    static constexpr bool MIN = false;
+    static constexpr int QK = 32, BB = 34, UPB = 1, UE = 32, PARTS = 1, PE = 32;
+    static constexpr bool MIN = false, QSIGNED = true;
+    __host__ __device__ static constexpr int ioff(int) { return 0; }
 
     __device__ static float dq_elem(const uint8_t* b, int k) {
         const float d = half_bits_to_float(ldg_u16(b));
         const int q = static_cast<int8_t>(ldg_u8(b + 2 + k));
         return fmul(static_cast<float>(q), d);
     }
-    __host__ __device__ static int xdests(int k, bool, int* c, int* e) { c[0] = 0; e[0] = k; return 1; }
-    __host__ __device__ static int part_xblock(int, int, bool) { return 0; }
-    __host__ __device__ static int part_half(int, int, bool) { return 0; }
+    __host__ __device__ static int part_elem0(int, int, bool) { return 0; }
+    __host__ __device__ static int item_dest(int kk, bool, int& c, int& p, int& j) {
+        c = 0; p = 0; j = kk >> 3; return 1;
+    }
 
     __device__ static void decode(const uint8_t* b, int, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
                                   float (&wm)[PARTS]) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) q[i] = lds_u32_a2(b + 2 + 4 * i);  // signed bytes
-        wd[0] = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b));
+        wd[0] = h2f(*reinterpret_cast<const uint16_t*>(b));
         wm[0] = 0.f;
     }
 };
@@ -123,12 +153,14 @@ struct Fmt<Q8_0> {
 // Q2_K: 256 elements, 84 bytes: scales[16] @0, qs[64] @16, d @80, dmin @82.
 // src/tensor.h:232-265.  Element 128n + 32j + 16h + l <- (qs[32n + 16h + l] >> 2j) & 3,
 // scale byte sc[8n + 2j + h] (low nibble: scale, high nibble: min).
-// Unit c = (n = c>>1, h = c&1): 64 elements, part j = the 16 elements of plane j.
+// Unit c = (n = c>>1, h = c&1): 64 elements; part j = the 16 elements of
+// plane j, its 2-bit values left in place (x 4^j).
 // =============================================================================
 template <>
 struct Fmt<Q2_K> {
-    static constexpr int QK = 256, BB = 84, UPB = 4, UE = 64, PARTS = 4, PE = 16, IOFF = 0;
-    static constexpr bool MIN = true;
+    static constexpr int QK = 256, BB = 84, UPB = 4, UE = 64, PARTS = 4, PE = 16;
+    static constexpr bool MIN = true, QSIGNED = false;
+    __host__ __device__ static constexpr int ioff(int) { return 0; }
 
     __device__ static float dq_elem(const uint8_t* b, int k) {
         const int n = k >> 7, r = k & 127, j = r >> 5, h = (r >> 4) & 1, l = r & 15;
@@ -140,30 +172,21 @@ struct Fmt<Q2_K> {
         const uint32_t v = (ldg_u8(b + 16 + 32 * n + 16 * h + l) >> (2 * j)) & 3u;
         return fsub(fmul(dl, static_cast<float>(v)), ml);
     }
-    // Format order: unit element e = 16j + l of unit c is block element
-    // 128n + 32j + 16h + l.  Reference-CPU order (cpu_matmul_transposed_q2_k,
-    // src/tensor.h:935-945): it is block element 128n + 16h + l for every j, so
-    // elements 128n + 32..127 are never used and the others feed four planes.
-    __host__ __device__ static int xdests(int k, bool refcpu, int* c, int* e) {
-        const int n = k >> 7, r = k & 127;
-        if (!refcpu) {
-            const int j = r >> 5, h = (r >> 4) & 1, l = r & 15;
-            c[0] = 2 * n + h;
-            e[0] = 16 * j + l;
-            return 1;
-        }
-        if (r >= 32) return 0;
-        const int h = r >> 4, l = r & 15;
-        for (int j = 0; j < 4; ++j) { c[j] = 2 * n + h; e[j] = 16 * j + l; }
-        return 4;
+    // Part j of unit c holds block elements 128n + 32j + 16h .. +15 (format
+    // order).  In the reference-CPU order (cpu_matmul_transposed_q2_k,
+    // src/tensor.h:935-945) every plane j reads activations 128n + 16h .. +15.
+    __host__ __device__ static int part_elem0(int c, int j, bool refcpu) {
+        return 128 * (c >> 1) + (refcpu ? 0 : 32 * j) + 16 * (c & 1);
     }
-    __host__ __device__ static int part_xblock(int c, int j, bool refcpu) {
-        return 4 * (c >> 1) + (refcpu ? 0 : j);
+    // Reference-CPU order: the item feeds parts 0..3 of its unit (or nothing).
+    __host__ __device__ static int item_dest(int kk, bool refcpu, int& c, int& p, int& j) {
+        const int n = kk >> 7, r = kk & 127;
+        c = 2 * n + ((r >> 4) & 1);
+        j = (r >> 3) & 1;
+        if (!refcpu) { p = r >> 5; return 1; }
+        p = 0;
+        return r < 32 ? 4 : 0;
     }
-    __host__ __device__ static int part_half(int c, int j, bool refcpu) {
-        return 8 * (c >> 1) + (refcpu ? 0 : 2 * j) + (c & 1);
-    }
-
     __device__ static void decode(const uint8_t* b, int c, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
                                   float (&wm)[PARTS]) {
         const int n = c >> 1, h = c & 1;
@@ -173,16 +196,17 @@ struct Fmt<Q2_K> {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) q[4 * j + i] = (w[i] >> (2 * j)) & 0x03030303u;
+            for (int i = 0; i < 4; ++i) q[4 * j + i] = w[i] & (0x03030303u << (2 * j));
         const uint32_t s_lo = lds_u32_a4(b + 8 * n);      // sc[8n .. 8n+3]
         const uint32_t s_hi = lds_u32_a4(b + 8 * n + 4);  // sc[8n+4 .. 8n+7]
         const uint32_t dd = lds_u32_a4(b + 80);
-        const float d = half_bits_to_float(dd & 0xFFFFu);
-        const float dmin = half_bits_to_float(dd >> 16);
+        const float d = h2f(dd & 0xFFFFu);
+        const float dmin = h2f(dd >> 16);
+        constexpr float inv4[4] = {1.0f, 0.25f, 0.0625f, 0.015625f};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const uint32_t s = byte_of(j < 2 ? s_lo : s_hi, 2 * (j & 1) + h);
-            wd[j] = d * static_cast<float>(s & 0xF);
+            wd[j] = d * static_cast<float>(s & 0xF) * inv4[j];
             wm[j] = dmin * static_cast<float>(s >> 4);
         }
     }
@@ -193,11 +217,13 @@ struct Fmt<Q2_K> {
 // src/tensor.h:269-326.  Element 128n + 32j + 16h + l:
 //   v = ((qs[32n + 16h + l] >> 2j) & 3) - (hmask[16h + l] bit (4n + j) ? 0 : 4),
 //   scale = scales_i8[8n + 2j + h].
+// Decoded as u = q2 | hbit << 2 in 0..7 with zero point 4.
 // =============================================================================
 template <>
 struct Fmt<Q3_K> {
-    static constexpr int QK = 256, BB = 110, UPB = 4, UE = 64, PARTS = 4, PE = 16, IOFF = 4;
-    static constexpr bool MIN = false;
+    static constexpr int QK = 256, BB = 110, UPB = 4, UE = 64, PARTS = 4, PE = 16;
+    static constexpr bool MIN = false, QSIGNED = false;
+    __host__ __device__ static constexpr int ioff(int) { return 4; }
 
     __device__ static float dq_elem(const uint8_t* b, int k) {
         const int n = k >> 7, r = k & 127, j = r >> 5, h = (r >> 4) & 1, l = r & 15;
@@ -214,14 +240,11 @@ struct Fmt<Q3_K> {
         const int hb = (ldg_u8(b + 16 * h + l) >> (4 * n + j)) & 1;
         return fmul(dl, static_cast<float>(q2 - (hb ? 0 : 4)));
     }
-    __host__ __device__ static int xdests(int k, bool, int* c, int* e) {
-        const int n = k >> 7, r = k & 127, j = r >> 5, h = (r >> 4) & 1, l = r & 15;
-        c[0] = 2 * n + h;
-        e[0] = 16 * j + l;
-        return 1;
+    __host__ __device__ static int part_elem0(int c, int j, bool) { return 128 * (c >> 1) + 32 * j + 16 * (c & 1); }
+    __host__ __device__ static int item_dest(int kk, bool, int& c, int& p, int& j) {
+        const int n = kk >> 7, r = kk & 127;
+        c = 2 * n + ((r >> 4) & 1); p = r >> 5; j = (r >> 3) & 1; return 1;
     }
-    __host__ __device__ static int part_xblock(int c, int j, bool) { return 4 * (c >> 1) + j; }
-    __host__ __device__ static int part_half(int c, int j, bool) { return 8 * (c >> 1) + 2 * j + (c & 1); }
 
     __device__ static void decode(const uint8_t* b, int c, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
                                   float (&wm)[PARTS]) {
@@ -230,16 +253,15 @@ struct Fmt<Q3_K> {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             w[i] = lds_u32_a2(b + 32 + 32 * n + 16 * h + 4 * i);
-            hm[i] = lds_u32_a2(b + 16 * h + 4 * i);
+            hm[i] = lds_u32_a2(b + 16 * h + 4 * i) >> (4 * n);
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j)
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-                q[4 * j + i] = ((w[i] >> (2 * j)) & 0x03030303u) |
-                               (((hm[i] >> (4 * n + j)) & 0x01010101u) << 2);
+                q[4 * j + i] = ((w[i] >> (2 * j)) & 0x03030303u) | (((hm[i] >> j) & 0x01010101u) << 2);
         const uint32_t t0 = lds_u32_a2(b + 96), t1 = lds_u32_a2(b + 100), t2 = lds_u32_a2(b + 104);
-        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b + 108));
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(b + 108));
         const uint32_t a_lo = q3k_scale_word(2 * n, t0, t1, t2);      // scales 8n .. 8n+3
         const uint32_t a_hi = q3k_scale_word(2 * n + 1, t0, t1, t2);  // scales 8n+4 .. 8n+7
 #pragma unroll
@@ -255,13 +277,14 @@ struct Fmt<Q3_K> {
 // Q4_K: 256 elements, 144 bytes: d @0, dmin @2, scales[12] @4, qs[128] @16.
 // src/tensor.h:329-358.  64-group g: elements 64g + l (l<32) <- qs[32g+l] & 15
 // with (sc, m) pair 2g; elements 64g + 32 + l <- qs[32g+l] >> 4 with pair 2g+1.
-// Unit c = group g: part 0 = low nibbles, part 1 = high nibbles; unit order is
-// block order (elements 64c .. 64c+63).
+// Unit c = group g: part 0 = low nibbles, part 1 = high nibbles kept in place
+// (x16).
 // =============================================================================
 template <>
 struct Fmt<Q4_K> {
-    static constexpr int QK = 256, BB = 144, UPB = 4, UE = 64, PARTS = 2, PE = 32, IOFF = 0;
-    static constexpr bool MIN = true;
+    static constexpr int QK = 256, BB = 144, UPB = 4, UE = 64, PARTS = 2, PE = 32;
+    static constexpr bool MIN = true, QSIGNED = false;
+    __host__ __device__ static constexpr int ioff(int) { return 0; }
 
     __device__ static float dq_elem(const uint8_t* b, int k) {
         const int g = k >> 6, r = k & 63, hi = r >> 5, l = r & 31;
@@ -279,9 +302,10 @@ struct Fmt<Q4_K> {
         const uint32_t qv = hi ? (v >> 4) : (v & 0xF);
         return fsub(fmul(d1, static_cast<float>(qv)), m1);
     }
-    __host__ __device__ static int xdests(int k, bool, int* c, int* e) { c[0] = k >> 6; e[0] = k & 63; return 1; }
-    __host__ __device__ static int part_xblock(int c, int p, bool) { return 2 * c + p; }
-    __host__ __device__ static int part_half(int c, int p, bool) { return 2 * (2 * c + p); }
+    __host__ __device__ static int part_elem0(int c, int p, bool) { return 64 * c + 32 * p; }
+    __host__ __device__ static int item_dest(int kk, bool, int& c, int& p, int& j) {
+        c = kk >> 6; p = (kk >> 5) & 1; j = (kk >> 3) & 3; return 1;
+    }
 
     __device__ static void decode(const uint8_t* b, int c, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
                                   float (&wm)[PARTS]) {
@@ -292,17 +316,16 @@ struct Fmt<Q4_K> {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             q[i] = w[i] & 0x0F0F0F0Fu;
-            q[8 + i] = (w[i] >> 4) & 0x0F0F0F0Fu;
+            q[8 + i] = w[i] & 0xF0F0F0F0u;
         }
-        const float d = half_bits_to_float(hd.x & 0xFFFFu);
-        const float dmin = half_bits_to_float(hd.x >> 16);
+        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hd.x));
         uint32_t sc0, m0, sc1, m1;
-        scale_min_k4(2 * c, hd.y, hd.z, hd.w, sc0, m0);
-        scale_min_k4(2 * c + 1, hd.y, hd.z, hd.w, sc1, m1);
-        wd[0] = d * static_cast<float>(sc0);
-        wm[0] = dmin * static_cast<float>(m0);
-        wd[1] = d * static_cast<float>(sc1);
-        wm[1] = dmin * static_cast<float>(m1);
+        scale_min_k4_unit(c, 0, hd.y, hd.z, hd.w, sc0, m0);
+        scale_min_k4_unit(c, 1, hd.y, hd.z, hd.w, sc1, m1);
+        wd[0] = dm.x * static_cast<float>(sc0);
+        wm[0] = dm.y * static_cast<float>(m0);
+        wd[1] = dm.x * static_cast<float>(sc1) * 0.0625f;
+        wm[1] = dm.y * static_cast<float>(m1);
     }
 };
 
@@ -313,8 +336,9 @@ struct Fmt<Q4_K> {
 // =============================================================================
 template <>
 struct Fmt<Q5_K> {
-    static constexpr int QK = 256, BB = 176, UPB = 4, UE = 64, PARTS = 2, PE = 32, IOFF = 0;
-    static constexpr bool MIN = true;
+    static constexpr int QK = 256, BB = 176, UPB = 4, UE = 64, PARTS = 2, PE = 32;
+    static constexpr bool MIN = true, QSIGNED = false;
+    __host__ __device__ static constexpr int ioff(int) { return 0; }
 
     __device__ static float dq_elem(const uint8_t* b, int k) {
         const int g = k >> 6, r = k & 63, hi = r >> 5, l = r & 31;
@@ -333,9 +357,10 @@ struct Fmt<Q5_K> {
         const uint32_t qv = (hi ? (v >> 4) : (v & 0xF)) + (hb ? 16u : 0u);
         return fsub(fmul(d1, static_cast<float>(qv)), m1);
     }
-    __host__ __device__ static int xdests(int k, bool, int* c, int* e) { c[0] = k >> 6; e[0] = k & 63; return 1; }
-    __host__ __device__ static int part_xblock(int c, int p, bool) { return 2 * c + p; }
-    __host__ __device__ static int part_half(int c, int p, bool) { return 2 * (2 * c + p); }
+    __host__ __device__ static int part_elem0(int c, int p, bool) { return 64 * c + 32 * p; }
+    __host__ __device__ static int item_dest(int kk, bool, int& c, int& p, int& j) {
+        c = kk >> 6; p = (kk >> 5) & 1; j = (kk >> 3) & 3; return 1;
+    }
 
     __device__ static void decode(const uint8_t* b, int c, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
                                   float (&wm)[PARTS]) {
@@ -348,18 +373,18 @@ struct Fmt<Q5_K> {
         const uint32_t qh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            q[i] = (w[i] & 0x0F0F0F0Fu) | (((qh[i] >> (2 * c)) & 0x01010101u) << 4);
-            q[8 + i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * c + 1)) & 0x01010101u) << 4);
+            const uint32_t hb = qh[i] >> (2 * c);
+            q[i] = (w[i] & 0x0F0F0F0Fu) | ((hb & 0x01010101u) << 4);
+            q[8 + i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | ((hb & 0x02020202u) << 3);
         }
-        const float d = half_bits_to_float(hd.x & 0xFFFFu);
-        const float dmin = half_bits_to_float(hd.x >> 16);
+        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hd.x));
         uint32_t sc0, m0, sc1, m1;
-        scale_min_k4(2 * c, hd.y, hd.z, hd.w, sc0, m0);
-        scale_min_k4(2 * c + 1, hd.y, hd.z, hd.w, sc1, m1);
-        wd[0] = d * static_cast<float>(sc0);
-        wm[0] = dmin * static_cast<float>(m0);
-        wd[1] = d * static_cast<float>(sc1);
-        wm[1] = dmin * static_cast<float>(m1);
+        scale_min_k4_unit(c, 0, hd.y, hd.z, hd.w, sc0, m0);
+        scale_min_k4_unit(c, 1, hd.y, hd.z, hd.w, sc1, m1);
+        wd[0] = dm.x * static_cast<float>(sc0);
+        wm[0] = dm.y * static_cast<float>(m0);
+        wd[1] = dm.x * static_cast<float>(sc1);
+        wm[1] = dm.y * static_cast<float>(m1);
     }
 };
 
@@ -373,8 +398,9 @@ struct Fmt<Q5_K> {
 // =============================================================================
 template <>
 struct Fmt<Q6_K> {
-    static constexpr int QK = 256, BB = 210, UPB = 4, UE = 64, PARTS = 4, PE = 16, IOFF = 32;
-    static constexpr bool MIN = false;
+    static constexpr int QK = 256, BB = 210, UPB = 4, UE = 64, PARTS = 4, PE = 16;
+    static constexpr bool MIN = false, QSIGNED = false;
+    __host__ __device__ static constexpr int ioff(int) { return 32; }
 
     __device__ static float dq_elem(const uint8_t* b, int k) {
         const int n = k >> 7, r = k & 127, kk = r >> 5, l = r & 31, is = l >> 4;
@@ -386,14 +412,11 @@ struct Fmt<Q6_K> {
         const int sc = static_cast<int8_t>(ldg_u8(b + 192 + 8 * n + is + 2 * kk));
         return fmul(fmul(d, static_cast<float>(sc)), static_cast<float>(qv));
     }
-    __host__ __device__ static int xdests(int k, bool, int* c, int* e) {
-        const int n = k >> 7, r = k & 127, kk = r >> 5, l = r & 31;
-        c[0] = 2 * n + (l >> 4);
-        e[0] = 16 * kk + (l & 15);
-        return 1;
+    __host__ __device__ static int part_elem0(int c, int k, bool) { return 128 * (c >> 1) + 32 * k + 16 * (c & 1); }
+    __host__ __device__ static int item_dest(int kk, bool, int& c, int& p, int& j) {
+        const int n = kk >> 7, r = kk & 127;
+        c = 2 * n + ((r >> 4) & 1); p = r >> 5; j = (r >> 3) & 1; return 1;
     }
-    __host__ __device__ static int part_xblock(int c, int k, bool) { return 4 * (c >> 1) + k; }
-    __host__ __device__ static int part_half(int c, int k, bool) { return 8 * (c >> 1) + 2 * k + (c & 1); }
 
     __device__ static void decode(const uint8_t* b, int c, uint32_t (&q)[UE / 4], float (&wd)[PARTS],
                                   float (&wm)[PARTS]) {
@@ -407,12 +430,12 @@ struct Fmt<Q6_K> {
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            q[i] = (A[i] & 0x0F0F0F0Fu) | ((H[i] & 0x03030303u) << 4);
-            q[4 + i] = (B[i] & 0x0F0F0F0Fu) | (((H[i] >> 2) & 0x03030303u) << 4);
-            q[8 + i] = ((A[i] >> 4) & 0x0F0F0F0Fu) | (((H[i] >> 4) & 0x03030303u) << 4);
-            q[12 + i] = ((B[i] >> 4) & 0x0F0F0F0Fu) | (((H[i] >> 6) & 0x03030303u) << 4);
+            q[i] = (A[i] & 0x0F0F0F0Fu) | ((H[i] << 4) & 0x30303030u);
+            q[4 + i] = (B[i] & 0x0F0F0F0Fu) | ((H[i] << 2) & 0x30303030u);
+            q[8 + i] = ((A[i] >> 4) & 0x0F0F0F0Fu) | (H[i] & 0x30303030u);
+            q[12 + i] = ((B[i] >> 4) & 0x0F0F0F0Fu) | ((H[i] >> 2) & 0x30303030u);
         }
-        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b + 208));
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(b + 208));
         const uint32_t s_lo = lds_u32_a2(b + 192 + 8 * n);      // sc[8n .. 8n+3]
         const uint32_t s_hi = lds_u32_a2(b + 192 + 8 * n + 4);  // sc[8n+4 .. 8n+7]
 #pragma unroll

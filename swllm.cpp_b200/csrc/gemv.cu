@@ -6,25 +6,36 @@
 // (src/tensor.h:1212).
 //
 // Design (HBM-bound streaming):
-//  * Persistent grid, CTA b owns a contiguous, balanced range of rows.
-//  * Warp 8 is the producer: one lane streams row chunks of raw blocks into a
-//    ring of shared-memory stages with cp.async.bulk (TMA bulk copies, no
-//    multicast, L2 evict-first), completion on per-stage mbarriers.
-//  * Warps 0-7 are consumers, one row per warp per stage.  A lane decodes one
-//    "unit" (32 or 64 elements) from shared memory into packed small integers
-//    and dots it with the activation row re-laid out as 16-bit fixed point
-//    (per-32-element scale) with dp2a; per-part sums are scaled in fp32.
-//  * The activation prep runs once per CTA (x -> shared memory) while the
-//    first weight stages are already in flight.
-//  * Programmatic dependent launch: weights (immutable inputs) are requested
-//    before the previous kernel on the stream has finished; activations are
-//    read only after griddepcontrol.wait.
+//  * Persistent grid of one CTA per SM; CTA b owns a contiguous, balanced range
+//    of rows.  Shared memory per CTA stays under half an SM so the CTAs of the
+//    next kernel on the stream (programmatic dependent launch) fit beside it
+//    and start streaming their weights while this one finishes.
+//  * Last warp = producer: one lane moves raw blocks into shared-memory stages
+//    with the TMA -- one 1-D bulk copy per stage of whole rows, or one 2-D
+//    tensor-map copy per stage of row chunks (no multicast, L2 evict-first)
+//    -- completing on per-stage mbarriers.  Weights are requested before
+//    griddepcontrol.wait (they are immutable inputs).  When a CTA's rows fit
+//    in shared memory every stage gets its own slot and all of them are in
+//    flight at once.
+//  * NCW consumer warps, one or two rows per warp per stage (two rows share
+//    each activation load and run two dot-product chains side by side).  A
+//    lane owns one unit (32 or 64 elements): it decodes the quant bits into
+//    packed small integers and dots each part with the activation row, held
+//    in shared memory as 16-bit fixed point (per-32-element scale), with dp2a.
+//  * The activation prep runs once per CTA after griddepcontrol.wait into a
+//    unit-chunk-major layout: for each group of 32 consecutive units, chunk j
+//    of all 32 units is one contiguous 512-byte plane, so a lane's loads are
+//    base + compile-time offsets and a warp's loads never conflict on banks.
+//    Each (unit, part) also gets its activation scale and integer sum.
 //  * Every wait is bounded; on timeout the kernel records it in the device
 //    status word, drains its own copies and returns.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cstdint>
+#include <cstring>
+#include <mutex>
 #include <numeric>
 
 #include "formats.cuh"
@@ -33,59 +44,198 @@
 
 namespace swq {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
+enum : int { MODE_PLAIN = 0, MODE_BULK_ROWS = 1, MODE_TMAP = 2 };
 
 struct GemvParams {
     const uint8_t* W;
     const float* X;
     float* Y;
     int M, N, K;
-    int nb;            // blocks per row
-    int row_bytes;     // nb * BB
-    int KC;            // blocks per chunk
-    int nchunks;       // chunks per row
-    int row_stride;    // bytes between rows inside a stage (16-aligned)
-    int stage_bytes;   // kConsumerWarps * row_stride
+    int nb;           // blocks per row
+    int row_bytes;    // nb * BB
+    int KC;           // blocks per chunk
+    int nchunks;      // chunks per row
+    int row_stride;   // bytes between rows inside a stage
+    int rg;           // rows per stage
+    int stage_bytes;  // rg * row_stride, 16-aligned
     int stages;
-    int bulk;          // 1: cp.async.bulk producer; 0: plain-load producer
-    int refcpu;        // Q2_K reference-CPU activation order
-    int early;         // weight prefetch before griddepcontrol.wait
-    int x_vec;         // X is 16-byte aligned: float4 activation loads
-    uint32_t off_xrec, off_xs, off_is, off_sx, off_h16, off_ring;  // smem offsets
+    int mode;    // MODE_*
+    int refcpu;  // Q2_K reference-CPU activation order
+    int early;   // weight prefetch before griddepcontrol.wait
+    int x_vec;   // X rows 16-byte aligned: float4 activation loads
+    int xstride; // bytes per activation row in shared memory
+    uint32_t off_xq, off_ring;  // smem offsets
 };
 
-// Layout helpers for the activation records.
+// dp2a with a signed 16-bit pair and four 8-bit values, unsigned or signed.
+template <bool SIGNED>
+__device__ __forceinline__ int dp2a_lo(int a, uint32_t b, int c) {
+    int d;
+    if (SIGNED) asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    else asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+template <bool SIGNED>
+__device__ __forceinline__ int dp2a_hi(int a, uint32_t b, int c) {
+    int d;
+    if (SIGNED) asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    else asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// 2-D tiled TMA load of a box of the weight bytes (tensor map over 8-byte
+// elements: inner = row bytes / 8, outer = rows).  No multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
+// Activation layout in shared memory, per activation row: units in groups of
+// 32; a group holds CPU chunk planes (32 x 16 B each: 8 int16 values of one
+// unit) then PARTS meta planes (32 x 8 B each: scale bits, integer sum).
 template <int T>
-struct XLayout {
+struct XLay {
     using F = Fmt<T>;
-    static constexpr int C = F::UE / 8;  // 16-byte chunks per unit record
-    static constexpr int L = 8 / C;      // records per 128-byte line
-    __device__ static int rot(int u) { return (u / L) & (C - 1); }
+    static constexpr int CPU = F::UE / 8;                         // chunks per unit
+    static constexpr int CPP = F::PE / 8;                         // chunks per part
+    static constexpr int GB = 32 * (F::UE * 2 + F::PARTS * 8);    // bytes per group
+    static constexpr int META = 32 * 16 * CPU;                    // offset of the meta planes
+    __host__ __device__ static int row_bytes(int K) { return ((K / F::UE + 31) / 32) * GB; }
+    __device__ static uint32_t chunk_off(int u) { return (u >> 5) * GB + (u & 31) * 16; }
+    __device__ static uint32_t meta_off(int u) { return (u >> 5) * GB + META + (u & 31) * 8; }
 };
+
+// Consumer warps per CTA for a padded activation-row count.
+template <int MT>
+struct Cfg {
+    static constexpr int NCW = MT <= 2 ? 12 : 8;
+    static constexpr int RPW = MT == 1 ? 2 : 1;  // rows per consumer warp per stage
+    static constexpr int RGMAX = NCW * RPW;      // rows per stage at most
+    static constexpr int THREADS = (NCW + 1) * 32;
+};
+
+// One unit of one row: decode the quant bits, dot every part with every
+// activation row, add into acc.
+template <int T, int MT>
+__device__ __forceinline__ void unit_dot(const uint8_t* blk, int c, int u, const uint8_t* xq, int xstride,
+                                         float (&acc)[MT]) {
+    using F = Fmt<T>;
+    using XL = XLay<T>;
+    constexpr int NW = F::UE / 4, WPP = NW / F::PARTS;
+    uint32_t q[NW];
+    float wd[F::PARTS], wm[F::PARTS];
+    F::decode(blk, c, q, wd, wm);
+    const uint32_t co = XL::chunk_off(u), mo = XL::meta_off(u);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        const uint8_t* xg = xq + static_cast<size_t>(m) * xstride + co;
+        const uint8_t* xm = xq + static_cast<size_t>(m) * xstride + mo;
+#pragma unroll
+        for (int pt = 0; pt < F::PARTS; ++pt) {
+            const int2 mt = *reinterpret_cast<const int2*>(xm + pt * 256);
+            int S0 = 0, S1 = 0;
+#pragma unroll
+            for (int j = 0; j < XL::CPP; ++j) {
+                const uint4 v = lds_u128(xg + (pt * XL::CPP + j) * 512);
+                const uint32_t w0 = q[pt * WPP + 2 * j], w1 = q[pt * WPP + 2 * j + 1];
+                S0 = dp2a_lo<F::QSIGNED>(static_cast<int>(v.x), w0, S0);
+                S1 = dp2a_hi<F::QSIGNED>(static_cast<int>(v.y), w0, S1);
+                S0 = dp2a_lo<F::QSIGNED>(static_cast<int>(v.z), w1, S0);
+                S1 = dp2a_hi<F::QSIGNED>(static_cast<int>(v.w), w1, S1);
+            }
+            float t = wd[pt] * static_cast<float>(S0 + S1 - F::ioff(pt) * mt.y);
+            if (F::MIN) t = fmaf(-wm[pt], static_cast<float>(mt.y), t);
+            acc[m] = fmaf(__int_as_float(mt.x), t, acc[m]);
+        }
+    }
+}
+
+// The same unit position in two rows: the activation loads are shared and
+// the two dot-product chains run side by side.
+template <int T, int MT>
+__device__ __forceinline__ void unit_dot2(const uint8_t* blkA, const uint8_t* blkB, int c, int u,
+                                          const uint8_t* xq, int xstride, float (&accA)[MT], float (&accB)[MT]) {
+    using F = Fmt<T>;
+    using XL = XLay<T>;
+    constexpr int NW = F::UE / 4, WPP = NW / F::PARTS;
+    uint32_t qa[NW], qb[NW];
+    float wda[F::PARTS], wma[F::PARTS], wdb[F::PARTS], wmb[F::PARTS];
+    F::decode(blkA, c, qa, wda, wma);
+    F::decode(blkB, c, qb, wdb, wmb);
+    const uint32_t co = XL::chunk_off(u), mo = XL::meta_off(u);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        const uint8_t* xg = xq + static_cast<size_t>(m) * xstride + co;
+        const uint8_t* xm = xq + static_cast<size_t>(m) * xstride + mo;
+#pragma unroll
+        for (int pt = 0; pt < F::PARTS; ++pt) {
+            const int2 mt = *reinterpret_cast<const int2*>(xm + pt * 256);
+            int A0 = 0, A1 = 0, B0 = 0, B1 = 0;
+#pragma unroll
+            for (int j = 0; j < XL::CPP; ++j) {
+                const uint4 v = lds_u128(xg + (pt * XL::CPP + j) * 512);
+                const uint32_t a0 = qa[pt * WPP + 2 * j], a1 = qa[pt * WPP + 2 * j + 1];
+                const uint32_t b0 = qb[pt * WPP + 2 * j], b1 = qb[pt * WPP + 2 * j + 1];
+                A0 = dp2a_lo<F::QSIGNED>(static_cast<int>(v.x), a0, A0);
+                B0 = dp2a_lo<F::QSIGNED>(static_cast<int>(v.x), b0, B0);
+                A1 = dp2a_hi<F::QSIGNED>(static_cast<int>(v.y), a0, A1);
+                B1 = dp2a_hi<F::QSIGNED>(static_cast<int>(v.y), b0, B1);
+                A0 = dp2a_lo<F::QSIGNED>(static_cast<int>(v.z), a1, A0);
+                B0 = dp2a_lo<F::QSIGNED>(static_cast<int>(v.z), b1, B0);
+                A1 = dp2a_hi<F::QSIGNED>(static_cast<int>(v.w), a1, A1);
+                B1 = dp2a_hi<F::QSIGNED>(static_cast<int>(v.w), b1, B1);
+            }
+            const float xs = __int_as_float(mt.x);
+            const int I = mt.y;
+            float ta = wda[pt] * static_cast<float>(A0 + A1 - F::ioff(pt) * I);
+            float tb = wdb[pt] * static_cast<float>(B0 + B1 - F::ioff(pt) * I);
+            if (F::MIN) {
+                ta = fmaf(-wma[pt], static_cast<float>(I), ta);
+                tb = fmaf(-wmb[pt], static_cast<float>(I), tb);
+            }
+            accA[m] = fmaf(xs, ta, accA[m]);
+            accB[m] = fmaf(xs, tb, accB[m]);
+        }
+    }
+}
+
+template <int MT>
+__device__ __forceinline__ void row_store(float (&acc)[MT], int lane, float* Y, int M, int N, int row) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        float v = acc[m];
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        if (lane == 0 && m < M) Y[static_cast<size_t>(m) * N + row] = v;
+        acc[m] = 0.f;
+    }
+}
 
 template <int T, int MT>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
+    gemv_kernel(const GemvParams p, const __grid_constant__ CUtensorMap tmap) {
     using F = Fmt<T>;
-    using XL = XLayout<T>;
-    constexpr int UE = F::UE, PARTS = F::PARTS, UPB = F::UPB, QK = F::QK, BB = F::BB;
-    constexpr int NW = UE / 4;  // q words per unit
+    using XL = XLay<T>;
+    constexpr int NCW = Cfg<MT>::NCW;
+    constexpr int UPB = F::UPB, QK = F::QK, BB = F::BB, PE = F::PE;
 
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + p.stages;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + p.stages);
-    uint8_t* xrec = smem + p.off_xrec;
-    float* xs_arr = reinterpret_cast<float*>(smem + p.off_xs);
-    int* is_arr = reinterpret_cast<int*>(smem + p.off_is);
-    float* sx = reinterpret_cast<float*>(smem + p.off_sx);
-    int* h16 = reinterpret_cast<int*>(smem + p.off_h16);
+    uint8_t* xq = smem + p.off_xq;
     uint8_t* ring = smem + p.off_ring;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int units = p.K / UE;  // units per row
+    const int RG = p.rg;
 
-    // Balanced contiguous row range of this CTA.
     const int G = gridDim.x, b = blockIdx.x;
     const int rlo = p.N / G, rex = p.N % G;
     const int r_begin = b * rlo + min(b, rex);
@@ -94,7 +244,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
+            mbar_init(&empty[s], NCW);
         }
         *abort_flag = 0;
         mbar_fence_init();
@@ -102,14 +252,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
     __syncthreads();
     pdl_launch_dependents();
 
-    if (warp == kConsumerWarps) {
+    if (warp == NCW) {
         // ------------------------------------------------------------ producer
         if (!p.early) pdl_wait_primary();
         const uint64_t pol = l2_policy_evict_first();
         int it = 0;
         bool ok = true;
-        for (int rg = r_begin; rg < r_end && ok; rg += kConsumerWarps) {
-            const int rows = min(kConsumerWarps, r_end - rg);
+        for (int rg = r_begin; rg < r_end && ok; rg += RG) {
+            const int rows = min(RG, r_end - rg);
             for (int ch = 0; ch < p.nchunks; ++ch, ++it) {
                 const int s = it % p.stages;
                 if (it >= p.stages) {
@@ -124,20 +274,20 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
                 const int kc = min(p.KC, p.nb - kb0);
                 const uint32_t bytes_row = static_cast<uint32_t>(kc * BB);
                 uint8_t* dst = ring + static_cast<size_t>(s) * p.stage_bytes;
-                const uint8_t* src = p.W + static_cast<size_t>(rg) * p.row_bytes +
-                                     static_cast<size_t>(kb0) * BB;
-                if (p.bulk) {
+                if (p.mode == MODE_TMAP) {
                     if (lane == 0) {
+                        // the box is always full: RG rows x KC blocks (rows past N read zeros)
+                        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(p.KC * BB * RG));
+                        tma_load_2d(dst, &tmap, kb0 * BB / 8, rg, &full[s], pol);
+                    }
+                } else if (p.mode == MODE_BULK_ROWS) {
+                    if (lane == 0) {
+                        const uint8_t* src = p.W + static_cast<size_t>(rg) * p.row_bytes;
                         mbar_arrive_expect_tx(&full[s], bytes_row * rows);
-                        if (p.nchunks == 1) {
-                            bulk_g2s(dst, src, bytes_row * rows, &full[s], pol);
-                        } else {
-                            for (int r = 0; r < rows; ++r)
-                                bulk_g2s(dst + r * p.row_stride, src + static_cast<size_t>(r) * p.row_bytes,
-                                         bytes_row, &full[s], pol);
-                        }
+                        bulk_g2s(dst, src, bytes_row * rows, &full[s], pol);
                     }
                 } else {
+                    const uint8_t* src = p.W + static_cast<size_t>(rg) * p.row_bytes + static_cast<size_t>(kb0) * BB;
                     for (int r = 0; r < rows; ++r) {
                         const uint8_t* sr = src + static_cast<size_t>(r) * p.row_bytes;
                         uint8_t* dr = dst + r * p.row_stride;
@@ -148,11 +298,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
                 }
             }
         }
-        // Drain: make sure no bulk copy of this CTA is still writing shared memory.
-        if (p.bulk && lane == 0) {
+        if (p.mode != MODE_PLAIN && lane == 0) {
+            // Drain: no TMA copy of this CTA may still be writing shared memory.
             const int issued = it;
             for (int s = 0; s < p.stages && s < issued; ++s) {
-                const int last = issued - 1 - ((issued - 1 - s) % p.stages);  // last iteration on stage s
+                const int last = issued - 1 - ((issued - 1 - s) % p.stages);
                 mbar_wait_bounded(&full[s], (last / p.stages) & 1, DEV_TIMEOUT_DRAIN);
             }
         }
@@ -161,165 +311,172 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
 
     // ---------------------------------------------------------------- consumers
     pdl_wait_primary();
-    const int ctid = threadIdx.x;  // 0 .. 255
-    constexpr int NCT = kConsumerWarps * 32;
+    constexpr int NCT = NCW * 32;
+    const int ctid = threadIdx.x;
+    const bool refcpu = p.refcpu != 0;
 
-    // Phase A: per 32-element block scale, 16-bit fixed point, per-16 sums;
-    // scatter the fixed-point values into unit-order records.
+    // Activation prep: item = 8 consecutive elements of one row (one 16-byte
+    // chunk of one unit part).  Four lanes hold one 32-element block (scale);
+    // PE/8 lanes one part (integer sum).  Loads for two items per thread are
+    // issued before any arithmetic.
     {
-        const int k4 = p.K / 4;
-        const int total = MT * k4;
-        for (int f0 = 0; f0 < total; f0 += NCT) {
-            const int f = f0 + ctid;  // total is a multiple of 8 (K % 32 == 0)
-            const bool act = f < total;
-            const int m = act ? f / k4 : 0;
-            const int kk = act ? (f - m * k4) * 4 : 0;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (act && m < p.M) {
-                const float* xp = p.X + static_cast<size_t>(m) * p.K + kk;
-                if (p.x_vec) {
-                    v = __ldg(reinterpret_cast<const float4*>(xp));
-                } else {
-                    v.x = __ldg(xp);
-                    v.y = __ldg(xp + 1);
-                    v.z = __ldg(xp + 2);
-                    v.w = __ldg(xp + 3);
+        const int ipr = p.K / 8;  // items per row (multiple of 4)
+        const int items = MT * ipr;
+        for (int base = 0; base < items; base += 2 * NCT) {
+            float v[2][8];
+            int mm[2], kk[2];
+            bool act[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int it = base + h * NCT + ctid;
+                act[h] = it < items;
+                mm[h] = (MT == 1 || !act[h]) ? 0 : it / ipr;
+                kk[h] = act[h] ? (it - mm[h] * ipr) * 8 : 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[h][i] = 0.f;
+                if (act[h] && mm[h] < p.M) {
+                    const float* xp = p.X + static_cast<size_t>(mm[h]) * p.K + kk[h];
+                    if (p.x_vec) {
+                        const float4 a = __ldg(reinterpret_cast<const float4*>(xp));
+                        const float4 c = __ldg(reinterpret_cast<const float4*>(xp + 4));
+                        v[h][0] = a.x; v[h][1] = a.y; v[h][2] = a.z; v[h][3] = a.w;
+                        v[h][4] = c.x; v[h][5] = c.y; v[h][6] = c.z; v[h][7] = c.w;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[h][i] = __ldg(xp + i);
+                    }
                 }
             }
-            float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-            a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
-            a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
-            a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
-            const float inv = a > 0.f ? 32767.0f / a : 0.f;
-            const float sc = a > 0.f ? a * (1.0f / 32767.0f) : 0.f;
-            int xi[4];
-            xi[0] = __float2int_rn(v.x * inv);
-            xi[1] = __float2int_rn(v.y * inv);
-            xi[2] = __float2int_rn(v.z * inv);
-            xi[3] = __float2int_rn(v.w * inv);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) xi[i] = max(-32767, min(32767, xi[i]));
-            int s16 = xi[0] + xi[1] + xi[2] + xi[3];
-            s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
-            s16 += __shfl_xor_sync(0xffffffffu, s16, 2);
-            if (act) {
-                if ((lane & 7) == 0) sx[m * (p.K / 32) + kk / 32] = sc;
-                if ((lane & 3) == 0) h16[m * (p.K / 16) + kk / 16] = s16;
+            for (int h = 0; h < 2; ++h) {
+                float a = 0.f;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int k = kk + i;
-                    const int kb = k / QK, kq = k % QK;
-                    int cs[4], es[4];
-                    const int nd = F::xdests(kq, p.refcpu != 0, cs, es);
-                    for (int t = 0; t < nd; ++t) {
-                        const int u = kb * UPB + cs[t];
-                        const int e = es[t];
-                        const int phys = ((e >> 3) + XL::rot(u)) & (XL::C - 1);
-                        int16_t* rec = reinterpret_cast<int16_t*>(
-                            xrec + (static_cast<size_t>(m) * units + u) * (2 * UE));
-                        rec[phys * 8 + (e & 7)] = static_cast<int16_t>(xi[i]);
+                for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[h][i]));
+                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+                // |v| <= a, so |v * inv| <= 32767 (to within the approximate
+                // reciprocal) and rounds into the int16 range.
+                const bool live = a > 1e-30f;
+                const float inv = live ? __fdividef(32767.0f, a) : 0.f;
+                // |v * inv| <= 32767: adding 1.5 * 2^23 rounds to the nearest integer
+                // in the low mantissa bits (exact, ties to even).
+                int xi[8], sum = 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    xi[i] = __float_as_int(fmaf(v[h][i], inv, 12582912.0f)) - 0x4B400000;
+                    sum += xi[i];
+                }
+                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                if (PE == 32) sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                if (act[h]) {
+                    uint4 pk;
+                    pk.x = __byte_perm(xi[0], xi[1], 0x5410);
+                    pk.y = __byte_perm(xi[2], xi[3], 0x5410);
+                    pk.z = __byte_perm(xi[4], xi[5], 0x5410);
+                    pk.w = __byte_perm(xi[6], xi[7], 0x5410);
+                    const float sc = live ? a * (1.0f / 32767.0f) : 0.f;
+                    const int kb = kk[h] / QK, kq = kk[h] - kb * QK;
+                    int c, p0, j;
+                    const int np = F::item_dest(kq, refcpu, c, p0, j);
+                    uint8_t* xrow = xq + static_cast<size_t>(mm[h]) * p.xstride;
+                    const int u = kb * UPB + c;
+                    for (int t = 0; t < np; ++t) {
+                        *reinterpret_cast<uint4*>(xrow + XL::chunk_off(u) + ((p0 + t) * XL::CPP + j) * 512) = pk;
+                        if (j == 0)
+                            *reinterpret_cast<int2*>(xrow + XL::meta_off(u) + (p0 + t) * 256) =
+                                make_int2(__float_as_int(sc), sum);
                     }
                 }
             }
         }
     }
     named_bar_sync(1, NCT);
-    // Phase B: per (m, unit, part) activation scale and integer sum.
-    {
-        const int total = MT * units * PARTS;
-        for (int t = ctid; t < total; t += NCT) {
-            const int m = t / (units * PARTS);
-            const int r = t - m * units * PARTS;
-            const int u = r / PARTS, part = r % PARTS;
-            const int kb = u / UPB, c = u % UPB;
-            const int xb = kb * (QK / 32) + F::part_xblock(c, part, p.refcpu != 0);
-            const int hb = kb * (QK / 16) + F::part_half(c, part, p.refcpu != 0);
-            int isum = h16[m * (p.K / 16) + hb];
-            if (F::PE == 32) isum += h16[m * (p.K / 16) + hb + 1];
-            xs_arr[t] = sx[m * (p.K / 32) + xb];
-            is_arr[t] = isum;
-        }
-    }
-    named_bar_sync(1, NCT);
 
-    float acc[MT];
+    float accA[MT], accB[MT];
 #pragma unroll
-    for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+    for (int m = 0; m < MT; ++m) accA[m] = accB[m] = 0.f;
 
-    int it = 0;
+    int s = 0;
+    uint32_t phase = 0;
     bool ok = true;
-    for (int rg = r_begin; rg < r_end && ok; rg += kConsumerWarps) {
-        const int rows = min(kConsumerWarps, r_end - rg);
-        for (int ch = 0; ch < p.nchunks; ++ch, ++it) {
-            const int s = it % p.stages;
-            if (!mbar_wait_bounded(&full[s], (it / p.stages) & 1, DEV_TIMEOUT_FULL) || *abort_flag) {
+    if (p.nchunks == 1) {
+        // Whole rows per stage: warp w takes rows w, w + NCW, w + 2 NCW, ... of
+        // the stage, two at a time, and stores each result right away.
+        for (int rg = r_begin; rg < r_end && ok; rg += RG) {
+            const int rows = min(RG, r_end - rg);
+            if (!mbar_wait_bounded(&full[s], phase, DEV_TIMEOUT_FULL) || *abort_flag) {
                 *abort_flag = 1;
                 ok = false;
                 break;
             }
-            if (warp < rows) {
-                const int kb0 = ch * p.KC;
-                const int kc = min(p.KC, p.nb - kb0);
-                const uint8_t* rowp = ring + static_cast<size_t>(s) * p.stage_bytes + warp * p.row_stride;
-                const int nu = kc * UPB;
-                for (int uu = lane; uu < nu; uu += 32) {
-                    const int kbl = uu / UPB, c = uu - kbl * UPB;
-                    uint32_t q[NW];
-                    float wd[PARTS], wm[PARTS];
-                    F::decode(rowp + kbl * BB, c, q, wd, wm);
-                    const int u = (kb0 + kbl) * UPB + c;
-                    const int rot = XL::rot(u);
-#pragma unroll
-                    for (int m = 0; m < MT; ++m) {
-                        const uint8_t* rec = xrec + (static_cast<size_t>(m) * units + u) * (2 * UE);
-                        uint32_t P[UE / 2];
-#pragma unroll
-                        for (int j = 0; j < XL::C; ++j) {
-                            const uint4 v = lds_u128(rec + 16 * ((j + rot) & (XL::C - 1)));
-                            P[4 * j + 0] = v.x;
-                            P[4 * j + 1] = v.y;
-                            P[4 * j + 2] = v.z;
-                            P[4 * j + 3] = v.w;
-                        }
-                        const int mi = (m * units + u) * PARTS;
-                        float a = acc[m];
-#pragma unroll
-                        for (int pt = 0; pt < PARTS; ++pt) {
-                            constexpr int WPP = NW / PARTS;  // q words per part
-                            int S = 0;
-#pragma unroll
-                            for (int w = 0; w < WPP; ++w) {
-                                const int wi = pt * WPP + w;
-                                S = __dp2a_lo(static_cast<int>(P[2 * wi]), static_cast<int>(q[wi]), S);
-                                S = __dp2a_hi(static_cast<int>(P[2 * wi + 1]), static_cast<int>(q[wi]), S);
-                            }
-                            const float xsv = xs_arr[mi + pt];
-                            const int I = is_arr[mi + pt];
-                            float t = wd[pt] * static_cast<float>(S - F::IOFF * I);
-                            if (F::MIN) t = fmaf(-wm[pt], static_cast<float>(I), t);
-                            a = fmaf(xsv, t, a);
-                        }
-                        acc[m] = a;
+            const int nu = p.nb * UPB;
+            const uint8_t* stage = ring + static_cast<size_t>(s) * p.stage_bytes;
+            for (int r0 = warp; r0 < rows; r0 += 2 * NCW) {
+                const uint8_t* rowA = stage + r0 * p.row_stride;
+                if (r0 + NCW < rows) {
+                    const uint8_t* rowB = rowA + NCW * p.row_stride;
+                    for (int uu = lane; uu < nu; uu += 32) {
+                        const int kbl = uu / UPB, c = uu - kbl * UPB;
+                        unit_dot2<T, MT>(rowA + kbl * BB, rowB + kbl * BB, c, uu, xq, p.xstride, accA, accB);
                     }
+                    row_store<MT>(accA, lane, p.Y, p.M, p.N, rg + r0);
+                    row_store<MT>(accB, lane, p.Y, p.M, p.N, rg + r0 + NCW);
+                } else {
+#pragma unroll 2
+                    for (int uu = lane; uu < nu; uu += 32) {
+                        const int kbl = uu / UPB, c = uu - kbl * UPB;
+                        unit_dot<T, MT>(rowA + kbl * BB, c, uu, xq, p.xstride, accA);
+                    }
+                    row_store<MT>(accA, lane, p.Y, p.M, p.N, rg + r0);
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
-        }
-        if (!ok) break;
-        if (warp < rows) {
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                float v = acc[m];
-                v += __shfl_xor_sync(0xffffffffu, v, 16);
-                v += __shfl_xor_sync(0xffffffffu, v, 8);
-                v += __shfl_xor_sync(0xffffffffu, v, 4);
-                v += __shfl_xor_sync(0xffffffffu, v, 2);
-                v += __shfl_xor_sync(0xffffffffu, v, 1);
-                if (lane == 0 && m < p.M) p.Y[static_cast<size_t>(m) * p.N + rg + warp] = v;
-                acc[m] = 0.f;
+            if (++s == p.stages) {
+                s = 0;
+                phase ^= 1u;
             }
         }
+        return;
+    }
+    // Row chunks: each warp keeps its (at most two) rows across the chunks.
+    for (int rg = r_begin; rg < r_end && ok; rg += RG) {
+        const int rows = min(RG, r_end - rg);
+        const bool hasA = warp < rows, hasB = warp + NCW < rows;
+        for (int ch = 0; ch < p.nchunks; ++ch) {
+            if (!mbar_wait_bounded(&full[s], phase, DEV_TIMEOUT_FULL) || *abort_flag) {
+                *abort_flag = 1;
+                ok = false;
+                break;
+            }
+            const int kb0 = ch * p.KC;
+            const int kc = min(p.KC, p.nb - kb0);
+            const int nu = kc * UPB;
+            const uint8_t* stage = ring + static_cast<size_t>(s) * p.stage_bytes;
+            const uint8_t* rowA = stage + warp * p.row_stride;
+            const uint8_t* rowB = stage + (warp + NCW) * p.row_stride;
+            if (hasB) {
+                for (int uu = lane; uu < nu; uu += 32) {
+                    const int kbl = uu / UPB, c = uu - kbl * UPB;
+                    unit_dot2<T, MT>(rowA + kbl * BB, rowB + kbl * BB, c, kb0 * UPB + uu, xq, p.xstride, accA, accB);
+                }
+            } else if (hasA) {
+#pragma unroll 2
+                for (int uu = lane; uu < nu; uu += 32) {
+                    const int kbl = uu / UPB, c = uu - kbl * UPB;
+                    unit_dot<T, MT>(rowA + kbl * BB, c, kb0 * UPB + uu, xq, p.xstride, accA);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == p.stages) {
+                s = 0;
+                phase ^= 1u;
+            }
+        }
+        if (!ok) break;
+        if (hasA) row_store<MT>(accA, lane, p.Y, p.M, p.N, rg + warp);
+        if (hasB) row_store<MT>(accB, lane, p.Y, p.M, p.N, rg + warp + NCW);
     }
 }
 
@@ -327,23 +484,34 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
 // Host side
 // ---------------------------------------------------------------------------
 
+static inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
 template <int T>
-static size_t x_bytes(int MT, int K) {
-    using F = Fmt<T>;
-    const size_t units = K / F::UE;
-    size_t b = 0;
-    b += static_cast<size_t>(MT) * units * 2 * F::UE;          // records
-    b += static_cast<size_t>(MT) * units * F::PARTS * 4 * 2;   // xs + isum
-    b += static_cast<size_t>(MT) * (K / 32) * 4;               // sx
-    b += static_cast<size_t>(MT) * (K / 16) * 4;               // h16
-    return b;
+static uint32_t x_area_bytes_t(int MT, int K) {
+    return static_cast<uint32_t>(MT) * static_cast<uint32_t>(XLay<T>::row_bytes(K));
 }
 
-static inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    });
+    return fn;
+}
 
 template <int T, int MT>
 static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
     using F = Fmt<T>;
+    constexpr int RGMAX = Cfg<MT>::RGMAX;
     GemvParams p{};
     p.W = static_cast<const uint8_t*>(L.W);
     p.X = L.X;
@@ -355,78 +523,130 @@ static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
     p.row_bytes = p.nb * F::BB;
     p.refcpu = L.refcpu;
     p.early = L.early;
-    // every row start is then 16-byte aligned too (K % 32 == 0)
-    p.x_vec = (reinterpret_cast<uintptr_t>(L.X) & 15u) == 0 ? 1 : 0;
+    p.x_vec = (reinterpret_cast<uintptr_t>(L.X) & 15u) == 0 ? 1 : 0;  // K % 32 keeps rows aligned
+    p.xstride = XLay<T>::row_bytes(L.K);
 
-    const bool base_al = (reinterpret_cast<uintptr_t>(L.W) & 15u) == 0;
-    p.bulk = (base_al && (p.row_bytes % 16) == 0) ? 1 : 0;
+    const int grid = std::max(1, std::min(L.num_sms, L.N));
+    const int rows_cta = (L.N + grid - 1) / grid;
 
-    // Blocks per chunk: a multiple of the count that keeps chunk starts
-    // 16-byte aligned, with stages near kStageTarget bytes.
-    const int al_blocks = 16 / std::gcd(F::BB, 16);
-    const int kStageTarget = 24 * 1024;
-    int KC = kStageTarget / (kConsumerWarps * F::BB);
-    KC = std::max(al_blocks, KC / al_blocks * al_blocks);
-    if (KC >= p.nb) KC = p.nb;
-    p.KC = KC;
-    p.nchunks = (p.nb + KC - 1) / KC;
-    p.row_stride = static_cast<int>(align_up(static_cast<uint32_t>(KC * F::BB), 16));
-    p.stage_bytes = kConsumerWarps * p.row_stride;
-
-    // Shared memory: barriers | x records | xs | isum | sx | h16 | ring.
-    const int units = L.K / F::UE;
-    uint32_t off = 0;
-    off += 2 * 16 * 8 + 16;  // up to 16 stages x 2 barriers + abort flag
+    // Shared memory: barriers | activations | ring.
+    uint32_t off = 2 * 16 * 8 + 16;
     off = align_up(off, 128);
-    p.off_xrec = off;
-    off += static_cast<uint32_t>(MT) * units * 2 * F::UE;
-    p.off_xs = off;
-    off += static_cast<uint32_t>(MT) * units * F::PARTS * 4;
-    p.off_is = off;
-    off += static_cast<uint32_t>(MT) * units * F::PARTS * 4;
-    p.off_sx = off;
-    off += static_cast<uint32_t>(MT) * (L.K / 32) * 4;
-    p.off_h16 = off;
-    off += static_cast<uint32_t>(MT) * (L.K / 16) * 4;
+    p.off_xq = off;
+    off += x_area_bytes_t<T>(MT, L.K);
     off = align_up(off, 128);
     p.off_ring = off;
-
     const uint32_t smem_cap = static_cast<uint32_t>(L.smem_per_block_optin);
-    const uint32_t sm_total = static_cast<uint32_t>(L.smem_per_sm);
-    if (off + 2u * p.stage_bytes > smem_cap) return cudaErrorInvalidConfiguration;
-    // Prefer two CTAs per SM with >= 3 stages, else one CTA with up to 8.
-    int ctas_per_sm = 1;
-    int stages = static_cast<int>((smem_cap - off) / p.stage_bytes);
-    const uint32_t half = sm_total / 2 - 1024;  // per-CTA budget at 2 CTAs/SM
-    if (half > off && static_cast<int>((half - off) / p.stage_bytes) >= 3) {
-        ctas_per_sm = 2;
-        stages = static_cast<int>((half - off) / p.stage_bytes);
+    // Two CTAs per SM: this kernel's and the next one's.
+    const uint32_t half_sm = static_cast<uint32_t>(L.smem_per_sm) / 2 - 1024;
+    const uint32_t budget = (off + 32 * 1024 <= half_sm) ? half_sm : smem_cap;
+    if (off >= budget) return cudaErrorInvalidConfiguration;
+    const uint32_t ring_cap = budget - off;
+
+    const bool aligned = (reinterpret_cast<uintptr_t>(L.W) & 15u) == 0 && (p.row_bytes % 16) == 0;
+    const int al_blocks = 16 / std::gcd(F::BB, 16);
+    constexpr uint32_t kStageCap = 96 * 1024;
+    bool chosen = false;
+    CUtensorMap tmap;
+    std::memset(&tmap, 0, sizeof(tmap));
+
+    if (aligned) {
+        // Whole rows, one contiguous bulk copy per stage; every stage its own
+        // slot when the CTA's rows fit (then usually a single stage).
+        constexpr int kRowsMax = 4 * Cfg<MT>::NCW;
+        const int min_rows = std::min(rows_cta, Cfg<MT>::NCW);  // at least one row per warp
+        for (int ngroups = (rows_cta + kRowsMax - 1) / kRowsMax; ngroups <= rows_cta; ++ngroups) {
+            const int rg = (rows_cta + ngroups - 1) / ngroups;
+            if (rg < min_rows) break;
+            const uint32_t sb = static_cast<uint32_t>(rg) * p.row_bytes;
+            if (sb > kStageCap) continue;
+            int stages;
+            if (ngroups <= 8 && static_cast<uint32_t>(ngroups) * sb <= ring_cap)
+                stages = ngroups;  // resident: every row group in flight at once
+            else if (2 * sb <= ring_cap)
+                stages = std::min<int>(static_cast<int>(ring_cap / sb), 8);
+            else
+                continue;
+            p.mode = MODE_BULK_ROWS;
+            p.KC = p.nb;
+            p.nchunks = 1;
+            p.rg = rg;
+            p.row_stride = p.row_bytes;
+            p.stage_bytes = static_cast<int>(sb);
+            p.stages = stages;
+            chosen = true;
+            break;
+        }
+        // Row chunks through a 2-D tensor map (box inner <= 256 x 8 bytes).
+        EncodeTiledFn enc = chosen ? nullptr : encode_fn();
+        if (!chosen && enc && (p.row_bytes % 8) == 0) {
+            int KC = std::min(2048 / F::BB, std::max(al_blocks, static_cast<int>((ring_cap / 2) / (RGMAX * F::BB))));
+            KC = KC / al_blocks * al_blocks;
+            while (KC >= al_blocks && p.nb % KC != 0) KC -= al_blocks;
+            // Fewer rows per stage when two stages of RGMAX rows do not fit (at
+            // least one row per consumer warp).  Tensor copies land on
+            // 128-byte aligned slots.
+            int rgt = RGMAX;
+            if (KC >= al_blocks) {
+                const int fit_rows = static_cast<int>((ring_cap / 2 - 128) / (KC * F::BB));
+                rgt = std::min(RGMAX, fit_rows);
+            }
+            const uint32_t sb = align_up(static_cast<uint32_t>(rgt) * KC * F::BB, 128);
+            if (KC >= al_blocks && KC < p.nb && KC * F::BB <= 2048 && rgt >= Cfg<MT>::NCW &&
+                ring_cap >= 2 * sb) {
+                const int nchunks = p.nb / KC;
+                const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.row_bytes / 8), static_cast<cuuint64_t>(L.N)};
+                const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.row_bytes)};
+                const cuuint32_t box[2] = {static_cast<cuuint32_t>(KC * F::BB / 8), static_cast<cuuint32_t>(rgt)};
+                const cuuint32_t estr[2] = {1, 1};
+                CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(L.W), dims, strides,
+                                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                if (r == CUDA_SUCCESS) {
+                    p.mode = MODE_TMAP;
+                    p.KC = KC;
+                    p.nchunks = nchunks;
+                    p.rg = rgt;
+                    p.row_stride = KC * F::BB;
+                    p.stage_bytes = static_cast<int>(sb);
+                    const int need = ((rows_cta + rgt - 1) / rgt) * nchunks;
+                    p.stages = std::max(2, std::min({static_cast<int>(ring_cap / sb), 8, need}));
+                    chosen = true;
+                }
+            }
+        }
     }
-    stages = std::min(stages, 8);
-    p.stages = stages;
-    const uint32_t smem = off + static_cast<uint32_t>(stages) * p.stage_bytes;
-
-    int grid = L.num_sms * ctas_per_sm;
-    if (grid > L.N) grid = L.N;
-    if (grid < 1) grid = 1;
-
+    if (!chosen) {
+        // Plain loads by the producer warp: any alignment.
+        int KC = static_cast<int>((28 * 1024) / (RGMAX * F::BB));
+        KC = std::max(al_blocks, KC / al_blocks * al_blocks);
+        if (KC >= p.nb) KC = p.nb;
+        p.mode = MODE_PLAIN;
+        p.KC = KC;
+        p.nchunks = (p.nb + KC - 1) / KC;
+        p.row_stride = static_cast<int>(align_up(static_cast<uint32_t>(KC * F::BB), 16));
+        p.rg = std::min(RGMAX, static_cast<int>(ring_cap / 2 / p.row_stride));
+        if (p.rg < 1) return cudaErrorInvalidConfiguration;
+        p.stage_bytes = p.rg * p.row_stride;
+        const int need = ((rows_cta + p.rg - 1) / p.rg) * p.nchunks;
+        p.stages = std::max(2, std::min({static_cast<int>(ring_cap / p.stage_bytes), 8, need}));
+    }
+    const uint32_t smem = off + static_cast<uint32_t>(p.stages) * p.stage_bytes;
     auto kern = gemv_kernel<T, MT>;
-    // The attribute is per device: raise it once to the largest size seen.
+    // The attribute is per device: raise it once to the opt-in maximum.
     static thread_local int set_dev = -1;
-    static thread_local uint32_t set_smem = 0;
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev != set_dev || smem > set_smem) {
+    if (dev != set_dev) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_cap));
         if (e != cudaSuccess) return e;
         set_dev = dev;
-        set_smem = smem_cap;
     }
 
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kGemvThreads);
+    cfg.blockDim = dim3(Cfg<MT>::THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -434,7 +654,7 @@ static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, p);
+    return cudaLaunchKernelEx(&cfg, kern, p, tmap);
 }
 
 template <int T>
@@ -447,13 +667,13 @@ static cudaError_t launch_fmt(const GemvLaunch& L, cudaStream_t s) {
 
 size_t gemv_smem_x_bytes(int type, int MT, int K) {
     switch (type) {
-        case Q4_0: return x_bytes<Q4_0>(MT, K);
-        case Q8_0: return x_bytes<Q8_0>(MT, K);
-        case Q2_K: return x_bytes<Q2_K>(MT, K);
-        case Q3_K: return x_bytes<Q3_K>(MT, K);
-        case Q4_K: return x_bytes<Q4_K>(MT, K);
-        case Q5_K: return x_bytes<Q5_K>(MT, K);
-        case Q6_K: return x_bytes<Q6_K>(MT, K);
+        case Q4_0: return x_area_bytes_t<Q4_0>(MT, K);
+        case Q8_0: return x_area_bytes_t<Q8_0>(MT, K);
+        case Q2_K: return x_area_bytes_t<Q2_K>(MT, K);
+        case Q3_K: return x_area_bytes_t<Q3_K>(MT, K);
+        case Q4_K: return x_area_bytes_t<Q4_K>(MT, K);
+        case Q5_K: return x_area_bytes_t<Q5_K>(MT, K);
+        case Q6_K: return x_area_bytes_t<Q6_K>(MT, K);
         default: return 0;
     }
 }

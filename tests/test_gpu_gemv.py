@@ -210,3 +210,54 @@ def test_module_dequantize_host(cuda, oracle_mod):
     dst = np.zeros(4096, np.float32)
     swq.dequantize(blocks, dst, 4096, t)
     assert np.array_equal(dst.view(np.uint32), oracle_mod.dequantize(t, blocks, 4096).view(np.uint32))
+
+
+@pytest.mark.parametrize("fmt,K", [("Q4_0", 96), ("Q4_0", 288), ("Q8_0", 288), ("Q8_0", 32), ("Q4_K", 768)])
+def test_k_not_multiple_of_64_elements(cuda, oracle_mod, fmt, K):
+    """Activation rows that end in a partial 128-byte line of shared memory."""
+    t = synth.IDS[fmt]
+    N = 211
+    blocks = synth.random_blocks(t, N, K, seed=800 + K)
+    X = synth.random_activations(3, K, seed=801)
+    got = _gemm_gpu(cuda, t, blocks, X, N, K)
+    assert rel_l2(got, oracle_mod.gemm(t, blocks, X, 3, N, K)) <= REL_L2_TOL
+
+
+def test_unaligned_activation_pointer(cuda, oracle_mod):
+    """X starting 4 bytes past a 16-byte boundary: scalar activation loads."""
+    torch = cuda
+    t = synth.Q5_K
+    N, K, M = 333, 1024, 2
+    blocks = synth.random_blocks(t, N, K, seed=900)
+    X = synth.random_activations(M, K, seed=901)
+    d_w = torch.from_numpy(blocks.reshape(-1)).cuda()
+    d_xbuf = torch.zeros(M * K + 4, dtype=torch.float32, device="cuda")
+    d_xbuf[1:1 + M * K] = torch.from_numpy(X.reshape(-1)).cuda()
+    d_y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    swq.gemm(t, d_w, d_xbuf.data_ptr() + 4, d_y, M, N, K)
+    swq.check()
+    assert rel_l2(d_y.cpu().numpy(), oracle_mod.gemm(t, blocks, X, M, N, K)) <= REL_L2_TOL
+
+
+@pytest.mark.parametrize("fmt", ["Q6_K", "Q4_K", "Q8_0", "Q5_K"])
+@pytest.mark.parametrize("M", [1, 2])
+def test_llama_down_proj_shape(cuda, oracle_mod, fmt, M):
+    """N=4096, K=14336 (Llama-3-8B FFN down-projection): rows split along K."""
+    t = synth.IDS[fmt]
+    N, K = 4096, 14336
+    blocks = synth.random_blocks(t, N, K, seed=1000 + t)
+    X = synth.random_activations(M, K, seed=1001)
+    got = _gemm_gpu(cuda, t, blocks, X, N, K)
+    assert rel_l2(got, oracle_mod.gemm(t, blocks, X, M, N, K)) <= REL_L2_TOL
+
+
+@pytest.mark.parametrize("fmt,N,K", [("Q4_K", 600, 3072), ("Q4_K", 333, 2048), ("Q4_0", 901, 4096),
+                                      ("Q8_0", 517, 8192), ("Q4_K", 700, 512), ("Q6_K", 257, 1024)])
+def test_whole_row_work_splits(cuda, oracle_mod, fmt, N, K):
+    """Row widths whose unit counts do (64, 128, 8, 16) and do not (48) divide
+    the consumer lanes, and several row groups per CTA."""
+    t = synth.IDS[fmt]
+    blocks = synth.random_blocks(t, N, K, seed=1100 + K)
+    X = synth.random_activations(1, K, seed=1101)
+    got = _gemm_gpu(cuda, t, blocks, X, N, K)
+    assert rel_l2(got, oracle_mod.gemm(t, blocks, X, 1, N, K)) <= REL_L2_TOL
