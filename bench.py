@@ -47,8 +47,8 @@ ALG_BYTES = W_BYTES + 4 * K_COLS * M_ROWS + 4 * N_ROWS * M_ROWS  # 9,469,952 per
 WORKLOAD = (f"Q4_K GEMV N={N_ROWS} K={K_COLS} M={M_ROWS}, {COPIES} rotating weight copies "
             f"({COPIES * W_BYTES / 1e6:.0f} MB)")
 # dram__bytes_read.sum + dram__bytes_write.sum of one gemv_kernel<Q4_K,1> launch
-# from ncu (profiles/gemv_q4k_4096x4096.md); None until captured.
-NCU_TRAFFIC_PER_LAUNCH = None
+# of this workload, from one ncu capture (profiles/gemv_q4k_4096x4096.md).
+NCU_TRAFFIC_PER_LAUNCH = 9_496_832
 
 
 def log(*a):
