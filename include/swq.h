@@ -101,7 +101,13 @@ enum {
      * 0: every read waits for the preceding kernel. */
     SWQ_OPT_EARLY_WEIGHT_PREFETCH = 2,
     /* Largest M served by the fused GEMV kernel; larger M use the GEMM. */
-    SWQ_OPT_GEMV_MAX_M = 3
+    SWQ_OPT_GEMV_MAX_M = 3,
+    /* 1 (default): M above SWQ_OPT_GEMV_MAX_M runs the tensor-core (tcgen05)
+     * dequant-GEMM, which rounds dequantized weights and activations to fp16
+     * before an fp32-accumulated product.  0: groups of rows through the GEMV
+     * kernel instead.  The GEMM needs the weight base aligned to 16 bytes for
+     * Q4_K/Q5_K, 4 for Q2_K, 2 otherwise; other pointers use the GEMV path. */
+    SWQ_OPT_TENSOR_CORE_GEMM = 4
 };
 swq_status swq_set_option(int option, int value);
 int swq_get_option(int option);

@@ -26,6 +26,7 @@ thread_local std::string g_last_error;
 std::atomic<int> g_opt_q2k_refcpu{0};
 std::atomic<int> g_opt_early_prefetch{1};
 std::atomic<int> g_opt_gemv_max_m{8};
+std::atomic<int> g_opt_gemm_tc{1};
 
 swq_status fail(swq_status s, const std::string& msg) {
     g_last_error = msg;
@@ -150,6 +151,10 @@ swq_status swq_set_option(int option, int value) {
             if (value < 0 || value > 8) return fail(SWQ_ERR_BAD_ARG, "GEMV max M must be in 0..8");
             g_opt_gemv_max_m = value;
             return SWQ_OK;
+        case SWQ_OPT_TENSOR_CORE_GEMM:
+            if (value != 0 && value != 1) return fail(SWQ_ERR_BAD_ARG, "option value must be 0 or 1");
+            g_opt_gemm_tc = value;
+            return SWQ_OK;
         default:
             return fail(SWQ_ERR_BAD_ARG, "unknown option " + std::to_string(option));
     }
@@ -160,6 +165,7 @@ int swq_get_option(int option) {
         case SWQ_OPT_Q2K_REFERENCE_CPU_ORDER: return g_opt_q2k_refcpu;
         case SWQ_OPT_EARLY_WEIGHT_PREFETCH: return g_opt_early_prefetch;
         case SWQ_OPT_GEMV_MAX_M: return g_opt_gemv_max_m;
+        case SWQ_OPT_TENSOR_CORE_GEMM: return g_opt_gemm_tc;
         default: return -1;
     }
 }
@@ -193,7 +199,7 @@ swq_status swq_gemm(int type, const void* W, const float* X, float* Y, int M, in
         return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
     }
     const int max_m = g_opt_gemv_max_m;
-    if (M > max_m && swq::gemm_tc_supported(type, M, N, K)) {
+    if (M > max_m && g_opt_gemm_tc && swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
         cudaError_t e = swq::gemm_tc_launch(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms, s);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
         return SWQ_OK;

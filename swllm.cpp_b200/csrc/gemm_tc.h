@@ -6,7 +6,7 @@
 namespace swq {
 
 // True when the tcgen05 GEMM serves this problem.
-bool gemm_tc_supported(int type, int M, int N, int K);
+bool gemm_tc_supported(int type, const void* W, int M, int N, int K, int refcpu);
 // Y[M x N] = X[M x K] . W[N x K]^T on tensor cores.
 cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, int M, int N, int K,
                            int refcpu, int num_sms, cudaStream_t s);

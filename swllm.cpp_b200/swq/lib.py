@@ -23,6 +23,7 @@ TYPE_NAMES = {v: k for k, v in TYPES.items()}
 OPT_Q2K_REFERENCE_CPU_ORDER = 1
 OPT_EARLY_WEIGHT_PREFETCH = 2
 OPT_GEMV_MAX_M = 3
+OPT_TENSOR_CORE_GEMM = 4
 
 
 class Status(enum.IntEnum):

@@ -1,0 +1,105 @@
+"""Tensor-core (tcgen05) dequant-GEMM against the oracle.
+
+The reference has no batched quantized path: its prefill is one
+Compute::matmul_transposed_q per token (src/main.cpp:284-287), so the oracle
+for M rows is M such calls.  Tolerance: relative L2 <= 1e-3 (REL_L2_TOL); the
+kernel rounds dequantized weights and activations to fp16 before an
+fp32-accumulated product (expected ~3e-4).
+"""
+import numpy as np
+import pytest
+
+import swq
+from conftest import REL_L2_TOL, rel_l2
+from swq import synth
+
+pytestmark = pytest.mark.gpu
+
+FORMATS = ["Q4_0", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"]
+
+
+def _gemm(torch, t, blocks, X, N, K):
+    M = X.shape[0]
+    d_w = torch.from_numpy(np.ascontiguousarray(blocks).reshape(-1)).cuda()
+    d_x = torch.from_numpy(np.ascontiguousarray(X, dtype=np.float32)).cuda()
+    d_y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    swq.gemm(t, d_w, d_x, d_y, M, N, K)
+    swq.check()
+    return d_y.cpu().numpy()
+
+
+@pytest.fixture(autouse=True)
+def _tensor_core_on():
+    swq.set_option(swq.OPT_TENSOR_CORE_GEMM, 1)
+    yield
+    swq.set_option(swq.OPT_TENSOR_CORE_GEMM, 1)
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("M", [9, 64, 130, 256])
+def test_formats(cuda, oracle_mod, fmt, M):
+    t = synth.IDS[fmt]
+    qk, _ = synth.block_geometry(t)
+    N, K = 384, 2048 if qk == 256 else 1024
+    blocks = synth.random_blocks(t, N, K, seed=2000 + t)
+    X = synth.random_activations(M, K, seed=2001 + M)
+    got = _gemm(cuda, t, blocks, X, N, K)
+    want = oracle_mod.gemm(t, blocks, X, M, N, K)
+    err = rel_l2(got, want)
+    assert err <= REL_L2_TOL, err
+    assert np.all(np.isfinite(got))
+
+
+@pytest.mark.parametrize("fmt,N,K,M", [("Q4_K", 200, 512, 70), ("Q4_0", 129, 96, 33), ("Q8_0", 257, 160, 300),
+                                        ("Q6_K", 130, 768, 17), ("Q5_K", 1000, 1280, 511)])
+def test_ragged_tiles(cuda, oracle_mod, fmt, N, K, M):
+    """N not a multiple of 128, M not a multiple of the token tile, K with an
+    odd number of 32-element blocks (a half-filled last K step)."""
+    t = synth.IDS[fmt]
+    blocks = synth.random_blocks(t, N, K, seed=2100 + N)
+    X = synth.random_activations(M, K, seed=2101)
+    got = _gemm(cuda, t, blocks, X, N, K)
+    assert rel_l2(got, oracle_mod.gemm(t, blocks, X, M, N, K)) <= REL_L2_TOL
+
+
+@pytest.mark.parametrize("fmt,M", [("Q4_K", 512), ("Q6_K", 64), ("Q8_0", 64), ("Q4_0", 64), ("Q2_K", 64),
+                                    ("Q3_K", 64), ("Q5_K", 64)])
+def test_llama_ffn_shape(cuda, oracle_mod, fmt, M):
+    """N=14336, K=4096 (Llama-3-8B FFN up-projection), prefill-sized M."""
+    t = synth.IDS[fmt]
+    N, K = 14336, 4096
+    blocks = synth.random_blocks(t, N, K, seed=2200 + t)
+    X = synth.random_activations(M, K, seed=2201)
+    got = _gemm(cuda, t, blocks, X, N, K)
+    assert rel_l2(got, oracle_mod.gemm(t, blocks, X, M, N, K)) <= REL_L2_TOL
+
+
+def test_gemv_path_when_unaligned(cuda, oracle_mod):
+    """Q4_K weights not 16-byte aligned: the tensor-core GEMM declines and the
+    GEMV kernel serves every row group."""
+    torch = cuda
+    t = synth.Q4_K
+    N, K, M = 256, 1024, 40
+    blocks = synth.random_blocks(t, N, K, seed=2300)
+    X = synth.random_activations(M, K, seed=2301)
+    flat = blocks.reshape(-1)
+    d_w = torch.zeros(flat.size + 64, dtype=torch.uint8, device="cuda")
+    d_w[8:8 + flat.size] = torch.from_numpy(flat).cuda()
+    d_x = torch.from_numpy(X).cuda()
+    d_y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    swq.gemm(t, d_w.data_ptr() + 8, d_x, d_y, M, N, K)
+    swq.check()
+    assert rel_l2(d_y.cpu().numpy(), oracle_mod.gemm(t, blocks, X, M, N, K)) <= REL_L2_TOL
+
+
+def test_deterministic(cuda):
+    torch = cuda
+    t = synth.Q4_K
+    N, K, M = 1024, 2048, 256
+    d_w = torch.from_numpy(synth.random_blocks(t, N, K, seed=2400).reshape(-1)).cuda()
+    d_x = torch.from_numpy(synth.random_activations(M, K, seed=2401)).cuda()
+    ys = [torch.empty((M, N), dtype=torch.float32, device="cuda") for _ in range(3)]
+    for y in ys:
+        swq.gemm(t, d_w, d_x, y, M, N, K)
+    swq.check()
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])
