@@ -12,7 +12,7 @@
 //    and start streaming their weights while this one finishes.
 //  * Last warp = producer: one lane moves raw blocks into shared-memory stages
 //    with the TMA -- one 1-D bulk copy per stage of whole rows, or one 2-D
-//    tensor-map copy per stage of row chunks (no multicast, L2 evict-first)
+//    tensor-map copy per stage of row chunks (into this CTA only, L2 evict-first)
 //    -- completing on per-stage mbarriers.  Weights are requested before
 //    griddepcontrol.wait (they are immutable inputs).  When a CTA's rows fit
 //    in shared memory every stage gets its own slot and all of them are in
@@ -84,7 +84,7 @@ __device__ __forceinline__ int dp2a_hi(int a, uint32_t b, int c) {
 }
 
 // 2-D tiled TMA load of a box of the weight bytes (tensor map over 8-byte
-// elements: inner = row bytes / 8, outer = rows).  No multicast.
+// elements: inner = row bytes / 8, outer = rows).  Into this CTA only.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
                                             uint64_t pol) {
     asm volatile(

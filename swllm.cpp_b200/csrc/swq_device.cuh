@@ -91,7 +91,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // ---- bulk async copy (TMA, non-tensor) ----------------------------------------
 
 // global -> shared, completes `bytes` of transaction on `bar`.
-// dst and src 16-byte aligned, bytes a multiple of 16.  No multicast.
+// dst and src 16-byte aligned, bytes a multiple of 16.  Destination: this CTA only.
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes,
                                          uint64_t* bar, uint64_t l2_policy) {
     asm volatile(
