@@ -85,6 +85,31 @@ swq_status swq_gemv(int ggml_type, const void* W, const float* x, float* y,
 swq_status swq_gemm(int ggml_type, const void* W, const float* X, float* Y,
                     int M, int N, int K, swq_stream_t stream);
 
+/* ---- Allocation-free GEMM ------------------------------------------------
+ *
+ * No counterpart in the reference.  swq_gemm's tensor-core path takes a
+ * temporary fp16 copy of X (M * K * 2 bytes) from cudaMallocAsync on the
+ * stream.  Some callers cannot let a library allocate device memory: processes
+ * whose own allocator already owns the GPU's memory (a serving engine that
+ * reserves what HBM is left for its KV cache at start-up, a caching allocator
+ * that hands out every device byte), where a hidden allocation can fail or
+ * fragment memory the caller has promised elsewhere.  swq_gemm_noalloc
+ * computes what swq_gemm computes and allocates nothing: the fp16 copy of X
+ * lives in a fixed device array inside libswq of SWQ_GEMM_NOALLOC_MAX_X_ELEMS
+ * halves (16 MiB), which every GPU that loads the library holds until the
+ * process exits.  The caller passes W, X and Y as for swq_gemm.
+ *   - M * K above SWQ_GEMM_NOALLOC_MAX_X_ELEMS: SWQ_ERR_BAD_SHAPE.
+ *   - The first call on a device looks up the array's address on that device
+ *     (cudaGetSymbolAddress with the device current); make that first call
+ *     before any stream capture.
+ *   - All calls on a device share the one array, which keeps the last call's
+ *     contents.  Calls whose kernels overlap on the GPU (other streams, other
+ *     host threads) race on it: order them on one stream or with events.
+ *     Every call writes all of the array it reads, so nothing needs clearing. */
+#define SWQ_GEMM_NOALLOC_MAX_X_ELEMS 8388608
+swq_status swq_gemm_noalloc(int ggml_type, const void* W, const float* X, float* Y,
+                            int M, int N, int K, swq_stream_t stream);
+
 /* Options (process-wide). */
 enum {
     /* 1: Q2_K uses the activation order of the reference's fused CPU routine

@@ -107,6 +107,31 @@ swq_status check_gemm_args(int type, const void* W, const float* X, const float*
     return SWQ_OK;
 }
 
+// Y = X . W^T through the GEMV kernel, groups of up to max_m rows of X.
+swq_status gemm_gemv_groups(int type, const void* W, const float* X, float* Y, int M, int N, int K, int max_m,
+                            const swq::DeviceInfo& dev, cudaStream_t s) {
+    const int g = gemv_group_rows(type, K, std::max(1, max_m));
+    if (g == 0) return fail(SWQ_ERR_BAD_SHAPE, "K=" + std::to_string(K) + " exceeds the GEMV activation buffer");
+    for (int m0 = 0; m0 < M; m0 += g) {
+        swq::GemvLaunch L{};
+        L.type = type;
+        L.W = W;
+        L.X = X + static_cast<size_t>(m0) * K;
+        L.Y = Y + static_cast<size_t>(m0) * N;
+        L.M = std::min(g, M - m0);
+        L.N = N;
+        L.K = K;
+        L.refcpu = g_opt_q2k_refcpu;
+        L.early = g_opt_early_prefetch;
+        L.num_sms = dev.num_sms;
+        L.smem_per_block_optin = dev.smem_per_block_optin;
+        L.smem_per_sm = dev.smem_per_sm;
+        cudaError_t e = swq::gemv_launch(L, s);
+        if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
+    }
+    return SWQ_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -204,26 +229,32 @@ swq_status swq_gemm(int type, const void* W, const float* X, float* Y, int M, in
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
         return SWQ_OK;
     }
-    const int g = gemv_group_rows(type, K, std::max(1, max_m));
-    if (g == 0) return fail(SWQ_ERR_BAD_SHAPE, "K=" + std::to_string(K) + " exceeds the GEMV activation buffer");
-    for (int m0 = 0; m0 < M; m0 += g) {
-        swq::GemvLaunch L{};
-        L.type = type;
-        L.W = W;
-        L.X = X + static_cast<size_t>(m0) * K;
-        L.Y = Y + static_cast<size_t>(m0) * N;
-        L.M = std::min(g, M - m0);
-        L.N = N;
-        L.K = K;
-        L.refcpu = g_opt_q2k_refcpu;
-        L.early = g_opt_early_prefetch;
-        L.num_sms = dev.num_sms;
-        L.smem_per_block_optin = dev.smem_per_block_optin;
-        L.smem_per_sm = dev.smem_per_sm;
-        cudaError_t e = swq::gemv_launch(L, s);
-        if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
+    return gemm_gemv_groups(type, W, X, Y, M, N, K, max_m, dev, s);
+}
+
+swq_status swq_gemm_noalloc(int type, const void* W, const float* X, float* Y, int M, int N, int K,
+                            swq_stream_t stream) {
+    TypeInfo ti;
+    swq_status st = check_gemm_args(type, W, X, Y, M, N, K, &ti);
+    if (st != SWQ_OK || M == 0 || N == 0) return st;
+    if (static_cast<int64_t>(M) * K > SWQ_GEMM_NOALLOC_MAX_X_ELEMS)
+        return fail(SWQ_ERR_BAD_SHAPE, "swq_gemm_noalloc: M*K = " + std::to_string(static_cast<int64_t>(M) * K) +
+                                           " exceeds its fixed scratch of " +
+                                           std::to_string(SWQ_GEMM_NOALLOC_MAX_X_ELEMS) + " elements");
+    swq::DeviceInfo dev;
+    if ((st = current_device(&dev)) != SWQ_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (K == 0) {
+        cudaError_t e = cudaMemsetAsync(Y, 0, sizeof(float) * static_cast<size_t>(M) * N, s);
+        return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
     }
-    return SWQ_OK;
+    const int max_m = g_opt_gemv_max_m;
+    if (M > max_m && g_opt_gemm_tc && swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
+        cudaError_t e = swq::gemm_tc_launch_noalloc(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms, s);
+        if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch (fixed scratch)");
+        return SWQ_OK;
+    }
+    return gemm_gemv_groups(type, W, X, Y, M, N, K, max_m, dev, s);
 }
 
 swq_status swq_gemv(int type, const void* W, const float* x, float* y, int N, int K, swq_stream_t stream) {

@@ -18,7 +18,8 @@
 //               32*(w%4)..+31 = W rows), coalesced fp32 stores of Y.
 // Accumulators are double-buffered in TMEM (2 x BN columns) so the epilogue of
 // one tile overlaps the MMAs of the next.  Every wait is bounded; on timeout the
-// kernel records it, drains what it issued and frees its TMEM.  No multicast.
+// kernel records it, drains what it issued and frees its TMEM.  Every copy lands
+// in the issuing CTA only.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -26,8 +27,10 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
+#include <map>
 #include <mutex>
 
+#include "../../include/swq.h"
 #include "formats.cuh"
 #include "gemm_tc.h"
 #include "swq_device.cuh"
@@ -789,6 +792,30 @@ static cudaError_t launch_tc_fmt(const void* W, const __half* Xh, float* Y, int 
     return launch_tc<T, 256>(W, Xh, Y, M, N, K, num_sms, s);
 }
 
+// X -> fp16 into Xh (M*K halves), then the GEMM that reads Xh.
+static cudaError_t gemm_tc_run(int type, const void* W, const float* X, __half* Xh, float* Y, int M, int N, int K,
+                               int num_sms, cudaStream_t s) {
+    const int64_t n = static_cast<int64_t>(M) * K;
+    const int64_t n4 = n / 4;
+    const int grid = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(num_sms) * 8));
+    if ((reinterpret_cast<uintptr_t>(X) & 15u) == 0)
+        x_to_f16_kernel<true><<<std::max(grid, 1), 256, 0, s>>>(X, Xh, n);
+    else
+        x_to_f16_kernel<false><<<std::max(grid, 1), 256, 0, s>>>(X, Xh, n);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    switch (type) {
+        case Q4_0: return launch_tc_fmt<Q4_0>(W, Xh, Y, M, N, K, num_sms, s);
+        case Q8_0: return launch_tc_fmt<Q8_0>(W, Xh, Y, M, N, K, num_sms, s);
+        case Q2_K: return launch_tc_fmt<Q2_K>(W, Xh, Y, M, N, K, num_sms, s);
+        case Q3_K: return launch_tc_fmt<Q3_K>(W, Xh, Y, M, N, K, num_sms, s);
+        case Q4_K: return launch_tc_fmt<Q4_K>(W, Xh, Y, M, N, K, num_sms, s);
+        case Q5_K: return launch_tc_fmt<Q5_K>(W, Xh, Y, M, N, K, num_sms, s);
+        case Q6_K: return launch_tc_fmt<Q6_K>(W, Xh, Y, M, N, K, num_sms, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, int M, int N, int K, int refcpu,
                            int num_sms, cudaStream_t s) {
     if (!gemm_tc_supported(type, W, M, N, K, refcpu)) return cudaErrorNotSupported;
@@ -796,27 +823,53 @@ cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, in
     __half* Xh = nullptr;
     cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&Xh), static_cast<size_t>(n) * 2, s);
     if (e != cudaSuccess) return e;
-    const int64_t n4 = n / 4;
-    const int grid = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(num_sms) * 8));
-    if ((reinterpret_cast<uintptr_t>(X) & 15u) == 0)
-        x_to_f16_kernel<true><<<std::max(grid, 1), 256, 0, s>>>(X, Xh, n);
-    else
-        x_to_f16_kernel<false><<<std::max(grid, 1), 256, 0, s>>>(X, Xh, n);
-    e = cudaGetLastError();
-    if (e == cudaSuccess) {
-        switch (type) {
-            case Q4_0: e = launch_tc_fmt<Q4_0>(W, Xh, Y, M, N, K, num_sms, s); break;
-            case Q8_0: e = launch_tc_fmt<Q8_0>(W, Xh, Y, M, N, K, num_sms, s); break;
-            case Q2_K: e = launch_tc_fmt<Q2_K>(W, Xh, Y, M, N, K, num_sms, s); break;
-            case Q3_K: e = launch_tc_fmt<Q3_K>(W, Xh, Y, M, N, K, num_sms, s); break;
-            case Q4_K: e = launch_tc_fmt<Q4_K>(W, Xh, Y, M, N, K, num_sms, s); break;
-            case Q5_K: e = launch_tc_fmt<Q5_K>(W, Xh, Y, M, N, K, num_sms, s); break;
-            case Q6_K: e = launch_tc_fmt<Q6_K>(W, Xh, Y, M, N, K, num_sms, s); break;
-            default: e = cudaErrorInvalidValue;
-        }
-    }
+    e = gemm_tc_run(type, W, X, Xh, Y, M, N, K, num_sms, s);
     cudaError_t e2 = cudaFreeAsync(Xh, s);
     return e != cudaSuccess ? e : e2;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant (swq_gemm_noalloc).  Callers whose process already
+// owns the GPU's memory through its own allocator (a serving engine that
+// reserves HBM for its KV cache at start-up, a caching allocator that hands
+// out every device byte) cannot let this library take a temporary buffer from
+// cudaMallocAsync.  For them the fp16 copy of X lives in this fixed array,
+// which every GPU that loads libswq holds until the process exits.  In host
+// code `g_noalloc_x16` only names the array; its address on a device comes
+// from cudaGetSymbolAddress with that device current, looked up once per
+// device on that device's first call.  All calls on a device share the array:
+// calls whose kernels overlap on the GPU race.  Each call writes every element
+// it reads (the tensor map stops at M x K), so nothing needs clearing.
+// ---------------------------------------------------------------------------
+
+static __device__ __align__(256) uint16_t g_noalloc_x16[SWQ_GEMM_NOALLOC_MAX_X_ELEMS];
+
+static cudaError_t noalloc_scratch(__half** out) {
+    static std::mutex mu;
+    static std::map<int, void*> addr;  // device -> device address of g_noalloc_x16
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = addr.find(dev);
+    if (it == addr.end()) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_x16);
+        if (e != cudaSuccess) return e;
+        it = addr.emplace(dev, p).first;
+    }
+    *out = static_cast<__half*>(it->second);
+    return cudaSuccess;
+}
+
+cudaError_t gemm_tc_launch_noalloc(int type, const void* W, const float* X, float* Y, int M, int N, int K,
+                                   int refcpu, int num_sms, cudaStream_t s) {
+    if (!gemm_tc_supported(type, W, M, N, K, refcpu)) return cudaErrorNotSupported;
+    if (static_cast<int64_t>(M) * K > SWQ_GEMM_NOALLOC_MAX_X_ELEMS) return cudaErrorInvalidValue;
+    __half* Xh = nullptr;
+    cudaError_t e = noalloc_scratch(&Xh);
+    if (e != cudaSuccess) return e;
+    return gemm_tc_run(type, W, X, Xh, Y, M, N, K, num_sms, s);
 }
 
 SWQ_DEFINE_STATUS_FETCH(gemm_tc)

@@ -10,6 +10,10 @@ bool gemm_tc_supported(int type, const void* W, int M, int N, int K, int refcpu)
 // Y[M x N] = X[M x K] . W[N x K]^T on tensor cores.
 cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, int M, int N, int K,
                            int refcpu, int num_sms, cudaStream_t s);
+// The same with the fp16 copy of X in libswq's fixed device array instead of a
+// stream-ordered allocation (swq_gemm_noalloc); M * K must fit that array.
+cudaError_t gemm_tc_launch_noalloc(int type, const void* W, const float* X, float* Y, int M, int N, int K,
+                                   int refcpu, int num_sms, cudaStream_t s);
 cudaError_t status_fetch_gemm_tc(unsigned* out, cudaStream_t s);
 
 }  // namespace swq

@@ -25,6 +25,8 @@ OPT_EARLY_WEIGHT_PREFETCH = 2
 OPT_GEMV_MAX_M = 3
 OPT_TENSOR_CORE_GEMM = 4
 
+GEMM_NOALLOC_MAX_X_ELEMS = 8388608  # SWQ_GEMM_NOALLOC_MAX_X_ELEMS
+
 
 class Status(enum.IntEnum):
     OK = 0
@@ -72,6 +74,7 @@ def lib() -> ctypes.CDLL:
         "swq_dequant": (i32, [i32, vp, vp, i64, vp]),
         "swq_gemv": (i32, [i32, vp, vp, vp, i32, i32, vp]),
         "swq_gemm": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
+        "swq_gemm_noalloc": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
         "swq_set_option": (i32, [i32, i32]),
         "swq_get_option": (i32, [i32]),
         "swq_check": (i32, [vp]),
@@ -161,6 +164,13 @@ def gemv(type_id: int, W, x, y, N: int, K: int, stream=None) -> None:
 def gemm(type_id: int, W, X, Y, M: int, N: int, K: int, stream=None) -> None:
     """Y[M x N] = X[M x K] . W[N x K]^T on device buffers (async)."""
     _raise(lib().swq_gemm(type_id, _ptr(W), _ptr(X), _ptr(Y), M, N, K, _stream(stream)))
+
+
+def gemm_noalloc(type_id: int, W, X, Y, M: int, N: int, K: int, stream=None) -> None:
+    """gemm() without any device allocation: the fp16 copy of X lives in
+    libswq's fixed per-device array (M * K <= GEMM_NOALLOC_MAX_X_ELEMS).
+    Calls that overlap on the GPU share that array and race."""
+    _raise(lib().swq_gemm_noalloc(type_id, _ptr(W), _ptr(X), _ptr(Y), M, N, K, _stream(stream)))
 
 
 def check(stream=None) -> None:
