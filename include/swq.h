@@ -88,8 +88,8 @@ swq_status swq_gemm(int ggml_type, const void* W, const float* X, float* Y,
 /* ---- Allocation-free GEMM ------------------------------------------------
  *
  * No counterpart in the reference.  swq_gemm's tensor-core path takes a
- * temporary fp16 copy of X (M * K * 2 bytes) from cudaMallocAsync on the
- * stream.  Some callers cannot let a library allocate device memory: processes
+ * temporary fp16 copy of X (M * K * 2 bytes) from a stream-ordered memory
+ * pool that libswq creates per device and keeps until exit.  Some callers cannot let a library allocate device memory: processes
  * whose own allocator already owns the GPU's memory (a serving engine that
  * reserves what HBM is left for its KV cache at start-up, a caching allocator
  * that hands out every device byte), where a hidden allocation can fail or

@@ -5,17 +5,25 @@
 // Compute::matmul_transposed_q per token, src/main.cpp:284-287 ->
 // src/tensor.h:1212); this kernel is the M-rows-at-once form of it.
 //
-// Per CTA (persistent, one per SM), output tile = 128 W rows x BN tokens:
-//   warp 0      TMA producer for the activation tiles (X converted to fp16 once,
-//               128-byte swizzled K-major boxes of 64 K x BN tokens); TMEM owner.
-//   warp 1      MMA issuer: one lane runs tcgen05.mma.cta_group::1.kind::f16
-//               (M = 128, N = BN, K = 16) into an fp32 TMEM accumulator.
-//   warps 2-5   W producers: thread i owns W row i of the tile; per 64-element
-//               K step it reads that row's GGUF bytes (L2 prefetch a few blocks
-//               ahead, one step of register double-buffering), dequantizes to
-//               fp16 and stores the 128-byte swizzled K-major A operand.
-//   warps 6-9   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
-//               32*(w%4)..+31 = W rows), coalesced fp32 stores of Y.
+// Per CTA (persistent, one per SM), output tile = 128 W rows x BN tokens, K in
+// steps of 64 (one 128-byte swizzle atom of fp16):
+//   X producer   TMA of the fp16 activation tile (64 K x BN tokens, 128-byte
+//                swizzled, K-major) per step.
+//   MMA issuer   one lane: tcgen05.mma.cta_group::1.kind::f16 (M = 128,
+//                N = BN, K = 16) into an fp32 TMEM accumulator.
+//   W producer   the GGUF bytes of 256 K elements of the tile's 128 rows per
+//                W stage (a 2-D tensor-map copy when rows are 16-byte aligned,
+//                else one bulk copy per row).
+//   16 dequantizer warps: four lanes per W row, eight rows per warp.
+//                Quant bits become fp16 with the
+//                0x6400 exponent trick (byte permute, then an exact fp16
+//                subtract of the bias and one HFMA2/HMUL2 with the scales) and
+//                are stored as the 128-byte-swizzled K-major A operand.
+//   4 epilogue warps: tcgen05.ld of the accumulator (TMEM lane quadrant
+//                = warp % 4), coalesced fp32 stores of Y.
+// The order of the 64 K positions inside a step is whatever makes the
+// dequantization cheapest for the format (tc_elem below); the activation
+// conversion writes X in the same order, so the products are unchanged.
 // Accumulators are double-buffered in TMEM (2 x BN columns) so the epilogue of
 // one tile overlaps the MMAs of the next.  Every wait is bounded; on timeout the
 // kernel records it, drains what it issued and frees its TMEM.  Every copy lands
@@ -40,9 +48,53 @@ namespace swq {
 namespace tc {
 
 constexpr int BM = 128;       // W rows per tile (MMA M)
-constexpr int BK = 64;        // K elements per stage (one 128-byte swizzle atom of fp16)
-constexpr int THREADS = 320;  // 10 warps
+constexpr int BK = 64;        // K elements per step (one 128-byte swizzle atom of fp16)
+constexpr int KG = 256;       // K elements per W stage (4 steps)
 constexpr int A_STAGE = BM * BK * 2;  // 16 KB
+constexpr int NDQ = 16;       // dequantizer warps
+constexpr int PASSES = BM / (8 * NDQ);  // W rows per dequantizer lane
+// Warp roles (a warp runs on SM sub-partition warp % 4): warps 0-3 epilogue
+// (TMEM lane quadrant = warp), 4 MMA issuer, 5 X producer, 6 W producer, 7 no
+// role, 8-23 dequantizers -- four per sub-partition, so the dequantization,
+// which sets the pace, uses the issue slots of all four.
+constexpr int NWARPS = 8 + NDQ;
+constexpr int THREADS = NWARPS * 32;  // 768
+constexpr int WARP_MMA = 4, WARP_X = 5, WARP_W = 6, WARP_DQ0 = 8;
+__host__ __device__ constexpr int dq_index(int w) { return w >= WARP_DQ0 && w < WARP_DQ0 + NDQ ? w - WARP_DQ0 : -1; }
+__host__ __device__ constexpr bool is_epilogue(int w) { return w < 4; }
+constexpr uint32_t FULL = 0xffffffffu;
+
+// Per-format constants of the W stages.
+struct TcFmt {
+    int qk, bb;   // elements and bytes per block
+    int gbytes;   // bytes of one W stage of one row (256 elements)
+    bool f2;      // element order family (tc_elem)
+};
+__host__ __device__ constexpr TcFmt tc_fmt(int t) {
+    return t == Q4_0   ? TcFmt{32, 18, 144, false}
+           : t == Q8_0 ? TcFmt{32, 34, 272, false}
+           : t == Q2_K ? TcFmt{256, 84, 84, true}
+           : t == Q3_K ? TcFmt{256, 110, 110, true}
+           : t == Q4_K ? TcFmt{256, 144, 144, false}
+           : t == Q5_K ? TcFmt{256, 176, 176, false}
+           : t == Q6_K ? TcFmt{256, 210, 210, true}
+                       : TcFmt{0, 0, 0, false};
+}
+
+// K position p (0..255) of a W stage -> the element of the stage it holds.
+// p = 64 s + 32 t + 8 q + i: step s, chunk half t, dequantizer lane q of the
+// row, element i of the 16-byte chunk.
+//   family 1 (Q4_K, Q5_K, Q8_0, Q4_0): 32-element group 2s + t, inside it
+//     16 (i / 4) + 4 q + i % 4 -- low/high nibbles or bytes of words q, q + 4.
+//   family 2 (Q2_K, Q3_K, Q6_K): half n = s / 2, plane 2t + i / 4, inside the
+//     plane 16 (s % 2) + 4 q + i % 4.
+// Family 1 keeps every 32-element block inside its own 32 positions, so a K
+// that ends half way through a step still maps positions < K to elements < K.
+__host__ __device__ constexpr int tc_elem(bool f2, int p) {
+    return f2 ? 128 * ((p >> 6) >> 1) + 32 * (2 * ((p >> 5) & 1) + ((p & 7) >> 2)) + 16 * ((p >> 6) & 1) +
+                    4 * ((p >> 3) & 3) + (p & 3)
+              : 64 * (p >> 6) + 32 * ((p >> 5) & 1) + 16 * ((p & 7) >> 2) + 4 * ((p >> 3) & 3) + (p & 3);
+}
 
 // ---- tcgen05 / UMMA helpers ---------------------------------------------------
 
@@ -80,6 +132,17 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  ::"r"(smem_u32(bar)) : "memory");
 }
 
+// true on exactly one lane of the (fully active) warp
+__device__ __forceinline__ bool elect_one() {
+    uint32_t e;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "elect.sync _|P, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(e));
+    return e != 0;
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -94,347 +157,281 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__device__ __forceinline__ void tma_load_2d_nohint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+// ---- shared-memory reads of the W stage -------------------------------------
+
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
 }
 
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
+// Little-endian word at byte address a: A4 -> a is 4-byte aligned; otherwise a
+// is 2-byte aligned and the word is funnel-shifted out of two aligned words.
+template <bool A4>
+__device__ __forceinline__ uint32_t ldw(uint32_t a) {
+    if constexpr (A4) {
+        return lds32(a);
+    } else {
+        const uint32_t b = a & ~3u;
+        return __funnelshift_r(lds32(b), lds32(b + 4), (a & 3u) << 3);
+    }
 }
 
-// ---- dequantization of one 64-element K step of one row into fp16 ----------
+// ---- fp16 arithmetic on packed pairs -------------------------------------------
+
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<const __half2*>(&u); }
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) { return h2u(__floats2half2_rn(a, b)); }
+// (1024 + byte0, 1024 + byte1) and (1024 + byte2, 1024 + byte3) as fp16 pairs
+__device__ __forceinline__ uint32_t h2b01(uint32_t q) { return __byte_perm(q, 0x64646464u, 0x4140u); }
+__device__ __forceinline__ uint32_t h2b23(uint32_t q) { return __byte_perm(q, 0x64646464u, 0x4342u); }
+__device__ __forceinline__ uint32_t bc_lo(uint32_t h) { return __byte_perm(h, 0u, 0x1010u); }  // (h.x, h.x)
+__device__ __forceinline__ uint32_t bc_hi(uint32_t h) { return __byte_perm(h, 0u, 0x3232u); }  // (h.y, h.y)
+
+// (v - bias) * d + n  and  (v - bias) * d, on fp16 pairs; v - bias is exact.
+__device__ __forceinline__ uint32_t fq(uint32_t v, uint32_t bias, uint32_t d, uint32_t n) {
+    return h2u(__hfma2(__hsub2(u2h(v), u2h(bias)), u2h(d), u2h(n)));
+}
+__device__ __forceinline__ uint32_t mq(uint32_t v, uint32_t bias, uint32_t d) {
+    return h2u(__hmul2(__hsub2(u2h(v), u2h(bias)), u2h(d)));
+}
+
+constexpr uint32_t B1024 = 0x64006400u;  // fp16 1024
+constexpr uint32_t B1028 = 0x64046404u;  // 1024 + 4
+constexpr uint32_t B1032 = 0x64086408u;  // 1024 + 8
+constexpr uint32_t B1056 = 0x64206420u;  // 1024 + 32
+constexpr uint32_t B1152 = 0x64806480u;  // 1024 + 128
+
+// fp16 bits (low 16) -> (h, h) pair
+__device__ __forceinline__ uint32_t bc_bits(uint32_t b) { return (b & 0xFFFFu) * 0x10001u; }
+
+// ---- per-format dequantization of one step, one row, one lane ------------------
 //
-// raw<T>: the bytes a K step needs, loaded from global memory one step ahead;
-// emit<T>: eight 16-byte chunks (8 fp16 each) in K order.  Values are the
-// reference's element values computed in fp32 and rounded once to fp16.
+// hdr(): per block (256-element formats), each lane precomputes the scales it
+// hands to the row's other lanes (lane q of a row is warp lane rr + 8 q).
+// step(): the lane's 16 elements of step s as two 16-byte chunks (c0: t = 0,
+// c1: t = 1) in the order of tc_elem.  `blk` is the shared-memory byte address
+// of the block (256-element formats) or of the 8-block group (Q4_0, Q8_0).
 
 template <int T>
-struct Step;
-
-__device__ __forceinline__ uint32_t g_u32_a4(const uint8_t* p) { return __ldg(reinterpret_cast<const uint32_t*>(p)); }
-__device__ __forceinline__ uint32_t g_u32_a2(const uint8_t* p) {
-    const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
-    return static_cast<uint32_t>(__ldg(q)) | (static_cast<uint32_t>(__ldg(q + 1)) << 16);
-}
-__device__ __forceinline__ uint4 g_u128(const uint8_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+struct Dq;
 
 template <>
-struct Step<Q4_K> {
-    static constexpr int QK = 256, BB = 144;
-    struct Raw { uint4 hd, a, b; };
-    // row_ptr: start of the row; k0: first element of the step (multiple of 64)
-    __device__ static void load(Raw& r, const uint8_t* row, int k0) {
-        const uint8_t* blk = row + (k0 >> 8) * BB;
-        const int g = (k0 >> 6) & 3;
-        r.hd = g_u128(blk);
-        r.a = g_u128(blk + 16 + 32 * g);
-        r.b = g_u128(blk + 32 + 32 * g);
-    }
-    __device__ static void emit(const Raw& r, int k0, uint4 (&out)[8]) {
-        const int g = (k0 >> 6) & 3;
-        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&r.hd.x));
+struct Dq<Q4_K> {  // d @0, dmin @2, scales[12] @4, qs[128] @16 (src/tensor.h:196-227)
+    struct Hdr { uint32_t dd, mm; };  // (d1, d2), (-m1, -m2) of sub-blocks 2q, 2q + 1
+    template <bool A4>
+    __device__ static void hdr(uint32_t blk, int q, Hdr& h) {
+        const uint32_t w0 = ldw<A4>(blk), s0 = ldw<A4>(blk + 4), s1 = ldw<A4>(blk + 8), s2 = ldw<A4>(blk + 12);
+        const float d = h2f(w0 & 0xFFFFu), dmin = h2f(w0 >> 16);
         uint32_t sc0, m0, sc1, m1;
-        scale_min_k4_unit(g, 0, r.hd.y, r.hd.z, r.hd.w, sc0, m0);
-        scale_min_k4_unit(g, 1, r.hd.y, r.hd.z, r.hd.w, sc1, m1);
-        const float d1 = dm.x * static_cast<float>(sc0), n1 = -dm.y * static_cast<float>(m0);
-        const float d2 = dm.x * static_cast<float>(sc1), n2 = -dm.y * static_cast<float>(m1);
-        const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const bool hi = c >= 4;
-            const uint32_t w0 = w[2 * (c & 3)], w1 = w[2 * (c & 3) + 1];
-            const float dd = hi ? d2 : d1, nn = hi ? n2 : n1;
-            const int sh = hi ? 4 : 0;
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t ww = i < 2 ? w0 : w1;
-                const int b0 = 8 * (2 * (i & 1)) + sh, b1 = 8 * (2 * (i & 1) + 1) + sh;
-                const float q0 = static_cast<float>((ww >> b0) & 15u), q1 = static_cast<float>((ww >> b1) & 15u);
-                o[i] = pack_h2(fmaf(dd, q0, nn), fmaf(dd, q1, nn));
-            }
-            out[c] = make_uint4(o[0], o[1], o[2], o[3]);
-        }
+        scale_min_k4_unit(q, 0, s0, s1, s2, sc0, m0);
+        scale_min_k4_unit(q, 1, s0, s1, s2, sc1, m1);
+        h.dd = pack_h2(d * static_cast<float>(sc0), d * static_cast<float>(sc1));
+        h.mm = pack_h2(-(dmin * static_cast<float>(m0)), -(dmin * static_cast<float>(m1)));
+    }
+    template <bool A4>
+    __device__ static void step(uint32_t blk, const Hdr& h, int s, int q, int rr, uint4& c0, uint4& c1) {
+        const uint32_t a = blk + 16 + 32 * s + 4 * q;
+        const uint32_t wa = ldw<A4>(a), wb = ldw<A4>(a + 16);
+        const uint32_t dd = __shfl_sync(FULL, h.dd, rr + 8 * s), mm = __shfl_sync(FULL, h.mm, rr + 8 * s);
+        const uint32_t d0 = bc_lo(dd), d1 = bc_hi(dd), n0 = bc_lo(mm), n1 = bc_hi(mm);
+        const uint32_t la = wa & 0x0F0F0F0Fu, lb = wb & 0x0F0F0F0Fu;
+        const uint32_t ha = (wa >> 4) & 0x0F0F0F0Fu, hb = (wb >> 4) & 0x0F0F0F0Fu;
+        c0 = make_uint4(fq(h2b01(la), B1024, d0, n0), fq(h2b23(la), B1024, d0, n0),
+                        fq(h2b01(lb), B1024, d0, n0), fq(h2b23(lb), B1024, d0, n0));
+        c1 = make_uint4(fq(h2b01(ha), B1024, d1, n1), fq(h2b23(ha), B1024, d1, n1),
+                        fq(h2b01(hb), B1024, d1, n1), fq(h2b23(hb), B1024, d1, n1));
     }
 };
 
 template <>
-struct Step<Q5_K> {
-    static constexpr int QK = 256, BB = 176;
-    struct Raw { uint4 hd, a, b, h0, h1; };
-    __device__ static void load(Raw& r, const uint8_t* row, int k0) {
-        const uint8_t* blk = row + (k0 >> 8) * BB;
-        const int g = (k0 >> 6) & 3;
-        r.hd = g_u128(blk);
-        r.h0 = g_u128(blk + 16);
-        r.h1 = g_u128(blk + 32);
-        r.a = g_u128(blk + 48 + 32 * g);
-        r.b = g_u128(blk + 64 + 32 * g);
-    }
-    __device__ static void emit(const Raw& r, int k0, uint4 (&out)[8]) {
-        const int g = (k0 >> 6) & 3;
-        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&r.hd.x));
-        uint32_t sc0, m0, sc1, m1;
-        scale_min_k4_unit(g, 0, r.hd.y, r.hd.z, r.hd.w, sc0, m0);
-        scale_min_k4_unit(g, 1, r.hd.y, r.hd.z, r.hd.w, sc1, m1);
-        const float d1 = dm.x * static_cast<float>(sc0), n1 = -dm.y * static_cast<float>(m0);
-        const float d2 = dm.x * static_cast<float>(sc1), n2 = -dm.y * static_cast<float>(m1);
-        const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
-        const uint32_t h[8] = {r.h0.x, r.h0.y, r.h0.z, r.h0.w, r.h1.x, r.h1.y, r.h1.z, r.h1.w};
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const bool hi = c >= 4;
-            const int wi = 2 * (c & 3);
-            const float dd = hi ? d2 : d1, nn = hi ? n2 : n1;
-            const int sh = hi ? 4 : 0, hb = 2 * g + (hi ? 1 : 0);
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t ww = w[wi + (i >> 1)], hh = h[wi + (i >> 1)];
-                const int e0 = 2 * (i & 1), e1 = e0 + 1;  // byte within the word
-                const uint32_t v0 = ((ww >> (8 * e0 + sh)) & 15u) | (((hh >> (8 * e0 + hb)) & 1u) << 4);
-                const uint32_t v1 = ((ww >> (8 * e1 + sh)) & 15u) | (((hh >> (8 * e1 + hb)) & 1u) << 4);
-                o[i] = pack_h2(fmaf(dd, static_cast<float>(v0), nn), fmaf(dd, static_cast<float>(v1), nn));
-            }
-            out[c] = make_uint4(o[0], o[1], o[2], o[3]);
-        }
+struct Dq<Q5_K> {  // d @0, dmin @2, scales[12] @4, qh[32] @16, qs[128] @48 (src/tensor.h:329-365)
+    using Hdr = Dq<Q4_K>::Hdr;
+    template <bool A4>
+    __device__ static void hdr(uint32_t blk, int q, Hdr& h) { Dq<Q4_K>::hdr<A4>(blk, q, h); }
+    template <bool A4>
+    __device__ static void step(uint32_t blk, const Hdr& h, int s, int q, int rr, uint4& c0, uint4& c1) {
+        const uint32_t a = blk + 48 + 32 * s + 4 * q;
+        const uint32_t wa = ldw<A4>(a), wb = ldw<A4>(a + 16);
+        // qh bytes of elements 4q.. and 16 + 4q.., bit 2s + t for sub-block 2s + t
+        const uint32_t qa = ldw<A4>(blk + 16 + 4 * q) >> (2 * s), qb = ldw<A4>(blk + 32 + 4 * q) >> (2 * s);
+        const uint32_t dd = __shfl_sync(FULL, h.dd, rr + 8 * s), mm = __shfl_sync(FULL, h.mm, rr + 8 * s);
+        const uint32_t d0 = bc_lo(dd), d1 = bc_hi(dd), n0 = bc_lo(mm), n1 = bc_hi(mm);
+        const uint32_t la = (wa & 0x0F0F0F0Fu) | ((qa << 4) & 0x10101010u);
+        const uint32_t lb = (wb & 0x0F0F0F0Fu) | ((qb << 4) & 0x10101010u);
+        const uint32_t ha = ((wa >> 4) & 0x0F0F0F0Fu) | ((qa << 3) & 0x10101010u);
+        const uint32_t hb = ((wb >> 4) & 0x0F0F0F0Fu) | ((qb << 3) & 0x10101010u);
+        c0 = make_uint4(fq(h2b01(la), B1024, d0, n0), fq(h2b23(la), B1024, d0, n0),
+                        fq(h2b01(lb), B1024, d0, n0), fq(h2b23(lb), B1024, d0, n0));
+        c1 = make_uint4(fq(h2b01(ha), B1024, d1, n1), fq(h2b23(ha), B1024, d1, n1),
+                        fq(h2b01(hb), B1024, d1, n1), fq(h2b23(hb), B1024, d1, n1));
     }
 };
 
 template <>
-struct Step<Q6_K> {
-    static constexpr int QK = 256, BB = 210;
-    // 64 elements = half n, planes 2(g&1) and 2(g&1)+1: ql[64n .. 64n+63],
-    // qh[32n .. 32n+31], scales sc[8n .. 8n+7], d.
-    struct Raw { uint32_t ql[16], qh[8], s0, s1, d; };
-    __device__ static void load(Raw& r, const uint8_t* row, int k0) {
-        const uint8_t* blk = row + (k0 >> 8) * BB;
-        const int n = (k0 >> 7) & 1;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) r.ql[i] = g_u32_a2(blk + 64 * n + 4 * i);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) r.qh[i] = g_u32_a2(blk + 128 + 32 * n + 4 * i);
-        r.s0 = g_u32_a2(blk + 192 + 8 * n);
-        r.s1 = g_u32_a2(blk + 196 + 8 * n);
-        r.d = static_cast<uint32_t>(__ldg(reinterpret_cast<const uint16_t*>(blk + 208)));
+struct Dq<Q6_K> {  // ql[128] @0, qh[64] @128, scales[16] (int8) @192, d @208 (src/tensor.h:368-403)
+    // Scale index 8n + 2kk + hb for plane kk of half n, l in 16hb ..: lane q
+    // holds d * s[4q .. 4q+3] as a0 = (s[4q], s[4q+2]), a1 = (s[4q+1], s[4q+3]).
+    struct Hdr { uint32_t a0, a1; };
+    template <bool A4>
+    __device__ static void hdr(uint32_t blk, int q, Hdr& h) {
+        const uint32_t sw = ldw<A4>(blk + 192 + 4 * q);
+        const float d = h2f(lds16(blk + 208));
+        const float s0 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 0)));
+        const float s1 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 1)));
+        const float s2 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 2)));
+        const float s3 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 3)));
+        h.a0 = pack_h2(d * s0, d * s2);
+        h.a1 = pack_h2(d * s1, d * s3);
     }
-    __device__ static void emit(const Raw& r, int k0, uint4 (&out)[8]) {
-        const int g = (k0 >> 6) & 3;
-        const int kkb = 2 * (g & 1);  // first plane
-        const float d = h2f(r.d);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const int kk = kkb + (c >> 2);     // plane
-            const int l0 = 8 * (c & 3);        // l of the first element
-            const int is = l0 >> 4;
-            const int sidx = is + 2 * kk;      // 0..7 within sc[8n ..]
-            const int s = static_cast<int8_t>(byte_of(sidx < 4 ? r.s0 : r.s1, sidx & 3));
-            const float ds = d * static_cast<float>(s);
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float v[2];
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int l = l0 + 2 * i + e;
-                    const int qb = l + 32 * (kk & 1);
-                    const uint32_t qlb = byte_of(r.ql[qb >> 2], qb & 3);
-                    const uint32_t nib = kk < 2 ? (qlb & 15u) : (qlb >> 4);
-                    const uint32_t hb = (byte_of(r.qh[l >> 2], l & 3) >> (2 * kk)) & 3u;
-                    v[e] = ds * static_cast<float>(static_cast<int>(nib | (hb << 4)) - 32);
-                }
-                o[i] = pack_h2(v[0], v[1]);
-            }
-            out[c] = make_uint4(o[0], o[1], o[2], o[3]);
-        }
+    template <bool A4>
+    __device__ static void step(uint32_t blk, const Hdr& h, int s, int q, int rr, uint4& c0, uint4& c1) {
+        const int n = s >> 1, hb = s & 1;
+        const uint32_t a = blk + 64 * n + 16 * hb + 4 * q;
+        const uint32_t wa = ldw<A4>(a), wb = ldw<A4>(a + 32), wc = ldw<A4>(blk + 128 + 32 * n + 16 * hb + 4 * q);
+        const uint32_t mine = hb ? h.a1 : h.a0;
+        const uint32_t s01 = __shfl_sync(FULL, mine, rr + 16 * n), s23 = __shfl_sync(FULL, mine, rr + 16 * n + 8);
+        const uint32_t sc0 = bc_lo(s01), sc1 = bc_hi(s01), sc2 = bc_lo(s23), sc3 = bc_hi(s23);
+        const uint32_t c4 = wc << 4;  // qh bits 2kk .. 2kk + 1 of each byte to bits 4 .. 5
+        const uint32_t p0 = (wa & 0x0F0F0F0Fu) | (c4 & 0x30303030u);
+        const uint32_t p1 = (wb & 0x0F0F0F0Fu) | ((c4 >> 2) & 0x30303030u);
+        const uint32_t p2 = ((wa >> 4) & 0x0F0F0F0Fu) | (wc & 0x30303030u);
+        const uint32_t p3 = ((wb >> 4) & 0x0F0F0F0Fu) | ((wc >> 2) & 0x30303030u);
+        c0 = make_uint4(mq(h2b01(p0), B1056, sc0), mq(h2b23(p0), B1056, sc0),
+                        mq(h2b01(p1), B1056, sc1), mq(h2b23(p1), B1056, sc1));
+        c1 = make_uint4(mq(h2b01(p2), B1056, sc2), mq(h2b23(p2), B1056, sc2),
+                        mq(h2b01(p3), B1056, sc3), mq(h2b23(p3), B1056, sc3));
     }
 };
 
 template <>
-struct Step<Q2_K> {
-    static constexpr int QK = 256, BB = 84;
-    // 64 elements = half n, planes 2(g&1), 2(g&1)+1: qs[32n .. 32n+31],
-    // sc[8n .. 8n+7], d, dmin.
-    struct Raw { uint32_t qs[8], s0, s1, dd; };
-    __device__ static void load(Raw& r, const uint8_t* row, int k0) {
-        const uint8_t* blk = row + (k0 >> 8) * BB;
-        const int n = (k0 >> 7) & 1;
+struct Dq<Q2_K> {  // scales[16] @0, qs[64] @16, d @80, dmin @82 (src/tensor.h:232-265)
+    struct Hdr { uint32_t d0, d1, m0, m1; };  // (dl, -ml) of scale indices (4q, 4q+2), (4q+1, 4q+3)
+    template <bool A4>
+    __device__ static void hdr(uint32_t blk, int q, Hdr& h) {
+        const uint32_t sw = ldw<A4>(blk + 4 * q), dw = ldw<A4>(blk + 80);
+        const float d = h2f(dw & 0xFFFFu), dmin = h2f(dw >> 16);
+        float dl[4], ml[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) r.qs[i] = g_u32_a4(blk + 16 + 32 * n + 4 * i);
-        r.s0 = g_u32_a4(blk + 8 * n);
-        r.s1 = g_u32_a4(blk + 8 * n + 4);
-        r.dd = g_u32_a4(blk + 80);
-    }
-    __device__ static void emit(const Raw& r, int k0, uint4 (&out)[8]) {
-        const int g = (k0 >> 6) & 3;
-        const int jb = 2 * (g & 1);
-        const float d = h2f(r.dd & 0xFFFFu), dmin = h2f(r.dd >> 16);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const int j = jb + (c >> 2);
-            const int e0 = 8 * (c & 3);  // 0..31 within the plane: h = e0 >> 4
-            const int h = e0 >> 4;
-            const uint32_t s = byte_of((2 * j + h) < 4 ? r.s0 : r.s1, (2 * j + h) & 3);
-            const float dl = d * static_cast<float>(s & 15u), nl = -dmin * static_cast<float>(s >> 4);
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int b0 = e0 + 2 * i;  // qs byte index within the 32 (16h + l)
-                const uint32_t v0 = (byte_of(r.qs[b0 >> 2], b0 & 3) >> (2 * j)) & 3u;
-                const uint32_t v1 = (byte_of(r.qs[(b0 + 1) >> 2], (b0 + 1) & 3) >> (2 * j)) & 3u;
-                o[i] = pack_h2(fmaf(dl, static_cast<float>(v0), nl), fmaf(dl, static_cast<float>(v1), nl));
-            }
-            out[c] = make_uint4(o[0], o[1], o[2], o[3]);
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t b = byte_of(sw, i);
+            dl[i] = d * static_cast<float>(b & 15u);
+            ml[i] = -(dmin * static_cast<float>(b >> 4));
         }
+        h.d0 = pack_h2(dl[0], dl[2]);
+        h.d1 = pack_h2(dl[1], dl[3]);
+        h.m0 = pack_h2(ml[0], ml[2]);
+        h.m1 = pack_h2(ml[1], ml[3]);
+    }
+    template <bool A4>
+    __device__ static void step(uint32_t blk, const Hdr& h, int s, int q, int rr, uint4& c0, uint4& c1) {
+        const int n = s >> 1, hb = s & 1;
+        const uint32_t w = ldw<A4>(blk + 16 + 32 * n + 16 * hb + 4 * q);
+        const uint32_t dm = hb ? h.d1 : h.d0, mm = hb ? h.m1 : h.m0;
+        const uint32_t d01 = __shfl_sync(FULL, dm, rr + 16 * n), d23 = __shfl_sync(FULL, dm, rr + 16 * n + 8);
+        const uint32_t m01 = __shfl_sync(FULL, mm, rr + 16 * n), m23 = __shfl_sync(FULL, mm, rr + 16 * n + 8);
+        const uint32_t p0 = w & 0x03030303u, p1 = (w >> 2) & 0x03030303u;
+        const uint32_t p2 = (w >> 4) & 0x03030303u, p3 = (w >> 6) & 0x03030303u;
+        const uint32_t e0 = bc_lo(d01), e1 = bc_hi(d01), e2 = bc_lo(d23), e3 = bc_hi(d23);
+        const uint32_t f0 = bc_lo(m01), f1 = bc_hi(m01), f2 = bc_lo(m23), f3 = bc_hi(m23);
+        c0 = make_uint4(fq(h2b01(p0), B1024, e0, f0), fq(h2b23(p0), B1024, e0, f0),
+                        fq(h2b01(p1), B1024, e1, f1), fq(h2b23(p1), B1024, e1, f1));
+        c1 = make_uint4(fq(h2b01(p2), B1024, e2, f2), fq(h2b23(p2), B1024, e2, f2),
+                        fq(h2b01(p3), B1024, e3, f3), fq(h2b23(p3), B1024, e3, f3));
     }
 };
 
 template <>
-struct Step<Q3_K> {
-    static constexpr int QK = 256, BB = 110;
-    struct Raw { uint32_t qs[8], hm[8], t0, t1, t2, d; };
-    __device__ static void load(Raw& r, const uint8_t* row, int k0) {
-        const uint8_t* blk = row + (k0 >> 8) * BB;
-        const int n = (k0 >> 7) & 1;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            r.qs[i] = g_u32_a2(blk + 32 + 32 * n + 4 * i);
-            r.hm[i] = g_u32_a2(blk + 4 * i);
-        }
-        r.t0 = g_u32_a2(blk + 96);
-        r.t1 = g_u32_a2(blk + 100);
-        r.t2 = g_u32_a2(blk + 104);
-        r.d = static_cast<uint32_t>(__ldg(reinterpret_cast<const uint16_t*>(blk + 108)));
+struct Dq<Q3_K> {  // hmask[32] @0, qs[64] @32, scales[12] @96, d @108 (src/tensor.h:269-326)
+    using Hdr = Dq<Q6_K>::Hdr;  // d * signed scale, same index split as Q6_K
+    template <bool A4>
+    __device__ static void hdr(uint32_t blk, int q, Hdr& h) {
+        const uint32_t t0 = ldw<A4>(blk + 96), t1 = ldw<A4>(blk + 100), t2 = ldw<A4>(blk + 104);
+        const float d = h2f(lds16(blk + 108));
+        const uint32_t sw = q3k_scale_word(q, t0, t1, t2);
+        const float s0 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 0)));
+        const float s1 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 1)));
+        const float s2 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 2)));
+        const float s3 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 3)));
+        h.a0 = pack_h2(d * s0, d * s2);
+        h.a1 = pack_h2(d * s1, d * s3);
     }
-    __device__ static void emit(const Raw& r, int k0, uint4 (&out)[8]) {
-        const int g = (k0 >> 6) & 3;
-        const int n = g >> 1, jb = 2 * (g & 1);
-        const float d = h2f(r.d);
-        const uint32_t a_lo = q3k_scale_word(2 * n, r.t0, r.t1, r.t2);
-        const uint32_t a_hi = q3k_scale_word(2 * n + 1, r.t0, r.t1, r.t2);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const int j = jb + (c >> 2);
-            const int e0 = 8 * (c & 3), h = e0 >> 4;
-            const int si = 2 * j + h;  // scale index within 8n ..
-            const int s = static_cast<int8_t>(byte_of(si < 4 ? a_lo : a_hi, si & 3));
-            const float dl = d * static_cast<float>(s);
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float v[2];
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int b = e0 + 2 * i + e;  // 16h + l
-                    const int q2 = (byte_of(r.qs[b >> 2], b & 3) >> (2 * j)) & 3;
-                    const int hb = (byte_of(r.hm[b >> 2], b & 3) >> (4 * n + j)) & 1;
-                    v[e] = dl * static_cast<float>(q2 - (hb ? 0 : 4));
-                }
-                o[i] = pack_h2(v[0], v[1]);
-            }
-            out[c] = make_uint4(o[0], o[1], o[2], o[3]);
-        }
+    template <bool A4>
+    __device__ static void step(uint32_t blk, const Hdr& h, int s, int q, int rr, uint4& c0, uint4& c1) {
+        const int n = s >> 1, hb = s & 1;
+        const uint32_t wq = ldw<A4>(blk + 32 + 32 * n + 16 * hb + 4 * q);
+        const uint32_t wh = ldw<A4>(blk + 16 * hb + 4 * q) >> (4 * n);  // plane j's high bit at bit j
+        const uint32_t mine = hb ? h.a1 : h.a0;
+        const uint32_t s01 = __shfl_sync(FULL, mine, rr + 16 * n), s23 = __shfl_sync(FULL, mine, rr + 16 * n + 8);
+        const uint32_t sc0 = bc_lo(s01), sc1 = bc_hi(s01), sc2 = bc_lo(s23), sc3 = bc_hi(s23);
+        const uint32_t h4 = wh << 2;  // bit j -> bit j + 2
+        const uint32_t p0 = (wq & 0x03030303u) | (h4 & 0x04040404u);
+        const uint32_t p1 = ((wq >> 2) & 0x03030303u) | ((h4 >> 1) & 0x04040404u);
+        const uint32_t p2 = ((wq >> 4) & 0x03030303u) | ((h4 >> 2) & 0x04040404u);
+        const uint32_t p3 = ((wq >> 6) & 0x03030303u) | ((h4 >> 3) & 0x04040404u);
+        c0 = make_uint4(mq(h2b01(p0), B1028, sc0), mq(h2b23(p0), B1028, sc0),
+                        mq(h2b01(p1), B1028, sc1), mq(h2b23(p1), B1028, sc1));
+        c1 = make_uint4(mq(h2b01(p2), B1028, sc2), mq(h2b23(p2), B1028, sc2),
+                        mq(h2b01(p3), B1028, sc3), mq(h2b23(p3), B1028, sc3));
     }
 };
 
 template <>
-struct Step<Q8_0> {
-    static constexpr int QK = 32, BB = 34;
-    // two blocks (elements k0 .. k0+63); the second may lie past K (valid = 0)
-    struct Raw { uint32_t q[16], d0, d1; };
-    __device__ static void load(Raw& r, const uint8_t* row, int k0, int K) {
-        const uint8_t* b0 = row + (k0 >> 5) * BB;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) r.q[i] = g_u32_a2(b0 + 2 + 4 * i);
-        r.d0 = static_cast<uint32_t>(__ldg(reinterpret_cast<const uint16_t*>(b0)));
-        if (k0 + 32 < K) {
-            const uint8_t* b1 = b0 + BB;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) r.q[8 + i] = g_u32_a2(b1 + 2 + 4 * i);
-            r.d1 = static_cast<uint32_t>(__ldg(reinterpret_cast<const uint16_t*>(b1)));
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) r.q[8 + i] = 0;
-            r.d1 = 0;
-        }
+struct Dq<Q8_0> {  // d @0, qs[32] (int8) @2 (src/tensor.h:157-166)
+    struct Hdr {};
+    template <bool A4>
+    __device__ static void hdr(uint32_t, int, Hdr&) {}
+    // one 32-element block: words q and q + 4 of its quants (bytes as q + 128)
+    template <bool A4>
+    __device__ static uint4 blk32(uint32_t b, int q) {
+        const uint32_t d = bc_bits(lds16(b));
+        const uint32_t wa = ldw<A4>(b + 2 + 4 * q) ^ 0x80808080u, wb = ldw<A4>(b + 18 + 4 * q) ^ 0x80808080u;
+        return make_uint4(mq(h2b01(wa), B1152, d), mq(h2b23(wa), B1152, d), mq(h2b01(wb), B1152, d),
+                          mq(h2b23(wb), B1152, d));
     }
-    __device__ static void emit(const Raw& r, int, uint4 (&out)[8]) {
-        const float d0 = h2f(r.d0), d1 = h2f(r.d1);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const float d = c < 4 ? d0 : d1;
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t w = r.q[2 * c + (i >> 1)];
-                const int e = 2 * (i & 1);
-                o[i] = pack_h2(d * static_cast<float>(static_cast<int8_t>(byte_of(w, e))),
-                               d * static_cast<float>(static_cast<int8_t>(byte_of(w, e + 1))));
-            }
-            out[c] = make_uint4(o[0], o[1], o[2], o[3]);
-        }
+    template <bool A4>
+    __device__ static void step(uint32_t grp, const Hdr&, int s, int q, int, uint4& c0, uint4& c1) {
+        c0 = blk32<A4>(grp + 34 * (2 * s), q);
+        c1 = blk32<A4>(grp + 34 * (2 * s + 1), q);
     }
 };
 
 template <>
-struct Step<Q4_0> {
-    static constexpr int QK = 32, BB = 18;
-    struct Raw { uint32_t q[8], d0, d1; };
-    __device__ static void load(Raw& r, const uint8_t* row, int k0, int K) {
-        const uint8_t* b0 = row + (k0 >> 5) * BB;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) r.q[i] = g_u32_a2(b0 + 2 + 4 * i);
-        r.d0 = static_cast<uint32_t>(__ldg(reinterpret_cast<const uint16_t*>(b0)));
-        if (k0 + 32 < K) {
-            const uint8_t* b1 = b0 + BB;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) r.q[4 + i] = g_u32_a2(b1 + 2 + 4 * i);
-            r.d1 = static_cast<uint32_t>(__ldg(reinterpret_cast<const uint16_t*>(b1)));
-        } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) r.q[4 + i] = 0x88888888u;
-            r.d1 = 0;
-        }
+struct Dq<Q4_0> {  // d @0, qs[16] @2: element l low nibble of byte l, l + 16 high (src/tensor.h:139-154)
+    struct Hdr {};
+    template <bool A4>
+    __device__ static void hdr(uint32_t, int, Hdr&) {}
+    template <bool A4>
+    __device__ static uint4 blk32(uint32_t b, int q) {
+        const uint32_t d = bc_bits(lds16(b));
+        const uint32_t w = ldw<A4>(b + 2 + 4 * q);
+        const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+        return make_uint4(mq(h2b01(lo), B1032, d), mq(h2b23(lo), B1032, d), mq(h2b01(hi), B1032, d),
+                          mq(h2b23(hi), B1032, d));
     }
-    __device__ static void emit(const Raw& r, int, uint4 (&out)[8]) {
-        const float d0 = h2f(r.d0), d1 = h2f(r.d1);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            // chunk c: block c >> 2; within it elements 8(c&3) .. +7: low nibbles of
-            // bytes 0..15 are elements 0..15, high nibbles elements 16..31
-            const int blk = c >> 2, cc = c & 3;
-            const float d = blk ? d1 : d0;
-            const int sh = cc >= 2 ? 4 : 0;
-            const int byte0 = 8 * (cc & 1);
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int b = byte0 + 2 * i;
-                const uint32_t w0 = r.q[4 * blk + (b >> 2)], w1 = r.q[4 * blk + ((b + 1) >> 2)];
-                const int q0 = static_cast<int>((byte_of(w0, b & 3) >> sh) & 15u) - 8;
-                const int q1 = static_cast<int>((byte_of(w1, (b + 1) & 3) >> sh) & 15u) - 8;
-                o[i] = pack_h2(d * static_cast<float>(q0), d * static_cast<float>(q1));
-            }
-            out[c] = make_uint4(o[0], o[1], o[2], o[3]);
-        }
+    template <bool A4>
+    __device__ static void step(uint32_t grp, const Hdr&, int s, int q, int, uint4& c0, uint4& c1) {
+        c0 = blk32<A4>(grp + 18 * (2 * s), q);
+        c1 = blk32<A4>(grp + 18 * (2 * s + 1), q);
     }
 };
-
-// Uniform load signature (the 32-element formats need K for a ragged last step).
-template <int T>
-__device__ __forceinline__ void step_load(typename Step<T>::Raw& r, const uint8_t* row, int k0, int K) {
-    if constexpr (T == Q8_0 || T == Q4_0) Step<T>::load(r, row, k0, K);
-    else Step<T>::load(r, row, k0);
-}
 
 struct Params {
     const uint8_t* W;
@@ -442,44 +439,58 @@ struct Params {
     int M, N, K;
     int row_bytes;
     int n_mtiles, n_ntiles, ksteps;
-    int stages;
+    int nblocks;      // blocks per row
+    int ngroups;      // W stages per tile = ceil(K / 256)
+    int stages;       // A/B ring depth
+    int wstages;      // W ring depth
+    int wp;           // W stage row pitch in shared memory (bytes, 16 x odd)
+    int rows_mode;    // 0: one tensor-map copy per W stage; 1: one bulk copy per row
+    const uint8_t* w_lo;  // W rounded down to 16 bytes
+    const uint8_t* w_hi;  // end of W rounded up to 16 bytes
 };
 
-struct Smem {
-    uint32_t a_off, b_off, bar_off;
-};
-
-template <int T, int BN>
+template <int T, int BN, bool A4>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_kernel(const Params p, const __grid_constant__ CUtensorMap xmap) {
-    using S = Step<T>;
+    gemm_kernel(const Params p, const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap) {
+    using D = Dq<T>;
+    constexpr TcFmt F = tc_fmt(T);
     constexpr int B_STAGE = BN * BK * 2;
     constexpr uint32_t IDESC = idesc_f16(BM, BN);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned base for the swizzled operands
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int S_ = p.stages;
+    const int S_ = p.stages, SW = p.wstages;
+    const int WSTAGE = BM * p.wp;
     uint8_t* a_st = smem;                                   // S x 16 KB
-    uint8_t* b_st = smem + S_ * A_STAGE;                    // S x B_STAGE
-    uint64_t* bars = reinterpret_cast<uint64_t*>(b_st + S_ * B_STAGE);
-    uint64_t* full_a = bars;              // [S] dequant warps (4 arrivals)
-    uint64_t* full_b = bars + S_;         // [S] TMA tx
-    uint64_t* empty = bars + 2 * S_;      // [S] MMA commit
-    uint64_t* tfull = bars + 3 * S_;      // [2] MMA commit per tile
-    uint64_t* tempty = bars + 3 * S_ + 2; // [2] epilogue (4 arrivals)
-    uint64_t* drain = bars + 3 * S_ + 4;  // final MMA commit before TMEM is freed
-    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 3 * S_ + 5);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * S_ + 5) + 1;
+    uint8_t* b_st = a_st + S_ * A_STAGE;                    // S x B_STAGE
+    uint8_t* w_st = b_st + S_ * B_STAGE;                    // SW x 128 rows x wp
+    // 16 bytes of slack after the W ring: a 2-byte aligned word read at the end
+    // of the last row touches the next aligned word.
+    uint64_t* bars = reinterpret_cast<uint64_t*>(w_st + SW * WSTAGE + 16);
+    uint64_t* full_a = bars;                 // [S] dequantizer warps (NDQ arrivals)
+    uint64_t* full_b = bars + S_;            // [S] X TMA bytes
+    uint64_t* empty = bars + 2 * S_;         // [S] MMA commit
+    uint64_t* wfull = bars + 3 * S_;         // [SW] W bytes (1 or 32 arrivals)
+    uint64_t* wempty = wfull + SW;           // [SW] dequantizer warps (NDQ arrivals)
+    uint64_t* tfull = wempty + SW;           // [2] MMA commit per tile
+    uint64_t* tempty = tfull + 2;            // [2] epilogue warps (4 arrivals)
+    uint64_t* drain = tempty + 2;            // final MMA commit before TMEM is freed
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 1) + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = p.n_mtiles * p.n_ntiles;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S_; ++s) {
-            mbar_init(&full_a[s], 4);
+            mbar_init(&full_a[s], NDQ);
             mbar_init(&full_b[s], 1);
             mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < SW; ++s) {
+            mbar_init(&wfull[s], p.rows_mode ? 32 : 1);
+            mbar_init(&wempty[s], NDQ);
         }
         for (int t = 0; t < 2; ++t) {
             mbar_init(&tfull[t], 1);
@@ -489,7 +500,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         *abort_flag = 0;
         mbar_fence_init();
     }
-    if (warp == 0) {
+    if (warp == WARP_MMA) {
         // 2 x BN fp32 columns of TMEM (double-buffered accumulator)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_u32(const_cast<uint32_t*>(tmem_slot))), "r"(2 * BN));
@@ -501,132 +512,237 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tmem_base = *tmem_slot;
     pdl_wait_primary();  // X (fp16) is written by the conversion kernel before this one
 
-    if (warp == 0) {
-        // ------------------------------------------------ activation TMA producer
-        if (lane == 0) {
-            int s = 0;
-            uint32_t ph = 0;
-            int it = 0;  // loads issued
-            for (int tile = blockIdx.x; tile < ntiles && !*abort_flag; tile += gridDim.x) {
-                const int mt = tile / p.n_ntiles;  // token tile
-                for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
-                    if (it >= S_ && !mbar_wait_bounded(&empty[s], ph ^ 1u, DEV_TIMEOUT_EMPTY)) {
-                        *abort_flag = 1;
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&full_b[s], B_STAGE);
-                    tma_load_2d_nohint(b_st + s * B_STAGE, &xmap, ks * BK, mt * BN, &full_b[s]);
-                    if (++s == S_) { s = 0; ph ^= 1u; }
+    if (warp == WARP_X) {
+        // -------------------------------------------------- activation TMA producer
+        // The whole warp runs the loop; one elected lane issues the copies.
+        int s = 0;
+        uint32_t ph = 0;
+        int it = 0;  // loads issued
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+            if (__shfl_sync(FULL, *abort_flag, 0)) break;
+            const int mt = tile / p.n_ntiles;  // token tile
+            bool ok = true;
+            for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+                const bool got = it < S_ || mbar_wait_bounded(&empty[s], ph ^ 1u, DEV_TIMEOUT_EMPTY);
+                if (!__all_sync(FULL, got)) {
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
                 }
+                if (elect_one()) {
+                    mbar_arrive_expect_tx(&full_b[s], B_STAGE);
+                    tma_load_2d(smem_u32(b_st + s * B_STAGE), &xmap, ks * BK, mt * BN, &full_b[s]);
+                }
+                __syncwarp();
+                if (++s == S_) { s = 0; ph ^= 1u; }
             }
-            // Wait for the last load issued into each stage, so that no copy is
-            // still writing shared memory when the CTA exits (immediate unless a
-            // wait above gave up).
-            for (int i = 0; i < S_ && i < it; ++i) {
-                const int idx = it - 1 - i;
-                mbar_wait_bounded(&full_b[idx % S_], static_cast<uint32_t>(idx / S_) & 1u, DEV_TIMEOUT_DRAIN);
-            }
+            if (!ok) break;
         }
-    } else if (warp == 1) {
+        // Wait for the last load issued into each stage, so that no copy is
+        // still writing shared memory when the CTA exits (immediate unless a
+        // wait above gave up).
+        for (int i = 0; i < S_ && i < it; ++i) {
+            const int idx = it - 1 - i;
+            mbar_wait_bounded(&full_b[idx % S_], static_cast<uint32_t>(idx / S_) & 1u, DEV_TIMEOUT_DRAIN);
+        }
+    } else if (warp == WARP_MMA) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            int s = 0;
-            uint32_t ph = 0;
-            int t_local = 0;
-            for (int tile = blockIdx.x; tile < ntiles && !*abort_flag; tile += gridDim.x, ++t_local) {
-                const int tb = t_local & 1;
-                const uint32_t tph = (t_local >> 1) & 1;
-                if (t_local >= 2 && !mbar_wait_bounded(&tempty[tb], tph ^ 1u, DEV_TIMEOUT_MMA)) {
+        // The whole warp runs the loop (warp-uniform descriptors); one elected
+        // lane issues the MMAs and the commits that track them.
+        int s = 0;
+        uint32_t ph = 0;
+        int t_local = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t_local) {
+            if (__shfl_sync(FULL, *abort_flag, 0)) break;
+            const int tb = t_local & 1;
+            const uint32_t tph = (t_local >> 1) & 1;
+            if (t_local >= 2) {
+                const bool got = mbar_wait_bounded(&tempty[tb], tph ^ 1u, DEV_TIMEOUT_MMA);
+                if (!__all_sync(FULL, got)) {
                     *abort_flag = 1;
                     break;
                 }
+            }
+            tc_fence_after();
+            const uint32_t dt = tmem_base + static_cast<uint32_t>(tb * BN);
+            bool ok = true;
+            for (int ks = 0; ks < p.ksteps; ++ks) {
+                const bool got = mbar_wait_bounded(&full_a[s], ph, DEV_TIMEOUT_FULL) &&
+                                 mbar_wait_bounded(&full_b[s], ph, DEV_TIMEOUT_FULL);
+                if (!__all_sync(FULL, got)) {
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
-                const uint32_t dt = tmem_base + static_cast<uint32_t>(tb * BN);
-                bool okk = true;
-                for (int ks = 0; ks < p.ksteps; ++ks) {
-                    if (!mbar_wait_bounded(&full_a[s], ph, DEV_TIMEOUT_FULL) ||
-                        !mbar_wait_bounded(&full_b[s], ph, DEV_TIMEOUT_FULL)) {
-                        *abort_flag = 1;
-                        okk = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint64_t da = smem_desc_sw128(smem_u32(a_st + s * A_STAGE));
-                    const uint64_t db = smem_desc_sw128(smem_u32(b_st + s * B_STAGE));
+                const uint64_t da = smem_desc_sw128(smem_u32(a_st + s * A_STAGE));
+                const uint64_t db = smem_desc_sw128(smem_u32(b_st + s * B_STAGE));
+                if (elect_one()) {
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)  // 32 bytes of K per instruction
                         mma_f16(dt, da + 2 * k, db + 2 * k, IDESC, (ks | k) ? 1u : 0u);
                     mma_commit(&empty[s]);
-                    if (++s == S_) { s = 0; ph ^= 1u; }
                 }
-                if (!okk) break;
-                mma_commit(&tfull[tb]);
+                __syncwarp();
+                if (++s == S_) { s = 0; ph ^= 1u; }
             }
-            // One more commit tracks every MMA this thread issued: once it
-            // arrives, no tensor-core write to TMEM is in flight.
-            mma_commit(drain);
-            mbar_wait_bounded(drain, 0u, DEV_TIMEOUT_DRAIN);
+            if (!ok) break;
+            if (elect_one()) mma_commit(&tfull[tb]);
+            __syncwarp();
         }
-    } else if (warp < 6) {
+        // One more commit tracks every MMA the elected lane issued: once it
+        // arrives, no tensor-core write to TMEM is in flight.
+        if (elect_one()) mma_commit(drain);
+        __syncwarp();
+        mbar_wait_bounded(drain, 0u, DEV_TIMEOUT_DRAIN);
+    } else if (warp == WARP_W) {
+        // --------------------------------------------------------- W producer
+        const uint64_t pol = l2_policy_evict_first();
+        int js = 0;
+        uint32_t jph = 0;
+        int jt = 0;  // W stages issued
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+            if (__shfl_sync(FULL, *abort_flag, 0)) break;
+            const int row0 = (tile % p.n_ntiles) * BM;
+            bool ok = true;
+            for (int g = 0; g < p.ngroups; ++g, ++jt) {
+                const bool got = jt < SW || mbar_wait_bounded(&wempty[js], jph ^ 1u, DEV_TIMEOUT_EMPTY);
+                if (!__all_sync(FULL, got)) {
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                const uint32_t dst = smem_u32(w_st + js * WSTAGE);
+                const size_t goff = static_cast<size_t>(g) * F.gbytes;
+                if (!p.rows_mode) {
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&wfull[js], static_cast<uint32_t>(WSTAGE));
+                        tma_load_2d(dst, &wmap, static_cast<int>((goff & ~size_t(15)) >> 1), row0, &wfull[js]);
+                    }
+                } else {
+                    // Rows lane, lane + 32, lane + 64, lane + 96 of the tile: copy
+                    // wp bytes from the 16-byte boundary at or below the row's
+                    // stage data, clipped at the end of W rounded up to 16.
+                    uint32_t bytes = 0;
+                    const uint8_t* src[4];
+                    uint32_t len[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int row = row0 + lane + 32 * k;
+                        len[k] = 0;
+                        src[k] = p.w_lo;
+                        if (row < p.N) {
+                            const uint8_t* a = p.W + static_cast<size_t>(row) * p.row_bytes + goff;
+                            const uint8_t* a16 = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(a) &
+                                                                                  ~uintptr_t(15));
+                            const size_t room = static_cast<size_t>(p.w_hi - a16);
+                            src[k] = a16;
+                            len[k] = static_cast<uint32_t>(room < static_cast<size_t>(p.wp) ? room : p.wp);
+                            bytes += len[k];
+                        }
+                    }
+                    mbar_arrive_expect_tx(&wfull[js], bytes);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (len[k]) bulk_g2s(w_st + js * WSTAGE + (lane + 32 * k) * p.wp, src[k], len[k], &wfull[js], pol);
+                }
+                if (++js == SW) { js = 0; jph ^= 1u; }
+            }
+            if (!ok) break;
+        }
+        // wait for the last W stage issued into each slot
+        if (lane == 0) {
+            for (int i = 0; i < SW && i < jt; ++i) {
+                const int idx = jt - 1 - i;
+                mbar_wait_bounded(&wfull[idx % SW], static_cast<uint32_t>(idx / SW) & 1u, DEV_TIMEOUT_DRAIN);
+            }
+        }
+    } else if (dq_index(warp) >= 0) {
         // ------------------------------------------------------- W dequantizers
-        const int r = threadIdx.x - 64;  // 0 .. 127: W row of the tile
+        const int rr = lane & 7, q = lane >> 3;
+        const int r0 = 8 * dq_index(warp) + rr;  // the lane's tile rows r0 + 8 NDQ p
+        const uintptr_t wbase = reinterpret_cast<uintptr_t>(p.W);
         int s = 0;
         uint32_t ph = 0;
         int it = 0;
+        int js = 0;
+        uint32_t jph = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-            if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
-            const int nt = tile % p.n_ntiles;
-            const int row = nt * BM + r;
-            const bool valid = row < p.N;
-            const uint8_t* rowp = p.W + static_cast<size_t>(valid ? row : 0) * p.row_bytes;
-            typename S::Raw cur, nxt;
-            if (valid) step_load<T>(cur, rowp, 0, p.K);
-            for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
-                const int k0 = ks * BK;
-                // L2 prefetch of the block four blocks ahead (once per block)
-                if (valid && ((k0 % S::QK) == 0 || S::QK < BK)) {
-                    const int kpf = k0 + 4 * (S::QK > BK ? S::QK : BK);
-                    if (kpf < p.K) {
-                        const uint8_t* pf = rowp + static_cast<size_t>(kpf / S::QK) * S::BB;
-                        prefetch_l2(pf);
-                        if (S::BB > 128) prefetch_l2(pf + 128);  // still inside the block
-                    }
-                }
-                if (valid && ks + 1 < p.ksteps) step_load<T>(nxt, rowp, k0 + BK, p.K);
-                uint4 out[8];
-                if (valid) {
-                    S::emit(cur, k0, out);
-                } else {
+            if (__shfl_sync(FULL, *abort_flag, 0)) break;
+            const int row0 = (tile % p.n_ntiles) * BM;
+            const bool ragged = row0 + BM > p.N;  // last row tile of a ragged N
+            bool valid[PASSES];
+            uintptr_t rowg[PASSES];
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) out[c] = make_uint4(0, 0, 0, 0);
-                }
-                const bool got = it < S_ || mbar_wait_bounded(&empty[s], ph ^ 1u, DEV_TIMEOUT_EMPTY);
-                if (!__all_sync(0xffffffffu, got)) {  // the warp leaves together
+            for (int pp = 0; pp < PASSES; ++pp) {
+                const int r = r0 + 8 * NDQ * pp;
+                valid[pp] = row0 + r < p.N;
+                rowg[pp] = wbase + static_cast<uintptr_t>(valid[pp] ? row0 + r : 0) * p.row_bytes;
+            }
+            bool ok = true;
+            for (int g = 0; g < p.ngroups && ok; ++g) {
+                const bool gotw = mbar_wait_bounded(&wfull[js], jph, DEV_TIMEOUT_FULL);
+                if (!__all_sync(FULL, gotw)) {
                     *abort_flag = 1;
+                    ok = false;
                     break;
                 }
-                uint8_t* a = a_st + s * A_STAGE + (r >> 3) * 1024 + (r & 7) * 128;
+                const uintptr_t goff = static_cast<uintptr_t>(g) * F.gbytes;
+                const uint32_t ws = smem_u32(w_st + js * WSTAGE);
+                // a row's stage data starts (its global address mod 16) into its smem row
+                uint32_t blk[PASSES];
+                typename D::Hdr hd[PASSES];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(a + ((c ^ (r & 7)) << 4)) = out[c];
-                fence_async_shared();
+                for (int pp = 0; pp < PASSES; ++pp) {
+                    blk[pp] = ws + (r0 + 8 * NDQ * pp) * p.wp + static_cast<uint32_t>((rowg[pp] + goff) & 15u);
+                    D::template hdr<A4>(blk[pp], q, hd[pp]);
+                }
+                const int nsteps = min(KG / BK, p.ksteps - g * (KG / BK));
+                for (int st = 0; st < nsteps; ++st, ++it) {
+                    const bool got = it < S_ || mbar_wait_bounded(&empty[s], ph ^ 1u, DEV_TIMEOUT_EMPTY);
+                    if (!__all_sync(FULL, got)) {  // the warp leaves together
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    // a 32-element block past the end of the row (K % 64 == 32) is zero
+                    const bool z1 = F.qk == 32 && g * 8 + 2 * st + 1 >= p.nblocks;
+                    const uint32_t as = smem_u32(a_st + s * A_STAGE);
+#pragma unroll
+                    for (int pp = 0; pp < PASSES; ++pp) {
+                        uint4 c0, c1;
+                        D::template step<A4>(blk[pp], hd[pp], st, q, rr, c0, c1);
+                        const uint4 zero = make_uint4(0, 0, 0, 0);
+                        if (ragged && !valid[pp]) { c0 = zero; c1 = zero; }
+                        if (z1) c1 = zero;
+                        const int r = r0 + 8 * NDQ * pp;
+                        const uint32_t line = as + (r >> 3) * 1024 + (r & 7) * 128;
+                        sts128(line + ((q ^ (r & 7)) << 4), c0);
+                        sts128(line + (((4 + q) ^ (r & 7)) << 4), c1);
+                    }
+                    fence_async_shared();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&full_a[s]);
+                    if (++s == S_) { s = 0; ph ^= 1u; }
+                }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&full_a[s]);
-                if (++s == S_) { s = 0; ph ^= 1u; }
-                cur = nxt;
+                if (lane == 0) mbar_arrive(&wempty[js]);
+                if (++js == SW) { js = 0; jph ^= 1u; }
             }
+            if (!ok) break;
         }
-    } else {
+    } else if (is_epilogue(warp)) {
         // -------------------------------------------------------------- epilogue
         const int q = warp & 3;        // TMEM lane quadrant
         const int r = 32 * q + lane;   // W row within the tile
         int t_local = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t_local) {
-            if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
+            if (__shfl_sync(FULL, *abort_flag, 0)) break;
             const int mt = tile / p.n_ntiles, nt = tile % p.n_ntiles;
             const int tb = t_local & 1;
             const uint32_t tph = (t_local >> 1) & 1;
             const bool got = mbar_wait_bounded(&tfull[tb], tph, DEV_TIMEOUT_MMA);
-            if (!__all_sync(0xffffffffu, got)) {
+            if (!__all_sync(FULL, got)) {
                 *abort_flag = 1;
                 break;
             }
@@ -653,32 +769,46 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 
     // Teardown: every role has left its loop (all waits are bounded), the MMA
-    // lane has seen its last commit and the TMA lane its last load.
+    // lane has seen its last commit and the producers their last loads.
     __syncwarp();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * BN));
+    if (warp == WARP_MMA)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * BN));
 }
 
 }  // namespace tc
 
-// fp32 -> fp16 activations (row-major, same shape).
-template <bool VEC>
+// fp32 -> fp16 activations in the K order of the tensor-core GEMM: within each
+// 256-element group, position p holds element tc_elem(F2, p).  One thread per
+// 8 positions = two runs of four consecutive elements (float4 when aligned).
+template <bool F2, bool VEC>
 __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__ X, __half* __restrict__ Xh,
-                                                       int64_t n) {
-    const int64_t n4 = n / 4;  // n is a multiple of 32
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+                                                       int M, int K) {
+    const int cpr = K / 8;  // 8-position chunks per row
+    const int64_t total = static_cast<int64_t>(M) * cpr;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        float4 v;
+        const int64_t tok = i / cpr;
+        const int p0 = static_cast<int>(i - tok * cpr) * 8;
+        const int g = p0 & ~255, pp = p0 & 255;
+        const float* xr = X + tok * K + g;
+        const int e0 = tc::tc_elem(F2, pp), e1 = tc::tc_elem(F2, pp + 4);
+        float4 a, b;
         if (VEC) {
-            v = reinterpret_cast<const float4*>(X)[i];
+            a = *reinterpret_cast<const float4*>(xr + e0);
+            b = *reinterpret_cast<const float4*>(xr + e1);
         } else {
-            v.x = X[4 * i]; v.y = X[4 * i + 1]; v.z = X[4 * i + 2]; v.w = X[4 * i + 3];
+            a = make_float4(xr[e0], xr[e0 + 1], xr[e0 + 2], xr[e0 + 3]);
+            b = make_float4(xr[e1], xr[e1 + 1], xr[e1 + 2], xr[e1 + 3]);
         }
-        __half2* o = reinterpret_cast<__half2*>(Xh) + 2 * i;
-        o[0] = __floats2half2_rn(v.x, v.y);
-        o[1] = __floats2half2_rn(v.z, v.w);
+        uint4 o;
+        o.x = tc::pack_h2(a.x, a.y);
+        o.y = tc::pack_h2(a.z, a.w);
+        o.z = tc::pack_h2(b.x, b.y);
+        o.w = tc::pack_h2(b.z, b.w);
+        *reinterpret_cast<uint4*>(Xh + tok * K + p0) = o;
     }
     pdl_launch_dependents();
 }
@@ -704,105 +834,155 @@ static EncodeTiledFn2 encode_fn2() {
     return fn;
 }
 
-static int type_qk(int t) { return (t == Q4_0 || t == Q8_0) ? 32 : 256; }
-static int type_bb(int t) {
-    switch (t) {
-        case Q4_0: return 18;
-        case Q8_0: return 34;
-        case Q2_K: return 84;
-        case Q3_K: return 110;
-        case Q4_K: return 144;
-        case Q5_K: return 176;
-        case Q6_K: return 210;
-        default: return 0;
-    }
-}
-
 bool gemm_tc_supported(int type, const void* W, int M, int N, int K, int refcpu) {
-    if (type_bb(type) == 0 || M <= 0 || N <= 0 || K <= 0 || K % 32 != 0) return false;
+    if (tc::tc_fmt(type).qk == 0 || M <= 0 || N <= 0 || K <= 0 || K % 32 != 0) return false;
     if (refcpu && type == Q2_K) return false;  // the GEMV kernel serves that activation order
-    // Weight loads: 16-byte vectors for Q4_K/Q5_K, 4-byte words for Q2_K, 2-byte
-    // halves otherwise; every row start keeps the base alignment.
-    const uintptr_t w = reinterpret_cast<uintptr_t>(W);
-    const uintptr_t need = (type == Q4_K || type == Q5_K) ? 16 : (type == Q2_K ? 4 : 2);
-    if (w % need != 0) return false;
+    // Shared-memory reads of the staged blocks are 2-byte aligned at least.
+    if (reinterpret_cast<uintptr_t>(W) % 2 != 0) return false;
     return encode_fn2() != nullptr;
 }
 
-template <int T, int BN>
+// Shared memory of one launch: A/B ring of `stages`, W ring of `wstages`.
+static size_t tc_smem_bytes(int bn, int stages, int wstages, int wp) {
+    const size_t bars = static_cast<size_t>(3 * stages + 2 * wstages + 5) * 8 + 8;
+    return 1024 + static_cast<size_t>(stages) * (tc::A_STAGE + bn * tc::BK * 2) +
+           static_cast<size_t>(wstages) * tc::BM * wp + 16 + bars;
+}
+
+template <int T, int BN, bool A4>
 static cudaError_t launch_tc(const void* W, const __half* Xh, float* Y, int M, int N, int K, int num_sms,
                              cudaStream_t stream) {
+    constexpr tc::TcFmt F = tc::tc_fmt(T);
     tc::Params p{};
     p.W = static_cast<const uint8_t*>(W);
     p.Y = Y;
     p.M = M;
     p.N = N;
     p.K = K;
-    p.row_bytes = (K / type_qk(T)) * type_bb(T);
+    p.nblocks = K / F.qk;
+    p.row_bytes = p.nblocks * F.bb;
     p.n_mtiles = (M + BN - 1) / BN;
     p.n_ntiles = (N + tc::BM - 1) / tc::BM;
     p.ksteps = (K + tc::BK - 1) / tc::BK;
-    constexpr int B_STAGE = BN * tc::BK * 2;
-    const int per_stage = tc::A_STAGE + B_STAGE;
-    int stages = (200 * 1024) / per_stage;
-    stages = std::max(2, std::min(stages, 6));
-    p.stages = stages;
-    const size_t smem = 1024 + static_cast<size_t>(stages) * per_stage + (3 * stages + 5) * 8 + 16;
+    p.ngroups = (K + tc::KG - 1) / tc::KG;
+    const uintptr_t w = reinterpret_cast<uintptr_t>(W);
+    const size_t wbytes = static_cast<size_t>(N) * p.row_bytes;
+    p.w_lo = reinterpret_cast<const uint8_t*>(w & ~uintptr_t(15));
+    p.w_hi = reinterpret_cast<const uint8_t*>((w + wbytes + 15) & ~uintptr_t(15));
 
-    CUtensorMap xmap;
-    std::memset(&xmap, 0, sizeof(xmap));
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(tc::BK), static_cast<cuuint32_t>(BN)};
-    const cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode_fn2()(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(Xh), dims, strides, box,
-                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    // One 2-D tensor-map copy per W stage needs 16-byte aligned rows; otherwise
+    // one bulk copy per row from the 16-byte boundary at or below the row's data.
+    bool tmap = (w % 16 == 0) && (p.row_bytes % 16 == 0);
+    for (int attempt = 0; attempt < 2; ++attempt) {
+        const bool offs = !tmap || (F.gbytes % 16 != 0);  // data may start up to 14 bytes into a smem row
+        int wp = (F.gbytes + (offs ? 14 : 0) + 15) / 16 * 16;
+        if ((wp / 16) % 2 == 0) wp += 16;  // odd multiple of 16: conflict-free across 8 rows
+        p.wp = wp;
+        p.rows_mode = tmap ? 0 : 1;
 
-    auto kern = tc::gemm_kernel<T, BN>;
-    static thread_local int set_dev = -1;
-    int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev != set_dev) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        // Deepest A/B ring that fits beside three W stages (two if three leave
+        // fewer than three A/B stages).
+        p.stages = 0;
+        for (int sw : {3, 2}) {
+            for (int st = 8; st >= 2; --st) {
+                if (tc_smem_bytes(BN, st, sw, wp) <= 227 * 1024) {
+                    p.stages = st;
+                    p.wstages = sw;
+                    break;
+                }
+            }
+            if (p.stages >= 3) break;
+        }
+        if (p.stages == 0) return cudaErrorInvalidConfiguration;
+
+        CUtensorMap wmap;
+        std::memset(&wmap, 0, sizeof(wmap));
+        if (tmap) {
+            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.row_bytes / 2), static_cast<cuuint64_t>(N)};
+            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.row_bytes)};
+            const cuuint32_t box[2] = {static_cast<cuuint32_t>(wp / 2), static_cast<cuuint32_t>(tc::BM)};
+            const cuuint32_t estr[2] = {1, 1};
+            CUresult r = encode_fn2()(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(W), dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) {
+                tmap = false;  // per-row copies need no tensor map
+                continue;
+            }
+        }
+
+        CUtensorMap xmap;
+        std::memset(&xmap, 0, sizeof(xmap));
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(tc::BK), static_cast<cuuint32_t>(BN)};
+        const cuuint32_t estr[2] = {1, 1};
+        CUresult r = encode_fn2()(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(Xh), dims, strides,
+                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+
+        auto kern = tc::gemm_kernel<T, BN, A4>;
+        static thread_local int set_dev = -1;
+        int dev = -1;
+        cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return e;
-        set_dev = dev;
+        if (dev != set_dev) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+            if (e != cudaSuccess) return e;
+            set_dev = dev;
+        }
+        const int ntiles = p.n_mtiles * p.n_ntiles;
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(std::min(ntiles, num_sms));
+        cfg.blockDim = dim3(tc::THREADS);
+        cfg.dynamicSmemBytes = tc_smem_bytes(BN, p.stages, p.wstages, p.wp);
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, kern, p, xmap, wmap);
     }
-    const int ntiles = p.n_mtiles * p.n_ntiles;
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(std::min(ntiles, num_sms));
-    cfg.blockDim = dim3(tc::THREADS);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, p, xmap);
+    return cudaErrorInvalidValue;
+}
+
+template <int T, bool A4>
+static cudaError_t launch_tc_bn(const void* W, const __half* Xh, float* Y, int M, int N, int K, int num_sms,
+                                cudaStream_t s) {
+    if (M <= 64) return launch_tc<T, 64, A4>(W, Xh, Y, M, N, K, num_sms, s);
+    if (M <= 128) return launch_tc<T, 128, A4>(W, Xh, Y, M, N, K, num_sms, s);
+    return launch_tc<T, 256, A4>(W, Xh, Y, M, N, K, num_sms, s);
 }
 
 template <int T>
 static cudaError_t launch_tc_fmt(const void* W, const __half* Xh, float* Y, int M, int N, int K, int num_sms,
                                  cudaStream_t s) {
-    if (M <= 64) return launch_tc<T, 64>(W, Xh, Y, M, N, K, num_sms, s);
-    if (M <= 128) return launch_tc<T, 128>(W, Xh, Y, M, N, K, num_sms, s);
-    return launch_tc<T, 256>(W, Xh, Y, M, N, K, num_sms, s);
+    // Q4_K, Q5_K and Q2_K keep every field of a block 4-byte aligned when W is.
+    if constexpr (T == Q4_K || T == Q5_K || T == Q2_K) {
+        if (reinterpret_cast<uintptr_t>(W) % 4 == 0) return launch_tc_bn<T, true>(W, Xh, Y, M, N, K, num_sms, s);
+    }
+    return launch_tc_bn<T, false>(W, Xh, Y, M, N, K, num_sms, s);
 }
 
-// X -> fp16 into Xh (M*K halves), then the GEMM that reads Xh.
+template <bool F2>
+static cudaError_t launch_x_to_f16(const float* X, __half* Xh, int M, int K, int num_sms, cudaStream_t s) {
+    const int64_t total = static_cast<int64_t>(M) * (K / 8);
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256,
+                                                                            static_cast<int64_t>(num_sms) * 8)));
+    if ((reinterpret_cast<uintptr_t>(X) & 15u) == 0)
+        x_to_f16_kernel<F2, true><<<grid, 256, 0, s>>>(X, Xh, M, K);
+    else
+        x_to_f16_kernel<F2, false><<<grid, 256, 0, s>>>(X, Xh, M, K);
+    return cudaGetLastError();
+}
+
+// X -> fp16 into Xh (M*K halves, K order of the format), then the GEMM.
 static cudaError_t gemm_tc_run(int type, const void* W, const float* X, __half* Xh, float* Y, int M, int N, int K,
                                int num_sms, cudaStream_t s) {
-    const int64_t n = static_cast<int64_t>(M) * K;
-    const int64_t n4 = n / 4;
-    const int grid = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(num_sms) * 8));
-    if ((reinterpret_cast<uintptr_t>(X) & 15u) == 0)
-        x_to_f16_kernel<true><<<std::max(grid, 1), 256, 0, s>>>(X, Xh, n);
-    else
-        x_to_f16_kernel<false><<<std::max(grid, 1), 256, 0, s>>>(X, Xh, n);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, M, K, num_sms, s)
+                                        : launch_x_to_f16<false>(X, Xh, M, K, num_sms, s);
     if (e != cudaSuccess) return e;
     switch (type) {
         case Q4_0: return launch_tc_fmt<Q4_0>(W, Xh, Y, M, N, K, num_sms, s);
@@ -816,12 +996,42 @@ static cudaError_t gemm_tc_run(int type, const void* W, const float* X, __half* 
     }
 }
 
+// Stream-ordered pool of the current device for the fp16 copy of X.  The pool
+// belongs to libswq and keeps freed memory for the next call (release threshold
+// = unlimited), so a call costs no trip to the driver's allocator once the
+// largest scratch has been seen.
+static cudaError_t scratch_pool(cudaMemPool_t* out) {
+    static std::mutex mu;
+    static std::map<int, cudaMemPool_t> pools;
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = pools.find(dev);
+    if (it == pools.end()) {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t pool = nullptr;
+        if ((e = cudaMemPoolCreate(&pool, &props)) != cudaSuccess) return e;
+        uint64_t keep = UINT64_MAX;
+        if ((e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep)) != cudaSuccess) return e;
+        it = pools.emplace(dev, pool).first;
+    }
+    *out = it->second;
+    return cudaSuccess;
+}
+
 cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, int M, int N, int K, int refcpu,
                            int num_sms, cudaStream_t s) {
     if (!gemm_tc_supported(type, W, M, N, K, refcpu)) return cudaErrorNotSupported;
     const int64_t n = static_cast<int64_t>(M) * K;
+    cudaMemPool_t pool = nullptr;
+    cudaError_t e = scratch_pool(&pool);
+    if (e != cudaSuccess) return e;
     __half* Xh = nullptr;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&Xh), static_cast<size_t>(n) * 2, s);
+    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), static_cast<size_t>(n) * 2, pool, s);
     if (e != cudaSuccess) return e;
     e = gemm_tc_run(type, W, X, Xh, Y, M, N, K, num_sms, s);
     cudaError_t e2 = cudaFreeAsync(Xh, s);
@@ -833,7 +1043,7 @@ cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, in
 // owns the GPU's memory through its own allocator (a serving engine that
 // reserves HBM for its KV cache at start-up, a caching allocator that hands
 // out every device byte) cannot let this library take a temporary buffer from
-// cudaMallocAsync.  For them the fp16 copy of X lives in this fixed array,
+// a stream-ordered pool of its own.  For them the fp16 copy of X lives in this fixed array,
 // which every GPU that loads libswq holds until the process exits.  In host
 // code `g_noalloc_x16` only names the array; its address on a device comes
 // from cudaGetSymbolAddress with that device current, looked up once per

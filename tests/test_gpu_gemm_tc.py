@@ -36,7 +36,7 @@ def _tensor_core_on():
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-@pytest.mark.parametrize("M", [9, 64, 130, 256])
+@pytest.mark.parametrize("M", [9, 64, 100, 130, 256])
 def test_formats(cuda, oracle_mod, fmt, M):
     t = synth.IDS[fmt]
     qk, _ = synth.block_geometry(t)
@@ -74,22 +74,36 @@ def test_llama_ffn_shape(cuda, oracle_mod, fmt, M):
     assert rel_l2(got, oracle_mod.gemm(t, blocks, X, M, N, K)) <= REL_L2_TOL
 
 
-def test_gemv_path_when_unaligned(cuda, oracle_mod):
-    """Q4_K weights not 16-byte aligned: the tensor-core GEMM declines and the
-    GEMV kernel serves every row group."""
+@pytest.mark.parametrize("fmt,K,off", [("Q4_K", 1024, 8), ("Q4_K", 1024, 2), ("Q5_K", 2048, 4), ("Q6_K", 2048, 2),
+                                        ("Q2_K", 768, 0), ("Q3_K", 1280, 0), ("Q8_0", 1024, 6), ("Q4_0", 1056, 2)])
+def test_row_copies(cuda, oracle_mod, fmt, K, off):
+    """Rows not 16-byte aligned (W offset from its allocation, or a row size
+    that is not a multiple of 16): the W stages arrive as one copy per row and
+    each row's blocks start part way into their shared-memory row."""
     torch = cuda
-    t = synth.Q4_K
-    N, K, M = 256, 1024, 40
-    blocks = synth.random_blocks(t, N, K, seed=2300)
+    t = synth.IDS[fmt]
+    N, M = 200, 40
+    blocks = synth.random_blocks(t, N, K, seed=2300 + off)
     X = synth.random_activations(M, K, seed=2301)
     flat = blocks.reshape(-1)
     d_w = torch.zeros(flat.size + 64, dtype=torch.uint8, device="cuda")
-    d_w[8:8 + flat.size] = torch.from_numpy(flat).cuda()
+    d_w[off:off + flat.size] = torch.from_numpy(flat).cuda()
     d_x = torch.from_numpy(X).cuda()
-    d_y = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    swq.gemm(t, d_w.data_ptr() + 8, d_x, d_y, M, N, K)
+    d_y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    swq.gemm(t, d_w.data_ptr() + off, d_x, d_y, M, N, K)
     swq.check()
     assert rel_l2(d_y.cpu().numpy(), oracle_mod.gemm(t, blocks, X, M, N, K)) <= REL_L2_TOL
+
+
+def test_gemv_groups_when_disabled(cuda, oracle_mod):
+    """SWQ_OPT_TENSOR_CORE_GEMM = 0: groups of rows through the GEMV kernel."""
+    t = synth.Q4_K
+    N, K, M = 256, 1024, 40
+    blocks = synth.random_blocks(t, N, K, seed=2350)
+    X = synth.random_activations(M, K, seed=2351)
+    swq.set_option(swq.OPT_TENSOR_CORE_GEMM, 0)
+    got = _gemm(cuda, t, blocks, X, N, K)
+    assert rel_l2(got, oracle_mod.gemm(t, blocks, X, M, N, K)) <= REL_L2_TOL
 
 
 def test_deterministic(cuda):
