@@ -9,6 +9,11 @@ A step is one GEMV over each of COPIES distinct weight matrices (64 x 9.4 MB
 = 604 MB, more than 4x the 126 MB L2, so every step streams from HBM).  The
 COPIES launches of a step are one CUDA graph; the timed region replays it.
 
+--workload gemm measures the prefill dequant-GEMM instead (one line, not the
+headline): Y[M x N] = X[M x K] . W^T for the Llama-3-8B FFN up-projection
+shape N=14336, K=4096 (default Q4_K, M=512), rotating over weight copies that
+exceed 4x L2, through swq_gemm on the tensor cores.
+
 Arms:
   --impl swq (default): libswq on each GPU.  Under torchrun every rank runs
       its own stream of GEMVs on its own weights (weak scaling, no data-path
@@ -62,6 +67,17 @@ def load_peaks() -> tuple[float, str]:
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def load_tensor_peak() -> tuple[float, str]:
+    """Dense bf16 TFLOP/s of this pool's B200s: the burst figure (a kernel
+    timed in a loop of well under a second is not power-capped for long)."""
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return 1590.0, "fallback"
 
 
 # ---------------------------------------------------------------- clocks
@@ -297,12 +313,136 @@ def run_swq(args, rank: int, world: int) -> None:
         print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- GEMM workload
+GEMM_N, GEMM_K = 14336, 4096
+TYPE_IDS = {"Q4_0": 2, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
+# dram__bytes_read.sum + dram__bytes_write.sum of one gemm_kernel launch, Q4_K
+# N=14336 K=4096 M=512, from one ncu capture (profiles/gemm_q4k_14336x4096_m512.md).
+NCU_TRAFFIC_GEMM_Q4K_M512 = 37_271_552 + 1_266_944
+
+
+def cpu_gemm_timing(type_id: int, M: int, seconds: float) -> dict | None:
+    """The reference's prefill: one Compute::matmul_transposed_q per token, on
+    all host cores.  A bounded sample of tokens; TFLOP/s of the rows done."""
+    import oracle
+    from swq import synth
+    if seconds <= 0:
+        return None
+    cores = oracle.host_cores()
+    if oracle.ref_available():
+        kind = "reference"
+        oracle.ref_set_threads(cores)
+        fn = lambda w, x: oracle.ref_gemv(type_id, w, x, GEMM_N, GEMM_K)  # noqa: E731
+    else:
+        kind = "port"
+        oracle.set_threads(cores)
+        fn = lambda w, x: oracle.gemv(type_id, w, x, GEMM_N, GEMM_K, format_order=False)  # noqa: E731
+    w = synth.random_blocks(type_id, GEMM_N, GEMM_K, seed=77)
+    X = synth.random_activations(min(M, 64), GEMM_K, seed=78)
+    fn(w, X[0])
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        fn(w, X[n % X.shape[0]])
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= M:
+            break
+    tf = 2.0 * GEMM_N * GEMM_K * n / el / 1e12
+    return {"value": round(tf, 5), "unit": "TFLOP/s", "cores": cores, "kind": kind,
+            "sample": f"{n} of the M={M} token rows (one matmul_transposed_q each), {el:.1f} s, "
+                      f"{cores} OpenMP threads"}
+
+
+def run_gemm(args, rank: int, world: int) -> None:
+    import numpy as np
+    import torch
+
+    import swq
+    from swq import synth
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    t = TYPE_IDS[args.format]
+    M, N, K = args.M, GEMM_N, GEMM_K
+    wbytes = synth.matrix_bytes(t, N, K)
+    copies = max(2, -(-4 * 126_000_000 // wbytes))
+    host_ws = [synth.random_blocks(t, N, K, seed=20_000 + i) for i in range(copies)]
+    d_ws = [torch.from_numpy(w.reshape(-1)).to(dev) for w in host_ws]
+    X = synth.random_activations(M, K, seed=21)
+    d_x = torch.from_numpy(X).to(dev)
+    d_y = torch.empty((M, N), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(max(3, args.warmup)):
+            swq.gemm(t, d_ws[i % copies], d_x, d_y, M, N, K, stream=stream)
+    swq.check(stream)
+    gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    gpu_uuid = gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}"
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_uuid) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for i in range(args.steps):
+                swq.gemm(t, d_ws[i % copies], d_x, d_y, M, N, K, stream=stream)
+            ev1.record(stream)
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    swq.check(stream)
+    flops = 2.0 * M * N * K
+    per_call_s = ms * 1e-3 / args.steps
+    value = flops * world / per_call_s / 1e12
+    peak, peak_kind = load_tensor_peak()
+
+    # End to end through the host-buffer API: host X in, host Y out.
+    comp = swq.Compute(device=local)
+    Y = np.zeros((M, N), np.float32)
+    qw = swq.QuantWeight(host_ws[0], t)
+    comp.matmul_q_batched(Y, X, qw, M, N, K)  # weights uploaded once
+    e2e_steps = max(1, min(args.steps, 50))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        comp.matmul_q_batched(Y, X, qw, M, N, K)
+    e2e_s = time.perf_counter() - t0
+    comp.close()
+    if rank != 0:
+        return
+    line = {
+        "metric": "dequant-GEMM TFLOP/s (prefill, N=14336 K=4096)", "value": round(value, 1),
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
+        "config": {"workload": f"{args.format} dequant-GEMM M={M} N={N} K={K}, {copies} rotating weight copies",
+                   "format": args.format, "M": M, "N": N, "K": K, "copies": copies,
+                   "l2": "inputs larger than L2 (rotating weights)"},
+        "roofline": {"bound": "tensor", "achieved": round(flops / per_call_s / 1e12, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(flops / per_call_s / 1e12 / peak, 4),
+                     "peak_kind": peak_kind,
+                     "traffic": NCU_TRAFFIC_GEMM_Q4K_M512 if (args.format, M) == ("Q4_K", 512) else None,
+                     "kernel": "swq::tc::gemm_kernel (+ x_to_f16_kernel)",
+                     "us_per_call": round(per_call_s * 1e6, 2)},
+        "cpu_baseline": cpu_gemm_timing(t, M, args.cpu_seconds) if world == 1 else None,
+        "e2e": {"value": round(flops * e2e_steps / e2e_s / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 4 * M * K, "d2h_bytes_per_step": 4 * M * N,
+                "api": "swq_ctx_matmul_q_batched (host fp32 X/Y, resident weights)", "steps": e2e_steps},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["swq", "reference"], default="swq")
+    ap.add_argument("--workload", choices=["gemv", "gemm"], default="gemv",
+                    help="gemv: the headline Q4_K GEMV; gemm: the prefill dequant-GEMM")
+    ap.add_argument("--format", choices=sorted(TYPE_IDS), default="Q4_K", help="GEMM weight format")
+    ap.add_argument("--M", type=int, default=512, help="GEMM activation rows")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU sample length (0: skip)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -312,6 +452,11 @@ def main() -> None:
     if args.warmup < 3:
         log("warm-up raised to 3 steps (minimum)")
         args.warmup = 3
+    if args.workload == "gemm":
+        if args.steps == ap.get_default("steps"):
+            args.steps = 2000
+        run_gemm(args, rank, world)
+        return
     run_swq(args, rank, world)
 
 

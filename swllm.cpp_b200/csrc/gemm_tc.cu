@@ -202,8 +202,8 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) { return h2u(__flo
 // (1024 + byte0, 1024 + byte1) and (1024 + byte2, 1024 + byte3) as fp16 pairs
 __device__ __forceinline__ uint32_t h2b01(uint32_t q) { return __byte_perm(q, 0x64646464u, 0x4140u); }
 __device__ __forceinline__ uint32_t h2b23(uint32_t q) { return __byte_perm(q, 0x64646464u, 0x4342u); }
-__device__ __forceinline__ uint32_t bc_lo(uint32_t h) { return __byte_perm(h, 0u, 0x1010u); }  // (h.x, h.x)
-__device__ __forceinline__ uint32_t bc_hi(uint32_t h) { return __byte_perm(h, 0u, 0x3232u); }  // (h.y, h.y)
+__device__ __forceinline__ uint32_t bc_lo(uint32_t h) { return h2u(__low2half2(u2h(h))); }   // (h.x, h.x)
+__device__ __forceinline__ uint32_t bc_hi(uint32_t h) { return h2u(__high2half2(u2h(h))); }  // (h.y, h.y)
 
 // (v - bias) * d + n  and  (v - bias) * d, on fp16 pairs; v - bias is exact.
 __device__ __forceinline__ uint32_t fq(uint32_t v, uint32_t bias, uint32_t d, uint32_t n) {
@@ -222,11 +222,15 @@ constexpr uint32_t B1152 = 0x64806480u;  // 1024 + 128
 // fp16 bits (low 16) -> (h, h) pair
 __device__ __forceinline__ uint32_t bc_bits(uint32_t b) { return (b & 0xFFFFu) * 0x10001u; }
 
-// ---- per-format dequantization of one step, one row, one lane ------------------
+// ---- per-format dequantization of one W stage, one row, one lane -------------
 //
-// hdr(): per block (256-element formats), each lane precomputes the scales it
-// hands to the row's other lanes (lane q of a row is warp lane rr + 8 q).
-// step(): the lane's 16 elements of step s as two 16-byte chunks (c0: t = 0,
+// load(): once per W stage (256 elements of the row), everything the lane needs
+// for the stage's four steps -- its quant words and its scales -- into
+// registers.  Scales are computed once per block, lane q of a row for part of
+// the block, and handed to the row's other lanes (lane q of a row is warp lane
+// rr + 8 q); the shuffles run here, on all 32 lanes.  After load() the stage's
+// shared memory is no longer read.
+// emit(s): the lane's 16 elements of step s as two 16-byte chunks (c0: t = 0,
 // c1: t = 1) in the order of tc_elem.  `blk` is the shared-memory byte address
 // of the block (256-element formats) or of the 8-block group (Q4_0, Q8_0).
 
@@ -235,23 +239,37 @@ struct Dq;
 
 template <>
 struct Dq<Q4_K> {  // d @0, dmin @2, scales[12] @4, qs[128] @16 (src/tensor.h:196-227)
-    struct Hdr { uint32_t dd, mm; };  // (d1, d2), (-m1, -m2) of sub-blocks 2q, 2q + 1
+    struct Stage {
+        uint32_t wa[4], wb[4];  // qs words q and q + 4 of step s's 32 bytes
+        uint32_t dd[4], mm[4];  // (d1, d2), (-m1, -m2) of sub-blocks 2s, 2s + 1
+    };
+    // (d * sc, -dmin * m) of sub-blocks 2q and 2q + 1
     template <bool A4>
-    __device__ static void hdr(uint32_t blk, int q, Hdr& h) {
+    __device__ static void scales(uint32_t blk, int q, uint32_t& dd, uint32_t& mm) {
         const uint32_t w0 = ldw<A4>(blk), s0 = ldw<A4>(blk + 4), s1 = ldw<A4>(blk + 8), s2 = ldw<A4>(blk + 12);
         const float d = h2f(w0 & 0xFFFFu), dmin = h2f(w0 >> 16);
         uint32_t sc0, m0, sc1, m1;
         scale_min_k4_unit(q, 0, s0, s1, s2, sc0, m0);
         scale_min_k4_unit(q, 1, s0, s1, s2, sc1, m1);
-        h.dd = pack_h2(d * static_cast<float>(sc0), d * static_cast<float>(sc1));
-        h.mm = pack_h2(-(dmin * static_cast<float>(m0)), -(dmin * static_cast<float>(m1)));
+        dd = pack_h2(d * static_cast<float>(sc0), d * static_cast<float>(sc1));
+        mm = pack_h2(-(dmin * static_cast<float>(m0)), -(dmin * static_cast<float>(m1)));
     }
     template <bool A4>
-    __device__ static void step(uint32_t blk, const Hdr& h, int s, int q, int rr, uint4& c0, uint4& c1) {
-        const uint32_t a = blk + 16 + 32 * s + 4 * q;
-        const uint32_t wa = ldw<A4>(a), wb = ldw<A4>(a + 16);
-        const uint32_t dd = __shfl_sync(FULL, h.dd, rr + 8 * s), mm = __shfl_sync(FULL, h.mm, rr + 8 * s);
-        const uint32_t d0 = bc_lo(dd), d1 = bc_hi(dd), n0 = bc_lo(mm), n1 = bc_hi(mm);
+    __device__ static void load(uint32_t blk, int q, int rr, Stage& g) {
+        uint32_t dd, mm;
+        scales<A4>(blk, q, dd, mm);
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const uint32_t a = blk + 16 + 32 * s + 4 * q;
+            g.wa[s] = ldw<A4>(a);
+            g.wb[s] = ldw<A4>(a + 16);
+            g.dd[s] = __shfl_sync(FULL, dd, rr + 8 * s);
+            g.mm[s] = __shfl_sync(FULL, mm, rr + 8 * s);
+        }
+    }
+    __device__ static void emit(const Stage& g, int s, uint4& c0, uint4& c1) {
+        const uint32_t d0 = bc_lo(g.dd[s]), d1 = bc_hi(g.dd[s]), n0 = bc_lo(g.mm[s]), n1 = bc_hi(g.mm[s]);
+        const uint32_t wa = g.wa[s], wb = g.wb[s];
         const uint32_t la = wa & 0x0F0F0F0Fu, lb = wb & 0x0F0F0F0Fu;
         const uint32_t ha = (wa >> 4) & 0x0F0F0F0Fu, hb = (wb >> 4) & 0x0F0F0F0Fu;
         c0 = make_uint4(fq(h2b01(la), B1024, d0, n0), fq(h2b23(la), B1024, d0, n0),
@@ -263,17 +281,31 @@ struct Dq<Q4_K> {  // d @0, dmin @2, scales[12] @4, qs[128] @16 (src/tensor.h:19
 
 template <>
 struct Dq<Q5_K> {  // d @0, dmin @2, scales[12] @4, qh[32] @16, qs[128] @48 (src/tensor.h:329-365)
-    using Hdr = Dq<Q4_K>::Hdr;
+    struct Stage {
+        uint32_t wa[4], wb[4];  // qs words q and q + 4 of step s's 32 bytes
+        uint32_t qa, qb;        // qh bytes of elements 4q .. and 16 + 4q .. (bit j: sub-block j)
+        uint32_t dd[4], mm[4];
+    };
     template <bool A4>
-    __device__ static void hdr(uint32_t blk, int q, Hdr& h) { Dq<Q4_K>::hdr<A4>(blk, q, h); }
-    template <bool A4>
-    __device__ static void step(uint32_t blk, const Hdr& h, int s, int q, int rr, uint4& c0, uint4& c1) {
-        const uint32_t a = blk + 48 + 32 * s + 4 * q;
-        const uint32_t wa = ldw<A4>(a), wb = ldw<A4>(a + 16);
-        // qh bytes of elements 4q.. and 16 + 4q.., bit 2s + t for sub-block 2s + t
-        const uint32_t qa = ldw<A4>(blk + 16 + 4 * q) >> (2 * s), qb = ldw<A4>(blk + 32 + 4 * q) >> (2 * s);
-        const uint32_t dd = __shfl_sync(FULL, h.dd, rr + 8 * s), mm = __shfl_sync(FULL, h.mm, rr + 8 * s);
-        const uint32_t d0 = bc_lo(dd), d1 = bc_hi(dd), n0 = bc_lo(mm), n1 = bc_hi(mm);
+    __device__ static void load(uint32_t blk, int q, int rr, Stage& g) {
+        uint32_t dd, mm;
+        Dq<Q4_K>::scales<A4>(blk, q, dd, mm);
+        g.qa = ldw<A4>(blk + 16 + 4 * q);
+        g.qb = ldw<A4>(blk + 32 + 4 * q);
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const uint32_t a = blk + 48 + 32 * s + 4 * q;
+            g.wa[s] = ldw<A4>(a);
+            g.wb[s] = ldw<A4>(a + 16);
+            g.dd[s] = __shfl_sync(FULL, dd, rr + 8 * s);
+            g.mm[s] = __shfl_sync(FULL, mm, rr + 8 * s);
+        }
+    }
+    __device__ static void emit(const Stage& g, int s, uint4& c0, uint4& c1) {
+        const uint32_t d0 = bc_lo(g.dd[s]), d1 = bc_hi(g.dd[s]), n0 = bc_lo(g.mm[s]), n1 = bc_hi(g.mm[s]);
+        const uint32_t wa = g.wa[s], wb = g.wb[s];
+        const uint32_t qa = g.qa >> (2 * s), qb = g.qb >> (2 * s);
+        // high bit of sub-block 2s + t: bit 2s + t of the qh byte, moved to bit 4
         const uint32_t la = (wa & 0x0F0F0F0Fu) | ((qa << 4) & 0x10101010u);
         const uint32_t lb = (wb & 0x0F0F0F0Fu) | ((qb << 4) & 0x10101010u);
         const uint32_t ha = ((wa >> 4) & 0x0F0F0F0Fu) | ((qa << 3) & 0x10101010u);
@@ -285,30 +317,48 @@ struct Dq<Q5_K> {  // d @0, dmin @2, scales[12] @4, qh[32] @16, qs[128] @48 (src
     }
 };
 
+// Scales of the planes of Q6_K / Q3_K / Q2_K: index 8n + 2kk + hb for plane kk of
+// half n and l in 16hb ..; lane q computes indices 4q .. 4q + 3 and holds them as
+// a0 = (s[4q], s[4q+2]), a1 = (s[4q+1], s[4q+3]).  Step s (n = s/2, hb = s%2)
+// takes a_hb of lane 2n (planes 0, 1) and of lane 2n + 1 (planes 2, 3).
+__device__ __forceinline__ void plane_scales(uint32_t a0, uint32_t a1, int rr, uint32_t (&p01)[4],
+                                             uint32_t (&p23)[4]) {
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const int n = s >> 1;
+        const uint32_t mine = (s & 1) ? a1 : a0;
+        p01[s] = __shfl_sync(FULL, mine, rr + 16 * n);
+        p23[s] = __shfl_sync(FULL, mine, rr + 16 * n + 8);
+    }
+}
+
 template <>
 struct Dq<Q6_K> {  // ql[128] @0, qh[64] @128, scales[16] (int8) @192, d @208 (src/tensor.h:368-403)
-    // Scale index 8n + 2kk + hb for plane kk of half n, l in 16hb ..: lane q
-    // holds d * s[4q .. 4q+3] as a0 = (s[4q], s[4q+2]), a1 = (s[4q+1], s[4q+3]).
-    struct Hdr { uint32_t a0, a1; };
+    struct Stage {
+        uint32_t wa[4], wb[4], wc[4];  // ql[64n + l], ql[64n + 32 + l], qh[32n + l] for l = 16hb + 4q ..
+        uint32_t s01[4], s23[4];       // d * scale of planes (0, 1) and (2, 3)
+    };
     template <bool A4>
-    __device__ static void hdr(uint32_t blk, int q, Hdr& h) {
+    __device__ static void load(uint32_t blk, int q, int rr, Stage& g) {
         const uint32_t sw = ldw<A4>(blk + 192 + 4 * q);
         const float d = h2f(lds16(blk + 208));
         const float s0 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 0)));
         const float s1 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 1)));
         const float s2 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 2)));
         const float s3 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 3)));
-        h.a0 = pack_h2(d * s0, d * s2);
-        h.a1 = pack_h2(d * s1, d * s3);
+        plane_scales(pack_h2(d * s0, d * s2), pack_h2(d * s1, d * s3), rr, g.s01, g.s23);
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const int n = s >> 1, hb = s & 1;
+            const uint32_t a = blk + 64 * n + 16 * hb + 4 * q;
+            g.wa[s] = ldw<A4>(a);
+            g.wb[s] = ldw<A4>(a + 32);
+            g.wc[s] = ldw<A4>(blk + 128 + 32 * n + 16 * hb + 4 * q);
+        }
     }
-    template <bool A4>
-    __device__ static void step(uint32_t blk, const Hdr& h, int s, int q, int rr, uint4& c0, uint4& c1) {
-        const int n = s >> 1, hb = s & 1;
-        const uint32_t a = blk + 64 * n + 16 * hb + 4 * q;
-        const uint32_t wa = ldw<A4>(a), wb = ldw<A4>(a + 32), wc = ldw<A4>(blk + 128 + 32 * n + 16 * hb + 4 * q);
-        const uint32_t mine = hb ? h.a1 : h.a0;
-        const uint32_t s01 = __shfl_sync(FULL, mine, rr + 16 * n), s23 = __shfl_sync(FULL, mine, rr + 16 * n + 8);
-        const uint32_t sc0 = bc_lo(s01), sc1 = bc_hi(s01), sc2 = bc_lo(s23), sc3 = bc_hi(s23);
+    __device__ static void emit(const Stage& g, int s, uint4& c0, uint4& c1) {
+        const uint32_t sc0 = bc_lo(g.s01[s]), sc1 = bc_hi(g.s01[s]), sc2 = bc_lo(g.s23[s]), sc3 = bc_hi(g.s23[s]);
+        const uint32_t wa = g.wa[s], wb = g.wb[s], wc = g.wc[s];
         const uint32_t c4 = wc << 4;  // qh bits 2kk .. 2kk + 1 of each byte to bits 4 .. 5
         const uint32_t p0 = (wa & 0x0F0F0F0Fu) | (c4 & 0x30303030u);
         const uint32_t p1 = (wb & 0x0F0F0F0Fu) | ((c4 >> 2) & 0x30303030u);
@@ -323,9 +373,12 @@ struct Dq<Q6_K> {  // ql[128] @0, qh[64] @128, scales[16] (int8) @192, d @208 (s
 
 template <>
 struct Dq<Q2_K> {  // scales[16] @0, qs[64] @16, d @80, dmin @82 (src/tensor.h:232-265)
-    struct Hdr { uint32_t d0, d1, m0, m1; };  // (dl, -ml) of scale indices (4q, 4q+2), (4q+1, 4q+3)
+    struct Stage {
+        uint32_t w[4];                         // qs[32n + l], l = 16hb + 4q ..
+        uint32_t d01[4], d23[4], m01[4], m23[4];  // (dl, -ml) of planes (0, 1), (2, 3)
+    };
     template <bool A4>
-    __device__ static void hdr(uint32_t blk, int q, Hdr& h) {
+    __device__ static void load(uint32_t blk, int q, int rr, Stage& g) {
         const uint32_t sw = ldw<A4>(blk + 4 * q), dw = ldw<A4>(blk + 80);
         const float d = h2f(dw & 0xFFFFu), dmin = h2f(dw >> 16);
         float dl[4], ml[4];
@@ -335,22 +388,17 @@ struct Dq<Q2_K> {  // scales[16] @0, qs[64] @16, d @80, dmin @82 (src/tensor.h:2
             dl[i] = d * static_cast<float>(b & 15u);
             ml[i] = -(dmin * static_cast<float>(b >> 4));
         }
-        h.d0 = pack_h2(dl[0], dl[2]);
-        h.d1 = pack_h2(dl[1], dl[3]);
-        h.m0 = pack_h2(ml[0], ml[2]);
-        h.m1 = pack_h2(ml[1], ml[3]);
+        plane_scales(pack_h2(dl[0], dl[2]), pack_h2(dl[1], dl[3]), rr, g.d01, g.d23);
+        plane_scales(pack_h2(ml[0], ml[2]), pack_h2(ml[1], ml[3]), rr, g.m01, g.m23);
+#pragma unroll
+        for (int s = 0; s < 4; ++s) g.w[s] = ldw<A4>(blk + 16 + 32 * (s >> 1) + 16 * (s & 1) + 4 * q);
     }
-    template <bool A4>
-    __device__ static void step(uint32_t blk, const Hdr& h, int s, int q, int rr, uint4& c0, uint4& c1) {
-        const int n = s >> 1, hb = s & 1;
-        const uint32_t w = ldw<A4>(blk + 16 + 32 * n + 16 * hb + 4 * q);
-        const uint32_t dm = hb ? h.d1 : h.d0, mm = hb ? h.m1 : h.m0;
-        const uint32_t d01 = __shfl_sync(FULL, dm, rr + 16 * n), d23 = __shfl_sync(FULL, dm, rr + 16 * n + 8);
-        const uint32_t m01 = __shfl_sync(FULL, mm, rr + 16 * n), m23 = __shfl_sync(FULL, mm, rr + 16 * n + 8);
+    __device__ static void emit(const Stage& g, int s, uint4& c0, uint4& c1) {
+        const uint32_t w = g.w[s];
         const uint32_t p0 = w & 0x03030303u, p1 = (w >> 2) & 0x03030303u;
         const uint32_t p2 = (w >> 4) & 0x03030303u, p3 = (w >> 6) & 0x03030303u;
-        const uint32_t e0 = bc_lo(d01), e1 = bc_hi(d01), e2 = bc_lo(d23), e3 = bc_hi(d23);
-        const uint32_t f0 = bc_lo(m01), f1 = bc_hi(m01), f2 = bc_lo(m23), f3 = bc_hi(m23);
+        const uint32_t e0 = bc_lo(g.d01[s]), e1 = bc_hi(g.d01[s]), e2 = bc_lo(g.d23[s]), e3 = bc_hi(g.d23[s]);
+        const uint32_t f0 = bc_lo(g.m01[s]), f1 = bc_hi(g.m01[s]), f2 = bc_lo(g.m23[s]), f3 = bc_hi(g.m23[s]);
         c0 = make_uint4(fq(h2b01(p0), B1024, e0, f0), fq(h2b23(p0), B1024, e0, f0),
                         fq(h2b01(p1), B1024, e1, f1), fq(h2b23(p1), B1024, e1, f1));
         c1 = make_uint4(fq(h2b01(p2), B1024, e2, f2), fq(h2b23(p2), B1024, e2, f2),
@@ -360,9 +408,13 @@ struct Dq<Q2_K> {  // scales[16] @0, qs[64] @16, d @80, dmin @82 (src/tensor.h:2
 
 template <>
 struct Dq<Q3_K> {  // hmask[32] @0, qs[64] @32, scales[12] @96, d @108 (src/tensor.h:269-326)
-    using Hdr = Dq<Q6_K>::Hdr;  // d * signed scale, same index split as Q6_K
+    struct Stage {
+        uint32_t wq[4];        // qs[32n + l], l = 16hb + 4q ..
+        uint32_t wh0, wh1;     // hmask[l] for hb = 0, 1 (bit 4n + j: plane j of half n)
+        uint32_t s01[4], s23[4];
+    };
     template <bool A4>
-    __device__ static void hdr(uint32_t blk, int q, Hdr& h) {
+    __device__ static void load(uint32_t blk, int q, int rr, Stage& g) {
         const uint32_t t0 = ldw<A4>(blk + 96), t1 = ldw<A4>(blk + 100), t2 = ldw<A4>(blk + 104);
         const float d = h2f(lds16(blk + 108));
         const uint32_t sw = q3k_scale_word(q, t0, t1, t2);
@@ -370,18 +422,17 @@ struct Dq<Q3_K> {  // hmask[32] @0, qs[64] @32, scales[12] @96, d @108 (src/tens
         const float s1 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 1)));
         const float s2 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 2)));
         const float s3 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 3)));
-        h.a0 = pack_h2(d * s0, d * s2);
-        h.a1 = pack_h2(d * s1, d * s3);
+        plane_scales(pack_h2(d * s0, d * s2), pack_h2(d * s1, d * s3), rr, g.s01, g.s23);
+        g.wh0 = ldw<A4>(blk + 4 * q);
+        g.wh1 = ldw<A4>(blk + 16 + 4 * q);
+#pragma unroll
+        for (int s = 0; s < 4; ++s) g.wq[s] = ldw<A4>(blk + 32 + 32 * (s >> 1) + 16 * (s & 1) + 4 * q);
     }
-    template <bool A4>
-    __device__ static void step(uint32_t blk, const Hdr& h, int s, int q, int rr, uint4& c0, uint4& c1) {
-        const int n = s >> 1, hb = s & 1;
-        const uint32_t wq = ldw<A4>(blk + 32 + 32 * n + 16 * hb + 4 * q);
-        const uint32_t wh = ldw<A4>(blk + 16 * hb + 4 * q) >> (4 * n);  // plane j's high bit at bit j
-        const uint32_t mine = hb ? h.a1 : h.a0;
-        const uint32_t s01 = __shfl_sync(FULL, mine, rr + 16 * n), s23 = __shfl_sync(FULL, mine, rr + 16 * n + 8);
-        const uint32_t sc0 = bc_lo(s01), sc1 = bc_hi(s01), sc2 = bc_lo(s23), sc3 = bc_hi(s23);
-        const uint32_t h4 = wh << 2;  // bit j -> bit j + 2
+    __device__ static void emit(const Stage& g, int s, uint4& c0, uint4& c1) {
+        const int n = s >> 1;
+        const uint32_t sc0 = bc_lo(g.s01[s]), sc1 = bc_hi(g.s01[s]), sc2 = bc_lo(g.s23[s]), sc3 = bc_hi(g.s23[s]);
+        const uint32_t wq = g.wq[s];
+        const uint32_t h4 = ((s & 1) ? g.wh1 : g.wh0) >> (4 * n) << 2;  // plane j's bit at bit j + 2
         const uint32_t p0 = (wq & 0x03030303u) | (h4 & 0x04040404u);
         const uint32_t p1 = ((wq >> 2) & 0x03030303u) | ((h4 >> 1) & 0x04040404u);
         const uint32_t p2 = ((wq >> 4) & 0x03030303u) | ((h4 >> 2) & 0x04040404u);
@@ -394,42 +445,56 @@ struct Dq<Q3_K> {  // hmask[32] @0, qs[64] @32, scales[12] @96, d @108 (src/tens
 };
 
 template <>
-struct Dq<Q8_0> {  // d @0, qs[32] (int8) @2 (src/tensor.h:157-166)
-    struct Hdr {};
+struct Dq<Q8_0> {  // d @0, qs[32] (int8) @2 (src/tensor.h:157-166); a W stage is 8 blocks
+    struct Stage {
+        uint32_t d[8];          // (d, d) of block b
+        uint32_t wa[8], wb[8];  // quant words q and q + 4 of block b
+    };
     template <bool A4>
-    __device__ static void hdr(uint32_t, int, Hdr&) {}
-    // one 32-element block: words q and q + 4 of its quants (bytes as q + 128)
-    template <bool A4>
-    __device__ static uint4 blk32(uint32_t b, int q) {
-        const uint32_t d = bc_bits(lds16(b));
-        const uint32_t wa = ldw<A4>(b + 2 + 4 * q) ^ 0x80808080u, wb = ldw<A4>(b + 18 + 4 * q) ^ 0x80808080u;
+    __device__ static void load(uint32_t grp, int q, int, Stage& g) {
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            const uint32_t a = grp + 34 * b;
+            g.d[b] = bc_bits(lds16(a));
+            g.wa[b] = ldw<A4>(a + 2 + 4 * q);
+            g.wb[b] = ldw<A4>(a + 18 + 4 * q);
+        }
+    }
+    // block b: bytes as q + 128, then (1152 + q) - 1152
+    __device__ static uint4 blk32(const Stage& g, int b) {
+        const uint32_t d = g.d[b], wa = g.wa[b] ^ 0x80808080u, wb = g.wb[b] ^ 0x80808080u;
         return make_uint4(mq(h2b01(wa), B1152, d), mq(h2b23(wa), B1152, d), mq(h2b01(wb), B1152, d),
                           mq(h2b23(wb), B1152, d));
     }
-    template <bool A4>
-    __device__ static void step(uint32_t grp, const Hdr&, int s, int q, int, uint4& c0, uint4& c1) {
-        c0 = blk32<A4>(grp + 34 * (2 * s), q);
-        c1 = blk32<A4>(grp + 34 * (2 * s + 1), q);
+    __device__ static void emit(const Stage& g, int s, uint4& c0, uint4& c1) {
+        c0 = blk32(g, 2 * s);
+        c1 = blk32(g, 2 * s + 1);
     }
 };
 
 template <>
 struct Dq<Q4_0> {  // d @0, qs[16] @2: element l low nibble of byte l, l + 16 high (src/tensor.h:139-154)
-    struct Hdr {};
+    struct Stage {
+        uint32_t d[8], w[8];  // (d, d) and quant word q of block b of the 8-block group
+    };
     template <bool A4>
-    __device__ static void hdr(uint32_t, int, Hdr&) {}
-    template <bool A4>
-    __device__ static uint4 blk32(uint32_t b, int q) {
-        const uint32_t d = bc_bits(lds16(b));
-        const uint32_t w = ldw<A4>(b + 2 + 4 * q);
+    __device__ static void load(uint32_t grp, int q, int, Stage& g) {
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            const uint32_t a = grp + 18 * b;
+            g.d[b] = bc_bits(lds16(a));
+            g.w[b] = ldw<A4>(a + 2 + 4 * q);
+        }
+    }
+    __device__ static uint4 blk32(const Stage& g, int b) {
+        const uint32_t d = g.d[b], w = g.w[b];
         const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
         return make_uint4(mq(h2b01(lo), B1032, d), mq(h2b23(lo), B1032, d), mq(h2b01(hi), B1032, d),
                           mq(h2b23(hi), B1032, d));
     }
-    template <bool A4>
-    __device__ static void step(uint32_t grp, const Hdr&, int s, int q, int, uint4& c0, uint4& c1) {
-        c0 = blk32<A4>(grp + 18 * (2 * s), q);
-        c1 = blk32<A4>(grp + 18 * (2 * s + 1), q);
+    __device__ static void emit(const Stage& g, int s, uint4& c0, uint4& c1) {
+        c0 = blk32(g, 2 * s);
+        c1 = blk32(g, 2 * s + 1);
     }
 };
 
@@ -689,16 +754,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 const uintptr_t goff = static_cast<uintptr_t>(g) * F.gbytes;
                 const uint32_t ws = smem_u32(w_st + js * WSTAGE);
-                // a row's stage data starts (its global address mod 16) into its smem row
-                uint32_t blk[PASSES];
-                typename D::Hdr hd[PASSES];
+                // The whole stage goes to registers, then the slot is handed back
+                // to the W producer before any of its steps is dequantized.  A
+                // row's stage data starts (its global address mod 16) into its
+                // smem row.
+                typename D::Stage stg[PASSES];
 #pragma unroll
                 for (int pp = 0; pp < PASSES; ++pp) {
-                    blk[pp] = ws + (r0 + 8 * NDQ * pp) * p.wp + static_cast<uint32_t>((rowg[pp] + goff) & 15u);
-                    D::template hdr<A4>(blk[pp], q, hd[pp]);
+                    const uint32_t blk =
+                        ws + (r0 + 8 * NDQ * pp) * p.wp + static_cast<uint32_t>((rowg[pp] + goff) & 15u);
+                    D::template load<A4>(blk, q, rr, stg[pp]);
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&wempty[js]);
+                if (++js == SW) { js = 0; jph ^= 1u; }
                 const int nsteps = min(KG / BK, p.ksteps - g * (KG / BK));
-                for (int st = 0; st < nsteps; ++st, ++it) {
+#pragma unroll
+                for (int st = 0; st < KG / BK; ++st) {
+                    if (st >= nsteps) break;
                     const bool got = it < S_ || mbar_wait_bounded(&empty[s], ph ^ 1u, DEV_TIMEOUT_EMPTY);
                     if (!__all_sync(FULL, got)) {  // the warp leaves together
                         *abort_flag = 1;
@@ -711,7 +784,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int pp = 0; pp < PASSES; ++pp) {
                         uint4 c0, c1;
-                        D::template step<A4>(blk[pp], hd[pp], st, q, rr, c0, c1);
+                        D::emit(stg[pp], st, c0, c1);
                         const uint4 zero = make_uint4(0, 0, 0, 0);
                         if (ragged && !valid[pp]) { c0 = zero; c1 = zero; }
                         if (z1) c1 = zero;
@@ -723,11 +796,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                     fence_async_shared();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&full_a[s]);
+                    ++it;
                     if (++s == S_) { s = 0; ph ^= 1u; }
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&wempty[js]);
-                if (++js == SW) { js = 0; jph ^= 1u; }
             }
             if (!ok) break;
         }
