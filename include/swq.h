@@ -85,6 +85,29 @@ swq_status swq_gemv(int ggml_type, const void* W, const float* x, float* y,
 swq_status swq_gemm(int ggml_type, const void* W, const float* X, float* Y,
                     int M, int N, int K, swq_stream_t stream);
 
+/* ---- MoE grouped expert GEMM ---------------------------------------------
+ *
+ * For each expert e: Y[r] = X[r] . W_e^T for the rows r = expert_offsets[e] ..
+ * expert_offsets[e+1]-1, i.e. the expert FFN projections of a mixture-of-experts
+ * layer after the tokens (or token x top-k slots) have been grouped by expert.
+ * The reference has no MoE path (its FFN is dense, src/model.h:520-528; the
+ * GGUF expert tensor names only appear at src/hf_loader.h:474-493), so this
+ * replaces the per-expert loop of Compute::matmul_transposed_q calls
+ * (src/tensor.h:1212) a MoE forward would make.
+ *   W_experts       device array of n_experts device pointers, each to an
+ *                   N x K GGUF matrix of `ggml_type` (any alignment)
+ *   expert_offsets  device int array of n_experts + 1 row offsets into X/Y;
+ *                   entries are clamped to [0, total_rows] and a decreasing
+ *                   step is read as an empty expert
+ *   X_sorted, Y     device fp32, total_rows x K and total_rows x N, row-major
+ * Rows outside every expert's range are left untouched.  Runs the tensor-core
+ * GEMM (fp16 operands, fp32 accumulation; same tolerance as swq_gemm) with a
+ * temporary fp16 copy of X from libswq's stream-ordered pool.  n_experts <=
+ * 4095. */
+swq_status swq_grouped_gemm(int ggml_type, const void* const* W_experts, const int* expert_offsets,
+                            const float* X_sorted, float* Y, int n_experts, int total_rows,
+                            int N, int K, swq_stream_t stream);
+
 /* ---- Allocation-free GEMM ------------------------------------------------
  *
  * No counterpart in the reference.  swq_gemm's tensor-core path takes a

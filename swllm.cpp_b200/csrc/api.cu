@@ -257,6 +257,30 @@ swq_status swq_gemm_noalloc(int type, const void* W, const float* X, float* Y, i
     return gemm_gemv_groups(type, W, X, Y, M, N, K, max_m, dev, s);
 }
 
+swq_status swq_grouped_gemm(int type, const void* const* W_experts, const int* expert_offsets, const float* X_sorted,
+                            float* Y, int n_experts, int total_rows, int N, int K, swq_stream_t stream) {
+    TypeInfo ti;
+    if (!type_info(type, &ti)) return fail(SWQ_ERR_BAD_TYPE, "type " + std::to_string(type) + " is not on this path");
+    if (n_experts < 0 || total_rows < 0 || N < 0 || K < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative size");
+    if (K % ti.qk != 0)
+        return fail(SWQ_ERR_BAD_SHAPE, "K=" + std::to_string(K) + " is not a multiple of " + std::to_string(ti.qk));
+    if (n_experts > 4095) return fail(SWQ_ERR_BAD_SHAPE, "n_experts above 4095");
+    if (n_experts == 0 || total_rows == 0 || N == 0) return SWQ_OK;
+    if (!W_experts || !expert_offsets || !X_sorted || !Y) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (K == 0) {
+        cudaError_t e = cudaMemsetAsync(Y, 0, sizeof(float) * static_cast<size_t>(total_rows) * N, s);
+        return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
+    }
+    cudaError_t e = swq::gemm_tc_grouped_launch(type, W_experts, expert_offsets, X_sorted, Y, n_experts, total_rows,
+                                                N, K, dev.num_sms, s);
+    if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
+    return SWQ_OK;
+}
+
 swq_status swq_gemv(int type, const void* W, const float* x, float* y, int N, int K, swq_stream_t stream) {
     return swq_gemm(type, W, x, y, 1, N, K, stream);
 }

@@ -172,18 +172,13 @@ __device__ __forceinline__ uint32_t lds32(uint32_t a) {
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
     return v;
 }
-__device__ __forceinline__ uint32_t lds16(uint32_t a) {
-    uint16_t v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
-    return v;
-}
 __device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
     asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
 }
 
-// Little-endian word at byte address a: A4 -> a is 4-byte aligned; otherwise a
-// is 2-byte aligned and the word is funnel-shifted out of two aligned words.
+// Little-endian word at byte address a: A4 -> a is 4-byte aligned; otherwise
+// the word is funnel-shifted out of the two aligned words around it.
 template <bool A4>
 __device__ __forceinline__ uint32_t ldw(uint32_t a) {
     if constexpr (A4) {
@@ -341,7 +336,7 @@ struct Dq<Q6_K> {  // ql[128] @0, qh[64] @128, scales[16] (int8) @192, d @208 (s
     template <bool A4>
     __device__ static void load(uint32_t blk, int q, int rr, Stage& g) {
         const uint32_t sw = ldw<A4>(blk + 192 + 4 * q);
-        const float d = h2f(lds16(blk + 208));
+        const float d = h2f(ldw<A4>(blk + 208) & 0xFFFFu);
         const float s0 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 0)));
         const float s1 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 1)));
         const float s2 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 2)));
@@ -416,7 +411,7 @@ struct Dq<Q3_K> {  // hmask[32] @0, qs[64] @32, scales[12] @96, d @108 (src/tens
     template <bool A4>
     __device__ static void load(uint32_t blk, int q, int rr, Stage& g) {
         const uint32_t t0 = ldw<A4>(blk + 96), t1 = ldw<A4>(blk + 100), t2 = ldw<A4>(blk + 104);
-        const float d = h2f(lds16(blk + 108));
+        const float d = h2f(ldw<A4>(blk + 108) & 0xFFFFu);
         const uint32_t sw = q3k_scale_word(q, t0, t1, t2);
         const float s0 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 0)));
         const float s1 = static_cast<float>(static_cast<int8_t>(byte_of(sw, 1)));
@@ -455,7 +450,7 @@ struct Dq<Q8_0> {  // d @0, qs[32] (int8) @2 (src/tensor.h:157-166); a W stage i
 #pragma unroll
         for (int b = 0; b < 8; ++b) {
             const uint32_t a = grp + 34 * b;
-            g.d[b] = bc_bits(lds16(a));
+            g.d[b] = bc_bits(ldw<A4>(a));
             g.wa[b] = ldw<A4>(a + 2 + 4 * q);
             g.wb[b] = ldw<A4>(a + 18 + 4 * q);
         }
@@ -482,7 +477,7 @@ struct Dq<Q4_0> {  // d @0, qs[16] @2: element l low nibble of byte l, l + 16 hi
 #pragma unroll
         for (int b = 0; b < 8; ++b) {
             const uint32_t a = grp + 18 * b;
-            g.d[b] = bc_bits(lds16(a));
+            g.d[b] = bc_bits(ldw<A4>(a));
             g.w[b] = ldw<A4>(a + 2 + 4 * q);
         }
     }
@@ -512,9 +507,52 @@ struct Params {
     int rows_mode;    // 0: one tensor-map copy per W stage; 1: one bulk copy per row
     const uint8_t* w_lo;  // W rounded down to 16 bytes
     const uint8_t* w_hi;  // end of W rounded up to 16 bytes
+    // grouped (MoE) mode: expert e multiplies rows offsets[e] .. offsets[e+1]-1
+    // of X by its own weights wptrs[e]; offsets are clamped to [0, rows_total]
+    // and made non-decreasing on the device.
+    const uint8_t* const* wptrs;
+    const int* offsets;
+    int n_experts;
+    int rows_total;
 };
 
-template <int T, int BN, bool A4>
+// One output tile: weights, token rows m0 .. m_end-1 (the tile covers m0 .. m0+BN-1),
+// W-row tile nt.
+struct TileRef {
+    const uint8_t* W;
+    int m0, m_end, nt;
+};
+
+__device__ __forceinline__ int clamp_off(const Params& p, int e) { return min(max(p.offsets[e], 0), p.rows_total); }
+
+// Tile index -> TileRef.  Dense: token tile = tile / n_ntiles.  Grouped: tiles are
+// numbered expert by expert (tpre[e] = first tile of expert e), ntiles per
+// token tile of the expert.
+template <bool G, int BN>
+__device__ __forceinline__ TileRef tile_ref(const Params& p, const int* tpre, int tile) {
+    TileRef r;
+    if constexpr (!G) {
+        r.nt = tile % p.n_ntiles;
+        r.m0 = (tile / p.n_ntiles) * BN;
+        r.m_end = p.M;
+        r.W = p.W;
+    } else {
+        int lo = 0, hi = p.n_experts;  // last e with tpre[e] <= tile (empty experts share values)
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (tpre[mid] <= tile) lo = mid; else hi = mid;
+        }
+        const int local = tile - tpre[lo];
+        const int a = clamp_off(p, lo), b = max(a, clamp_off(p, lo + 1));
+        r.nt = local % p.n_ntiles;
+        r.m0 = a + (local / p.n_ntiles) * BN;
+        r.m_end = b;
+        r.W = p.wptrs[lo];
+    }
+    return r;
+}
+
+template <int T, int BN, bool A4, bool G>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const Params p, const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap) {
     using D = Dq<T>;
@@ -543,9 +581,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* drain = tempty + 2;            // final MMA commit before TMEM is freed
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 1) + 1;
+    int* tpre = reinterpret_cast<int*>(drain + 2);  // grouped: n_experts + 1 tile offsets
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntiles = p.n_mtiles * p.n_ntiles;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S_; ++s) {
@@ -565,6 +603,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         *abort_flag = 0;
         mbar_fence_init();
     }
+    if (G && warp == 0) {
+        // tiles of expert e = ceil(rows_e / BN) * n_ntiles; tpre = exclusive prefix
+        int carry = 0;
+        for (int base = 0; base < p.n_experts; base += 32) {
+            const int e = base + lane;
+            int v = 0;
+            if (e < p.n_experts) {
+                const int a = clamp_off(p, e), b = max(a, clamp_off(p, e + 1));
+                v = ((b - a + BN - 1) / BN) * p.n_ntiles;
+            }
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int u = __shfl_up_sync(FULL, v, d);
+                if (lane >= d) v += u;
+            }
+            if (e < p.n_experts) tpre[e + 1] = carry + v;
+            carry += __shfl_sync(FULL, v, 31);
+        }
+        if (lane == 0) tpre[0] = 0;
+    }
     if (warp == WARP_MMA) {
         // 2 x BN fp32 columns of TMEM (double-buffered accumulator)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -575,6 +633,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    const int ntiles = G ? tpre[p.n_experts] : p.n_mtiles * p.n_ntiles;
     pdl_wait_primary();  // X (fp16) is written by the conversion kernel before this one
 
     if (warp == WARP_X) {
@@ -585,7 +644,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         int it = 0;  // loads issued
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
             if (__shfl_sync(FULL, *abort_flag, 0)) break;
-            const int mt = tile / p.n_ntiles;  // token tile
+            const TileRef tr = tile_ref<G, BN>(p, tpre, tile);
             bool ok = true;
             for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
                 const bool got = it < S_ || mbar_wait_bounded(&empty[s], ph ^ 1u, DEV_TIMEOUT_EMPTY);
@@ -596,7 +655,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 if (elect_one()) {
                     mbar_arrive_expect_tx(&full_b[s], B_STAGE);
-                    tma_load_2d(smem_u32(b_st + s * B_STAGE), &xmap, ks * BK, mt * BN, &full_b[s]);
+                    tma_load_2d(smem_u32(b_st + s * B_STAGE), &xmap, ks * BK, tr.m0, &full_b[s]);
                 }
                 __syncwarp();
                 if (++s == S_) { s = 0; ph ^= 1u; }
@@ -668,7 +727,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         int jt = 0;  // W stages issued
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
             if (__shfl_sync(FULL, *abort_flag, 0)) break;
-            const int row0 = (tile % p.n_ntiles) * BM;
+            const TileRef tr = tile_ref<G, BN>(p, tpre, tile);
+            const int row0 = tr.nt * BM;
+            const uint8_t* w_hi = G ? reinterpret_cast<const uint8_t*>(
+                                          (reinterpret_cast<uintptr_t>(tr.W) + static_cast<size_t>(p.N) * p.row_bytes +
+                                           15) & ~uintptr_t(15))
+                                    : p.w_hi;
             bool ok = true;
             for (int g = 0; g < p.ngroups; ++g, ++jt) {
                 const bool got = jt < SW || mbar_wait_bounded(&wempty[js], jph ^ 1u, DEV_TIMEOUT_EMPTY);
@@ -679,7 +743,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 const uint32_t dst = smem_u32(w_st + js * WSTAGE);
                 const size_t goff = static_cast<size_t>(g) * F.gbytes;
-                if (!p.rows_mode) {
+                if (!G && !p.rows_mode) {
                     if (lane == 0) {
                         mbar_arrive_expect_tx(&wfull[js], static_cast<uint32_t>(WSTAGE));
                         tma_load_2d(dst, &wmap, static_cast<int>((goff & ~size_t(15)) >> 1), row0, &wfull[js]);
@@ -695,12 +759,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int k = 0; k < 4; ++k) {
                         const int row = row0 + lane + 32 * k;
                         len[k] = 0;
-                        src[k] = p.w_lo;
+                        src[k] = tr.W;
                         if (row < p.N) {
-                            const uint8_t* a = p.W + static_cast<size_t>(row) * p.row_bytes + goff;
+                            const uint8_t* a = tr.W + static_cast<size_t>(row) * p.row_bytes + goff;
                             const uint8_t* a16 = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(a) &
                                                                                   ~uintptr_t(15));
-                            const size_t room = static_cast<size_t>(p.w_hi - a16);
+                            const size_t room = static_cast<size_t>(w_hi - a16);
                             src[k] = a16;
                             len[k] = static_cast<uint32_t>(room < static_cast<size_t>(p.wp) ? room : p.wp);
                             bytes += len[k];
@@ -726,7 +790,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ------------------------------------------------------- W dequantizers
         const int rr = lane & 7, q = lane >> 3;
         const int r0 = 8 * dq_index(warp) + rr;  // the lane's tile rows r0 + 8 NDQ p
-        const uintptr_t wbase = reinterpret_cast<uintptr_t>(p.W);
         int s = 0;
         uint32_t ph = 0;
         int it = 0;
@@ -734,7 +797,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t jph = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
             if (__shfl_sync(FULL, *abort_flag, 0)) break;
-            const int row0 = (tile % p.n_ntiles) * BM;
+            const TileRef tr = tile_ref<G, BN>(p, tpre, tile);
+            const uintptr_t wbase = reinterpret_cast<uintptr_t>(tr.W);
+            const int row0 = tr.nt * BM;
             const bool ragged = row0 + BM > p.N;  // last row tile of a ragged N
             bool valid[PASSES];
             uintptr_t rowg[PASSES];
@@ -809,7 +874,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         int t_local = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t_local) {
             if (__shfl_sync(FULL, *abort_flag, 0)) break;
-            const int mt = tile / p.n_ntiles, nt = tile % p.n_ntiles;
+            const TileRef tr = tile_ref<G, BN>(p, tpre, tile);
+            const int nt = tr.nt;
             const int tb = t_local & 1;
             const uint32_t tph = (t_local >> 1) & 1;
             const bool got = mbar_wait_bounded(&tfull[tb], tph, DEV_TIMEOUT_MMA);
@@ -828,8 +894,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (row < p.N) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const int tok = mt * BN + c0 + j;
-                        if (tok < p.M) p.Y[static_cast<size_t>(tok) * p.N + row] = __uint_as_float(v[j]);
+                        const int tok = tr.m0 + c0 + j;
+                        if (tok < tr.m_end) p.Y[static_cast<size_t>(tok) * p.N + row] = __uint_as_float(v[j]);
                     }
                 }
             }
@@ -914,15 +980,25 @@ bool gemm_tc_supported(int type, const void* W, int M, int N, int K, int refcpu)
 }
 
 // Shared memory of one launch: A/B ring of `stages`, W ring of `wstages`.
-static size_t tc_smem_bytes(int bn, int stages, int wstages, int wp) {
+// Shared memory of one launch: A/B ring of `stages`, W ring of `wstages`,
+// barriers, and `extra` bytes after them (the grouped tile table).
+static size_t tc_smem_bytes(int bn, int stages, int wstages, int wp, size_t extra) {
     const size_t bars = static_cast<size_t>(3 * stages + 2 * wstages + 5) * 8 + 8;
     return 1024 + static_cast<size_t>(stages) * (tc::A_STAGE + bn * tc::BK * 2) +
-           static_cast<size_t>(wstages) * tc::BM * wp + 16 + bars;
+           static_cast<size_t>(wstages) * tc::BM * wp + 16 + bars + extra;
 }
 
-template <int T, int BN, bool A4>
+// Experts of a grouped launch (device arrays).
+struct ExpertSet {
+    const uint8_t* const* wptrs;
+    const int* offsets;
+    int n_experts;
+};
+
+// M is the number of X rows (grouped: all experts' rows together).
+template <int T, int BN, bool A4, bool G>
 static cudaError_t launch_tc(const void* W, const __half* Xh, float* Y, int M, int N, int K, int num_sms,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, const ExpertSet* ex) {
     constexpr tc::TcFmt F = tc::tc_fmt(T);
     tc::Params p{};
     p.W = static_cast<const uint8_t*>(W);
@@ -940,13 +1016,27 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, float* Y, int M, i
     const size_t wbytes = static_cast<size_t>(N) * p.row_bytes;
     p.w_lo = reinterpret_cast<const uint8_t*>(w & ~uintptr_t(15));
     p.w_hi = reinterpret_cast<const uint8_t*>((w + wbytes + 15) & ~uintptr_t(15));
+    size_t extra = 0;
+    int max_tiles = p.n_mtiles * p.n_ntiles;
+    if constexpr (G) {
+        p.wptrs = ex->wptrs;
+        p.offsets = ex->offsets;
+        p.n_experts = ex->n_experts;
+        p.rows_total = M;
+        extra = static_cast<size_t>(ex->n_experts + 1) * sizeof(int);
+        // each expert adds at most one partial token tile
+        max_tiles = static_cast<int>(std::min<int64_t>(
+            INT32_MAX, static_cast<int64_t>(p.n_ntiles) * ((M + BN - 1) / BN + ex->n_experts)));
+    }
 
     // One 2-D tensor-map copy per W stage needs 16-byte aligned rows; otherwise
-    // one bulk copy per row from the 16-byte boundary at or below the row's data.
-    bool tmap = (w % 16 == 0) && (p.row_bytes % 16 == 0);
+    // (and always for grouped launches, whose expert weights are separate
+    // allocations) one bulk copy per row from the 16-byte boundary at or below
+    // the row's data.
+    bool tmap = !G && (w % 16 == 0) && (p.row_bytes % 16 == 0);
     for (int attempt = 0; attempt < 2; ++attempt) {
-        const bool offs = !tmap || (F.gbytes % 16 != 0);  // data may start up to 14 bytes into a smem row
-        int wp = (F.gbytes + (offs ? 14 : 0) + 15) / 16 * 16;
+        const bool offs = !tmap || (F.gbytes % 16 != 0);  // data may start up to 15 bytes into a smem row
+        int wp = (F.gbytes + (offs ? 15 : 0) + 15) / 16 * 16;
         if ((wp / 16) % 2 == 0) wp += 16;  // odd multiple of 16: conflict-free across 8 rows
         p.wp = wp;
         p.rows_mode = tmap ? 0 : 1;
@@ -956,7 +1046,7 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, float* Y, int M, i
         p.stages = 0;
         for (int sw : {3, 2}) {
             for (int st = 8; st >= 2; --st) {
-                if (tc_smem_bytes(BN, st, sw, wp) <= 227 * 1024) {
+                if (tc_smem_bytes(BN, st, sw, wp, extra) <= 227 * 1024) {
                     p.stages = st;
                     p.wstages = sw;
                     break;
@@ -993,7 +1083,7 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, float* Y, int M, i
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
 
-        auto kern = tc::gemm_kernel<T, BN, A4>;
+        auto kern = tc::gemm_kernel<T, BN, A4, G>;
         static thread_local int set_dev = -1;
         int dev = -1;
         cudaError_t e = cudaGetDevice(&dev);
@@ -1003,11 +1093,10 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, float* Y, int M, i
             if (e != cudaSuccess) return e;
             set_dev = dev;
         }
-        const int ntiles = p.n_mtiles * p.n_ntiles;
         cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3(std::min(ntiles, num_sms));
+        cfg.gridDim = dim3(std::max(1, std::min(max_tiles, num_sms)));
         cfg.blockDim = dim3(tc::THREADS);
-        cfg.dynamicSmemBytes = tc_smem_bytes(BN, p.stages, p.wstages, p.wp);
+        cfg.dynamicSmemBytes = tc_smem_bytes(BN, p.stages, p.wstages, p.wp, extra);
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1022,9 +1111,19 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, float* Y, int M, i
 template <int T, bool A4>
 static cudaError_t launch_tc_bn(const void* W, const __half* Xh, float* Y, int M, int N, int K, int num_sms,
                                 cudaStream_t s) {
-    if (M <= 64) return launch_tc<T, 64, A4>(W, Xh, Y, M, N, K, num_sms, s);
-    if (M <= 128) return launch_tc<T, 128, A4>(W, Xh, Y, M, N, K, num_sms, s);
-    return launch_tc<T, 256, A4>(W, Xh, Y, M, N, K, num_sms, s);
+    if (M <= 64) return launch_tc<T, 64, A4, false>(W, Xh, Y, M, N, K, num_sms, s, nullptr);
+    if (M <= 128) return launch_tc<T, 128, A4, false>(W, Xh, Y, M, N, K, num_sms, s, nullptr);
+    return launch_tc<T, 256, A4, false>(W, Xh, Y, M, N, K, num_sms, s, nullptr);
+}
+
+// Grouped: the token tile follows the mean rows per expert.
+template <int T>
+static cudaError_t launch_tc_grouped(const ExpertSet& ex, const __half* Xh, float* Y, int rows, int N, int K,
+                                     int num_sms, cudaStream_t s) {
+    const int mean = (rows + ex.n_experts - 1) / ex.n_experts;
+    if (mean <= 64) return launch_tc<T, 64, false, true>(nullptr, Xh, Y, rows, N, K, num_sms, s, &ex);
+    if (mean <= 128) return launch_tc<T, 128, false, true>(nullptr, Xh, Y, rows, N, K, num_sms, s, &ex);
+    return launch_tc<T, 256, false, true>(nullptr, Xh, Y, rows, N, K, num_sms, s, &ex);
 }
 
 template <int T>
@@ -1105,6 +1204,35 @@ cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, in
     e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), static_cast<size_t>(n) * 2, pool, s);
     if (e != cudaSuccess) return e;
     e = gemm_tc_run(type, W, X, Xh, Y, M, N, K, num_sms, s);
+    cudaError_t e2 = cudaFreeAsync(Xh, s);
+    return e != cudaSuccess ? e : e2;
+}
+
+cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
+                                   int n_experts, int rows, int N, int K, int num_sms, cudaStream_t s) {
+    if (tc::tc_fmt(type).qk == 0 || K % 32 != 0 || encode_fn2() == nullptr) return cudaErrorNotSupported;
+    const int64_t n = static_cast<int64_t>(rows) * K;
+    cudaMemPool_t pool = nullptr;
+    cudaError_t e = scratch_pool(&pool);
+    if (e != cudaSuccess) return e;
+    __half* Xh = nullptr;
+    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), static_cast<size_t>(n) * 2, pool, s);
+    if (e != cudaSuccess) return e;
+    e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rows, K, num_sms, s)
+                            : launch_x_to_f16<false>(X, Xh, rows, K, num_sms, s);
+    if (e == cudaSuccess) {
+        const ExpertSet ex{reinterpret_cast<const uint8_t* const*>(wptrs), offsets, n_experts};
+        switch (type) {
+            case Q4_0: e = launch_tc_grouped<Q4_0>(ex, Xh, Y, rows, N, K, num_sms, s); break;
+            case Q8_0: e = launch_tc_grouped<Q8_0>(ex, Xh, Y, rows, N, K, num_sms, s); break;
+            case Q2_K: e = launch_tc_grouped<Q2_K>(ex, Xh, Y, rows, N, K, num_sms, s); break;
+            case Q3_K: e = launch_tc_grouped<Q3_K>(ex, Xh, Y, rows, N, K, num_sms, s); break;
+            case Q4_K: e = launch_tc_grouped<Q4_K>(ex, Xh, Y, rows, N, K, num_sms, s); break;
+            case Q5_K: e = launch_tc_grouped<Q5_K>(ex, Xh, Y, rows, N, K, num_sms, s); break;
+            case Q6_K: e = launch_tc_grouped<Q6_K>(ex, Xh, Y, rows, N, K, num_sms, s); break;
+            default: e = cudaErrorInvalidValue;
+        }
+    }
     cudaError_t e2 = cudaFreeAsync(Xh, s);
     return e != cudaSuccess ? e : e2;
 }

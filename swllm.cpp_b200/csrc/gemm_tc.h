@@ -14,6 +14,11 @@ cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, in
 // stream-ordered allocation (swq_gemm_noalloc); M * K must fit that array.
 cudaError_t gemm_tc_launch_noalloc(int type, const void* W, const float* X, float* Y, int M, int N, int K,
                                    int refcpu, int num_sms, cudaStream_t s);
+// MoE grouped GEMM: expert e multiplies rows offsets[e] .. offsets[e+1]-1 of X
+// (rows x K) by the GGUF matrix wptrs[e] (N x K) into the same rows of Y.
+// wptrs and offsets are device arrays of n_experts and n_experts + 1 entries.
+cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
+                                   int n_experts, int rows, int N, int K, int num_sms, cudaStream_t s);
 cudaError_t status_fetch_gemm_tc(unsigned* out, cudaStream_t s);
 
 }  // namespace swq

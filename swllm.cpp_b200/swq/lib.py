@@ -75,6 +75,7 @@ def lib() -> ctypes.CDLL:
         "swq_gemv": (i32, [i32, vp, vp, vp, i32, i32, vp]),
         "swq_gemm": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
         "swq_gemm_noalloc": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
+        "swq_grouped_gemm": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "swq_set_option": (i32, [i32, i32]),
         "swq_get_option": (i32, [i32]),
         "swq_check": (i32, [vp]),
@@ -164,6 +165,15 @@ def gemv(type_id: int, W, x, y, N: int, K: int, stream=None) -> None:
 def gemm(type_id: int, W, X, Y, M: int, N: int, K: int, stream=None) -> None:
     """Y[M x N] = X[M x K] . W[N x K]^T on device buffers (async)."""
     _raise(lib().swq_gemm(type_id, _ptr(W), _ptr(X), _ptr(Y), M, N, K, _stream(stream)))
+
+
+def grouped_gemm(type_id: int, w_ptrs, offsets, X, Y, n_experts: int, total_rows: int, N: int, K: int,
+                 stream=None) -> None:
+    """MoE grouped GEMM: rows offsets[e] .. offsets[e+1]-1 of X times W_e^T into
+    the same rows of Y.  w_ptrs: device int64 tensor of the experts' weight
+    addresses; offsets: device int32 tensor of n_experts + 1 row offsets."""
+    _raise(lib().swq_grouped_gemm(type_id, _ptr(w_ptrs), _ptr(offsets), _ptr(X), _ptr(Y), n_experts, total_rows,
+                                  N, K, _stream(stream)))
 
 
 def gemm_noalloc(type_id: int, W, X, Y, M: int, N: int, K: int, stream=None) -> None:

@@ -96,3 +96,14 @@ def test_ctx_null_handle_errors():
     assert L.swq_ctx_resident_bytes(None) == 0
     out = ctypes.c_void_p()
     assert isinstance(out, ctypes.c_void_p)
+
+
+def test_grouped_gemm_argument_checks():
+    """swq_grouped_gemm rejects bad arguments before any device work."""
+    L = swq.lib()
+    assert _rc(L.swq_grouped_gemm, 99, 16, 16, 16, 16, 4, 8, 64, 256, None) is Status.BAD_TYPE
+    assert _rc(L.swq_grouped_gemm, kat.Q4_K, 16, 16, 16, 16, 4, 8, 64, 100, None) is Status.BAD_SHAPE
+    assert _rc(L.swq_grouped_gemm, kat.Q4_K, 16, 16, 16, 16, 5000, 8, 64, 256, None) is Status.BAD_SHAPE
+    assert _rc(L.swq_grouped_gemm, kat.Q4_K, None, 16, 16, 16, 4, 8, 64, 256, None) is Status.NULL_PTR
+    # nothing to do: no rows
+    assert _rc(L.swq_grouped_gemm, kat.Q4_K, None, None, None, None, 4, 0, 64, 256, None) is Status.OK
