@@ -29,7 +29,7 @@ from typing import Callable, Sequence
 
 import numpy as np
 
-from . import lib as _lib
+from .lib import gemm as _swq_gemm, grouped_gemm as _swq_grouped_gemm
 from .synth import block_geometry
 
 
@@ -62,7 +62,7 @@ def _world(group) -> tuple[int, int]:
 
 
 def _default_gemm(type_id, W, X, Y, M, N, K):
-    _lib.gemm(type_id, W, X, Y, M, N, K)
+    _swq_gemm(type_id, W, X, Y, M, N, K)
 
 
 # ---------------------------------------------------------------- dense TP
@@ -144,7 +144,7 @@ class _GroupedCUDA:
         return torch.tensor([w.data_ptr() for w in weights], dtype=torch.int64, device=self.device)
 
     def __call__(self, type_id, weights, table, offsets, X, Y, N, K):
-        _lib.grouped_gemm(type_id, table, offsets, X, Y, len(weights), X.shape[0], N, K)
+        _swq_grouped_gemm(type_id, table, offsets, X, Y, len(weights), X.shape[0], N, K)
 
 
 class ExpertParallelMoE:
