@@ -85,6 +85,45 @@ swq_status swq_gemv(int ggml_type, const void* W, const float* x, float* y,
 swq_status swq_gemm(int ggml_type, const void* W, const float* X, float* Y,
                     int M, int N, int K, swq_stream_t stream);
 
+/* ---- Decode step around the GEMVs ------------------------------------------
+ *
+ * Device-resident forms of the Compute helpers Model::forward calls between
+ * its projections (src/model.h:257-543; helpers src/tensor.h:1028-1180,
+ * 1280-1340), fp32 as there.  `rows` sequences decode together at the same
+ * position, read from device memory (*pos) so a captured step replays for
+ * every token.  KV caches are per layer [rows][max_seq][kv_dim] fp32. */
+
+/* out[r] = x[r] / sqrt(mean(x[r]^2) + eps) * w  (Compute::rmsnorm, :1280) */
+swq_status swq_rmsnorm(float* out, const float* x, const float* w, int n, float eps, int rows,
+                       swq_stream_t stream);
+/* RoPE of q (in place) and k at position *pos, then k and v into the caches
+ * (Compute::rope, :1313, and the cache stores of src/model.h:326-327); freqs
+ * [rope_dim/2] = 1/theta^(2i/rope_dim); neox != 0 rotates (i, i + rope_dim/2)
+ * pairs, else (2i, 2i+1). */
+swq_status swq_rope_kv(float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                       const int* pos, const float* freqs, int q_dim, int kv_dim, int head_dim,
+                       int rope_dim, int neox, int rows, int max_seq, swq_stream_t stream);
+/* Grouped-query decode attention over positions 0 .. *pos (src/model.h:329-361),
+ * split over the context; `workspace` of swq_attention_workspace_bytes() bytes
+ * (caller-owned, so the call allocates nothing). */
+size_t swq_attention_workspace_bytes(int num_heads, int num_kv_heads, int head_dim, int rows, int max_seq);
+swq_status swq_attention_decode(float* out, const float* q, const float* k_cache, const float* v_cache,
+                                const int* pos, void* workspace, size_t workspace_bytes, int num_heads,
+                                int num_kv_heads, int head_dim, int rows, int max_seq, swq_stream_t stream);
+/* out[r][i] = silu(gate[r*ld + i]) * up[r*ld + i]  (Compute::silu_mul, :1300) */
+swq_status swq_silu_mul(float* out, const float* gate, const float* up, int n, int rows, int ld,
+                        swq_stream_t stream);
+/* x += y  (Compute::add, :1336) */
+swq_status swq_add(float* x, const float* y, int64_t n, swq_stream_t stream);
+/* x[r] = table[tokens[r]], fp32 rows of `dim` (src/model.h:265) */
+swq_status swq_embed(float* x, const float* table, const int* tokens, int dim, int rows, swq_stream_t stream);
+/* tokens[r] = argmax of logits[r] (first maximum); history[*step * rows + r] too
+ * when history is not NULL (greedy sampling). */
+swq_status swq_argmax(const float* logits, int n, int rows, int* tokens, int* history, const int* step,
+                      swq_stream_t stream);
+/* *pos += 1 and, when step is not NULL, *step += 1 */
+swq_status swq_decode_advance(int* pos, int* step, swq_stream_t stream);
+
 /* ---- MoE grouped expert GEMM ---------------------------------------------
  *
  * For each expert e: Y[r] = X[r] . W_e^T for the rows r = expert_offsets[e] ..
@@ -155,7 +194,12 @@ enum {
      * before an fp32-accumulated product.  0: groups of rows through the GEMV
      * kernel instead.  The GEMM needs the weight base aligned to 16 bytes for
      * Q4_K/Q5_K, 4 for Q2_K, 2 otherwise; other pointers use the GEMV path. */
-    SWQ_OPT_TENSOR_CORE_GEMM = 4
+    SWQ_OPT_TENSOR_CORE_GEMM = 4,
+    /* Smallest M that runs the tensor-core GEMM (default 32, at least
+     * SWQ_OPT_GEMV_MAX_M + 1); smaller M run the GEMV kernel over groups of
+     * rows, which reads the weights once per group but beats the
+     * dequantization-bound tensor-core path while the groups are few. */
+    SWQ_OPT_TENSOR_CORE_MIN_M = 5
 };
 swq_status swq_set_option(int option, int value);
 int swq_get_option(int option);

@@ -1,0 +1,104 @@
+"""CPU restatement of the reference's dense Llama decode forward
+(TEST INFRASTRUCTURE ONLY).
+
+``RefLlama.forward(token, pos)`` follows Model::forward (src/model.h:257-543)
+on the full-attention, dense-FFN path, in fp32 numpy:
+
+  x = token_embd[token]                                   (:265)
+  per layer: xb = rmsnorm(x, attn_norm)                   (:272, src/tensor.h:1028-1033)
+             q, k, v = W{q,k,v} . xb                       (:284-289)
+             rope(q, k) at pos, interleaved pairs          (:322-323, src/tensor.h:1068-1107)
+             cache k, v at pos                             (:326-327)
+             per head: scores = q.k_t / sqrt(head_dim), t <= pos; softmax; out = sum p v_t
+                                                           (:329-361, src/tensor.h:1036-1047)
+             x += Wo . out                                 (:363-366)
+             xb = rmsnorm(x, ffn_norm); h = silu(Wg . xb) * (Wu . xb); x += Wd . h
+                                                           (:521-541, src/tensor.h:1050-1064)
+  logits = Woutput . rmsnorm(x, output_norm)               (:545-551)
+
+The quantized matmuls are the reference's own routine compiled from source
+(oracle/_ref) when it was built, else this package's C restatement in the
+reference's accumulation order.  Only tests use this module.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import gemv as _port_gemv
+from . import ref_available, ref_gemv
+
+F32 = np.float32
+
+
+def matmul(type_id: int, blocks: np.ndarray, x: np.ndarray, N: int, K: int) -> np.ndarray:
+    if ref_available():
+        return ref_gemv(type_id, blocks, x, N, K)
+    return _port_gemv(type_id, blocks, x, N, K, format_order=False)
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    ss = F32(0.0)
+    for v in x.astype(F32):  # sequential fp32 sum, as the reference loop
+        ss = F32(ss + v * v)
+    scale = F32(1.0) / np.sqrt(F32(ss / F32(len(x)) + F32(eps)))
+    return (x * scale * w).astype(F32)
+
+
+def rope_interleaved(vec: np.ndarray, head_dim: int, pos: int, freqs: np.ndarray) -> np.ndarray:
+    out = vec.astype(F32).copy()
+    heads = len(vec) // head_dim
+    for h in range(heads):
+        for i in range(0, head_dim, 2):
+            angle = F32(pos) * freqs[i // 2]
+            c, s = np.cos(angle, dtype=F32), np.sin(angle, dtype=F32)
+            a, b = out[h * head_dim + i], out[h * head_dim + i + 1]
+            out[h * head_dim + i] = a * c - b * s
+            out[h * head_dim + i + 1] = a * s + b * c
+    return out
+
+
+def softmax(x: np.ndarray) -> np.ndarray:
+    m = x.max()
+    e = np.exp((x - m).astype(F32)).astype(F32)
+    return (e / e.sum(dtype=F32)).astype(F32)
+
+
+class RefLlama:
+    """cfg: swq.model.LlamaConfig-like (n_layers, dim, n_heads, n_kv_heads,
+    head_dim, ffn, vocab, eps, types); weights: the host arrays LlamaDecoder takes."""
+
+    def __init__(self, cfg, weights: dict, freqs: np.ndarray, max_seq: int):
+        self.cfg, self.W, self.freqs = cfg, weights, freqs.astype(F32)
+        self.kc = np.zeros((cfg.n_layers, max_seq, cfg.n_kv_heads * cfg.head_dim), F32)
+        self.vc = np.zeros_like(self.kc)
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        c, W, t = self.cfg, self.W, self.cfg.types
+        hd, nh, nkv = c.head_dim, c.n_heads, c.n_kv_heads
+        q_dim, kv_dim = nh * hd, nkv * hd
+        x = np.asarray(W["token_embd"][token], F32).copy()
+        for li, L in enumerate(W["layers"]):
+            xb = rmsnorm(x, L["attn_norm"], c.eps)
+            q = matmul(t["wq"], L["wq"], xb, q_dim, c.dim)
+            k = matmul(t["wk"], L["wk"], xb, kv_dim, c.dim)
+            v = matmul(t["wv"], L["wv"], xb, kv_dim, c.dim)
+            q = rope_interleaved(q, hd, pos, self.freqs)
+            k = rope_interleaved(k, hd, pos, self.freqs)
+            self.kc[li, pos], self.vc[li, pos] = k, v
+            att = np.zeros(q_dim, F32)
+            mul = nh // nkv
+            for h in range(nh):
+                kvh = h // mul
+                qh = q[h * hd:(h + 1) * hd]
+                ks = self.kc[li, :pos + 1, kvh * hd:(kvh + 1) * hd]
+                vs = self.vc[li, :pos + 1, kvh * hd:(kvh + 1) * hd]
+                p = softmax((ks @ qh).astype(F32) / np.sqrt(F32(hd)))
+                att[h * hd:(h + 1) * hd] = (p @ vs).astype(F32)
+            x = (x + matmul(t["wo"], L["wo"], att, c.dim, q_dim)).astype(F32)
+            xb = rmsnorm(x, L["ffn_norm"], c.eps)
+            g = matmul(t["w_gate"], L["w_gate"], xb, c.ffn, c.dim)
+            u = matmul(t["w_up"], L["w_up"], xb, c.ffn, c.dim)
+            hmid = (g / (F32(1.0) + np.exp(-g)) * u).astype(F32)
+            x = (x + matmul(t["w_down"], L["w_down"], hmid, c.dim, c.ffn)).astype(F32)
+        x = rmsnorm(x, W["output_norm"], c.eps)
+        return matmul(t["output"], W["output"], x, c.vocab, c.dim)

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "../../include/swq.h"
+#include "decode.h"
 #include "gemm_tc.h"
 #include "gemv.h"
 
@@ -27,6 +28,7 @@ std::atomic<int> g_opt_q2k_refcpu{0};
 std::atomic<int> g_opt_early_prefetch{1};
 std::atomic<int> g_opt_gemv_max_m{8};
 std::atomic<int> g_opt_gemm_tc{1};
+std::atomic<int> g_opt_tc_min_m{32};
 
 swq_status fail(swq_status s, const std::string& msg) {
     g_last_error = msg;
@@ -180,6 +182,10 @@ swq_status swq_set_option(int option, int value) {
             if (value != 0 && value != 1) return fail(SWQ_ERR_BAD_ARG, "option value must be 0 or 1");
             g_opt_gemm_tc = value;
             return SWQ_OK;
+        case SWQ_OPT_TENSOR_CORE_MIN_M:
+            if (value < 2) return fail(SWQ_ERR_BAD_ARG, "tensor-core minimum M must be >= 2");
+            g_opt_tc_min_m = value;
+            return SWQ_OK;
         default:
             return fail(SWQ_ERR_BAD_ARG, "unknown option " + std::to_string(option));
     }
@@ -191,6 +197,7 @@ int swq_get_option(int option) {
         case SWQ_OPT_EARLY_WEIGHT_PREFETCH: return g_opt_early_prefetch;
         case SWQ_OPT_GEMV_MAX_M: return g_opt_gemv_max_m;
         case SWQ_OPT_TENSOR_CORE_GEMM: return g_opt_gemm_tc;
+        case SWQ_OPT_TENSOR_CORE_MIN_M: return g_opt_tc_min_m;
         default: return -1;
     }
 }
@@ -224,7 +231,8 @@ swq_status swq_gemm(int type, const void* W, const float* X, float* Y, int M, in
         return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
     }
     const int max_m = g_opt_gemv_max_m;
-    if (M > max_m && g_opt_gemm_tc && swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
+    if (M > max_m && M >= g_opt_tc_min_m && g_opt_gemm_tc &&
+        swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
         cudaError_t e = swq::gemm_tc_launch(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms, s);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
         return SWQ_OK;
@@ -249,7 +257,8 @@ swq_status swq_gemm_noalloc(int type, const void* W, const float* X, float* Y, i
         return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
     }
     const int max_m = g_opt_gemv_max_m;
-    if (M > max_m && g_opt_gemm_tc && swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
+    if (M > max_m && M >= g_opt_tc_min_m && g_opt_gemm_tc &&
+        swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
         cudaError_t e = swq::gemm_tc_launch_noalloc(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms, s);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch (fixed scratch)");
         return SWQ_OK;
@@ -279,6 +288,126 @@ swq_status swq_grouped_gemm(int type, const void* const* W_experts, const int* e
                                                 N, K, dev.num_sms, s);
     if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
     return SWQ_OK;
+}
+
+// ---- decode step -------------------------------------------------------------
+
+static swq_status launch_status(cudaError_t e, const char* what) {
+    return e == cudaSuccess ? SWQ_OK : cuda_fail(e, what);
+}
+
+swq_status swq_rmsnorm(float* out, const float* x, const float* w, int n, float eps, int rows, swq_stream_t stream) {
+    if (n < 0 || rows < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative size");
+    if (n == 0 || rows == 0) return SWQ_OK;
+    if (!out || !x || !w) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::rmsnorm_launch(out, x, w, n, eps, rows, reinterpret_cast<cudaStream_t>(stream)),
+                         "rmsnorm launch");
+}
+
+swq_status swq_rope_kv(float* q, const float* k, const float* v, float* k_cache, float* v_cache, const int* pos,
+                       const float* freqs, int q_dim, int kv_dim, int head_dim, int rope_dim, int neox, int rows,
+                       int max_seq, swq_stream_t stream) {
+    if (head_dim <= 0 || rope_dim <= 0 || rope_dim > head_dim || rope_dim % 2 || q_dim % head_dim ||
+        kv_dim % head_dim || rows < 0 || max_seq <= 0)
+        return fail(SWQ_ERR_BAD_SHAPE, "inconsistent RoPE dimensions");
+    if (rows == 0) return SWQ_OK;
+    if (!q || !k || !v || !k_cache || !v_cache || !pos || !freqs) return fail(SWQ_ERR_NULL_PTR, "null pointer");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::rope_kv_launch(q, k, v, k_cache, v_cache, pos, freqs, q_dim, kv_dim, head_dim, rope_dim,
+                                             neox, rows, max_seq, dev.num_sms, reinterpret_cast<cudaStream_t>(stream)),
+                         "rope launch");
+}
+
+static int attention_splits_for(int rows, int num_kv_heads, int max_seq) {
+    swq::DeviceInfo dev;
+    if (current_device(&dev) != SWQ_OK) return 1;
+    return swq::attention_splits(rows, num_kv_heads, max_seq, dev.num_sms);
+}
+
+size_t swq_attention_workspace_bytes(int num_heads, int num_kv_heads, int head_dim, int rows, int max_seq) {
+    if (num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || rows <= 0 || max_seq <= 0) return 0;
+    const size_t slots = static_cast<size_t>(rows) * num_heads * attention_splits_for(rows, num_kv_heads, max_seq);
+    return slots * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
+}
+
+swq_status swq_attention_decode(float* out, const float* q, const float* k_cache, const float* v_cache, const int* pos,
+                                void* workspace, size_t workspace_bytes, int num_heads, int num_kv_heads, int head_dim,
+                                int rows, int max_seq, swq_stream_t stream) {
+    if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads || head_dim % 32 || head_dim > 256 ||
+        rows < 0 || max_seq <= 0 || (num_heads / num_kv_heads) > 8 || ((num_heads / num_kv_heads) & (num_heads / num_kv_heads - 1)))
+        return fail(SWQ_ERR_BAD_SHAPE, "attention: head_dim 64/128/256, 1/2/4/8 query heads per kv head");
+    if (rows == 0) return SWQ_OK;
+    if (!out || !q || !k_cache || !v_cache || !pos || !workspace) return fail(SWQ_ERR_NULL_PTR, "null pointer");
+    const size_t need = swq_attention_workspace_bytes(num_heads, num_kv_heads, head_dim, rows, max_seq);
+    if (workspace_bytes < need) return fail(SWQ_ERR_BAD_ARG, "attention workspace too small");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    const int splits = swq::attention_splits(rows, num_kv_heads, max_seq, dev.num_sms);
+    float* part_o = static_cast<float*>(workspace);
+    float* part_ml = part_o + static_cast<size_t>(rows) * num_heads * splits * head_dim;
+    return launch_status(swq::attention_launch(out, q, k_cache, v_cache, pos, part_o, part_ml, num_heads, num_kv_heads,
+                                               head_dim, rows, max_seq, splits, reinterpret_cast<cudaStream_t>(stream)),
+                         "attention launch");
+}
+
+swq_status swq_silu_mul(float* out, const float* gate, const float* up, int n, int rows, int ld, swq_stream_t stream) {
+    if (n < 0 || rows < 0 || ld < n) return fail(SWQ_ERR_BAD_SHAPE, "bad silu_mul sizes");
+    if (n == 0 || rows == 0) return SWQ_OK;
+    if (!out || !gate || !up) return fail(SWQ_ERR_NULL_PTR, "null pointer");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(
+        swq::silu_mul_launch(out, gate, up, n, rows, ld, dev.num_sms, reinterpret_cast<cudaStream_t>(stream)),
+        "silu_mul launch");
+}
+
+swq_status swq_add(float* x, const float* y, int64_t n, swq_stream_t stream) {
+    if (n < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative size");
+    if (n == 0) return SWQ_OK;
+    if (!x || !y) return fail(SWQ_ERR_NULL_PTR, "null pointer");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::add_launch(x, y, n, dev.num_sms, reinterpret_cast<cudaStream_t>(stream)), "add launch");
+}
+
+swq_status swq_embed(float* x, const float* table, const int* tokens, int dim, int rows, swq_stream_t stream) {
+    if (dim < 0 || rows < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative size");
+    if (dim == 0 || rows == 0) return SWQ_OK;
+    if (!x || !table || !tokens) return fail(SWQ_ERR_NULL_PTR, "null pointer");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::embed_launch(x, table, tokens, dim, rows, reinterpret_cast<cudaStream_t>(stream)),
+                         "embed launch");
+}
+
+swq_status swq_argmax(const float* logits, int n, int rows, int* tokens, int* history, const int* step,
+                      swq_stream_t stream) {
+    if (n <= 0 || rows < 0) return fail(SWQ_ERR_BAD_SHAPE, "bad argmax sizes");
+    if (rows == 0) return SWQ_OK;
+    if (!logits || !tokens || (history && !step)) return fail(SWQ_ERR_NULL_PTR, "null pointer");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(
+        swq::argmax_launch(logits, n, rows, tokens, history, step, reinterpret_cast<cudaStream_t>(stream)),
+        "argmax launch");
+}
+
+swq_status swq_decode_advance(int* pos, int* step, swq_stream_t stream) {
+    if (!pos) return fail(SWQ_ERR_NULL_PTR, "null pos");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::advance_launch(pos, step, reinterpret_cast<cudaStream_t>(stream)), "advance launch");
 }
 
 swq_status swq_gemv(int type, const void* W, const float* x, float* y, int N, int K, swq_stream_t stream) {

@@ -24,6 +24,7 @@ OPT_Q2K_REFERENCE_CPU_ORDER = 1
 OPT_EARLY_WEIGHT_PREFETCH = 2
 OPT_GEMV_MAX_M = 3
 OPT_TENSOR_CORE_GEMM = 4
+OPT_TENSOR_CORE_MIN_M = 5
 
 GEMM_NOALLOC_MAX_X_ELEMS = 8388608  # SWQ_GEMM_NOALLOC_MAX_X_ELEMS
 
@@ -76,6 +77,15 @@ def lib() -> ctypes.CDLL:
         "swq_gemm": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
         "swq_gemm_noalloc": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
         "swq_grouped_gemm": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
+        "swq_rmsnorm": (i32, [vp, vp, vp, i32, ctypes.c_float, i32, vp]),
+        "swq_rope_kv": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp]),
+        "swq_attention_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
+        "swq_attention_decode": (i32, [vp, vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, i32, vp]),
+        "swq_silu_mul": (i32, [vp, vp, vp, i32, i32, i32, vp]),
+        "swq_add": (i32, [vp, vp, i64, vp]),
+        "swq_embed": (i32, [vp, vp, vp, i32, i32, vp]),
+        "swq_argmax": (i32, [vp, i32, i32, vp, vp, vp, vp]),
+        "swq_decode_advance": (i32, [vp, vp, vp]),
         "swq_set_option": (i32, [i32, i32]),
         "swq_get_option": (i32, [i32]),
         "swq_check": (i32, [vp]),
@@ -181,6 +191,48 @@ def gemm_noalloc(type_id: int, W, X, Y, M: int, N: int, K: int, stream=None) -> 
     libswq's fixed per-device array (M * K <= GEMM_NOALLOC_MAX_X_ELEMS).
     Calls that overlap on the GPU share that array and race."""
     _raise(lib().swq_gemm_noalloc(type_id, _ptr(W), _ptr(X), _ptr(Y), M, N, K, _stream(stream)))
+
+
+# ---- decode step (device pointers or torch tensors; async on `stream`) ----
+def rmsnorm(out, x, w, n: int, eps: float, rows: int = 1, stream=None) -> None:
+    _raise(lib().swq_rmsnorm(_ptr(out), _ptr(x), _ptr(w), n, eps, rows, _stream(stream)))
+
+
+def rope_kv(q, k, v, k_cache, v_cache, pos, freqs, q_dim: int, kv_dim: int, head_dim: int, rope_dim: int,
+            neox: bool, rows: int, max_seq: int, stream=None) -> None:
+    _raise(lib().swq_rope_kv(_ptr(q), _ptr(k), _ptr(v), _ptr(k_cache), _ptr(v_cache), _ptr(pos), _ptr(freqs), q_dim,
+                             kv_dim, head_dim, rope_dim, 1 if neox else 0, rows, max_seq, _stream(stream)))
+
+
+def attention_workspace_bytes(num_heads: int, num_kv_heads: int, head_dim: int, rows: int, max_seq: int) -> int:
+    return int(lib().swq_attention_workspace_bytes(num_heads, num_kv_heads, head_dim, rows, max_seq))
+
+
+def attention_decode(out, q, k_cache, v_cache, pos, workspace, workspace_bytes: int, num_heads: int,
+                     num_kv_heads: int, head_dim: int, rows: int, max_seq: int, stream=None) -> None:
+    _raise(lib().swq_attention_decode(_ptr(out), _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(pos), _ptr(workspace),
+                                      workspace_bytes, num_heads, num_kv_heads, head_dim, rows, max_seq,
+                                      _stream(stream)))
+
+
+def silu_mul(out, gate, up, n: int, rows: int = 1, ld: int | None = None, stream=None) -> None:
+    _raise(lib().swq_silu_mul(_ptr(out), _ptr(gate), _ptr(up), n, rows, n if ld is None else ld, _stream(stream)))
+
+
+def add(x, y, n: int, stream=None) -> None:
+    _raise(lib().swq_add(_ptr(x), _ptr(y), n, _stream(stream)))
+
+
+def embed(x, table, tokens, dim: int, rows: int = 1, stream=None) -> None:
+    _raise(lib().swq_embed(_ptr(x), _ptr(table), _ptr(tokens), dim, rows, _stream(stream)))
+
+
+def argmax(logits, n: int, rows: int, tokens, history=None, step=None, stream=None) -> None:
+    _raise(lib().swq_argmax(_ptr(logits), n, rows, _ptr(tokens), _ptr(history), _ptr(step), _stream(stream)))
+
+
+def decode_advance(pos, step=None, stream=None) -> None:
+    _raise(lib().swq_decode_advance(_ptr(pos), _ptr(step), _stream(stream)))
 
 
 def check(stream=None) -> None:

@@ -30,9 +30,12 @@ def _gemm(torch, t, blocks, X, N, K):
 
 @pytest.fixture(autouse=True)
 def _tensor_core_on():
+    """Every M above the GEMV limit takes the tensor-core path in these tests."""
     swq.set_option(swq.OPT_TENSOR_CORE_GEMM, 1)
+    swq.set_option(swq.OPT_TENSOR_CORE_MIN_M, 9)
     yield
     swq.set_option(swq.OPT_TENSOR_CORE_GEMM, 1)
+    swq.set_option(swq.OPT_TENSOR_CORE_MIN_M, 32)
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
