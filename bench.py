@@ -275,6 +275,8 @@ def run_swq(args, rank: int, world: int) -> None:
     if not np.allclose(out, y_last, rtol=1e-5, atol=1e-4):
         raise RuntimeError("host-buffer path disagrees with the device path")
 
+    decode = run_decode(rank, world) if args.decode else None
+
     line = None
     if rank == 0:
         cpu = None
@@ -304,6 +306,7 @@ def run_swq(args, rank: int, world: int) -> None:
                     "steps": e2e_steps},
             "gpu_launches": launches,
             "clocks": clk.summary(),
+            "decode": decode,
         }
     del graph
     if dist:
@@ -311,6 +314,56 @@ def run_swq(args, rank: int, world: int) -> None:
         dist.destroy_process_group()
     if line is not None:
         print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- decode workload
+def run_decode(rank: int, world: int, batches=(1, 16), prefill: int = 512, steps: int = 256,
+               warmup: int = 5) -> dict:
+    """Greedy decode of a Llama-3-8B-shaped model (32 layers, hidden 4096,
+    32/8 heads of 128, FFN 14336, vocab 128256, Q4_K_M mix, synthetic weights
+    generated on the device) after a synthetic 512-token context: `steps`
+    graph-replayed steps per batch size, CUDA-event timed.  Every rank runs its
+    own model (replicas); tok/s is summed over ranks (max time over ranks)."""
+    import torch
+
+    from swq.model import LlamaConfig, LlamaDecoder
+
+    cfg = LlamaConfig(max_seq=prefill + steps + warmup + 8)
+    out = {"model": "Llama-3-8B shape, Q4_K_M mix (Q6_K attn_v/ffn_down/output, Q4_K else), synthetic weights",
+           "context": prefill, "steps": steps,
+           "weight_bytes_per_token": cfg.weight_bytes_per_token(), "batches": {}}
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    for B in batches:
+        dec = LlamaDecoder(cfg, rows=B, seed=100 + rank)
+        dec.reset(list(range(B)), 0)
+        dec.capture()
+        dec.reset([(7 * i + 1) % cfg.vocab for i in range(B)], 0)
+        dec.fill_kv(prefill)
+        dec.generate(warmup)
+        dec.stream.synchronize()
+        if dist:
+            dist.barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(dec.stream)
+        dec.generate(steps)
+        ev1.record(dec.stream)
+        ev1.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        if dist:
+            t = torch.tensor([ms], dtype=torch.float64, device=dec.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        ok = bool(torch.isfinite(dec.logits).all().item())
+        per_tok_ms = ms / steps
+        out["batches"][str(B)] = {
+            "tok_s": round(B * steps * world / (ms * 1e-3), 1), "ms_per_step": round(per_tok_ms, 4),
+            "weight_GBps": round(cfg.weight_bytes_per_token() / (per_tok_ms * 1e-3) / 1e9, 1),
+            "finite_logits": ok}
+        del dec
+        torch.cuda.empty_cache()
+    return out
 
 
 # ---------------------------------------------------------------- GEMM workload
@@ -438,11 +491,14 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["swq", "reference"], default="swq")
-    ap.add_argument("--workload", choices=["gemv", "gemm"], default="gemv",
-                    help="gemv: the headline Q4_K GEMV; gemm: the prefill dequant-GEMM")
+    ap.add_argument("--workload", choices=["gemv", "gemm", "decode"], default="gemv",
+                    help="gemv: the headline Q4_K GEMV (with decode tok/s); gemm: the prefill dequant-GEMM; "
+                         "decode: Llama-3-8B greedy decode tok/s alone")
     ap.add_argument("--format", choices=sorted(TYPE_IDS), default="Q4_K", help="GEMM weight format")
     ap.add_argument("--M", type=int, default=512, help="GEMM activation rows")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU sample length (0: skip)")
+    ap.add_argument("--no-decode", dest="decode", action="store_false",
+                    help="skip the Llama-3-8B decode tok/s measurement of the default run")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -452,6 +508,26 @@ def main() -> None:
     if args.warmup < 3:
         log("warm-up raised to 3 steps (minimum)")
         args.warmup = 3
+    if args.workload == "decode":
+        import torch
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                    device_id=torch.device("cuda", local))
+        d = run_decode(rank, world, steps=args.steps if args.steps != ap.get_default("steps") else 256)
+        if rank == 0:
+            b1 = d["batches"]["1"]
+            print(json.dumps({"metric": "decode tok/s (Llama-3-8B Q4_K_M, batch 1)", "value": b1["tok_s"],
+                              "unit": "tok/s", "n_gpus": world, "higher_is_better": True, "scaling": "weak",
+                              "data": "synthetic", "decode": d}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.workload == "gemm":
         if args.steps == ap.get_default("steps"):
             args.steps = 2000

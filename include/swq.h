@@ -96,29 +96,42 @@ swq_status swq_gemm(int ggml_type, const void* W, const float* X, float* Y,
 /* out[r] = x[r] / sqrt(mean(x[r]^2) + eps) * w  (Compute::rmsnorm, :1280) */
 swq_status swq_rmsnorm(float* out, const float* x, const float* w, int n, float eps, int rows,
                        swq_stream_t stream);
+/* x[r] += y[r], then out[r] = rmsnorm(x[r]): a residual add and the RMSNorm
+ * that follows it (src/model.h:363-366 then :519-520), in one pass. */
+swq_status swq_add_rmsnorm(float* out, float* x, const float* y, const float* w, int n, float eps, int rows,
+                           swq_stream_t stream);
 /* RoPE of q (in place) and k at position *pos, then k and v into the caches
  * (Compute::rope, :1313, and the cache stores of src/model.h:326-327); freqs
  * [rope_dim/2] = 1/theta^(2i/rope_dim); neox != 0 rotates (i, i + rope_dim/2)
- * pairs, else (2i, 2i+1). */
+ * pairs, else (2i, 2i+1).  Row r of q, k, v starts at r*ldq, r*ldk, r*ldv
+ * (0: q_dim, kv_dim, kv_dim), so q and k may be slices of one projection. */
 swq_status swq_rope_kv(float* q, const float* k, const float* v, float* k_cache, float* v_cache,
                        const int* pos, const float* freqs, int q_dim, int kv_dim, int head_dim,
-                       int rope_dim, int neox, int rows, int max_seq, swq_stream_t stream);
+                       int rope_dim, int neox, int rows, int max_seq, int ldq, int ldk, int ldv,
+                       swq_stream_t stream);
 /* Grouped-query decode attention over positions 0 .. *pos (src/model.h:329-361),
- * split over the context; `workspace` of swq_attention_workspace_bytes() bytes
- * (caller-owned, so the call allocates nothing). */
+ * split over the context; the last split of each (sequence, kv head) merges
+ * the others.  `workspace`: swq_attention_workspace_bytes() bytes, caller-owned
+ * (the call allocates nothing), zero-filled before its first use; every call
+ * leaves it zeroed again.  Row r of q starts at r*ldq (0: num_heads*head_dim).
+ * out is rows x num_heads*head_dim. */
 size_t swq_attention_workspace_bytes(int num_heads, int num_kv_heads, int head_dim, int rows, int max_seq);
 swq_status swq_attention_decode(float* out, const float* q, const float* k_cache, const float* v_cache,
                                 const int* pos, void* workspace, size_t workspace_bytes, int num_heads,
-                                int num_kv_heads, int head_dim, int rows, int max_seq, swq_stream_t stream);
+                                int num_kv_heads, int head_dim, int rows, int max_seq, int ldq,
+                                swq_stream_t stream);
 /* out[r][i] = silu(gate[r*ld + i]) * up[r*ld + i]  (Compute::silu_mul, :1300) */
 swq_status swq_silu_mul(float* out, const float* gate, const float* up, int n, int rows, int ld,
                         swq_stream_t stream);
 /* x += y  (Compute::add, :1336) */
 swq_status swq_add(float* x, const float* y, int64_t n, swq_stream_t stream);
-/* x[r] = table[tokens[r]], fp32 rows of `dim` (src/model.h:265) */
-swq_status swq_embed(float* x, const float* table, const int* tokens, int dim, int rows, swq_stream_t stream);
-/* tokens[r] = argmax of logits[r] (first maximum); history[*step * rows + r] too
- * when history is not NULL (greedy sampling). */
+/* x[r] = table[tokens[r]], fp32 rows of `dim` (src/model.h:265); a token id
+ * outside [0, vocab) reads row 0. */
+swq_status swq_embed(float* x, const float* table, const int* tokens, int dim, int vocab, int rows,
+                     swq_stream_t stream);
+/* tokens[r] = argmax of logits[r] (first maximum; 0 when no element exceeds
+ * -inf, e.g. all NaN); history[*step * rows + r] too when history is not NULL
+ * (greedy sampling). */
 swq_status swq_argmax(const float* logits, int n, int rows, int* tokens, int* history, const int* step,
                       swq_stream_t stream);
 /* *pos += 1 and, when step is not NULL, *step += 1 */
@@ -150,16 +163,18 @@ swq_status swq_grouped_gemm(int ggml_type, const void* const* W_experts, const i
 /* ---- Allocation-free GEMM ------------------------------------------------
  *
  * No counterpart in the reference.  swq_gemm's tensor-core path takes a
- * temporary fp16 copy of X (M * K * 2 bytes) from a stream-ordered memory
- * pool that libswq creates per device and keeps until exit.  Some callers cannot let a library allocate device memory: processes
+ * temporary fp16 copy of X (M * K * 2 bytes, plus M fp32 row scales) from a
+ * stream-ordered memory pool that libswq creates per device and keeps until
+ * exit.  Some callers cannot let a library allocate device memory: processes
  * whose own allocator already owns the GPU's memory (a serving engine that
  * reserves what HBM is left for its KV cache at start-up, a caching allocator
  * that hands out every device byte), where a hidden allocation can fail or
  * fragment memory the caller has promised elsewhere.  swq_gemm_noalloc
  * computes what swq_gemm computes and allocates nothing: the fp16 copy of X
  * lives in a fixed device array inside libswq of SWQ_GEMM_NOALLOC_MAX_X_ELEMS
- * halves (16 MiB), which every GPU that loads the library holds until the
- * process exits.  The caller passes W, X and Y as for swq_gemm.
+ * halves (16 MiB), its row scales in a second one of
+ * SWQ_GEMM_NOALLOC_MAX_X_ELEMS / 32 floats (1 MiB), which every GPU that
+ * loads the library holds until the process exits.  The caller passes W, X and Y as for swq_gemm.
  *   - M * K above SWQ_GEMM_NOALLOC_MAX_X_ELEMS: SWQ_ERR_BAD_SHAPE.
  *   - The first call on a device looks up the array's address on that device
  *     (cudaGetSymbolAddress with the device current); make that first call
@@ -187,18 +202,19 @@ enum {
      * kernel.  Activations are always read after that kernel completes.
      * 0: every read waits for the preceding kernel. */
     SWQ_OPT_EARLY_WEIGHT_PREFETCH = 2,
-    /* Largest M served by the fused GEMV kernel; larger M use the GEMM. */
+    /* Largest number of activation rows one GEMV kernel launch serves
+     * (default 8); GEMV work on more rows runs in groups of this size. */
     SWQ_OPT_GEMV_MAX_M = 3,
-    /* 1 (default): M above SWQ_OPT_GEMV_MAX_M runs the tensor-core (tcgen05)
-     * dequant-GEMM, which rounds dequantized weights and activations to fp16
-     * before an fp32-accumulated product.  0: groups of rows through the GEMV
-     * kernel instead.  The GEMM needs the weight base aligned to 16 bytes for
-     * Q4_K/Q5_K, 4 for Q2_K, 2 otherwise; other pointers use the GEMV path. */
+    /* 1 (default): M >= SWQ_OPT_TENSOR_CORE_MIN_M runs the tensor-core
+     * (tcgen05) dequant-GEMM, which rounds dequantized weights and
+     * activations to fp16 before an fp32-accumulated product.  0: the GEMV
+     * kernel over groups of rows instead.  The GEMM needs the weight base
+     * 2-byte aligned; other pointers use the GEMV path. */
     SWQ_OPT_TENSOR_CORE_GEMM = 4,
-    /* Smallest M that runs the tensor-core GEMM (default 32, at least
-     * SWQ_OPT_GEMV_MAX_M + 1); smaller M run the GEMV kernel over groups of
-     * rows, which reads the weights once per group but beats the
-     * dequantization-bound tensor-core path while the groups are few. */
+    /* Smallest M that runs the tensor-core GEMM (default 5, at least 2).  The
+     * GEMV kernel's cost grows with its rows (it is bound by the integer dot
+     * products from about 4 rows on), so from 5 rows on the tensor cores win
+     * on the Llama projection shapes. */
     SWQ_OPT_TENSOR_CORE_MIN_M = 5
 };
 swq_status swq_set_option(int option, int value);

@@ -28,7 +28,7 @@ std::atomic<int> g_opt_q2k_refcpu{0};
 std::atomic<int> g_opt_early_prefetch{1};
 std::atomic<int> g_opt_gemv_max_m{8};
 std::atomic<int> g_opt_gemm_tc{1};
-std::atomic<int> g_opt_tc_min_m{32};
+std::atomic<int> g_opt_tc_min_m{5};
 
 swq_status fail(swq_status s, const std::string& msg) {
     g_last_error = msg;
@@ -231,7 +231,7 @@ swq_status swq_gemm(int type, const void* W, const float* X, float* Y, int M, in
         return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
     }
     const int max_m = g_opt_gemv_max_m;
-    if (M > max_m && M >= g_opt_tc_min_m && g_opt_gemm_tc &&
+    if (M >= g_opt_tc_min_m && g_opt_gemm_tc &&
         swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
         cudaError_t e = swq::gemm_tc_launch(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms, s);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
@@ -257,7 +257,7 @@ swq_status swq_gemm_noalloc(int type, const void* W, const float* X, float* Y, i
         return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
     }
     const int max_m = g_opt_gemv_max_m;
-    if (M > max_m && M >= g_opt_tc_min_m && g_opt_gemm_tc &&
+    if (M >= g_opt_tc_min_m && g_opt_gemm_tc &&
         swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
         cudaError_t e = swq::gemm_tc_launch_noalloc(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms, s);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch (fixed scratch)");
@@ -303,13 +303,30 @@ swq_status swq_rmsnorm(float* out, const float* x, const float* w, int n, float 
     swq::DeviceInfo dev;
     swq_status st = current_device(&dev);
     if (st != SWQ_OK) return st;
-    return launch_status(swq::rmsnorm_launch(out, x, w, n, eps, rows, reinterpret_cast<cudaStream_t>(stream)),
+    return launch_status(swq::rmsnorm_launch(out, const_cast<float*>(x), nullptr, w, n, eps, rows,
+                                             reinterpret_cast<cudaStream_t>(stream)),
                          "rmsnorm launch");
+}
+
+swq_status swq_add_rmsnorm(float* out, float* x, const float* y, const float* w, int n, float eps, int rows,
+                           swq_stream_t stream) {
+    if (n < 0 || rows < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative size");
+    if (n == 0 || rows == 0) return SWQ_OK;
+    if (!out || !x || !y || !w) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::rmsnorm_launch(out, x, y, w, n, eps, rows, reinterpret_cast<cudaStream_t>(stream)),
+                         "add_rmsnorm launch");
 }
 
 swq_status swq_rope_kv(float* q, const float* k, const float* v, float* k_cache, float* v_cache, const int* pos,
                        const float* freqs, int q_dim, int kv_dim, int head_dim, int rope_dim, int neox, int rows,
-                       int max_seq, swq_stream_t stream) {
+                       int max_seq, int ldq, int ldk, int ldv, swq_stream_t stream) {
+    ldq = ldq ? ldq : q_dim;
+    ldk = ldk ? ldk : kv_dim;
+    ldv = ldv ? ldv : kv_dim;
+    if (ldq < q_dim || ldk < kv_dim || ldv < kv_dim) return fail(SWQ_ERR_BAD_SHAPE, "row stride below row size");
     if (head_dim <= 0 || rope_dim <= 0 || rope_dim > head_dim || rope_dim % 2 || q_dim % head_dim ||
         kv_dim % head_dim || rows < 0 || max_seq <= 0)
         return fail(SWQ_ERR_BAD_SHAPE, "inconsistent RoPE dimensions");
@@ -319,7 +336,8 @@ swq_status swq_rope_kv(float* q, const float* k, const float* v, float* k_cache,
     swq_status st = current_device(&dev);
     if (st != SWQ_OK) return st;
     return launch_status(swq::rope_kv_launch(q, k, v, k_cache, v_cache, pos, freqs, q_dim, kv_dim, head_dim, rope_dim,
-                                             neox, rows, max_seq, dev.num_sms, reinterpret_cast<cudaStream_t>(stream)),
+                                             neox, rows, max_seq, ldq, ldk, ldv, dev.num_sms,
+                                             reinterpret_cast<cudaStream_t>(stream)),
                          "rope launch");
 }
 
@@ -331,13 +349,13 @@ static int attention_splits_for(int rows, int num_kv_heads, int max_seq) {
 
 size_t swq_attention_workspace_bytes(int num_heads, int num_kv_heads, int head_dim, int rows, int max_seq) {
     if (num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || rows <= 0 || max_seq <= 0) return 0;
-    const size_t slots = static_cast<size_t>(rows) * num_heads * attention_splits_for(rows, num_kv_heads, max_seq);
-    return slots * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
+    return swq::attention_workspace(num_heads, num_kv_heads, head_dim, rows,
+                                    attention_splits_for(rows, num_kv_heads, max_seq));
 }
 
 swq_status swq_attention_decode(float* out, const float* q, const float* k_cache, const float* v_cache, const int* pos,
                                 void* workspace, size_t workspace_bytes, int num_heads, int num_kv_heads, int head_dim,
-                                int rows, int max_seq, swq_stream_t stream) {
+                                int rows, int max_seq, int ldq, swq_stream_t stream) {
     if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads || head_dim % 32 || head_dim > 256 ||
         rows < 0 || max_seq <= 0 || (num_heads / num_kv_heads) > 8 || ((num_heads / num_kv_heads) & (num_heads / num_kv_heads - 1)))
         return fail(SWQ_ERR_BAD_SHAPE, "attention: head_dim 64/128/256, 1/2/4/8 query heads per kv head");
@@ -348,11 +366,12 @@ swq_status swq_attention_decode(float* out, const float* q, const float* k_cache
     swq::DeviceInfo dev;
     swq_status st = current_device(&dev);
     if (st != SWQ_OK) return st;
+    ldq = ldq ? ldq : num_heads * head_dim;
+    if (ldq < num_heads * head_dim) return fail(SWQ_ERR_BAD_SHAPE, "row stride below row size");
     const int splits = swq::attention_splits(rows, num_kv_heads, max_seq, dev.num_sms);
-    float* part_o = static_cast<float*>(workspace);
-    float* part_ml = part_o + static_cast<size_t>(rows) * num_heads * splits * head_dim;
-    return launch_status(swq::attention_launch(out, q, k_cache, v_cache, pos, part_o, part_ml, num_heads, num_kv_heads,
-                                               head_dim, rows, max_seq, splits, reinterpret_cast<cudaStream_t>(stream)),
+    return launch_status(swq::attention_launch(out, q, k_cache, v_cache, pos, workspace, num_heads, num_kv_heads,
+                                               head_dim, rows, max_seq, splits, ldq,
+                                               reinterpret_cast<cudaStream_t>(stream)),
                          "attention launch");
 }
 
@@ -378,14 +397,15 @@ swq_status swq_add(float* x, const float* y, int64_t n, swq_stream_t stream) {
     return launch_status(swq::add_launch(x, y, n, dev.num_sms, reinterpret_cast<cudaStream_t>(stream)), "add launch");
 }
 
-swq_status swq_embed(float* x, const float* table, const int* tokens, int dim, int rows, swq_stream_t stream) {
-    if (dim < 0 || rows < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative size");
+swq_status swq_embed(float* x, const float* table, const int* tokens, int dim, int vocab, int rows,
+                     swq_stream_t stream) {
+    if (dim < 0 || rows < 0 || vocab <= 0) return fail(SWQ_ERR_BAD_SHAPE, "bad embedding sizes");
     if (dim == 0 || rows == 0) return SWQ_OK;
     if (!x || !table || !tokens) return fail(SWQ_ERR_NULL_PTR, "null pointer");
     swq::DeviceInfo dev;
     swq_status st = current_device(&dev);
     if (st != SWQ_OK) return st;
-    return launch_status(swq::embed_launch(x, table, tokens, dim, rows, reinterpret_cast<cudaStream_t>(stream)),
+    return launch_status(swq::embed_launch(x, table, tokens, dim, vocab, rows, reinterpret_cast<cudaStream_t>(stream)),
                          "embed launch");
 }
 

@@ -1,17 +1,19 @@
 // decode.cu -- the device-resident decode step around the quantized GEMVs:
-// embedding row, RMSNorm, RoPE + KV-cache append, decode attention, SiLU-mul,
-// residual add, argmax (the reference's Model::forward, src/model.h:257-543,
-// with its Compute helpers, src/tensor.h:1028-1180).
+// embedding row, RMSNorm (alone or fused with the residual add before it),
+// RoPE + KV-cache append, decode attention, SiLU-mul, residual add, argmax
+// (the reference's Model::forward, src/model.h:257-543, with its Compute
+// helpers, src/tensor.h:1028-1180).
 //
 // All activations are fp32, as in the reference.  B sequences decode in step
-// (same position), row b of every [B x n] buffer belongs to sequence b.  The
-// position lives in device memory (`pos`, advanced by swq_decode_advance) so a
+// (same position); row b of every [B x n] buffer belongs to sequence b.  The
+// position lives in device memory (`pos`, advanced by advance_kernel) so a
 // whole decode step can be captured once in a CUDA graph and replayed.
 //
 // KV cache layout (fp32): [layer][sequence b][position t][kv_dim].
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "decode.h"
@@ -26,43 +28,88 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// RMSNorm of each row: out = x * (1 / sqrt(mean(x^2) + eps)) * w
-// (src/tensor.h:1028-1033).  One CTA per row.
-__global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ out, const float* __restrict__ x,
-                                                      const float* __restrict__ w, int n, float eps) {
-    const float* xr = x + static_cast<size_t>(blockIdx.x) * n;
-    float* orow = out + static_cast<size_t>(blockIdx.x) * n;
-    __shared__ float part[8];
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+// Sum over the CTA (blockDim.x a multiple of 32, at most 1024); every thread
+// gets the result.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
     if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
-        v = warp_sum(v);
-        if (threadIdx.x == 0) part[0] = v;
+        float u = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        u = warp_sum(u);
+        if (threadIdx.x == 0) red[32] = u;
     }
     __syncthreads();
-    const float scale = 1.0f / sqrtf(part[0] / static_cast<float>(n) + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = xr[i] * scale * w[i];
+    return red[32];
+}
+
+// RMSNorm of each row, optionally after the residual add x += y:
+//   out = x / sqrt(mean(x^2) + eps) * w      (src/tensor.h:1028-1033)
+// One CTA per row; VEC: n % 4 == 0 and 16-byte aligned rows.  With y, x is
+// updated in place first (src/model.h:363-366 and 519-520 in one pass).
+template <bool VEC, bool ADD>
+__global__ void __launch_bounds__(1024) rmsnorm_kernel(float* __restrict__ out, float* __restrict__ x,
+                                                       const float* __restrict__ y, const float* __restrict__ w,
+                                                       int n, float eps) {
+    __shared__ float red[33];
+    float* xr = x + static_cast<size_t>(blockIdx.x) * n;
+    const float* yr = ADD ? y + static_cast<size_t>(blockIdx.x) * n : nullptr;
+    float* orow = out + static_cast<size_t>(blockIdx.x) * n;
+    float ss = 0.f;
+    if (VEC) {
+        float4* x4 = reinterpret_cast<float4*>(xr);
+        for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
+            float4 a = x4[i];
+            if (ADD) {
+                const float4 b = reinterpret_cast<const float4*>(yr)[i];
+                a.x += b.x;
+                a.y += b.y;
+                a.z += b.z;
+                a.w += b.w;
+                x4[i] = a;
+            }
+            ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, ss))));
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            float a = xr[i];
+            if (ADD) {
+                a += yr[i];
+                xr[i] = a;
+            }
+            ss = fmaf(a, a, ss);
+        }
+    }
+    ss = block_sum(ss, red);
+    const float scale = 1.0f / sqrtf(ss / static_cast<float>(n) + eps);
+    if (VEC) {
+        const float4* x4 = reinterpret_cast<const float4*>(xr);
+        const float4* w4 = reinterpret_cast<const float4*>(w);
+        float4* o4 = reinterpret_cast<float4*>(orow);
+        for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
+            const float4 a = x4[i], g = w4[i];
+            o4[i] = make_float4(a.x * scale * g.x, a.y * scale * g.y, a.z * scale * g.z, a.w * scale * g.w);
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = xr[i] * scale * w[i];
+    }
 }
 
 // RoPE on q (in place) and k, then k and v into the cache at `pos`.
 // Interleaved pairs (2i, 2i+1) (src/tensor.h:1068-1107) or, with neox, pairs
 // (i, i + rope_dim/2) (src/tensor.h:1121-1161); angle = pos * freqs[i].
-// One thread per rotated pair (q heads, then k heads), plus v copies.
+// Row b of q / k / v starts at b * ldq / ldk / ldv.
 __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                                float* __restrict__ kcache, float* __restrict__ vcache, const int* __restrict__ pos_p,
                                const float* __restrict__ freqs, int q_dim, int kv_dim, int head_dim, int rope_dim,
-                               int neox, int max_seq) {
+                               int neox, int max_seq, int ldq, int ldk, int ldv) {
     const int b = blockIdx.y;
     const int pos = *pos_p;
     const int half = rope_dim / 2;
     const int qpairs = (q_dim / head_dim) * half, kpairs = (kv_dim / head_dim) * half;
-    float* qb = q + static_cast<size_t>(b) * q_dim;
-    const float* kb = k + static_cast<size_t>(b) * kv_dim;
-    const float* vb = v + static_cast<size_t>(b) * kv_dim;
+    float* qb = q + static_cast<size_t>(b) * ldq;
+    const float* kb = k + static_cast<size_t>(b) * ldk;
+    const float* vb = v + static_cast<size_t>(b) * ldv;
     float* kc = kcache + (static_cast<size_t>(b) * max_seq + pos) * kv_dim;
     float* vc = vcache + (static_cast<size_t>(b) * max_seq + pos) * kv_dim;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < qpairs + kpairs + kv_dim; i += gridDim.x * blockDim.x) {
@@ -96,18 +143,22 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
 }
 
 // Decode attention, split over the context: CTA (split, kv head, sequence)
-// handles timesteps [split*chunk, ...) for the kv_mul query heads that share
-// the kv head (src/model.h:329-361: score = q.k / sqrt(head_dim), softmax over
-// t <= pos, out = sum softmax * v).  Writes per split the running max m, the
-// sum l of exp(score - m) and the unnormalised output; attn_combine merges them.
+// handles timesteps [split*chunk, ...) for the MUL query heads that share the
+// kv head (src/model.h:329-361: score = q.k / sqrt(head_dim), softmax over
+// t <= pos, out = sum softmax * v), keeping a running max m, the sum l of
+// exp(score - m) and the unnormalised output.  Each CTA writes its partial
+// (m, l, o) per head; the last CTA of a (sequence, kv head) to finish -- an
+// atomic count in the workspace, reset by that CTA -- merges the splits.
 constexpr int ATT_THREADS = 128;
+constexpr int ATT_MAXSPLIT = 64;  // the merge keeps MUL x splits weights in the partial buffer
 
 // MUL query heads per kv head, PER = head_dim / 32 elements per lane.
 template <int MUL, int PER>
-__global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
+__global__ void __launch_bounds__(ATT_THREADS) attn_kernel(
     const float* __restrict__ q, const float* __restrict__ kcache, const float* __restrict__ vcache,
-    const int* __restrict__ pos_p, float* __restrict__ part_o, float* __restrict__ part_ml, int num_heads,
-    int num_kv_heads, int max_seq, int chunk) {
+    const int* __restrict__ pos_p, float* __restrict__ part_o, float* __restrict__ part_ml,
+    unsigned* __restrict__ done, float* __restrict__ out, int num_heads, int num_kv_heads, int max_seq, int chunk,
+    int ldq) {
     constexpr int HD = 32 * PER;
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int nsplit = gridDim.x;
@@ -118,13 +169,14 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
     const float inv_sqrt = 1.0f / sqrtf(static_cast<float>(HD));
     __shared__ float s_m[ATT_THREADS / 32][MUL], s_l[ATT_THREADS / 32][MUL];
     __shared__ float s_o[ATT_THREADS / 32][MUL][HD];
+    __shared__ unsigned s_last;
 
     float qv[MUL][PER], acc[MUL][PER], m[MUL], l[MUL];
 #pragma unroll
     for (int j = 0; j < MUL; ++j) {
         m[j] = -INFINITY;
         l[j] = 0.f;
-        const float* qh = q + (static_cast<size_t>(b) * num_heads + kvh * MUL + j) * HD;
+        const float* qh = q + static_cast<size_t>(b) * ldq + (kvh * MUL + j) * HD;
 #pragma unroll
         for (int e = 0; e < PER; ++e) {
             acc[j][e] = 0.f;
@@ -156,7 +208,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
             m[j] = mn;
         }
     }
-    // merge the warps of the CTA
+    // merge the warps of the CTA into this split's partial
 #pragma unroll
     for (int j = 0; j < MUL; ++j) {
         if (lane == 0) {
@@ -184,27 +236,42 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
             part_ml[2 * slot + 1] = ll;
         }
     }
-}
-
-// out[b, h*head_dim + d] = sum_s o_s * exp(m_s - M) / sum_s l_s * exp(m_s - M)
-__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
-                                    float* __restrict__ out, int num_heads, int head_dim, int nsplit) {
-    const int h = blockIdx.x, b = blockIdx.y;
-    const size_t base = (static_cast<size_t>(b) * num_heads + h) * nsplit;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_ml[2 * (base + s)]);
-    float L = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-        const float ms = part_ml[2 * (base + s)];
-        if (ms != -INFINITY) L += part_ml[2 * (base + s) + 1] * expf(ms - M);
+    // the last split of this (sequence, kv head) merges all splits
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned* cnt = done + static_cast<size_t>(b) * num_kv_heads + kvh;
+        s_last = atomicAdd(cnt, 1u) == static_cast<unsigned>(nsplit - 1);
+        if (s_last) *cnt = 0u;  // ready for the next call
     }
-    for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
-        float o = 0.f;
-        for (int s = 0; s < nsplit; ++s) {
-            const float ms = part_ml[2 * (base + s)];
-            if (ms != -INFINITY) o += part_o[(base + s) * head_dim + d] * expf(ms - M);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // weight of split s for head j: exp(m_s - M) / sum_s' l_s' exp(m_s' - M)
+    float* s_w = &s_o[0][0][0];  // MUL x nsplit (nsplit <= ATT_MAXSPLIT)
+    for (int j = warp; j < MUL; j += ATT_THREADS / 32) {
+        const size_t base = (static_cast<size_t>(b) * num_heads + kvh * MUL + j) * nsplit;
+        float M = -INFINITY;
+        for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(&part_ml[2 * (base + s)]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.f;
+        for (int s = lane; s < nsplit; s += 32) {
+            const float ms = __ldcg(&part_ml[2 * (base + s)]);
+            const float c = ms == -INFINITY ? 0.f : expf(ms - M);
+            s_w[j * nsplit + s] = c;
+            L += __ldcg(&part_ml[2 * (base + s) + 1]) * c;
         }
-        out[(static_cast<size_t>(b) * num_heads + h) * head_dim + d] = o / L;
+        L = warp_sum(L);
+        for (int s = lane; s < nsplit; s += 32) s_w[j * nsplit + s] /= L;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < MUL * HD; idx += ATT_THREADS) {
+        const int j = idx / HD, d = idx % HD;
+        const size_t base = (static_cast<size_t>(b) * num_heads + kvh * MUL + j) * nsplit;
+        float o = 0.f;
+        for (int s = 0; s < nsplit; ++s) o = fmaf(__ldcg(&part_o[(base + s) * HD + d]), s_w[j * nsplit + s], o);
+        out[(static_cast<size_t>(b) * num_heads + kvh * MUL + j) * HD + d] = o;
     }
 }
 
@@ -228,47 +295,63 @@ __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, i
         x[i] += y[i];
 }
 
-// x[b] = table[token[b]] (fp32 rows, src/model.h:265).
+// x[b] = table[token[b]] (fp32 rows, src/model.h:265); a token id outside
+// [0, vocab) reads row 0.
 __global__ void embed_kernel(float* __restrict__ x, const float* __restrict__ table, const int* __restrict__ tokens,
-                             int dim) {
+                             int dim, int vocab) {
     const int b = blockIdx.y;
-    const float* row = table + static_cast<size_t>(tokens[b]) * dim;
+    const int tok = tokens[b];
+    const float* row = table + static_cast<size_t>(tok >= 0 && tok < vocab ? tok : 0) * dim;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
         x[static_cast<size_t>(b) * dim + i] = row[i];
 }
 
+__device__ __forceinline__ void better(float v, int i, float& best, int& bi) {
+    if (v > best || (v == best && i < bi)) {
+        best = v;
+        bi = i;
+    }
+}
+
 // Greedy next token: the first index of the row maximum.  One CTA per row;
 // writes tokens[b] and, when history is given, history[step * B + b].
+template <bool VEC>
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int n, int* __restrict__ tokens,
                                                       int* __restrict__ history, const int* __restrict__ step_p) {
     const int b = blockIdx.x;
     const float* row = logits + static_cast<size_t>(b) * n;
+    // index 0 until a larger value is seen: a row of NaN still yields a valid token
     float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = row[i];
-        if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+    int bi = 0;
+    if (VEC) {
+        const float4* r4 = reinterpret_cast<const float4*>(row);
+        for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
+            const float4 v = r4[i];
+            better(v.x, 4 * i, best, bi);
+            better(v.y, 4 * i + 1, best, bi);
+            better(v.z, 4 * i + 2, best, bi);
+            better(v.w, 4 * i + 3, best, bi);
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) better(row[i], i, best, bi);
     }
     __shared__ float sv[32];
     __shared__ int si[32];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    for (int o = 16; o > 0; o >>= 1)
+        better(__shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o), best, bi);
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = best;
+        si[threadIdx.x >> 5] = bi;
     }
-    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
     __syncthreads();
     if (threadIdx.x < 32) {
         const int nw = blockDim.x >> 5;
         best = threadIdx.x < nw ? sv[threadIdx.x] : -INFINITY;
-        bi = threadIdx.x < nw ? si[threadIdx.x] : 0x7fffffff;
+        bi = threadIdx.x < nw ? si[threadIdx.x] : 0;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-        }
+        for (int o = 16; o > 0; o >>= 1)
+            better(__shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o), best, bi);
         if (threadIdx.x == 0) {
             tokens[b] = bi;
             if (history) history[static_cast<size_t>(*step_p) * gridDim.x + b] = bi;
@@ -286,60 +369,87 @@ int grid_for(int64_t n, int num_sms) {
     return static_cast<int>(g < 4LL * num_sms ? (g > 0 ? g : 1) : 4LL * num_sms);
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 }  // namespace
 
-cudaError_t rmsnorm_launch(float* out, const float* x, const float* w, int n, float eps, int rows, cudaStream_t s) {
-    rmsnorm_kernel<<<rows, 256, 0, s>>>(out, x, w, n, eps);
+cudaError_t rmsnorm_launch(float* out, float* x, const float* y, const float* w, int n, float eps, int rows,
+                           cudaStream_t s) {
+    const bool vec = n % 4 == 0 && aligned16(out) && aligned16(x) && aligned16(w) && (!y || aligned16(y));
+    const int threads = std::min(1024, std::max(32, ((vec ? n / 4 : n) + 31) / 32 * 32));
+    if (y) {
+        if (vec) rmsnorm_kernel<true, true><<<rows, threads, 0, s>>>(out, x, y, w, n, eps);
+        else rmsnorm_kernel<false, true><<<rows, threads, 0, s>>>(out, x, y, w, n, eps);
+    } else {
+        if (vec) rmsnorm_kernel<true, false><<<rows, threads, 0, s>>>(out, x, nullptr, w, n, eps);
+        else rmsnorm_kernel<false, false><<<rows, threads, 0, s>>>(out, x, nullptr, w, n, eps);
+    }
     return cudaGetLastError();
 }
 
 cudaError_t rope_kv_launch(float* q, const float* k, const float* v, float* kcache, float* vcache, const int* pos,
                            const float* freqs, int q_dim, int kv_dim, int head_dim, int rope_dim, int neox, int rows,
-                           int max_seq, int num_sms, cudaStream_t s) {
+                           int max_seq, int ldq, int ldk, int ldv, int num_sms, cudaStream_t s) {
     const int items = (q_dim / head_dim + kv_dim / head_dim) * (rope_dim / 2) + kv_dim;
     const dim3 grid(static_cast<unsigned>(grid_for(items, num_sms)), static_cast<unsigned>(rows));
     rope_kv_kernel<<<grid, 256, 0, s>>>(q, k, v, kcache, vcache, pos, freqs, q_dim, kv_dim, head_dim, rope_dim, neox,
-                                        max_seq);
+                                        max_seq, ldq, ldk, ldv);
     return cudaGetLastError();
 }
 
 int attention_splits(int rows, int num_kv_heads, int max_seq, int num_sms) {
     int splits = (2 * num_sms + rows * num_kv_heads - 1) / (rows * num_kv_heads);
     splits = splits < 1 ? 1 : splits;
-    const int max_splits = (max_seq + 15) / 16;  // at least 16 positions per split
+    int max_splits = (max_seq + 31) / 32;  // at least 32 positions per split
+    max_splits = max_splits < ATT_MAXSPLIT ? max_splits : ATT_MAXSPLIT;
     return splits > max_splits ? max_splits : splits;
 }
 
+size_t attention_workspace(int num_heads, int num_kv_heads, int head_dim, int rows, int splits) {
+    const size_t slots = static_cast<size_t>(rows) * num_heads * splits;
+    return slots * (static_cast<size_t>(head_dim) + 2) * sizeof(float) +
+           static_cast<size_t>(rows) * num_kv_heads * sizeof(unsigned);
+}
+
 template <int MUL>
-static cudaError_t attn_split_per(int per, dim3 grid, cudaStream_t s, const float* q, const float* kc, const float* vc,
-                                  const int* pos, float* po, float* pml, int nh, int nkv, int max_seq, int chunk) {
+static cudaError_t attn_per(int per, dim3 grid, cudaStream_t s, const float* q, const float* kc, const float* vc,
+                            const int* pos, float* po, float* pml, unsigned* done, float* out, int nh, int nkv,
+                            int max_seq, int chunk, int ldq) {
     switch (per) {
-        case 2: attn_split_kernel<MUL, 2><<<grid, ATT_THREADS, 0, s>>>(q, kc, vc, pos, po, pml, nh, nkv, max_seq, chunk); break;
-        case 4: attn_split_kernel<MUL, 4><<<grid, ATT_THREADS, 0, s>>>(q, kc, vc, pos, po, pml, nh, nkv, max_seq, chunk); break;
-        case 8: attn_split_kernel<MUL, 8><<<grid, ATT_THREADS, 0, s>>>(q, kc, vc, pos, po, pml, nh, nkv, max_seq, chunk); break;
+        case 2:
+            attn_kernel<MUL, 2><<<grid, ATT_THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
+                                                             chunk, ldq);
+            break;
+        case 4:
+            attn_kernel<MUL, 4><<<grid, ATT_THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
+                                                             chunk, ldq);
+            break;
+        case 8:
+            attn_kernel<MUL, 8><<<grid, ATT_THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
+                                                             chunk, ldq);
+            break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
 
 cudaError_t attention_launch(float* out, const float* q, const float* kcache, const float* vcache, const int* pos,
-                             float* part_o, float* part_ml, int num_heads, int num_kv_heads, int head_dim, int rows,
-                             int max_seq, int splits, cudaStream_t s) {
+                             void* workspace, int num_heads, int num_kv_heads, int head_dim, int rows, int max_seq,
+                             int splits, int ldq, cudaStream_t s) {
     if (num_kv_heads <= 0 || num_heads % num_kv_heads != 0 || head_dim % 32 != 0) return cudaErrorInvalidValue;
     const int mul = num_heads / num_kv_heads, per = head_dim / 32;
     const int chunk = (max_seq + splits - 1) / splits;
     const dim3 grid(splits, num_kv_heads, rows);
-    cudaError_t e;
+    float* part_o = static_cast<float*>(workspace);
+    float* part_ml = part_o + static_cast<size_t>(rows) * num_heads * splits * head_dim;
+    unsigned* done = reinterpret_cast<unsigned*>(part_ml + static_cast<size_t>(rows) * num_heads * splits * 2);
     switch (mul) {
-        case 1: e = attn_split_per<1>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, num_heads, num_kv_heads, max_seq, chunk); break;
-        case 2: e = attn_split_per<2>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, num_heads, num_kv_heads, max_seq, chunk); break;
-        case 4: e = attn_split_per<4>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, num_heads, num_kv_heads, max_seq, chunk); break;
-        case 8: e = attn_split_per<8>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, num_heads, num_kv_heads, max_seq, chunk); break;
+        case 1: return attn_per<1>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, chunk, ldq);
+        case 2: return attn_per<2>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, chunk, ldq);
+        case 4: return attn_per<4>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, chunk, ldq);
+        case 8: return attn_per<8>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, chunk, ldq);
         default: return cudaErrorInvalidValue;
     }
-    if (e != cudaSuccess) return e;
-    attn_combine_kernel<<<dim3(num_heads, rows), 128, 0, s>>>(part_o, part_ml, out, num_heads, head_dim, splits);
-    return cudaGetLastError();
 }
 
 cudaError_t silu_mul_launch(float* out, const float* gate, const float* up, int n, int rows, int ld, int num_sms,
@@ -353,14 +463,18 @@ cudaError_t add_launch(float* x, const float* y, int64_t n, int num_sms, cudaStr
     return cudaGetLastError();
 }
 
-cudaError_t embed_launch(float* x, const float* table, const int* tokens, int dim, int rows, cudaStream_t s) {
-    embed_kernel<<<dim3((dim + 255) / 256, rows), 256, 0, s>>>(x, table, tokens, dim);
+cudaError_t embed_launch(float* x, const float* table, const int* tokens, int dim, int vocab, int rows,
+                         cudaStream_t s) {
+    embed_kernel<<<dim3((dim + 255) / 256, rows), 256, 0, s>>>(x, table, tokens, dim, vocab);
     return cudaGetLastError();
 }
 
 cudaError_t argmax_launch(const float* logits, int n, int rows, int* tokens, int* history, const int* step,
                           cudaStream_t s) {
-    argmax_kernel<<<rows, 1024, 0, s>>>(logits, n, tokens, history, step);
+    if (n % 4 == 0 && aligned16(logits))
+        argmax_kernel<true><<<rows, 1024, 0, s>>>(logits, n, tokens, history, step);
+    else
+        argmax_kernel<false><<<rows, 1024, 0, s>>>(logits, n, tokens, history, step);
     return cudaGetLastError();
 }
 

@@ -496,6 +496,7 @@ struct Dq<Q4_0> {  // d @0, qs[16] @2: element l low nibble of byte l, l + 16 hi
 struct Params {
     const uint8_t* W;
     float* Y;
+    const float* rowscale;  // per X row: 2^k undoing the conversion's scaling
     int M, N, K;
     int row_bytes;
     int n_mtiles, n_ntiles, ksteps;
@@ -895,7 +896,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int tok = tr.m0 + c0 + j;
-                        if (tok < tr.m_end) p.Y[static_cast<size_t>(tok) * p.N + row] = __uint_as_float(v[j]);
+                        if (tok < tr.m_end)
+                            p.Y[static_cast<size_t>(tok) * p.N + row] = __uint_as_float(v[j]) * __ldg(&p.rowscale[tok]);
                     }
                 }
             }
@@ -918,34 +920,59 @@ __global__ void __launch_bounds__(THREADS, 1)
 }  // namespace tc
 
 // fp32 -> fp16 activations in the K order of the tensor-core GEMM: within each
-// 256-element group, position p holds element tc_elem(F2, p).  One thread per
-// 8 positions = two runs of four consecutive elements (float4 when aligned).
+// 256-element group, position p holds element tc_elem(F2, p).  Each row is
+// first scaled by the power of two 2^-k that brings its largest finite
+// magnitude into [2^14, 2^15): no element overflows fp16 (65504) and small
+// rows keep fp16's full precision instead of falling into its subnormals;
+// rowscale[row] = 2^k undoes it exactly in the epilogue.  All-zero rows and
+// rows holding inf keep k = 0.  One CTA per row (grid-stride); 8 positions per thread-step, two
+// runs of four consecutive elements (float4 when aligned).
 template <bool F2, bool VEC>
 __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__ X, __half* __restrict__ Xh,
-                                                       int M, int K) {
-    const int cpr = K / 8;  // 8-position chunks per row
-    const int64_t total = static_cast<int64_t>(M) * cpr;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t tok = i / cpr;
-        const int p0 = static_cast<int>(i - tok * cpr) * 8;
-        const int g = p0 & ~255, pp = p0 & 255;
-        const float* xr = X + tok * K + g;
-        const int e0 = tc::tc_elem(F2, pp), e1 = tc::tc_elem(F2, pp + 4);
-        float4 a, b;
+                                                       float* __restrict__ rowscale, int M, int K) {
+    __shared__ float red[8];
+    for (int row = blockIdx.x; row < M; row += gridDim.x) {
+        const float* xr = X + static_cast<int64_t>(row) * K;
+        float mx = 0.f;
         if (VEC) {
-            a = *reinterpret_cast<const float4*>(xr + e0);
-            b = *reinterpret_cast<const float4*>(xr + e1);
+            for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+                const float4 v = reinterpret_cast<const float4*>(xr)[i];
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            }
         } else {
-            a = make_float4(xr[e0], xr[e0 + 1], xr[e0 + 2], xr[e0 + 3]);
-            b = make_float4(xr[e1], xr[e1 + 1], xr[e1 + 2], xr[e1 + 3]);
+            for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(xr[i]));
         }
-        uint4 o;
-        o.x = tc::pack_h2(a.x, a.y);
-        o.y = tc::pack_h2(a.z, a.w);
-        o.z = tc::pack_h2(b.x, b.y);
-        o.w = tc::pack_h2(b.z, b.w);
-        *reinterpret_cast<uint4*>(Xh + tok * K + p0) = o;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+        __syncthreads();
+        mx = red[0];
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
+        int k = 0;
+        if (mx > 0.f && mx <= 3.402823466e38f) k = max(((__float_as_int(mx) >> 23) & 0xFF) - 127 - 14, -100);
+        const float sc = __int_as_float((127 - k) << 23);  // 2^-k
+        if (threadIdx.x == 0) rowscale[row] = __int_as_float((127 + k) << 23);
+        for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
+            const int p0 = c * 8;
+            const int g = p0 & ~255, pp = p0 & 255;
+            const float* xg = xr + g;
+            const int e0 = tc::tc_elem(F2, pp), e1 = tc::tc_elem(F2, pp + 4);
+            float4 a, b;
+            if (VEC) {
+                a = *reinterpret_cast<const float4*>(xg + e0);
+                b = *reinterpret_cast<const float4*>(xg + e1);
+            } else {
+                a = make_float4(xg[e0], xg[e0 + 1], xg[e0 + 2], xg[e0 + 3]);
+                b = make_float4(xg[e1], xg[e1 + 1], xg[e1 + 2], xg[e1 + 3]);
+            }
+            uint4 o;
+            o.x = tc::pack_h2(a.x * sc, a.y * sc);
+            o.y = tc::pack_h2(a.z * sc, a.w * sc);
+            o.z = tc::pack_h2(b.x * sc, b.y * sc);
+            o.w = tc::pack_h2(b.z * sc, b.w * sc);
+            *reinterpret_cast<uint4*>(Xh + static_cast<int64_t>(row) * K + p0) = o;
+        }
+        __syncthreads();  // red is reused by the next row
     }
     pdl_launch_dependents();
 }
@@ -997,12 +1024,13 @@ struct ExpertSet {
 
 // M is the number of X rows (grouped: all experts' rows together).
 template <int T, int BN, bool A4, bool G>
-static cudaError_t launch_tc(const void* W, const __half* Xh, float* Y, int M, int N, int K, int num_sms,
-                             cudaStream_t stream, const ExpertSet* ex) {
+static cudaError_t launch_tc(const void* W, const __half* Xh, const float* rowscale, float* Y, int M, int N, int K,
+                             int num_sms, cudaStream_t stream, const ExpertSet* ex) {
     constexpr tc::TcFmt F = tc::tc_fmt(T);
     tc::Params p{};
     p.W = static_cast<const uint8_t*>(W);
     p.Y = Y;
+    p.rowscale = rowscale;
     p.M = M;
     p.N = N;
     p.K = K;
@@ -1109,59 +1137,63 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, float* Y, int M, i
 }
 
 template <int T, bool A4>
-static cudaError_t launch_tc_bn(const void* W, const __half* Xh, float* Y, int M, int N, int K, int num_sms,
-                                cudaStream_t s) {
-    if (M <= 64) return launch_tc<T, 64, A4, false>(W, Xh, Y, M, N, K, num_sms, s, nullptr);
-    if (M <= 128) return launch_tc<T, 128, A4, false>(W, Xh, Y, M, N, K, num_sms, s, nullptr);
-    return launch_tc<T, 256, A4, false>(W, Xh, Y, M, N, K, num_sms, s, nullptr);
+static cudaError_t launch_tc_bn(const void* W, const __half* Xh, const float* rs, float* Y, int M, int N, int K,
+                                int num_sms, cudaStream_t s) {
+    if (M <= 64) return launch_tc<T, 64, A4, false>(W, Xh, rs, Y, M, N, K, num_sms, s, nullptr);
+    if (M <= 128) return launch_tc<T, 128, A4, false>(W, Xh, rs, Y, M, N, K, num_sms, s, nullptr);
+    return launch_tc<T, 256, A4, false>(W, Xh, rs, Y, M, N, K, num_sms, s, nullptr);
 }
 
 // Grouped: the token tile follows the mean rows per expert.
 template <int T>
-static cudaError_t launch_tc_grouped(const ExpertSet& ex, const __half* Xh, float* Y, int rows, int N, int K,
-                                     int num_sms, cudaStream_t s) {
+static cudaError_t launch_tc_grouped(const ExpertSet& ex, const __half* Xh, const float* rs, float* Y, int rows,
+                                     int N, int K, int num_sms, cudaStream_t s) {
     const int mean = (rows + ex.n_experts - 1) / ex.n_experts;
-    if (mean <= 64) return launch_tc<T, 64, false, true>(nullptr, Xh, Y, rows, N, K, num_sms, s, &ex);
-    if (mean <= 128) return launch_tc<T, 128, false, true>(nullptr, Xh, Y, rows, N, K, num_sms, s, &ex);
-    return launch_tc<T, 256, false, true>(nullptr, Xh, Y, rows, N, K, num_sms, s, &ex);
+    if (mean <= 64) return launch_tc<T, 64, false, true>(nullptr, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
+    if (mean <= 128) return launch_tc<T, 128, false, true>(nullptr, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
+    return launch_tc<T, 256, false, true>(nullptr, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
 }
 
 template <int T>
-static cudaError_t launch_tc_fmt(const void* W, const __half* Xh, float* Y, int M, int N, int K, int num_sms,
-                                 cudaStream_t s) {
+static cudaError_t launch_tc_fmt(const void* W, const __half* Xh, const float* rs, float* Y, int M, int N, int K,
+                                 int num_sms, cudaStream_t s) {
     // Q4_K, Q5_K and Q2_K keep every field of a block 4-byte aligned when W is.
     if constexpr (T == Q4_K || T == Q5_K || T == Q2_K) {
-        if (reinterpret_cast<uintptr_t>(W) % 4 == 0) return launch_tc_bn<T, true>(W, Xh, Y, M, N, K, num_sms, s);
+        if (reinterpret_cast<uintptr_t>(W) % 4 == 0)
+            return launch_tc_bn<T, true>(W, Xh, rs, Y, M, N, K, num_sms, s);
     }
-    return launch_tc_bn<T, false>(W, Xh, Y, M, N, K, num_sms, s);
+    return launch_tc_bn<T, false>(W, Xh, rs, Y, M, N, K, num_sms, s);
 }
 
 template <bool F2>
-static cudaError_t launch_x_to_f16(const float* X, __half* Xh, int M, int K, int num_sms, cudaStream_t s) {
-    const int64_t total = static_cast<int64_t>(M) * (K / 8);
-    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256,
-                                                                            static_cast<int64_t>(num_sms) * 8)));
+static cudaError_t launch_x_to_f16(const float* X, __half* Xh, float* rowscale, int M, int K, int num_sms,
+                                   cudaStream_t s) {
+    const int grid = std::max(1, std::min(M, num_sms * 8));
     if ((reinterpret_cast<uintptr_t>(X) & 15u) == 0)
-        x_to_f16_kernel<F2, true><<<grid, 256, 0, s>>>(X, Xh, M, K);
+        x_to_f16_kernel<F2, true><<<grid, 256, 0, s>>>(X, Xh, rowscale, M, K);
     else
-        x_to_f16_kernel<F2, false><<<grid, 256, 0, s>>>(X, Xh, M, K);
+        x_to_f16_kernel<F2, false><<<grid, 256, 0, s>>>(X, Xh, rowscale, M, K);
     return cudaGetLastError();
 }
 
-// X -> fp16 into Xh (M*K halves, K order of the format), then the GEMM.
-static cudaError_t gemm_tc_run(int type, const void* W, const float* X, __half* Xh, float* Y, int M, int N, int K,
-                               int num_sms, cudaStream_t s) {
-    cudaError_t e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, M, K, num_sms, s)
-                                        : launch_x_to_f16<false>(X, Xh, M, K, num_sms, s);
+// Scratch of one call: the fp16 copy of X (M*K halves) and, after it, M row scales.
+static size_t scratch_bytes(int64_t M, int64_t K) { return static_cast<size_t>(M * K) * 2 + static_cast<size_t>(M) * 4; }
+
+// X -> fp16 into Xh (M*K halves, K order of the format) with row scales rs
+// (M floats), then the GEMM.
+static cudaError_t gemm_tc_run(int type, const void* W, const float* X, __half* Xh, float* rs, float* Y, int M,
+                               int N, int K, int num_sms, cudaStream_t s) {
+    cudaError_t e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, M, K, num_sms, s)
+                                        : launch_x_to_f16<false>(X, Xh, rs, M, K, num_sms, s);
     if (e != cudaSuccess) return e;
     switch (type) {
-        case Q4_0: return launch_tc_fmt<Q4_0>(W, Xh, Y, M, N, K, num_sms, s);
-        case Q8_0: return launch_tc_fmt<Q8_0>(W, Xh, Y, M, N, K, num_sms, s);
-        case Q2_K: return launch_tc_fmt<Q2_K>(W, Xh, Y, M, N, K, num_sms, s);
-        case Q3_K: return launch_tc_fmt<Q3_K>(W, Xh, Y, M, N, K, num_sms, s);
-        case Q4_K: return launch_tc_fmt<Q4_K>(W, Xh, Y, M, N, K, num_sms, s);
-        case Q5_K: return launch_tc_fmt<Q5_K>(W, Xh, Y, M, N, K, num_sms, s);
-        case Q6_K: return launch_tc_fmt<Q6_K>(W, Xh, Y, M, N, K, num_sms, s);
+        case Q4_0: return launch_tc_fmt<Q4_0>(W, Xh, rs, Y, M, N, K, num_sms, s);
+        case Q8_0: return launch_tc_fmt<Q8_0>(W, Xh, rs, Y, M, N, K, num_sms, s);
+        case Q2_K: return launch_tc_fmt<Q2_K>(W, Xh, rs, Y, M, N, K, num_sms, s);
+        case Q3_K: return launch_tc_fmt<Q3_K>(W, Xh, rs, Y, M, N, K, num_sms, s);
+        case Q4_K: return launch_tc_fmt<Q4_K>(W, Xh, rs, Y, M, N, K, num_sms, s);
+        case Q5_K: return launch_tc_fmt<Q5_K>(W, Xh, rs, Y, M, N, K, num_sms, s);
+        case Q6_K: return launch_tc_fmt<Q6_K>(W, Xh, rs, Y, M, N, K, num_sms, s);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -1201,9 +1233,9 @@ cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, in
     cudaError_t e = scratch_pool(&pool);
     if (e != cudaSuccess) return e;
     __half* Xh = nullptr;
-    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), static_cast<size_t>(n) * 2, pool, s);
+    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), scratch_bytes(M, K), pool, s);
     if (e != cudaSuccess) return e;
-    e = gemm_tc_run(type, W, X, Xh, Y, M, N, K, num_sms, s);
+    e = gemm_tc_run(type, W, X, Xh, reinterpret_cast<float*>(Xh + n), Y, M, N, K, num_sms, s);
     cudaError_t e2 = cudaFreeAsync(Xh, s);
     return e != cudaSuccess ? e : e2;
 }
@@ -1216,20 +1248,21 @@ cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int
     cudaError_t e = scratch_pool(&pool);
     if (e != cudaSuccess) return e;
     __half* Xh = nullptr;
-    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), static_cast<size_t>(n) * 2, pool, s);
+    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), scratch_bytes(rows, K), pool, s);
     if (e != cudaSuccess) return e;
-    e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rows, K, num_sms, s)
-                            : launch_x_to_f16<false>(X, Xh, rows, K, num_sms, s);
+    float* rs = reinterpret_cast<float*>(Xh + n);
+    e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, rows, K, num_sms, s)
+                            : launch_x_to_f16<false>(X, Xh, rs, rows, K, num_sms, s);
     if (e == cudaSuccess) {
         const ExpertSet ex{reinterpret_cast<const uint8_t* const*>(wptrs), offsets, n_experts};
         switch (type) {
-            case Q4_0: e = launch_tc_grouped<Q4_0>(ex, Xh, Y, rows, N, K, num_sms, s); break;
-            case Q8_0: e = launch_tc_grouped<Q8_0>(ex, Xh, Y, rows, N, K, num_sms, s); break;
-            case Q2_K: e = launch_tc_grouped<Q2_K>(ex, Xh, Y, rows, N, K, num_sms, s); break;
-            case Q3_K: e = launch_tc_grouped<Q3_K>(ex, Xh, Y, rows, N, K, num_sms, s); break;
-            case Q4_K: e = launch_tc_grouped<Q4_K>(ex, Xh, Y, rows, N, K, num_sms, s); break;
-            case Q5_K: e = launch_tc_grouped<Q5_K>(ex, Xh, Y, rows, N, K, num_sms, s); break;
-            case Q6_K: e = launch_tc_grouped<Q6_K>(ex, Xh, Y, rows, N, K, num_sms, s); break;
+            case Q4_0: e = launch_tc_grouped<Q4_0>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
+            case Q8_0: e = launch_tc_grouped<Q8_0>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
+            case Q2_K: e = launch_tc_grouped<Q2_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
+            case Q3_K: e = launch_tc_grouped<Q3_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
+            case Q4_K: e = launch_tc_grouped<Q4_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
+            case Q5_K: e = launch_tc_grouped<Q5_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
+            case Q6_K: e = launch_tc_grouped<Q6_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
             default: e = cudaErrorInvalidValue;
         }
     }
@@ -1248,14 +1281,17 @@ cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int
 // from cudaGetSymbolAddress with that device current, looked up once per
 // device on that device's first call.  All calls on a device share the array:
 // calls whose kernels overlap on the GPU race.  Each call writes every element
-// it reads (the tensor map stops at M x K), so nothing needs clearing.
+// it reads (the tensor map stops at M x K, and M row scales), so nothing needs
+// clearing.
 // ---------------------------------------------------------------------------
 
 static __device__ __align__(256) uint16_t g_noalloc_x16[SWQ_GEMM_NOALLOC_MAX_X_ELEMS];
+// one scale per X row; K >= 32, so M <= SWQ_GEMM_NOALLOC_MAX_X_ELEMS / 32
+static __device__ __align__(256) float g_noalloc_rowscale[SWQ_GEMM_NOALLOC_MAX_X_ELEMS / 32];
 
-static cudaError_t noalloc_scratch(__half** out) {
+static cudaError_t noalloc_scratch(__half** xh, float** rs) {
     static std::mutex mu;
-    static std::map<int, void*> addr;  // device -> device address of g_noalloc_x16
+    static std::map<int, std::pair<void*, void*>> addr;  // device -> device addresses of the two arrays
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -1263,11 +1299,15 @@ static cudaError_t noalloc_scratch(__half** out) {
     auto it = addr.find(dev);
     if (it == addr.end()) {
         void* p = nullptr;
+        void* q = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_x16);
         if (e != cudaSuccess) return e;
-        it = addr.emplace(dev, p).first;
+        e = cudaGetSymbolAddress(&q, g_noalloc_rowscale);
+        if (e != cudaSuccess) return e;
+        it = addr.emplace(dev, std::make_pair(p, q)).first;
     }
-    *out = static_cast<__half*>(it->second);
+    *xh = static_cast<__half*>(it->second.first);
+    *rs = static_cast<float*>(it->second.second);
     return cudaSuccess;
 }
 
@@ -1276,9 +1316,10 @@ cudaError_t gemm_tc_launch_noalloc(int type, const void* W, const float* X, floa
     if (!gemm_tc_supported(type, W, M, N, K, refcpu)) return cudaErrorNotSupported;
     if (static_cast<int64_t>(M) * K > SWQ_GEMM_NOALLOC_MAX_X_ELEMS) return cudaErrorInvalidValue;
     __half* Xh = nullptr;
-    cudaError_t e = noalloc_scratch(&Xh);
+    float* rs = nullptr;
+    cudaError_t e = noalloc_scratch(&Xh, &rs);
     if (e != cudaSuccess) return e;
-    return gemm_tc_run(type, W, X, Xh, Y, M, N, K, num_sms, s);
+    return gemm_tc_run(type, W, X, Xh, rs, Y, M, N, K, num_sms, s);
 }
 
 SWQ_DEFINE_STATUS_FETCH(gemm_tc)

@@ -78,12 +78,13 @@ def lib() -> ctypes.CDLL:
         "swq_gemm_noalloc": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
         "swq_grouped_gemm": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "swq_rmsnorm": (i32, [vp, vp, vp, i32, ctypes.c_float, i32, vp]),
-        "swq_rope_kv": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp]),
+        "swq_add_rmsnorm": (i32, [vp, vp, vp, vp, i32, ctypes.c_float, i32, vp]),
+        "swq_rope_kv": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, vp]),
         "swq_attention_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
-        "swq_attention_decode": (i32, [vp, vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, i32, vp]),
+        "swq_attention_decode": (i32, [vp, vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, i32, i32, vp]),
         "swq_silu_mul": (i32, [vp, vp, vp, i32, i32, i32, vp]),
         "swq_add": (i32, [vp, vp, i64, vp]),
-        "swq_embed": (i32, [vp, vp, vp, i32, i32, vp]),
+        "swq_embed": (i32, [vp, vp, vp, i32, i32, i32, vp]),
         "swq_argmax": (i32, [vp, i32, i32, vp, vp, vp, vp]),
         "swq_decode_advance": (i32, [vp, vp, vp]),
         "swq_set_option": (i32, [i32, i32]),
@@ -198,10 +199,15 @@ def rmsnorm(out, x, w, n: int, eps: float, rows: int = 1, stream=None) -> None:
     _raise(lib().swq_rmsnorm(_ptr(out), _ptr(x), _ptr(w), n, eps, rows, _stream(stream)))
 
 
+def add_rmsnorm(out, x, y, w, n: int, eps: float, rows: int = 1, stream=None) -> None:
+    _raise(lib().swq_add_rmsnorm(_ptr(out), _ptr(x), _ptr(y), _ptr(w), n, eps, rows, _stream(stream)))
+
+
 def rope_kv(q, k, v, k_cache, v_cache, pos, freqs, q_dim: int, kv_dim: int, head_dim: int, rope_dim: int,
-            neox: bool, rows: int, max_seq: int, stream=None) -> None:
+            neox: bool, rows: int, max_seq: int, ldq: int = 0, ldk: int = 0, ldv: int = 0, stream=None) -> None:
     _raise(lib().swq_rope_kv(_ptr(q), _ptr(k), _ptr(v), _ptr(k_cache), _ptr(v_cache), _ptr(pos), _ptr(freqs), q_dim,
-                             kv_dim, head_dim, rope_dim, 1 if neox else 0, rows, max_seq, _stream(stream)))
+                             kv_dim, head_dim, rope_dim, 1 if neox else 0, rows, max_seq, ldq, ldk, ldv,
+                             _stream(stream)))
 
 
 def attention_workspace_bytes(num_heads: int, num_kv_heads: int, head_dim: int, rows: int, max_seq: int) -> int:
@@ -209,9 +215,9 @@ def attention_workspace_bytes(num_heads: int, num_kv_heads: int, head_dim: int, 
 
 
 def attention_decode(out, q, k_cache, v_cache, pos, workspace, workspace_bytes: int, num_heads: int,
-                     num_kv_heads: int, head_dim: int, rows: int, max_seq: int, stream=None) -> None:
+                     num_kv_heads: int, head_dim: int, rows: int, max_seq: int, ldq: int = 0, stream=None) -> None:
     _raise(lib().swq_attention_decode(_ptr(out), _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(pos), _ptr(workspace),
-                                      workspace_bytes, num_heads, num_kv_heads, head_dim, rows, max_seq,
+                                      workspace_bytes, num_heads, num_kv_heads, head_dim, rows, max_seq, ldq,
                                       _stream(stream)))
 
 
@@ -223,8 +229,8 @@ def add(x, y, n: int, stream=None) -> None:
     _raise(lib().swq_add(_ptr(x), _ptr(y), n, _stream(stream)))
 
 
-def embed(x, table, tokens, dim: int, rows: int = 1, stream=None) -> None:
-    _raise(lib().swq_embed(_ptr(x), _ptr(table), _ptr(tokens), dim, rows, _stream(stream)))
+def embed(x, table, tokens, dim: int, vocab: int, rows: int = 1, stream=None) -> None:
+    _raise(lib().swq_embed(_ptr(x), _ptr(table), _ptr(tokens), dim, vocab, rows, _stream(stream)))
 
 
 def argmax(logits, n: int, rows: int, tokens, history=None, step=None, stream=None) -> None:

@@ -3,9 +3,11 @@
 `LlamaDecoder` runs the reference's decode forward (Model::forward,
 src/model.h:257-543, dense Llama path) entirely on one GPU through libswq:
 embedding row, per layer RMSNorm, q/k/v GEMVs, RoPE + KV-cache append,
-grouped-query attention, o GEMV, residual, RMSNorm, gate+up GEMV (the two
-matrices stacked into one when they share a type), SiLU-mul, down GEMV,
-residual; final RMSNorm, LM-head GEMV and greedy argmax.  `rows` sequences
+grouped-query attention, o GEMV, residual, RMSNorm, gate+up GEMV, SiLU-mul,
+down GEMV, residual; final RMSNorm, LM-head GEMV and greedy argmax.  Matrices
+of one type that read the same input are stacked into one GEMV (q with k,
+gate with up), and every residual add runs in one kernel with the RMSNorm
+after it.  `rows` sequences
 decode in step.  The position lives in device memory, so one decode step is
 captured once in a CUDA graph and replayed per token.
 
@@ -21,8 +23,9 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import lib as _lib_mod  # noqa: F401  (module import for the ctypes table)
-from .lib import (OPT_TENSOR_CORE_MIN_M, add, argmax, attention_decode, attention_workspace_bytes, decode_advance,
-                  embed, gemm, get_option, rmsnorm, rope_kv, silu_mul)
+from .lib import (GEMM_NOALLOC_MAX_X_ELEMS, OPT_TENSOR_CORE_MIN_M, add_rmsnorm, argmax, attention_decode,
+                  attention_workspace_bytes, decode_advance, embed, gemm, gemm_noalloc, get_option, rmsnorm,
+                  rope_kv, silu_mul)
 from .synth import LAYOUT, Q4_K, Q6_K, Q8_0, row_bytes
 
 
@@ -115,6 +118,7 @@ class LlamaDecoder:
                             else 1.0 + 0.01 * torch.randn(cfg.dim, generator=g, **f32))
         self.output = blocks("output", cfg.vocab, cfg.dim, W.get("output"))
         self.fuse_gate_up = t["w_gate"] == t["w_up"]
+        self.fuse_qk = t["wq"] == t["wk"]
         self.layers = []
         for layer in range(cfg.n_layers):
             lw = W["layers"][layer] if weights else {}
@@ -126,13 +130,14 @@ class LlamaDecoder:
                 L[name] = blocks(name, N, K, lw.get(name))
             if self.fuse_gate_up:  # rows of gate then rows of up: one GEMV
                 L["w_gate_up"] = torch.cat([L.pop("w_gate"), L.pop("w_up")])
+            if self.fuse_qk:  # rows of q then rows of k
+                L["w_qk"] = torch.cat([L.pop("wq"), L.pop("wk")])
             self.layers.append(L)
         self.freqs = torch.from_numpy(rope_freqs(cfg)).to(dev)
         B = rows
         self.x = torch.zeros((B, cfg.dim), **f32)
         self.xb = torch.zeros_like(self.x)
-        self.q = torch.zeros((B, cfg.q_dim), **f32)
-        self.k = torch.zeros((B, cfg.kv_dim), **f32)
+        self.qk = torch.zeros((B, cfg.q_dim + cfg.kv_dim), **f32)  # q then k, per row
         self.v = torch.zeros((B, cfg.kv_dim), **f32)
         self.att = torch.zeros((B, cfg.q_dim), **f32)
         self.gu = torch.zeros((B, 2 * cfg.ffn), **f32)
@@ -145,43 +150,60 @@ class LlamaDecoder:
         self.step_no = torch.zeros(1, dtype=torch.int32, device=dev)
         self.history = torch.zeros((max_steps, B), dtype=torch.int32, device=dev)
         self.ws_bytes = attention_workspace_bytes(cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, B, cfg.max_seq)
-        self.ws = torch.zeros(max(1, self.ws_bytes // 4), **f32)
+        self.ws = torch.zeros(max(1, self.ws_bytes // 4), **f32)  # zero-filled, as the kernel expects
+        self.max_steps = max_steps
+        self.steps_issued = 0
         self.stream = torch.cuda.Stream(device=dev)
         self.graph = None
 
     # ------------------------------------------------------------ one token
+    def _gemm(self, type_id, W, X, Y, M, N, K, stream):
+        # Rows that take the tensor-core GEMM use its allocation-free form, so
+        # a captured step holds no allocation (one stream orders the calls).
+        if M >= get_option(OPT_TENSOR_CORE_MIN_M) and M * K <= GEMM_NOALLOC_MAX_X_ELEMS:
+            gemm_noalloc(type_id, W, X, Y, M, N, K, stream=stream)
+        else:
+            gemm(type_id, W, X, Y, M, N, K, stream=stream)
+
     def step(self, greedy: bool = True) -> None:
         """One decode step for all rows at position *pos: logits of the current
         tokens; with greedy, tokens <- argmax (also into history) and pos += 1."""
         c, B, s = self.cfg, self.rows, self.stream
         t = c.types
-        embed(self.x, self.token_embd, self.tokens, c.dim, B, stream=s)
+        gemm = self._gemm  # noqa: F811
+        ld = c.q_dim + c.kv_dim
+        q, k = self.qk, self.qk[:, c.q_dim:]
+        embed(self.x, self.token_embd, self.tokens, c.dim, c.vocab, B, stream=s)
+        rmsnorm(self.xb, self.x, self.layers[0]["attn_norm"], c.dim, c.eps, B, stream=s)
         for li, L in enumerate(self.layers):
-            rmsnorm(self.xb, self.x, L["attn_norm"], c.dim, c.eps, B, stream=s)
-            gemm(t["wq"], L["wq"], self.xb, self.q, B, c.q_dim, c.dim, stream=s)
-            gemm(t["wk"], L["wk"], self.xb, self.k, B, c.kv_dim, c.dim, stream=s)
+            if self.fuse_qk:
+                gemm(t["wq"], L["w_qk"], self.xb, self.qk, B, ld, c.dim, stream=s)
+            else:
+                gemm(t["wq"], L["wq"], self.xb, self.att, B, c.q_dim, c.dim, stream=s)
+                q[:, :c.q_dim].copy_(self.att)
+                gemm(t["wk"], L["wk"], self.xb, self.v, B, c.kv_dim, c.dim, stream=s)
+                k.copy_(self.v)
             gemm(t["wv"], L["wv"], self.xb, self.v, B, c.kv_dim, c.dim, stream=s)
             kc, vc = self.kcache[li], self.vcache[li]
-            rope_kv(self.q, self.k, self.v, kc, vc, self.pos, self.freqs, c.q_dim, c.kv_dim, c.head_dim,
-                    c.head_dim, c.rope_neox, B, c.max_seq, stream=s)
-            attention_decode(self.att, self.q, kc, vc, self.pos, self.ws, self.ws_bytes, c.n_heads, c.n_kv_heads,
-                             c.head_dim, B, c.max_seq, stream=s)
+            rope_kv(q, k, self.v, kc, vc, self.pos, self.freqs, c.q_dim, c.kv_dim, c.head_dim, c.head_dim,
+                    c.rope_neox, B, c.max_seq, ldq=ld, ldk=ld, stream=s)
+            attention_decode(self.att, q, kc, vc, self.pos, self.ws, self.ws_bytes, c.n_heads, c.n_kv_heads,
+                             c.head_dim, B, c.max_seq, ldq=ld, stream=s)
             gemm(t["wo"], L["wo"], self.att, self.xb, B, c.dim, c.q_dim, stream=s)
-            add(self.x, self.xb, B * c.dim, stream=s)
-            rmsnorm(self.xb, self.x, L["ffn_norm"], c.dim, c.eps, B, stream=s)
+            add_rmsnorm(self.xb, self.x, self.xb, L["ffn_norm"], c.dim, c.eps, B, stream=s)  # x += o; xb = norm(x)
             if self.fuse_gate_up:
                 gemm(t["w_gate"], L["w_gate_up"], self.xb, self.gu, B, 2 * c.ffn, c.dim, stream=s)
-                silu_mul(self.h, self.gu, self.gu[:, c.ffn:], c.ffn, B, 2 * c.ffn, stream=s)
             else:
-                gate, up = self.gu[:, :c.ffn], self.gu[:, c.ffn:]
                 gemm(t["w_gate"], L["w_gate"], self.xb, self.h, B, c.ffn, c.dim, stream=s)
-                gate.copy_(self.h)
+                self.gu[:, :c.ffn].copy_(self.h)
                 gemm(t["w_up"], L["w_up"], self.xb, self.h, B, c.ffn, c.dim, stream=s)
-                up.copy_(self.h)
-                silu_mul(self.h, self.gu, self.gu[:, c.ffn:], c.ffn, B, 2 * c.ffn, stream=s)
+                self.gu[:, c.ffn:].copy_(self.h)
+            silu_mul(self.h, self.gu, self.gu[:, c.ffn:], c.ffn, B, 2 * c.ffn, stream=s)
             gemm(t["w_down"], L["w_down"], self.h, self.xb, B, c.dim, c.ffn, stream=s)
-            add(self.x, self.xb, B * c.dim, stream=s)
-        rmsnorm(self.x, self.x, self.output_norm, c.dim, c.eps, B, stream=s)
+            if li + 1 < len(self.layers):  # x += down; xb = next layer's attention norm of x
+                add_rmsnorm(self.xb, self.x, self.xb, self.layers[li + 1]["attn_norm"], c.dim, c.eps, B, stream=s)
+            else:  # x += down; x = output norm of x
+                add_rmsnorm(self.x, self.x, self.xb, self.output_norm, c.dim, c.eps, B, stream=s)
         gemm(t["output"], self.output, self.x, self.logits, B, c.vocab, c.dim, stream=s)
         if greedy:
             argmax(self.logits, c.vocab, B, self.tokens, self.history, self.step_no, stream=s)
@@ -191,8 +213,6 @@ class LlamaDecoder:
         """Capture one greedy step in a CUDA graph (after one eager warm-up step
         that loads the kernels; the caller resets the state afterwards)."""
         import torch
-        if self.rows > get_option(OPT_TENSOR_CORE_MIN_M) - 1:
-            raise ValueError("graph capture needs the GEMV path (rows below the tensor-core minimum M)")
         with torch.cuda.stream(self.stream):
             self.step()
         self.stream.synchronize()
@@ -201,14 +221,20 @@ class LlamaDecoder:
             self.step()
 
     def reset(self, tokens, pos: int = 0) -> None:
+        """Set the current tokens and position (ordered on the decode stream)."""
         import torch
-        self.tokens.copy_(torch.as_tensor(np.asarray(tokens, np.int32)).to(self.device))
-        self.pos.fill_(pos)
-        self.step_no.fill_(0)
+        with torch.cuda.stream(self.stream):
+            self.tokens.copy_(torch.as_tensor(np.asarray(tokens, np.int32)).to(self.device))
+            self.pos.fill_(pos)
+            self.step_no.fill_(0)
+        self.steps_issued = 0
 
     def generate(self, n: int) -> None:
         """n greedy steps (graph replays when captured) on self.stream."""
         import torch
+        if self.steps_issued + n > self.max_steps:
+            raise ValueError(f"more than max_steps={self.max_steps} steps since reset()")
+        self.steps_issued += n
         with torch.cuda.stream(self.stream):
             for _ in range(n):
                 if self.graph is not None:
@@ -222,6 +248,7 @@ class LlamaDecoder:
         import torch
         g = torch.Generator(device=self.device)
         g.manual_seed(seed)
-        self.kcache[:, :, :n_pos].normal_(generator=g)
-        self.vcache[:, :, :n_pos].normal_(generator=g)
-        self.pos.fill_(n_pos)
+        with torch.cuda.stream(self.stream):
+            self.kcache[:, :, :n_pos].normal_(generator=g)
+            self.vcache[:, :, :n_pos].normal_(generator=g)
+            self.pos.fill_(n_pos)

@@ -77,7 +77,7 @@ def test_options():
     swq.set_option(swq.OPT_TENSOR_CORE_GEMM, 1)
     with pytest.raises(swq.SwqError):
         swq.set_option(swq.OPT_TENSOR_CORE_GEMM, 2)
-    assert swq.get_option(swq.OPT_TENSOR_CORE_MIN_M) == 32
+    assert swq.get_option(swq.OPT_TENSOR_CORE_MIN_M) == 5
     with pytest.raises(swq.SwqError):
         swq.set_option(swq.OPT_TENSOR_CORE_MIN_M, 1)
     swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 1)

@@ -35,7 +35,7 @@ def _tensor_core_on():
     swq.set_option(swq.OPT_TENSOR_CORE_MIN_M, 9)
     yield
     swq.set_option(swq.OPT_TENSOR_CORE_GEMM, 1)
-    swq.set_option(swq.OPT_TENSOR_CORE_MIN_M, 32)
+    swq.set_option(swq.OPT_TENSOR_CORE_MIN_M, 5)
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
@@ -107,6 +107,32 @@ def test_gemv_groups_when_disabled(cuda, oracle_mod):
     swq.set_option(swq.OPT_TENSOR_CORE_GEMM, 0)
     got = _gemm(cuda, t, blocks, X, N, K)
     assert rel_l2(got, oracle_mod.gemm(t, blocks, X, M, N, K)) <= REL_L2_TOL
+
+
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K", "Q8_0"])
+def test_activations_beyond_fp16_range(cuda, oracle_mod, fmt):
+    """Rows whose magnitudes exceed fp16's 65504 (a SwiGLU output of large
+    gate/up values) next to ordinary, tiny and all-zero rows: each row is
+    scaled by a power of two before the fp16 conversion, so every row keeps
+    the relative accuracy of an ordinary one and nothing overflows."""
+    t = synth.IDS[fmt]
+    N, K, M = 256, 1024, 24
+    blocks = synth.random_blocks(t, N, K, seed=2450 + t)
+    X = synth.random_activations(M, K, seed=2451)
+    X[1] *= 3.0e5
+    X[2] *= 1.0e9
+    X[3, 17] = 2.0e7
+    X[4] *= 1.0e-6
+    X[5] = 0.0
+    X[6] *= 6.0e4
+    got = _gemm(cuda, t, blocks, X, N, K)
+    want = oracle_mod.gemm(t, blocks, X, M, N, K)
+    assert np.all(np.isfinite(got))
+    assert np.all(got[5] == 0.0)
+    for r in range(M):
+        if r == 5:
+            continue
+        assert rel_l2(got[r], want[r]) <= REL_L2_TOL, (r, rel_l2(got[r], want[r]))
 
 
 def test_deterministic(cuda):

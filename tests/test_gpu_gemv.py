@@ -15,6 +15,14 @@ from swq import synth
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True)
+def _gemv_kernel_for_every_m():
+    """These tests cover the GEMV kernel: keep every M off the tensor-core path."""
+    swq.set_option(swq.OPT_TENSOR_CORE_MIN_M, 1 << 20)
+    yield
+    swq.set_option(swq.OPT_TENSOR_CORE_MIN_M, 5)
+
 FORMATS = ["Q4_0", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"]
 
 
