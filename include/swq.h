@@ -163,9 +163,10 @@ swq_status swq_grouped_gemm(int ggml_type, const void* const* W_experts, const i
 /* ---- Allocation-free GEMM ------------------------------------------------
  *
  * No counterpart in the reference.  swq_gemm's tensor-core path takes a
- * temporary fp16 copy of X (M * K * 2 bytes, plus M fp32 row scales) from a
- * stream-ordered memory pool that libswq creates per device and keeps until
- * exit.  Some callers cannot let a library allocate device memory: processes
+ * temporary fp16 copy of X (M * K * 2 bytes, plus M fp32 row scales and, for
+ * calls with fewer output tiles than half the SMs, split-K partial products)
+ * from a stream-ordered memory pool that libswq creates per device and keeps
+ * until exit.  Some callers cannot let a library allocate device memory: processes
  * whose own allocator already owns the GPU's memory (a serving engine that
  * reserves what HBM is left for its KV cache at start-up, a caching allocator
  * that hands out every device byte), where a hidden allocation can fail or
@@ -173,8 +174,11 @@ swq_status swq_grouped_gemm(int ggml_type, const void* const* W_experts, const i
  * computes what swq_gemm computes and allocates nothing: the fp16 copy of X
  * lives in a fixed device array inside libswq of SWQ_GEMM_NOALLOC_MAX_X_ELEMS
  * halves (16 MiB), its row scales in a second one of
- * SWQ_GEMM_NOALLOC_MAX_X_ELEMS / 32 floats (1 MiB), which every GPU that
- * loads the library holds until the process exits.  The caller passes W, X and Y as for swq_gemm.
+ * SWQ_GEMM_NOALLOC_MAX_X_ELEMS / 32 floats (1 MiB), and the split-K partial
+ * products of calls with few output tiles (small M and N) in a third of 4 Mi
+ * floats (16 MiB) with 4096 tile counters -- a call whose split does not fit
+ * there runs unsplit -- which every GPU that loads the library holds until
+ * the process exits.  The caller passes W, X and Y as for swq_gemm.
  *   - M * K above SWQ_GEMM_NOALLOC_MAX_X_ELEMS: SWQ_ERR_BAD_SHAPE.
  *   - The first call on a device looks up the array's address on that device
  *     (cudaGetSymbolAddress with the device current); make that first call
@@ -215,7 +219,19 @@ enum {
      * GEMV kernel's cost grows with its rows (it is bound by the integer dot
      * products from about 4 rows on), so from 5 rows on the tensor cores win
      * on the Llama projection shapes. */
-    SWQ_OPT_TENSOR_CORE_MIN_M = 5
+    SWQ_OPT_TENSOR_CORE_MIN_M = 5,
+    /* Shared memory one GEMV CTA may use, in KB (0, the default: automatic --
+     * half an SM, so the next kernel's CTAs fit beside this one's and start
+     * streaming their weights early, unless the matrix is large enough that a
+     * deeper weight ring pays more; larger values are capped at the per-block
+     * maximum). */
+    SWQ_OPT_GEMV_SMEM_KB = 6,
+    /* Largest weight stage of the GEMV ring, in KB (0, the default: 96). */
+    SWQ_OPT_GEMV_STAGE_KB = 7,
+    /* GEMV CTAs per SM (0, the default: automatic; 1..4 forces it).  More
+     * than one puts more consumer warps on each SM, each CTA with its share
+     * of the SM's shared memory. */
+    SWQ_OPT_GEMV_CTAS_PER_SM = 8
 };
 swq_status swq_set_option(int option, int value);
 int swq_get_option(int option);

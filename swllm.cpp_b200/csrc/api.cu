@@ -29,6 +29,9 @@ std::atomic<int> g_opt_early_prefetch{1};
 std::atomic<int> g_opt_gemv_max_m{8};
 std::atomic<int> g_opt_gemm_tc{1};
 std::atomic<int> g_opt_tc_min_m{5};
+std::atomic<int> g_opt_gemv_smem_kb{0};
+std::atomic<int> g_opt_gemv_stage_kb{0};
+std::atomic<int> g_opt_gemv_ctas{0};
 
 swq_status fail(swq_status s, const std::string& msg) {
     g_last_error = msg;
@@ -128,6 +131,9 @@ swq_status gemm_gemv_groups(int type, const void* W, const float* X, float* Y, i
         L.num_sms = dev.num_sms;
         L.smem_per_block_optin = dev.smem_per_block_optin;
         L.smem_per_sm = dev.smem_per_sm;
+        L.smem_kb = g_opt_gemv_smem_kb;
+        L.stage_kb = g_opt_gemv_stage_kb;
+        L.ctas_per_sm = g_opt_gemv_ctas;
         cudaError_t e = swq::gemv_launch(L, s);
         if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
     }
@@ -186,6 +192,18 @@ swq_status swq_set_option(int option, int value) {
             if (value < 2) return fail(SWQ_ERR_BAD_ARG, "tensor-core minimum M must be >= 2");
             g_opt_tc_min_m = value;
             return SWQ_OK;
+        case SWQ_OPT_GEMV_SMEM_KB:
+            if (value < 0 || value > 1024) return fail(SWQ_ERR_BAD_ARG, "GEMV shared memory must be 0..1024 KB");
+            g_opt_gemv_smem_kb = value;
+            return SWQ_OK;
+        case SWQ_OPT_GEMV_STAGE_KB:
+            if (value < 0 || value > 1024) return fail(SWQ_ERR_BAD_ARG, "GEMV stage size must be 0..1024 KB");
+            g_opt_gemv_stage_kb = value;
+            return SWQ_OK;
+        case SWQ_OPT_GEMV_CTAS_PER_SM:
+            if (value < 0 || value > 4) return fail(SWQ_ERR_BAD_ARG, "GEMV CTAs per SM must be 0..4");
+            g_opt_gemv_ctas = value;
+            return SWQ_OK;
         default:
             return fail(SWQ_ERR_BAD_ARG, "unknown option " + std::to_string(option));
     }
@@ -198,6 +216,9 @@ int swq_get_option(int option) {
         case SWQ_OPT_GEMV_MAX_M: return g_opt_gemv_max_m;
         case SWQ_OPT_TENSOR_CORE_GEMM: return g_opt_gemm_tc;
         case SWQ_OPT_TENSOR_CORE_MIN_M: return g_opt_tc_min_m;
+        case SWQ_OPT_GEMV_SMEM_KB: return g_opt_gemv_smem_kb;
+        case SWQ_OPT_GEMV_STAGE_KB: return g_opt_gemv_stage_kb;
+        case SWQ_OPT_GEMV_CTAS_PER_SM: return g_opt_gemv_ctas;
         default: return -1;
     }
 }

@@ -143,32 +143,51 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
 }
 
 // Decode attention, split over the context: CTA (split, kv head, sequence)
-// handles timesteps [split*chunk, ...) for the MUL query heads that share the
+// handles a slice of the timesteps for the MUL query heads that share the
 // kv head (src/model.h:329-361: score = q.k / sqrt(head_dim), softmax over
 // t <= pos, out = sum softmax * v), keeping a running max m, the sum l of
 // exp(score - m) and the unnormalised output.  Each CTA writes its partial
 // (m, l, o) per head; the last CTA of a (sequence, kv head) to finish -- an
 // atomic count in the workspace, reset by that CTA -- merges the splits.
-constexpr int ATT_THREADS = 128;
 constexpr int ATT_MAXSPLIT = 64;  // the merge keeps MUL x splits weights in the partial buffer
 
-// MUL query heads per kv head, PER = head_dim / 32 elements per lane.
+// Warps per CTA and consecutive positions a warp takes at once; the CTA's
+// per-warp partials (NW x MUL x head_dim floats) stay within 32 KB.
 template <int MUL, int PER>
-__global__ void __launch_bounds__(ATT_THREADS) attn_kernel(
+struct AttCfg {
+    static constexpr int NW = MUL * PER <= 32 ? 8 : 4;
+    static constexpr int U = PER <= 4 ? 8 : 4;
+    static constexpr int THREADS = NW * 32;
+    static constexpr int MINCHUNK = NW * U;  // positions per split at least
+};
+
+// MUL query heads per kv head, PER = head_dim / 32 elements per lane.
+// The live context [0, pos] is cut into ns = ceil(n_ctx / chunk) splits of
+// chunk = max(MINCHUNK, ceil(n_ctx / gridDim.x)) positions (worked out on the
+// device from pos, so a captured launch adapts to the position); CTAs past ns
+// return at once.  Inside a split, warp w takes positions w U .. w U + U - 1,
+// then the next NW U: all their K and V loads are issued before any
+// arithmetic, then one online-softmax update per query head for the U scores.
+template <int MUL, int PER>
+__global__ void __launch_bounds__(AttCfg<MUL, PER>::THREADS) attn_kernel(
     const float* __restrict__ q, const float* __restrict__ kcache, const float* __restrict__ vcache,
     const int* __restrict__ pos_p, float* __restrict__ part_o, float* __restrict__ part_ml,
-    unsigned* __restrict__ done, float* __restrict__ out, int num_heads, int num_kv_heads, int max_seq, int chunk,
-    int ldq) {
+    unsigned* __restrict__ done, float* __restrict__ out, int num_heads, int num_kv_heads, int max_seq, int ldq) {
+    using C = AttCfg<MUL, PER>;
     constexpr int HD = 32 * PER;
+    constexpr int NW = C::NW, U = C::U, NT = C::THREADS;
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-    const int nsplit = gridDim.x;
+    const int ns_grid = gridDim.x;  // slot stride of the partials
     const int kv_dim = num_kv_heads * HD;
-    const int n_ctx = *pos_p + 1;
+    const int n_ctx = min(*pos_p + 1, max_seq);
+    const int chunk = max(C::MINCHUNK, (n_ctx + ns_grid - 1) / ns_grid);
+    const int nsplit = (n_ctx + chunk - 1) / chunk;
+    if (split >= nsplit) return;
     const int t0 = split * chunk, t1 = min(n_ctx, t0 + chunk);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float inv_sqrt = 1.0f / sqrtf(static_cast<float>(HD));
-    __shared__ float s_m[ATT_THREADS / 32][MUL], s_l[ATT_THREADS / 32][MUL];
-    __shared__ float s_o[ATT_THREADS / 32][MUL][HD];
+    __shared__ float s_m[NW][MUL], s_l[NW][MUL];
+    __shared__ float s_o[NW][MUL][HD];
     __shared__ unsigned s_last;
 
     float qv[MUL][PER], acc[MUL][PER], m[MUL], l[MUL];
@@ -180,31 +199,57 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(
 #pragma unroll
         for (int e = 0; e < PER; ++e) {
             acc[j][e] = 0.f;
-            qv[j][e] = qh[e * 32 + lane];
+            qv[j][e] = qh[e * 32 + lane] * inv_sqrt;
         }
     }
     const float* kbase = kcache + static_cast<size_t>(b) * max_seq * kv_dim + kvh * HD;
     const float* vbase = vcache + static_cast<size_t>(b) * max_seq * kv_dim + kvh * HD;
-    for (int t = t0 + warp; t < t1; t += ATT_THREADS / 32) {
-        const float* kt = kbase + static_cast<size_t>(t) * kv_dim;
-        const float* vt = vbase + static_cast<size_t>(t) * kv_dim;
-        float kk[PER], vv[PER];
+    for (int tb = t0 + warp * U; tb < t1; tb += NW * U) {
+        float kk[U][PER], vv[U][PER];
 #pragma unroll
-        for (int e = 0; e < PER; ++e) {
-            kk[e] = kt[e * 32 + lane];
-            vv[e] = vt[e * 32 + lane];
+        for (int u = 0; u < U; ++u) {
+            const int t = min(tb + u, t1 - 1);  // past the end: a repeat, masked below
+            const float* kt = kbase + static_cast<size_t>(t) * kv_dim;
+            const float* vt = vbase + static_cast<size_t>(t) * kv_dim;
+#pragma unroll
+            for (int e = 0; e < PER; ++e) {
+                kk[u][e] = __ldcg(kt + e * 32 + lane);
+                vv[u][e] = __ldcg(vt + e * 32 + lane);
+            }
         }
 #pragma unroll
         for (int j = 0; j < MUL; ++j) {
-            float sdot = 0.f;
+            float sc[U];
 #pragma unroll
-            for (int e = 0; e < PER; ++e) sdot = fmaf(qv[j][e], kk[e], sdot);
-            const float score = warp_sum(sdot) * inv_sqrt;
-            const float mn = fmaxf(m[j], score);
-            const float corr = expf(m[j] - mn), pexp = expf(score - mn);
-            l[j] = l[j] * corr + pexp;
+            for (int u = 0; u < U; ++u) {
+                float d = 0.f;
 #pragma unroll
-            for (int e = 0; e < PER; ++e) acc[j][e] = fmaf(pexp, vv[e], acc[j][e] * corr);
+                for (int e = 0; e < PER; ++e) d = fmaf(qv[j][e], kk[u][e], d);
+                sc[u] = d;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                for (int u = 0; u < U; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+            }
+            float mn = m[j];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (tb + u >= t1) sc[u] = -INFINITY;
+                mn = fmaxf(mn, sc[u]);
+            }
+            const float corr = expf(m[j] - mn);
+            float ps = 0.f;
+#pragma unroll
+            for (int e = 0; e < PER; ++e) acc[j][e] *= corr;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const float pe = expf(sc[u] - mn);
+                ps += pe;
+#pragma unroll
+                for (int e = 0; e < PER; ++e) acc[j][e] = fmaf(pe, vv[u][e], acc[j][e]);
+            }
+            l[j] = l[j] * corr + ps;
             m[j] = mn;
         }
     }
@@ -219,17 +264,17 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(
         for (int e = 0; e < PER; ++e) s_o[warp][j][e * 32 + lane] = acc[j][e];
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < MUL * HD; idx += ATT_THREADS) {
+    for (int idx = threadIdx.x; idx < MUL * HD; idx += NT) {
         const int j = idx / HD, d = idx % HD;
         float mm = -INFINITY;
-        for (int w = 0; w < ATT_THREADS / 32; ++w) mm = fmaxf(mm, s_m[w][j]);
+        for (int w = 0; w < NW; ++w) mm = fmaxf(mm, s_m[w][j]);
         float ll = 0.f, oo = 0.f;
-        for (int w = 0; w < ATT_THREADS / 32; ++w) {
+        for (int w = 0; w < NW; ++w) {
             const float c = s_m[w][j] == -INFINITY ? 0.f : expf(s_m[w][j] - mm);
             ll += s_l[w][j] * c;
             oo += s_o[w][j][d] * c;
         }
-        const size_t slot = (static_cast<size_t>(b) * num_heads + kvh * MUL + j) * nsplit + split;
+        const size_t slot = (static_cast<size_t>(b) * num_heads + kvh * MUL + j) * ns_grid + split;
         part_o[slot * HD + d] = oo;
         if (d == 0) {
             part_ml[2 * slot] = mm;
@@ -249,8 +294,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(
     __threadfence();
     // weight of split s for head j: exp(m_s - M) / sum_s' l_s' exp(m_s' - M)
     float* s_w = &s_o[0][0][0];  // MUL x nsplit (nsplit <= ATT_MAXSPLIT)
-    for (int j = warp; j < MUL; j += ATT_THREADS / 32) {
-        const size_t base = (static_cast<size_t>(b) * num_heads + kvh * MUL + j) * nsplit;
+    for (int j = warp; j < MUL; j += NW) {
+        const size_t base = (static_cast<size_t>(b) * num_heads + kvh * MUL + j) * ns_grid;
         float M = -INFINITY;
         for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(&part_ml[2 * (base + s)]));
 #pragma unroll
@@ -266,11 +311,19 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(
         for (int s = lane; s < nsplit; s += 32) s_w[j * nsplit + s] /= L;
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < MUL * HD; idx += ATT_THREADS) {
+    for (int idx = threadIdx.x; idx < MUL * HD; idx += NT) {
         const int j = idx / HD, d = idx % HD;
-        const size_t base = (static_cast<size_t>(b) * num_heads + kvh * MUL + j) * nsplit;
+        const size_t base = (static_cast<size_t>(b) * num_heads + kvh * MUL + j) * ns_grid;
+        // eight partials in flight per batch (the loads do not wait on the sum)
         float o = 0.f;
-        for (int s = 0; s < nsplit; ++s) o = fmaf(__ldcg(&part_o[(base + s) * HD + d]), s_w[j * nsplit + s], o);
+        for (int s0 = 0; s0 < nsplit; s0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = s0 + u < nsplit ? __ldcg(&part_o[(base + s0 + u) * HD + d]) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (s0 + u < nsplit) o = fmaf(v[u], s_w[j * nsplit + s0 + u], o);
+        }
         out[(static_cast<size_t>(b) * num_heads + kvh * MUL + j) * HD + d] = o;
     }
 }
@@ -414,19 +467,19 @@ size_t attention_workspace(int num_heads, int num_kv_heads, int head_dim, int ro
 template <int MUL>
 static cudaError_t attn_per(int per, dim3 grid, cudaStream_t s, const float* q, const float* kc, const float* vc,
                             const int* pos, float* po, float* pml, unsigned* done, float* out, int nh, int nkv,
-                            int max_seq, int chunk, int ldq) {
+                            int max_seq, int ldq) {
     switch (per) {
         case 2:
-            attn_kernel<MUL, 2><<<grid, ATT_THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
-                                                             chunk, ldq);
+            attn_kernel<MUL, 2><<<grid, AttCfg<MUL, 2>::THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
+                                                             ldq);
             break;
         case 4:
-            attn_kernel<MUL, 4><<<grid, ATT_THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
-                                                             chunk, ldq);
+            attn_kernel<MUL, 4><<<grid, AttCfg<MUL, 4>::THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
+                                                             ldq);
             break;
         case 8:
-            attn_kernel<MUL, 8><<<grid, ATT_THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
-                                                             chunk, ldq);
+            attn_kernel<MUL, 8><<<grid, AttCfg<MUL, 8>::THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
+                                                             ldq);
             break;
         default: return cudaErrorInvalidValue;
     }
@@ -438,16 +491,15 @@ cudaError_t attention_launch(float* out, const float* q, const float* kcache, co
                              int splits, int ldq, cudaStream_t s) {
     if (num_kv_heads <= 0 || num_heads % num_kv_heads != 0 || head_dim % 32 != 0) return cudaErrorInvalidValue;
     const int mul = num_heads / num_kv_heads, per = head_dim / 32;
-    const int chunk = (max_seq + splits - 1) / splits;
     const dim3 grid(splits, num_kv_heads, rows);
     float* part_o = static_cast<float*>(workspace);
     float* part_ml = part_o + static_cast<size_t>(rows) * num_heads * splits * head_dim;
     unsigned* done = reinterpret_cast<unsigned*>(part_ml + static_cast<size_t>(rows) * num_heads * splits * 2);
     switch (mul) {
-        case 1: return attn_per<1>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, chunk, ldq);
-        case 2: return attn_per<2>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, chunk, ldq);
-        case 4: return attn_per<4>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, chunk, ldq);
-        case 8: return attn_per<8>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, chunk, ldq);
+        case 1: return attn_per<1>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, ldq);
+        case 2: return attn_per<2>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, ldq);
+        case 4: return attn_per<4>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, ldq);
+        case 8: return attn_per<8>(per, grid, s, q, kcache, vcache, pos, part_o, part_ml, done, out, num_heads, num_kv_heads, max_seq, ldq);
         default: return cudaErrorInvalidValue;
     }
 }

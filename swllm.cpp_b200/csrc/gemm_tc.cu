@@ -63,6 +63,7 @@ constexpr int WARP_MMA = 4, WARP_X = 5, WARP_W = 6, WARP_DQ0 = 8;
 __host__ __device__ constexpr int dq_index(int w) { return w >= WARP_DQ0 && w < WARP_DQ0 + NDQ ? w - WARP_DQ0 : -1; }
 __host__ __device__ constexpr bool is_epilogue(int w) { return w < 4; }
 constexpr uint32_t FULL = 0xffffffffu;
+constexpr int TC_MAX_SPLIT = 8;  // split-K parts per output tile at most
 
 // Per-format constants of the W stages.
 struct TcFmt {
@@ -515,6 +516,15 @@ struct Params {
     const int* offsets;
     int n_experts;
     int rows_total;
+    // split-K (dense only): each output tile is computed as ksplit work units
+    // of gps W stages each; unit u = tile * ksplit + split.  With ksplit > 1
+    // every unit writes its partial tile to part[split][M][N], and the unit
+    // that finishes a tile last (count in tcount[tile], zeroed by the
+    // activation conversion, reset by that unit) sums the partials in split
+    // order into Y.
+    int ksplit, gps;
+    float* part;
+    unsigned* tcount;
 };
 
 // One output tile: weights, token rows m0 .. m_end-1 (the tile covers m0 .. m0+BN-1),
@@ -550,6 +560,19 @@ __device__ __forceinline__ TileRef tile_ref(const Params& p, const int* tpre, in
         r.m_end = b;
         r.W = p.wptrs[lo];
     }
+    return r;
+}
+
+// Work unit -> (tile, W stage range [g0, g1)).
+struct UnitRef {
+    int tile, split, g0, g1;
+};
+__device__ __forceinline__ UnitRef unit_ref(const Params& p, int u) {
+    UnitRef r;
+    r.tile = u / p.ksplit;
+    r.split = u - r.tile * p.ksplit;
+    r.g0 = r.split * p.gps;
+    r.g1 = min(p.ngroups, r.g0 + p.gps);
     return r;
 }
 
@@ -634,7 +657,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int ntiles = G ? tpre[p.n_experts] : p.n_mtiles * p.n_ntiles;
+    const int ntiles = G ? tpre[p.n_experts] : p.n_mtiles * p.n_ntiles * p.ksplit;  // work units
     pdl_wait_primary();  // X (fp16) is written by the conversion kernel before this one
 
     if (warp == WARP_X) {
@@ -645,9 +668,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         int it = 0;  // loads issued
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
             if (__shfl_sync(FULL, *abort_flag, 0)) break;
-            const TileRef tr = tile_ref<G, BN>(p, tpre, tile);
+            const UnitRef ur = unit_ref(p, tile);
+            const TileRef tr = tile_ref<G, BN>(p, tpre, ur.tile);
+            const int ks1 = min(p.ksteps, ur.g1 * (KG / BK));
             bool ok = true;
-            for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+            for (int ks = ur.g0 * (KG / BK); ks < ks1; ++ks, ++it) {
                 const bool got = it < S_ || mbar_wait_bounded(&empty[s], ph ^ 1u, DEV_TIMEOUT_EMPTY);
                 if (!__all_sync(FULL, got)) {
                     *abort_flag = 1;
@@ -690,8 +715,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             tc_fence_after();
             const uint32_t dt = tmem_base + static_cast<uint32_t>(tb * BN);
+            const UnitRef ur = unit_ref(p, tile);
+            const int ks0 = ur.g0 * (KG / BK), ks1 = min(p.ksteps, ur.g1 * (KG / BK));
             bool ok = true;
-            for (int ks = 0; ks < p.ksteps; ++ks) {
+            for (int ks = ks0; ks < ks1; ++ks) {
                 const bool got = mbar_wait_bounded(&full_a[s], ph, DEV_TIMEOUT_FULL) &&
                                  mbar_wait_bounded(&full_b[s], ph, DEV_TIMEOUT_FULL);
                 if (!__all_sync(FULL, got)) {
@@ -705,7 +732,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (elect_one()) {
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)  // 32 bytes of K per instruction
-                        mma_f16(dt, da + 2 * k, db + 2 * k, IDESC, (ks | k) ? 1u : 0u);
+                        mma_f16(dt, da + 2 * k, db + 2 * k, IDESC, (ks > ks0 || k) ? 1u : 0u);
                     mma_commit(&empty[s]);
                 }
                 __syncwarp();
@@ -728,14 +755,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         int jt = 0;  // W stages issued
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
             if (__shfl_sync(FULL, *abort_flag, 0)) break;
-            const TileRef tr = tile_ref<G, BN>(p, tpre, tile);
+            const UnitRef ur = unit_ref(p, tile);
+            const TileRef tr = tile_ref<G, BN>(p, tpre, ur.tile);
             const int row0 = tr.nt * BM;
             const uint8_t* w_hi = G ? reinterpret_cast<const uint8_t*>(
                                           (reinterpret_cast<uintptr_t>(tr.W) + static_cast<size_t>(p.N) * p.row_bytes +
                                            15) & ~uintptr_t(15))
                                     : p.w_hi;
             bool ok = true;
-            for (int g = 0; g < p.ngroups; ++g, ++jt) {
+            for (int g = ur.g0; g < ur.g1; ++g, ++jt) {
                 const bool got = jt < SW || mbar_wait_bounded(&wempty[js], jph ^ 1u, DEV_TIMEOUT_EMPTY);
                 if (!__all_sync(FULL, got)) {
                     *abort_flag = 1;
@@ -798,7 +826,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t jph = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
             if (__shfl_sync(FULL, *abort_flag, 0)) break;
-            const TileRef tr = tile_ref<G, BN>(p, tpre, tile);
+            const UnitRef ur = unit_ref(p, tile);
+            const TileRef tr = tile_ref<G, BN>(p, tpre, ur.tile);
             const uintptr_t wbase = reinterpret_cast<uintptr_t>(tr.W);
             const int row0 = tr.nt * BM;
             const bool ragged = row0 + BM > p.N;  // last row tile of a ragged N
@@ -811,7 +840,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 rowg[pp] = wbase + static_cast<uintptr_t>(valid[pp] ? row0 + r : 0) * p.row_bytes;
             }
             bool ok = true;
-            for (int g = 0; g < p.ngroups && ok; ++g) {
+            for (int g = ur.g0; g < ur.g1 && ok; ++g) {
                 const bool gotw = mbar_wait_bounded(&wfull[js], jph, DEV_TIMEOUT_FULL);
                 if (!__all_sync(FULL, gotw)) {
                     *abort_flag = 1;
@@ -873,9 +902,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int q = warp & 3;        // TMEM lane quadrant
         const int r = 32 * q + lane;   // W row within the tile
         int t_local = 0;
+        const bool split = !G && p.ksplit > 1;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t_local) {
             if (__shfl_sync(FULL, *abort_flag, 0)) break;
-            const TileRef tr = tile_ref<G, BN>(p, tpre, tile);
+            const UnitRef ur = unit_ref(p, tile);
+            const TileRef tr = tile_ref<G, BN>(p, tpre, ur.tile);
             const int nt = tr.nt;
             const int tb = t_local & 1;
             const uint32_t tph = (t_local >> 1) & 1;
@@ -887,6 +918,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
             const int row = nt * BM + r;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(tb * BN);
+            float* dst = split ? p.part + static_cast<size_t>(ur.split) * p.M * p.N : p.Y;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 uint32_t v[16];
@@ -897,13 +929,52 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int j = 0; j < 16; ++j) {
                         const int tok = tr.m0 + c0 + j;
                         if (tok < tr.m_end)
-                            p.Y[static_cast<size_t>(tok) * p.N + row] = __uint_as_float(v[j]) * __ldg(&p.rowscale[tok]);
+                            dst[static_cast<size_t>(tok) * p.N + row] =
+                                split ? __uint_as_float(v[j]) : __uint_as_float(v[j]) * __ldg(&p.rowscale[tok]);
                     }
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[tb]);
+            if (split) {
+                // This warp's 32 rows of the tile: the warp that writes its
+                // partial last sums all of them, in split order, into Y.  Each
+                // warp counts for itself, so no warp ever waits on another.
+                __threadfence();
+                __syncwarp();
+                unsigned last = 0;
+                if (lane == 0) {
+                    unsigned* cnt = p.tcount + static_cast<size_t>(ur.tile) * 4 + q;
+                    last = atomicAdd(cnt, 1u) == static_cast<unsigned>(p.ksplit - 1);
+                    if (last) *cnt = 0u;  // ready for the next call
+                }
+                if (__shfl_sync(FULL, last, 0)) {
+                    __threadfence();
+                    const int tend = min(tr.m_end, tr.m0 + BN);
+                    if (row < p.N) {
+                        for (int t0 = tr.m0; t0 < tend; t0 += 4) {
+                            float v[4][TC_MAX_SPLIT];
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                                for (int sp = 0; sp < TC_MAX_SPLIT; ++sp)
+                                    v[i][sp] = (t0 + i < tend && sp < p.ksplit)
+                                                   ? __ldcg(&p.part[(static_cast<size_t>(sp) * p.M + t0 + i) * p.N + row])
+                                                   : 0.f;
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                if (t0 + i >= tend) break;
+                                float acc = 0.f;
+#pragma unroll
+                                for (int sp = 0; sp < TC_MAX_SPLIT; ++sp)
+                                    if (sp < p.ksplit) acc += v[i][sp];
+                                p.Y[static_cast<size_t>(t0 + i) * p.N + row] = acc * __ldg(&p.rowscale[t0 + i]);
+                            }
+                        }
+                    }
+                }
+            }
         }
     }
 
@@ -929,8 +1000,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 // runs of four consecutive elements (float4 when aligned).
 template <bool F2, bool VEC>
 __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__ X, __half* __restrict__ Xh,
-                                                       float* __restrict__ rowscale, int M, int K) {
+                                                       float* __restrict__ rowscale, int M, int K,
+                                                       unsigned* __restrict__ tcount, int ncount) {
     __shared__ float red[8];
+    // split-K tile counters of the GEMM that follows start at zero
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncount; i += gridDim.x * blockDim.x) tcount[i] = 0u;
     for (int row = blockIdx.x; row < M; row += gridDim.x) {
         const float* xr = X + static_cast<int64_t>(row) * K;
         float mx = 0.f;
@@ -1023,9 +1097,38 @@ struct ExpertSet {
 };
 
 // M is the number of X rows (grouped: all experts' rows together).
+// Split-K plan of a dense call and its scratch (part: ksplit x M x N floats,
+// tcount: 4 counters per output tile).
+struct SplitK {
+    int ksplit = 1, gps = 0;
+    float* part = nullptr;
+    unsigned* tcount = nullptr;
+};
+
+static int token_tile(int M) { return M <= 64 ? 64 : M <= 128 ? 128 : 256; }
+
+// Output tiles fewer than half the SMs: split K so that about one work unit
+// lands on every SM, each unit at least two W stages (512 K), at most
+// TC_MAX_SPLIT parts.
+static SplitK plan_split(int M, int N, int K, int num_sms) {
+    SplitK sk;
+    const int tiles = ((M + token_tile(M) - 1) / token_tile(M)) * ((N + tc::BM - 1) / tc::BM);
+    const int ngroups = (K + tc::KG - 1) / tc::KG;
+    sk.gps = ngroups;
+    if (2 * tiles > num_sms) return sk;
+    int S = std::min({tc::TC_MAX_SPLIT, num_sms / tiles, ngroups / 2});
+    if (S <= 1) return sk;
+    sk.gps = (ngroups + S - 1) / S;
+    sk.ksplit = (ngroups + sk.gps - 1) / sk.gps;
+    return sk;
+}
+static size_t split_tiles(int M, int N) {
+    return static_cast<size_t>((M + token_tile(M) - 1) / token_tile(M)) * ((N + tc::BM - 1) / tc::BM);
+}
+
 template <int T, int BN, bool A4, bool G>
 static cudaError_t launch_tc(const void* W, const __half* Xh, const float* rowscale, float* Y, int M, int N, int K,
-                             int num_sms, cudaStream_t stream, const ExpertSet* ex) {
+                             int num_sms, cudaStream_t stream, const ExpertSet* ex, const SplitK& sk = SplitK{}) {
     constexpr tc::TcFmt F = tc::tc_fmt(T);
     tc::Params p{};
     p.W = static_cast<const uint8_t*>(W);
@@ -1045,7 +1148,11 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, const float* rowsc
     p.w_lo = reinterpret_cast<const uint8_t*>(w & ~uintptr_t(15));
     p.w_hi = reinterpret_cast<const uint8_t*>((w + wbytes + 15) & ~uintptr_t(15));
     size_t extra = 0;
-    int max_tiles = p.n_mtiles * p.n_ntiles;
+    p.ksplit = G ? 1 : sk.ksplit;
+    p.gps = G || sk.ksplit == 1 ? p.ngroups : sk.gps;
+    p.part = sk.part;
+    p.tcount = sk.tcount;
+    int max_tiles = p.n_mtiles * p.n_ntiles * p.ksplit;
     if constexpr (G) {
         p.wptrs = ex->wptrs;
         p.offsets = ex->offsets;
@@ -1138,10 +1245,10 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, const float* rowsc
 
 template <int T, bool A4>
 static cudaError_t launch_tc_bn(const void* W, const __half* Xh, const float* rs, float* Y, int M, int N, int K,
-                                int num_sms, cudaStream_t s) {
-    if (M <= 64) return launch_tc<T, 64, A4, false>(W, Xh, rs, Y, M, N, K, num_sms, s, nullptr);
-    if (M <= 128) return launch_tc<T, 128, A4, false>(W, Xh, rs, Y, M, N, K, num_sms, s, nullptr);
-    return launch_tc<T, 256, A4, false>(W, Xh, rs, Y, M, N, K, num_sms, s, nullptr);
+                                int num_sms, cudaStream_t s, const SplitK& sk) {
+    if (M <= 64) return launch_tc<T, 64, A4, false>(W, Xh, rs, Y, M, N, K, num_sms, s, nullptr, sk);
+    if (M <= 128) return launch_tc<T, 128, A4, false>(W, Xh, rs, Y, M, N, K, num_sms, s, nullptr, sk);
+    return launch_tc<T, 256, A4, false>(W, Xh, rs, Y, M, N, K, num_sms, s, nullptr, sk);
 }
 
 // Grouped: the token tile follows the mean rows per expert.
@@ -1156,44 +1263,63 @@ static cudaError_t launch_tc_grouped(const ExpertSet& ex, const __half* Xh, cons
 
 template <int T>
 static cudaError_t launch_tc_fmt(const void* W, const __half* Xh, const float* rs, float* Y, int M, int N, int K,
-                                 int num_sms, cudaStream_t s) {
+                                 int num_sms, cudaStream_t s, const SplitK& sk) {
     // Q4_K, Q5_K and Q2_K keep every field of a block 4-byte aligned when W is.
     if constexpr (T == Q4_K || T == Q5_K || T == Q2_K) {
         if (reinterpret_cast<uintptr_t>(W) % 4 == 0)
-            return launch_tc_bn<T, true>(W, Xh, rs, Y, M, N, K, num_sms, s);
+            return launch_tc_bn<T, true>(W, Xh, rs, Y, M, N, K, num_sms, s, sk);
     }
-    return launch_tc_bn<T, false>(W, Xh, rs, Y, M, N, K, num_sms, s);
+    return launch_tc_bn<T, false>(W, Xh, rs, Y, M, N, K, num_sms, s, sk);
 }
 
 template <bool F2>
 static cudaError_t launch_x_to_f16(const float* X, __half* Xh, float* rowscale, int M, int K, int num_sms,
-                                   cudaStream_t s) {
+                                   cudaStream_t s, unsigned* tcount = nullptr, int ncount = 0) {
     const int grid = std::max(1, std::min(M, num_sms * 8));
     if ((reinterpret_cast<uintptr_t>(X) & 15u) == 0)
-        x_to_f16_kernel<F2, true><<<grid, 256, 0, s>>>(X, Xh, rowscale, M, K);
+        x_to_f16_kernel<F2, true><<<grid, 256, 0, s>>>(X, Xh, rowscale, M, K, tcount, ncount);
     else
-        x_to_f16_kernel<F2, false><<<grid, 256, 0, s>>>(X, Xh, rowscale, M, K);
+        x_to_f16_kernel<F2, false><<<grid, 256, 0, s>>>(X, Xh, rowscale, M, K, tcount, ncount);
     return cudaGetLastError();
 }
 
-// Scratch of one call: the fp16 copy of X (M*K halves) and, after it, M row scales.
+static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
+
+// Scratch of one call: the fp16 copy of X (M*K halves), M row scales, then
+// for a split-K plan the tile counters and the partial products.
 static size_t scratch_bytes(int64_t M, int64_t K) { return static_cast<size_t>(M * K) * 2 + static_cast<size_t>(M) * 4; }
+static size_t scratch_bytes(int64_t M, int64_t N, int64_t K, const SplitK& sk) {
+    size_t b = align16(scratch_bytes(M, K));
+    if (sk.ksplit > 1)
+        b += align16(split_tiles(static_cast<int>(M), static_cast<int>(N)) * 4 * sizeof(unsigned)) +
+             static_cast<size_t>(sk.ksplit) * M * N * sizeof(float);
+    return b;
+}
+// Points sk.tcount and sk.part into the scratch at `base` laid out as above.
+static void place_split(SplitK& sk, void* base, int64_t M, int64_t N, int64_t K) {
+    if (sk.ksplit <= 1) return;
+    uint8_t* b = static_cast<uint8_t*>(base) + align16(scratch_bytes(M, K));
+    sk.tcount = reinterpret_cast<unsigned*>(b);
+    sk.part = reinterpret_cast<float*>(b + align16(split_tiles(static_cast<int>(M), static_cast<int>(N)) * 4 *
+                                                   sizeof(unsigned)));
+}
 
 // X -> fp16 into Xh (M*K halves, K order of the format) with row scales rs
-// (M floats), then the GEMM.
+// (M floats) and the split-K counters zeroed, then the GEMM.
 static cudaError_t gemm_tc_run(int type, const void* W, const float* X, __half* Xh, float* rs, float* Y, int M,
-                               int N, int K, int num_sms, cudaStream_t s) {
-    cudaError_t e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, M, K, num_sms, s)
-                                        : launch_x_to_f16<false>(X, Xh, rs, M, K, num_sms, s);
+                               int N, int K, int num_sms, cudaStream_t s, const SplitK& sk) {
+    const int ncount = sk.ksplit > 1 ? static_cast<int>(split_tiles(M, N) * 4) : 0;
+    cudaError_t e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, M, K, num_sms, s, sk.tcount, ncount)
+                                        : launch_x_to_f16<false>(X, Xh, rs, M, K, num_sms, s, sk.tcount, ncount);
     if (e != cudaSuccess) return e;
     switch (type) {
-        case Q4_0: return launch_tc_fmt<Q4_0>(W, Xh, rs, Y, M, N, K, num_sms, s);
-        case Q8_0: return launch_tc_fmt<Q8_0>(W, Xh, rs, Y, M, N, K, num_sms, s);
-        case Q2_K: return launch_tc_fmt<Q2_K>(W, Xh, rs, Y, M, N, K, num_sms, s);
-        case Q3_K: return launch_tc_fmt<Q3_K>(W, Xh, rs, Y, M, N, K, num_sms, s);
-        case Q4_K: return launch_tc_fmt<Q4_K>(W, Xh, rs, Y, M, N, K, num_sms, s);
-        case Q5_K: return launch_tc_fmt<Q5_K>(W, Xh, rs, Y, M, N, K, num_sms, s);
-        case Q6_K: return launch_tc_fmt<Q6_K>(W, Xh, rs, Y, M, N, K, num_sms, s);
+        case Q4_0: return launch_tc_fmt<Q4_0>(W, Xh, rs, Y, M, N, K, num_sms, s, sk);
+        case Q8_0: return launch_tc_fmt<Q8_0>(W, Xh, rs, Y, M, N, K, num_sms, s, sk);
+        case Q2_K: return launch_tc_fmt<Q2_K>(W, Xh, rs, Y, M, N, K, num_sms, s, sk);
+        case Q3_K: return launch_tc_fmt<Q3_K>(W, Xh, rs, Y, M, N, K, num_sms, s, sk);
+        case Q4_K: return launch_tc_fmt<Q4_K>(W, Xh, rs, Y, M, N, K, num_sms, s, sk);
+        case Q5_K: return launch_tc_fmt<Q5_K>(W, Xh, rs, Y, M, N, K, num_sms, s, sk);
+        case Q6_K: return launch_tc_fmt<Q6_K>(W, Xh, rs, Y, M, N, K, num_sms, s, sk);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -1232,10 +1358,12 @@ cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, in
     cudaMemPool_t pool = nullptr;
     cudaError_t e = scratch_pool(&pool);
     if (e != cudaSuccess) return e;
+    SplitK sk = plan_split(M, N, K, num_sms);
     __half* Xh = nullptr;
-    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), scratch_bytes(M, K), pool, s);
+    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), scratch_bytes(M, N, K, sk), pool, s);
     if (e != cudaSuccess) return e;
-    e = gemm_tc_run(type, W, X, Xh, reinterpret_cast<float*>(Xh + n), Y, M, N, K, num_sms, s);
+    place_split(sk, Xh, M, N, K);
+    e = gemm_tc_run(type, W, X, Xh, reinterpret_cast<float*>(Xh + n), Y, M, N, K, num_sms, s, sk);
     cudaError_t e2 = cudaFreeAsync(Xh, s);
     return e != cudaSuccess ? e : e2;
 }
@@ -1288,26 +1416,37 @@ cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int
 static __device__ __align__(256) uint16_t g_noalloc_x16[SWQ_GEMM_NOALLOC_MAX_X_ELEMS];
 // one scale per X row; K >= 32, so M <= SWQ_GEMM_NOALLOC_MAX_X_ELEMS / 32
 static __device__ __align__(256) float g_noalloc_rowscale[SWQ_GEMM_NOALLOC_MAX_X_ELEMS / 32];
+// split-K partial products and tile counters (a call whose plan does not fit
+// runs unsplit)
+constexpr size_t NOALLOC_PART_ELEMS = size_t(1) << 22;
+constexpr size_t NOALLOC_TCOUNT = 4096;
+static __device__ __align__(256) float g_noalloc_part[NOALLOC_PART_ELEMS];
+static __device__ __align__(256) unsigned g_noalloc_tcount[NOALLOC_TCOUNT];
 
-static cudaError_t noalloc_scratch(__half** xh, float** rs) {
+struct NoallocArrays {
+    void* x16;
+    void* rowscale;
+    void* part;
+    void* tcount;
+};
+
+static cudaError_t noalloc_scratch(NoallocArrays* out) {
     static std::mutex mu;
-    static std::map<int, std::pair<void*, void*>> addr;  // device -> device addresses of the two arrays
+    static std::map<int, NoallocArrays> addr;  // device -> device addresses of the arrays
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lk(mu);
     auto it = addr.find(dev);
     if (it == addr.end()) {
-        void* p = nullptr;
-        void* q = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_x16);
-        if (e != cudaSuccess) return e;
-        e = cudaGetSymbolAddress(&q, g_noalloc_rowscale);
-        if (e != cudaSuccess) return e;
-        it = addr.emplace(dev, std::make_pair(p, q)).first;
+        NoallocArrays a{};
+        if ((e = cudaGetSymbolAddress(&a.x16, g_noalloc_x16)) != cudaSuccess) return e;
+        if ((e = cudaGetSymbolAddress(&a.rowscale, g_noalloc_rowscale)) != cudaSuccess) return e;
+        if ((e = cudaGetSymbolAddress(&a.part, g_noalloc_part)) != cudaSuccess) return e;
+        if ((e = cudaGetSymbolAddress(&a.tcount, g_noalloc_tcount)) != cudaSuccess) return e;
+        it = addr.emplace(dev, a).first;
     }
-    *xh = static_cast<__half*>(it->second.first);
-    *rs = static_cast<float*>(it->second.second);
+    *out = it->second;
     return cudaSuccess;
 }
 
@@ -1315,11 +1454,21 @@ cudaError_t gemm_tc_launch_noalloc(int type, const void* W, const float* X, floa
                                    int refcpu, int num_sms, cudaStream_t s) {
     if (!gemm_tc_supported(type, W, M, N, K, refcpu)) return cudaErrorNotSupported;
     if (static_cast<int64_t>(M) * K > SWQ_GEMM_NOALLOC_MAX_X_ELEMS) return cudaErrorInvalidValue;
-    __half* Xh = nullptr;
-    float* rs = nullptr;
-    cudaError_t e = noalloc_scratch(&Xh, &rs);
+    NoallocArrays a{};
+    cudaError_t e = noalloc_scratch(&a);
     if (e != cudaSuccess) return e;
-    return gemm_tc_run(type, W, X, Xh, rs, Y, M, N, K, num_sms, s);
+    SplitK sk = plan_split(M, N, K, num_sms);
+    if (sk.ksplit > 1 && (static_cast<size_t>(sk.ksplit) * M * N > NOALLOC_PART_ELEMS ||
+                          split_tiles(M, N) * 4 > NOALLOC_TCOUNT)) {
+        sk = SplitK{};
+        sk.gps = (K + tc::KG - 1) / tc::KG;
+    }
+    if (sk.ksplit > 1) {
+        sk.part = static_cast<float*>(a.part);
+        sk.tcount = static_cast<unsigned*>(a.tcount);
+    }
+    return gemm_tc_run(type, W, X, static_cast<__half*>(a.x16), static_cast<float*>(a.rowscale), Y, M, N, K,
+                       num_sms, s, sk);
 }
 
 SWQ_DEFINE_STATUS_FETCH(gemm_tc)

@@ -218,6 +218,12 @@ __device__ __forceinline__ void row_store(float (&acc)[MT], int lane, float* Y, 
     }
 }
 
+// First W row of the tensor-map box of the row group starting at rg: rg, or
+// r_end - RG when the group is short and the CTA has RG rows before r_end.
+__device__ __forceinline__ int tmap_row0(int rg, int r_begin, int r_end, int RG) {
+    return (rg + RG > r_end && r_end - RG >= r_begin) ? r_end - RG : rg;
+}
+
 template <int T, int MT>
 __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
     gemv_kernel(const GemvParams p, const __grid_constant__ CUtensorMap tmap) {
@@ -276,9 +282,12 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
                 uint8_t* dst = ring + static_cast<size_t>(s) * p.stage_bytes;
                 if (p.mode == MODE_TMAP) {
                     if (lane == 0) {
-                        // the box is always full: RG rows x KC blocks (rows past N read zeros)
+                        // The box is always full: RG rows x KC blocks (rows past N
+                        // read zeros).  A last group shorter than RG starts lower,
+                        // on rows of this CTA's previous group (just read, so
+                        // L2 hits) rather than past r_end on the next CTA's rows.
                         mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(p.KC * BB * RG));
-                        tma_load_2d(dst, &tmap, kb0 * BB / 8, rg, &full[s], pol);
+                        tma_load_2d(dst, &tmap, kb0 * BB / 8, tmap_row0(rg, r_begin, r_end, RG), &full[s], pol);
                     }
                 } else if (p.mode == MODE_BULK_ROWS) {
                     if (lane == 0) {
@@ -452,7 +461,8 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
             const int kb0 = ch * p.KC;
             const int kc = min(p.KC, p.nb - kb0);
             const int nu = kc * UPB;
-            const uint8_t* stage = ring + static_cast<size_t>(s) * p.stage_bytes;
+            const int shift = p.mode == MODE_TMAP ? rg - tmap_row0(rg, r_begin, r_end, RG) : 0;
+            const uint8_t* stage = ring + static_cast<size_t>(s) * p.stage_bytes + static_cast<size_t>(shift) * p.row_stride;
             const uint8_t* rowA = stage + warp * p.row_stride;
             const uint8_t* rowB = stage + (warp + NCW) * p.row_stride;
             if (hasB) {
@@ -526,7 +536,8 @@ static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
     p.x_vec = (reinterpret_cast<uintptr_t>(L.X) & 15u) == 0 ? 1 : 0;  // K % 32 keeps rows aligned
     p.xstride = XLay<T>::row_bytes(L.K);
 
-    const int grid = std::max(1, std::min(L.num_sms, L.N));
+    const int per_sm = L.ctas_per_sm > 0 ? L.ctas_per_sm : 1;
+    const int grid = std::max(1, std::min(L.num_sms * per_sm, L.N));
     const int rows_cta = (L.N + grid - 1) / grid;
 
     // Shared memory: barriers | activations | ring.
@@ -539,13 +550,15 @@ static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
     const uint32_t smem_cap = static_cast<uint32_t>(L.smem_per_block_optin);
     // Two CTAs per SM: this kernel's and the next one's.
     const uint32_t half_sm = static_cast<uint32_t>(L.smem_per_sm) / 2 - 1024;
-    const uint32_t budget = (off + 32 * 1024 <= half_sm) ? half_sm : smem_cap;
+    uint32_t budget = (off + 32 * 1024 <= half_sm) ? half_sm : smem_cap;
+    if (per_sm > 1) budget = std::min(smem_cap, static_cast<uint32_t>(L.smem_per_sm) / per_sm - 1024);
+    if (L.smem_kb > 0) budget = std::min(smem_cap, static_cast<uint32_t>(L.smem_kb) * 1024u);
     if (off >= budget) return cudaErrorInvalidConfiguration;
     const uint32_t ring_cap = budget - off;
 
     const bool aligned = (reinterpret_cast<uintptr_t>(L.W) & 15u) == 0 && (p.row_bytes % 16) == 0;
     const int al_blocks = 16 / std::gcd(F::BB, 16);
-    constexpr uint32_t kStageCap = 96 * 1024;
+    const uint32_t kStageCap = L.stage_kb > 0 ? static_cast<uint32_t>(L.stage_kb) * 1024u : 96u * 1024u;
     bool chosen = false;
     CUtensorMap tmap;
     std::memset(&tmap, 0, sizeof(tmap));

@@ -27,6 +27,9 @@ struct GemvLaunch {
     int num_sms;
     int smem_per_block_optin;
     int smem_per_sm;
+    int smem_kb;   // CTA shared-memory budget in KB (0: automatic)
+    int stage_kb;  // largest weight stage in KB (0: 96)
+    int ctas_per_sm;  // 0: automatic
 };
 
 // Fused dequant + GEMV for M <= 8 activation rows.

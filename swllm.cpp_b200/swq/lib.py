@@ -25,6 +25,9 @@ OPT_EARLY_WEIGHT_PREFETCH = 2
 OPT_GEMV_MAX_M = 3
 OPT_TENSOR_CORE_GEMM = 4
 OPT_TENSOR_CORE_MIN_M = 5
+OPT_GEMV_SMEM_KB = 6
+OPT_GEMV_STAGE_KB = 7
+OPT_GEMV_CTAS_PER_SM = 8
 
 GEMM_NOALLOC_MAX_X_ELEMS = 8388608  # SWQ_GEMM_NOALLOC_MAX_X_ELEMS
 

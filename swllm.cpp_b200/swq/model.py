@@ -15,6 +15,17 @@ Weights are GGUF blocks in device memory: either given (host arrays, for the
 tests) or synthetic -- seeded random blocks with the benchmark's value
 distributions, generated on the device -- in the Q4_K_M mix (Q6_K for attn_v,
 ffn_down and the output matrix, Q4_K elsewhere).
+
+Tensor parallelism (one process per GPU, `group` of G ranks): rank r keeps
+query heads [r H/G, (r+1) H/G) and kv heads [r Hkv/G, ...) -- the rows of
+wq, wk, wv -- the same rows of gate and up, columns [r ffn/G, ...) of
+w_down, columns [r H hd/G, ...) of wo, and rows [r V/G, ...) of the LM head.
+Attention is local to the rank's heads; the o and down projections give
+partial sums that one all-reduce each completes; the rank's slice of the
+logits is all-gathered before the argmax.  Every collective is issued on the
+decode stream, so the step with its collectives is captured in one graph.
+The reference runs one process (no tensor parallelism); a G-rank decoder is
+checked against the same model on one rank.
 """
 from __future__ import annotations
 
@@ -45,6 +56,12 @@ class LlamaConfig:
     # GGML types of the Q4_K_M mix
     types: dict = field(default_factory=lambda: {"wq": Q4_K, "wk": Q4_K, "wv": Q6_K, "wo": Q4_K,
                                                  "w_gate": Q4_K, "w_up": Q4_K, "w_down": Q6_K, "output": Q6_K})
+
+    @classmethod
+    def llama3_70b(cls, **kw) -> "LlamaConfig":
+        """Llama-3-70B shape: 80 layers, hidden 8192, 64 query / 8 kv heads of
+        128, FFN 28672, vocab 128256."""
+        return cls(n_layers=80, dim=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn=28672, vocab=128256, **kw)
 
     @property
     def q_dim(self) -> int:
@@ -91,27 +108,77 @@ def synthetic_blocks(type_id: int, N: int, K: int, generator, device):
     return b.reshape(-1)
 
 
+def _shard(host, type_id: int, N: int, K: int, rows: tuple[int, int] | None, cols: tuple[int, int] | None):
+    """Rows [r0, r1) or columns [k0, k1) (whole blocks) of an N x K block matrix."""
+    qk, bb = LAYOUT[type_id][:2]
+    b = np.asarray(host).reshape(N, (K // qk) * bb)
+    if rows is not None:
+        b = b[rows[0]:rows[1]]
+    if cols is not None:
+        b = b[:, (cols[0] // qk) * bb:(cols[1] // qk) * bb]
+    return np.ascontiguousarray(b)
+
+
 class LlamaDecoder:
     def __init__(self, cfg: LlamaConfig, rows: int = 1, device="cuda", seed: int = 0, weights: dict | None = None,
-                 max_steps: int = 4096):
+                 max_steps: int = 4096, group=None, weights_from: "LlamaDecoder | None" = None):
         """weights: None for synthetic weights, else host arrays: 'token_embd'
         [vocab, dim] fp32, 'output_norm' [dim], 'output' blocks, and per layer
         'layers'[l] with 'attn_norm', 'ffn_norm' [dim] fp32 and the blocks of
-        wq wk wv wo w_gate w_up w_down."""
+        wq wk wv wo w_gate w_up w_down (whole matrices; each rank keeps its
+        shard).  group: torch.distributed group for tensor parallelism (None:
+        the default group when one is initialised with more than one rank).
+        weights_from: a decoder of the same config and group whose device
+        weights this one shares (another batch size of the same model)."""
         import torch
+        from .parallel import _world
         self.cfg, self.rows, self.device = cfg, rows, torch.device(device)
+        self.group = group
+        self.rank, self.world = _world(group)
+        G, r = self.world, self.rank
+        for what, n in (("query heads", cfg.n_heads), ("kv heads", cfg.n_kv_heads), ("ffn", cfg.ffn),
+                        ("vocab", cfg.vocab)):
+            if n % G:
+                raise ValueError(f"{what}={n} does not split over {G} ranks")
+        self.nh, self.nkv = cfg.n_heads // G, cfg.n_kv_heads // G
+        self.q_dim, self.kv_dim = self.nh * cfg.head_dim, self.nkv * cfg.head_dim
+        self.ffn, self.vocab = cfg.ffn // G, cfg.vocab // G
         dev = self.device
         t = cfg.types
         g = torch.Generator(device=dev)
-        g.manual_seed(seed)
+        g.manual_seed(seed + 1000003 * r)
         f32 = dict(dtype=torch.float32, device=dev)
+        # local (rows, K) of every matrix, and the slice of the whole matrix it is
+        row_part = {"wq": self.q_dim, "wk": self.kv_dim, "wv": self.kv_dim, "w_gate": self.ffn, "w_up": self.ffn,
+                    "output": self.vocab}
+        col_part = {"wo": self.q_dim, "w_down": self.ffn}
 
         def blocks(name, N, K, host):
+            if name in row_part:
+                n = row_part[name]
+                Nl, Kl, rs, cs = n, K, (r * n, (r + 1) * n), None
+            else:
+                k = col_part[name]
+                Nl, Kl, rs, cs = N, k, None, (r * k, (r + 1) * k)
             if host is not None:
-                return torch.from_numpy(np.ascontiguousarray(host).reshape(-1)).to(dev)
-            return synthetic_blocks(t[name], N, K, g, dev)
+                part = _shard(host, t[name], N, K, rs, cs) if G > 1 else np.ascontiguousarray(host)
+                return torch.from_numpy(part.reshape(-1)).to(dev)
+            return synthetic_blocks(t[name], Nl, Kl, g, dev)
 
         W = weights or {}
+        if weights_from is not None:
+            if weights_from.cfg != cfg or weights_from.world != G:
+                raise ValueError("weights_from must have the same config and group size")
+            for name in ("token_embd", "output_norm", "output", "fuse_gate_up", "fuse_qk", "layers", "freqs"):
+                setattr(self, name, getattr(weights_from, name))
+        else:
+            self._load_weights(cfg, W, weights, blocks, g, f32)
+        self._alloc_state(cfg, rows, max_steps, f32)
+
+    def _load_weights(self, cfg, W, weights, blocks, g, f32):
+        import torch
+        dev = self.device
+        t = cfg.types
         self.token_embd = (torch.from_numpy(np.asarray(W["token_embd"], np.float32)).to(dev) if weights
                            else torch.randn((cfg.vocab, cfg.dim), generator=g, **f32))
         self.output_norm = (torch.from_numpy(np.asarray(W["output_norm"], np.float32)).to(dev) if weights
@@ -134,27 +201,45 @@ class LlamaDecoder:
                 L["w_qk"] = torch.cat([L.pop("wq"), L.pop("wk")])
             self.layers.append(L)
         self.freqs = torch.from_numpy(rope_freqs(cfg)).to(dev)
+
+    def _alloc_state(self, cfg, rows, max_steps, f32):
+        import torch
+        dev, G = self.device, self.world
         B = rows
         self.x = torch.zeros((B, cfg.dim), **f32)
         self.xb = torch.zeros_like(self.x)
-        self.qk = torch.zeros((B, cfg.q_dim + cfg.kv_dim), **f32)  # q then k, per row
-        self.v = torch.zeros((B, cfg.kv_dim), **f32)
-        self.att = torch.zeros((B, cfg.q_dim), **f32)
-        self.gu = torch.zeros((B, 2 * cfg.ffn), **f32)
-        self.h = torch.zeros((B, cfg.ffn), **f32)
+        self.qk = torch.zeros((B, self.q_dim + self.kv_dim), **f32)  # q then k, per row
+        self.v = torch.zeros((B, self.kv_dim), **f32)
+        self.att = torch.zeros((B, self.q_dim), **f32)
+        self.gu = torch.zeros((B, 2 * self.ffn), **f32)
+        self.h = torch.zeros((B, self.ffn), **f32)
         self.logits = torch.zeros((B, cfg.vocab), **f32)
-        self.kcache = torch.zeros((cfg.n_layers, B, cfg.max_seq, cfg.kv_dim), **f32)
+        if G > 1:
+            self.logits_l = torch.zeros((B, self.vocab), **f32)       # this rank's slice
+            self.logits_g = torch.zeros((G, B, self.vocab), **f32)    # all slices, rank-major
+        self.kcache = torch.zeros((cfg.n_layers, B, cfg.max_seq, self.kv_dim), **f32)
         self.vcache = torch.zeros_like(self.kcache)
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.step_no = torch.zeros(1, dtype=torch.int32, device=dev)
         self.history = torch.zeros((max_steps, B), dtype=torch.int32, device=dev)
-        self.ws_bytes = attention_workspace_bytes(cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, B, cfg.max_seq)
+        self.ws_bytes = attention_workspace_bytes(self.nh, self.nkv, cfg.head_dim, B, cfg.max_seq)
         self.ws = torch.zeros(max(1, self.ws_bytes // 4), **f32)  # zero-filled, as the kernel expects
         self.max_steps = max_steps
         self.steps_issued = 0
         self.stream = torch.cuda.Stream(device=dev)
         self.graph = None
+        self.all_reduce = self._nccl_all_reduce
+
+    # ------------------------------------------------------------ collectives
+    def _nccl_all_reduce(self, t) -> None:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+
+    def _gather_logits(self) -> None:
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(self.logits_g, self.logits_l, group=self.group)
+        self.logits.view(self.rows, self.world, self.vocab).copy_(self.logits_g.transpose(0, 1))
 
     # ------------------------------------------------------------ one token
     def _gemm(self, type_id, W, X, Y, M, N, K, stream):
@@ -171,40 +256,50 @@ class LlamaDecoder:
         c, B, s = self.cfg, self.rows, self.stream
         t = c.types
         gemm = self._gemm  # noqa: F811
-        ld = c.q_dim + c.kv_dim
-        q, k = self.qk, self.qk[:, c.q_dim:]
+        qd, kvd, ffn = self.q_dim, self.kv_dim, self.ffn
+        tp = self.world > 1
+        ld = qd + kvd
+        q, k = self.qk, self.qk[:, qd:]
         embed(self.x, self.token_embd, self.tokens, c.dim, c.vocab, B, stream=s)
         rmsnorm(self.xb, self.x, self.layers[0]["attn_norm"], c.dim, c.eps, B, stream=s)
         for li, L in enumerate(self.layers):
             if self.fuse_qk:
                 gemm(t["wq"], L["w_qk"], self.xb, self.qk, B, ld, c.dim, stream=s)
             else:
-                gemm(t["wq"], L["wq"], self.xb, self.att, B, c.q_dim, c.dim, stream=s)
-                q[:, :c.q_dim].copy_(self.att)
-                gemm(t["wk"], L["wk"], self.xb, self.v, B, c.kv_dim, c.dim, stream=s)
+                gemm(t["wq"], L["wq"], self.xb, self.att, B, qd, c.dim, stream=s)
+                q[:, :qd].copy_(self.att)
+                gemm(t["wk"], L["wk"], self.xb, self.v, B, kvd, c.dim, stream=s)
                 k.copy_(self.v)
-            gemm(t["wv"], L["wv"], self.xb, self.v, B, c.kv_dim, c.dim, stream=s)
+            gemm(t["wv"], L["wv"], self.xb, self.v, B, kvd, c.dim, stream=s)
             kc, vc = self.kcache[li], self.vcache[li]
-            rope_kv(q, k, self.v, kc, vc, self.pos, self.freqs, c.q_dim, c.kv_dim, c.head_dim, c.head_dim,
+            rope_kv(q, k, self.v, kc, vc, self.pos, self.freqs, qd, kvd, c.head_dim, c.head_dim,
                     c.rope_neox, B, c.max_seq, ldq=ld, ldk=ld, stream=s)
-            attention_decode(self.att, q, kc, vc, self.pos, self.ws, self.ws_bytes, c.n_heads, c.n_kv_heads,
+            attention_decode(self.att, q, kc, vc, self.pos, self.ws, self.ws_bytes, self.nh, self.nkv,
                              c.head_dim, B, c.max_seq, ldq=ld, stream=s)
-            gemm(t["wo"], L["wo"], self.att, self.xb, B, c.dim, c.q_dim, stream=s)
+            gemm(t["wo"], L["wo"], self.att, self.xb, B, c.dim, qd, stream=s)
+            if tp:
+                self.all_reduce(self.xb)
             add_rmsnorm(self.xb, self.x, self.xb, L["ffn_norm"], c.dim, c.eps, B, stream=s)  # x += o; xb = norm(x)
             if self.fuse_gate_up:
-                gemm(t["w_gate"], L["w_gate_up"], self.xb, self.gu, B, 2 * c.ffn, c.dim, stream=s)
+                gemm(t["w_gate"], L["w_gate_up"], self.xb, self.gu, B, 2 * ffn, c.dim, stream=s)
             else:
-                gemm(t["w_gate"], L["w_gate"], self.xb, self.h, B, c.ffn, c.dim, stream=s)
-                self.gu[:, :c.ffn].copy_(self.h)
-                gemm(t["w_up"], L["w_up"], self.xb, self.h, B, c.ffn, c.dim, stream=s)
-                self.gu[:, c.ffn:].copy_(self.h)
-            silu_mul(self.h, self.gu, self.gu[:, c.ffn:], c.ffn, B, 2 * c.ffn, stream=s)
-            gemm(t["w_down"], L["w_down"], self.h, self.xb, B, c.dim, c.ffn, stream=s)
+                gemm(t["w_gate"], L["w_gate"], self.xb, self.h, B, ffn, c.dim, stream=s)
+                self.gu[:, :ffn].copy_(self.h)
+                gemm(t["w_up"], L["w_up"], self.xb, self.h, B, ffn, c.dim, stream=s)
+                self.gu[:, ffn:].copy_(self.h)
+            silu_mul(self.h, self.gu, self.gu[:, ffn:], ffn, B, 2 * ffn, stream=s)
+            gemm(t["w_down"], L["w_down"], self.h, self.xb, B, c.dim, ffn, stream=s)
+            if tp:
+                self.all_reduce(self.xb)
             if li + 1 < len(self.layers):  # x += down; xb = next layer's attention norm of x
                 add_rmsnorm(self.xb, self.x, self.xb, self.layers[li + 1]["attn_norm"], c.dim, c.eps, B, stream=s)
             else:  # x += down; x = output norm of x
                 add_rmsnorm(self.x, self.x, self.xb, self.output_norm, c.dim, c.eps, B, stream=s)
-        gemm(t["output"], self.output, self.x, self.logits, B, c.vocab, c.dim, stream=s)
+        if tp:
+            gemm(t["output"], self.output, self.x, self.logits_l, B, self.vocab, c.dim, stream=s)
+            self._gather_logits()
+        else:
+            gemm(t["output"], self.output, self.x, self.logits, B, c.vocab, c.dim, stream=s)
         if greedy:
             argmax(self.logits, c.vocab, B, self.tokens, self.history, self.step_no, stream=s)
             decode_advance(self.pos, self.step_no, stream=s)

@@ -135,6 +135,35 @@ def test_activations_beyond_fp16_range(cuda, oracle_mod, fmt):
         assert rel_l2(got[r], want[r]) <= REL_L2_TOL, (r, rel_l2(got[r], want[r]))
 
 
+@pytest.mark.parametrize("fmt,N,K,M", [("Q4_K", 4096, 4096, 16), ("Q6_K", 4096, 14336, 16), ("Q6_K", 1024, 4096, 9),
+                                        ("Q4_K", 5120, 4096, 32), ("Q5_K", 640, 1280, 20), ("Q4_0", 300, 2336, 12),
+                                        ("Q8_0", 256, 544, 64), ("Q2_K", 4096, 8192, 64), ("Q3_K", 1024, 3072, 100)])
+def test_split_k(cuda, oracle_mod, fmt, N, K, M):
+    """Output tiles fewer than half the SMs: K is split into parts whose
+    partial tiles the last part sums (in split order) -- decode-batch shapes,
+    an odd number of W stages, a Q4_0 K ending half way through a step, two
+    token tiles."""
+    t = synth.IDS[fmt]
+    blocks = synth.random_blocks(t, N, K, seed=2500 + N + M)
+    X = synth.random_activations(M, K, seed=2501)
+    got = _gemm(cuda, t, blocks, X, N, K)
+    assert np.all(np.isfinite(got))
+    assert rel_l2(got, oracle_mod.gemm(t, blocks, X, M, N, K)) <= REL_L2_TOL
+
+
+def test_split_k_deterministic(cuda):
+    torch = cuda
+    t = synth.Q6_K
+    N, K, M = 4096, 14336, 16
+    d_w = torch.from_numpy(synth.random_blocks(t, N, K, seed=2600).reshape(-1)).cuda()
+    d_x = torch.from_numpy(synth.random_activations(M, K, seed=2601)).cuda()
+    ys = [torch.empty((M, N), dtype=torch.float32, device="cuda") for _ in range(3)]
+    for y in ys:
+        swq.gemm(t, d_w, d_x, y, M, N, K)
+    swq.check()
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])
+
+
 def test_deterministic(cuda):
     torch = cuda
     t = synth.Q4_K

@@ -269,3 +269,25 @@ def test_whole_row_work_splits(cuda, oracle_mod, fmt, N, K):
     X = synth.random_activations(1, K, seed=1101)
     got = _gemm_gpu(cuda, t, blocks, X, N, K)
     assert rel_l2(got, oracle_mod.gemm(t, blocks, X, 1, N, K)) <= REL_L2_TOL
+
+
+@pytest.mark.parametrize("smem_kb,stage_kb,ctas", [(220, 0, 0), (220, 24, 0), (0, 16, 0), (100, 40, 0), (0, 0, 2), (0, 32, 2)])
+@pytest.mark.parametrize("fmt,N,K", [("Q4_K", 28672, 4096), ("Q6_K", 4096, 14336), ("Q6_K", 1000, 4096),
+                                      ("Q4_K", 333, 2048)])
+def test_ring_options(cuda, oracle_mod, smem_kb, stage_kb, ctas, fmt, N, K):
+    """Other weight-ring shapes (SWQ_OPT_GEMV_SMEM_KB / SWQ_OPT_GEMV_STAGE_KB /
+    SWQ_OPT_GEMV_CTAS_PER_SM): whole-row and row-chunk stages, groups shorter
+    than a stage, two CTAs per SM."""
+    t = synth.IDS[fmt]
+    blocks = synth.random_blocks(t, N, K, seed=N + K)
+    X = synth.random_activations(1, K, seed=K)
+    swq.set_option(swq.OPT_GEMV_SMEM_KB, smem_kb)
+    swq.set_option(swq.OPT_GEMV_STAGE_KB, stage_kb)
+    swq.set_option(swq.OPT_GEMV_CTAS_PER_SM, ctas)
+    try:
+        got = _gemm_gpu(cuda, t, blocks, X, N, K)
+    finally:
+        swq.set_option(swq.OPT_GEMV_SMEM_KB, 0)
+        swq.set_option(swq.OPT_GEMV_STAGE_KB, 0)
+        swq.set_option(swq.OPT_GEMV_CTAS_PER_SM, 0)
+    assert rel_l2(got, oracle_mod.gemm(t, blocks, X, 1, N, K)) <= REL_L2_TOL

@@ -92,9 +92,10 @@ def test_unaligned_expert_weights(cuda, oracle_mod, fmt):
 
 
 def test_one_expert_equals_gemm(cuda):
-    """A single expert covering every row is the dense GEMM, bit for bit."""
+    """A single expert covering every row is the dense GEMM, bit for bit (80
+    output tiles: the dense call does not split K, so both sum in one order)."""
     torch = cuda
-    t, N, K, M = synth.Q4_K, 640, 2048, 200
+    t, N, K, M = synth.Q4_K, 10240, 1024, 200
     w = torch.from_numpy(synth.random_blocks(t, N, K, seed=4500).reshape(-1)).cuda()
     x = torch.from_numpy(synth.random_activations(M, K, seed=4501)).cuda()
     y1 = torch.empty((M, N), dtype=torch.float32, device="cuda")

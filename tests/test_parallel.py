@@ -132,3 +132,19 @@ def test_shards_are_valid_matrices():
     assert np.array_equal(np.concatenate(cols, axis=1), b.reshape(N, -1))
     with pytest.raises(ValueError):
         parallel.split_k(b, t, N, K, 0, 8)  # 128-column shards are not whole blocks
+
+
+def test_decoder_shards_reassemble():
+    """The decoder's weight shards: rows of a column-parallel matrix and the
+    whole blocks of a row-parallel one, which put back together give the
+    matrix (and match the parallel-layer split functions)."""
+    from swq.model import _shard
+    from swq.parallel import split_k, split_rows
+    for t, N, K in ((synth.Q4_K, 64, 1024), (synth.Q6_K, 32, 2048), (synth.Q8_0, 16, 256)):
+        b = synth.random_blocks(t, N, K, seed=t)
+        rows = [_shard(b, t, N, K, (r * N // 4, (r + 1) * N // 4), None) for r in range(4)]
+        assert np.array_equal(np.concatenate(rows), b.reshape(N, -1))
+        assert np.array_equal(rows[1], split_rows(b, N, 1, 4)[0])
+        cols = [_shard(b, t, N, K, None, (r * K // 2, (r + 1) * K // 2)) for r in range(2)]
+        assert np.array_equal(np.concatenate(cols, axis=1), b.reshape(N, -1))
+        assert np.array_equal(cols[1], split_k(b, t, N, K, 1, 2)[0])
