@@ -369,7 +369,7 @@ def run_decode(rank: int, world: int, batches=(1, 16), prefill: int = 512, steps
 
 
 def run_decode_tp(rank: int, world: int, batches=(1, 8, 32), context: int = 2048, steps: int = 32,
-                  warmup: int = 4) -> dict:
+                  warmup: int = 4, collective: str = "peer") -> dict:
     """Greedy decode of a Llama-3-70B-shaped model (80 layers, hidden 8192,
     64/8 heads of 128, FFN 28672, vocab 128256, Q4_K_M mix, synthetic weights
     generated on the device), tensor-parallel over all ranks (column-sharded
@@ -383,16 +383,18 @@ def run_decode_tp(rank: int, world: int, batches=(1, 8, 32), context: int = 2048
 
     cfg = LlamaConfig.llama3_70b(max_seq=context + steps + warmup + 8)
     wbytes = cfg.weight_bytes_per_token()
+    sums = ("one-shot all-reduce over NVLink peer memory (libswq)" if collective == "peer"
+            else "NCCL all-reduce")
     out = {"model": "Llama-3-70B shape, Q4_K_M mix, synthetic weights", "tensor_parallel": world,
            "context": context, "steps": steps, "weight_bytes_per_token": wbytes,
-           "collectives": "NCCL all-reduce after o and down, all-gather of the logits, in the CUDA graph"
+           "collectives": f"{sums} after o and down, NCCL all-gather of the logits, in the CUDA graph"
            if world > 1 else "none", "batches": {}}
     dist = None
     if world > 1:
         import torch.distributed as dist
     base = None
     for B in batches:
-        dec = LlamaDecoder(cfg, rows=B, seed=7, weights_from=base)
+        dec = LlamaDecoder(cfg, rows=B, seed=7, weights_from=base, collective=collective)
         base = base or dec
         dec.reset(list(range(B)), 0)
         dec.capture()
@@ -560,6 +562,8 @@ def main() -> None:
     ap.add_argument("--format", choices=sorted(TYPE_IDS), default="Q4_K", help="GEMM weight format")
     ap.add_argument("--M", type=int, default=512, help="GEMM activation rows")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU sample length (0: skip)")
+    ap.add_argument("--collective", choices=["peer", "nccl"], default="peer",
+                    help="decode70b: sums of the row-parallel projections")
     ap.add_argument("--no-decode", dest="decode", action="store_false",
                     help="skip the Llama-3-8B decode tok/s measurement of the default run")
     args = ap.parse_args()
@@ -585,7 +589,8 @@ def main() -> None:
             d = run_decode(rank, world, steps=args.steps if args.steps != ap.get_default("steps") else 256)
             name, scaling = "decode tok/s (Llama-3-8B Q4_K_M, batch 1)", "weak"
         else:
-            d = run_decode_tp(rank, world, steps=args.steps if args.steps != ap.get_default("steps") else 32)
+            d = run_decode_tp(rank, world, steps=args.steps if args.steps != ap.get_default("steps") else 32,
+                              collective=args.collective)
             name, scaling = f"decode tok/s (Llama-3-70B Q4_K_M, batch 1, tensor-parallel x{world})", "strong"
         if rank == 0:
             b1 = d["batches"]["1"]

@@ -200,11 +200,12 @@ enum {
      * is the GGUF format order and what the reference's CUDA backend computes
      * (host dequantize, then SGEMM, src/tensor.h:1219-1223). */
     SWQ_OPT_Q2K_REFERENCE_CPU_ORDER = 1,
-    /* 1 (default): the GEMV kernel starts streaming weight blocks before the
-     * previous kernel on the stream has finished (programmatic dependent
-     * launch); weights must then not be written by the immediately preceding
-     * kernel.  Activations are always read after that kernel completes.
-     * 0: every read waits for the preceding kernel. */
+    /* 1 (default): the GEMV and tensor-core GEMM kernels start streaming
+     * weight blocks before the previous kernel on the stream has finished
+     * (programmatic dependent launch); weights must then not be written by
+     * the kernel immediately preceding the call.  Activations are always read
+     * after that kernel completes.  0: every read waits for the preceding
+     * kernel. */
     SWQ_OPT_EARLY_WEIGHT_PREFETCH = 2,
     /* Largest number of activation rows one GEMV kernel launch serves
      * (default 8); GEMV work on more rows runs in groups of this size. */
@@ -241,6 +242,34 @@ int swq_get_option(int option);
  * this device gave up a wait since the last check, SWQ_ERR_CUDA if the
  * synchronize failed, else SWQ_OK. */
 swq_status swq_check(swq_stream_t stream);
+
+/* ---- Tensor-parallel all-reduce over peer memory -------------------------
+ *
+ * No counterpart in the reference: it runs one process, with no tensor
+ * parallelism (its model forward, src/model.h:257-543, has no collective).
+ * For the tensor-parallel decode of this library (one process per GPU,
+ * row-parallel o and down projections), the partial products are summed with
+ * a one-shot all-reduce: every rank's buffer is mapped by every other rank
+ * (CUDA IPC); each call copies the rank's vector into its buffer, publishes
+ * an epoch, waits (bounded) for the same slice of every peer, and sums the
+ * slices in rank order, so every rank ends with the same bits.
+ *   1. swq_allreduce_create on every rank (device current), for vectors of at
+ *      most max_elems floats; handle_out receives SWQ_ALLREDUCE_HANDLE_BYTES
+ *      bytes.
+ *   2. Exchange the handles (e.g. an all-gather of bytes), then
+ *      swq_allreduce_open with the world handles in rank order.
+ *   3. swq_allreduce_sum(ar, data, n, stream): in place, the same n on every
+ *      rank, calls in the same order on every rank (also inside CUDA graphs).
+ *      A wait that gives up (a peer that never arrives) records
+ *      SWQ_ERR_TIMEOUT for swq_check.
+ *   4. swq_allreduce_destroy once no call is in flight on any rank.
+ * At most 8 ranks. */
+#define SWQ_ALLREDUCE_HANDLE_BYTES 64
+typedef struct swq_allreduce swq_allreduce;
+swq_status swq_allreduce_create(size_t max_elems, int rank, int world, swq_allreduce** out, void* handle_out);
+swq_status swq_allreduce_open(swq_allreduce* ar, const void* handles);
+swq_status swq_allreduce_sum(swq_allreduce* ar, float* data, size_t n, swq_stream_t stream);
+swq_status swq_allreduce_destroy(swq_allreduce* ar);
 
 /* ---- Host-buffer entry point (the reference's calling convention) --------
  *

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "../../include/swq.h"
+#include "allreduce.h"
 #include "decode.h"
 #include "gemm_tc.h"
 #include "gemv.h"
@@ -179,6 +180,7 @@ swq_status swq_set_option(int option, int value) {
         case SWQ_OPT_EARLY_WEIGHT_PREFETCH:
             if (value != 0 && value != 1) return fail(SWQ_ERR_BAD_ARG, "option value must be 0 or 1");
             g_opt_early_prefetch = value;
+            swq::gemm_tc_set_early_prefetch(value);
             return SWQ_OK;
         case SWQ_OPT_GEMV_MAX_M:
             if (value < 0 || value > 8) return fail(SWQ_ERR_BAD_ARG, "GEMV max M must be in 0..8");
@@ -459,16 +461,118 @@ swq_status swq_check(swq_stream_t stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
-    unsigned a = 0, b = 0, c = 0;
+    unsigned a = 0, b = 0, c = 0, d = 0;
     if ((e = swq::status_fetch_gemv(&a, s)) != cudaSuccess ||
         (e = swq::status_fetch_dequant(&b, s)) != cudaSuccess ||
-        (e = swq::status_fetch_gemm_tc(&c, s)) != cudaSuccess)
+        (e = swq::status_fetch_gemm_tc(&c, s)) != cudaSuccess ||
+        (e = swq::status_fetch_allreduce(&d, s)) != cudaSuccess)
         return cuda_fail(e, "status fetch");
-    if (a | b | c) {
-        char buf[96];
-        std::snprintf(buf, sizeof(buf), "device wait timeout (gemv=%#x dequant=%#x gemm=%#x)", a, b, c);
+    if (a | b | c | d) {
+        char buf[128];
+        std::snprintf(buf, sizeof(buf), "device wait timeout (gemv=%#x dequant=%#x gemm=%#x allreduce=%#x)", a, b,
+                      c, d);
         return fail(SWQ_ERR_TIMEOUT, buf);
     }
+    return SWQ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Peer-memory all-reduce of a tensor-parallel group (one process per GPU).
+// ---------------------------------------------------------------------------
+
+static_assert(sizeof(cudaIpcMemHandle_t) == SWQ_ALLREDUCE_HANDLE_BYTES, "IPC handle size");
+
+struct swq_allreduce {
+    int device = -1;
+    int rank = 0, world = 1;
+    size_t max_elems = 0;
+    void* own = nullptr;
+    void* peer[SWQ_AR_MAX_RANKS] = {};
+    swq::ArBuffer bufs[SWQ_AR_MAX_RANKS] = {};
+    bool opened = false;
+};
+
+swq_status swq_allreduce_create(size_t max_elems, int rank, int world, swq_allreduce** out, void* handle_out) {
+    if (!out || !handle_out) return fail(SWQ_ERR_NULL_PTR, "null output pointer");
+    *out = nullptr;
+    if (world < 1 || world > SWQ_AR_MAX_RANKS || rank < 0 || rank >= world)
+        return fail(SWQ_ERR_BAD_ARG, "rank/world outside 0 <= rank < world <= 8");
+    if (max_elems == 0) return fail(SWQ_ERR_BAD_SHAPE, "max_elems must be positive");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    auto* ar = new swq_allreduce();
+    ar->device = dev.device;
+    ar->rank = rank;
+    ar->world = world;
+    ar->max_elems = max_elems;
+    const size_t bytes = swq::allreduce_buffer_bytes(max_elems);
+    cudaError_t e = cudaMalloc(&ar->own, bytes);
+    if (e == cudaSuccess) e = cudaMemset(ar->own, 0, bytes);  // flags and epochs start at 0
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, ar->own);
+    if (e != cudaSuccess) {
+        if (ar->own) cudaFree(ar->own);
+        delete ar;
+        return cuda_fail(e, "all-reduce buffer");
+    }
+    std::memcpy(handle_out, &h, sizeof(h));
+    ar->bufs[rank] = swq::ar_view(ar->own, max_elems);
+    *out = ar;
+    return SWQ_OK;
+}
+
+swq_status swq_allreduce_open(swq_allreduce* ar, const void* handles) {
+    if (!ar || !handles) return fail(SWQ_ERR_NULL_PTR, "null all-reduce or handles");
+    if (ar->opened) return fail(SWQ_ERR_BAD_ARG, "peers already opened");
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != ar->device) return fail(SWQ_ERR_BAD_ARG, "current device is not the all-reduce's device");
+    for (int r = 0; r < ar->world; ++r) {
+        if (r == ar->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + static_cast<size_t>(r) * SWQ_ALLREDUCE_HANDLE_BYTES,
+                    sizeof(h));
+        cudaError_t e = cudaIpcOpenMemHandle(&ar->peer[r], h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; ++q)
+                if (ar->peer[q]) {
+                    cudaIpcCloseMemHandle(ar->peer[q]);
+                    ar->peer[q] = nullptr;
+                }
+            return cuda_fail(e, "cudaIpcOpenMemHandle");
+        }
+        ar->bufs[r] = swq::ar_view(ar->peer[r], ar->max_elems);
+    }
+    ar->opened = true;
+    return SWQ_OK;
+}
+
+swq_status swq_allreduce_sum(swq_allreduce* ar, float* data, size_t n, swq_stream_t stream) {
+    if (!ar || !data) return fail(SWQ_ERR_NULL_PTR, "null all-reduce or data");
+    if (!ar->opened && ar->world > 1) return fail(SWQ_ERR_BAD_ARG, "swq_allreduce_open has not run");
+    if (n > ar->max_elems) return fail(SWQ_ERR_BAD_SHAPE, "vector longer than the all-reduce buffer");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    if (dev.device != ar->device) return fail(SWQ_ERR_BAD_ARG, "current device is not the all-reduce's device");
+    return launch_status(swq::allreduce_launch(ar->bufs, ar->rank, ar->world, data, n, dev.num_sms,
+                                               reinterpret_cast<cudaStream_t>(stream)),
+                         "all-reduce launch");
+}
+
+swq_status swq_allreduce_destroy(swq_allreduce* ar) {
+    if (!ar) return SWQ_OK;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    cudaSetDevice(ar->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < ar->world; ++r)
+        if (ar->peer[r]) cudaIpcCloseMemHandle(ar->peer[r]);
+    if (ar->own) cudaFree(ar->own);
+    if (cur >= 0) cudaSetDevice(cur);
+    delete ar;
     return SWQ_OK;
 }
 

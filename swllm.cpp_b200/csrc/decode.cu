@@ -10,6 +10,13 @@
 // whole decode step can be captured once in a CUDA graph and replayed.
 //
 // KV cache layout (fp32): [layer][sequence b][position t][kv_dim].
+//
+// Every kernel here is launched as a programmatic dependent of the kernel
+// before it on the stream: it is resident early and begins with
+// griddepcontrol.wait, so nothing here touches memory before its predecessor
+// completed.  It lets its own dependents launch (griddepcontrol.launch_dependents)
+// only once its work is done: the GEMV that usually follows spreads one CTA per
+// SM over a GPU that no longer holds the previous GEMV's CTAs.
 #include <cuda_runtime.h>
 #include <math.h>
 
@@ -17,6 +24,7 @@
 #include <cstdint>
 
 #include "decode.h"
+#include "swq_device.cuh"
 
 namespace swq {
 
@@ -51,6 +59,7 @@ template <bool VEC, bool ADD>
 __global__ void __launch_bounds__(1024) rmsnorm_kernel(float* __restrict__ out, float* __restrict__ x,
                                                        const float* __restrict__ y, const float* __restrict__ w,
                                                        int n, float eps) {
+    pdl_wait_primary();
     __shared__ float red[33];
     float* xr = x + static_cast<size_t>(blockIdx.x) * n;
     const float* yr = ADD ? y + static_cast<size_t>(blockIdx.x) * n : nullptr;
@@ -103,6 +112,7 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
                                float* __restrict__ kcache, float* __restrict__ vcache, const int* __restrict__ pos_p,
                                const float* __restrict__ freqs, int q_dim, int kv_dim, int head_dim, int rope_dim,
                                int neox, int max_seq, int ldq, int ldk, int ldv) {
+    pdl_wait_primary();
     const int b = blockIdx.y;
     const int pos = *pos_p;
     const int half = rope_dim / 2;
@@ -173,6 +183,7 @@ __global__ void __launch_bounds__(AttCfg<MUL, PER>::THREADS) attn_kernel(
     const float* __restrict__ q, const float* __restrict__ kcache, const float* __restrict__ vcache,
     const int* __restrict__ pos_p, float* __restrict__ part_o, float* __restrict__ part_ml,
     unsigned* __restrict__ done, float* __restrict__ out, int num_heads, int num_kv_heads, int max_seq, int ldq) {
+    pdl_wait_primary();
     using C = AttCfg<MUL, PER>;
     constexpr int HD = 32 * PER;
     constexpr int NW = C::NW, U = C::U, NT = C::THREADS;
@@ -332,6 +343,7 @@ __global__ void __launch_bounds__(AttCfg<MUL, PER>::THREADS) attn_kernel(
 // (src/tensor.h:1050-1064); out is rows x n, row-major.
 __global__ void silu_mul_kernel(float* __restrict__ out, const float* __restrict__ gate, const float* __restrict__ up,
                                 int n, int rows, int ld) {
+    pdl_wait_primary();
     const int64_t total = static_cast<int64_t>(n) * rows;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -343,6 +355,7 @@ __global__ void silu_mul_kernel(float* __restrict__ out, const float* __restrict
 
 // x += y (the residual adds of src/model.h:363, 541).
 __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, int64_t n) {
+    pdl_wait_primary();
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x)
         x[i] += y[i];
@@ -352,6 +365,7 @@ __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, i
 // [0, vocab) reads row 0.
 __global__ void embed_kernel(float* __restrict__ x, const float* __restrict__ table, const int* __restrict__ tokens,
                              int dim, int vocab) {
+    pdl_wait_primary();
     const int b = blockIdx.y;
     const int tok = tokens[b];
     const float* row = table + static_cast<size_t>(tok >= 0 && tok < vocab ? tok : 0) * dim;
@@ -371,6 +385,7 @@ __device__ __forceinline__ void better(float v, int i, float& best, int& bi) {
 template <bool VEC>
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int n, int* __restrict__ tokens,
                                                       int* __restrict__ history, const int* __restrict__ step_p) {
+    pdl_wait_primary();
     const int b = blockIdx.x;
     const float* row = logits + static_cast<size_t>(b) * n;
     // index 0 until a larger value is seen: a row of NaN still yields a valid token
@@ -413,8 +428,25 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
 }
 
 __global__ void advance_kernel(int* pos, int* step) {
+    pdl_wait_primary();
     *pos += 1;
     if (step) *step += 1;
+}
+
+// Launch as a programmatic dependent of the previous kernel on the stream.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
 int grid_for(int64_t n, int num_sms) {
@@ -424,6 +456,12 @@ int grid_for(int64_t n, int num_sms) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+#define ERR_RET(call)                            \
+    do {                                         \
+        const cudaError_t e_ = (call);           \
+        if (e_ != cudaSuccess) return e_;        \
+    } while (0)
+
 }  // namespace
 
 cudaError_t rmsnorm_launch(float* out, float* x, const float* y, const float* w, int n, float eps, int rows,
@@ -431,11 +469,11 @@ cudaError_t rmsnorm_launch(float* out, float* x, const float* y, const float* w,
     const bool vec = n % 4 == 0 && aligned16(out) && aligned16(x) && aligned16(w) && (!y || aligned16(y));
     const int threads = std::min(1024, std::max(32, ((vec ? n / 4 : n) + 31) / 32 * 32));
     if (y) {
-        if (vec) rmsnorm_kernel<true, true><<<rows, threads, 0, s>>>(out, x, y, w, n, eps);
-        else rmsnorm_kernel<false, true><<<rows, threads, 0, s>>>(out, x, y, w, n, eps);
+        if (vec) ERR_RET(launch_pdl(rmsnorm_kernel<true, true>, dim3(rows), dim3(threads), s, out, x, y, w, n, eps));
+        else ERR_RET(launch_pdl(rmsnorm_kernel<false, true>, dim3(rows), dim3(threads), s, out, x, y, w, n, eps));
     } else {
-        if (vec) rmsnorm_kernel<true, false><<<rows, threads, 0, s>>>(out, x, nullptr, w, n, eps);
-        else rmsnorm_kernel<false, false><<<rows, threads, 0, s>>>(out, x, nullptr, w, n, eps);
+        if (vec) ERR_RET(launch_pdl(rmsnorm_kernel<true, false>, dim3(rows), dim3(threads), s, out, x, nullptr, w, n, eps));
+        else ERR_RET(launch_pdl(rmsnorm_kernel<false, false>, dim3(rows), dim3(threads), s, out, x, nullptr, w, n, eps));
     }
     return cudaGetLastError();
 }
@@ -445,8 +483,7 @@ cudaError_t rope_kv_launch(float* q, const float* k, const float* v, float* kcac
                            int max_seq, int ldq, int ldk, int ldv, int num_sms, cudaStream_t s) {
     const int items = (q_dim / head_dim + kv_dim / head_dim) * (rope_dim / 2) + kv_dim;
     const dim3 grid(static_cast<unsigned>(grid_for(items, num_sms)), static_cast<unsigned>(rows));
-    rope_kv_kernel<<<grid, 256, 0, s>>>(q, k, v, kcache, vcache, pos, freqs, q_dim, kv_dim, head_dim, rope_dim, neox,
-                                        max_seq, ldq, ldk, ldv);
+    ERR_RET(launch_pdl(rope_kv_kernel, dim3(grid), dim3(256), s, q, k, v, kcache, vcache, pos, freqs, q_dim, kv_dim, head_dim, rope_dim, neox, max_seq, ldq, ldk, ldv));
     return cudaGetLastError();
 }
 
@@ -470,16 +507,13 @@ static cudaError_t attn_per(int per, dim3 grid, cudaStream_t s, const float* q, 
                             int max_seq, int ldq) {
     switch (per) {
         case 2:
-            attn_kernel<MUL, 2><<<grid, AttCfg<MUL, 2>::THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
-                                                             ldq);
+            ERR_RET(launch_pdl(attn_kernel<MUL, 2>, dim3(grid), dim3(AttCfg<MUL, 2>::THREADS), s, q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq, ldq));
             break;
         case 4:
-            attn_kernel<MUL, 4><<<grid, AttCfg<MUL, 4>::THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
-                                                             ldq);
+            ERR_RET(launch_pdl(attn_kernel<MUL, 4>, dim3(grid), dim3(AttCfg<MUL, 4>::THREADS), s, q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq, ldq));
             break;
         case 8:
-            attn_kernel<MUL, 8><<<grid, AttCfg<MUL, 8>::THREADS, 0, s>>>(q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq,
-                                                             ldq);
+            ERR_RET(launch_pdl(attn_kernel<MUL, 8>, dim3(grid), dim3(AttCfg<MUL, 8>::THREADS), s, q, kc, vc, pos, po, pml, done, out, nh, nkv, max_seq, ldq));
             break;
         default: return cudaErrorInvalidValue;
     }
@@ -506,32 +540,33 @@ cudaError_t attention_launch(float* out, const float* q, const float* kcache, co
 
 cudaError_t silu_mul_launch(float* out, const float* gate, const float* up, int n, int rows, int ld, int num_sms,
                             cudaStream_t s) {
-    silu_mul_kernel<<<grid_for(static_cast<int64_t>(n) * rows, num_sms), 256, 0, s>>>(out, gate, up, n, rows, ld);
+    ERR_RET(launch_pdl(silu_mul_kernel, dim3(grid_for(static_cast<int64_t>(n) * rows, num_sms)), dim3(256), s, out,
+                       gate, up, n, rows, ld));
     return cudaGetLastError();
 }
 
 cudaError_t add_launch(float* x, const float* y, int64_t n, int num_sms, cudaStream_t s) {
-    add_kernel<<<grid_for(n, num_sms), 256, 0, s>>>(x, y, n);
+    ERR_RET(launch_pdl(add_kernel, dim3(grid_for(n, num_sms)), dim3(256), s, x, y, n));
     return cudaGetLastError();
 }
 
 cudaError_t embed_launch(float* x, const float* table, const int* tokens, int dim, int vocab, int rows,
                          cudaStream_t s) {
-    embed_kernel<<<dim3((dim + 255) / 256, rows), 256, 0, s>>>(x, table, tokens, dim, vocab);
+    ERR_RET(launch_pdl(embed_kernel, dim3((dim + 255) / 256, rows), dim3(256), s, x, table, tokens, dim, vocab));
     return cudaGetLastError();
 }
 
 cudaError_t argmax_launch(const float* logits, int n, int rows, int* tokens, int* history, const int* step,
                           cudaStream_t s) {
     if (n % 4 == 0 && aligned16(logits))
-        argmax_kernel<true><<<rows, 1024, 0, s>>>(logits, n, tokens, history, step);
+        ERR_RET(launch_pdl(argmax_kernel<true>, dim3(rows), dim3(1024), s, logits, n, tokens, history, step));
     else
-        argmax_kernel<false><<<rows, 1024, 0, s>>>(logits, n, tokens, history, step);
+        ERR_RET(launch_pdl(argmax_kernel<false>, dim3(rows), dim3(1024), s, logits, n, tokens, history, step));
     return cudaGetLastError();
 }
 
 cudaError_t advance_launch(int* pos, int* step, cudaStream_t s) {
-    advance_kernel<<<1, 1, 0, s>>>(pos, step);
+    ERR_RET(launch_pdl(advance_kernel, dim3(1), dim3(1), s, pos, step));
     return cudaGetLastError();
 }
 

@@ -33,6 +33,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 #include <map>
@@ -516,6 +517,7 @@ struct Params {
     const int* offsets;
     int n_experts;
     int rows_total;
+    int early;  // the W producer may read weights before the previous kernel completes
     // split-K (dense only): each output tile is computed as ksplit work units
     // of gps W stages each; unit u = tile * ksplit + split.  With ksplit > 1
     // every unit writes its partial tile to part[split][M][N], and the unit
@@ -627,6 +629,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         *abort_flag = 0;
         mbar_fence_init();
     }
+    if (G) pdl_wait_primary();  // the expert offsets may come from the previous kernels
     if (G && warp == 0) {
         // tiles of expert e = ceil(rows_e / BN) * n_ntiles; tpre = exclusive prefix
         int carry = 0;
@@ -658,7 +661,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int ntiles = G ? tpre[p.n_experts] : p.n_mtiles * p.n_ntiles * p.ksplit;  // work units
-    pdl_wait_primary();  // X (fp16) is written by the conversion kernel before this one
+    // Programmatic dependency on the conversion kernel before this one: the
+    // roles that read X16 (X producer) or write Y and the split-K buffers
+    // (epilogue) wait for it; the W producer, the dequantizers and the MMA
+    // touch only the immutable weights and shared memory, so the first W
+    // stages stream in while the conversion finishes.  Grouped launches read
+    // the expert offsets above, so everything waits.
+    if (!G && (!p.early || warp == WARP_X || is_epilogue(warp))) pdl_wait_primary();
 
     if (warp == WARP_X) {
         // -------------------------------------------------- activation TMA producer
@@ -1003,6 +1012,10 @@ __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__
                                                        float* __restrict__ rowscale, int M, int K,
                                                        unsigned* __restrict__ tcount, int ncount) {
     __shared__ float red[8];
+    // The GEMM launched after this kernel may start (its weight loads do not
+    // depend on this kernel); this kernel itself waits for its predecessor.
+    pdl_launch_dependents();
+    pdl_wait_primary();
     // split-K tile counters of the GEMM that follows start at zero
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncount; i += gridDim.x * blockDim.x) tcount[i] = 0u;
     for (int row = blockIdx.x; row < M; row += gridDim.x) {
@@ -1048,7 +1061,6 @@ __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__
         }
         __syncthreads();  // red is reused by the next row
     }
-    pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -1097,6 +1109,9 @@ struct ExpertSet {
 };
 
 // M is the number of X rows (grouped: all experts' rows together).
+static std::atomic<int> g_early_prefetch{1};
+void gemm_tc_set_early_prefetch(int on) { g_early_prefetch = on ? 1 : 0; }
+
 // Split-K plan of a dense call and its scratch (part: ksplit x M x N floats,
 // tcount: 4 counters per output tile).
 struct SplitK {
@@ -1148,6 +1163,7 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, const float* rowsc
     p.w_lo = reinterpret_cast<const uint8_t*>(w & ~uintptr_t(15));
     p.w_hi = reinterpret_cast<const uint8_t*>((w + wbytes + 15) & ~uintptr_t(15));
     size_t extra = 0;
+    p.early = g_early_prefetch.load(std::memory_order_relaxed);
     p.ksplit = G ? 1 : sk.ksplit;
     p.gps = G || sk.ksplit == 1 ? p.ngroups : sk.gps;
     p.part = sk.part;
@@ -1276,11 +1292,18 @@ template <bool F2>
 static cudaError_t launch_x_to_f16(const float* X, __half* Xh, float* rowscale, int M, int K, int num_sms,
                                    cudaStream_t s, unsigned* tcount = nullptr, int ncount = 0) {
     const int grid = std::max(1, std::min(M, num_sms * 8));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if ((reinterpret_cast<uintptr_t>(X) & 15u) == 0)
-        x_to_f16_kernel<F2, true><<<grid, 256, 0, s>>>(X, Xh, rowscale, M, K, tcount, ncount);
-    else
-        x_to_f16_kernel<F2, false><<<grid, 256, 0, s>>>(X, Xh, rowscale, M, K, tcount, ncount);
-    return cudaGetLastError();
+        return cudaLaunchKernelEx(&cfg, x_to_f16_kernel<F2, true>, X, Xh, rowscale, M, K, tcount, ncount);
+    return cudaLaunchKernelEx(&cfg, x_to_f16_kernel<F2, false>, X, Xh, rowscale, M, K, tcount, ncount);
 }
 
 static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }

@@ -21,4 +21,8 @@ cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int
                                    int n_experts, int rows, int N, int K, int num_sms, cudaStream_t s);
 cudaError_t status_fetch_gemm_tc(unsigned* out, cudaStream_t s);
 
+// SWQ_OPT_EARLY_WEIGHT_PREFETCH for the tensor-core GEMM: 1 lets its weight
+// loads start before the previous kernel on the stream completes.
+void gemm_tc_set_early_prefetch(int on);
+
 }  // namespace swq

@@ -93,6 +93,10 @@ def lib() -> ctypes.CDLL:
         "swq_set_option": (i32, [i32, i32]),
         "swq_get_option": (i32, [i32]),
         "swq_check": (i32, [vp]),
+        "swq_allreduce_create": (i32, [sz, i32, i32, ctypes.POINTER(vp), vp]),
+        "swq_allreduce_open": (i32, [vp, vp]),
+        "swq_allreduce_sum": (i32, [vp, vp, sz, vp]),
+        "swq_allreduce_destroy": (i32, [vp]),
         "swq_ctx_create": (i32, [i32, ctypes.POINTER(vp)]),
         "swq_ctx_destroy": (i32, [vp]),
         "swq_ctx_matmul_transposed_q": (i32, [vp, vp, vp, vp, i32, i32, i32]),

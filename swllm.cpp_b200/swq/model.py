@@ -121,7 +121,8 @@ def _shard(host, type_id: int, N: int, K: int, rows: tuple[int, int] | None, col
 
 class LlamaDecoder:
     def __init__(self, cfg: LlamaConfig, rows: int = 1, device="cuda", seed: int = 0, weights: dict | None = None,
-                 max_steps: int = 4096, group=None, weights_from: "LlamaDecoder | None" = None):
+                 max_steps: int = 4096, group=None, weights_from: "LlamaDecoder | None" = None,
+                 collective: str = "peer"):
         """weights: None for synthetic weights, else host arrays: 'token_embd'
         [vocab, dim] fp32, 'output_norm' [dim], 'output' blocks, and per layer
         'layers'[l] with 'attn_norm', 'ffn_norm' [dim] fp32 and the blocks of
@@ -129,7 +130,9 @@ class LlamaDecoder:
         shard).  group: torch.distributed group for tensor parallelism (None:
         the default group when one is initialised with more than one rank).
         weights_from: a decoder of the same config and group whose device
-        weights this one shares (another batch size of the same model)."""
+        weights this one shares (another batch size of the same model).
+        collective: "peer" (libswq's one-shot all-reduce over peer memory)
+        or "nccl" (torch.distributed.all_reduce) for the o/down sums."""
         import torch
         from .parallel import _world
         self.cfg, self.rows, self.device = cfg, rows, torch.device(device)
@@ -174,6 +177,14 @@ class LlamaDecoder:
         else:
             self._load_weights(cfg, W, weights, blocks, g, f32)
         self._alloc_state(cfg, rows, max_steps, f32)
+        if collective not in ("peer", "nccl"):
+            raise ValueError(f"collective must be 'peer' or 'nccl', not {collective!r}")
+        self.collective = collective
+        self._peer = None
+        if G > 1 and collective == "peer":
+            from .comm import PeerAllReduce
+            self._peer = PeerAllReduce(rows * cfg.dim, group=group, device=dev)
+            self.all_reduce = lambda t: self._peer(t, stream=self.stream)
 
     def _load_weights(self, cfg, W, weights, blocks, g, f32):
         import torch
