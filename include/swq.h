@@ -160,6 +160,37 @@ swq_status swq_grouped_gemm(int ggml_type, const void* const* W_experts, const i
                             const float* X_sorted, float* Y, int n_experts, int total_rows,
                             int N, int K, swq_stream_t stream);
 
+/* ---- GEMM with a fused activation prologue --------------------------------
+ *
+ * No counterpart in the reference: its decode step runs RMSNorm
+ * (src/tensor.h:1028-1033) and SiLU-mul (src/tensor.h:1050-1064) as separate
+ * passes before the projections that read them (src/model.h:272-289,
+ * 519-541).  swq_gemm_act computes swq_gemm on a transformed X, the transform
+ * done while the kernel stages the activations (no extra pass over memory):
+ *   SWQ_ACT_NONE     X as given.
+ *   SWQ_ACT_RMSNORM  x = X[m] (+ residual[m] when residual != NULL), then
+ *                    x / sqrt(mean(x^2) + eps) * norm_w (K weights).  With
+ *                    sum_out != NULL, x (the residual sum) is also written
+ *                    there (M x K); sum_out must not overlap X or residual.
+ *   SWQ_ACT_SWIGLU   x[k] = silu(g[k]) * u[k] with g = X[m*ld + k] and
+ *                    u = X[m*ld + K + k] (gate then up in one row of stride
+ *                    ld >= 2K; ld = 0 means 2K).
+ * flags: SWQ_GEMM_NOALLOC runs as swq_gemm_noalloc (same limit).  act = NULL
+ * is SWQ_ACT_NONE.  Tolerance as swq_gemm (the scale 1/rms is applied to the
+ * outputs, in fp32). */
+enum { SWQ_ACT_NONE = 0, SWQ_ACT_RMSNORM = 1, SWQ_ACT_SWIGLU = 2 };
+enum { SWQ_GEMM_NOALLOC = 1 };
+typedef struct swq_act {
+    int kind;
+    const float* residual;
+    const float* norm_w;
+    float eps;
+    float* sum_out;
+    int ld;
+} swq_act;
+swq_status swq_gemm_act(int ggml_type, const void* W, const float* X, float* Y, int M, int N, int K,
+                        const swq_act* act, int flags, swq_stream_t stream);
+
 /* ---- Allocation-free GEMM ------------------------------------------------
  *
  * No counterpart in the reference.  swq_gemm's tensor-core path takes a

@@ -115,15 +115,22 @@ swq_status check_gemm_args(int type, const void* W, const float* X, const float*
 
 // Y = X . W^T through the GEMV kernel, groups of up to max_m rows of X.
 swq_status gemm_gemv_groups(int type, const void* W, const float* X, float* Y, int M, int N, int K, int max_m,
-                            const swq::DeviceInfo& dev, cudaStream_t s) {
+                            const swq::DeviceInfo& dev, cudaStream_t s, const swq::ActArgs& act = swq::ActArgs{}) {
     const int g = gemv_group_rows(type, K, std::max(1, max_m));
     if (g == 0) return fail(SWQ_ERR_BAD_SHAPE, "K=" + std::to_string(K) + " exceeds the GEMV activation buffer");
+    const int ld = act.ld > 0 ? act.ld : K;
     for (int m0 = 0; m0 < M; m0 += g) {
         swq::GemvLaunch L{};
         L.type = type;
         L.W = W;
-        L.X = X + static_cast<size_t>(m0) * K;
+        L.X = X + static_cast<size_t>(m0) * ld;
         L.Y = Y + static_cast<size_t>(m0) * N;
+        L.act = act.kind;
+        L.R = act.R ? act.R + static_cast<size_t>(m0) * K : nullptr;
+        L.normw = act.normw;
+        L.eps = act.eps;
+        L.sum_out = act.sum_out ? act.sum_out + static_cast<size_t>(m0) * K : nullptr;
+        L.ld = ld;
         L.M = std::min(g, M - m0);
         L.N = N;
         L.K = K;
@@ -261,6 +268,46 @@ swq_status swq_gemm(int type, const void* W, const float* X, float* Y, int M, in
         return SWQ_OK;
     }
     return gemm_gemv_groups(type, W, X, Y, M, N, K, max_m, dev, s);
+}
+
+swq_status swq_gemm_act(int type, const void* W, const float* X, float* Y, int M, int N, int K,
+                        const swq_act* act, int flags, swq_stream_t stream) {
+    TypeInfo ti;
+    swq_status st = check_gemm_args(type, W, X, Y, M, N, K, &ti);
+    if (st != SWQ_OK || M == 0 || N == 0) return st;
+    if (flags & ~SWQ_GEMM_NOALLOC) return fail(SWQ_ERR_BAD_ARG, "unknown flags");
+    swq::ActArgs a;
+    if (act) {
+        if (act->kind != SWQ_ACT_NONE && act->kind != SWQ_ACT_RMSNORM && act->kind != SWQ_ACT_SWIGLU)
+            return fail(SWQ_ERR_BAD_ARG, "unknown activation prologue " + std::to_string(act->kind));
+        a.kind = act->kind;
+        if (a.kind == SWQ_ACT_RMSNORM) {
+            if (!act->norm_w) return fail(SWQ_ERR_NULL_PTR, "RMSNORM needs norm_w");
+            if (!(act->eps >= 0.f)) return fail(SWQ_ERR_BAD_ARG, "eps must be >= 0");
+            a.R = act->residual;
+            a.normw = act->norm_w;
+            a.eps = act->eps;
+            a.sum_out = act->sum_out;
+        } else if (a.kind == SWQ_ACT_SWIGLU) {
+            a.ld = act->ld > 0 ? act->ld : 2 * K;
+            if (a.ld < 2 * K) return fail(SWQ_ERR_BAD_SHAPE, "SWIGLU row stride below 2K");
+        }
+    }
+    const bool noalloc = (flags & SWQ_GEMM_NOALLOC) != 0;
+    if (noalloc && static_cast<int64_t>(M) * K > SWQ_GEMM_NOALLOC_MAX_X_ELEMS)
+        return fail(SWQ_ERR_BAD_SHAPE, "swq_gemm_act: M*K exceeds the fixed scratch");
+    swq::DeviceInfo dev;
+    if ((st = current_device(&dev)) != SWQ_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (K == 0) return fail(SWQ_ERR_BAD_SHAPE, "swq_gemm_act needs K > 0");
+    if (M >= g_opt_tc_min_m && g_opt_gemm_tc && swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
+        cudaError_t e = noalloc ? swq::gemm_tc_launch_noalloc(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms,
+                                                              s, a)
+                                : swq::gemm_tc_launch(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms, s, a);
+        if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
+        return SWQ_OK;
+    }
+    return gemm_gemv_groups(type, W, X, Y, M, N, K, g_opt_gemv_max_m, dev, s, a);
 }
 
 swq_status swq_gemm_noalloc(int type, const void* W, const float* X, float* Y, int M, int N, int K,

@@ -1007,51 +1007,101 @@ __global__ void __launch_bounds__(THREADS, 1)
 // rowscale[row] = 2^k undoes it exactly in the epilogue.  All-zero rows and
 // rows holding inf keep k = 0.  One CTA per row (grid-stride); 8 positions per thread-step, two
 // runs of four consecutive elements (float4 when aligned).
+// Four consecutive prologue inputs at k (k % 4 == 0): the value the GEMM
+// multiplies (v), and for RMSNORM the sum x = X + R before the weights.
+template <bool VEC>
+__device__ __forceinline__ float4 ld4(const float* p) {
+    if (VEC) return *reinterpret_cast<const float4*>(p);
+    return make_float4(p[0], p[1], p[2], p[3]);
+}
+template <bool VEC>
+__device__ __forceinline__ float4 act4(const ActArgs& a, const float* xr, const float* rr, int K, int k, float4& x) {
+    x = ld4<VEC>(xr + k);
+    if (a.kind == 2) {
+        const float4 u = ld4<VEC>(xr + K + k);
+        return make_float4(x.x / (1.0f + expf(-x.x)) * u.x, x.y / (1.0f + expf(-x.y)) * u.y,
+                           x.z / (1.0f + expf(-x.z)) * u.z, x.w / (1.0f + expf(-x.w)) * u.w);
+    }
+    if (a.kind == 1) {
+        if (rr) {
+            const float4 r = ld4<VEC>(rr + k);
+            x.x += r.x; x.y += r.y; x.z += r.z; x.w += r.w;
+        }
+        const float4 w = ld4<VEC>(a.normw + k);
+        return make_float4(x.x * w.x, x.y * w.y, x.z * w.z, x.w * w.w);
+    }
+    return x;
+}
+
+// fp32 -> fp16 activations in the K order of the tensor-core GEMM: within each
+// 256-element group, position p holds element tc_elem(F2, p).  Each row (after
+// the activation prologue) is first scaled by the power of two 2^-k that
+// brings its largest finite magnitude into [2^14, 2^15): no element overflows
+// fp16 (65504) and small rows keep fp16's full precision instead of falling
+// into its subnormals; rowscale[row] = 2^k (times the RMSNORM factor) undoes
+// it exactly in the epilogue.  All-zero rows and rows holding inf keep k = 0.
+// One CTA per row (grid-stride); 8 positions per thread-step, two runs of four
+// consecutive elements (float4 when aligned).
 template <bool F2, bool VEC>
 __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__ X, __half* __restrict__ Xh,
                                                        float* __restrict__ rowscale, int M, int K,
-                                                       unsigned* __restrict__ tcount, int ncount) {
-    __shared__ float red[8];
+                                                       unsigned* __restrict__ tcount, int ncount, const ActArgs act) {
+    __shared__ float red[8], red2[8];
     // The GEMM launched after this kernel may start (its weight loads do not
     // depend on this kernel); this kernel itself waits for its predecessor.
     pdl_launch_dependents();
     pdl_wait_primary();
     // split-K tile counters of the GEMM that follows start at zero
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncount; i += gridDim.x * blockDim.x) tcount[i] = 0u;
+    const int ld = act.ld > 0 ? act.ld : K;
     for (int row = blockIdx.x; row < M; row += gridDim.x) {
-        const float* xr = X + static_cast<int64_t>(row) * K;
-        float mx = 0.f;
-        if (VEC) {
-            for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
-                const float4 v = reinterpret_cast<const float4*>(xr)[i];
-                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        const float* xr = X + static_cast<int64_t>(row) * ld;
+        const float* rr = act.R ? act.R + static_cast<int64_t>(row) * K : nullptr;
+        float* so = act.sum_out ? act.sum_out + static_cast<int64_t>(row) * K : nullptr;
+        float mx = 0.f, ss = 0.f;
+        for (int k = 4 * threadIdx.x; k < K; k += 4 * blockDim.x) {
+            float4 x;
+            const float4 v = act4<VEC>(act, xr, rr, K, k, x);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            if (act.kind == 1) {
+                ss = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, fmaf(x.w, x.w, ss))));
+                if (so) {
+                    if (VEC) *reinterpret_cast<float4*>(so + k) = x;
+                    else { so[k] = x.x; so[k + 1] = x.y; so[k + 2] = x.z; so[k + 3] = x.w; }
+                }
             }
-        } else {
-            for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(xr[i]));
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+        for (int o = 16; o > 0; o >>= 1) {
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        }
+        if ((threadIdx.x & 31) == 0) {
+            red[threadIdx.x >> 5] = mx;
+            red2[threadIdx.x >> 5] = ss;
+        }
         __syncthreads();
         mx = red[0];
-        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
+        ss = red2[0];
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) {
+            mx = fmaxf(mx, red[w]);
+            ss += red2[w];
+        }
         int k = 0;
         if (mx > 0.f && mx <= 3.402823466e38f) k = max(((__float_as_int(mx) >> 23) & 0xFF) - 127 - 14, -100);
         const float sc = __int_as_float((127 - k) << 23);  // 2^-k
-        if (threadIdx.x == 0) rowscale[row] = __int_as_float((127 + k) << 23);
+        if (threadIdx.x == 0) {
+            float rs = __int_as_float((127 + k) << 23);
+            if (act.kind == 1) rs *= 1.0f / sqrtf(ss / static_cast<float>(K) + act.eps);
+            rowscale[row] = rs;
+        }
         for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
             const int p0 = c * 8;
             const int g = p0 & ~255, pp = p0 & 255;
-            const float* xg = xr + g;
-            const int e0 = tc::tc_elem(F2, pp), e1 = tc::tc_elem(F2, pp + 4);
-            float4 a, b;
-            if (VEC) {
-                a = *reinterpret_cast<const float4*>(xg + e0);
-                b = *reinterpret_cast<const float4*>(xg + e1);
-            } else {
-                a = make_float4(xg[e0], xg[e0 + 1], xg[e0 + 2], xg[e0 + 3]);
-                b = make_float4(xg[e1], xg[e1 + 1], xg[e1 + 2], xg[e1 + 3]);
-            }
+            const int e0 = g + tc::tc_elem(F2, pp), e1 = g + tc::tc_elem(F2, pp + 4);
+            float4 x;
+            const float4 a = act4<VEC>(act, xr, rr, K, e0, x);
+            const float4 b = act4<VEC>(act, xr, rr, K, e1, x);
             uint4 o;
             o.x = tc::pack_h2(a.x * sc, a.y * sc);
             o.y = tc::pack_h2(a.z * sc, a.w * sc);
@@ -1290,7 +1340,8 @@ static cudaError_t launch_tc_fmt(const void* W, const __half* Xh, const float* r
 
 template <bool F2>
 static cudaError_t launch_x_to_f16(const float* X, __half* Xh, float* rowscale, int M, int K, int num_sms,
-                                   cudaStream_t s, unsigned* tcount = nullptr, int ncount = 0) {
+                                   cudaStream_t s, unsigned* tcount = nullptr, int ncount = 0,
+                                   const ActArgs& act = ActArgs{}) {
     const int grid = std::max(1, std::min(M, num_sms * 8));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
@@ -1301,9 +1352,10 @@ static cudaError_t launch_x_to_f16(const float* X, __half* Xh, float* rowscale, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if ((reinterpret_cast<uintptr_t>(X) & 15u) == 0)
-        return cudaLaunchKernelEx(&cfg, x_to_f16_kernel<F2, true>, X, Xh, rowscale, M, K, tcount, ncount);
-    return cudaLaunchKernelEx(&cfg, x_to_f16_kernel<F2, false>, X, Xh, rowscale, M, K, tcount, ncount);
+    auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    const bool vec = al(X) && al(act.R) && al(act.normw) && al(act.sum_out) && (act.ld <= 0 || act.ld % 4 == 0);
+    if (vec) return cudaLaunchKernelEx(&cfg, x_to_f16_kernel<F2, true>, X, Xh, rowscale, M, K, tcount, ncount, act);
+    return cudaLaunchKernelEx(&cfg, x_to_f16_kernel<F2, false>, X, Xh, rowscale, M, K, tcount, ncount, act);
 }
 
 static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
@@ -1330,10 +1382,10 @@ static void place_split(SplitK& sk, void* base, int64_t M, int64_t N, int64_t K)
 // X -> fp16 into Xh (M*K halves, K order of the format) with row scales rs
 // (M floats) and the split-K counters zeroed, then the GEMM.
 static cudaError_t gemm_tc_run(int type, const void* W, const float* X, __half* Xh, float* rs, float* Y, int M,
-                               int N, int K, int num_sms, cudaStream_t s, const SplitK& sk) {
+                               int N, int K, int num_sms, cudaStream_t s, const SplitK& sk, const ActArgs& act) {
     const int ncount = sk.ksplit > 1 ? static_cast<int>(split_tiles(M, N) * 4) : 0;
-    cudaError_t e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, M, K, num_sms, s, sk.tcount, ncount)
-                                        : launch_x_to_f16<false>(X, Xh, rs, M, K, num_sms, s, sk.tcount, ncount);
+    cudaError_t e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, M, K, num_sms, s, sk.tcount, ncount, act)
+                                        : launch_x_to_f16<false>(X, Xh, rs, M, K, num_sms, s, sk.tcount, ncount, act);
     if (e != cudaSuccess) return e;
     switch (type) {
         case Q4_0: return launch_tc_fmt<Q4_0>(W, Xh, rs, Y, M, N, K, num_sms, s, sk);
@@ -1375,7 +1427,7 @@ static cudaError_t scratch_pool(cudaMemPool_t* out) {
 }
 
 cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, int M, int N, int K, int refcpu,
-                           int num_sms, cudaStream_t s) {
+                           int num_sms, cudaStream_t s, const ActArgs& act) {
     if (!gemm_tc_supported(type, W, M, N, K, refcpu)) return cudaErrorNotSupported;
     const int64_t n = static_cast<int64_t>(M) * K;
     cudaMemPool_t pool = nullptr;
@@ -1386,7 +1438,7 @@ cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, in
     e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), scratch_bytes(M, N, K, sk), pool, s);
     if (e != cudaSuccess) return e;
     place_split(sk, Xh, M, N, K);
-    e = gemm_tc_run(type, W, X, Xh, reinterpret_cast<float*>(Xh + n), Y, M, N, K, num_sms, s, sk);
+    e = gemm_tc_run(type, W, X, Xh, reinterpret_cast<float*>(Xh + n), Y, M, N, K, num_sms, s, sk, act);
     cudaError_t e2 = cudaFreeAsync(Xh, s);
     return e != cudaSuccess ? e : e2;
 }
@@ -1474,7 +1526,7 @@ static cudaError_t noalloc_scratch(NoallocArrays* out) {
 }
 
 cudaError_t gemm_tc_launch_noalloc(int type, const void* W, const float* X, float* Y, int M, int N, int K,
-                                   int refcpu, int num_sms, cudaStream_t s) {
+                                   int refcpu, int num_sms, cudaStream_t s, const ActArgs& act) {
     if (!gemm_tc_supported(type, W, M, N, K, refcpu)) return cudaErrorNotSupported;
     if (static_cast<int64_t>(M) * K > SWQ_GEMM_NOALLOC_MAX_X_ELEMS) return cudaErrorInvalidValue;
     NoallocArrays a{};
@@ -1491,7 +1543,7 @@ cudaError_t gemm_tc_launch_noalloc(int type, const void* W, const float* X, floa
         sk.tcount = static_cast<unsigned*>(a.tcount);
     }
     return gemm_tc_run(type, W, X, static_cast<__half*>(a.x16), static_cast<float*>(a.rowscale), Y, M, N, K,
-                       num_sms, s, sk);
+                       num_sms, s, sk, act);
 }
 
 SWQ_DEFINE_STATUS_FETCH(gemm_tc)

@@ -5,15 +5,29 @@
 
 namespace swq {
 
+// Activation prologue of the conversion to fp16 (kinds as swq_act.kind): the
+// input row m of the GEMM is
+//   RMSNORM: x = X[m] (+ R[m]), then x * normw; 1/sqrt(mean(x^2) + eps) goes
+//            into the row's output scale, and x is written to sum_out when given
+//   SWIGLU:  silu(X[m*ld + k]) * X[m*ld + K + k]
+struct ActArgs {
+    int kind = 0;  // 0 none, 1 RMSNORM, 2 SWIGLU
+    const float* R = nullptr;
+    const float* normw = nullptr;
+    float eps = 0.f;
+    float* sum_out = nullptr;
+    int ld = 0;  // X row stride in elements (0: K)
+};
+
 // True when the tcgen05 GEMM serves this problem.
 bool gemm_tc_supported(int type, const void* W, int M, int N, int K, int refcpu);
 // Y[M x N] = X[M x K] . W[N x K]^T on tensor cores.
 cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, int M, int N, int K,
-                           int refcpu, int num_sms, cudaStream_t s);
+                           int refcpu, int num_sms, cudaStream_t s, const ActArgs& act = ActArgs{});
 // The same with the fp16 copy of X in libswq's fixed device array instead of a
 // stream-ordered allocation (swq_gemm_noalloc); M * K must fit that array.
 cudaError_t gemm_tc_launch_noalloc(int type, const void* W, const float* X, float* Y, int M, int N, int K,
-                                   int refcpu, int num_sms, cudaStream_t s);
+                                   int refcpu, int num_sms, cudaStream_t s, const ActArgs& act = ActArgs{});
 // MoE grouped GEMM: expert e multiplies rows offsets[e] .. offsets[e+1]-1 of X
 // (rows x K) by the GGUF matrix wptrs[e] (N x K) into the same rows of Y.
 // wptrs and offsets are device arrays of n_experts and n_experts + 1 entries.

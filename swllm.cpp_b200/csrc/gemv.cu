@@ -46,6 +46,28 @@ namespace swq {
 
 enum : int { MODE_PLAIN = 0, MODE_BULK_ROWS = 1, MODE_TMAP = 2 };
 
+// 8 consecutive floats (two float4 loads when VEC), and the store of 8
+__device__ __forceinline__ void load8(const float* p, float (&v)[8], bool vec) {
+    if (vec) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+        const float4 c = __ldg(reinterpret_cast<const float4*>(p + 4));
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __ldg(p + i);
+    }
+}
+__device__ __forceinline__ void store8(float* p, const float (&v)[8], bool vec) {
+    if (vec) {
+        reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) p[i] = v[i];
+    }
+}
+
 struct GemvParams {
     const uint8_t* W;
     const float* X;
@@ -65,6 +87,16 @@ struct GemvParams {
     int x_vec;   // X rows 16-byte aligned: float4 activation loads
     int xstride; // bytes per activation row in shared memory
     uint32_t off_xq, off_ring;  // smem offsets
+    // activation prologue (ACT_*): the GEMV's input row m is
+    //   RMSNORM: x = X[m] (+ R[m]), then x * normw (the 1/rms of x scales the
+    //            outputs of row m); CTA 0 writes x to sum_out when given
+    //   SWIGLU:  silu(X[m*ld + k]) * X[m*ld + K + k]
+    int act;
+    const float* R;
+    const float* normw;
+    float eps;
+    float* sum_out;
+    int ld;  // X row stride in elements (SWIGLU), else K
 };
 
 // dp2a with a signed 16-bit pair and four 8-bit values, unsigned or signed.
@@ -204,7 +236,8 @@ __device__ __forceinline__ void unit_dot2(const uint8_t* blkA, const uint8_t* bl
 }
 
 template <int MT>
-__device__ __forceinline__ void row_store(float (&acc)[MT], int lane, float* Y, int M, int N, int row) {
+__device__ __forceinline__ void row_store(float (&acc)[MT], int lane, float* Y, int M, int N, int row,
+                                          const float* rscale) {
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
         float v = acc[m];
@@ -213,7 +246,7 @@ __device__ __forceinline__ void row_store(float (&acc)[MT], int lane, float* Y, 
         v += __shfl_xor_sync(0xffffffffu, v, 4);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
         v += __shfl_xor_sync(0xffffffffu, v, 1);
-        if (lane == 0 && m < M) Y[static_cast<size_t>(m) * N + row] = v;
+        if (lane == 0 && m < M) Y[static_cast<size_t>(m) * N + row] = rscale ? v * rscale[m] : v;
         acc[m] = 0.f;
     }
 }
@@ -323,6 +356,11 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
     constexpr int NCT = NCW * 32;
     const int ctid = threadIdx.x;
     const bool refcpu = p.refcpu != 0;
+    const bool rms = p.act == ACT_RMSNORM;
+    __shared__ float s_sq[NCW][MT];  // RMSNORM: each warp's sum of squares of each input row
+    float sqm[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) sqm[m] = 0.f;
 
     // Activation prep: item = 8 consecutive elements of one row (one 16-byte
     // chunk of one unit part).  Four lanes hold one 32-element block (scale);
@@ -344,15 +382,31 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
 #pragma unroll
                 for (int i = 0; i < 8; ++i) v[h][i] = 0.f;
                 if (act[h] && mm[h] < p.M) {
-                    const float* xp = p.X + static_cast<size_t>(mm[h]) * p.K + kk[h];
-                    if (p.x_vec) {
-                        const float4 a = __ldg(reinterpret_cast<const float4*>(xp));
-                        const float4 c = __ldg(reinterpret_cast<const float4*>(xp + 4));
-                        v[h][0] = a.x; v[h][1] = a.y; v[h][2] = a.z; v[h][3] = a.w;
-                        v[h][4] = c.x; v[h][5] = c.y; v[h][6] = c.z; v[h][7] = c.w;
-                    } else {
+                    const size_t xo = static_cast<size_t>(mm[h]) * p.ld + kk[h];
+                    load8(p.X + xo, v[h], p.x_vec);
+                    if (p.act == ACT_SWIGLU) {
+                        float u[8];
+                        load8(p.X + xo + p.K, u, p.x_vec);
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) v[h][i] = __ldg(xp + i);
+                        for (int i = 0; i < 8; ++i) v[h][i] = v[h][i] / (1.0f + expf(-v[h][i])) * u[i];
+                    } else if (rms) {
+                        const size_t ro = static_cast<size_t>(mm[h]) * p.K + kk[h];
+                        if (p.R) {
+                            float r[8];
+                            load8(p.R + ro, r, p.x_vec);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) v[h][i] += r[i];
+                        }
+                        if (p.sum_out && blockIdx.x == 0) store8(p.sum_out + ro, v[h], p.x_vec);
+                        float sq = 0.f, w[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) sq = fmaf(v[h][i], v[h][i], sq);
+#pragma unroll
+                        for (int m = 0; m < MT; ++m)
+                            if (m == mm[h]) sqm[m] += sq;
+                        load8(p.normw + kk[h], w, p.x_vec);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[h][i] *= w[i];
                     }
                 }
             }
@@ -399,7 +453,27 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
             }
         }
     }
+    if (rms) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            float t = sqm[m];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+            if ((ctid & 31) == 0) s_sq[ctid >> 5][m] = t;
+        }
+    }
     named_bar_sync(1, NCT);
+    // RMSNORM: outputs of row m scale by 1 / sqrt(mean(x^2) + eps); the warps'
+    // sums are added in warp order, so every CTA and every run agree.
+    float rsv[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        float t = 0.f;
+        if (rms)
+            for (int w = 0; w < NCW; ++w) t += s_sq[w][m];
+        rsv[m] = rms ? 1.0f / sqrtf(t / static_cast<float>(p.K) + p.eps) : 1.f;
+    }
+    const float* rsc = rms ? rsv : nullptr;
 
     float accA[MT], accB[MT];
 #pragma unroll
@@ -428,15 +502,15 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
                         const int kbl = uu / UPB, c = uu - kbl * UPB;
                         unit_dot2<T, MT>(rowA + kbl * BB, rowB + kbl * BB, c, uu, xq, p.xstride, accA, accB);
                     }
-                    row_store<MT>(accA, lane, p.Y, p.M, p.N, rg + r0);
-                    row_store<MT>(accB, lane, p.Y, p.M, p.N, rg + r0 + NCW);
+                    row_store<MT>(accA, lane, p.Y, p.M, p.N, rg + r0, rsc);
+                    row_store<MT>(accB, lane, p.Y, p.M, p.N, rg + r0 + NCW, rsc);
                 } else {
 #pragma unroll 2
                     for (int uu = lane; uu < nu; uu += 32) {
                         const int kbl = uu / UPB, c = uu - kbl * UPB;
                         unit_dot<T, MT>(rowA + kbl * BB, c, uu, xq, p.xstride, accA);
                     }
-                    row_store<MT>(accA, lane, p.Y, p.M, p.N, rg + r0);
+                    row_store<MT>(accA, lane, p.Y, p.M, p.N, rg + r0, rsc);
                 }
             }
             __syncwarp();
@@ -485,8 +559,8 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
             }
         }
         if (!ok) break;
-        if (hasA) row_store<MT>(accA, lane, p.Y, p.M, p.N, rg + warp);
-        if (hasB) row_store<MT>(accB, lane, p.Y, p.M, p.N, rg + warp + NCW);
+        if (hasA) row_store<MT>(accA, lane, p.Y, p.M, p.N, rg + warp, rsc);
+        if (hasB) row_store<MT>(accB, lane, p.Y, p.M, p.N, rg + warp + NCW, rsc);
     }
 }
 
@@ -533,7 +607,15 @@ static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
     p.row_bytes = p.nb * F::BB;
     p.refcpu = L.refcpu;
     p.early = L.early;
-    p.x_vec = (reinterpret_cast<uintptr_t>(L.X) & 15u) == 0 ? 1 : 0;  // K % 32 keeps rows aligned
+    p.act = L.act;
+    p.R = L.R;
+    p.normw = L.normw;
+    p.eps = L.eps;
+    p.sum_out = L.sum_out;
+    p.ld = L.ld > 0 ? L.ld : (L.act == ACT_SWIGLU ? 2 * L.K : L.K);
+    // float4 activation loads: every row start 16-byte aligned (K % 32 == 0)
+    auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    p.x_vec = (al(L.X) && al(L.R) && al(L.normw) && al(L.sum_out) && p.ld % 4 == 0) ? 1 : 0;
     p.xstride = XLay<T>::row_bytes(L.K);
 
     const int per_sm = L.ctas_per_sm > 0 ? L.ctas_per_sm : 1;
@@ -547,11 +629,15 @@ static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
     off += x_area_bytes_t<T>(MT, L.K);
     off = align_up(off, 128);
     p.off_ring = off;
-    const uint32_t smem_cap = static_cast<uint32_t>(L.smem_per_block_optin);
+    // (1 KB stays free for the kernel's static shared memory)
+    const uint32_t smem_cap = static_cast<uint32_t>(L.smem_per_block_optin) - 1024;
     // Two CTAs per SM: this kernel's and the next one's.
-    const uint32_t half_sm = static_cast<uint32_t>(L.smem_per_sm) / 2 - 1024;
+    // Two CTAs per SM (this kernel's and the next one's) must fit beside each
+    // other with their static shared memory and the 1 KB the SM reserves per CTA.
+    constexpr uint32_t kStatic = 1024 + sizeof(float) * Cfg<MT>::NCW * MT;
+    const uint32_t half_sm = static_cast<uint32_t>(L.smem_per_sm) / 2 - kStatic;
     uint32_t budget = (off + 32 * 1024 <= half_sm) ? half_sm : smem_cap;
-    if (per_sm > 1) budget = std::min(smem_cap, static_cast<uint32_t>(L.smem_per_sm) / per_sm - 1024);
+    if (per_sm > 1) budget = std::min(smem_cap, static_cast<uint32_t>(L.smem_per_sm) / per_sm - kStatic);
     if (L.smem_kb > 0) budget = std::min(smem_cap, static_cast<uint32_t>(L.smem_kb) * 1024u);
     if (off >= budget) return cudaErrorInvalidConfiguration;
     const uint32_t ring_cap = budget - off;

@@ -16,6 +16,9 @@ struct DeviceInfo {
     int cc_major = 0, cc_minor = 0;
 };
 
+// Activation prologue kinds (values of swq_act.kind).
+enum : int { ACT_NONE = 0, ACT_RMSNORM = 1, ACT_SWIGLU = 2 };
+
 struct GemvLaunch {
     int type;
     const void* W;
@@ -30,6 +33,13 @@ struct GemvLaunch {
     int smem_kb;   // CTA shared-memory budget in KB (0: automatic)
     int stage_kb;  // largest weight stage in KB (0: 96)
     int ctas_per_sm;  // 0: automatic
+    // activation prologue (ACT_*); ld = X row stride in elements (0: K, SWIGLU: 2K)
+    int act = ACT_NONE;
+    const float* R = nullptr;
+    const float* normw = nullptr;
+    float eps = 0.f;
+    float* sum_out = nullptr;
+    int ld = 0;
 };
 
 // Fused dequant + GEMV for M <= 8 activation rows.

@@ -17,10 +17,12 @@ from __future__ import annotations
 from .lib import (  # noqa: F401
     Q2_K, Q3_K, Q4_0, Q4_K, Q5_K, Q6_K, Q8_0, TYPES, TYPE_NAMES,
     OPT_EARLY_WEIGHT_PREFETCH, OPT_GEMV_MAX_M, OPT_Q2K_REFERENCE_CPU_ORDER, OPT_TENSOR_CORE_GEMM,
-    OPT_TENSOR_CORE_MIN_M, OPT_GEMV_SMEM_KB, OPT_GEMV_STAGE_KB, OPT_GEMV_CTAS_PER_SM, add, add_rmsnorm, argmax, attention_decode, attention_workspace_bytes, decode_advance, embed,
+    OPT_TENSOR_CORE_MIN_M, OPT_GEMV_SMEM_KB, OPT_GEMV_STAGE_KB, OPT_GEMV_CTAS_PER_SM,
+    ACT_NONE, ACT_RMSNORM, ACT_SWIGLU,
+    add, add_rmsnorm, argmax, attention_decode, attention_workspace_bytes, decode_advance, embed,
     rmsnorm, rope_kv, silu_mul,
     GEMM_NOALLOC_MAX_X_ELEMS, SwqError, Status, block_size, build, check, dequant, exported_symbols, gemm,
-    gemm_noalloc, gemv, grouped_gemm,
+    gemm_act, gemm_noalloc, gemv, grouped_gemm,
     get_option, header_symbols, lib, lib_path, set_option, type_size,
 )
 from .compute import Backend, Compute, QuantWeight, dequantize  # noqa: F401

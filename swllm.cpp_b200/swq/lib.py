@@ -79,6 +79,7 @@ def lib() -> ctypes.CDLL:
         "swq_gemv": (i32, [i32, vp, vp, vp, i32, i32, vp]),
         "swq_gemm": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
         "swq_gemm_noalloc": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
+        "swq_gemm_act": (i32, [i32, vp, vp, vp, i32, i32, i32, ctypes.POINTER(ActArgs), i32, vp]),
         "swq_grouped_gemm": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "swq_rmsnorm": (i32, [vp, vp, vp, i32, ctypes.c_float, i32, vp]),
         "swq_add_rmsnorm": (i32, [vp, vp, vp, vp, i32, ctypes.c_float, i32, vp]),
@@ -192,6 +193,28 @@ def grouped_gemm(type_id: int, w_ptrs, offsets, X, Y, n_experts: int, total_rows
     addresses; offsets: device int32 tensor of n_experts + 1 row offsets."""
     _raise(lib().swq_grouped_gemm(type_id, _ptr(w_ptrs), _ptr(offsets), _ptr(X), _ptr(Y), n_experts, total_rows,
                                   N, K, _stream(stream)))
+
+
+ACT_NONE, ACT_RMSNORM, ACT_SWIGLU = 0, 1, 2
+GEMM_NOALLOC = 1
+
+
+class ActArgs(ctypes.Structure):
+    """swq_act (include/swq.h)."""
+    _fields_ = [("kind", ctypes.c_int), ("residual", ctypes.c_void_p), ("norm_w", ctypes.c_void_p),
+                ("eps", ctypes.c_float), ("sum_out", ctypes.c_void_p), ("ld", ctypes.c_int)]
+
+
+def gemm_act(type_id: int, W, X, Y, M: int, N: int, K: int, kind: int = ACT_NONE, residual=None, norm_w=None,
+             eps: float = 0.0, sum_out=None, ld: int = 0, noalloc: bool = False, stream=None) -> None:
+    """gemm() on a transformed X (swq_gemm_act): RMSNORM of X (+ residual),
+    weights norm_w, the sum written to sum_out; or SWIGLU of the gate/up row
+    halves (row stride ld, 0 = 2K)."""
+    a = ActArgs(kind, _ptr(residual) if residual is not None else None,
+                _ptr(norm_w) if norm_w is not None else None, eps,
+                _ptr(sum_out) if sum_out is not None else None, ld)
+    _raise(lib().swq_gemm_act(type_id, _ptr(W), _ptr(X), _ptr(Y), M, N, K, ctypes.byref(a),
+                              GEMM_NOALLOC if noalloc else 0, _stream(stream)))
 
 
 def gemm_noalloc(type_id: int, W, X, Y, M: int, N: int, K: int, stream=None) -> None:

@@ -6,10 +6,10 @@ embedding row, per layer RMSNorm, q/k/v GEMVs, RoPE + KV-cache append,
 grouped-query attention, o GEMV, residual, RMSNorm, gate+up GEMV, SiLU-mul,
 down GEMV, residual; final RMSNorm, LM-head GEMV and greedy argmax.  Matrices
 of one type that read the same input are stacked into one GEMV (q with k,
-gate with up), and every residual add runs in one kernel with the RMSNorm
-after it.  `rows` sequences
-decode in step.  The position lives in device memory, so one decode step is
-captured once in a CUDA graph and replayed per token.
+gate with up), and every residual add runs in one pass with the RMSNorm
+after it (optionally inside the projection that reads the norm).  `rows`
+sequences decode in step.  The position lives in device memory, so one
+decode step is captured once in a CUDA graph and replayed per token.
 
 Weights are GGUF blocks in device memory: either given (host arrays, for the
 tests) or synthetic -- seeded random blocks with the benchmark's value
@@ -34,9 +34,9 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import lib as _lib_mod  # noqa: F401  (module import for the ctypes table)
-from .lib import (GEMM_NOALLOC_MAX_X_ELEMS, OPT_TENSOR_CORE_MIN_M, add_rmsnorm, argmax, attention_decode,
-                  attention_workspace_bytes, decode_advance, embed, gemm, gemm_noalloc, get_option, rmsnorm,
-                  rope_kv, silu_mul)
+from .lib import (ACT_NONE, ACT_RMSNORM, ACT_SWIGLU, GEMM_NOALLOC_MAX_X_ELEMS, OPT_TENSOR_CORE_MIN_M, argmax,
+                  add_rmsnorm, attention_decode, attention_workspace_bytes, decode_advance, embed, gemm_act,
+                  get_option, rmsnorm, rope_kv, silu_mul)
 from .synth import LAYOUT, Q4_K, Q6_K, Q8_0, row_bytes
 
 
@@ -122,7 +122,7 @@ def _shard(host, type_id: int, N: int, K: int, rows: tuple[int, int] | None, col
 class LlamaDecoder:
     def __init__(self, cfg: LlamaConfig, rows: int = 1, device="cuda", seed: int = 0, weights: dict | None = None,
                  max_steps: int = 4096, group=None, weights_from: "LlamaDecoder | None" = None,
-                 collective: str = "peer"):
+                 collective: str = "peer", fuse: tuple | str = "auto"):
         """weights: None for synthetic weights, else host arrays: 'token_embd'
         [vocab, dim] fp32, 'output_norm' [dim], 'output' blocks, and per layer
         'layers'[l] with 'attn_norm', 'ffn_norm' [dim] fp32 and the blocks of
@@ -132,7 +132,14 @@ class LlamaDecoder:
         weights_from: a decoder of the same config and group whose device
         weights this one shares (another batch size of the same model).
         collective: "peer" (libswq's one-shot all-reduce over peer memory)
-        or "nccl" (torch.distributed.all_reduce) for the o/down sums."""
+        or "nccl" (torch.distributed.all_reduce) for the o/down sums.
+        fuse: activation transforms run inside the projection that reads them
+        (swq_gemm_act) instead of as their own pass -- "rmsnorm" (with the
+        residual add), "swiglu".  "auto": RMSNorm inside the projections when
+        the tensor-core GEMM serves them (one CTA per row converts the
+        activations), nothing on the GEMV path (every GEMV CTA would repeat
+        the whole row's transform; measured slower), SwiGLU never (slower on
+        both paths)."""
         import torch
         from .parallel import _world
         self.cfg, self.rows, self.device = cfg, rows, torch.device(device)
@@ -180,6 +187,11 @@ class LlamaDecoder:
         if collective not in ("peer", "nccl"):
             raise ValueError(f"collective must be 'peer' or 'nccl', not {collective!r}")
         self.collective = collective
+        if fuse == "auto":
+            fuse = ("rmsnorm",) if rows >= get_option(OPT_TENSOR_CORE_MIN_M) else ()
+        if not set(fuse) <= {"rmsnorm", "swiglu"}:
+            raise ValueError(f"fuse takes 'rmsnorm' and 'swiglu', not {fuse!r}")
+        self.fuse = tuple(fuse)
         self._peer = None
         if G > 1 and collective == "peer":
             from .comm import PeerAllReduce
@@ -218,7 +230,9 @@ class LlamaDecoder:
         dev, G = self.device, self.world
         B = rows
         self.x = torch.zeros((B, cfg.dim), **f32)
-        self.xb = torch.zeros_like(self.x)
+        self.x2 = torch.zeros_like(self.x)    # fused norms: the residual stream alternates between x and x2
+        self.xb = torch.zeros_like(self.x)    # output of the o / down projection (added to the residual)
+        self.xn = torch.zeros_like(self.x)    # the normalized input of the next projection
         self.qk = torch.zeros((B, self.q_dim + self.kv_dim), **f32)  # q then k, per row
         self.v = torch.zeros((B, self.kv_dim), **f32)
         self.att = torch.zeros((B, self.q_dim), **f32)
@@ -253,17 +267,22 @@ class LlamaDecoder:
         self.logits.view(self.rows, self.world, self.vocab).copy_(self.logits_g.transpose(0, 1))
 
     # ------------------------------------------------------------ one token
-    def _gemm(self, type_id, W, X, Y, M, N, K, stream):
+    def _gemm(self, type_id, W, X, Y, M, N, K, stream, kind=ACT_NONE, residual=None, norm_w=None, sum_out=None,
+              ld=0):
         # Rows that take the tensor-core GEMM use its allocation-free form, so
         # a captured step holds no allocation (one stream orders the calls).
-        if M >= get_option(OPT_TENSOR_CORE_MIN_M) and M * K <= GEMM_NOALLOC_MAX_X_ELEMS:
-            gemm_noalloc(type_id, W, X, Y, M, N, K, stream=stream)
-        else:
-            gemm(type_id, W, X, Y, M, N, K, stream=stream)
+        noalloc = M >= get_option(OPT_TENSOR_CORE_MIN_M) and M * K <= GEMM_NOALLOC_MAX_X_ELEMS
+        gemm_act(type_id, W, X, Y, M, N, K, kind=kind, residual=residual, norm_w=norm_w, eps=self.cfg.eps,
+                 sum_out=sum_out, ld=ld, noalloc=noalloc, stream=stream)
 
     def step(self, greedy: bool = True) -> None:
         """One decode step for all rows at position *pos: logits of the current
-        tokens; with greedy, tokens <- argmax (also into history) and pos += 1."""
+        tokens; with greedy, tokens <- argmax (also into history) and pos += 1.
+
+        The residual stream is x; d holds the output of the last o or down
+        projection, added to x by the RMSNorm pass that follows it (or, with
+        fuse=("rmsnorm",), by the projection that reads the norm, which then
+        writes the sum to x2 and the stream alternates between x and x2)."""
         c, B, s = self.cfg, self.rows, self.stream
         t = c.types
         gemm = self._gemm  # noqa: F811
@@ -271,46 +290,71 @@ class LlamaDecoder:
         tp = self.world > 1
         ld = qd + kvd
         q, k = self.qk, self.qk[:, qd:]
-        embed(self.x, self.token_embd, self.tokens, c.dim, c.vocab, B, stream=s)
-        rmsnorm(self.xb, self.x, self.layers[0]["attn_norm"], c.dim, c.eps, B, stream=s)
+        fuse_rms, fuse_glu = "rmsnorm" in self.fuse, "swiglu" in self.fuse
+        x, x2, d, xb = self.x, self.x2, self.xb, self.xn
+        embed(x, self.token_embd, self.tokens, c.dim, c.vocab, B, stream=s)
+        if not fuse_rms:
+            rmsnorm(xb, x, self.layers[0]["attn_norm"], c.dim, c.eps, B, stream=s)
+        pending = None  # fused: d to add to the residual before the next norm
         for li, L in enumerate(self.layers):
-            if self.fuse_qk:
-                gemm(t["wq"], L["w_qk"], self.xb, self.qk, B, ld, c.dim, stream=s)
+            # q, k, v of norm(x) (fused: x2 = x + pending first)
+            if fuse_rms:
+                src, a_in = x, dict(kind=ACT_RMSNORM, residual=pending, norm_w=L["attn_norm"])
+                a_qk = dict(a_in, sum_out=x2)
             else:
-                gemm(t["wq"], L["wq"], self.xb, self.att, B, qd, c.dim, stream=s)
+                src, a_in, a_qk = xb, {}, {}
+            if self.fuse_qk:
+                gemm(t["wq"], L["w_qk"], src, self.qk, B, ld, c.dim, stream=s, **a_qk)
+            else:
+                gemm(t["wq"], L["wq"], src, self.att, B, qd, c.dim, stream=s, **a_qk)
                 q[:, :qd].copy_(self.att)
-                gemm(t["wk"], L["wk"], self.xb, self.v, B, kvd, c.dim, stream=s)
+                gemm(t["wk"], L["wk"], src, self.v, B, kvd, c.dim, stream=s, **a_in)
                 k.copy_(self.v)
-            gemm(t["wv"], L["wv"], self.xb, self.v, B, kvd, c.dim, stream=s)
+            gemm(t["wv"], L["wv"], src, self.v, B, kvd, c.dim, stream=s, **a_in)
             kc, vc = self.kcache[li], self.vcache[li]
             rope_kv(q, k, self.v, kc, vc, self.pos, self.freqs, qd, kvd, c.head_dim, c.head_dim,
                     c.rope_neox, B, c.max_seq, ldq=ld, ldk=ld, stream=s)
             attention_decode(self.att, q, kc, vc, self.pos, self.ws, self.ws_bytes, self.nh, self.nkv,
                              c.head_dim, B, c.max_seq, ldq=ld, stream=s)
-            gemm(t["wo"], L["wo"], self.att, self.xb, B, c.dim, qd, stream=s)
+            gemm(t["wo"], L["wo"], self.att, d, B, c.dim, qd, stream=s)
             if tp:
-                self.all_reduce(self.xb)
-            add_rmsnorm(self.xb, self.x, self.xb, L["ffn_norm"], c.dim, c.eps, B, stream=s)  # x += o; xb = norm(x)
-            if self.fuse_gate_up:
-                gemm(t["w_gate"], L["w_gate_up"], self.xb, self.gu, B, 2 * ffn, c.dim, stream=s)
+                self.all_reduce(d)
+            # gate, up of norm(residual + o)
+            if fuse_rms:
+                src, a_in = x2, dict(kind=ACT_RMSNORM, residual=d, norm_w=L["ffn_norm"])
+                a_g = dict(a_in, sum_out=x)
             else:
-                gemm(t["w_gate"], L["w_gate"], self.xb, self.h, B, ffn, c.dim, stream=s)
+                add_rmsnorm(xb, x, d, L["ffn_norm"], c.dim, c.eps, B, stream=s)  # x += o; xb = norm(x)
+                src, a_in, a_g = xb, {}, {}
+            if self.fuse_gate_up:
+                gemm(t["w_gate"], L["w_gate_up"], src, self.gu, B, 2 * ffn, c.dim, stream=s, **a_g)
+            else:
+                gemm(t["w_gate"], L["w_gate"], src, self.h, B, ffn, c.dim, stream=s, **a_g)
                 self.gu[:, :ffn].copy_(self.h)
-                gemm(t["w_up"], L["w_up"], self.xb, self.h, B, ffn, c.dim, stream=s)
+                gemm(t["w_up"], L["w_up"], src, self.h, B, ffn, c.dim, stream=s, **a_in)
                 self.gu[:, ffn:].copy_(self.h)
-            silu_mul(self.h, self.gu, self.gu[:, ffn:], ffn, B, 2 * ffn, stream=s)
-            gemm(t["w_down"], L["w_down"], self.h, self.xb, B, c.dim, ffn, stream=s)
+            if fuse_glu:
+                gemm(t["w_down"], L["w_down"], self.gu, d, B, c.dim, ffn, stream=s, kind=ACT_SWIGLU, ld=2 * ffn)
+            else:
+                silu_mul(self.h, self.gu, self.gu[:, ffn:], ffn, B, 2 * ffn, stream=s)
+                gemm(t["w_down"], L["w_down"], self.h, d, B, c.dim, ffn, stream=s)
             if tp:
-                self.all_reduce(self.xb)
-            if li + 1 < len(self.layers):  # x += down; xb = next layer's attention norm of x
-                add_rmsnorm(self.xb, self.x, self.xb, self.layers[li + 1]["attn_norm"], c.dim, c.eps, B, stream=s)
-            else:  # x += down; x = output norm of x
-                add_rmsnorm(self.x, self.x, self.xb, self.output_norm, c.dim, c.eps, B, stream=s)
+                self.all_reduce(d)
+            if fuse_rms:
+                pending = d
+            elif li + 1 < len(self.layers):  # x += down; xb = next layer's attention norm of x
+                add_rmsnorm(xb, x, d, self.layers[li + 1]["attn_norm"], c.dim, c.eps, B, stream=s)
+            else:  # x += down; xb = output norm of x
+                add_rmsnorm(xb, x, d, self.output_norm, c.dim, c.eps, B, stream=s)
+        if fuse_rms:
+            src, a_out = x, dict(kind=ACT_RMSNORM, residual=pending, norm_w=self.output_norm)
+        else:
+            src, a_out = xb, {}
         if tp:
-            gemm(t["output"], self.output, self.x, self.logits_l, B, self.vocab, c.dim, stream=s)
+            gemm(t["output"], self.output, src, self.logits_l, B, self.vocab, c.dim, stream=s, **a_out)
             self._gather_logits()
         else:
-            gemm(t["output"], self.output, self.x, self.logits, B, c.vocab, c.dim, stream=s)
+            gemm(t["output"], self.output, src, self.logits, B, c.vocab, c.dim, stream=s, **a_out)
         if greedy:
             argmax(self.logits, c.vocab, B, self.tokens, self.history, self.step_no, stream=s)
             decode_advance(self.pos, self.step_no, stream=s)
