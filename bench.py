@@ -43,6 +43,7 @@ for _p in (str(REPO), str(REPO / "swllm.cpp_b200")):
         sys.path.insert(0, _p)
 
 METRIC = "Q4_K GEMV achieved HBM GB/s (% peak); decode tok/s at 1/2/4/8 B200"
+DECODE_DEADLINE_S = 420  # all decode measurements of the default run (about 60 s on one GPU)
 N_ROWS, K_COLS, M_ROWS = 4096, 4096, 1
 COPIES = 64
 Q4_K = 12
@@ -56,8 +57,11 @@ WORKLOAD = (f"Q4_K GEMV N={N_ROWS} K={K_COLS} M={M_ROWS}, {COPIES} rotating weig
 NCU_TRAFFIC_PER_LAUNCH = 9_496_832
 
 
+_T0 = time.time()
+
+
 def log(*a):
-    print(*a, file=sys.stderr, flush=True)
+    print(f"[{time.time() - _T0:7.1f}s]", *a, file=sys.stderr, flush=True)
 
 
 def load_peaks() -> tuple[float, str]:
@@ -195,6 +199,7 @@ def run_swq(args, rank: int, world: int) -> None:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
 
+    log(f"gemv: rank {rank}/{world} building {COPIES} weight copies")
     # Weights: COPIES distinct seeded matrices per rank, resident in HBM.
     host_ws = [synth.random_blocks(Q4_K, N_ROWS, K_COLS, seed=10_000 * rank + i) for i in range(COPIES)]
     d_ws = [torch.from_numpy(w.reshape(-1)).to(dev) for w in host_ws]
@@ -226,6 +231,7 @@ def run_swq(args, rank: int, world: int) -> None:
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
+    log(f"gemv: timing {args.steps} steps")
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(gpu_uuid) as clk:
         with torch.cuda.stream(stream):
@@ -275,9 +281,6 @@ def run_swq(args, rank: int, world: int) -> None:
     if not np.allclose(out, y_last, rtol=1e-5, atol=1e-4):
         raise RuntimeError("host-buffer path disagrees with the device path")
 
-    decode = run_decode(rank, world, steps=128) if args.decode else None
-    decode_tp = run_decode_tp(rank, world) if args.decode else None
-
     line = None
     if rank == 0:
         cpu = None
@@ -307,10 +310,36 @@ def run_swq(args, rank: int, world: int) -> None:
                     "steps": e2e_steps},
             "gpu_launches": launches,
             "clocks": clk.summary(),
-            "decode": decode,
-            "decode_70b": decode_tp,
+            "decode": None,
+            "decode_70b": None,
         }
     del graph
+
+    # The decode measurements run under a deadline: if one does not finish
+    # (a collective that never completes), rank 0 prints the line with what
+    # was measured and a note, and every rank leaves.  Every device-side wait
+    # of libswq is bounded, so leaving the process releases the GPU.
+    import threading
+
+    def _deadline():
+        if line is not None:
+            line["decode_timeout"] = f"decode measurements did not finish within {DECODE_DEADLINE_S} s"
+            print(json.dumps(line), flush=True)
+        log("decode deadline reached; exiting")
+        os._exit(0 if line is not None or rank != 0 else 1)
+
+    timer = threading.Timer(DECODE_DEADLINE_S, _deadline)
+    timer.daemon = True
+    timer.start()
+    if args.decode:
+        log("gemv: done; decode next")
+        decode = run_decode(rank, world, steps=128)
+        if line is not None:
+            line["decode"] = decode
+        decode_tp = run_decode_tp(rank, world)
+        if line is not None:
+            line["decode_70b"] = decode_tp
+    timer.cancel()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -338,6 +367,7 @@ def run_decode(rank: int, world: int, batches=(1, 16), prefill: int = 512, steps
     if world > 1:
         import torch.distributed as dist
     for B in batches:
+        log(f"decode8b: batch {B} (one model per rank)")
         dec = LlamaDecoder(cfg, rows=B, seed=100 + rank)
         dec.reset(list(range(B)), 0)
         dec.capture()
@@ -394,14 +424,20 @@ def run_decode_tp(rank: int, world: int, batches=(1, 8, 32), context: int = 2048
         import torch.distributed as dist
     base = None
     for B in batches:
-        dec = LlamaDecoder(cfg, rows=B, seed=7, weights_from=base, collective=collective)
+        log(f"decode70b: tp={world} batch {B}: building")
+        dec = LlamaDecoder(cfg, rows=B, seed=7, weights_from=base, collective=collective,
+                           group=dist.group.WORLD if dist else None)
         base = base or dec
         dec.reset(list(range(B)), 0)
         dec.capture()
+        import swq
+        swq.check(dec.stream)  # a collective that timed out fails here, not in the timed loop
+        log(f"decode70b: tp={world} batch {B}: captured")
         dec.reset([(7 * i + 1) % cfg.vocab for i in range(B)], 0)
         dec.fill_kv(context)
         dec.generate(warmup)
         dec.stream.synchronize()
+        swq.check(dec.stream)
         if dist:
             dist.barrier()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

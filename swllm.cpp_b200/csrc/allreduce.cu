@@ -20,8 +20,9 @@
 // before every peer has published e + 1, which each does only after it has
 // finished reading epoch e.
 //
-// Every wait is bounded (kWaitLimitNs); on timeout the CTA records
-// DEV_TIMEOUT_PEER in the device status word and returns.
+// Every wait is bounded (kPeerWaitNs, 50 ms: a peer that is alive arrives
+// within microseconds); on timeout the CTA records DEV_TIMEOUT_PEER in the
+// device status word and returns, so a broken group fails fast.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -36,6 +37,7 @@ namespace swq {
 namespace {
 
 constexpr int AR_THREADS = 512;
+constexpr uint64_t kPeerWaitNs = 50ull * 1000ull * 1000ull;
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -90,7 +92,7 @@ __global__ void __launch_bounds__(AR_THREADS) allreduce_kernel(const ArArgs a) {
             const uint64_t t0 = globaltimer_ns();
             for (uint32_t i = 1;; ++i) {
                 if (static_cast<int>(ld_acquire_sys(f) - epoch) >= 0) break;
-                if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+                if ((i & 63u) == 0 && globaltimer_ns() - t0 > kPeerWaitNs) {
                     atomicOr(&g_swq_dev_status, DEV_TIMEOUT_PEER);
                     s_ok = 0;
                     break;

@@ -16,6 +16,28 @@ from .lib import _raise, lib, _ptr, _stream
 HANDLE_BYTES = 64
 
 
+_SHARED: dict = {}
+
+
+def shared_peer_allreduce(max_elems: int, group=None, device=None) -> "PeerAllReduce":
+    """One PeerAllReduce per (group, device), grown when a caller needs more
+    elements and never freed while the process runs: buffers that other
+    processes have mapped are not released and re-allocated between decoders
+    (a new allocation could reuse an address a peer still maps).  Every rank
+    must make the same calls in the same order."""
+    import torch
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    key = (id(group), dev.index)
+    ar = _SHARED.get(key)
+    if ar is None or ar.max_elems < max_elems:
+        ar = PeerAllReduce(max_elems, group=group, device=dev)
+        _SHARED.setdefault(("retired", key), []).append(_SHARED.get(key))
+        _SHARED[key] = ar
+    return ar
+
+
 class PeerAllReduce:
     def __init__(self, max_elems: int, group=None, device=None):
         import torch

@@ -128,7 +128,7 @@ class LlamaDecoder:
         'layers'[l] with 'attn_norm', 'ffn_norm' [dim] fp32 and the blocks of
         wq wk wv wo w_gate w_up w_down (whole matrices; each rank keeps its
         shard).  group: torch.distributed group for tensor parallelism (None:
-        the default group when one is initialised with more than one rank).
+        this process alone, whatever process groups exist).
         weights_from: a decoder of the same config and group whose device
         weights this one shares (another batch size of the same model).
         collective: "peer" (libswq's one-shot all-reduce over peer memory)
@@ -144,7 +144,7 @@ class LlamaDecoder:
         from .parallel import _world
         self.cfg, self.rows, self.device = cfg, rows, torch.device(device)
         self.group = group
-        self.rank, self.world = _world(group)
+        self.rank, self.world = _world(group) if group is not None else (0, 1)
         G, r = self.world, self.rank
         for what, n in (("query heads", cfg.n_heads), ("kv heads", cfg.n_kv_heads), ("ffn", cfg.ffn),
                         ("vocab", cfg.vocab)):
@@ -194,8 +194,8 @@ class LlamaDecoder:
         self.fuse = tuple(fuse)
         self._peer = None
         if G > 1 and collective == "peer":
-            from .comm import PeerAllReduce
-            self._peer = PeerAllReduce(rows * cfg.dim, group=group, device=dev)
+            from .comm import shared_peer_allreduce
+            self._peer = shared_peer_allreduce(rows * cfg.dim, group=group, device=dev)
             self.all_reduce = lambda t: self._peer(t, stream=self.stream)
 
     def _load_weights(self, cfg, W, weights, blocks, g, f32):

@@ -53,7 +53,7 @@ def _rank(rank, world, port, path, graph, collective="peer"):
                             timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     try:
         dec = LlamaDecoder(_cfg(), rows=1, weights=_weights(_cfg(), seed=11), device=f"cuda:{rank}",
-                           collective=collective)
+                           collective=collective, group=dist.group.WORLD)
         assert dec.world == world and dec.nh == 8 // world
         logits = _run(dec, graph)
         dec.graph = None
