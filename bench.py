@@ -474,7 +474,7 @@ TYPE_IDS = {"Q4_0": 2, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13
 NCU_TRAFFIC_GEMM_Q4K_M512 = 37_271_552 + 1_266_944
 
 
-def cpu_gemm_timing(type_id: int, M: int, seconds: float) -> dict | None:
+def cpu_gemm_timing(type_id: int, M: int, seconds: float, N: int = GEMM_N, K: int = GEMM_K) -> dict | None:
     """The reference's prefill: one Compute::matmul_transposed_q per token, on
     all host cores.  A bounded sample of tokens; TFLOP/s of the rows done."""
     import oracle
@@ -485,13 +485,13 @@ def cpu_gemm_timing(type_id: int, M: int, seconds: float) -> dict | None:
     if oracle.ref_available():
         kind = "reference"
         oracle.ref_set_threads(cores)
-        fn = lambda w, x: oracle.ref_gemv(type_id, w, x, GEMM_N, GEMM_K)  # noqa: E731
+        fn = lambda w, x: oracle.ref_gemv(type_id, w, x, N, K)  # noqa: E731
     else:
         kind = "port"
         oracle.set_threads(cores)
-        fn = lambda w, x: oracle.gemv(type_id, w, x, GEMM_N, GEMM_K, format_order=False)  # noqa: E731
-    w = synth.random_blocks(type_id, GEMM_N, GEMM_K, seed=77)
-    X = synth.random_activations(min(M, 64), GEMM_K, seed=78)
+        fn = lambda w, x: oracle.gemv(type_id, w, x, N, K, format_order=False)  # noqa: E731
+    w = synth.random_blocks(type_id, N, K, seed=77)
+    X = synth.random_activations(min(M, 64), K, seed=78)
     fn(w, X[0])
     n = 0
     t0 = time.perf_counter()
@@ -501,7 +501,7 @@ def cpu_gemm_timing(type_id: int, M: int, seconds: float) -> dict | None:
         el = time.perf_counter() - t0
         if el >= seconds or n >= M:
             break
-    tf = 2.0 * GEMM_N * GEMM_K * n / el / 1e12
+    tf = 2.0 * N * K * n / el / 1e12
     return {"value": round(tf, 5), "unit": "TFLOP/s", "cores": cores, "kind": kind,
             "sample": f"{n} of the M={M} token rows (one matmul_transposed_q each), {el:.1f} s, "
                       f"{cores} OpenMP threads"}
@@ -518,7 +518,7 @@ def run_gemm(args, rank: int, world: int) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     t = TYPE_IDS[args.format]
-    M, N, K = args.M, GEMM_N, GEMM_K
+    M, N, K = args.M, args.N, args.K
     wbytes = synth.matrix_bytes(t, N, K)
     copies = max(2, -(-4 * 126_000_000 // wbytes))
     host_ws = [synth.random_blocks(t, N, K, seed=20_000 + i) for i in range(copies)]
@@ -562,7 +562,7 @@ def run_gemm(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     line = {
-        "metric": "dequant-GEMM TFLOP/s (prefill, N=14336 K=4096)", "value": round(value, 1),
+        "metric": f"dequant-GEMM TFLOP/s (N={N} K={K})", "value": round(value, 1),
         "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
@@ -575,12 +575,13 @@ def run_gemm(args, rank: int, world: int) -> None:
                      "traffic": NCU_TRAFFIC_GEMM_Q4K_M512 if (args.format, M) == ("Q4_K", 512) else None,
                      "kernel": "swq::tc::gemm_kernel (+ x_to_f16_kernel)",
                      "us_per_call": round(per_call_s * 1e6, 2)},
-        "cpu_baseline": cpu_gemm_timing(t, M, args.cpu_seconds) if world == 1 else None,
+        "cpu_baseline": cpu_gemm_timing(t, M, args.cpu_seconds, N, K) if world == 1 else None,
         "e2e": {"value": round(flops * e2e_steps / e2e_s / 1e12, 2), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": 4 * M * K, "d2h_bytes_per_step": 4 * M * N,
                 "api": "swq_ctx_matmul_q_batched (host fp32 X/Y, resident weights)", "steps": e2e_steps},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": (2 if M >= swq.get_option(swq.OPT_TENSOR_CORE_MIN_M) else 1) * args.steps,
         "clocks": clk.summary(),
+        "weight_GBps": round(wbytes / per_call_s / 1e9, 1),
     }
     print(json.dumps(line), flush=True)
 
@@ -596,7 +597,9 @@ def main() -> None:
                          "decode: Llama-3-8B greedy decode tok/s alone (replicas); decode70b: Llama-3-70B "
                          "decode tok/s, tensor-parallel over the ranks")
     ap.add_argument("--format", choices=sorted(TYPE_IDS), default="Q4_K", help="GEMM weight format")
-    ap.add_argument("--M", type=int, default=512, help="GEMM activation rows")
+    ap.add_argument("--M", type=int, default=512, help="GEMM activation rows (below 5: the GEMV kernel)")
+    ap.add_argument("--N", type=int, default=GEMM_N, help="GEMM weight rows")
+    ap.add_argument("--K", type=int, default=GEMM_K, help="GEMM weight columns")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU sample length (0: skip)")
     ap.add_argument("--collective", choices=["peer", "nccl"], default="peer",
                     help="decode70b: sums of the row-parallel projections")

@@ -422,12 +422,11 @@ struct Fmt<Q6_K> {
                                   float (&wm)[PARTS]) {
         const int n = c >> 1, h = c & 1;
         uint32_t A[4], B[4], H[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            A[i] = lds_u32_a2(b + 64 * n + 16 * h + 4 * i);
-            B[i] = lds_u32_a2(b + 64 * n + 32 + 16 * h + 4 * i);
-            H[i] = lds_u32_a2(b + 128 + 32 * n + 16 * h + 4 * i);
-        }
+        // 16-byte runs at 2-byte aligned addresses (210-byte blocks); the last
+        // run ends at byte 192 of the block, so the extra word stays inside it
+        lds_u32x4_a2(b + 64 * n + 16 * h, A);
+        lds_u32x4_a2(b + 64 * n + 32 + 16 * h, B);
+        lds_u32x4_a2(b + 128 + 32 * n + 16 * h, H);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             q[i] = (A[i] & 0x0F0F0F0Fu) | ((H[i] << 4) & 0x30303030u);

@@ -166,6 +166,20 @@ __device__ __forceinline__ uint32_t lds_u32_a4(const uint8_t* p) {
     return *reinterpret_cast<const uint32_t*>(p);
 }
 
+// Four consecutive little-endian words at a 2-byte aligned shared-memory
+// address: five aligned 32-bit loads and funnel shifts (by 0 or 16 bits)
+// instead of eight 16-bit loads.  Reads up to 4 bytes past the region.
+__device__ __forceinline__ void lds_u32x4_a2(const uint8_t* p, uint32_t (&w)[4]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t* base = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+    const uint32_t sh = static_cast<uint32_t>(a & 2u) << 3;
+    uint32_t v[5];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) v[i] = base[i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(v[i], v[i + 1], sh);
+}
+
 __device__ __forceinline__ uint4 lds_u128(const uint8_t* p) {
     return *reinterpret_cast<const uint4*>(p);
 }
