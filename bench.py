@@ -466,6 +466,115 @@ def run_decode_tp(rank: int, world: int, batches=(1, 8, 32), context: int = 2048
     return out
 
 
+# ---------------------------------------------------------------- MoE workload
+def run_moe(rank: int, world: int, steps: int = 20, warmup: int = 3) -> dict:
+    """Mixture-of-experts FFN of the MoE decoder shape: hidden 2048, 256 routed
+    experts of intermediate 512 (gate, up, down in Q4_K, synthetic blocks
+    generated on the device) with top-8 routing from random router logits.
+    Reports (a) the grouped quantized GEMMs alone (gate, up, down over the
+    routed rows sorted by expert) for a 1024-token prefill and a batch of 32
+    decode tokens, on this rank's experts, and (b) the whole expert-parallel
+    layer -- all-to-all dispatch, grouped GEMMs, SwiGLU, all-to-all combine --
+    over all ranks (experts sharded E/G per rank), tokens per second and the
+    dispatch time, max over ranks."""
+    import torch
+
+    import swq
+    from swq import parallel
+    from swq.model import synthetic_blocks
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    E, H, F, k = 256, 2048, 512, 8
+    t = swq.Q4_K
+    if E % world:
+        return {"skipped": f"{E} experts do not split over {world} ranks"}
+    el = E // world
+    g = torch.Generator(device=dev)
+    g.manual_seed(31 + rank)
+    experts = [None] * E
+    for e in range(rank * el, (rank + 1) * el):
+        experts[e] = (synthetic_blocks(t, F, H, g, dev), synthetic_blocks(t, F, H, g, dev),
+                      synthetic_blocks(t, H, F, g, dev))
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    wbytes_local = el * 3 * swq.type_size(t) * (F * H // swq.block_size(t))
+    out = {"model": "MoE FFN: hidden 2048, 256 experts x (gate, up 512x2048; down 2048x512) Q4_K, top-8",
+           "expert_parallel": world, "experts_per_rank": el, "weight_bytes_per_rank": wbytes_local}
+
+    def timed(fn, n):
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        if dist:
+            tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        return ms
+
+    # (a) grouped GEMMs on this rank's experts, rows spread as top-8 routing spreads them
+    grouped = parallel._GroupedCUDA(dev)
+    gate = [experts[e][0] for e in range(rank * el, (rank + 1) * el)]
+    up = [experts[e][1] for e in range(rank * el, (rank + 1) * el)]
+    down = [experts[e][2] for e in range(rank * el, (rank + 1) * el)]
+    tabs = [grouped.table(w) for w in (gate, up, down)]
+    for name, tokens in (("prefill_1024", 1024), ("decode_32", 32)):
+        logits = torch.randn(tokens, E, generator=g, device=dev)
+        ids, _ = parallel.route_topk(logits, k)
+        local = ids.reshape(-1)
+        local = local[(local >= rank * el) & (local < (rank + 1) * el)] - rank * el
+        rows = int(local.numel())
+        counts = torch.bincount(local.long(), minlength=el)
+        offs = torch.zeros(el + 1, dtype=torch.int32, device=dev)
+        offs[1:] = torch.cumsum(counts, 0).to(torch.int32)
+        xs = torch.randn(max(rows, 1), H, generator=g, device=dev)
+        gg = torch.empty(max(rows, 1), F, device=dev)
+        hh = torch.randn(max(rows, 1), F, generator=g, device=dev)
+        yy = torch.empty(max(rows, 1), H, device=dev)
+
+        def three():
+            grouped(t, gate, tabs[0], offs, xs, gg, F, H)
+            grouped(t, up, tabs[1], offs, xs, gg, F, H)
+            grouped(t, down, tabs[2], offs, hh, yy, H, F)
+
+        for _ in range(warmup):
+            three()
+        swq.check()
+        ms = timed(three, steps)
+        flops = 2.0 * rows * 3 * F * H
+        out[f"grouped_{name}"] = {"routed_rows_this_rank": rows, "ms": round(ms, 4),
+                                  "tflops_per_rank": round(flops / (ms * 1e-3) / 1e12, 2),
+                                  "weight_GBps_per_rank": round(wbytes_local / (ms * 1e-3) / 1e9, 1)}
+    # (b) the expert-parallel layer
+    moe = parallel.ExpertParallelMoE(experts, (t, t, t), H, F, device=dev,
+                                     group=dist.group.WORLD if dist else None)
+    for name, tokens in (("prefill_1024", 1024), ("decode_32", 32)):
+        x = torch.randn(tokens, H, generator=g, device=dev)
+        ids, w = parallel.route_topk(torch.randn(tokens, E, generator=g, device=dev), k)
+        for _ in range(warmup):
+            moe(x, ids, w)
+        swq.check()
+        ms = timed(lambda: moe(x, ids, w), steps)
+        xr = torch.randn(tokens * k // world, H, device=dev)
+
+        def a2a():
+            moe._a2a(xr, [tokens * k // world // world] * world, [tokens * k // world // world] * world)
+
+        ms_a2a = timed(a2a, steps) if world > 1 else 0.0
+        out[f"layer_{name}"] = {"tokens": tokens, "ms": round(ms, 4),
+                                "tok_s": round(tokens / (ms * 1e-3), 1),
+                                "dispatch_a2a_ms": round(ms_a2a, 4),
+                                "dispatch_bytes_per_rank": tokens * k // world * H * 4}
+    return out
+
+
 # ---------------------------------------------------------------- GEMM workload
 GEMM_N, GEMM_K = 14336, 4096
 TYPE_IDS = {"Q4_0": 2, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
@@ -547,6 +656,8 @@ def run_gemm(args, rank: int, world: int) -> None:
     per_call_s = ms * 1e-3 / args.steps
     value = flops * world / per_call_s / 1e12
     peak, peak_kind = load_tensor_peak()
+    hbm_peak, hbm_kind = load_peaks()
+    tc_path = M >= swq.get_option(swq.OPT_TENSOR_CORE_MIN_M)
 
     # End to end through the host-buffer API: host X in, host Y out.
     comp = swq.Compute(device=local)
@@ -569,17 +680,21 @@ def run_gemm(args, rank: int, world: int) -> None:
         "config": {"workload": f"{args.format} dequant-GEMM M={M} N={N} K={K}, {copies} rotating weight copies",
                    "format": args.format, "M": M, "N": N, "K": K, "copies": copies,
                    "l2": "inputs larger than L2 (rotating weights)"},
-        "roofline": {"bound": "tensor", "achieved": round(flops / per_call_s / 1e12, 1), "peak": peak,
-                     "unit": "TFLOP/s", "frac": round(flops / per_call_s / 1e12 / peak, 4),
-                     "peak_kind": peak_kind,
-                     "traffic": NCU_TRAFFIC_GEMM_Q4K_M512 if (args.format, M) == ("Q4_K", 512) else None,
-                     "kernel": "swq::tc::gemm_kernel (+ x_to_f16_kernel)",
-                     "us_per_call": round(per_call_s * 1e6, 2)},
+        "roofline": ({"bound": "tensor", "achieved": round(flops / per_call_s / 1e12, 1), "peak": peak,
+                      "unit": "TFLOP/s", "frac": round(flops / per_call_s / 1e12 / peak, 4),
+                      "peak_kind": peak_kind,
+                      "traffic": NCU_TRAFFIC_GEMM_Q4K_M512 if (args.format, M) == ("Q4_K", 512) else None,
+                      "kernel": "swq::tc::gemm_kernel (+ x_to_f16_kernel)",
+                      "us_per_call": round(per_call_s * 1e6, 2)} if tc_path else
+                     {"bound": "hbm", "achieved": round(wbytes / per_call_s / 1e9, 1), "peak": hbm_peak,
+                      "unit": "GB/s", "frac": round(wbytes / per_call_s / 1e9 / hbm_peak, 4),
+                      "peak_kind": hbm_kind, "traffic": None, "kernel": f"swq::gemv_kernel<{args.format},M>",
+                      "us_per_call": round(per_call_s * 1e6, 2)}),
         "cpu_baseline": cpu_gemm_timing(t, M, args.cpu_seconds, N, K) if world == 1 else None,
         "e2e": {"value": round(flops * e2e_steps / e2e_s / 1e12, 2), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": 4 * M * K, "d2h_bytes_per_step": 4 * M * N,
                 "api": "swq_ctx_matmul_q_batched (host fp32 X/Y, resident weights)", "steps": e2e_steps},
-        "gpu_launches": (2 if M >= swq.get_option(swq.OPT_TENSOR_CORE_MIN_M) else 1) * args.steps,
+        "gpu_launches": (2 if tc_path else 1) * args.steps,
         "clocks": clk.summary(),
         "weight_GBps": round(wbytes / per_call_s / 1e9, 1),
     }
@@ -592,7 +707,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["swq", "reference"], default="swq")
-    ap.add_argument("--workload", choices=["gemv", "gemm", "decode", "decode70b"], default="gemv",
+    ap.add_argument("--workload", choices=["gemv", "gemm", "decode", "decode70b", "moe"], default="gemv",
                     help="gemv: the headline Q4_K GEMV (with decode tok/s); gemm: the prefill dequant-GEMM; "
                          "decode: Llama-3-8B greedy decode tok/s alone (replicas); decode70b: Llama-3-70B "
                          "decode tok/s, tensor-parallel over the ranks")
@@ -614,6 +729,27 @@ def main() -> None:
     if args.warmup < 3:
         log("warm-up raised to 3 steps (minimum)")
         args.warmup = 3
+    if args.workload == "moe":
+        import torch
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                    device_id=torch.device("cuda", local))
+        d = run_moe(rank, world, steps=args.steps if args.steps != ap.get_default("steps") else 20)
+        if rank == 0:
+            lay = d.get("layer_decode_32", {})
+            print(json.dumps({"metric": "MoE layer tok/s (decode batch 32, 256 experts top-8, Q4_K)",
+                              "value": lay.get("tok_s"), "unit": "tok/s", "n_gpus": world,
+                              "higher_is_better": True, "scaling": "strong", "data": "synthetic", "moe": d}),
+                  flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.workload in ("decode", "decode70b"):
         import torch
         local = int(os.environ.get("LOCAL_RANK", "0"))

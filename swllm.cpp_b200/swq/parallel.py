@@ -151,7 +151,9 @@ class ExpertParallelMoE:
     """A SwiGLU mixture-of-experts FFN with experts sharded over ranks.
 
     experts: E triples (gate, up, down) of GGUF block arrays, gate/up [F x H]
-    and down [H x F] (only this rank's experts are kept).  types: the GGML type
+    and down [H x F] (only this rank's experts are kept; each may also be a
+    torch uint8 tensor already on the device, and the other ranks' entries
+    may be None).  types: the GGML type
     of gate, up and down.  grouped: expert matmul (type, weights, table,
     offsets, X, Y, N, K) over rows grouped by local expert; default libswq."""
 
@@ -166,7 +168,10 @@ class ExpertParallelMoE:
         self.e0 = self.rank * self.el
         self.H, self.F, self.types, self.group, self.device = H, F, types, group, device
         own = experts[self.e0:self.e0 + self.el]
-        to_dev = lambda a: torch.from_numpy(np.ascontiguousarray(a).reshape(-1)).to(device)  # noqa: E731
+        def to_dev(a):
+            if isinstance(a, torch.Tensor):
+                return a.reshape(-1).to(device)
+            return torch.from_numpy(np.ascontiguousarray(a).reshape(-1)).to(device)
         self.gate = [to_dev(g) for g, _, _ in own]
         self.up = [to_dev(u) for _, u, _ in own]
         self.down = [to_dev(d) for _, _, d in own]
