@@ -191,6 +191,22 @@ typedef struct swq_act {
 swq_status swq_gemm_act(int ggml_type, const void* W, const float* X, float* Y, int M, int N, int K,
                         const swq_act* act, int flags, swq_stream_t stream);
 
+/* ---- Grouped GEMV for MoE decode ------------------------------------------
+ *
+ * No counterpart in the reference (it has no MoE path, src/model.h:520-528).
+ * The same contract as swq_grouped_gemm, for the decode case of a few rows per
+ * expert: a GEMV over each expert's own rows (fixed-point activations, the
+ * same tolerance as swq_gemv) instead of the tensor-core GEMM, which works in
+ * tiles of 64 or more rows.  Only experts that have rows are read.  Unlike
+ * swq_grouped_gemm, every expert matrix must start on a 16-byte boundary; an
+ * expert that does not is skipped and swq_check then returns SWQ_ERR_BAD_ARG.
+ * Rows per expert are served in groups of 1, 2 or 4 (by the mean of
+ * total_rows / n_experts); any count is correct, many rows per expert are
+ * faster through swq_grouped_gemm.  n_experts <= 65535. */
+swq_status swq_grouped_gemv(int ggml_type, const void* const* W_experts, const int* expert_offsets,
+                            const float* X_sorted, float* Y, int n_experts, int total_rows, int N, int K,
+                            swq_stream_t stream);
+
 /* ---- Allocation-free GEMM ------------------------------------------------
  *
  * No counterpart in the reference.  swq_gemm's tensor-core path takes a

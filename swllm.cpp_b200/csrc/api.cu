@@ -360,6 +360,30 @@ swq_status swq_grouped_gemm(int type, const void* const* W_experts, const int* e
     return SWQ_OK;
 }
 
+swq_status swq_grouped_gemv(int type, const void* const* W_experts, const int* expert_offsets, const float* X_sorted,
+                            float* Y, int n_experts, int total_rows, int N, int K, swq_stream_t stream) {
+    TypeInfo ti;
+    if (!type_info(type, &ti)) return fail(SWQ_ERR_BAD_TYPE, "type " + std::to_string(type) + " is not on this path");
+    if (n_experts < 0 || total_rows < 0 || N < 0 || K < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative size");
+    if (K % ti.qk != 0)
+        return fail(SWQ_ERR_BAD_SHAPE, "K=" + std::to_string(K) + " is not a multiple of " + std::to_string(ti.qk));
+    if (n_experts > 65535) return fail(SWQ_ERR_BAD_SHAPE, "n_experts above 65535");
+    if (n_experts == 0 || total_rows == 0 || N == 0) return SWQ_OK;
+    if (!W_experts || !expert_offsets || !X_sorted || !Y) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (K == 0) {
+        cudaError_t e = cudaMemsetAsync(Y, 0, sizeof(float) * static_cast<size_t>(total_rows) * N, s);
+        return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
+    }
+    cudaError_t e = swq::grouped_gemv_launch(type, W_experts, expert_offsets, X_sorted, Y, n_experts, total_rows, N,
+                                             K, g_opt_q2k_refcpu, dev.smem_per_block_optin, s);
+    if (e != cudaSuccess) return cuda_fail(e, "grouped GEMV launch");
+    return SWQ_OK;
+}
+
 // ---- decode step -------------------------------------------------------------
 
 static swq_status launch_status(cudaError_t e, const char* what) {
@@ -514,6 +538,13 @@ swq_status swq_check(swq_stream_t stream) {
         (e = swq::status_fetch_gemm_tc(&c, s)) != cudaSuccess ||
         (e = swq::status_fetch_allreduce(&d, s)) != cudaSuccess)
         return cuda_fail(e, "status fetch");
+    if ((a | b | c | d) & swq::kStatusBadAlign) {
+        char buf[160];
+        std::snprintf(buf, sizeof(buf),
+                      "an expert matrix given to swq_grouped_gemv is not 16-byte aligned; its rows were skipped "
+                      "(status gemv=%#x)", a);
+        return fail(SWQ_ERR_BAD_ARG, buf);
+    }
     if (a | b | c | d) {
         char buf[128];
         std::snprintf(buf, sizeof(buf), "device wait timeout (gemv=%#x dequant=%#x gemm=%#x allreduce=%#x)", a, b,

@@ -790,6 +790,178 @@ cudaError_t gemv_launch(const GemvLaunch& L, cudaStream_t s) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Grouped GEMV (MoE decode): expert e multiplies its rows offsets[e] ..
+// offsets[e+1]-1 of X (few per expert) by its own GGUF matrix wptrs[e].
+// CTA (chunk, e) takes W rows [64 chunk, 64 chunk + 64) of expert e: an
+// expert without rows costs one early exit, and no other expert's weights
+// are read.  The expert's activation rows are converted MT at a time into the
+// GEMV's shared-memory layout (16-bit fixed point per 32-element block), then
+// each warp dots whole W rows read straight from global memory (a lane per
+// unit, the same decoders and dp2a chains as gemv_kernel).  The unit decoders
+// read 32-bit words, so every expert matrix must start on a 16-byte boundary:
+// an expert that does not is skipped and recorded (DEV_BAD_ALIGN) for
+// swq_check, never read misaligned.
+// ---------------------------------------------------------------------------
+
+static_assert(DEV_BAD_ALIGN == kStatusBadAlign, "status bit shared with the host");
+
+struct GroupedGemvParams {
+    const uint8_t* const* wptrs;
+    const int* offsets;
+    const float* X;
+    float* Y;
+    int n_experts, rows_total, N, K, nb, row_bytes, xstride, refcpu, x_vec;
+};
+
+constexpr int GG_WARPS = 8;
+constexpr int GG_ROWS = 64;  // W rows per CTA
+
+// rows (<= MT) activation rows of length K at X (row stride K) -> the GEMV's
+// shared-memory layout at xq; rows MT-rows .. MT-1 are zero.  Every thread of
+// the CTA takes part (full-warp shuffles); nthreads is a multiple of 32.
+template <int T, int MT>
+__device__ void prep_x_rows(const float* X, int K, int rows, uint8_t* xq, int xstride, bool refcpu, bool vec,
+                            int tid, int nthreads) {
+    using F = Fmt<T>;
+    using XL = XLay<T>;
+    const int ipr = K / 8;  // items per row (multiple of 4: K % 32 == 0)
+    const int items = MT * ipr;
+    for (int base = 0; base < items; base += nthreads) {
+        const int it = base + tid;
+        const bool act = it < items;
+        const int mm = act ? it / ipr : 0;
+        const int kk = act ? (it - mm * ipr) * 8 : 0;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        if (act && mm < rows) load8(X + static_cast<size_t>(mm) * K + kk, v, vec);
+        float a = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[i]));
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+        const bool live = a > 1e-30f;
+        const float inv = live ? __fdividef(32767.0f, a) : 0.f;
+        int xi[8], sum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            xi[i] = __float_as_int(fmaf(v[i], inv, 12582912.0f)) - 0x4B400000;
+            sum += xi[i];
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        if (F::PE == 32) sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (act) {
+            uint4 pk;
+            pk.x = __byte_perm(xi[0], xi[1], 0x5410);
+            pk.y = __byte_perm(xi[2], xi[3], 0x5410);
+            pk.z = __byte_perm(xi[4], xi[5], 0x5410);
+            pk.w = __byte_perm(xi[6], xi[7], 0x5410);
+            const float sc = live ? a * (1.0f / 32767.0f) : 0.f;
+            const int kb = kk / F::QK, kq = kk - kb * F::QK;
+            int c, p0, j;
+            const int np = F::item_dest(kq, refcpu, c, p0, j);
+            uint8_t* xrow = xq + static_cast<size_t>(mm) * xstride;
+            const int u = kb * F::UPB + c;
+            for (int t = 0; t < np; ++t) {
+                *reinterpret_cast<uint4*>(xrow + XL::chunk_off(u) + ((p0 + t) * XL::CPP + j) * 512) = pk;
+                if (j == 0)
+                    *reinterpret_cast<int2*>(xrow + XL::meta_off(u) + (p0 + t) * 256) =
+                        make_int2(__float_as_int(sc), sum);
+            }
+        }
+    }
+}
+
+template <int T, int MT>
+__global__ void __launch_bounds__(GG_WARPS * 32) grouped_gemv_kernel(const GroupedGemvParams p) {
+    using F = Fmt<T>;
+    extern __shared__ __align__(128) uint8_t xq[];
+    pdl_wait_primary();  // X and the offsets may come from the previous kernels
+    const int e = blockIdx.y;
+    const int a = min(max(p.offsets[e], 0), p.rows_total);
+    const int b = max(a, min(max(p.offsets[e + 1], 0), p.rows_total));
+    const int r0 = blockIdx.x * GG_ROWS;
+    if (b <= a || r0 >= p.N) return;
+    const int r1 = min(p.N, r0 + GG_ROWS);
+    const uint8_t* W = p.wptrs[e];
+    if (reinterpret_cast<uintptr_t>(W) & 15u) {
+        if (threadIdx.x == 0) atomicOr(&g_swq_dev_status, DEV_BAD_ALIGN);
+        return;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nu = p.nb * F::UPB;
+    for (int m0 = a; m0 < b; m0 += MT) {
+        const int mrows = min(MT, b - m0);
+        prep_x_rows<T, MT>(p.X + static_cast<size_t>(m0) * p.K, p.K, mrows, xq, p.xstride, p.refcpu != 0,
+                           p.x_vec != 0, threadIdx.x, GG_WARPS * 32);
+        __syncthreads();
+        for (int row = r0 + warp; row < r1; row += GG_WARPS) {
+            float acc[MT];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+            const uint8_t* wr = W + static_cast<size_t>(row) * p.row_bytes;
+            for (int uu = lane; uu < nu; uu += 32) {
+                const int kbl = uu / F::UPB, c = uu - kbl * F::UPB;
+                unit_dot<T, MT>(wr + kbl * F::BB, c, uu, xq, p.xstride, acc);
+            }
+            row_store<MT>(acc, lane, p.Y + static_cast<size_t>(m0) * p.N, mrows, p.N, row, nullptr);
+        }
+        __syncthreads();  // the next group's rows overwrite xq
+    }
+}
+
+template <int T, int MT>
+static cudaError_t launch_grouped_gemv_t(const GroupedGemvParams& p0, int smem_optin, cudaStream_t s) {
+    GroupedGemvParams p = p0;
+    p.xstride = XLay<T>::row_bytes(p.K);
+    const size_t smem = static_cast<size_t>(MT) * p.xstride;
+    if (smem > static_cast<size_t>(smem_optin)) return cudaErrorInvalidConfiguration;
+    auto kern = grouped_gemv_kernel<T, MT>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    const dim3 grid(static_cast<unsigned>((p.N + GG_ROWS - 1) / GG_ROWS), static_cast<unsigned>(p.n_experts));
+    kern<<<grid, GG_WARPS * 32, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+template <int T>
+static cudaError_t launch_grouped_gemv_fmt(const GroupedGemvParams& p, int mt, int smem_optin, cudaStream_t s) {
+    if (mt <= 1) return launch_grouped_gemv_t<T, 1>(p, smem_optin, s);
+    if (mt <= 2) return launch_grouped_gemv_t<T, 2>(p, smem_optin, s);
+    return launch_grouped_gemv_t<T, 4>(p, smem_optin, s);
+}
+
+cudaError_t grouped_gemv_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
+                                int n_experts, int rows_total, int N, int K, int refcpu, int smem_optin,
+                                cudaStream_t s) {
+    GroupedGemvParams p{};
+    p.wptrs = reinterpret_cast<const uint8_t* const*>(wptrs);
+    p.offsets = offsets;
+    p.X = X;
+    p.Y = Y;
+    p.n_experts = n_experts;
+    p.rows_total = rows_total;
+    p.N = N;
+    p.K = K;
+    p.refcpu = refcpu;
+    p.x_vec = (reinterpret_cast<uintptr_t>(X) & 15u) == 0 ? 1 : 0;
+    // activation rows per pass: the mean rows per expert (1, 2 or 4)
+    const int mt = (rows_total + n_experts - 1) / n_experts;
+    switch (type) {
+        case Q4_0: p.nb = K / Fmt<Q4_0>::QK; p.row_bytes = p.nb * Fmt<Q4_0>::BB; return launch_grouped_gemv_fmt<Q4_0>(p, mt, smem_optin, s);
+        case Q8_0: p.nb = K / Fmt<Q8_0>::QK; p.row_bytes = p.nb * Fmt<Q8_0>::BB; return launch_grouped_gemv_fmt<Q8_0>(p, mt, smem_optin, s);
+        case Q2_K: p.nb = K / Fmt<Q2_K>::QK; p.row_bytes = p.nb * Fmt<Q2_K>::BB; return launch_grouped_gemv_fmt<Q2_K>(p, mt, smem_optin, s);
+        case Q3_K: p.nb = K / Fmt<Q3_K>::QK; p.row_bytes = p.nb * Fmt<Q3_K>::BB; return launch_grouped_gemv_fmt<Q3_K>(p, mt, smem_optin, s);
+        case Q4_K: p.nb = K / Fmt<Q4_K>::QK; p.row_bytes = p.nb * Fmt<Q4_K>::BB; return launch_grouped_gemv_fmt<Q4_K>(p, mt, smem_optin, s);
+        case Q5_K: p.nb = K / Fmt<Q5_K>::QK; p.row_bytes = p.nb * Fmt<Q5_K>::BB; return launch_grouped_gemv_fmt<Q5_K>(p, mt, smem_optin, s);
+        case Q6_K: p.nb = K / Fmt<Q6_K>::QK; p.row_bytes = p.nb * Fmt<Q6_K>::BB; return launch_grouped_gemv_fmt<Q6_K>(p, mt, smem_optin, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 SWQ_DEFINE_STATUS_FETCH(gemv)
 
 }  // namespace swq

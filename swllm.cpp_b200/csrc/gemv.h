@@ -44,6 +44,16 @@ struct GemvLaunch {
 
 // Fused dequant + GEMV for M <= 8 activation rows.
 cudaError_t gemv_launch(const GemvLaunch& L, cudaStream_t s);
+// Device status bit of an input a kernel skipped because it was misaligned
+// (DEV_BAD_ALIGN in the device code).
+constexpr unsigned kStatusBadAlign = 32u;
+
+// Grouped GEMV (MoE decode): expert e multiplies rows offsets[e] ..
+// offsets[e+1]-1 of X by its GGUF matrix wptrs[e] (device arrays); every expert
+// matrix 16-byte aligned (a misaligned one is skipped and flagged).
+cudaError_t grouped_gemv_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
+                                int n_experts, int rows_total, int N, int K, int refcpu, int smem_optin,
+                                cudaStream_t s);
 // Shared-memory bytes of the per-CTA activation prep for padded row count MT.
 size_t gemv_smem_x_bytes(int type, int MT, int K);
 

@@ -22,7 +22,7 @@ from .lib import (  # noqa: F401
     add, add_rmsnorm, argmax, attention_decode, attention_workspace_bytes, decode_advance, embed,
     rmsnorm, rope_kv, silu_mul,
     GEMM_NOALLOC_MAX_X_ELEMS, SwqError, Status, block_size, build, check, dequant, exported_symbols, gemm,
-    gemm_act, gemm_noalloc, gemv, grouped_gemm,
+    gemm_act, gemm_noalloc, gemv, grouped_gemm, grouped_gemv,
     get_option, header_symbols, lib, lib_path, set_option, type_size,
 )
 from .compute import Backend, Compute, QuantWeight, dequantize  # noqa: F401

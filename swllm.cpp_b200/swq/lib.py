@@ -81,6 +81,7 @@ def lib() -> ctypes.CDLL:
         "swq_gemm_noalloc": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
         "swq_gemm_act": (i32, [i32, vp, vp, vp, i32, i32, i32, ctypes.POINTER(ActArgs), i32, vp]),
         "swq_grouped_gemm": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
+        "swq_grouped_gemv": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "swq_rmsnorm": (i32, [vp, vp, vp, i32, ctypes.c_float, i32, vp]),
         "swq_add_rmsnorm": (i32, [vp, vp, vp, vp, i32, ctypes.c_float, i32, vp]),
         "swq_rope_kv": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, vp]),
@@ -215,6 +216,14 @@ def gemm_act(type_id: int, W, X, Y, M: int, N: int, K: int, kind: int = ACT_NONE
                 _ptr(sum_out) if sum_out is not None else None, ld)
     _raise(lib().swq_gemm_act(type_id, _ptr(W), _ptr(X), _ptr(Y), M, N, K, ctypes.byref(a),
                               GEMM_NOALLOC if noalloc else 0, _stream(stream)))
+
+
+def grouped_gemv(type_id: int, w_ptrs, offsets, X, Y, n_experts: int, total_rows: int, N: int, K: int,
+                 stream=None) -> None:
+    """grouped_gemm for a few rows per expert (MoE decode): a GEMV per expert's
+    rows; every expert matrix must be 16-byte aligned."""
+    _raise(lib().swq_grouped_gemv(type_id, _ptr(w_ptrs), _ptr(offsets), _ptr(X), _ptr(Y), n_experts, total_rows,
+                                  N, K, _stream(stream)))
 
 
 def gemm_noalloc(type_id: int, W, X, Y, M: int, N: int, K: int, stream=None) -> None:

@@ -29,7 +29,7 @@ from typing import Callable, Sequence
 
 import numpy as np
 
-from .lib import gemm as _swq_gemm, grouped_gemm as _swq_grouped_gemm
+from .lib import gemm as _swq_gemm, grouped_gemm as _swq_grouped_gemm, grouped_gemv as _swq_grouped_gemv
 from .synth import block_geometry
 
 
@@ -133,18 +133,24 @@ def route_topk(logits, k: int):
 
 
 class _GroupedCUDA:
-    """Expert matmuls through swq_grouped_gemm: one device table of the local
-    experts' weight addresses per projection."""
+    """Expert matmuls through libswq: one device table of the local experts'
+    weight addresses per projection.  A few rows per expert (decode, at most
+    `gemv_rows` on average) take swq_grouped_gemv, more take the tensor-core
+    swq_grouped_gemm.  The expert weights are separate torch allocations, so
+    they start on the 16-byte boundary the GEMV path needs."""
 
-    def __init__(self, device):
+    def __init__(self, device, gemv_rows: int = 4):
         self.device = device
+        self.gemv_rows = gemv_rows
 
     def table(self, weights: Sequence):
         import torch
         return torch.tensor([w.data_ptr() for w in weights], dtype=torch.int64, device=self.device)
 
     def __call__(self, type_id, weights, table, offsets, X, Y, N, K):
-        _swq_grouped_gemm(type_id, table, offsets, X, Y, len(weights), X.shape[0], N, K)
+        rows, E = X.shape[0], len(weights)
+        fn = _swq_grouped_gemv if rows <= self.gemv_rows * E else _swq_grouped_gemm
+        fn(type_id, table, offsets, X, Y, E, rows, N, K)
 
 
 class ExpertParallelMoE:

@@ -15,7 +15,7 @@ from swq import synth
 pytestmark = pytest.mark.gpu
 
 
-def _run(torch, oracle_mod, t, counts, N, K, seed, offsets_bytes=None):
+def _run(torch, oracle_mod, t, counts, N, K, seed, offsets_bytes=None, fn=None):
     """Experts with `counts[e]` rows each; returns per-expert rel-L2 and the
     rows outside every expert (must stay NaN)."""
     E = len(counts)
@@ -39,7 +39,7 @@ def _run(torch, oracle_mod, t, counts, N, K, seed, offsets_bytes=None):
     d_x = torch.from_numpy(np.ascontiguousarray(X, dtype=np.float32)).cuda() if rows else \
         torch.zeros((1, K), dtype=torch.float32, device="cuda")
     d_y = torch.full((max(rows, 1), N), float("nan"), dtype=torch.float32, device="cuda")
-    swq.grouped_gemm(t, ptrs, d_off, d_x, d_y, E, rows, N, K)
+    (fn or swq.grouped_gemm)(t, ptrs, d_off, d_x, d_y, E, rows, N, K)
     swq.check()
     Y = d_y.cpu().numpy()
     errs = []
@@ -121,3 +121,52 @@ def test_rows_outside_experts_untouched(cuda):
     swq.check()
     assert torch.all(y[25:] == 7.0)
     assert torch.all(torch.isfinite(y[:25]))
+
+
+# ---------------------------------------------------------------- grouped GEMV
+@pytest.mark.parametrize("fmt", ["Q4_0", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"])
+def test_grouped_gemv_decode_routing(cuda, oracle_mod, fmt):
+    """swq_grouped_gemv: 1-2 rows per expert, most of 64 experts empty."""
+    rng = np.random.default_rng(13)
+    counts = np.where(rng.random(64) < 0.4, rng.integers(1, 3, size=64), 0)
+    errs = _run(cuda, oracle_mod, synth.IDS[fmt], counts, 512, 2048, seed=4700, fn=swq.grouped_gemv)
+    assert errs and max(errs) <= REL_L2_TOL, errs
+
+
+@pytest.mark.parametrize("counts", [[9, 0, 1, 5, 0, 3], [4, 4, 4, 4], [1] * 40])
+def test_grouped_gemv_rows_per_expert(cuda, oracle_mod, counts):
+    """More rows per expert than one pass holds (groups of 1, 2 or 4 rows), and
+    the expert down-projection shape (N=2048, K=512)."""
+    errs = _run(cuda, oracle_mod, synth.Q4_K, counts, 2048, 512, seed=4800, fn=swq.grouped_gemv)
+    assert max(errs) <= REL_L2_TOL, errs
+
+
+def test_grouped_gemv_matches_grouped_gemm(cuda, oracle_mod):
+    """The GEMV and tensor-core grouped paths agree within the GEMM tolerance."""
+    rng = np.random.default_rng(14)
+    counts = rng.integers(0, 3, size=32)
+    e1 = _run(cuda, oracle_mod, synth.Q6_K, counts, 640, 1024, seed=4900, fn=swq.grouped_gemv)
+    e2 = _run(cuda, oracle_mod, synth.Q6_K, counts, 640, 1024, seed=4900)
+    assert max(e1) <= REL_L2_TOL and max(e2) <= REL_L2_TOL
+
+
+def test_grouped_gemv_misaligned_expert_reported(cuda):
+    """An expert matrix off a 16-byte boundary is skipped (its rows keep their
+    value) and swq_check reports it; the aligned experts are computed."""
+    torch = cuda
+    t, N, K = synth.Q4_K, 256, 512
+    wb = synth.matrix_bytes(t, N, K)
+    buf = torch.zeros(2 * wb + 64, dtype=torch.uint8, device="cuda")
+    blocks = synth.random_blocks(t, N, K, seed=5000)
+    buf[:wb] = torch.from_numpy(blocks.reshape(-1)).cuda()
+    buf[wb + 2:2 * wb + 2] = torch.from_numpy(blocks.reshape(-1)).cuda()
+    ptrs = torch.tensor([buf.data_ptr(), buf.data_ptr() + wb + 2], dtype=torch.int64, device="cuda")
+    offs = torch.tensor([0, 3, 6], dtype=torch.int32, device="cuda")
+    x = torch.from_numpy(synth.random_activations(6, K, seed=5001)).cuda()
+    y = torch.full((6, N), 7.0, dtype=torch.float32, device="cuda")
+    swq.grouped_gemv(t, ptrs, offs, x, y, 2, 6, N, K)
+    with pytest.raises(swq.SwqError):
+        swq.check()
+    swq.check()  # the status was cleared by the check that reported it
+    assert torch.all(y[3:] == 7.0)
+    assert torch.all(torch.isfinite(y[:3])) and not torch.all(y[:3] == 7.0)
