@@ -7,6 +7,7 @@ differ only by the order of the all-reduce sum and by row grouping).
 """
 import os
 import socket
+import tempfile
 
 import numpy as np
 import pytest
@@ -57,7 +58,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, results):
+def _nccl_worker(rank, world, port, path):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -87,7 +88,9 @@ def _nccl_worker(rank, world, port, results):
         y_ep = moe(xm, ids.cuda(), w.cuda())
         torch.cuda.synchronize()
         if rank == 0:
-            results.put((y_tp.cpu().numpy(), y_ep.cpu().numpy()))
+            # through a file: a queue's pipe holds 64 KB, and a larger put()
+            # would block until the parent reads, which it does only after join
+            np.savez(path, y_tp=y_tp.cpu().numpy(), y_ep=y_ep.cpu().numpy())
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -96,10 +99,11 @@ def _nccl_worker(rank, world, port, results):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_two_gpu_tensor_and_expert_parallel(cuda):
     import torch.multiprocessing as mp
-    ctx = mp.get_context("spawn")
-    results = ctx.SimpleQueue()
-    mp.start_processes(_nccl_worker, args=(2, _free_port(), results), nprocs=2, join=True, start_method="spawn")
-    y_tp, y_ep = results.get()
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "results.npz")
+        mp.start_processes(_nccl_worker, args=(2, _free_port(), path), nprocs=2, join=True, start_method="spawn")
+        got = np.load(path)
+        y_tp, y_ep = got["y_tp"], got["y_ep"]
     # the same layers on one GPU
     t1, t2 = synth.Q4_K, synth.Q6_K
     M, K, N1, N2 = 7, 2048, 1024, 2048
