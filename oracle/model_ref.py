@@ -18,7 +18,14 @@ on the full-attention, dense-FFN path, in fp32 numpy:
 
 The quantized matmuls are the reference's own routine compiled from source
 (oracle/_ref) when it was built, else this package's C restatement in the
-reference's accumulation order.  Only tests use this module.
+reference's accumulation order.  Per-layer type mixes (cfg.layer_type_map) and
+an embedding table given as (GGML type, blocks) are read as the reference's
+Model::load reads them.  Only tests use this module.
+
+Pinned: tests/test_gguf.py runs it against the reference's own Model::forward
+(src/model.h compiled from source, oracle/model_shim.cpp) on tiny GGUF models,
+live and through the golden logits the reference produced
+(tests/golden/golden_llama_*.npz); they agree to ~4e-7 relative L2.
 """
 from __future__ import annotations
 
@@ -68,16 +75,24 @@ class RefLlama:
     head_dim, ffn, vocab, eps, types); weights: the host arrays LlamaDecoder takes."""
 
     def __init__(self, cfg, weights: dict, freqs: np.ndarray, max_seq: int):
+        te = weights["token_embd"]
+        if isinstance(te, tuple):  # (GGML type, blocks): dequantized at load, src/model.h:771-772
+            from . import dequantize as _port_dequant
+            from . import ref_dequantize
+            deq = ref_dequantize if ref_available() else _port_dequant
+            weights = dict(weights, token_embd=deq(te[0], np.asarray(te[1]), cfg.vocab * cfg.dim).reshape(
+                cfg.vocab, cfg.dim))
         self.cfg, self.W, self.freqs = cfg, weights, freqs.astype(F32)
         self.kc = np.zeros((cfg.n_layers, max_seq, cfg.n_kv_heads * cfg.head_dim), F32)
         self.vc = np.zeros_like(self.kc)
 
     def forward(self, token: int, pos: int) -> np.ndarray:
-        c, W, t = self.cfg, self.W, self.cfg.types
+        c, W = self.cfg, self.W
         hd, nh, nkv = c.head_dim, c.n_heads, c.n_kv_heads
         q_dim, kv_dim = nh * hd, nkv * hd
         x = np.asarray(W["token_embd"][token], F32).copy()
         for li, L in enumerate(W["layers"]):
+            t = c.layer_type_map(li) if hasattr(c, "layer_type_map") else c.types
             xb = rmsnorm(x, L["attn_norm"], c.eps)
             q = matmul(t["wq"], L["wq"], xb, q_dim, c.dim)
             k = matmul(t["wk"], L["wk"], xb, kv_dim, c.dim)
@@ -98,7 +113,8 @@ class RefLlama:
             xb = rmsnorm(x, L["ffn_norm"], c.eps)
             g = matmul(t["w_gate"], L["w_gate"], xb, c.ffn, c.dim)
             u = matmul(t["w_up"], L["w_up"], xb, c.ffn, c.dim)
-            hmid = (g / (F32(1.0) + np.exp(-g)) * u).astype(F32)
+            with np.errstate(over="ignore"):  # exp(-g) = inf for very negative g: silu -> -0, as expf
+                hmid = (g / (F32(1.0) + np.exp(-g)) * u).astype(F32)
             x = (x + matmul(t["w_down"], L["w_down"], hmid, c.dim, c.ffn)).astype(F32)
         x = rmsnorm(x, W["output_norm"], c.eps)
-        return matmul(t["output"], W["output"], x, c.vocab, c.dim)
+        return matmul(c.types["output"], W["output"], x, c.vocab, c.dim)

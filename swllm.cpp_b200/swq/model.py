@@ -35,8 +35,8 @@ import numpy as np
 
 from . import lib as _lib_mod  # noqa: F401  (module import for the ctypes table)
 from .lib import (ACT_NONE, ACT_RMSNORM, ACT_SWIGLU, GEMM_NOALLOC_MAX_X_ELEMS, OPT_TENSOR_CORE_MIN_M, argmax,
-                  add_rmsnorm, attention_decode, attention_workspace_bytes, decode_advance, embed, gemm_act,
-                  get_option, rmsnorm, rope_kv, silu_mul)
+                  add_rmsnorm, attention_decode, attention_workspace_bytes, decode_advance, dequant, embed,
+                  gemm_act, get_option, rmsnorm, rope_kv, silu_mul)
 from .synth import LAYOUT, Q4_K, Q6_K, Q8_0, row_bytes
 
 
@@ -56,6 +56,10 @@ class LlamaConfig:
     # GGML types of the Q4_K_M mix
     types: dict = field(default_factory=lambda: {"wq": Q4_K, "wk": Q4_K, "wv": Q6_K, "wo": Q4_K,
                                                  "w_gate": Q4_K, "w_up": Q4_K, "w_down": Q6_K, "output": Q6_K})
+    # per layer, the types of its seven matrices when they differ between
+    # layers (a GGUF Q4_K_M file keeps attn_v / ffn_down in Q6_K on some
+    # layers only); None: every layer has `types`
+    layer_types: tuple | None = None
 
     @classmethod
     def llama3_70b(cls, **kw) -> "LlamaConfig":
@@ -77,10 +81,17 @@ class LlamaConfig:
                 "wo": (self.dim, self.q_dim), "w_gate": (self.ffn, self.dim), "w_up": (self.ffn, self.dim),
                 "w_down": (self.dim, self.ffn)}
 
+    def layer_type_map(self, layer: int) -> dict:
+        """GGML type of each of layer `layer`'s seven matrices."""
+        if self.layer_types:
+            return self.layer_types[layer]
+        return {k: self.types[k] for k in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down")}
+
     def weight_bytes_per_token(self) -> int:
         """Quantized weight bytes one decode step reads (all layers + LM head)."""
-        per_layer = sum(n * row_bytes(self.types[k], kk) for k, (n, kk) in self.shapes().items())
-        return self.n_layers * per_layer + self.vocab * row_bytes(self.types["output"], self.dim)
+        per_layer = [sum(n * row_bytes(self.layer_type_map(li)[k], kk) for k, (n, kk) in self.shapes().items())
+                     for li in range(self.n_layers)]
+        return sum(per_layer) + self.vocab * row_bytes(self.types["output"], self.dim)
 
 
 def rope_freqs(cfg: LlamaConfig) -> np.ndarray:
@@ -106,6 +117,18 @@ def synthetic_blocks(type_id: int, N: int, K: int, generator, device):
         q = b[:, :, 2:]
         q[q == 0x80] = 0x81
     return b.reshape(-1)
+
+
+def _upload(host: np.ndarray, device):
+    """Host array -> device tensor.  A read-only array (a view of a memory-mapped
+    GGUF file) is uploaded from the mapping itself, without a host copy; torch
+    only reads it."""
+    import warnings
+
+    import torch
+    with warnings.catch_warnings():
+        warnings.filterwarnings("ignore", message="The given NumPy array is not writable")
+        return torch.from_numpy(host).to(device)
 
 
 def _shard(host, type_id: int, N: int, K: int, rows: tuple[int, int] | None, cols: tuple[int, int] | None):
@@ -154,7 +177,6 @@ class LlamaDecoder:
         self.q_dim, self.kv_dim = self.nh * cfg.head_dim, self.nkv * cfg.head_dim
         self.ffn, self.vocab = cfg.ffn // G, cfg.vocab // G
         dev = self.device
-        t = cfg.types
         g = torch.Generator(device=dev)
         g.manual_seed(seed + 1000003 * r)
         f32 = dict(dtype=torch.float32, device=dev)
@@ -163,7 +185,7 @@ class LlamaDecoder:
                     "output": self.vocab}
         col_part = {"wo": self.q_dim, "w_down": self.ffn}
 
-        def blocks(name, N, K, host):
+        def blocks(name, N, K, host, type_id):
             if name in row_part:
                 n = row_part[name]
                 Nl, Kl, rs, cs = n, K, (r * n, (r + 1) * n), None
@@ -171,9 +193,9 @@ class LlamaDecoder:
                 k = col_part[name]
                 Nl, Kl, rs, cs = N, k, None, (r * k, (r + 1) * k)
             if host is not None:
-                part = _shard(host, t[name], N, K, rs, cs) if G > 1 else np.ascontiguousarray(host)
-                return torch.from_numpy(part.reshape(-1)).to(dev)
-            return synthetic_blocks(t[name], Nl, Kl, g, dev)
+                part = _shard(host, type_id, N, K, rs, cs) if G > 1 else np.ascontiguousarray(host)
+                return _upload(part.reshape(-1), dev)
+            return synthetic_blocks(type_id, Nl, Kl, g, dev)
 
         W = weights or {}
         if weights_from is not None:
@@ -198,29 +220,57 @@ class LlamaDecoder:
             self._peer = shared_peer_allreduce(rows * cfg.dim, group=group, device=dev)
             self.all_reduce = lambda t: self._peer(t, stream=self.stream)
 
+    @classmethod
+    def from_gguf(cls, path, rows: int = 1, context_override: int = 0, **kw) -> "LlamaDecoder":
+        """A decoder of the dense Llama-family GGUF file at `path`: its config
+        and type mix read as the reference's Model::load does, every projection
+        uploaded in its GGUF blocks straight from the memory-mapped file, a
+        quantized embedding table dequantized on the device.  The KV cache
+        holds the file's context length, capped as the reference caps it
+        (context_override when smaller; 4096 when none is given and the file's
+        exceeds 8192).  Other keywords as the constructor's."""
+        from .gguf import llama_from_gguf
+        cfg, W, g = llama_from_gguf(path, context_override)
+        try:
+            return cls(cfg, rows=rows, weights=W, **kw)
+        finally:
+            del W
+            g.close()
+
     def _load_weights(self, cfg, W, weights, blocks, g, f32):
         import torch
         dev = self.device
         t = cfg.types
-        self.token_embd = (torch.from_numpy(np.asarray(W["token_embd"], np.float32)).to(dev) if weights
-                           else torch.randn((cfg.vocab, cfg.dim), generator=g, **f32))
-        self.output_norm = (torch.from_numpy(np.asarray(W["output_norm"], np.float32)).to(dev) if weights
+        if weights and isinstance(W["token_embd"], tuple):
+            # (GGML type, blocks) of a quantized embedding table: dequantized on
+            # the device (bit-exact, as the reference dequantizes it at load,
+            # src/model.h:771-772), then ordered before the decode stream's use
+            type_id, tb = W["token_embd"]
+            self.token_embd = torch.empty((cfg.vocab, cfg.dim), **f32)
+            dequant(type_id, _upload(np.ascontiguousarray(tb).reshape(-1), dev), self.token_embd,
+                    cfg.vocab * cfg.dim)
+            torch.cuda.current_stream(dev).synchronize()
+        else:
+            self.token_embd = (_upload(np.ascontiguousarray(W["token_embd"], np.float32), dev) if weights
+                               else torch.randn((cfg.vocab, cfg.dim), generator=g, **f32))
+        self.output_norm = (_upload(np.ascontiguousarray(W["output_norm"], np.float32), dev) if weights
                             else 1.0 + 0.01 * torch.randn(cfg.dim, generator=g, **f32))
-        self.output = blocks("output", cfg.vocab, cfg.dim, W.get("output"))
-        self.fuse_gate_up = t["w_gate"] == t["w_up"]
-        self.fuse_qk = t["wq"] == t["wk"]
+        self.output = blocks("output", cfg.vocab, cfg.dim, W.get("output"), t["output"])
+        lts = [cfg.layer_type_map(layer) for layer in range(cfg.n_layers)]
+        self.fuse_gate_up = all(lt["w_gate"] == lt["w_up"] for lt in lts)
+        self.fuse_qk = all(lt["wq"] == lt["wk"] for lt in lts)
         self.layers = []
-        for layer in range(cfg.n_layers):
+        for layer, lt in enumerate(lts):
             lw = W["layers"][layer] if weights else {}
-            L = {}
+            L = {"types": lt}
             for name in ("attn_norm", "ffn_norm"):
-                L[name] = (torch.from_numpy(np.asarray(lw[name], np.float32)).to(dev) if weights
+                L[name] = (_upload(np.ascontiguousarray(lw[name], np.float32), dev) if weights
                            else 1.0 + 0.01 * torch.randn(cfg.dim, generator=g, **f32))
             for name, (N, K) in cfg.shapes().items():
-                L[name] = blocks(name, N, K, lw.get(name))
-            if self.fuse_gate_up:  # rows of gate then rows of up: one GEMV
+                L[name] = blocks(name, N, K, lw.get(name), lt[name])
+            if lt["w_gate"] == lt["w_up"]:  # rows of gate then rows of up: one GEMV
                 L["w_gate_up"] = torch.cat([L.pop("w_gate"), L.pop("w_up")])
-            if self.fuse_qk:  # rows of q then rows of k
+            if lt["wq"] == lt["wk"]:  # rows of q then rows of k
                 L["w_qk"] = torch.cat([L.pop("wq"), L.pop("wk")])
             self.layers.append(L)
         self.freqs = torch.from_numpy(rope_freqs(cfg)).to(dev)
@@ -284,7 +334,6 @@ class LlamaDecoder:
         fuse=("rmsnorm",), by the projection that reads the norm, which then
         writes the sum to x2 and the stream alternates between x and x2)."""
         c, B, s = self.cfg, self.rows, self.stream
-        t = c.types
         gemm = self._gemm  # noqa: F811
         qd, kvd, ffn = self.q_dim, self.kv_dim, self.ffn
         tp = self.world > 1
@@ -297,13 +346,14 @@ class LlamaDecoder:
             rmsnorm(xb, x, self.layers[0]["attn_norm"], c.dim, c.eps, B, stream=s)
         pending = None  # fused: d to add to the residual before the next norm
         for li, L in enumerate(self.layers):
+            t = L["types"]
             # q, k, v of norm(x) (fused: x2 = x + pending first)
             if fuse_rms:
                 src, a_in = x, dict(kind=ACT_RMSNORM, residual=pending, norm_w=L["attn_norm"])
                 a_qk = dict(a_in, sum_out=x2)
             else:
                 src, a_in, a_qk = xb, {}, {}
-            if self.fuse_qk:
+            if "w_qk" in L:
                 gemm(t["wq"], L["w_qk"], src, self.qk, B, ld, c.dim, stream=s, **a_qk)
             else:
                 gemm(t["wq"], L["wq"], src, self.att, B, qd, c.dim, stream=s, **a_qk)
@@ -326,7 +376,7 @@ class LlamaDecoder:
             else:
                 add_rmsnorm(xb, x, d, L["ffn_norm"], c.dim, c.eps, B, stream=s)  # x += o; xb = norm(x)
                 src, a_in, a_g = xb, {}, {}
-            if self.fuse_gate_up:
+            if "w_gate_up" in L:
                 gemm(t["w_gate"], L["w_gate_up"], src, self.gu, B, 2 * ffn, c.dim, stream=s, **a_g)
             else:
                 gemm(t["w_gate"], L["w_gate"], src, self.h, B, ffn, c.dim, stream=s, **a_g)
@@ -350,11 +400,12 @@ class LlamaDecoder:
             src, a_out = x, dict(kind=ACT_RMSNORM, residual=pending, norm_w=self.output_norm)
         else:
             src, a_out = xb, {}
+        t_out = c.types["output"]
         if tp:
-            gemm(t["output"], self.output, src, self.logits_l, B, self.vocab, c.dim, stream=s, **a_out)
+            gemm(t_out, self.output, src, self.logits_l, B, self.vocab, c.dim, stream=s, **a_out)
             self._gather_logits()
         else:
-            gemm(t["output"], self.output, src, self.logits, B, c.vocab, c.dim, stream=s, **a_out)
+            gemm(t_out, self.output, src, self.logits, B, c.vocab, c.dim, stream=s, **a_out)
         if greedy:
             argmax(self.logits, c.vocab, B, self.tokens, self.history, self.step_no, stream=s)
             decode_advance(self.pos, self.step_no, stream=s)

@@ -1,0 +1,98 @@
+"""Tiny dense Llama models written as GGUF files, for the model-level parity
+tests and their golden logits.
+
+Each variant is fully determined by its spec (shapes, per-layer GGML types,
+seeds), so the file is rebuilt byte for byte wherever the tests run and only
+its SHA-256 and the reference's logits are stored (tests/golden/).
+
+* "mix":  2 layers, hidden 256, 4 query / 2 kv heads of 64, FFN 512, vocab
+          300; every one of the seven formats appears; the layers have
+          different type mixes; F32 embedding table; Q6_K output matrix;
+          general.alignment 64; no llama.vocab_size (the token list sets it).
+* "tied": the same shape with a Q4_K_M-style mix on both layers, a Q8_0
+          embedding table and no output.weight (the LM head is the
+          embedding table, src/model.h:776-779), as small Llama models ship.
+"""
+from __future__ import annotations
+
+import hashlib
+from pathlib import Path
+
+import numpy as np
+
+from swq import gguf as G
+from swq import synth
+
+TOKENS = [7, 123, 45, 299, 0, 200]   # teacher-forced tokens at positions 0..5
+
+SHAPE = dict(layers=2, hidden=256, heads=4, kv_heads=2, ffn=512, vocab=300, context=32)
+_STEMS = {"wq": "attn_q", "wk": "attn_k", "wv": "attn_v", "wo": "attn_output", "w_gate": "ffn_gate",
+          "w_up": "ffn_up", "w_down": "ffn_down"}
+
+VARIANTS = {
+    "mix": dict(
+        alignment=64, embd=G.F32, output=G.Q6_K, vocab_key=False,
+        layers=[dict(wq=G.Q4_K, wk=G.Q4_K, wv=G.Q6_K, wo=G.Q4_0, w_gate=G.Q4_K, w_up=G.Q4_K, w_down=G.Q6_K),
+                dict(wq=G.Q5_K, wk=G.Q5_K, wv=G.Q8_0, wo=G.Q2_K, w_gate=G.Q3_K, w_up=G.Q3_K, w_down=G.Q4_K)]),
+    "tied": dict(
+        alignment=32, embd=G.Q8_0, output=None, vocab_key=True,
+        layers=[dict(wq=G.Q4_K, wk=G.Q4_K, wv=G.Q6_K, wo=G.Q4_K, w_gate=G.Q4_K, w_up=G.Q4_K, w_down=G.Q6_K)] * 2),
+}
+
+
+def _shapes(s):
+    hd = s["hidden"] // s["heads"]
+    q, kv = s["heads"] * hd, s["kv_heads"] * hd
+    return {"wq": (q, s["hidden"]), "wk": (kv, s["hidden"]), "wv": (kv, s["hidden"]), "wo": (s["hidden"], q),
+            "w_gate": (s["ffn"], s["hidden"]), "w_up": (s["ffn"], s["hidden"]), "w_down": (s["hidden"], s["ffn"])}
+
+
+def write(path: Path, variant: str) -> Path:
+    """Write the variant's GGUF file at path."""
+    v, s = VARIANTS[variant], SHAPE
+    rng = np.random.default_rng({"mix": 11, "tied": 12}[variant])
+    meta = {
+        "general.architecture": "llama",
+        "general.name": f"tiny-{variant}",
+        "general.alignment": v["alignment"],
+        "llama.context_length": s["context"],
+        "llama.embedding_length": s["hidden"],
+        "llama.block_count": s["layers"],
+        "llama.feed_forward_length": s["ffn"],
+        "llama.attention.head_count": s["heads"],
+        "llama.attention.head_count_kv": s["kv_heads"],
+        "llama.rope.freq_base": G.GGUFValue(G.FLOAT32, 500000.0),
+        "llama.attention.layer_norm_rms_epsilon": G.GGUFValue(G.FLOAT32, 1e-5),
+        "tokenizer.ggml.model": "llama",
+        "tokenizer.ggml.tokens": [f"<t{i}>" for i in range(s["vocab"])],
+        "tokenizer.ggml.scores": [float(-i) for i in range(s["vocab"])],
+    }
+    if v["vocab_key"]:
+        meta["llama.vocab_size"] = s["vocab"]
+    tensors = []
+
+    def norm(name):
+        tensors.append((name, G.F32, (s["hidden"],), (1 + 0.01 * rng.standard_normal(s["hidden"])).astype(np.float32)))
+
+    def mat(name, t, N, K, seed):
+        tensors.append((name, t, (K, N), synth.random_blocks(t, N, K, seed=seed)))
+
+    if v["embd"] == G.F32:
+        tensors.append(("token_embd.weight", G.F32, (s["hidden"], s["vocab"]),
+                        rng.standard_normal((s["vocab"], s["hidden"])).astype(np.float32)))
+    else:
+        mat("token_embd.weight", v["embd"], s["vocab"], s["hidden"], 900)
+    norm("output_norm.weight")
+    if v["output"] is not None:
+        mat("output.weight", v["output"], s["vocab"], s["hidden"], 901)
+    for li, lt in enumerate(v["layers"]):
+        norm(f"blk.{li}.attn_norm.weight")
+        norm(f"blk.{li}.ffn_norm.weight")
+        for j, (key, (N, K)) in enumerate(_shapes(s).items()):
+            mat(f"blk.{li}.{_STEMS[key]}.weight", lt[key], N, K, 1000 + 10 * li + j)
+    G.write_gguf(path, meta, tensors, alignment=v["alignment"])
+    return path
+
+
+def sha256(path: Path) -> str:
+    return hashlib.sha256(Path(path).read_bytes()).hexdigest()
