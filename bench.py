@@ -20,7 +20,9 @@ Arms:
       collective); the time is the max over ranks.
   --impl reference: the reference's own CPU code (Compute::matmul_transposed_q,
       compiled from source into oracle/_ref; the oracle port if that is
-      absent) on all host cores, one Q4_K 4096x4096 GEMV per step.
+      absent) on all host cores, one Q4_K 4096x4096 GEMV per step; and, in
+      "decode", the reference's Model::forward tok/s on a Llama-3-8B-shaped
+      Q4_K_M GGUF file written for the run (src/model.h compiled from source).
 
 One JSON line on rank 0.
 """
@@ -31,6 +33,7 @@ import csv
 import io
 import json
 import os
+import shutil
 import statistics
 import subprocess
 import sys
@@ -164,6 +167,111 @@ def cpu_gemv_timing(seconds: float, max_steps: int | None = None, copies: int = 
                       f"{el:.1f} s, {cores} OpenMP threads", "seconds": round(el, 2), "steps": n}
 
 
+def write_llama_gguf(path, cfg, seed: int = 0) -> int:
+    """A GGUF file of `cfg`'s dense Llama shape with synthetic weights in its
+    type mix (the metric's block distributions, a Q4_K embedding table as in
+    a Q4_K_M file, norms 1 + N(0, 0.01)), written one tensor at a time.
+    Returns the file's size."""
+    import numpy as np
+
+    from swq import gguf as G
+    from swq import synth
+
+    stems = {"wq": "attn_q", "wk": "attn_k", "wv": "attn_v", "wo": "attn_output", "w_gate": "ffn_gate",
+             "w_up": "ffn_up", "w_down": "ffn_down"}
+    rng = np.random.default_rng(seed)
+    meta = {"general.architecture": "llama", "general.name": "synthetic",
+            "llama.context_length": cfg.max_seq, "llama.embedding_length": cfg.dim,
+            "llama.block_count": cfg.n_layers, "llama.feed_forward_length": cfg.ffn,
+            "llama.attention.head_count": cfg.n_heads, "llama.attention.head_count_kv": cfg.n_kv_heads,
+            "llama.rope.freq_base": G.GGUFValue(G.FLOAT32, cfg.theta),
+            "llama.attention.layer_norm_rms_epsilon": G.GGUFValue(G.FLOAT32, cfg.eps),
+            "llama.vocab_size": cfg.vocab, "tokenizer.ggml.model": "llama",
+            "tokenizer.ggml.tokens": [f"<{i}>" for i in range(cfg.vocab)]}
+    mats = lambda t, N, K, sd: (lambda: synth.fast_random_blocks(t, N, K, seed=sd))  # noqa: E731
+    norm = lambda: (1 + 0.01 * rng.standard_normal(cfg.dim)).astype(np.float32)  # noqa: E731
+    tensors = [("token_embd.weight", G.Q4_K, (cfg.dim, cfg.vocab), mats(G.Q4_K, cfg.vocab, cfg.dim, seed + 1)),
+               ("output_norm.weight", G.F32, (cfg.dim,), norm()),
+               ("output.weight", cfg.types["output"], (cfg.dim, cfg.vocab),
+                mats(cfg.types["output"], cfg.vocab, cfg.dim, seed + 2))]
+    for li in range(cfg.n_layers):
+        lt = cfg.layer_type_map(li)
+        tensors += [(f"blk.{li}.attn_norm.weight", G.F32, (cfg.dim,), norm()),
+                    (f"blk.{li}.ffn_norm.weight", G.F32, (cfg.dim,), norm())]
+        for j, (key, (N, K)) in enumerate(cfg.shapes().items()):
+            tensors.append((f"blk.{li}.{stems[key]}.weight", lt[key], (K, N),
+                            mats(lt[key], N, K, seed + 100 + 10 * li + j)))
+    G.write_gguf(path, meta, tensors)
+    return os.path.getsize(path)
+
+
+def _mem_available() -> int:
+    try:
+        with open("/proc/meminfo") as f:
+            for ln in f:
+                if ln.startswith("MemAvailable:"):
+                    return int(ln.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
+
+
+def ref_decode_timing(cfg, seconds: float = 20.0, max_tokens: int = 8, workdir: str | None = None) -> dict:
+    """The reference's own decode on the host cores: Model::load of a GGUF file
+    of `cfg`'s shape (written here, deleted once loaded -- the reference keeps
+    the whole file in memory), then Model::forward calls at positions 0, 1,
+    2, ... on seeded token ids (teacher-forced), timed with the wall clock
+    after one warm-up call.  The context stays short, so the reference reads less
+    KV per token than after a real prefill (its number is, if anything, high)."""
+    import tempfile
+
+    import numpy as np
+
+    import oracle
+    from oracle.ref_model import RefModel, model_ref_available
+
+    if not model_ref_available():
+        return {"unavailable": "the reference's model library was not built (oracle/_ref)"}
+    est = cfg.weight_bytes_per_token() + cfg.vocab * cfg.dim * 144 // 256
+    if workdir is None:  # memory-backed when it has room: the reference freads the whole file
+        roomy = [d for d in ("/dev/shm", tempfile.gettempdir())
+                 if os.path.isdir(d) and os.access(d, os.W_OK) and shutil.disk_usage(d).free >= est + (2 << 30)]
+        workdir = roomy[0] if roomy else tempfile.gettempdir()
+    free = shutil.disk_usage(workdir).free
+    if free < est + (2 << 30):
+        return {"unavailable": f"{free / 1e9:.1f} GB free in {workdir}, the model file needs {est / 1e9:.1f} GB"}
+    need_ram = est + cfg.vocab * cfg.dim * 4 + (4 << 30)  # the file in memory + the fp32 embedding table
+    if 0 < _mem_available() < need_ram:
+        return {"unavailable": f"{_mem_available() / 1e9:.1f} GB of host memory available, "
+                               f"{need_ram / 1e9:.1f} GB needed"}
+    cores = oracle.host_cores()
+    t0 = time.perf_counter()
+    with tempfile.TemporaryDirectory(dir=workdir) as d:
+        path = os.path.join(d, "model.gguf")
+        size = write_llama_gguf(path, cfg)
+        t_write = time.perf_counter() - t0
+        m = RefModel(path)
+        os.unlink(path)
+    t_load = time.perf_counter() - t0 - t_write
+    toks = np.random.default_rng(3).integers(0, cfg.vocab, size=max_tokens + 1).tolist()
+    finite = bool(np.isfinite(m.forward(toks[0], 0)).all())  # warm-up
+    n, t1 = 0, time.perf_counter()
+    while n < max_tokens:
+        finite &= bool(np.isfinite(m.forward(toks[n + 1], n + 1)).all())
+        n += 1
+        if time.perf_counter() - t1 >= seconds:
+            break
+    el = time.perf_counter() - t1
+    m.close()
+    per_tok = el / n
+    return {"tok_s": round(1.0 / per_tok, 3), "ms_per_step": round(1e3 * per_tok, 2),
+            "weight_GBps": round(cfg.weight_bytes_per_token() / per_tok / 1e9, 2), "finite_logits": finite,
+            "cores": cores, "kind": "reference",
+            "sample": f"{n} Model::forward calls at positions 1..{n} after one warm-up call, {el:.1f} s, "
+                      f"{cores} OpenMP threads; model file {size / 1e9:.2f} GB written to {workdir} in "
+                      f"{t_write:.1f} s, loaded in {t_load:.1f} s (not timed)"}
+
+
 def run_reference(args, rank: int) -> None:
     if rank != 0:
         return
@@ -178,6 +286,20 @@ def run_reference(args, rank: int) -> None:
             "cpu_baseline": {"value": r["value"], "unit": "GB/s", "cores": r["cores"], "kind": r["kind"],
                              "sample": r["sample"]},
             "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if args.decode:
+        from swq.model import LlamaConfig
+        cfg = LlamaConfig(max_seq=1024)
+        log("reference decode: writing and loading the Llama-3-8B-shaped GGUF")
+        try:
+            dec = ref_decode_timing(cfg, seconds=20.0, max_tokens=max(2, min(args.steps, 16)))
+        except Exception as e:  # the GEMV line stands without it
+            dec = {"unavailable": f"{type(e).__name__}: {e}"}
+        line["decode"] = {
+            "model": "Llama-3-8B shape, Q4_K_M mix (Q6_K attn_v/ffn_down/output, Q4_K else), synthetic weights",
+            "weight_bytes_per_token": cfg.weight_bytes_per_token(),
+            "note": "the reference's Model::forward decodes one sequence per call (src/main.cpp), so a batch "
+                    "of B sequences takes B calls: its tok/s is the same at every batch size",
+            "batches": {"1": dec}}
     print(json.dumps(line), flush=True)
 
 

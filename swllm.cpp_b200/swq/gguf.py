@@ -319,11 +319,13 @@ def _pack_value(out: list, val: GGUFValue, with_type: bool = True) -> None:
 def write_gguf(path: str | os.PathLike, metadata: dict, tensors: list, alignment: int = DEFAULT_ALIGNMENT) -> None:
     """Write a version-3 GGUF file.
 
-    metadata: key -> GGUFValue, or a plain value (bool, int -> UINT32 / INT64,
-    float -> FLOAT32, str, list).  tensors: (name, GGML type, dims, data) with
-    dims innermost first (dims[0] = row length) and data the tensor's bytes
-    (any array; its raw bytes are written).  A general.alignment entry other
-    than `alignment` is rejected."""
+    metadata: key -> GGUFValue, or a plain value (bool, int -> UINT32 /
+    INT32 / INT64, float -> FLOAT32, str, list).  tensors: (name, GGML type,
+    dims, data) with dims innermost first (dims[0] = row length) and data the
+    tensor's bytes -- any array (its raw bytes are written), or a function
+    that returns one, called when the tensor is written, so a model larger
+    than memory can be written one tensor at a time.  A general.alignment
+    entry other than `alignment` is rejected."""
     meta = {k: _infer(v) for k, v in metadata.items()}
     if "general.alignment" in meta and meta["general.alignment"].to_int() != alignment:
         raise ValueError("general.alignment disagrees with the alignment argument")
@@ -331,28 +333,30 @@ def write_gguf(path: str | os.PathLike, metadata: dict, tensors: list, alignment
     for k, v in meta.items():
         _pack_value(out, GGUFValue(STRING, k), False)
         _pack_value(out, v)
-    offset, blobs = 0, []
-    for name, ttype, dims, data in tensors:
-        raw = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+    offset, infos = 0, []
+    for name, ttype, dims, _ in tensors:
         info = GGUFTensorInfo(name, len(dims), tuple(dims) + (1,) * (4 - len(dims)), ttype, offset)
-        if raw.size != info.num_bytes():
-            raise ValueError(f"tensor '{name}': {raw.size} bytes given, type {ttype} dims {dims} "
-                             f"need {info.num_bytes()}")
+        if type_block(ttype)[1] == 0:
+            raise ValueError(f"tensor '{name}': unknown GGML type {ttype}")
         _pack_value(out, GGUFValue(STRING, name), False)
         out.append(struct.pack("<I", len(dims)) + struct.pack(f"<{len(dims)}Q", *dims))
         out.append(struct.pack("<IQ", ttype, offset))
-        blobs.append((offset, raw))
-        offset = (offset + raw.size + alignment - 1) // alignment * alignment
+        infos.append(info)
+        offset = (offset + info.num_bytes() + alignment - 1) // alignment * alignment
     header = b"".join(out)
     data_offset = (len(header) + alignment - 1) // alignment * alignment
     with open(path, "wb") as f:
         f.write(header)
         f.write(b"\0" * (data_offset - len(header)))
         pos = 0
-        for off, raw in blobs:
-            f.write(b"\0" * (off - pos))
-            f.write(raw.tobytes())
-            pos = off + raw.size
+        for info, (name, ttype, dims, data) in zip(infos, tensors):
+            raw = np.ascontiguousarray(data() if callable(data) else data).view(np.uint8).reshape(-1)
+            if raw.size != info.num_bytes():
+                raise ValueError(f"tensor '{name}': {raw.size} bytes given, type {ttype} dims {dims} "
+                                 f"need {info.num_bytes()}")
+            f.write(b"\0" * (info.offset - pos))
+            f.write(raw.data)
+            pos = info.offset + raw.size
 
 
 # ---------------------------------------------------------------- Llama models

@@ -71,6 +71,30 @@ def random_blocks(type_id: int, N: int, K: int, seed: int = 0,
     return blk.reshape(N, nb * bb)
 
 
+def fast_random_blocks(type_id: int, N: int, K: int, seed: int = 0,
+                       d_scale: float = 2e-3, dmin_scale: float = 1e-3) -> np.ndarray:
+    """random_blocks' value distributions drawn from 64-bit words (about 3
+    GB/s), for model-sized matrices; the bytes differ from random_blocks' for
+    the same seed.  Q8_0 quants stay in -127..127."""
+    qk, bb, d_off, m_off = LAYOUT[type_id]
+    nb = K // qk
+    if nb * qk != K:
+        raise ValueError(f"K={K} is not a multiple of {qk}")
+    rng = np.random.default_rng(seed)
+    n = N * nb * bb
+    words = rng.integers(0, 2 ** 64, size=(n + 7) // 8, dtype=np.uint64)
+    blk = words.view(np.uint8)[:n].reshape(N, nb, bb)
+    if type_id == Q8_0:
+        q = blk[:, :, 2:]
+        q[q == 0x80] = 0x81
+    d = np.abs(rng.standard_normal((N, nb), dtype=np.float32)) * np.float32(d_scale)
+    blk[:, :, d_off:d_off + 2] = _half_bytes(d)
+    if m_off is not None:
+        dm = np.abs(rng.standard_normal((N, nb), dtype=np.float32)) * np.float32(dmin_scale)
+        blk[:, :, m_off:m_off + 2] = _half_bytes(dm)
+    return blk.reshape(N, nb * bb)
+
+
 def random_activations(M: int, K: int, seed: int = 1) -> np.ndarray:
     rng = np.random.default_rng(seed)
     return rng.standard_normal((M, K), dtype=np.float32)

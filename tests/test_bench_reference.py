@@ -1,0 +1,42 @@
+"""bench.py's reference decode leg on the CPU: a GGUF file of a dense Llama
+shape written by the bench, loaded and run by the reference's own Model
+(src/model.h compiled from source), at a tiny shape."""
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+
+def _tiny():
+    from swq.model import LlamaConfig
+    return LlamaConfig(n_layers=2, dim=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512, vocab=300, max_seq=32)
+
+
+def test_bench_model_file_reads_back(tmp_path):
+    import bench
+    from swq import gguf as G
+    cfg = _tiny()
+    size = bench.write_llama_gguf(tmp_path / "m.gguf", cfg)
+    g = G.GGUFFile(tmp_path / "m.gguf")
+    assert size == g.file_size
+    got = G.llama_config(g)
+    for k in ("n_layers", "dim", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab", "max_seq", "types"):
+        assert getattr(got, k) == getattr(cfg, k), k
+    assert np.float32(got.theta) == np.float32(cfg.theta) and np.float32(got.eps) == np.float32(cfg.eps)
+    assert g.tensors["token_embd.weight"].type == G.Q4_K
+
+
+def test_reference_decode_timing_runs(tmp_path):
+    from oracle.ref_model import model_ref_available
+    if not model_ref_available():
+        pytest.skip("reference model library not built (needs the reference sources)")
+    import bench
+    r = bench.ref_decode_timing(_tiny(), seconds=1.0, max_tokens=3, workdir=str(tmp_path))
+    assert r["finite_logits"] and r["tok_s"] > 0 and r["kind"] == "reference"
+    assert "3 Model::forward calls" in r["sample"]
+    assert list(tmp_path.iterdir()) == []  # the model file is gone
