@@ -13,6 +13,12 @@
 
 #include "model.h"
 
+// Backend the refm_* entry points load the model with: the CPU build, or
+// Backend::CUDA in the drop-in build (make_dropin.py, dropin_backend.cpp).
+#ifndef REF_BACKEND
+#define REF_BACKEND Backend::CPU
+#endif
+
 extern "C" {
 
 // ---- GGUF file ----
@@ -89,7 +95,7 @@ long long refg_array_len(void* h, const char* key) {
 // ---- model ----
 
 void* refm_load(const char* path, int context_override) {
-    auto* m = new Model(Backend::CPU);
+    auto* m = new Model(REF_BACKEND);
     if (!m->load(path, context_override)) {
         delete m;
         return nullptr;

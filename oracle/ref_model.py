@@ -5,6 +5,9 @@ TEST INFRASTRUCTURE ONLY.
 ``RefGGUF(path)``  -- GGUFFile::load (src/gguf.h:238-257) and its lookups.
 ``RefModel(path)`` -- Model::load (src/model.h:220-255) on the CPU backend;
                       ``forward(token, pos)`` is Model::forward (:257-543).
+``RefModel(path, dropin=True)`` -- the same reference code in its CUDA build
+                      with Compute::matmul_transposed_q routed to libswq
+                      (_ref/libswllm_dropin.so, make_dropin.py): the drop-in.
 """
 from __future__ import annotations
 
@@ -15,19 +18,24 @@ import numpy as np
 from . import HERE
 
 MODEL_REF_SO = HERE / "_ref" / "libswllm_model_ref.so"
-_lib = None
+DROPIN_SO = HERE / "_ref" / "libswllm_dropin.so"
+_libs: dict = {}
 
 
 def model_ref_available() -> bool:
     return MODEL_REF_SO.exists()
 
 
-def _l() -> ctypes.CDLL:
-    global _lib
-    if _lib is None:
-        if not MODEL_REF_SO.exists():
-            raise FileNotFoundError(f"{MODEL_REF_SO} not built (needs the reference sources)")
-        lib = ctypes.CDLL(str(MODEL_REF_SO))
+def dropin_available() -> bool:
+    return DROPIN_SO.exists()
+
+
+def _l(dropin: bool = False) -> ctypes.CDLL:
+    path = DROPIN_SO if dropin else MODEL_REF_SO
+    if path not in _libs:
+        if not path.exists():
+            raise FileNotFoundError(f"{path} not built (needs the reference sources)")
+        lib = ctypes.CDLL(str(path))
         vp, cp, ull = ctypes.c_void_p, ctypes.c_char_p, ctypes.c_ulonglong
         lib.refg_open.restype = vp
         lib.refg_open.argtypes = [cp]
@@ -53,8 +61,8 @@ def _l() -> ctypes.CDLL:
         lib.refm_config_f.argtypes = [vp, ctypes.POINTER(ctypes.c_float)]
         lib.refm_forward.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]
         lib.refm_clear.argtypes = [vp]
-        _lib = lib
-    return _lib
+        _libs[path] = lib
+    return _libs[path]
 
 
 class RefGGUF:
@@ -104,28 +112,35 @@ class RefModel:
     CONFIG_I = ("hidden", "ffn", "layers", "heads", "kv_heads", "head_dim", "vocab", "max_seq", "rope_neox",
                 "rope_dim")
 
-    def __init__(self, path, context_override: int = 0):
-        self.h = _l().refm_load(str(path).encode(), context_override)
+    def __init__(self, path, context_override: int = 0, dropin: bool = False):
+        self.lib, self.dropin = _l(dropin), dropin
+        self.h = self.lib.refm_load(str(path).encode(), context_override)
         if not self.h:
             raise ValueError(f"reference Model::load failed on {path}")
         ci = (ctypes.c_int * 10)()
         cf = (ctypes.c_float * 2)()
-        _l().refm_config_i(self.h, ci)
-        _l().refm_config_f(self.h, cf)
+        self.lib.refm_config_i(self.h, ci)
+        self.lib.refm_config_f(self.h, cf)
         self.config = dict(zip(self.CONFIG_I, list(ci)))
         self.config["eps"], self.config["theta"] = float(cf[0]), float(cf[1])
 
     def close(self):
         if self.h:
-            _l().refm_free(self.h)
+            self.lib.refm_free(self.h)
             self.h = None
+            if self.dropin:  # libswq's weights were keyed by the freed file buffer
+                self.lib.dropin_reset()
 
     __del__ = close
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         out = np.zeros(self.config["vocab"], np.float32)
-        _l().refm_forward(self.h, token, pos, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+        self.lib.refm_forward(self.h, token, pos, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
         return out
 
     def clear(self) -> None:
-        _l().refm_clear(self.h)
+        self.lib.refm_clear(self.h)
+
+    def dropin_errors(self) -> int:
+        """libswq calls of the drop-in build that returned an error."""
+        return self.lib.dropin_errors()
