@@ -109,6 +109,23 @@ swq_status swq_rope_kv(float* q, const float* k, const float* v, float* k_cache,
                        const int* pos, const float* freqs, int q_dim, int kv_dim, int head_dim,
                        int rope_dim, int neox, int rows, int max_seq, int ldq, int ldk, int ldv,
                        swq_stream_t stream);
+/* Prefill: no counterpart in the reference, which runs a prompt as one
+ * Model::forward per token (src/main.cpp:284-287).  The prompt's seq_len
+ * tokens of num_seqs sequences are the rows m = s*seq_len + p of q / k / v /
+ * out (token p of sequence s, at position pos0 + p; pos0 + seq_len <= max_seq),
+ * so the projections around these calls are M-row swq_gemm calls.
+ * swq_rope_kv_prefill: swq_rope_kv at each row's own position, k and v into
+ * the cache of the row's sequence.  swq_attention_prefill: causal
+ * grouped-query attention, row m over positions 0 .. pos0 + p of its
+ * sequence (src/model.h:329-361); allocates nothing; head_dim 32/64/128/256.
+ * Strides 0 mean packed rows. */
+swq_status swq_rope_kv_prefill(float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                               int pos0, int seq_len, const float* freqs, int q_dim, int kv_dim, int head_dim,
+                               int rope_dim, int neox, int num_seqs, int max_seq, int ldq, int ldk, int ldv,
+                               swq_stream_t stream);
+swq_status swq_attention_prefill(float* out, const float* q, const float* k_cache, const float* v_cache,
+                                 int pos0, int seq_len, int num_heads, int num_kv_heads, int head_dim,
+                                 int num_seqs, int max_seq, int ldq, int ldo, swq_stream_t stream);
 /* Grouped-query decode attention over positions 0 .. *pos (src/model.h:329-361),
  * split over the context; the last split of each (sequence, kv head) merges
  * the others.  `workspace`: swq_attention_workspace_bytes() bytes, caller-owned

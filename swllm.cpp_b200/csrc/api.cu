@@ -18,6 +18,7 @@
 #include "../../include/swq.h"
 #include "allreduce.h"
 #include "decode.h"
+#include "prefill.h"
 #include "gemm_tc.h"
 #include "gemv.h"
 
@@ -433,6 +434,65 @@ swq_status swq_rope_kv(float* q, const float* k, const float* v, float* k_cache,
                                              neox, rows, max_seq, ldq, ldk, ldv, dev.num_sms,
                                              reinterpret_cast<cudaStream_t>(stream)),
                          "rope launch");
+}
+
+// ---- prefill (rows m = s * seq_len + p: token p of sequence s at pos0 + p) ----
+
+static swq_status prefill_rows(int num_seqs, int seq_len, int pos0, int max_seq, int* rows) {
+    if (num_seqs < 0 || seq_len < 0 || pos0 < 0 || max_seq <= 0)
+        return fail(SWQ_ERR_BAD_SHAPE, "prefill: negative size or empty cache");
+    if (static_cast<long long>(pos0) + seq_len > max_seq)
+        return fail(SWQ_ERR_BAD_SHAPE, "prefill: pos0 + seq_len exceeds the cache (max_seq)");
+    const long long m = static_cast<long long>(num_seqs) * seq_len;
+    if (m > 0x7fffffffLL) return fail(SWQ_ERR_BAD_SHAPE, "prefill: too many rows");
+    *rows = static_cast<int>(m);
+    return SWQ_OK;
+}
+
+swq_status swq_rope_kv_prefill(float* q, const float* k, const float* v, float* k_cache, float* v_cache, int pos0,
+                               int seq_len, const float* freqs, int q_dim, int kv_dim, int head_dim, int rope_dim,
+                               int neox, int num_seqs, int max_seq, int ldq, int ldk, int ldv, swq_stream_t stream) {
+    ldq = ldq ? ldq : q_dim;
+    ldk = ldk ? ldk : kv_dim;
+    ldv = ldv ? ldv : kv_dim;
+    if (ldq < q_dim || ldk < kv_dim || ldv < kv_dim) return fail(SWQ_ERR_BAD_SHAPE, "row stride below row size");
+    if (head_dim <= 0 || rope_dim <= 0 || rope_dim > head_dim || rope_dim % 2 || q_dim <= 0 || kv_dim <= 0 ||
+        q_dim % head_dim || kv_dim % head_dim)
+        return fail(SWQ_ERR_BAD_SHAPE, "inconsistent RoPE dimensions");
+    int rows = 0;
+    swq_status st = prefill_rows(num_seqs, seq_len, pos0, max_seq, &rows);
+    if (st != SWQ_OK || rows == 0) return st;
+    if (!q || !k || !v || !k_cache || !v_cache || !freqs) return fail(SWQ_ERR_NULL_PTR, "null pointer");
+    swq::DeviceInfo dev;
+    st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::rope_kv_prefill_launch(q, k, v, k_cache, v_cache, pos0, seq_len, freqs, q_dim, kv_dim,
+                                                     head_dim, rope_dim, neox, rows, max_seq, ldq, ldk, ldv,
+                                                     reinterpret_cast<cudaStream_t>(stream)),
+                         "prefill rope launch");
+}
+
+swq_status swq_attention_prefill(float* out, const float* q, const float* k_cache, const float* v_cache, int pos0,
+                                 int seq_len, int num_heads, int num_kv_heads, int head_dim, int num_seqs,
+                                 int max_seq, int ldq, int ldo, swq_stream_t stream) {
+    if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads ||
+        (head_dim != 32 && head_dim != 64 && head_dim != 128 && head_dim != 256))
+        return fail(SWQ_ERR_BAD_SHAPE, "prefill attention: head_dim 32/64/128/256, kv heads dividing query heads");
+    const int row = num_heads * head_dim;
+    ldq = ldq ? ldq : row;
+    ldo = ldo ? ldo : row;
+    if (ldq < row || ldo < row) return fail(SWQ_ERR_BAD_SHAPE, "row stride below row size");
+    int rows = 0;
+    swq_status st = prefill_rows(num_seqs, seq_len, pos0, max_seq, &rows);
+    if (st != SWQ_OK || rows == 0) return st;
+    if (!out || !q || !k_cache || !v_cache) return fail(SWQ_ERR_NULL_PTR, "null pointer");
+    swq::DeviceInfo dev;
+    st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::attention_prefill_launch(out, q, k_cache, v_cache, pos0, seq_len, rows, num_heads,
+                                                       num_kv_heads, head_dim, max_seq, ldq, ldo,
+                                                       reinterpret_cast<cudaStream_t>(stream)),
+                         "prefill attention launch");
 }
 
 static int attention_splits_for(int rows, int num_kv_heads, int max_seq) {

@@ -87,6 +87,9 @@ def lib() -> ctypes.CDLL:
         "swq_rope_kv": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, vp]),
         "swq_attention_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
         "swq_attention_decode": (i32, [vp, vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, i32, i32, vp]),
+        "swq_rope_kv_prefill": (i32, [vp, vp, vp, vp, vp, i32, i32, vp, i32, i32, i32, i32, i32, i32, i32, i32,
+                                      i32, i32, vp]),
+        "swq_attention_prefill": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, vp]),
         "swq_silu_mul": (i32, [vp, vp, vp, i32, i32, i32, vp]),
         "swq_add": (i32, [vp, vp, i64, vp]),
         "swq_embed": (i32, [vp, vp, vp, i32, i32, i32, vp]),
@@ -258,6 +261,22 @@ def attention_decode(out, q, k_cache, v_cache, pos, workspace, workspace_bytes: 
     _raise(lib().swq_attention_decode(_ptr(out), _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(pos), _ptr(workspace),
                                       workspace_bytes, num_heads, num_kv_heads, head_dim, rows, max_seq, ldq,
                                       _stream(stream)))
+
+
+def rope_kv_prefill(q, k, v, k_cache, v_cache, pos0: int, seq_len: int, freqs, q_dim: int, kv_dim: int,
+                    head_dim: int, rope_dim: int, neox: bool, num_seqs: int, max_seq: int, ldq: int = 0, ldk: int = 0,
+                    ldv: int = 0, stream=None) -> None:
+    """RoPE + KV append for prompt rows m = s*seq_len + p at position pos0 + p."""
+    _raise(lib().swq_rope_kv_prefill(_ptr(q), _ptr(k), _ptr(v), _ptr(k_cache), _ptr(v_cache), pos0, seq_len,
+                                     _ptr(freqs), q_dim, kv_dim, head_dim, rope_dim, 1 if neox else 0, num_seqs,
+                                     max_seq, ldq, ldk, ldv, _stream(stream)))
+
+
+def attention_prefill(out, q, k_cache, v_cache, pos0: int, seq_len: int, num_heads: int, num_kv_heads: int,
+                      head_dim: int, num_seqs: int, max_seq: int, ldq: int = 0, ldo: int = 0, stream=None) -> None:
+    """Causal attention of prompt rows m = s*seq_len + p over positions 0 .. pos0 + p."""
+    _raise(lib().swq_attention_prefill(_ptr(out), _ptr(q), _ptr(k_cache), _ptr(v_cache), pos0, seq_len, num_heads,
+                                       num_kv_heads, head_dim, num_seqs, max_seq, ldq, ldo, _stream(stream)))
 
 
 def silu_mul(out, gate, up, n: int, rows: int = 1, ld: int | None = None, stream=None) -> None:

@@ -34,9 +34,9 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import lib as _lib_mod  # noqa: F401  (module import for the ctypes table)
-from .lib import (ACT_NONE, ACT_RMSNORM, ACT_SWIGLU, GEMM_NOALLOC_MAX_X_ELEMS, OPT_TENSOR_CORE_MIN_M, argmax,
-                  add_rmsnorm, attention_decode, attention_workspace_bytes, decode_advance, dequant, embed,
-                  gemm_act, get_option, rmsnorm, rope_kv, silu_mul)
+from .lib import (ACT_NONE, ACT_RMSNORM, ACT_SWIGLU, GEMM_NOALLOC_MAX_X_ELEMS, OPT_TENSOR_CORE_MIN_M, add, argmax,
+                  add_rmsnorm, attention_decode, attention_prefill, attention_workspace_bytes, decode_advance,
+                  dequant, embed, gemm_act, get_option, rmsnorm, rope_kv, rope_kv_prefill, silu_mul)
 from .synth import LAYOUT, Q4_K, Q6_K, Q8_0, row_bytes
 
 
@@ -409,6 +409,105 @@ class LlamaDecoder:
         if greedy:
             argmax(self.logits, c.vocab, B, self.tokens, self.history, self.step_no, stream=s)
             decode_advance(self.pos, self.step_no, stream=s)
+
+    def prefill(self, prompts, pos0: int = 0, all_logits: bool = False):
+        """Batched prefill: the prompt tokens of every sequence through the whole
+        model at once -- M = rows x P activation rows, every projection one
+        M-row tensor-core GEMM, causal attention over each sequence's cache
+        (swq_rope_kv_prefill, swq_attention_prefill).  The reference runs a
+        prompt as P calls of Model::forward (src/main.cpp:284-287); the logits
+        of each position are the same computation.
+
+        prompts: rows lists (or a [rows, P] array) of P token ids, written at
+        positions pos0 .. pos0 + P - 1 of each sequence's KV cache.  Afterwards
+        the decoder continues from there: self.logits holds the last prompt
+        position's logits, tokens = their argmax (also history[0]), pos =
+        pos0 + P, and generate() decodes on.  all_logits: also return the
+        logits of every prompt position, [rows, P, vocab] (one process)."""
+        import torch
+        c, B, s = self.cfg, self.rows, self.stream
+        toks = np.asarray(prompts, dtype=np.int32)
+        if toks.ndim != 2 or toks.shape[0] != B or toks.shape[1] < 1:
+            raise ValueError(f"prompts must be {B} lists of at least one token, got shape {toks.shape}")
+        P = int(toks.shape[1])
+        if pos0 < 0 or pos0 + P > c.max_seq:
+            raise ValueError(f"positions {pos0}..{pos0 + P - 1} do not fit max_seq={c.max_seq}")
+        if np.any((toks < 0) | (toks >= c.vocab)):
+            raise ValueError("token id outside the vocabulary")
+        tp = self.world > 1
+        if tp and all_logits:
+            raise ValueError("all_logits needs the whole vocabulary on one process")
+        M, dev, gemm = B * P, self.device, self._gemm
+        qd, kvd, ffn, hd = self.q_dim, self.kv_dim, self.ffn, c.head_dim
+        ld = qd + kvd
+        f32 = dict(dtype=torch.float32, device=dev)
+        with torch.cuda.stream(s):
+            tok_d = torch.from_numpy(toks.reshape(-1)).to(dev, non_blocking=False)
+            x = torch.empty((M, c.dim), **f32)
+            xn, d = torch.empty_like(x), torch.empty_like(x)
+            qk = torch.empty((M, ld), **f32)
+            v = torch.empty((M, kvd), **f32)
+            att = torch.empty((M, qd), **f32)
+            gu = torch.empty((M, 2 * ffn), **f32)
+            h = torch.empty((M, ffn), **f32)
+            embed(x, self.token_embd, tok_d, c.dim, c.vocab, M, stream=s)
+            rmsnorm(xn, x, self.layers[0]["attn_norm"], c.dim, c.eps, M, stream=s)
+            for li, L in enumerate(self.layers):
+                t = L["types"]
+                if "w_qk" in L:
+                    gemm(t["wq"], L["w_qk"], xn, qk, M, ld, c.dim, s)
+                else:
+                    gemm(t["wq"], L["wq"], xn, att, M, qd, c.dim, s)
+                    qk[:, :qd].copy_(att)
+                    gemm(t["wk"], L["wk"], xn, v, M, kvd, c.dim, s)
+                    qk[:, qd:].copy_(v)
+                gemm(t["wv"], L["wv"], xn, v, M, kvd, c.dim, s)
+                kc, vc = self.kcache[li], self.vcache[li]
+                rope_kv_prefill(qk, qk[:, qd:], v, kc, vc, pos0, P, self.freqs, qd, kvd, hd, hd, c.rope_neox, B,
+                                c.max_seq, ldq=ld, ldk=ld, ldv=kvd, stream=s)
+                attention_prefill(att, qk, kc, vc, pos0, P, self.nh, self.nkv, hd, B, c.max_seq, ldq=ld, ldo=qd,
+                                  stream=s)
+                gemm(t["wo"], L["wo"], att, d, M, c.dim, qd, s)
+                if tp:
+                    self._nccl_all_reduce(d)
+                add_rmsnorm(xn, x, d, L["ffn_norm"], c.dim, c.eps, M, stream=s)  # x += o; xn = norm(x)
+                if "w_gate_up" in L:
+                    gemm(t["w_gate"], L["w_gate_up"], xn, gu, M, 2 * ffn, c.dim, s)
+                else:
+                    gemm(t["w_gate"], L["w_gate"], xn, h, M, ffn, c.dim, s)
+                    gu[:, :ffn].copy_(h)
+                    gemm(t["w_up"], L["w_up"], xn, h, M, ffn, c.dim, s)
+                    gu[:, ffn:].copy_(h)
+                silu_mul(h, gu, gu[:, ffn:], ffn, M, 2 * ffn, stream=s)
+                gemm(t["w_down"], L["w_down"], h, d, M, c.dim, ffn, s)
+                if tp:
+                    self._nccl_all_reduce(d)
+                if li + 1 < len(self.layers):
+                    add_rmsnorm(xn, x, d, self.layers[li + 1]["attn_norm"], c.dim, c.eps, M, stream=s)
+                else:
+                    add(x, d, M * c.dim, stream=s)
+            t_out = c.types["output"]
+            every = None
+            if all_logits:
+                rmsnorm(xn, x, self.output_norm, c.dim, c.eps, M, stream=s)
+                every = torch.empty((M, c.vocab), **f32)
+                gemm(t_out, self.output, xn, every, M, c.vocab, c.dim, s)
+                self.logits.copy_(every.view(B, P, c.vocab)[:, P - 1])
+            else:
+                x_last = x.view(B, P, c.dim)[:, P - 1].contiguous()
+                xl = torch.empty_like(x_last)
+                rmsnorm(xl, x_last, self.output_norm, c.dim, c.eps, B, stream=s)
+                if tp:
+                    gemm(t_out, self.output, xl, self.logits_l, B, self.vocab, c.dim, s)
+                    self._gather_logits()
+                else:
+                    gemm(t_out, self.output, xl, self.logits, B, c.vocab, c.dim, s)
+            self.step_no.fill_(0)
+            argmax(self.logits, c.vocab, B, self.tokens, self.history, self.step_no, stream=s)
+            self.pos.fill_(pos0 + P)
+            self.step_no.fill_(1)
+        self.steps_issued = 1
+        return None if every is None else every.view(B, P, c.vocab)
 
     def capture(self) -> None:
         """Capture one greedy step in a CUDA graph (after one eager warm-up step

@@ -58,6 +58,32 @@ def test_gemv_argument_errors():
     assert _rc(L.swq_gemm, kat.Q4_K, None, None, None, 0, 4, 256, None) is Status.OK
 
 
+def test_prefill_argument_errors():
+    """Prompt rows past the cache, unsupported head sizes, null pointers: each
+    rejected before anything runs; zero rows is a no-op."""
+    L = lib()
+    # rope: (q, k, v, kc, vc, pos0, seq_len, freqs, q_dim, kv_dim, head_dim, rope_dim, neox, seqs, max_seq, ld x3)
+    rope = lambda pos0, P, hd=64, rd=64, seqs=1, q=1: _rc(  # noqa: E731
+        L.swq_rope_kv_prefill, q, 1, 1, 1, 1, pos0, P, 1, 512, 128, hd, rd, 0, seqs, 16, 0, 0, 0, None)
+    assert rope(10, 7) is Status.BAD_SHAPE           # positions 10..16 past max_seq 16
+    assert b"max_seq" in L.swq_last_error()
+    assert rope(-1, 2) is Status.BAD_SHAPE
+    assert rope(0, 4, rd=63) is Status.BAD_SHAPE     # odd rotary dimension
+    assert rope(0, 4, hd=96) is Status.BAD_SHAPE     # 512 is not a multiple of 96
+    assert rope(0, 4, q=None) is Status.NULL_PTR
+    assert rope(0, 0, q=None) is Status.OK           # no rows
+    assert rope(0, 4, seqs=0, q=None) is Status.OK
+    # attention: (out, q, kc, vc, pos0, seq_len, heads, kv_heads, head_dim, seqs, max_seq, ldq, ldo)
+    att = lambda pos0, P, H=8, Hkv=2, hd=64, out=1, ldq=0: _rc(  # noqa: E731
+        L.swq_attention_prefill, out, 1, 1, 1, pos0, P, H, Hkv, hd, 1, 16, ldq, 0, None)
+    assert att(0, 17) is Status.BAD_SHAPE
+    assert att(0, 4, Hkv=3) is Status.BAD_SHAPE      # kv heads must divide query heads
+    assert att(0, 4, hd=96) is Status.BAD_SHAPE      # head_dim 32/64/128/256
+    assert att(0, 4, ldq=100) is Status.BAD_SHAPE    # row stride below 8 x 64
+    assert att(0, 4, out=None) is Status.NULL_PTR
+    assert att(0, 0, out=None) is Status.OK
+
+
 def test_dequant_argument_errors():
     L = lib()
     assert _rc(L.swq_dequant, 1, 1, 1, 32, None) is Status.BAD_TYPE
