@@ -469,6 +469,41 @@ def run_swq(args, rank: int, world: int) -> None:
         print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- prefill workload
+def run_prefill(rank: int, prompt: int = 512, reps: int = 3, warmup: int = 1, seventy: bool = False) -> dict:
+    """Batched prefill of one `prompt`-token sequence of uniform-random token
+    ids through a Llama-3-8B-shaped (or, with seventy, Llama-3-70B-shaped)
+    Q4_K_M model with synthetic weights on one GPU: LlamaDecoder.prefill, every
+    projection one M-row tensor-core GEMM, CUDA-event timed on the decode
+    stream (median of `reps` after `warmup`).  TFLOP/s counts the projections
+    only: 2 x prompt x the layers' weight elements, plus the LM head for the
+    last row (attention excluded)."""
+    import numpy as np
+    import torch
+
+    from swq.model import LlamaConfig, LlamaDecoder
+
+    cfg = (LlamaConfig.llama3_70b if seventy else LlamaConfig)(max_seq=prompt + 8)
+    dec = LlamaDecoder(cfg, rows=1, seed=300 + rank)
+    toks = np.random.default_rng(5).integers(0, cfg.vocab, size=(1, prompt)).tolist()
+    # layer projections for every prompt row, the LM head for the last row only
+    flops = 2.0 * prompt * cfg.n_layers * sum(n * k for n, k in cfg.shapes().values()) + 2.0 * cfg.vocab * cfg.dim
+    ms = []
+    for i in range(warmup + reps):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(dec.stream)
+        dec.prefill(toks)
+        ev1.record(dec.stream)
+        ev1.synchronize()
+        if i >= warmup:
+            ms.append(ev0.elapsed_time(ev1))
+    t = statistics.median(ms)
+    return {"model": ("Llama-3-70B" if seventy else "Llama-3-8B") + " shape, Q4_K_M mix, synthetic weights",
+            "prompt_tokens": prompt, "ms": round(t, 2), "tok_s": round(prompt / (t * 1e-3), 1),
+            "projection_TFLOPs": round(flops / (t * 1e-3) / 1e12, 1),
+            "finite_logits": bool(torch.isfinite(dec.logits).all().item()), "reps_ms": [round(x, 2) for x in ms]}
+
+
 # ---------------------------------------------------------------- decode workload
 def run_decode(rank: int, world: int, batches=(1, 16), prefill: int = 512, steps: int = 256,
                warmup: int = 5) -> dict:
@@ -829,10 +864,12 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["swq", "reference"], default="swq")
-    ap.add_argument("--workload", choices=["gemv", "gemm", "decode", "decode70b", "moe"], default="gemv",
+    ap.add_argument("--workload", choices=["gemv", "gemm", "decode", "decode70b", "moe", "prefill", "prefill70b"],
+                    default="gemv",
                     help="gemv: the headline Q4_K GEMV (with decode tok/s); gemm: the prefill dequant-GEMM; "
                          "decode: Llama-3-8B greedy decode tok/s alone (replicas); decode70b: Llama-3-70B "
-                         "decode tok/s, tensor-parallel over the ranks")
+                         "decode tok/s, tensor-parallel over the ranks; prefill / prefill70b: batched prefill "
+                         "of one prompt (--M tokens, default 512) on one GPU")
     ap.add_argument("--format", choices=sorted(TYPE_IDS), default="Q4_K", help="GEMM weight format")
     ap.add_argument("--M", type=int, default=512, help="GEMM activation rows (below 5: the GEMV kernel)")
     ap.add_argument("--N", type=int, default=GEMM_N, help="GEMM weight rows")
@@ -871,6 +908,18 @@ def main() -> None:
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
+        return
+    if args.workload in ("prefill", "prefill70b"):
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        if world > 1 and rank == 0:
+            log("prefill runs on one GPU; other ranks exit")
+        if rank != 0:
+            return
+        d = run_prefill(rank, prompt=args.M, seventy=args.workload == "prefill70b")
+        print(json.dumps({"metric": f"prefill tok/s ({d['model']}, {args.M}-token prompt)", "value": d["tok_s"],
+                          "unit": "tok/s", "n_gpus": 1, "higher_is_better": True, "data": "synthetic",
+                          "prefill": d}), flush=True)
         return
     if args.workload in ("decode", "decode70b"):
         import torch
