@@ -450,7 +450,9 @@ class LlamaDecoder:
             att = torch.empty((M, qd), **f32)
             gu = torch.empty((M, 2 * ffn), **f32)
             h = torch.empty((M, ffn), **f32)
-            embed(x, self.token_embd, tok_d, c.dim, c.vocab, M, stream=s)
+            for r0 in range(0, M, 65535):  # the embedding kernel's grid holds 65535 rows
+                r1 = min(M, r0 + 65535)
+                embed(x[r0:r1], self.token_embd, tok_d[r0:r1], c.dim, c.vocab, r1 - r0, stream=s)
             rmsnorm(xn, x, self.layers[0]["attn_norm"], c.dim, c.eps, M, stream=s)
             for li, L in enumerate(self.layers):
                 t = L["types"]
