@@ -279,3 +279,45 @@ def test_restated_forward_matches_reference_live(files, variant):
     toks = [3, 250, 17, 17, 88, 1, 299, 42]
     for pos, tok in enumerate(toks):
         assert rel_l2(ref.forward(tok, pos), m.forward(tok, pos)) <= FORWARD_TOL, pos
+
+
+@pytest.mark.parametrize("ttype", [G.F32, G.F16, G.BF16])
+def test_float_tables_as_reference_dequantize(tmp_path, ttype):
+    """F32 / F16 / BF16 norm and embedding tables read as the reference's
+    dequantize() reads them at load (src/tensor.h:451-460): bit for bit,
+    subnormals, infinities and signed zeros included."""
+    from oracle import ref_available, ref_dequantize
+    bits = np.random.default_rng(3).integers(0, 2 ** 16, size=4096, dtype=np.uint16)
+    bits[:6] = [0x0000, 0x8000, 0x0001, 0x7C00, 0xFC00, 0x03FF]
+    data = np.random.default_rng(4).standard_normal(4096).astype(np.float32) if ttype == G.F32 else bits
+    p = tmp_path / "f.gguf"
+    G.write_gguf(p, {"general.architecture": "llama"}, [("t", ttype, (data.size,), data)])
+    got = G.GGUFFile(p).float_array("t")
+    if ttype == G.F32:
+        assert np.array_equal(got.view(np.uint32), data.view(np.uint32))
+    if ref_available():
+        want = ref_dequantize(ttype, data.view(np.uint8), data.size)
+        nan = np.isnan(want)
+        assert np.array_equal(np.isnan(got), nan)
+        assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32))
+
+
+def test_tensor_ranks_and_writer_errors(tmp_path):
+    p = tmp_path / "r.gguf"
+    t3 = np.arange(24, dtype=np.float32)
+    t4 = synth.random_blocks(G.Q8_0, 4, 64, seed=5)
+    G.write_gguf(p, {}, [("three", G.F32, (2, 3, 4), t3), ("four", G.Q8_0, (64, 2, 1, 2), t4)])
+    g = G.GGUFFile(p)
+    assert g.tensors["three"].dims == (2, 3, 4, 1) and g.tensors["three"].num_elements() == 24
+    assert g.tensors["four"].num_bytes() == t4.nbytes and g.blocks("four").shape == (4, 68)
+    with pytest.raises(ValueError):  # bytes do not match the type and dims
+        G.write_gguf(tmp_path / "e1.gguf", {}, [("x", G.F32, (5,), np.zeros(4, np.float32))])
+    with pytest.raises(ValueError):  # no such GGML type
+        G.write_gguf(tmp_path / "e2.gguf", {}, [("x", 99, (4,), np.zeros(4, np.uint8))])
+    with pytest.raises(ValueError):
+        G.write_gguf(tmp_path / "e3.gguf", {"general.alignment": 64}, [], alignment=32)
+    with pytest.raises(TypeError):  # mixed array element types
+        G.write_gguf(tmp_path / "e4.gguf", {"a": [1, "x"]}, [])
+    with pytest.raises(G.GGUFError):  # rows not whole blocks
+        G.write_gguf(tmp_path / "e5.gguf", {}, [("q", G.Q4_K, (100, 1), np.zeros(0, np.uint8))])
+        G.GGUFFile(tmp_path / "e5.gguf").blocks("q")
