@@ -133,15 +133,27 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU arm
-def cpu_gemv_timing(seconds: float, max_steps: int | None = None, copies: int = 16) -> dict:
-    """The reference CPU routine on all host cores, one 4096x4096 Q4_K GEMV per
-    step, rotating over `copies` weight matrices (151 MB, beyond the LLC)."""
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_gemv_timing(seconds: float, max_steps: int | None = None, copies: int = 16, threads: int = 0) -> dict:
+    """The reference CPU routine on all host cores (or `threads`), one
+    4096x4096 Q4_K GEMV per step, rotating over `copies` weight matrices
+    (151 MB, beyond the LLC)."""
     import numpy as np
 
     import oracle
     from swq import synth
 
-    cores = oracle.host_cores()
+    cores = threads or oracle.host_cores()
     if oracle.ref_available():
         kind = "reference"
         oracle.ref_set_threads(cores)
@@ -277,6 +289,9 @@ def run_reference(args, rank: int) -> None:
         return
     budget = 60.0  # seconds of CPU work for the whole --steps run
     r = cpu_gemv_timing(seconds=budget, max_steps=max(1, args.steps))
+    one = cpu_gemv_timing(seconds=5.0, max_steps=max(1, args.steps), copies=4, threads=1)
+    import oracle
+    (oracle.ref_set_threads if oracle.ref_available() else oracle.set_threads)(oracle.host_cores())
     line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "GB/s",
             "n_gpus": args.gpus, "steps": r["steps"], "warmup": args.warmup,
             "ms_per_step": round(1e3 * r["seconds"] / r["steps"], 4), "higher_is_better": True,
@@ -284,7 +299,8 @@ def run_reference(args, rank: int) -> None:
             "config": {"workload": f"Q4_K GEMV N={N_ROWS} K={K_COLS} M=1 (reference CPU path)",
                        "format": "Q4_K", "N": N_ROWS, "K": K_COLS, "M": 1},
             "cpu_baseline": {"value": r["value"], "unit": "GB/s", "cores": r["cores"], "kind": r["kind"],
-                             "sample": r["sample"]},
+                             "sample": r["sample"], "cpu_model": cpu_model(),
+                             "single_thread": {"value": one["value"], "unit": "GB/s", "sample": one["sample"]}},
             "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if args.decode:
         from swq.model import LlamaConfig

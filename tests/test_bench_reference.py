@@ -40,3 +40,10 @@ def test_reference_decode_timing_runs(tmp_path):
     assert r["finite_logits"] and r["tok_s"] > 0 and r["kind"] == "reference"
     assert "3 Model::forward calls" in r["sample"]
     assert list(tmp_path.iterdir()) == []  # the model file is gone
+
+
+def test_cpu_gemv_timing_threads():
+    import bench
+    r = bench.cpu_gemv_timing(seconds=0.2, max_steps=2, copies=2, threads=1)
+    assert r["cores"] == 1 and r["value"] > 0 and "1 OpenMP threads" in r["sample"]
+    assert isinstance(bench.cpu_model(), str)
