@@ -253,6 +253,8 @@ def ref_decode_timing(cfg, seconds: float = 20.0, max_tokens: int = 8, workdir: 
     if free < est + (2 << 30):
         return {"unavailable": f"{free / 1e9:.1f} GB free in {workdir}, the model file needs {est / 1e9:.1f} GB"}
     need_ram = est + cfg.vocab * cfg.dim * 4 + (4 << 30)  # the file in memory + the fp32 embedding table
+    if workdir.startswith("/dev/shm"):  # the file itself sits in memory until it is loaded and deleted
+        need_ram += est
     if 0 < _mem_available() < need_ram:
         return {"unavailable": f"{_mem_available() / 1e9:.1f} GB of host memory available, "
                                f"{need_ram / 1e9:.1f} GB needed"}
