@@ -19,8 +19,8 @@ from .lib import (  # noqa: F401
     OPT_EARLY_WEIGHT_PREFETCH, OPT_GEMV_MAX_M, OPT_Q2K_REFERENCE_CPU_ORDER, OPT_TENSOR_CORE_GEMM,
     OPT_TENSOR_CORE_MIN_M, OPT_GEMV_SMEM_KB, OPT_GEMV_STAGE_KB, OPT_GEMV_CTAS_PER_SM,
     ACT_NONE, ACT_RMSNORM, ACT_SWIGLU,
-    add, add_rmsnorm, argmax, attention_decode, attention_workspace_bytes, decode_advance, embed,
-    rmsnorm, rope_kv, silu_mul,
+    add, add_rmsnorm, argmax, attention_decode, attention_prefill, attention_workspace_bytes, decode_advance, embed,
+    rmsnorm, rope_kv, rope_kv_prefill, silu_mul,
     GEMM_NOALLOC_MAX_X_ELEMS, SwqError, Status, block_size, build, check, dequant, exported_symbols, gemm,
     gemm_act, gemm_noalloc, gemv, grouped_gemm, grouped_gemv,
     get_option, header_symbols, lib, lib_path, set_option, type_size,
