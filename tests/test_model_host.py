@@ -1,0 +1,156 @@
+"""LlamaDecoder's host logic on the CPU: which libswq operations a decode
+step, a prefill and a GGUF load issue, with what sizes, strides and buffers.
+
+The device operations are replaced by recorders (no kernel runs) and the
+decoder's tensors live on the CPU, so this checks only the wiring: per-layer
+GGML types reach the right projections, stacked q/k and gate/up matrices are
+used exactly when a layer's types allow it, prefill rows and cache slices are
+laid out as the kernels expect, and the decoder's state after a prefill.
+The numerics are the GPU tests' (test_gpu_model.py, test_gpu_x_prefill.py,
+test_gpu_whole_model_files.py)."""
+import contextlib
+
+import numpy as np
+import pytest
+import torch
+
+import llama_gguf as LG
+import swq.model as M
+from swq import synth
+from test_gpu_model import _small, _weights
+
+OPS = ("embed", "rmsnorm", "add_rmsnorm", "gemm_act", "rope_kv", "attention_decode", "silu_mul", "argmax",
+       "decode_advance", "rope_kv_prefill", "attention_prefill", "add", "dequant")
+
+
+class _Stream:
+    def synchronize(self):
+        pass
+
+
+@pytest.fixture
+def calls(monkeypatch):
+    log = []
+
+    def recorder(name):
+        def f(*a, **kw):
+            log.append((name, a, kw))
+        return f
+
+    for name in OPS:
+        monkeypatch.setattr(M, name, recorder(name))
+    monkeypatch.setattr(torch.cuda, "Stream", lambda device=None: _Stream())
+    monkeypatch.setattr(torch.cuda, "stream", lambda s: contextlib.nullcontext())
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda device=None: _Stream())
+    return log
+
+
+def _gemms(log):
+    """(type, weight tensor, M, N, K) of every projection, in order."""
+    return [(a[0], a[1], a[4], a[5], a[6]) for name, a, _ in log if name == "gemm_act"]
+
+
+def _mixed_cfg():
+    cfg = _small()
+    cfg.layer_types = ({"wq": synth.Q4_K, "wk": synth.Q4_K, "wv": synth.Q6_K, "wo": synth.Q4_K,
+                        "w_gate": synth.Q4_K, "w_up": synth.Q4_K, "w_down": synth.Q6_K},
+                       {"wq": synth.Q5_K, "wk": synth.Q8_0, "wv": synth.Q8_0, "wo": synth.Q2_K,
+                        "w_gate": synth.Q3_K, "w_up": synth.Q4_0, "w_down": synth.Q4_K})
+    return cfg
+
+
+def _weights_for(cfg, seed):
+    rng = np.random.default_rng(seed)
+    layers = []
+    for li in range(cfg.n_layers):
+        lt = cfg.layer_type_map(li)
+        L = {"attn_norm": np.ones(cfg.dim, np.float32), "ffn_norm": np.ones(cfg.dim, np.float32)}
+        for k, (n, kk) in cfg.shapes().items():
+            L[k] = synth.random_blocks(lt[k], n, kk, seed=seed + 10 * li + len(L))
+        layers.append(L)
+    return {"token_embd": rng.standard_normal((cfg.vocab, cfg.dim)).astype(np.float32),
+            "output_norm": np.ones(cfg.dim, np.float32),
+            "output": synth.random_blocks(cfg.types["output"], cfg.vocab, cfg.dim, seed=seed + 99), "layers": layers}
+
+
+def test_step_uses_each_layers_types(calls):
+    cfg = _mixed_cfg()
+    dec = M.LlamaDecoder(cfg, rows=1, device="cpu", weights=_weights_for(cfg, 5))
+    assert "w_qk" in dec.layers[0] and "w_gate_up" in dec.layers[0]
+    assert "w_qk" not in dec.layers[1] and "w_gate_up" not in dec.layers[1]  # types differ: separate matrices
+    dec.step()
+    g = _gemms(calls)
+    qd, kvd, ffn, dim = dec.q_dim, dec.kv_dim, dec.ffn, cfg.dim
+    L0, L1 = dec.layers
+    want = [(synth.Q4_K, L0["w_qk"], 1, qd + kvd, dim), (synth.Q6_K, L0["wv"], 1, kvd, dim),
+            (synth.Q4_K, L0["wo"], 1, dim, qd), (synth.Q4_K, L0["w_gate_up"], 1, 2 * ffn, dim),
+            (synth.Q6_K, L0["w_down"], 1, dim, ffn),
+            (synth.Q5_K, L1["wq"], 1, qd, dim), (synth.Q8_0, L1["wk"], 1, kvd, dim),
+            (synth.Q8_0, L1["wv"], 1, kvd, dim), (synth.Q2_K, L1["wo"], 1, dim, qd),
+            (synth.Q3_K, L1["w_gate"], 1, ffn, dim), (synth.Q4_0, L1["w_up"], 1, ffn, dim),
+            (synth.Q4_K, L1["w_down"], 1, dim, ffn), (cfg.types["output"], dec.output, 1, cfg.vocab, dim)]
+    assert len(g) == len(want)
+    for got, exp in zip(g, want):
+        assert got[0] == exp[0] and got[1] is exp[1] and got[2:] == exp[2:], (got[0], got[2:], exp[0], exp[2:])
+    # weight bytes per token follow the per-layer mix
+    per_layer = [sum(n * synth.row_bytes(cfg.layer_type_map(li)[k], kk) for k, (n, kk) in cfg.shapes().items())
+                 for li in range(2)]
+    assert cfg.weight_bytes_per_token() == sum(per_layer) + cfg.vocab * synth.row_bytes(cfg.types["output"], dim)
+
+
+@pytest.mark.parametrize("rows,P,pos0,every", [(1, 7, 0, True), (3, 5, 2, False)])
+def test_prefill_wiring(calls, rows, P, pos0, every):
+    cfg = _small()
+    dec = M.LlamaDecoder(cfg, rows=rows, device="cpu", weights=_weights(cfg, seed=9))
+    prompts = [[(5 * r + 3 * p) % cfg.vocab for p in range(P)] for r in range(rows)]
+    out = dec.prefill(prompts, pos0=pos0, all_logits=every)
+    Mr, qd, kvd, ffn = rows * P, dec.q_dim, dec.kv_dim, dec.ffn
+    names = [c[0] for c in calls]
+    assert names[0] == "embed" and calls[0][1][5] == Mr
+    ropes = [c for c in calls if c[0] == "rope_kv_prefill"]
+    atts = [c for c in calls if c[0] == "attention_prefill"]
+    assert len(ropes) == len(atts) == cfg.n_layers
+    for li, (r, a) in enumerate(zip(ropes, atts)):
+        ra, rk = r[1], r[2]
+        assert ra[3] is not None and ra[3].data_ptr() == dec.kcache[li].data_ptr()  # this layer's cache
+        assert (ra[5], ra[6], ra[8], ra[9], ra[13], ra[14]) == (pos0, P, qd, kvd, rows, cfg.max_seq)
+        assert ra[1].data_ptr() == ra[0].data_ptr() + 4 * qd  # k: the columns after q in the same rows
+        assert rk == {"ldq": qd + kvd, "ldk": qd + kvd, "ldv": kvd, "stream": dec.stream}
+        aa, ak = a[1], a[2]
+        assert (aa[4], aa[5], aa[6], aa[7], aa[9], aa[10]) == (pos0, P, dec.nh, dec.nkv, rows, cfg.max_seq)
+        assert ak["ldq"] == qd + kvd and ak["ldo"] == qd
+    g = _gemms(calls)
+    assert all(x[2] == Mr for x in g[:-1])                 # every layer projection has M = rows x P
+    assert g[-1][2] == (Mr if every else rows) and g[-1][3] == cfg.vocab
+    assert names[-1] == "argmax"
+    assert int(dec.pos.item()) == pos0 + P and int(dec.step_no.item()) == 1 and dec.steps_issued == 1
+    assert (out is not None) == every and (out is None or tuple(out.shape) == (rows, P, cfg.vocab))
+
+
+def test_prefill_rejects_bad_prompts(calls):
+    cfg = _small()
+    dec = M.LlamaDecoder(cfg, rows=2, device="cpu", weights=_weights(cfg, seed=9))
+    with pytest.raises(ValueError):
+        dec.prefill([[1, 2, 3]])                           # one prompt for two rows
+    with pytest.raises(ValueError):
+        dec.prefill([[1] * 60, [2] * 60], pos0=10)         # past max_seq = 64
+    with pytest.raises(ValueError):
+        dec.prefill([[1, cfg.vocab], [2, 3]])              # token id outside the vocabulary
+    assert calls == []
+
+
+def test_from_gguf_wiring(calls, tmp_path):
+    """The tied file: a Q8_0 embedding table dequantized on the device (once,
+    vocab x dim elements) and used as the LM head; the mix file: every
+    layer's projections with its own types."""
+    dec = M.LlamaDecoder.from_gguf(LG.write(tmp_path / "t.gguf", "tied"), device="cpu")
+    dq = [c for c in calls if c[0] == "dequant"]
+    assert len(dq) == 1 and dq[0][1][0] == synth.Q8_0 and dq[0][1][3] == dec.cfg.vocab * dec.cfg.dim
+    assert dec.cfg.types["output"] == synth.Q8_0 and dec.output.numel() == dec.cfg.vocab * dec.cfg.dim // 32 * 34
+    calls.clear()
+    dec = M.LlamaDecoder.from_gguf(LG.write(tmp_path / "m.gguf", "mix"), device="cpu")
+    dec.step()
+    types = [x[0] for x in _gemms(calls)]
+    v = LG.VARIANTS["mix"]["layers"]
+    assert types == [v[0]["wq"], v[0]["wv"], v[0]["wo"], v[0]["w_gate"], v[0]["w_down"],
+                     v[1]["wq"], v[1]["wv"], v[1]["wo"], v[1]["w_gate"], v[1]["w_down"], synth.Q6_K]
