@@ -154,3 +154,37 @@ def test_from_gguf_wiring(calls, tmp_path):
     v = LG.VARIANTS["mix"]["layers"]
     assert types == [v[0]["wq"], v[0]["wv"], v[0]["wo"], v[0]["w_gate"], v[0]["w_down"],
                      v[1]["wq"], v[1]["wv"], v[1]["wo"], v[1]["w_gate"], v[1]["w_down"], synth.Q6_K]
+
+
+@pytest.mark.parametrize("rank", [0, 1])
+def test_tensor_parallel_shards_with_mixed_types(calls, monkeypatch, rank):
+    """Rank r of 2 keeps rows [r N/2, (r+1) N/2) of the column-parallel
+    matrices and whole blocks of columns [r K/2, (r+1) K/2) of wo and w_down,
+    whatever each layer's block size (32 or 256 elements)."""
+    import swq.parallel as P
+    monkeypatch.setattr(P, "_world", lambda group: (rank, 2))
+    cfg = _mixed_cfg()
+    W = _weights_for(cfg, 5)
+    dec = M.LlamaDecoder(cfg, rows=1, device="cpu", weights=W, group=object(), collective="nccl")
+    assert (dec.nh, dec.nkv, dec.ffn, dec.vocab) == (4, 1, 512, 500)
+    for li, L in enumerate(dec.layers):
+        lt = cfg.layer_type_map(li)
+        for key, (N, K) in cfg.shapes().items():
+            qk, bb = synth.block_geometry(lt[key])
+            full = W["layers"][li][key].reshape(N, K // qk, bb)
+            if key in ("wo", "w_down"):
+                nb = K // qk // 2
+                want = full[:, rank * nb:(rank + 1) * nb]
+            else:
+                want = full[rank * N // 2:(rank + 1) * N // 2]
+            if key in ("wq", "wk") and "w_qk" in L:
+                nq = dec.q_dim * synth.row_bytes(lt["wq"], K)
+                got = L["w_qk"][:nq] if key == "wq" else L["w_qk"][nq:]
+            elif key in ("w_gate", "w_up") and "w_gate_up" in L:
+                ng = dec.ffn * synth.row_bytes(lt["w_gate"], K)
+                got = L["w_gate_up"][:ng] if key == "w_gate" else L["w_gate_up"][ng:]
+            else:
+                got = L[key]
+            assert np.array_equal(got.numpy(), want.reshape(-1)), (li, key)
+    out = W["output"].reshape(cfg.vocab, -1)[rank * 500:(rank + 1) * 500]
+    assert np.array_equal(dec.output.numpy(), out.reshape(-1))
