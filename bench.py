@@ -523,6 +523,28 @@ def run_prefill(rank: int, prompt: int = 512, reps: int = 3, warmup: int = 1, se
 
 
 # ---------------------------------------------------------------- decode workload
+# How the decode measurements build their context: "synthetic" (random K/V in
+# the cache, Decoder.fill_kv) or "prefill" (LlamaDecoder.prefill of uniform
+# random prompt tokens, timed on its own and reported as prefill_ms).
+DECODE_CONTEXT = "synthetic"
+
+
+def _build_context(dec, n: int, seed: int) -> dict:
+    """Positions 0..n-1 of every sequence, then the decoder stands at position n."""
+    import numpy as np
+    import torch
+    if DECODE_CONTEXT == "prefill":
+        toks = np.random.default_rng(seed).integers(0, dec.cfg.vocab, size=(dec.rows, n)).tolist()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(dec.stream)
+        dec.prefill(toks)
+        ev1.record(dec.stream)
+        ev1.synchronize()
+        return {"context": f"prefill of {n} uniform random tokens", "prefill_ms": round(ev0.elapsed_time(ev1), 2)}
+    dec.reset([(7 * i + 1) % dec.cfg.vocab for i in range(dec.rows)], 0)
+    dec.fill_kv(n)
+    return {"context": f"synthetic K/V for {n} positions"}
+
 def run_decode(rank: int, world: int, batches=(1, 16), prefill: int = 512, steps: int = 256,
                warmup: int = 5) -> dict:
     """Greedy decode of a Llama-3-8B-shaped model (32 layers, hidden 4096,
@@ -546,8 +568,7 @@ def run_decode(rank: int, world: int, batches=(1, 16), prefill: int = 512, steps
         dec = LlamaDecoder(cfg, rows=B, seed=100 + rank)
         dec.reset(list(range(B)), 0)
         dec.capture()
-        dec.reset([(7 * i + 1) % cfg.vocab for i in range(B)], 0)
-        dec.fill_kv(prefill)
+        ctx = _build_context(dec, prefill, seed=11)
         dec.generate(warmup)
         dec.stream.synchronize()
         if dist:
@@ -567,7 +588,7 @@ def run_decode(rank: int, world: int, batches=(1, 16), prefill: int = 512, steps
         out["batches"][str(B)] = {
             "tok_s": round(B * steps * world / (ms * 1e-3), 1), "ms_per_step": round(per_tok_ms, 4),
             "weight_GBps": round(cfg.weight_bytes_per_token() / (per_tok_ms * 1e-3) / 1e9, 1),
-            "finite_logits": ok}
+            "finite_logits": ok, **ctx}
         del dec
         torch.cuda.empty_cache()
     return out
@@ -608,8 +629,7 @@ def run_decode_tp(rank: int, world: int, batches=(1, 8, 32), context: int = 2048
         import swq
         swq.check(dec.stream)  # a collective that timed out fails here, not in the timed loop
         log(f"decode70b: tp={world} batch {B}: captured")
-        dec.reset([(7 * i + 1) % cfg.vocab for i in range(B)], 0)
-        dec.fill_kv(context)
+        ctx = _build_context(dec, context, seed=13)  # the same prompt on every rank
         dec.generate(warmup)
         dec.stream.synchronize()
         swq.check(dec.stream)
@@ -630,7 +650,7 @@ def run_decode_tp(rank: int, world: int, batches=(1, 8, 32), context: int = 2048
         out["batches"][str(B)] = {
             "tok_s": round(B * steps / (ms * 1e-3), 1), "ms_per_step": round(per_step, 3),
             "weight_GBps_per_gpu": round(wbytes / world / (per_step * 1e-3) / 1e9, 1),
-            "finite_logits": ok}
+            "finite_logits": ok, **ctx}
         dec.graph = None  # release the graph (it holds NCCL calls) before the next one
         if dec is not base:
             del dec
@@ -897,7 +917,12 @@ def main() -> None:
                     help="decode70b: sums of the row-parallel projections")
     ap.add_argument("--no-decode", dest="decode", action="store_false",
                     help="skip the Llama-3-8B decode tok/s measurement of the default run")
+    ap.add_argument("--decode-context", choices=["synthetic", "prefill"], default="synthetic",
+                    help="decode measurements: context as random K/V (synthetic) or a batched prefill of "
+                         "random prompt tokens (prefill, also timed)")
     args = ap.parse_args()
+    global DECODE_CONTEXT
+    DECODE_CONTEXT = args.decode_context
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":

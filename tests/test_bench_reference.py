@@ -47,3 +47,25 @@ def test_cpu_gemv_timing_threads():
     r = bench.cpu_gemv_timing(seconds=0.2, max_steps=2, copies=2, threads=1)
     assert r["cores"] == 1 and r["value"] > 0 and "1 OpenMP threads" in r["sample"]
     assert isinstance(bench.cpu_model(), str)
+
+
+def test_decode_context_synthetic_is_the_kv_fill():
+    """The default decode context: the same tokens and random K/V fill the
+    decode measurements always used."""
+    import bench
+
+    class Dec:
+        rows = 3
+        cfg = type("Cfg", (), {"vocab": 1000})()
+
+        def reset(self, tokens, pos):
+            self.reset_args = (list(tokens), pos)
+
+        def fill_kv(self, n):
+            self.filled = n
+
+    assert bench.DECODE_CONTEXT == "synthetic"
+    d = Dec()
+    out = bench._build_context(d, 512, seed=1)
+    assert d.reset_args == ([1, 8, 15], 0) and d.filled == 512
+    assert out == {"context": "synthetic K/V for 512 positions"}
