@@ -8,6 +8,7 @@ on the full-attention, dense-FFN path, in fp32 numpy:
   per layer: xb = rmsnorm(x, attn_norm)                   (:272, src/tensor.h:1028-1033)
              q, k, v = W{q,k,v} . xb                       (:284-289)
              rope(q, k) at pos, interleaved pairs          (:322-323, src/tensor.h:1068-1107)
+               (pairs (i, i + head_dim/2) for the neox architectures, :1121-1161)
              cache k, v at pos                             (:326-327)
              per head: scores = q.k_t / sqrt(head_dim), t <= pos; softmax; out = sum p v_t
                                                            (:329-361, src/tensor.h:1036-1047)
@@ -64,6 +65,20 @@ def rope_interleaved(vec: np.ndarray, head_dim: int, pos: int, freqs: np.ndarray
     return out
 
 
+def rope_neox(vec: np.ndarray, head_dim: int, pos: int, freqs: np.ndarray) -> np.ndarray:
+    """Pairs (i, i + head_dim/2) (cpu_rope_neox_apply, src/tensor.h:1121-1161)."""
+    out = vec.astype(F32).copy()
+    half = head_dim // 2
+    for h in range(len(vec) // head_dim):
+        for i in range(half):
+            angle = F32(pos) * freqs[i]
+            c, s = np.cos(angle, dtype=F32), np.sin(angle, dtype=F32)
+            a, b = out[h * head_dim + i], out[h * head_dim + i + half]
+            out[h * head_dim + i] = a * c - b * s
+            out[h * head_dim + i + half] = b * c + a * s
+    return out
+
+
 def softmax(x: np.ndarray) -> np.ndarray:
     m = x.max()
     e = np.exp((x - m).astype(F32)).astype(F32)
@@ -97,8 +112,9 @@ class RefLlama:
             q = matmul(t["wq"], L["wq"], xb, q_dim, c.dim)
             k = matmul(t["wk"], L["wk"], xb, kv_dim, c.dim)
             v = matmul(t["wv"], L["wv"], xb, kv_dim, c.dim)
-            q = rope_interleaved(q, hd, pos, self.freqs)
-            k = rope_interleaved(k, hd, pos, self.freqs)
+            rope = rope_neox if getattr(c, "rope_neox", False) else rope_interleaved
+            q = rope(q, hd, pos, self.freqs)
+            k = rope(k, hd, pos, self.freqs)
             self.kc[li, pos], self.vc[li, pos] = k, v
             att = np.zeros(q_dim, F32)
             mul = nh // nkv

@@ -15,7 +15,7 @@ stores, per variant:
                                         max_seq, rope_neox, rope_dim
                               config_f -- rms_norm_eps, rope_theta
 
-usage: python tests/golden/make_golden_model.py
+usage: python tests/golden/make_golden_model.py [variant ...]   (default: all)
 """
 from __future__ import annotations
 
@@ -35,7 +35,7 @@ from oracle.ref_model import RefModel  # noqa: E402
 
 def main() -> None:
     with tempfile.TemporaryDirectory(dir=REPO / "tests" / "golden") as tmp:
-        for variant in llama_gguf.VARIANTS:
+        for variant in sys.argv[1:] or llama_gguf.VARIANTS:
             path = llama_gguf.write(Path(tmp) / f"{variant}.gguf", variant)
             m = RefModel(path)
             logits = np.stack([m.forward(tok, pos) for pos, tok in enumerate(llama_gguf.TOKENS)])

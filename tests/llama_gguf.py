@@ -12,6 +12,9 @@ its SHA-256 and the reference's logits are stored (tests/golden/).
 * "tied": the same shape with a Q4_K_M-style mix on both layers, a Q8_0
           embedding table and no output.weight (the LM head is the
           embedding table, src/model.h:776-779), as small Llama models ship.
+* "neox": the same shape under the "qwen2" architecture name (no biases),
+          which the reference runs with neox RoPE, pairs (i, i + head_dim/2)
+          (src/model.h:629-634).
 """
 from __future__ import annotations
 
@@ -37,6 +40,9 @@ VARIANTS = {
     "tied": dict(
         alignment=32, embd=G.Q8_0, output=None, vocab_key=True,
         layers=[dict(wq=G.Q4_K, wk=G.Q4_K, wv=G.Q6_K, wo=G.Q4_K, w_gate=G.Q4_K, w_up=G.Q4_K, w_down=G.Q6_K)] * 2),
+    "neox": dict(
+        arch="qwen2", alignment=32, embd=G.F32, output=G.Q6_K, vocab_key=True,
+        layers=[dict(wq=G.Q4_K, wk=G.Q4_K, wv=G.Q6_K, wo=G.Q4_K, w_gate=G.Q4_K, w_up=G.Q4_K, w_down=G.Q6_K)] * 2),
 }
 
 
@@ -50,25 +56,26 @@ def _shapes(s):
 def write(path: Path, variant: str) -> Path:
     """Write the variant's GGUF file at path."""
     v, s = VARIANTS[variant], SHAPE
-    rng = np.random.default_rng({"mix": 11, "tied": 12}[variant])
+    a = v.get("arch", "llama")
+    rng = np.random.default_rng({"mix": 11, "tied": 12, "neox": 13}[variant])
     meta = {
-        "general.architecture": "llama",
+        "general.architecture": a,
         "general.name": f"tiny-{variant}",
         "general.alignment": v["alignment"],
-        "llama.context_length": s["context"],
-        "llama.embedding_length": s["hidden"],
-        "llama.block_count": s["layers"],
-        "llama.feed_forward_length": s["ffn"],
-        "llama.attention.head_count": s["heads"],
-        "llama.attention.head_count_kv": s["kv_heads"],
-        "llama.rope.freq_base": G.GGUFValue(G.FLOAT32, 500000.0),
-        "llama.attention.layer_norm_rms_epsilon": G.GGUFValue(G.FLOAT32, 1e-5),
+        f"{a}.context_length": s["context"],
+        f"{a}.embedding_length": s["hidden"],
+        f"{a}.block_count": s["layers"],
+        f"{a}.feed_forward_length": s["ffn"],
+        f"{a}.attention.head_count": s["heads"],
+        f"{a}.attention.head_count_kv": s["kv_heads"],
+        f"{a}.rope.freq_base": G.GGUFValue(G.FLOAT32, 500000.0),
+        f"{a}.attention.layer_norm_rms_epsilon": G.GGUFValue(G.FLOAT32, 1e-5),
         "tokenizer.ggml.model": "llama",
         "tokenizer.ggml.tokens": [f"<t{i}>" for i in range(s["vocab"])],
         "tokenizer.ggml.scores": [float(-i) for i in range(s["vocab"])],
     }
     if v["vocab_key"]:
-        meta["llama.vocab_size"] = s["vocab"]
+        meta[f"{a}.vocab_size"] = s["vocab"]
     tensors = []
 
     def norm(name):

@@ -2,7 +2,8 @@
 
 The tiny Llama GGUF files of tests/llama_gguf.py ("mix": all seven formats,
 a different type mix per layer, F32 embedding table; "tied": a Q8_0 embedding
-table that is also the LM head), teacher-forced over the golden tokens, against
+table that is also the LM head; "neox": an architecture the reference runs
+with neox RoPE), teacher-forced over the golden tokens, against
 the logits the reference's CPU build produced (tests/golden/golden_llama_*.npz):
 
 * LlamaDecoder.from_gguf -- libswq's device decode step;
@@ -22,7 +23,7 @@ from test_gpu_model import LOGIT_TOL, _teacher_forced
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("variant", ["mix", "tied"])
+@pytest.mark.parametrize("variant", ["mix", "tied", "neox"])
 def test_gguf_model_matches_reference_logits(cuda, tmp_path, variant):
     """LlamaDecoder.from_gguf on a tiny GGUF file -- "mix": all seven formats,
     a different type mix per layer, F32 embedding table; "tied": a Q8_0
@@ -45,7 +46,7 @@ def test_gguf_model_matches_reference_logits(cuda, tmp_path, variant):
             assert int(np.argmax(got[pos, 0])) == int(np.argmax(want)), pos
 
 
-@pytest.mark.parametrize("variant", ["mix", "tied"])
+@pytest.mark.parametrize("variant", ["mix", "tied", "neox"])
 def test_reference_model_runs_on_libswq(cuda, tmp_path, variant):
     """The drop-in: the reference's own Model::load / Model::forward, built with
     its CUDA backend and the one matmul branch of tensor.h calling
