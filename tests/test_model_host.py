@@ -188,3 +188,22 @@ def test_tensor_parallel_shards_with_mixed_types(calls, monkeypatch, rank):
             assert np.array_equal(got.numpy(), want.reshape(-1)), (li, key)
     out = W["output"].reshape(cfg.vocab, -1)[rank * 500:(rank + 1) * 500]
     assert np.array_equal(dec.output.numpy(), out.reshape(-1))
+
+
+def test_tensor_parallel_prefill_collectives(calls, monkeypatch):
+    """Two sums per layer (after o and down, on the M-row partial outputs) and
+    one gather of the vocab-sharded logits, in that order on every rank."""
+    import swq.parallel as P
+    monkeypatch.setattr(P, "_world", lambda group: (1, 2))
+    cfg = _small()
+    dec = M.LlamaDecoder(cfg, rows=2, device="cpu", weights=_weights(cfg, seed=9), group=object(),
+                         collective="nccl")
+    seen = []
+    monkeypatch.setattr(dec, "_nccl_all_reduce", lambda t: seen.append(("sum", tuple(t.shape))))
+    monkeypatch.setattr(dec, "_gather_logits", lambda: seen.append(("gather",)))
+    dec.prefill([[1, 2, 3], [4, 5, 6]])
+    assert seen == [("sum", (6, cfg.dim))] * (2 * cfg.n_layers) + [("gather",)]
+    g = _gemms(calls)
+    assert g[-1][1] is dec.output and g[-1][2:] == (2, cfg.vocab // 2, cfg.dim)  # this rank's vocab rows
+    with pytest.raises(ValueError):
+        dec.prefill([[1, 2], [3, 4]], all_logits=True)  # the whole vocabulary lives on no single rank
