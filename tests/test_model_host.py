@@ -207,3 +207,23 @@ def test_tensor_parallel_prefill_collectives(calls, monkeypatch):
     assert g[-1][1] is dec.output and g[-1][2:] == (2, cfg.vocab // 2, cfg.dim)  # this rank's vocab rows
     with pytest.raises(ValueError):
         dec.prefill([[1, 2], [3, 4]], all_logits=True)  # the whole vocabulary lives on no single rank
+
+
+def test_tensor_parallel_step_collectives(calls, monkeypatch):
+    """A decode step on the peer all-reduce: two sums per layer of the
+    [rows, dim] partial outputs on the decode stream, then the logits gather."""
+    import swq.comm as C
+    import swq.parallel as P
+    monkeypatch.setattr(P, "_world", lambda group: (0, 2))
+    seen = []
+
+    def fake_shared(n, group=None, device=None):
+        assert n == 3 * _small().dim  # rows x dim floats per sum
+        return lambda t, stream=None: seen.append(("sum", tuple(t.shape), stream))
+
+    monkeypatch.setattr(C, "shared_peer_allreduce", fake_shared)
+    cfg = _small()
+    dec = M.LlamaDecoder(cfg, rows=3, device="cpu", weights=_weights(cfg, seed=9), group=object())
+    monkeypatch.setattr(dec, "_gather_logits", lambda: seen.append(("gather",)))
+    dec.step()
+    assert seen == [("sum", (3, cfg.dim), dec.stream)] * (2 * cfg.n_layers) + [("gather",)]
