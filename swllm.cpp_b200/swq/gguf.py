@@ -251,10 +251,10 @@ class GGUFFile:
         dims[1] = N rows, src/model.h:729-758)."""
         info = self.tensors[name]
         bs, ts = type_block(info.type)
-        K, N = info.dims[0], info.num_elements() // info.dims[0]
-        if ts == 0 or K % bs:
+        K = info.dims[0]
+        if ts == 0 or K == 0 or K % bs:
             raise GGUFError(f"tensor '{name}': type {info.type} rows of {K} elements are not whole blocks")
-        return self.get_tensor_data(name).reshape(N, K // bs * ts)
+        return self.get_tensor_data(name).reshape(info.num_elements() // K, K // bs * ts)
 
     def float_array(self, name: str) -> np.ndarray:
         """An F32 / F16 / BF16 tensor as float32 (exact conversions)."""
