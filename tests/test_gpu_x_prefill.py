@@ -118,3 +118,21 @@ def test_prefill_logits_match_reference(cuda, rows, P):
         want = ref.forward(int(first[r]), P)
         assert rel_l2(after[r], want) <= TC_LOGIT_TOL, (r, rel_l2(after[r], want))
         assert hist[1, r] == int(np.argmax(after[r]))
+
+
+@pytest.mark.parametrize("variant", ["mix", "tied", "neox"])
+def test_gguf_prefill_matches_reference_logits(cuda, tmp_path, variant):
+    """A GGUF file's prompt in one prefill (6 rows: the tensor-core GEMMs)
+    against the logits of the reference's own Model::forward run token by
+    token on the same file (tests/golden/golden_llama_<variant>.npz)."""
+    import llama_gguf as LG
+    from conftest import GOLDEN
+    gold = np.load(GOLDEN / f"golden_llama_{variant}.npz")
+    path = LG.write(tmp_path / "m.gguf", variant)
+    assert LG.sha256(path) == str(gold["sha256"])
+    dec = LlamaDecoder.from_gguf(path, rows=1)
+    every = dec.prefill([gold["tokens"].tolist()], all_logits=True)
+    dec.stream.synchronize()
+    got = every[0].cpu().numpy()
+    for p in range(got.shape[0]):
+        assert rel_l2(got[p], gold["logits"][p]) <= TC_LOGIT_TOL, (p, rel_l2(got[p], gold["logits"][p]))
