@@ -321,3 +321,65 @@ def test_tensor_ranks_and_writer_errors(tmp_path):
     with pytest.raises(G.GGUFError):  # rows not whole blocks
         G.write_gguf(tmp_path / "e5.gguf", {}, [("q", G.Q4_K, (100, 1), np.zeros(0, np.uint8))])
         G.GGUFFile(tmp_path / "e5.gguf").blocks("q")
+
+
+def _random_gguf(rng, path):
+    """A random, valid GGUF file: every metadata value type (nested arrays
+    too), tensors of every GGML type and rank 1-4, an uncommon alignment."""
+    scalar_types = [G.UINT8, G.INT8, G.UINT16, G.INT16, G.UINT32, G.INT32, G.FLOAT32, G.BOOL, G.UINT64, G.INT64,
+                    G.FLOAT64]
+    lims = {G.UINT8: (0, 255), G.INT8: (-128, 127), G.UINT16: (0, 65535), G.INT16: (-32768, 32767),
+            G.UINT32: (0, 2 ** 32 - 1), G.INT32: (-2 ** 31, 2 ** 31 - 1), G.UINT64: (0, 2 ** 64 - 1),
+            G.INT64: (-2 ** 63, 2 ** 63 - 1)}
+
+    def value(t):
+        if t in lims:
+            lo, hi = lims[t]
+            return G.GGUFValue(t, int(rng.integers(lo, hi, endpoint=True, dtype=np.uint64 if t == G.UINT64
+                                                   else np.int64)))
+        if t == G.BOOL:
+            return G.GGUFValue(t, bool(rng.integers(0, 2)))
+        if t in (G.FLOAT32, G.FLOAT64):
+            return G.GGUFValue(t, float(np.float32(rng.standard_normal())) if t == G.FLOAT32
+                               else float(rng.standard_normal()))
+        return G.GGUFValue(G.STRING, "".join(chr(int(c)) for c in rng.integers(32, 0x2FF, size=rng.integers(0, 12))))
+
+    meta = {}
+    for i in range(int(rng.integers(1, 25))):
+        kind = rng.integers(0, 4)
+        if kind == 0:
+            v = value(G.STRING)
+        elif kind == 1:
+            v = value(scalar_types[rng.integers(len(scalar_types))])
+        elif kind == 2:
+            t = [G.STRING, *scalar_types][rng.integers(len(scalar_types) + 1)]
+            v = G.GGUFValue(G.ARRAY, [value(t) for _ in range(rng.integers(0, 6))], t)
+        else:
+            inner = scalar_types[rng.integers(len(scalar_types))]
+            v = G.GGUFValue(G.ARRAY, [G.GGUFValue(G.ARRAY, [value(inner) for _ in range(rng.integers(0, 3))], inner)
+                                      for _ in range(rng.integers(0, 3))], G.ARRAY)
+        meta[f"k{i}.{rng.integers(1000)}"] = v
+    alignment = int([8, 16, 32, 64, 128][rng.integers(5)])
+    meta["general.alignment"] = G.GGUFValue(G.UINT32, alignment)
+    tensors = []
+    for i in range(int(rng.integers(0, 8))):
+        t = list(G.GGML_TYPES)[rng.integers(len(G.GGML_TYPES))]
+        bs, ts = G.type_block(t)
+        rank = int(rng.integers(1, 5))
+        dims = [int(bs * rng.integers(1, 4))] + [int(rng.integers(1, 4)) for _ in range(rank - 1)]
+        n = int(np.prod(dims)) // bs * ts
+        tensors.append((f"t{i}", t, tuple(dims), rng.integers(0, 256, size=n, dtype=np.uint8)))
+    G.write_gguf(path, meta, tensors, alignment=alignment)
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_random_files_read_as_reference(tmp_path, seed):
+    ref_model = _model_ref()
+    p = tmp_path / f"r{seed}.gguf"
+    _random_gguf(np.random.default_rng(1000 + seed), p)
+    _compare_with_reference(ref_model, p)
+    g = G.GGUFFile(p)
+    for name, info in g.tensors.items():  # and the bytes are where both say they are
+        raw = p.read_bytes()
+        off = g.tensor_file_offset(name)
+        assert np.array_equal(g.get_tensor_data(name), np.frombuffer(raw[off:off + info.num_bytes()], np.uint8))
