@@ -383,3 +383,25 @@ def test_random_files_read_as_reference(tmp_path, seed):
         raw = p.read_bytes()
         off = g.tensor_file_offset(name)
         assert np.array_equal(g.get_tensor_data(name), np.frombuffer(raw[off:off + info.num_bytes()], np.uint8))
+
+
+def test_minimal_header_as_reference_test(tmp_path):
+    """The reference's tests/test_gguf.cpp:199-243 builds a GGUF v3 header with
+    no metadata and no tensors: magic 0x46554747 ("GGUF"), version 3, two
+    zero u64 counts.  The writer emits exactly those 24 bytes for an empty
+    file; the reader (and the reference's) parse it, the data section at 32."""
+    p = tmp_path / "min.gguf"
+    G.write_gguf(p, {}, [])
+    raw = p.read_bytes()
+    assert raw[:4] == b"GGUF" and raw[:24] == struct.pack("<IIQQ", 0x46554747, 3, 0, 0)
+    g = G.GGUFFile(p)
+    assert (g.version, g.tensor_count, g.metadata_kv_count, g.data_offset) == (3, 0, 0, 32)
+    p24 = tmp_path / "min24.gguf"
+    p24.write_bytes(raw[:24])  # the reference test's buffer, no padding
+    g24 = G.GGUFFile(p24)
+    assert (g24.version, g24.tensors, g24.metadata) == (3, {}, {})
+    from oracle.ref_model import model_ref_available
+    if model_ref_available():
+        from oracle.ref_model import RefGGUF
+        r = RefGGUF(p24)
+        assert (r.version, r.tensor_count, r.metadata_kv_count, r.data_offset) == (3, 0, 0, 32)
