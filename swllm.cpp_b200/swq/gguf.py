@@ -474,8 +474,12 @@ def llama_weights(g: GGUFFile, cfg) -> dict:
         output = te_blocks  # quantized (checked by llama_config)
     layers = []
     for li in range(cfg.n_layers):
-        L = {"attn_norm": vec(f"blk.{li}.attn_norm.weight", cfg.dim),
-             "ffn_norm": vec(f"blk.{li}.ffn_norm.weight", cfg.dim)}
+        # files that name the post-attention norm post_attention_norm
+        # instead of ffn_norm: the reference's fallback, src/model.h:838-844
+        ffn_norm = f"blk.{li}.ffn_norm.weight"
+        if ffn_norm not in g.tensors and f"blk.{li}.post_attention_norm.weight" in g.tensors:
+            ffn_norm = f"blk.{li}.post_attention_norm.weight"
+        L = {"attn_norm": vec(f"blk.{li}.attn_norm.weight", cfg.dim), "ffn_norm": vec(ffn_norm, cfg.dim)}
         for key, (N, K) in cfg.shapes().items():
             name = f"blk.{li}.{_MATRICES[key]}.weight"
             check_shape(name, N, K)

@@ -405,3 +405,39 @@ def test_minimal_header_as_reference_test(tmp_path):
         from oracle.ref_model import RefGGUF
         r = RefGGUF(p24)
         assert (r.version, r.tensor_count, r.metadata_kv_count, r.data_offset) == (3, 0, 0, 32)
+
+
+def test_context_cap_known_answers(tmp_path):
+    """The reference's test_context_auto_cap (tests/test_gguf.cpp:1040-1072):
+    40960 -> 4096 without an override, 4096 unchanged, an explicit 2048 kept."""
+    g = G.GGUFFile(files_with(tmp_path, {"llama.context_length": 40960}))
+    assert G.llama_config(g).max_seq == 4096 and G.llama_config(g, 2048).max_seq == 2048
+    g = G.GGUFFile(files_with(tmp_path, {"llama.context_length": 4096}))
+    assert G.llama_config(g).max_seq == 4096
+
+
+def test_qwen3_architecture_config(tmp_path):
+    """The reference's test_qwen3_config (tests/test_gguf.cpp:727-760): qwen3
+    runs neox RoPE, head_dim = hidden / heads."""
+    src = G.GGUFFile(LG.write(tmp_path / "b.gguf", "tied"))
+    meta = {k.replace("llama.", "qwen3."): v for k, v in src.metadata.items()}
+    meta["general.architecture"] = "qwen3"
+    cfg = G.llama_config(G.GGUFFile(files_with(tmp_path, meta)))
+    assert cfg.rope_neox and cfg.head_dim == cfg.dim // cfg.n_heads
+
+
+def test_post_attention_norm_fallback(tmp_path):
+    """Without ffn_norm.weight the post-attention norm is read from
+    post_attention_norm.weight, as the reference's load_weights does
+    (src/model.h:838-844, tests/test_gguf.cpp:1358-1398)."""
+    src = G.GGUFFile(LG.write(tmp_path / "b.gguf", "tied"))
+    norm = src.float_array("blk.1.ffn_norm.weight").copy()
+    p = files_with(tmp_path, {}, drop=("blk.1.ffn_norm.weight",),
+                   extra_tensors=[("blk.1.post_attention_norm.weight", G.F32, (norm.size,), norm)])
+    g = G.GGUFFile(p)
+    W = G.llama_weights(g, G.llama_config(g))
+    assert np.array_equal(W["layers"][1]["ffn_norm"], norm)
+    p2 = files_with(tmp_path, {}, drop=("blk.1.ffn_norm.weight",))
+    with pytest.raises(G.GGUFError):
+        g2 = G.GGUFFile(p2)
+        G.llama_weights(g2, G.llama_config(g2))
