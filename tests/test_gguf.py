@@ -441,3 +441,23 @@ def test_post_attention_norm_fallback(tmp_path):
     with pytest.raises(G.GGUFError):
         g2 = G.GGUFFile(p2)
         G.llama_weights(g2, G.llama_config(g2))
+
+
+def test_restated_rope_known_answers():
+    """The reference's test_cpu_rope / _gqa / _neox (tests/test_gguf.cpp:508-600)
+    on the restatement's two RoPE functions: identity at position 0; at
+    position 1 a unit vector turns by angle 1 (freq 1/theta^0) into
+    (cos 1, sin 1), on the next element (interleaved) or the one head_dim/2
+    away (neox), alike in every head (GQA)."""
+    from oracle.model_ref import rope_interleaved, rope_neox
+    freqs = (1.0 / np.power(np.float32(10000.0), np.arange(2, dtype=np.float32) * 2 / np.float32(4))).astype(
+        np.float32)
+    c, s = np.cos(np.float32(1.0)), np.sin(np.float32(1.0))
+    for rope in (rope_interleaved, rope_neox):
+        v = np.array([1, 2, 3, 4, 5, 6, 7, 8], np.float32)
+        assert np.allclose(rope(v, 4, 0, freqs), v, atol=1e-5)
+    q = np.array([1, 0, 0, 0, 1, 0, 0, 0], np.float32)
+    out = rope_interleaved(q, 4, 1, freqs)
+    assert np.allclose(out[[0, 1, 4, 5]], [c, s, c, s], atol=1e-5)
+    out = rope_neox(q, 4, 1, freqs)
+    assert np.allclose(out[[0, 2, 4, 6]], [c, s, c, s], atol=1e-5)
