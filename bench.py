@@ -546,26 +546,42 @@ def _build_context(dec, n: int, seed: int) -> dict:
     return {"context": f"synthetic K/V for {n} positions"}
 
 def run_decode(rank: int, world: int, batches=(1, 16), prefill: int = 512, steps: int = 256,
-               warmup: int = 5) -> dict:
+               warmup: int = 5, gguf: str | None = None) -> dict:
     """Greedy decode of a Llama-3-8B-shaped model (32 layers, hidden 4096,
     32/8 heads of 128, FFN 14336, vocab 128256, Q4_K_M mix, synthetic weights
     generated on the device) after a synthetic 512-token context: `steps`
     graph-replayed steps per batch size, CUDA-event timed.  Every rank runs its
-    own model (replicas); tok/s is summed over ranks (max time over ranks)."""
+    own model (replicas); tok/s is summed over ranks (max time over ranks).
+    gguf: the model of that GGUF file instead (its weights uploaded once and
+    shared by the batch sizes)."""
     import torch
 
     from swq.model import LlamaConfig, LlamaDecoder
 
-    cfg = LlamaConfig(max_seq=prefill + steps + warmup + 8)
-    out = {"model": "Llama-3-8B shape, Q4_K_M mix (Q6_K attn_v/ffn_down/output, Q4_K else), synthetic weights",
-           "context": prefill, "steps": steps,
+    need = prefill + steps + warmup + 8
+    W = None
+    if gguf is None:
+        cfg = LlamaConfig(max_seq=need)
+        model = "Llama-3-8B shape, Q4_K_M mix (Q6_K attn_v/ffn_down/output, Q4_K else), synthetic weights"
+    else:
+        from swq.gguf import llama_from_gguf
+        cfg, W, _file = llama_from_gguf(gguf, context_override=need)
+        if cfg.max_seq < need:
+            raise ValueError(f"{gguf}: context {cfg.max_seq} < the {need} positions this run needs")
+        model = f"GGUF file {os.path.basename(gguf)} ({cfg.n_layers} layers, hidden {cfg.dim}, vocab {cfg.vocab})"
+    out = {"model": model, "context": prefill, "steps": steps,
            "weight_bytes_per_token": cfg.weight_bytes_per_token(), "batches": {}}
     dist = None
     if world > 1:
         import torch.distributed as dist
+    first = None
     for B in batches:
         log(f"decode8b: batch {B} (one model per rank)")
-        dec = LlamaDecoder(cfg, rows=B, seed=100 + rank)
+        if gguf is None:
+            dec = LlamaDecoder(cfg, rows=B, seed=100 + rank)
+        else:
+            dec = LlamaDecoder(cfg, rows=B, weights=None if first else W, weights_from=first)
+            first = first or dec
         dec.reset(list(range(B)), 0)
         dec.capture()
         ctx = _build_context(dec, prefill, seed=11)
@@ -589,8 +605,9 @@ def run_decode(rank: int, world: int, batches=(1, 16), prefill: int = 512, steps
             "tok_s": round(B * steps * world / (ms * 1e-3), 1), "ms_per_step": round(per_tok_ms, 4),
             "weight_GBps": round(cfg.weight_bytes_per_token() / (per_tok_ms * 1e-3) / 1e9, 1),
             "finite_logits": ok, **ctx}
-        del dec
-        torch.cuda.empty_cache()
+        if dec is not first:
+            del dec
+            torch.cuda.empty_cache()
     return out
 
 
@@ -917,6 +934,8 @@ def main() -> None:
                     help="decode70b: sums of the row-parallel projections")
     ap.add_argument("--no-decode", dest="decode", action="store_false",
                     help="skip the Llama-3-8B decode tok/s measurement of the default run")
+    ap.add_argument("--gguf", default=None, help="--workload decode: decode this GGUF model file instead of "
+                                                  "the synthetic Llama-3-8B-shaped one")
     ap.add_argument("--decode-context", choices=["synthetic", "prefill"], default="synthetic",
                     help="decode measurements: context as random K/V (synthetic) or a batched prefill of "
                          "random prompt tokens (prefill, also timed)")
@@ -975,8 +994,10 @@ def main() -> None:
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                     device_id=torch.device("cuda", local))
         if args.workload == "decode":
-            d = run_decode(rank, world, steps=args.steps if args.steps != ap.get_default("steps") else 256)
-            name, scaling = "decode tok/s (Llama-3-8B Q4_K_M, batch 1)", "weak"
+            d = run_decode(rank, world, steps=args.steps if args.steps != ap.get_default("steps") else 256,
+                           gguf=args.gguf)
+            name = f"decode tok/s ({'Llama-3-8B Q4_K_M' if args.gguf is None else d['model']}, batch 1)"
+            scaling = "weak"
         else:
             d = run_decode_tp(rank, world, steps=args.steps if args.steps != ap.get_default("steps") else 32,
                               collective=args.collective)
