@@ -9,6 +9,12 @@ It mirrors the reference's interface for this path (src/tensor.h):
   keep weights and activations resident on the GPU (torch tensors or raw
   pointers).
 
+Around them: ``swq.model.LlamaDecoder`` (device decode step and batched
+prefill, CUDA graphs, tensor parallelism; ``from_gguf`` loads a model file),
+``swq.gguf`` (GGUF reader and writer, read as the reference's GGUFFile,
+src/gguf.h), ``swq.parallel`` / ``swq.comm`` (parallel layers, expert-parallel
+MoE, peer all-reduce).
+
 All arithmetic runs in the CUDA kernels of libswq.  There is no CPU fallback:
 if the library is missing or the GPU is not an sm_100 part, calls raise.
 """
