@@ -46,3 +46,23 @@ def test_dropin_library_calls_libswq():
     # the drop-in's libswq is the very library the package loads
     assert ctypes.cast(d.swq_ctx_matmul_transposed_q, ctypes.c_void_p).value == \
         ctypes.cast(swq.lib().swq_ctx_matmul_transposed_q, ctypes.c_void_p).value
+
+
+def test_dropin_fails_loudly_without_a_gpu(tmp_path, capfd):
+    """No GPU: the reference's model loads, but every quantized matmul of its
+    forward goes to libswq, which reports an error (printed and counted) --
+    the drop-in has no silent CPU fallback for the seven formats."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present (the GPU test runs the drop-in)")
+    from oracle.ref_model import RefModel, dropin_available
+    if not dropin_available():
+        pytest.skip("drop-in build not made (needs the reference sources)")
+    import llama_gguf as LG
+    m = RefModel(LG.write(tmp_path / "m.gguf", "mix"), dropin=True)
+    before = m.dropin_errors()  # the count is per process
+    m.forward(7, 0)
+    # 2 layers x 7 projections + the LM head, every one refused
+    assert m.dropin_errors() - before == 15
+    assert "swq:" in capfd.readouterr().err
+    m.close()
