@@ -109,6 +109,15 @@ swq_status swq_rope_kv(float* q, const float* k, const float* v, float* k_cache,
                        const int* pos, const float* freqs, int q_dim, int kv_dim, int head_dim,
                        int rope_dim, int neox, int rows, int max_seq, int ldq, int ldk, int ldv,
                        swq_stream_t stream);
+/* The optional steps between the q/k/v projections and RoPE of the reference's
+ * dense forward (src/model.h:291-318): q += bq, k += bk, v += bv
+ * (Compute::add), then the RMSNorm of every q head with q_norm and every k
+ * head with k_norm ([head_dim] weights shared by the heads; Compute::rmsnorm
+ * with rms_norm_eps).  In place on `rows` rows (strides ldq / ldk / ldv, 0:
+ * packed); any of the six vectors may be NULL (nothing to do for it). */
+swq_status swq_qkv_bias_norm(float* q, float* k, float* v, const float* bq, const float* bk, const float* bv,
+                              const float* q_norm, const float* k_norm, int q_dim, int kv_dim, int head_dim,
+                              float eps, int rows, int ldq, int ldk, int ldv, swq_stream_t stream);
 /* Prefill: no counterpart in the reference, which runs a prompt as one
  * Model::forward per token (src/main.cpp:284-287).  The prompt's seq_len
  * tokens of num_seqs sequences are the rows m = s*seq_len + p of q / k / v /

@@ -7,6 +7,7 @@ on the full-attention, dense-FFN path, in fp32 numpy:
   x = token_embd[token]                                   (:265)
   per layer: xb = rmsnorm(x, attn_norm)                   (:272, src/tensor.h:1028-1033)
              q, k, v = W{q,k,v} . xb                       (:284-289)
+             + biases, per-head q/k RMSNorm when present   (:291-318)
              rope(q, k) at pos, interleaved pairs          (:322-323, src/tensor.h:1068-1107)
                (pairs (i, i + head_dim/2) for the neox architectures, :1121-1161)
              cache k, v at pos                             (:326-327)
@@ -112,6 +113,14 @@ class RefLlama:
             q = matmul(t["wq"], L["wq"], xb, q_dim, c.dim)
             k = matmul(t["wk"], L["wk"], xb, kv_dim, c.dim)
             v = matmul(t["wv"], L["wv"], xb, kv_dim, c.dim)
+            # optional biases, then per-head RMSNorm of q and k (src/model.h:291-318)
+            q = (q + L["bq"]).astype(F32) if "bq" in L else q
+            k = (k + L["bk"]).astype(F32) if "bk" in L else k
+            v = (v + L["bv"]).astype(F32) if "bv" in L else v
+            if "q_norm" in L:
+                q = np.concatenate([rmsnorm(q[h * hd:(h + 1) * hd], L["q_norm"], c.eps) for h in range(nh)])
+            if "k_norm" in L:
+                k = np.concatenate([rmsnorm(k[h * hd:(h + 1) * hd], L["k_norm"], c.eps) for h in range(nkv)])
             rope = rope_neox if getattr(c, "rope_neox", False) else rope_interleaved
             q = rope(q, hd, pos, self.freqs)
             k = rope(k, hd, pos, self.freqs)

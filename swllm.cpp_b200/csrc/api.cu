@@ -19,6 +19,7 @@
 #include "allreduce.h"
 #include "decode.h"
 #include "prefill.h"
+#include "qkv_extras.h"
 #include "gemm_tc.h"
 #include "gemv.h"
 
@@ -434,6 +435,26 @@ swq_status swq_rope_kv(float* q, const float* k, const float* v, float* k_cache,
                                              neox, rows, max_seq, ldq, ldk, ldv, dev.num_sms,
                                              reinterpret_cast<cudaStream_t>(stream)),
                          "rope launch");
+}
+
+swq_status swq_qkv_bias_norm(float* q, float* k, float* v, const float* bq, const float* bk, const float* bv,
+                              const float* q_norm, const float* k_norm, int q_dim, int kv_dim, int head_dim,
+                              float eps, int rows, int ldq, int ldk, int ldv, swq_stream_t stream) {
+    ldq = ldq ? ldq : q_dim;
+    ldk = ldk ? ldk : kv_dim;
+    ldv = ldv ? ldv : kv_dim;
+    if (head_dim <= 0 || q_dim <= 0 || kv_dim <= 0 || q_dim % head_dim || kv_dim % head_dim || rows < 0)
+        return fail(SWQ_ERR_BAD_SHAPE, "q/k/v extras: inconsistent head dimensions");
+    if (ldq < q_dim || ldk < kv_dim || ldv < kv_dim) return fail(SWQ_ERR_BAD_SHAPE, "row stride below row size");
+    if (rows == 0 || !(bq || bk || bv || q_norm || k_norm)) return SWQ_OK;  // nothing to do
+    if (((bq || q_norm) && !q) || ((bk || k_norm) && !k) || (bv && !v))
+        return fail(SWQ_ERR_NULL_PTR, "null q / k / v with a bias or norm for it");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::qkv_extras_launch(q, k, v, bq, bk, bv, q_norm, k_norm, q_dim, kv_dim, head_dim, eps,
+                                                rows, ldq, ldk, ldv, reinterpret_cast<cudaStream_t>(stream)),
+                         "q/k/v extras launch");
 }
 
 // ---- prefill (rows m = s * seq_len + p: token p of sequence s at pos0 + p) ----

@@ -367,10 +367,13 @@ NEOX_ARCHS = ("qwen2", "qwen3", "qwen2moe", "qwen35", "qwen35moe", "starcoder2",
               "stablelm", "codeshell")
 _MATRICES = {"wq": "attn_q", "wk": "attn_k", "wv": "attn_v", "wo": "attn_output", "w_gate": "ffn_gate",
              "w_up": "ffn_up", "w_down": "ffn_down"}
-# tensors of layer kinds LlamaDecoder does not run (biases, QK-norm: Qwen;
-# GatedDeltaNet: hybrid layers), src/model.h:783-845
-_UNSUPPORTED = ("attn_q.bias", "attn_k.bias", "attn_v.bias", "attn_q_norm.weight", "attn_k_norm.weight",
-                "attn_qkv.weight", "ssm_out.weight")
+# tensors of layer kinds LlamaDecoder does not run (GatedDeltaNet layers of
+# hybrid models), src/model.h:783-800
+_UNSUPPORTED = ("attn_qkv.weight", "ssm_out.weight")
+# optional per-layer tensors the decoder applies after the q/k/v projections
+# (src/model.h:291-318, loaded at :822-837): name in the weights dict -> GGUF stem
+_EXTRAS = {"bq": "attn_q.bias", "bk": "attn_k.bias", "bv": "attn_v.bias", "q_norm": "attn_q_norm.weight",
+           "k_norm": "attn_k_norm.weight"}
 
 
 def llama_config(g: GGUFFile, context_override: int = 0):
@@ -444,6 +447,9 @@ def llama_weights(g: GGUFFile, cfg) -> dict:
     (src/model.h:771-772).  A file without output.weight ties the LM head to
     the embedding table (src/model.h:776-779); it must then be one of the
     quantized formats."""
+    extra_len = {"bq": cfg.q_dim, "bk": cfg.kv_dim, "bv": cfg.kv_dim, "q_norm": cfg.head_dim,
+                 "k_norm": cfg.head_dim}
+
     def check_shape(name, N, K):
         info = g.tensors.get(name)
         if info is None:
@@ -484,6 +490,9 @@ def llama_weights(g: GGUFFile, cfg) -> dict:
             name = f"blk.{li}.{_MATRICES[key]}.weight"
             check_shape(name, N, K)
             L[key] = g.blocks(name)
+        for key, stem in _EXTRAS.items():
+            if f"blk.{li}.{stem}" in g.tensors:
+                L[key] = vec(f"blk.{li}.{stem}", extra_len[key])
         layers.append(L)
     return {"token_embd": token_embd, "output_norm": vec("output_norm.weight", cfg.dim), "output": output,
             "layers": layers}

@@ -90,6 +90,8 @@ def lib() -> ctypes.CDLL:
         "swq_rope_kv_prefill": (i32, [vp, vp, vp, vp, vp, i32, i32, vp, i32, i32, i32, i32, i32, i32, i32, i32,
                                       i32, i32, vp]),
         "swq_attention_prefill": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, vp]),
+        "swq_qkv_bias_norm": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, ctypes.c_float, i32, i32, i32,
+                                    i32, vp]),
         "swq_silu_mul": (i32, [vp, vp, vp, i32, i32, i32, vp]),
         "swq_add": (i32, [vp, vp, i64, vp]),
         "swq_embed": (i32, [vp, vp, vp, i32, i32, i32, vp]),
@@ -277,6 +279,13 @@ def attention_prefill(out, q, k_cache, v_cache, pos0: int, seq_len: int, num_hea
     """Causal attention of prompt rows m = s*seq_len + p over positions 0 .. pos0 + p."""
     _raise(lib().swq_attention_prefill(_ptr(out), _ptr(q), _ptr(k_cache), _ptr(v_cache), pos0, seq_len, num_heads,
                                        num_kv_heads, head_dim, num_seqs, max_seq, ldq, ldo, _stream(stream)))
+
+
+def qkv_bias_norm(q, k, v, bq, bk, bv, q_norm, k_norm, q_dim: int, kv_dim: int, head_dim: int, eps: float,
+                  rows: int, ldq: int = 0, ldk: int = 0, ldv: int = 0, stream=None) -> None:
+    """q/k/v bias adds, then per-head RMSNorm of q and k (any vector may be None)."""
+    _raise(lib().swq_qkv_bias_norm(_ptr(q), _ptr(k), _ptr(v), _ptr(bq), _ptr(bk), _ptr(bv), _ptr(q_norm),
+                                   _ptr(k_norm), q_dim, kv_dim, head_dim, eps, rows, ldq, ldk, ldv, _stream(stream)))
 
 
 def silu_mul(out, gate, up, n: int, rows: int = 1, ld: int | None = None, stream=None) -> None:

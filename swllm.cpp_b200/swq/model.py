@@ -36,7 +36,8 @@ import numpy as np
 from . import lib as _lib_mod  # noqa: F401  (module import for the ctypes table)
 from .lib import (ACT_NONE, ACT_RMSNORM, ACT_SWIGLU, GEMM_NOALLOC_MAX_X_ELEMS, OPT_TENSOR_CORE_MIN_M, add, argmax,
                   add_rmsnorm, attention_decode, attention_prefill, attention_workspace_bytes, decode_advance,
-                  dequant, embed, gemm_act, get_option, rmsnorm, rope_kv, rope_kv_prefill, silu_mul)
+                  dequant, embed, gemm_act, get_option, qkv_bias_norm, rmsnorm, rope_kv, rope_kv_prefill,
+                  silu_mul)
 from .synth import LAYOUT, Q4_K, Q6_K, Q8_0, row_bytes
 
 
@@ -119,6 +120,10 @@ def synthetic_blocks(type_id: int, N: int, K: int, generator, device):
     return b.reshape(-1)
 
 
+# the optional per-layer tensors applied between the q/k/v projections and RoPE
+_EXTRAS = frozenset(("bq", "bk", "bv", "q_norm", "k_norm"))
+
+
 def _upload(host: np.ndarray, device):
     """Host array -> device tensor.  A read-only array (a view of a memory-mapped
     GGUF file) is uploaded from the mapping itself, without a host copy; torch
@@ -147,10 +152,11 @@ class LlamaDecoder:
                  max_steps: int = 4096, group=None, weights_from: "LlamaDecoder | None" = None,
                  collective: str = "peer", fuse: tuple | str = "auto"):
         """weights: None for synthetic weights, else host arrays: 'token_embd'
-        [vocab, dim] fp32, 'output_norm' [dim], 'output' blocks, and per layer
-        'layers'[l] with 'attn_norm', 'ffn_norm' [dim] fp32 and the blocks of
-        wq wk wv wo w_gate w_up w_down (whole matrices; each rank keeps its
-        shard).  group: torch.distributed group for tensor parallelism (None:
+        [vocab, dim] fp32 (or (GGML type, blocks)), 'output_norm' [dim], 'output'
+        blocks, and per layer 'layers'[l] with 'attn_norm', 'ffn_norm' [dim]
+        fp32 and the blocks of wq wk wv wo w_gate w_up w_down (whole matrices;
+        each rank keeps its shard), optionally the biases 'bq' [q_dim], 'bk',
+        'bv' [kv_dim] and the head norms 'q_norm', 'k_norm' [head_dim].  group: torch.distributed group for tensor parallelism (None:
         this process alone, whatever process groups exist).
         weights_from: a decoder of the same config and group whose device
         weights this one shares (another batch size of the same model).
@@ -268,6 +274,16 @@ class LlamaDecoder:
                            else 1.0 + 0.01 * torch.randn(cfg.dim, generator=g, **f32))
             for name, (N, K) in cfg.shapes().items():
                 L[name] = blocks(name, N, K, lw.get(name), lt[name])
+            # optional q/k/v biases and q/k head norms (Qwen-style files,
+            # src/model.h:291-318): this rank's heads of each bias, the
+            # [head_dim] norms whole
+            r, G = self.rank, self.world
+            for name, n in (("bq", self.q_dim), ("bk", self.kv_dim), ("bv", self.kv_dim)):
+                if lw.get(name) is not None:
+                    L[name] = _upload(np.ascontiguousarray(np.asarray(lw[name], np.float32)[r * n:(r + 1) * n]), dev)
+            for name in ("q_norm", "k_norm"):
+                if lw.get(name) is not None:
+                    L[name] = _upload(np.ascontiguousarray(lw[name], np.float32), dev)
             if lt["w_gate"] == lt["w_up"]:  # rows of gate then rows of up: one GEMV
                 L["w_gate_up"] = torch.cat([L.pop("w_gate"), L.pop("w_up")])
             if lt["wq"] == lt["wk"]:  # rows of q then rows of k
@@ -361,6 +377,9 @@ class LlamaDecoder:
                 gemm(t["wk"], L["wk"], src, self.v, B, kvd, c.dim, stream=s, **a_in)
                 k.copy_(self.v)
             gemm(t["wv"], L["wv"], src, self.v, B, kvd, c.dim, stream=s, **a_in)
+            if _EXTRAS.intersection(L):
+                qkv_bias_norm(q, k, self.v, L.get("bq"), L.get("bk"), L.get("bv"), L.get("q_norm"), L.get("k_norm"),
+                              qd, kvd, c.head_dim, c.eps, B, ldq=ld, ldk=ld, ldv=kvd, stream=s)
             kc, vc = self.kcache[li], self.vcache[li]
             rope_kv(q, k, self.v, kc, vc, self.pos, self.freqs, qd, kvd, c.head_dim, c.head_dim,
                     c.rope_neox, B, c.max_seq, ldq=ld, ldk=ld, stream=s)
@@ -464,6 +483,9 @@ class LlamaDecoder:
                     gemm(t["wk"], L["wk"], xn, v, M, kvd, c.dim, s)
                     qk[:, qd:].copy_(v)
                 gemm(t["wv"], L["wv"], xn, v, M, kvd, c.dim, s)
+                if _EXTRAS.intersection(L):
+                    qkv_bias_norm(qk, qk[:, qd:], v, L.get("bq"), L.get("bk"), L.get("bv"), L.get("q_norm"),
+                                  L.get("k_norm"), qd, kvd, hd, c.eps, M, ldq=ld, ldk=ld, ldv=kvd, stream=s)
                 kc, vc = self.kcache[li], self.vcache[li]
                 rope_kv_prefill(qk, qk[:, qd:], v, kc, vc, pos0, P, self.freqs, qd, kvd, hd, hd, c.rope_neox, B,
                                 c.max_seq, ldq=ld, ldk=ld, ldv=kvd, stream=s)

@@ -15,6 +15,8 @@ its SHA-256 and the reference's logits are stored (tests/golden/).
 * "neox": the same shape under the "qwen2" architecture name (no biases),
           which the reference runs with neox RoPE, pairs (i, i + head_dim/2)
           (src/model.h:629-634).
+* "bias": "qwen2" with q/k/v biases (src/model.h:291-294).
+* "qknorm": "qwen3" with per-head q/k RMSNorm weights (src/model.h:296-318).
 """
 from __future__ import annotations
 
@@ -43,6 +45,12 @@ VARIANTS = {
     "neox": dict(
         arch="qwen2", alignment=32, embd=G.F32, output=G.Q6_K, vocab_key=True,
         layers=[dict(wq=G.Q4_K, wk=G.Q4_K, wv=G.Q6_K, wo=G.Q4_K, w_gate=G.Q4_K, w_up=G.Q4_K, w_down=G.Q6_K)] * 2),
+    "bias": dict(
+        arch="qwen2", alignment=32, embd=G.F32, output=G.Q6_K, vocab_key=True, biases=True,
+        layers=[dict(wq=G.Q4_K, wk=G.Q4_K, wv=G.Q6_K, wo=G.Q4_K, w_gate=G.Q4_K, w_up=G.Q4_K, w_down=G.Q6_K)] * 2),
+    "qknorm": dict(
+        arch="qwen3", alignment=32, embd=G.F32, output=G.Q6_K, vocab_key=True, qk_norm=True,
+        layers=[dict(wq=G.Q4_K, wk=G.Q4_K, wv=G.Q6_K, wo=G.Q4_K, w_gate=G.Q4_K, w_up=G.Q4_K, w_down=G.Q6_K)] * 2),
 }
 
 
@@ -57,7 +65,7 @@ def write(path: Path, variant: str) -> Path:
     """Write the variant's GGUF file at path."""
     v, s = VARIANTS[variant], SHAPE
     a = v.get("arch", "llama")
-    rng = np.random.default_rng({"mix": 11, "tied": 12, "neox": 13}[variant])
+    rng = np.random.default_rng({"mix": 11, "tied": 12, "neox": 13, "bias": 14, "qknorm": 15}[variant])
     meta = {
         "general.architecture": a,
         "general.name": f"tiny-{variant}",
@@ -97,6 +105,14 @@ def write(path: Path, variant: str) -> Path:
         norm(f"blk.{li}.ffn_norm.weight")
         for j, (key, (N, K)) in enumerate(_shapes(s).items()):
             mat(f"blk.{li}.{_STEMS[key]}.weight", lt[key], N, K, 1000 + 10 * li + j)
+        hd = s["hidden"] // s["heads"]
+        if v.get("biases"):
+            for stem, n in (("attn_q", s["heads"] * hd), ("attn_k", s["kv_heads"] * hd), ("attn_v", s["kv_heads"] * hd)):
+                tensors.append((f"blk.{li}.{stem}.bias", G.F32, (n,), rng.standard_normal(n).astype(np.float32)))
+        if v.get("qk_norm"):
+            for stem in ("attn_q_norm", "attn_k_norm"):
+                tensors.append((f"blk.{li}.{stem}.weight", G.F32, (hd,),
+                                (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)))
     G.write_gguf(path, meta, tensors, alignment=v["alignment"])
     return path
 

@@ -84,6 +84,21 @@ def test_prefill_argument_errors():
     assert att(0, 0, out=None) is Status.OK
 
 
+def test_qkv_bias_norm_argument_errors():
+    L = lib()
+    # (q, k, v, bq, bk, bv, q_norm, k_norm, q_dim, kv_dim, head_dim, eps, rows, ldq, ldk, ldv)
+    def f(q=1, k=1, v=1, bq=1, bk=None, bv=None, qn=None, kn=None, hd=64, rows=2, ldq=0):
+        return _rc(L.swq_qkv_bias_norm, q, k, v, bq, bk, bv, qn, kn, 512, 128, hd, 1e-5, rows, ldq, 0, 0, None)
+
+    assert f(hd=96) is Status.BAD_SHAPE            # 512 is not a multiple of 96
+    assert f(ldq=100) is Status.BAD_SHAPE          # row stride below q_dim
+    assert f(rows=-1) is Status.BAD_SHAPE
+    assert f(q=None) is Status.NULL_PTR            # a q bias with no q
+    assert f(k=None, kn=1, bq=None) is Status.NULL_PTR
+    assert f(q=None, k=None, v=None, bq=None) is Status.OK   # no bias, no norm: nothing to do
+    assert f(rows=0, q=None) is Status.OK
+
+
 def test_dequant_argument_errors():
     L = lib()
     assert _rc(L.swq_dequant, 1, 1, 1, 32, None) is Status.BAD_TYPE

@@ -218,10 +218,10 @@ def files_with(tmp_path, changes: dict, drop=(), extra_tensors=(), retype=None):
 
 
 def test_unsupported_models_rejected(tmp_path):
-    bias = ("blk.0.attn_q.bias", G.F32, (256,), np.zeros(256, np.float32))
+    gdn = ("blk.0.attn_qkv.weight", G.F32, (256,), np.zeros(256, np.float32))  # a GatedDeltaNet layer
     for kw in (dict(changes={"general.architecture": "qwen35"}),
                dict(changes={"llama.rope.dimension_count": 32}),
-               dict(changes={}, extra_tensors=[bias]),
+               dict(changes={}, extra_tensors=[gdn]),
                dict(changes={}, drop=("blk.1.ffn_up.weight",)),
                dict(changes={}, retype=("blk.0.attn_q.weight", G.F16)),
                dict(changes={"llama.block_count": 0})):

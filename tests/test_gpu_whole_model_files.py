@@ -23,7 +23,7 @@ from test_gpu_model import LOGIT_TOL, _teacher_forced
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("variant", ["mix", "tied", "neox"])
+@pytest.mark.parametrize("variant", ["mix", "tied", "neox", "bias", "qknorm"])
 def test_gguf_model_matches_reference_logits(cuda, tmp_path, variant):
     """LlamaDecoder.from_gguf on a tiny GGUF file -- "mix": all seven formats,
     a different type mix per layer, F32 embedding table; "tied": a Q8_0
@@ -46,7 +46,12 @@ def test_gguf_model_matches_reference_logits(cuda, tmp_path, variant):
             assert int(np.argmax(got[pos, 0])) == int(np.argmax(want)), pos
 
 
-@pytest.mark.parametrize("variant", ["mix", "tied", "neox"])
+# The reference's CUDA backend interface rotates with cuda_rope(q, k, q_dim,
+# k_dim, head_dim, pos, theta) (src/tensor.h:27, Compute::rope), which has no
+# neox argument: a CUDA build of the reference rotates interleaved pairs for
+# every architecture.  The drop-in keeps that interface, so it is checked on
+# the interleaved-RoPE files; the neox ones run through LlamaDecoder above.
+@pytest.mark.parametrize("variant", ["mix", "tied"])
 def test_reference_model_runs_on_libswq(cuda, tmp_path, variant):
     """The drop-in: the reference's own Model::load / Model::forward, built with
     its CUDA backend and the one matmul branch of tensor.h calling
@@ -66,3 +71,42 @@ def test_reference_model_runs_on_libswq(cuda, tmp_path, variant):
         want = gold["logits"][pos]
         assert rel_l2(got, want) <= LOGIT_TOL, (pos, rel_l2(got, want))
     m.close()
+
+
+@pytest.mark.parametrize("which", ["bias", "norm", "both", "v_only"])
+def test_qkv_bias_norm_matches_numpy(cuda, which):
+    """swq_qkv_bias_norm on strided rows (q and k in one buffer) against the
+    reference's order in numpy: q/k/v bias adds, then the RMSNorm of every q
+    and k head with the shared [head_dim] weights (src/model.h:291-318)."""
+    torch = cuda
+    import swq
+    rows, nh, nkv, hd, eps = 3, 8, 2, 64, 1e-5
+    qd, kvd = nh * hd, nkv * hd
+    rng = np.random.default_rng({"bias": 1, "norm": 2, "both": 3, "v_only": 4}[which])
+    qk = rng.standard_normal((rows, qd + kvd), dtype=np.float32)
+    v = rng.standard_normal((rows, kvd), dtype=np.float32)
+    bq, bk, bv = (rng.standard_normal(n, dtype=np.float32) for n in (qd, kvd, kvd))
+    qn, kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32), (1 + 0.1 * rng.standard_normal(hd)).astype(
+        np.float32)
+    use_b, use_n = which in ("bias", "both"), which in ("norm", "both")
+    if which == "v_only":
+        bq = bk = None
+        use_b = False
+    q_ref, k_ref, v_ref = qk[:, :qd].astype(np.float64), qk[:, qd:].astype(np.float64), v.astype(np.float64)
+    if use_b:
+        q_ref, k_ref = q_ref + bq, k_ref + bk
+    if use_b or which == "v_only":
+        v_ref = v_ref + bv
+    if use_n:
+        def hn(x, n, w):
+            x = x.reshape(rows, n, hd)
+            return (x / np.sqrt((x * x).mean(-1, keepdims=True) + eps) * w).reshape(rows, n * hd)
+        q_ref, k_ref = hn(q_ref, nh, qn), hn(k_ref, nkv, kn)
+    d_qk, d_v = torch.from_numpy(qk).cuda(), torch.from_numpy(v).cuda()
+    dev = lambda a, on: torch.from_numpy(a).cuda() if (on and a is not None) else None  # noqa: E731
+    swq.qkv_bias_norm(d_qk, d_qk[:, qd:], d_v, dev(bq, use_b), dev(bk, use_b), dev(bv, use_b or which == "v_only"),
+                      dev(qn, use_n), dev(kn, use_n), qd, kvd, hd, eps, rows, ldq=qd + kvd, ldk=qd + kvd, ldv=kvd)
+    swq.check()
+    got = d_qk.cpu().numpy()
+    assert rel_l2(got[:, :qd], q_ref) <= 1e-6 and rel_l2(got[:, qd:], k_ref) <= 1e-6
+    assert rel_l2(d_v.cpu().numpy(), v_ref) <= 1e-6

@@ -120,7 +120,7 @@ def test_prefill_logits_match_reference(cuda, rows, P):
         assert hist[1, r] == int(np.argmax(after[r]))
 
 
-@pytest.mark.parametrize("variant", ["mix", "tied", "neox"])
+@pytest.mark.parametrize("variant", ["mix", "tied", "neox", "bias", "qknorm"])
 def test_gguf_prefill_matches_reference_logits(cuda, tmp_path, variant):
     """A GGUF file's prompt in one prefill (6 rows: the tensor-core GEMMs)
     against the logits of the reference's own Model::forward run token by

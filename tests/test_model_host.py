@@ -20,7 +20,7 @@ from swq import synth
 from test_gpu_model import _small, _weights
 
 OPS = ("embed", "rmsnorm", "add_rmsnorm", "gemm_act", "rope_kv", "attention_decode", "silu_mul", "argmax",
-       "decode_advance", "rope_kv_prefill", "attention_prefill", "add", "dequant")
+       "qkv_bias_norm", "decode_advance", "rope_kv_prefill", "attention_prefill", "add", "dequant")
 
 
 class _Stream:
@@ -227,3 +227,52 @@ def test_tensor_parallel_step_collectives(calls, monkeypatch):
     monkeypatch.setattr(dec, "_gather_logits", lambda: seen.append(("gather",)))
     dec.step()
     assert seen == [("sum", (3, cfg.dim), dec.stream)] * (2 * cfg.n_layers) + [("gather",)]
+
+
+@pytest.mark.parametrize("variant", ["bias", "qknorm"])
+def test_qkv_extras_wiring(calls, tmp_path, variant):
+    """Qwen-style files: after the q/k/v projections of every layer, one
+    swq_qkv_bias_norm on the same rows (decode: rows; prefill: rows x P),
+    with exactly the layer's biases / norms; Llama files never call it."""
+    dec = M.LlamaDecoder.from_gguf(LG.write(tmp_path / "m.gguf", variant), rows=2, device="cpu")
+    dec.step()
+    ex = [c for c in calls if c[0] == "qkv_bias_norm"]
+    assert len(ex) == dec.cfg.n_layers
+    qd, kvd = dec.q_dim, dec.kv_dim
+    for li, (_, a, kw) in enumerate(ex):
+        L = dec.layers[li]
+        assert a[0].data_ptr() == dec.qk.data_ptr() and a[1].data_ptr() == dec.qk.data_ptr() + 4 * qd
+        assert a[2] is dec.v
+        for i, key in enumerate(("bq", "bk", "bv", "q_norm", "k_norm")):
+            assert a[3 + i] is L.get(key), key
+        assert a[8:13] == (qd, kvd, dec.cfg.head_dim, dec.cfg.eps, 2)
+        assert kw["ldq"] == kw["ldk"] == qd + kvd and kw["ldv"] == kvd
+    names = [c[0] for c in calls]
+    assert names.index("qkv_bias_norm") < names.index("rope_kv")
+    calls.clear()
+    dec.prefill([[1, 2, 3], [4, 5, 6]])
+    ex = [c for c in calls if c[0] == "qkv_bias_norm"]
+    assert len(ex) == dec.cfg.n_layers and all(c[1][12] == 6 for c in ex)
+
+
+def test_llama_layers_never_call_qkv_extras(calls):
+    cfg = _small()
+    dec = M.LlamaDecoder(cfg, rows=1, device="cpu", weights=_weights(cfg, seed=9))
+    dec.step()
+    dec.prefill([[1, 2, 3]])
+    assert not [c for c in calls if c[0] == "qkv_bias_norm"]
+
+
+@pytest.mark.parametrize("rank", [0, 1])
+def test_tensor_parallel_bias_slices(calls, monkeypatch, tmp_path, rank):
+    """Each rank keeps the bias elements of its own heads; head norms whole."""
+    import swq.parallel as P
+    monkeypatch.setattr(P, "_world", lambda group: (rank, 2))
+    from swq import gguf as G
+    g = G.GGUFFile(LG.write(tmp_path / "b.gguf", "bias"))
+    cfg = G.llama_config(g)
+    W = G.llama_weights(g, cfg)
+    dec = M.LlamaDecoder(cfg, rows=1, device="cpu", weights=W, group=object(), collective="nccl")
+    for li, L in enumerate(dec.layers):
+        for key, n in (("bq", dec.q_dim), ("bk", dec.kv_dim), ("bv", dec.kv_dim)):
+            assert np.array_equal(L[key].numpy(), W["layers"][li][key][rank * n:(rank + 1) * n])
