@@ -110,7 +110,62 @@ def _moe_worker(rank, world, port):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("worker", [_tp_worker, _moe_worker], ids=["tensor_parallel", "expert_parallel"])
+def _decoder_worker(rank, world, port):
+    """The tensor-parallel LlamaDecoder's host path on real ranks: its device
+    operations are recorded, not run (no GPU here), but every collective of a
+    decode step and of a prefill goes through gloo, so both ranks must issue
+    the same ones in the same order.  (gloo's tensor all-gather wants equal
+    chunk shapes; the logits gather uses its list form, the same exchange.)"""
+    import contextlib
+
+    import swq.model as M
+    from test_gpu_model import _small, _weights
+
+    class _S:
+        def synchronize(self):
+            pass
+
+    _init(rank, world, port)
+    try:
+        for name in ("embed", "rmsnorm", "add_rmsnorm", "gemm_act", "rope_kv", "attention_decode", "silu_mul",
+                     "argmax", "decode_advance", "rope_kv_prefill", "attention_prefill", "add", "qkv_bias_norm"):
+            setattr(M, name, lambda *a, **k: None)
+        torch.cuda.Stream = lambda device=None: _S()
+        torch.cuda.stream = lambda st: contextlib.nullcontext()
+        cfg = _small()
+        dec = M.LlamaDecoder(cfg, rows=2, device="cpu", weights=_weights(cfg, seed=9), group=dist.group.WORLD,
+                             collective="nccl")
+        assert (dec.rank, dec.world) == (rank, world)
+        seen = []
+        orig = dec._nccl_all_reduce
+
+        def counted(t):
+            seen.append(("sum", tuple(t.shape)))
+            orig(t)
+
+        def gather():
+            parts = [torch.empty_like(dec.logits_l) for _ in range(world)]
+            dist.all_gather(parts, dec.logits_l, group=dec.group)
+            dec.logits.view(dec.rows, world, dec.vocab).copy_(torch.stack(parts).transpose(0, 1))
+            seen.append(("gather",))
+
+        dec.all_reduce = dec._nccl_all_reduce = counted
+        dec._gather_logits = gather
+        dec.logits_l.fill_(float(rank))
+        dec.step()
+        assert [tuple(dec.logits[0, i * dec.vocab:(i + 1) * dec.vocab].unique().tolist()) for i in range(world)] == \
+            [(float(i),) for i in range(world)]  # each rank's slice in rank order
+        dec.prefill([[1, 2, 3], [4, 5, 6]])
+        per = [("sum", (2, cfg.dim))] * (2 * cfg.n_layers) + [("gather",)]
+        per_prefill = [("sum", (6, cfg.dim))] * (2 * cfg.n_layers) + [("gather",)]
+        assert seen == per + per_prefill, seen
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("worker", [_tp_worker, _moe_worker, _decoder_worker],
+                         ids=["tensor_parallel", "expert_parallel", "decoder"])
 def test_two_ranks(worker):
     mp.spawn(worker, args=(2, _free_port()), nprocs=2, join=True)
 
