@@ -11,7 +11,9 @@ the logits the reference's CPU build produced (tests/golden/golden_llama_*.npz):
   backend and the one matmul branch of tensor.h calling libswq.
 
 Bound: LOGIT_TOL of the decode tests (2e-3 relative L2, the GEMV path's 16-bit
-activations compounding over the layers).
+activations compounding over the layers).  "bias" and "qknorm" carry the
+optional q/k/v biases and q/k head norms; swq_qkv_bias_norm, which applies
+them, is also checked alone against numpy (1e-6).
 """
 import numpy as np
 import pytest
