@@ -277,7 +277,7 @@ class LlamaDecoder:
             # optional q/k/v biases and q/k head norms (Qwen-style files,
             # src/model.h:291-318): this rank's heads of each bias, the
             # [head_dim] norms whole
-            r, G = self.rank, self.world
+            r = self.rank
             for name, n in (("bq", self.q_dim), ("bk", self.kv_dim), ("bv", self.kv_dim)):
                 if lw.get(name) is not None:
                     L[name] = _upload(np.ascontiguousarray(np.asarray(lw[name], np.float32)[r * n:(r + 1) * n]), dev)
