@@ -217,6 +217,23 @@ typedef struct swq_act {
 swq_status swq_gemm_act(int ggml_type, const void* W, const float* X, float* Y, int M, int N, int K,
                         const swq_act* act, int flags, swq_stream_t stream);
 
+/* swq_gemm_act with the tensor-core path's scratch (the fp16 copy of X, its
+ * row scales, split-K counters and partial products) in a caller-owned
+ * workspace instead of libswq's pool.  No counterpart in the reference.  Each
+ * owner of a workspace (e.g. each decoder of a process) gets scratch of its
+ * own, so calls on different workspaces never share memory; calls on one
+ * workspace must not overlap on the GPU.  A call captured in a CUDA graph
+ * allocates nothing.
+ *   swq_gemm_workspace_bytes: bytes a call of this shape needs on the current
+ *     device (0 when it runs the GEMV kernel, which needs none; 0 for
+ *     invalid arguments).
+ *   workspace: 256-byte aligned; NULL or too small for a call that needs it
+ *     is SWQ_ERR_NULL_PTR / SWQ_ERR_BAD_ARG before any device work.  The
+ *     counters in it are reset by the call itself: no clearing needed. */
+size_t swq_gemm_workspace_bytes(int ggml_type, int M, int N, int K);
+swq_status swq_gemm_act_ws(int ggml_type, const void* W, const float* X, float* Y, int M, int N, int K,
+                           const swq_act* act, void* workspace, size_t workspace_bytes, swq_stream_t stream);
+
 /* ---- Grouped GEMV for MoE decode ------------------------------------------
  *
  * No counterpart in the reference (it has no MoE path, src/model.h:520-528).
@@ -266,12 +283,15 @@ swq_status swq_gemm_noalloc(int ggml_type, const void* W, const float* X, float*
 
 /* Options (process-wide). */
 enum {
-    /* 1: Q2_K uses the activation order of the reference's fused CPU routine
-     * cpu_matmul_transposed_q2_k (src/tensor.h:935-945), which reads
-     * x[n + l] / x[n + l + 16] for all four 2-bit planes.  0 (default): Q2_K
-     * uses the element order of dequantize_q2_k (src/tensor.h:232-265), which
-     * is the GGUF format order and what the reference's CUDA backend computes
-     * (host dequantize, then SGEMM, src/tensor.h:1219-1223). */
+    /* 1 (default): Q2_K matmuls (GEMV, GEMM, grouped) use the activation
+     * order of the reference's fused CPU routine cpu_matmul_transposed_q2_k
+     * (src/tensor.h:935-945), which reads x[n + l] / x[n + l + 16] for all
+     * four 2-bit planes of each 128-element half -- what
+     * Compute::matmul_transposed_q returns on the reference's CPU backend, the
+     * one that builds.  0: Q2_K uses the element order of dequantize_q2_k
+     * (src/tensor.h:232-265), the GGUF format order, which is what the
+     * reference's CUDA backend would compute (host dequantize, then SGEMM,
+     * src/tensor.h:1219-1223).  swq_dequant always uses the format order. */
     SWQ_OPT_Q2K_REFERENCE_CPU_ORDER = 1,
     /* 1 (default): the GEMV and tensor-core GEMM kernels start streaming
      * weight blocks before the previous kernel on the stream has finished

@@ -141,9 +141,11 @@ def dequantize(type_id: int, blocks: np.ndarray, n: int) -> np.ndarray:
 
 
 def gemv(type_id: int, blocks: np.ndarray, x: np.ndarray, N: int, K: int,
-         format_order: bool = True) -> np.ndarray:
-    """out[N] = W . x.  ``format_order`` selects Q2_K's dequantize_q2_k element
-    order (identical for every other format)."""
+         format_order: bool = False) -> np.ndarray:
+    """out[N] = W . x, as Compute::matmul_transposed_q (src/tensor.h:1212) on
+    the reference's CPU backend.  ``format_order`` selects, for Q2_K only, the
+    element order of dequantize_q2_k (src/tensor.h:232-265) instead of the
+    fused routine's (src/tensor.h:935-945); every other format has one order."""
     b = _check_w(blocks)
     xx = np.ascontiguousarray(x, dtype=np.float32)
     assert xx.size == K
@@ -157,7 +159,9 @@ def gemv(type_id: int, blocks: np.ndarray, x: np.ndarray, N: int, K: int,
 
 
 def gemm(type_id: int, blocks: np.ndarray, X: np.ndarray, M: int, N: int, K: int,
-         format_order: bool = True) -> np.ndarray:
+         format_order: bool = False) -> np.ndarray:
+    """Y[M x N] = X . W^T: M calls of gemv (the reference has no batched
+    quantized path), same ``format_order`` meaning."""
     b = _check_w(blocks)
     XX = np.ascontiguousarray(X, dtype=np.float32).reshape(M, K)
     Y = np.zeros((M, N), dtype=np.float32)
@@ -204,6 +208,18 @@ def ref_gemv_f32(w: np.ndarray, x: np.ndarray, N: int, K: int) -> np.ndarray:
 
 def ref_set_threads(n: int) -> None:
     ref_lib().ref_set_threads(n)
+
+
+def ref_src() -> Path:
+    """Directory of the reference's sources: $REF_SRC, else the default the
+    oracle's Makefile builds _ref/ from."""
+    env = os.environ.get("REF_SRC")
+    if env:
+        return Path(env)
+    for ln in (Path(__file__).resolve().parent / "Makefile").read_text().splitlines():
+        if ln.startswith("REF_SRC ?="):
+            return Path(ln.split("?=", 1)[1].strip())
+    return Path("reference-sources-not-configured")
 
 
 def host_cores() -> int:

@@ -27,7 +27,7 @@ namespace {
 
 thread_local std::string g_last_error;
 
-std::atomic<int> g_opt_q2k_refcpu{0};
+std::atomic<int> g_opt_q2k_refcpu{1};
 std::atomic<int> g_opt_early_prefetch{1};
 std::atomic<int> g_opt_gemv_max_m{8};
 std::atomic<int> g_opt_gemm_tc{1};
@@ -272,6 +272,26 @@ swq_status swq_gemm(int type, const void* W, const float* X, float* Y, int M, in
     return gemm_gemv_groups(type, W, X, Y, M, N, K, max_m, dev, s);
 }
 
+// swq_act -> kernel arguments, with the checks every act-taking entry makes.
+static swq_status parse_act(const swq_act* act, int K, swq::ActArgs* a) {
+    if (!act) return SWQ_OK;
+    if (act->kind != SWQ_ACT_NONE && act->kind != SWQ_ACT_RMSNORM && act->kind != SWQ_ACT_SWIGLU)
+        return fail(SWQ_ERR_BAD_ARG, "unknown activation prologue " + std::to_string(act->kind));
+    a->kind = act->kind;
+    if (a->kind == SWQ_ACT_RMSNORM) {
+        if (!act->norm_w) return fail(SWQ_ERR_NULL_PTR, "RMSNORM needs norm_w");
+        if (!(act->eps >= 0.f)) return fail(SWQ_ERR_BAD_ARG, "eps must be >= 0");
+        a->R = act->residual;
+        a->normw = act->norm_w;
+        a->eps = act->eps;
+        a->sum_out = act->sum_out;
+    } else if (a->kind == SWQ_ACT_SWIGLU) {
+        a->ld = act->ld > 0 ? act->ld : 2 * K;
+        if (a->ld < 2 * K) return fail(SWQ_ERR_BAD_SHAPE, "SWIGLU row stride below 2K");
+    }
+    return SWQ_OK;
+}
+
 swq_status swq_gemm_act(int type, const void* W, const float* X, float* Y, int M, int N, int K,
                         const swq_act* act, int flags, swq_stream_t stream) {
     TypeInfo ti;
@@ -279,22 +299,7 @@ swq_status swq_gemm_act(int type, const void* W, const float* X, float* Y, int M
     if (st != SWQ_OK || M == 0 || N == 0) return st;
     if (flags & ~SWQ_GEMM_NOALLOC) return fail(SWQ_ERR_BAD_ARG, "unknown flags");
     swq::ActArgs a;
-    if (act) {
-        if (act->kind != SWQ_ACT_NONE && act->kind != SWQ_ACT_RMSNORM && act->kind != SWQ_ACT_SWIGLU)
-            return fail(SWQ_ERR_BAD_ARG, "unknown activation prologue " + std::to_string(act->kind));
-        a.kind = act->kind;
-        if (a.kind == SWQ_ACT_RMSNORM) {
-            if (!act->norm_w) return fail(SWQ_ERR_NULL_PTR, "RMSNORM needs norm_w");
-            if (!(act->eps >= 0.f)) return fail(SWQ_ERR_BAD_ARG, "eps must be >= 0");
-            a.R = act->residual;
-            a.normw = act->norm_w;
-            a.eps = act->eps;
-            a.sum_out = act->sum_out;
-        } else if (a.kind == SWQ_ACT_SWIGLU) {
-            a.ld = act->ld > 0 ? act->ld : 2 * K;
-            if (a.ld < 2 * K) return fail(SWQ_ERR_BAD_SHAPE, "SWIGLU row stride below 2K");
-        }
-    }
+    if ((st = parse_act(act, K, &a)) != SWQ_OK) return st;
     const bool noalloc = (flags & SWQ_GEMM_NOALLOC) != 0;
     if (noalloc && static_cast<int64_t>(M) * K > SWQ_GEMM_NOALLOC_MAX_X_ELEMS)
         return fail(SWQ_ERR_BAD_SHAPE, "swq_gemm_act: M*K exceeds the fixed scratch");
@@ -307,6 +312,42 @@ swq_status swq_gemm_act(int type, const void* W, const float* X, float* Y, int M
                                                               s, a)
                                 : swq::gemm_tc_launch(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms, s, a);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
+        return SWQ_OK;
+    }
+    return gemm_gemv_groups(type, W, X, Y, M, N, K, g_opt_gemv_max_m, dev, s, a);
+}
+
+size_t swq_gemm_workspace_bytes(int type, int M, int N, int K) {
+    TypeInfo ti;
+    if (!type_info(type, &ti) || M <= 0 || N <= 0 || K <= 0 || K % ti.qk != 0) return 0;
+    if (M < g_opt_tc_min_m || !g_opt_gemm_tc) return 0;  // the GEMV kernel needs no scratch
+    swq::DeviceInfo dev;
+    if (current_device(&dev) != SWQ_OK) return 0;
+    return swq::gemm_tc_workspace_bytes(M, N, K, dev.num_sms);
+}
+
+swq_status swq_gemm_act_ws(int type, const void* W, const float* X, float* Y, int M, int N, int K,
+                           const swq_act* act, void* workspace, size_t workspace_bytes, swq_stream_t stream) {
+    TypeInfo ti;
+    swq_status st = check_gemm_args(type, W, X, Y, M, N, K, &ti);
+    if (st != SWQ_OK || M == 0 || N == 0) return st;
+    swq::ActArgs a;
+    if ((st = parse_act(act, K, &a)) != SWQ_OK) return st;
+    if (K == 0) return fail(SWQ_ERR_BAD_SHAPE, "swq_gemm_act_ws needs K > 0");
+    swq::DeviceInfo dev;
+    if ((st = current_device(&dev)) != SWQ_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (M >= g_opt_tc_min_m && g_opt_gemm_tc && swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
+        const size_t need = swq::gemm_tc_workspace_bytes(M, N, K, dev.num_sms);
+        if (!workspace) return fail(SWQ_ERR_NULL_PTR, "swq_gemm_act_ws: this call needs a workspace");
+        if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+            return fail(SWQ_ERR_BAD_ARG, "swq_gemm_act_ws: workspace not 256-byte aligned");
+        if (workspace_bytes < need)
+            return fail(SWQ_ERR_BAD_ARG, "swq_gemm_act_ws: workspace of " + std::to_string(workspace_bytes) +
+                                             " bytes, this call needs " + std::to_string(need));
+        cudaError_t e = swq::gemm_tc_launch_ws(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms, s, a,
+                                               workspace, workspace_bytes);
+        if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch (caller workspace)");
         return SWQ_OK;
     }
     return gemm_gemv_groups(type, W, X, Y, M, N, K, g_opt_gemv_max_m, dev, s, a);
@@ -357,7 +398,7 @@ swq_status swq_grouped_gemm(int type, const void* const* W_experts, const int* e
         return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
     }
     cudaError_t e = swq::gemm_tc_grouped_launch(type, W_experts, expert_offsets, X_sorted, Y, n_experts, total_rows,
-                                                N, K, dev.num_sms, s);
+                                                N, K, g_opt_q2k_refcpu, dev.num_sms, s);
     if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
     return SWQ_OK;
 }

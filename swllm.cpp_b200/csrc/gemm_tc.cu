@@ -1045,7 +1045,8 @@ __device__ __forceinline__ float4 act4(const ActArgs& a, const float* xr, const 
 template <bool F2, bool VEC>
 __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__ X, __half* __restrict__ Xh,
                                                        float* __restrict__ rowscale, int M, int K,
-                                                       unsigned* __restrict__ tcount, int ncount, const ActArgs act) {
+                                                       unsigned* __restrict__ tcount, int ncount, const ActArgs act,
+                                                       int q2ref) {
     __shared__ float red[8], red2[8];
     // The GEMM launched after this kernel may start (its weight loads do not
     // depend on this kernel); this kernel itself waits for its predecessor.
@@ -1098,7 +1099,11 @@ __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__
         for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
             const int p0 = c * 8;
             const int g = p0 & ~255, pp = p0 & 255;
-            const int e0 = g + tc::tc_elem(F2, pp), e1 = g + tc::tc_elem(F2, pp + 4);
+            int e0 = g + tc::tc_elem(F2, pp), e1 = g + tc::tc_elem(F2, pp + 4);
+            if (q2ref) {  // Q2_K, reference CPU order: all four planes of a half read x[half + l], l < 32
+                e0 = (e0 & ~127) | (e0 & 31);
+                e1 = (e1 & ~127) | (e1 & 31);
+            }
             float4 x;
             const float4 a = act4<VEC>(act, xr, rr, K, e0, x);
             const float4 b = act4<VEC>(act, xr, rr, K, e1, x);
@@ -1136,7 +1141,6 @@ static EncodeTiledFn2 encode_fn2() {
 
 bool gemm_tc_supported(int type, const void* W, int M, int N, int K, int refcpu) {
     if (tc::tc_fmt(type).qk == 0 || M <= 0 || N <= 0 || K <= 0 || K % 32 != 0) return false;
-    if (refcpu && type == Q2_K) return false;  // the GEMV kernel serves that activation order
     // Shared-memory reads of the staged blocks are 2-byte aligned at least.
     if (reinterpret_cast<uintptr_t>(W) % 2 != 0) return false;
     return encode_fn2() != nullptr;
@@ -1341,7 +1345,7 @@ static cudaError_t launch_tc_fmt(const void* W, const __half* Xh, const float* r
 template <bool F2>
 static cudaError_t launch_x_to_f16(const float* X, __half* Xh, float* rowscale, int M, int K, int num_sms,
                                    cudaStream_t s, unsigned* tcount = nullptr, int ncount = 0,
-                                   const ActArgs& act = ActArgs{}) {
+                                   const ActArgs& act = ActArgs{}, int q2ref = 0) {
     const int grid = std::max(1, std::min(M, num_sms * 8));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
@@ -1354,8 +1358,9 @@ static cudaError_t launch_x_to_f16(const float* X, __half* Xh, float* rowscale, 
     cfg.numAttrs = 1;
     auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     const bool vec = al(X) && al(act.R) && al(act.normw) && al(act.sum_out) && (act.ld <= 0 || act.ld % 4 == 0);
-    if (vec) return cudaLaunchKernelEx(&cfg, x_to_f16_kernel<F2, true>, X, Xh, rowscale, M, K, tcount, ncount, act);
-    return cudaLaunchKernelEx(&cfg, x_to_f16_kernel<F2, false>, X, Xh, rowscale, M, K, tcount, ncount, act);
+    if (vec)
+        return cudaLaunchKernelEx(&cfg, x_to_f16_kernel<F2, true>, X, Xh, rowscale, M, K, tcount, ncount, act, q2ref);
+    return cudaLaunchKernelEx(&cfg, x_to_f16_kernel<F2, false>, X, Xh, rowscale, M, K, tcount, ncount, act, q2ref);
 }
 
 static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
@@ -1382,10 +1387,13 @@ static void place_split(SplitK& sk, void* base, int64_t M, int64_t N, int64_t K)
 // X -> fp16 into Xh (M*K halves, K order of the format) with row scales rs
 // (M floats) and the split-K counters zeroed, then the GEMM.
 static cudaError_t gemm_tc_run(int type, const void* W, const float* X, __half* Xh, float* rs, float* Y, int M,
-                               int N, int K, int num_sms, cudaStream_t s, const SplitK& sk, const ActArgs& act) {
+                               int N, int K, int num_sms, cudaStream_t s, const SplitK& sk, const ActArgs& act,
+                               int refcpu) {
     const int ncount = sk.ksplit > 1 ? static_cast<int>(split_tiles(M, N) * 4) : 0;
-    cudaError_t e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, M, K, num_sms, s, sk.tcount, ncount, act)
-                                        : launch_x_to_f16<false>(X, Xh, rs, M, K, num_sms, s, sk.tcount, ncount, act);
+    const int q2ref = (type == Q2_K && refcpu) ? 1 : 0;
+    cudaError_t e = tc::tc_fmt(type).f2
+                        ? launch_x_to_f16<true>(X, Xh, rs, M, K, num_sms, s, sk.tcount, ncount, act, q2ref)
+                        : launch_x_to_f16<false>(X, Xh, rs, M, K, num_sms, s, sk.tcount, ncount, act, q2ref);
     if (e != cudaSuccess) return e;
     switch (type) {
         case Q4_0: return launch_tc_fmt<Q4_0>(W, Xh, rs, Y, M, N, K, num_sms, s, sk);
@@ -1438,13 +1446,33 @@ cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, in
     e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), scratch_bytes(M, N, K, sk), pool, s);
     if (e != cudaSuccess) return e;
     place_split(sk, Xh, M, N, K);
-    e = gemm_tc_run(type, W, X, Xh, reinterpret_cast<float*>(Xh + n), Y, M, N, K, num_sms, s, sk, act);
+    e = gemm_tc_run(type, W, X, Xh, reinterpret_cast<float*>(Xh + n), Y, M, N, K, num_sms, s, sk, act, refcpu);
     cudaError_t e2 = cudaFreeAsync(Xh, s);
     return e != cudaSuccess ? e : e2;
 }
 
+// Workspace of one call from the caller (swq_gemm_act_ws): the same layout as
+// the pool allocation above -- fp16 X, row scales, split-K counters and
+// partials -- so each caller (e.g. each decoder) owns its scratch and calls on
+// different workspaces never share memory.
+size_t gemm_tc_workspace_bytes(int M, int N, int K, int num_sms) {
+    return scratch_bytes(M, N, K, plan_split(M, N, K, num_sms));
+}
+
+cudaError_t gemm_tc_launch_ws(int type, const void* W, const float* X, float* Y, int M, int N, int K, int refcpu,
+                              int num_sms, cudaStream_t s, const ActArgs& act, void* ws, size_t ws_bytes) {
+    if (!gemm_tc_supported(type, W, M, N, K, refcpu)) return cudaErrorNotSupported;
+    SplitK sk = plan_split(M, N, K, num_sms);
+    if (ws == nullptr || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0 || ws_bytes < scratch_bytes(M, N, K, sk))
+        return cudaErrorInvalidValue;
+    __half* Xh = static_cast<__half*>(ws);
+    place_split(sk, Xh, M, N, K);
+    return gemm_tc_run(type, W, X, Xh, reinterpret_cast<float*>(Xh + static_cast<int64_t>(M) * K), Y, M, N, K,
+                       num_sms, s, sk, act, refcpu);
+}
+
 cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
-                                   int n_experts, int rows, int N, int K, int num_sms, cudaStream_t s) {
+                                   int n_experts, int rows, int N, int K, int refcpu, int num_sms, cudaStream_t s) {
     if (tc::tc_fmt(type).qk == 0 || K % 32 != 0 || encode_fn2() == nullptr) return cudaErrorNotSupported;
     const int64_t n = static_cast<int64_t>(rows) * K;
     cudaMemPool_t pool = nullptr;
@@ -1454,8 +1482,9 @@ cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int
     e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&Xh), scratch_bytes(rows, K), pool, s);
     if (e != cudaSuccess) return e;
     float* rs = reinterpret_cast<float*>(Xh + n);
-    e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, rows, K, num_sms, s)
-                            : launch_x_to_f16<false>(X, Xh, rs, rows, K, num_sms, s);
+    const int q2ref = (type == Q2_K && refcpu) ? 1 : 0;
+    e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, rows, K, num_sms, s, nullptr, 0, ActArgs{}, q2ref)
+                            : launch_x_to_f16<false>(X, Xh, rs, rows, K, num_sms, s, nullptr, 0, ActArgs{}, q2ref);
     if (e == cudaSuccess) {
         const ExpertSet ex{reinterpret_cast<const uint8_t* const*>(wptrs), offsets, n_experts};
         switch (type) {
@@ -1543,7 +1572,7 @@ cudaError_t gemm_tc_launch_noalloc(int type, const void* W, const float* X, floa
         sk.tcount = static_cast<unsigned*>(a.tcount);
     }
     return gemm_tc_run(type, W, X, static_cast<__half*>(a.x16), static_cast<float*>(a.rowscale), Y, M, N, K,
-                       num_sms, s, sk, act);
+                       num_sms, s, sk, act, refcpu);
 }
 
 SWQ_DEFINE_STATUS_FETCH(gemm_tc)

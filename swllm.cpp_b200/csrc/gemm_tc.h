@@ -28,11 +28,17 @@ cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, in
 // stream-ordered allocation (swq_gemm_noalloc); M * K must fit that array.
 cudaError_t gemm_tc_launch_noalloc(int type, const void* W, const float* X, float* Y, int M, int N, int K,
                                    int refcpu, int num_sms, cudaStream_t s, const ActArgs& act = ActArgs{});
+// The same with the scratch in a caller-owned workspace (256-byte aligned,
+// at least gemm_tc_workspace_bytes); cudaErrorInvalidValue when it is not.
+size_t gemm_tc_workspace_bytes(int M, int N, int K, int num_sms);
+cudaError_t gemm_tc_launch_ws(int type, const void* W, const float* X, float* Y, int M, int N, int K, int refcpu,
+                              int num_sms, cudaStream_t s, const ActArgs& act, void* ws, size_t ws_bytes);
 // MoE grouped GEMM: expert e multiplies rows offsets[e] .. offsets[e+1]-1 of X
 // (rows x K) by the GGUF matrix wptrs[e] (N x K) into the same rows of Y.
 // wptrs and offsets are device arrays of n_experts and n_experts + 1 entries.
+// refcpu: Q2_K in the reference CPU routine's activation order.
 cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
-                                   int n_experts, int rows, int N, int K, int num_sms, cudaStream_t s);
+                                   int n_experts, int rows, int N, int K, int refcpu, int num_sms, cudaStream_t s);
 cudaError_t status_fetch_gemm_tc(unsigned* out, cudaStream_t s);
 
 // SWQ_OPT_EARLY_WEIGHT_PREFETCH for the tensor-core GEMM: 1 lets its weight

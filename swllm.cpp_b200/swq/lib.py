@@ -80,6 +80,8 @@ def lib() -> ctypes.CDLL:
         "swq_gemm": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
         "swq_gemm_noalloc": (i32, [i32, vp, vp, vp, i32, i32, i32, vp]),
         "swq_gemm_act": (i32, [i32, vp, vp, vp, i32, i32, i32, ctypes.POINTER(ActArgs), i32, vp]),
+        "swq_gemm_workspace_bytes": (sz, [i32, i32, i32, i32]),
+        "swq_gemm_act_ws": (i32, [i32, vp, vp, vp, i32, i32, i32, ctypes.POINTER(ActArgs), vp, sz, vp]),
         "swq_grouped_gemm": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "swq_grouped_gemv": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "swq_rmsnorm": (i32, [vp, vp, vp, i32, ctypes.c_float, i32, vp]),
@@ -221,6 +223,27 @@ def gemm_act(type_id: int, W, X, Y, M: int, N: int, K: int, kind: int = ACT_NONE
                 _ptr(sum_out) if sum_out is not None else None, ld)
     _raise(lib().swq_gemm_act(type_id, _ptr(W), _ptr(X), _ptr(Y), M, N, K, ctypes.byref(a),
                               GEMM_NOALLOC if noalloc else 0, _stream(stream)))
+
+
+def gemm_workspace_bytes(type_id: int, M: int, N: int, K: int) -> int:
+    """Workspace bytes gemm_act_ws needs for this shape on the current device
+    (0 when the GEMV kernel serves it)."""
+    return int(lib().swq_gemm_workspace_bytes(type_id, M, N, K))
+
+
+def gemm_act_ws(type_id: int, W, X, Y, M: int, N: int, K: int, workspace, workspace_bytes: int,
+                kind: int = ACT_NONE, residual=None, norm_w=None, eps: float = 0.0, sum_out=None, ld: int = 0,
+                stream=None) -> None:
+    """gemm_act() with the tensor-core path's scratch in `workspace` (a device
+    buffer of at least gemm_workspace_bytes(), 256-byte aligned, owned by the
+    caller): nothing is allocated, and callers with separate workspaces never
+    share scratch."""
+    a = ActArgs(kind, _ptr(residual) if residual is not None else None,
+                _ptr(norm_w) if norm_w is not None else None, eps,
+                _ptr(sum_out) if sum_out is not None else None, ld)
+    _raise(lib().swq_gemm_act_ws(type_id, _ptr(W), _ptr(X), _ptr(Y), M, N, K, ctypes.byref(a),
+                                 _ptr(workspace) if workspace is not None else None, workspace_bytes,
+                                 _stream(stream)))
 
 
 def grouped_gemv(type_id: int, w_ptrs, offsets, X, Y, n_experts: int, total_rows: int, N: int, K: int,

@@ -34,9 +34,9 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import lib as _lib_mod  # noqa: F401  (module import for the ctypes table)
-from .lib import (ACT_NONE, ACT_RMSNORM, ACT_SWIGLU, GEMM_NOALLOC_MAX_X_ELEMS, OPT_TENSOR_CORE_MIN_M, add, argmax,
-                  add_rmsnorm, attention_decode, attention_prefill, attention_workspace_bytes, decode_advance,
-                  dequant, embed, gemm_act, get_option, qkv_bias_norm, rmsnorm, rope_kv, rope_kv_prefill,
+from .lib import (ACT_NONE, ACT_RMSNORM, ACT_SWIGLU, OPT_TENSOR_CORE_MIN_M, add, argmax, add_rmsnorm,
+                  attention_decode, attention_prefill, attention_workspace_bytes, decode_advance, dequant, embed,
+                  gemm_act_ws, gemm_workspace_bytes, get_option, qkv_bias_norm, rmsnorm, rope_kv, rope_kv_prefill,
                   silu_mul)
 from .synth import LAYOUT, Q4_K, Q6_K, Q8_0, row_bytes
 
@@ -316,6 +316,7 @@ class LlamaDecoder:
         self.history = torch.zeros((max_steps, B), dtype=torch.int32, device=dev)
         self.ws_bytes = attention_workspace_bytes(self.nh, self.nkv, cfg.head_dim, B, cfg.max_seq)
         self.ws = torch.zeros(max(1, self.ws_bytes // 4), **f32)  # zero-filled, as the kernel expects
+        self.gemm_ws, self.gemm_ws_bytes = None, 0  # tensor-core GEMM scratch, grown on first need
         self.max_steps = max_steps
         self.steps_issued = 0
         self.stream = torch.cuda.Stream(device=dev)
@@ -335,11 +336,19 @@ class LlamaDecoder:
     # ------------------------------------------------------------ one token
     def _gemm(self, type_id, W, X, Y, M, N, K, stream, kind=ACT_NONE, residual=None, norm_w=None, sum_out=None,
               ld=0):
-        # Rows that take the tensor-core GEMM use its allocation-free form, so
-        # a captured step holds no allocation (one stream orders the calls).
-        noalloc = M >= get_option(OPT_TENSOR_CORE_MIN_M) and M * K <= GEMM_NOALLOC_MAX_X_ELEMS
-        gemm_act(type_id, W, X, Y, M, N, K, kind=kind, residual=residual, norm_w=norm_w, eps=self.cfg.eps,
-                 sum_out=sum_out, ld=ld, noalloc=noalloc, stream=stream)
+        # The tensor-core GEMM's scratch is this decoder's own workspace: a
+        # captured step allocates nothing, and two decoders on one device never
+        # share scratch.  Every call of this decoder runs on its one stream.
+        need = gemm_workspace_bytes(type_id, M, N, K)
+        if need > self.gemm_ws_bytes:
+            import torch
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError(f"GEMM workspace of {self.gemm_ws_bytes} bytes, a captured call needs {need}")
+            self.stream.synchronize()  # the old workspace may still be read by queued kernels
+            self.gemm_ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+            self.gemm_ws_bytes = need
+        gemm_act_ws(type_id, W, X, Y, M, N, K, self.gemm_ws, self.gemm_ws_bytes, kind=kind, residual=residual,
+                    norm_w=norm_w, eps=self.cfg.eps, sum_out=sum_out, ld=ld, stream=stream)
 
     def step(self, greedy: bool = True) -> None:
         """One decode step for all rows at position *pos: logits of the current

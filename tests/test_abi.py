@@ -110,7 +110,7 @@ def test_dequant_argument_errors():
 
 
 def test_options():
-    assert swq.get_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER) == 0
+    assert swq.get_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER) == 1
     assert swq.get_option(swq.OPT_EARLY_WEIGHT_PREFETCH) == 1
     assert swq.get_option(swq.OPT_TENSOR_CORE_GEMM) == 1
     swq.set_option(swq.OPT_TENSOR_CORE_GEMM, 0)
@@ -121,9 +121,9 @@ def test_options():
     assert swq.get_option(swq.OPT_TENSOR_CORE_MIN_M) == 5
     with pytest.raises(swq.SwqError):
         swq.set_option(swq.OPT_TENSOR_CORE_MIN_M, 1)
-    swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 1)
-    assert swq.get_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER) == 1
     swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 0)
+    assert swq.get_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER) == 0
+    swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 1)
     with pytest.raises(swq.SwqError) as ei:
         swq.set_option(swq.OPT_GEMV_MAX_M, 9)
     assert ei.value.status is Status.BAD_ARG

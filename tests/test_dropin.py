@@ -10,7 +10,9 @@ import pytest
 
 from conftest import REPO
 
-REF_TENSOR_H = Path("/root/reference/src/tensor.h")
+import oracle
+
+REF_TENSOR_H = oracle.ref_src() / "tensor.h"
 
 
 def test_derived_header_changes_only_the_matmul_branch():

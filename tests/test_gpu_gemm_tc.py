@@ -53,6 +53,29 @@ def test_formats(cuda, oracle_mod, fmt, M):
     assert np.all(np.isfinite(got))
 
 
+@pytest.mark.parametrize("order", ["reference_cpu", "format"])
+@pytest.mark.parametrize("M", [9, 130])
+def test_q2k_orders(cuda, oracle_mod, order, M):
+    """Q2_K on the tensor cores in both activation orders: the reference's
+    fused CPU routine (default; the fp16 copy of X repeats the first 32
+    elements of each 128-element half for all four planes) and
+    dequantize_q2_k's order (SWQ_OPT_Q2K_REFERENCE_CPU_ORDER = 0)."""
+    t = synth.IDS["Q2_K"]
+    N, K = 384, 2048
+    blocks = synth.random_blocks(t, N, K, seed=2050)
+    X = synth.random_activations(M, K, seed=2051)
+    fmt_order = order == "format"
+    swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 0 if fmt_order else 1)
+    try:
+        got = _gemm(cuda, t, blocks, X, N, K)
+    finally:
+        swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 1)
+    want = oracle_mod.gemm(t, blocks, X, M, N, K, format_order=fmt_order)
+    other = oracle_mod.gemm(t, blocks, X, M, N, K, format_order=not fmt_order)
+    assert rel_l2(got, want) <= REL_L2_TOL
+    assert rel_l2(got, other) > 0.1  # the two orders are far apart
+
+
 @pytest.mark.parametrize("fmt,N,K,M", [("Q4_K", 200, 512, 70), ("Q4_0", 129, 96, 33), ("Q8_0", 257, 160, 300),
                                         ("Q6_K", 130, 768, 17), ("Q5_K", 1000, 1280, 511)])
 def test_ragged_tiles(cuda, oracle_mod, fmt, N, K, M):

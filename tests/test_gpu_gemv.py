@@ -1,9 +1,10 @@
 """Fused dequant-GEMV / small-M GEMM on the GPU against the oracle.
 
 Tolerance: relative L2 <= 1e-3 against the reference's fp32 result on the same
-seeded inputs (REL_L2_TOL).  Q2_K is compared in the element order of
-dequantize_q2_k by default, and in the reference fused-CPU order with
-SWQ_OPT_Q2K_REFERENCE_CPU_ORDER.
+seeded inputs (REL_L2_TOL).  Q2_K is compared in the activation order of
+the reference's fused CPU routine (the default, what
+Compute::matmul_transposed_q returns) and, with
+SWQ_OPT_Q2K_REFERENCE_CPU_ORDER = 0, in the element order of dequantize_q2_k.
 """
 import numpy as np
 import pytest
@@ -92,19 +93,20 @@ def test_golden_vectors(cuda, golden, fmt):
     g = golden(fmt)
     t, N, K = int(g["type"]), int(g["N"]), int(g["K"])
     got = _gemm_gpu(cuda, t, g["blocks"], g["x"], N, K)
-    want = g["gemv_dq"] if fmt == "Q2_K" else g["gemv_ref"]
-    assert rel_l2(got, want) <= REL_L2_TOL
+    assert rel_l2(got, g["gemv_ref"]) <= REL_L2_TOL
 
 
-def test_q2k_reference_cpu_order_option(cuda, golden):
+def test_q2k_format_order_option(cuda, golden):
+    """SWQ_OPT_Q2K_REFERENCE_CPU_ORDER = 0: dequantize_q2_k's element order,
+    the reference's dequantize followed by an fp32 GEMV."""
     g = golden("Q2_K")
     t, N, K = int(g["type"]), int(g["N"]), int(g["K"])
-    swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 1)
+    swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 0)
     try:
         got = _gemm_gpu(cuda, t, g["blocks"], g["x"], N, K)
     finally:
-        swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 0)
-    assert rel_l2(got, g["gemv_ref"]) <= REL_L2_TOL
+        swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 1)
+    assert rel_l2(got, g["gemv_dq"]) <= REL_L2_TOL
 
 
 @pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K", "Q2_K", "Q8_0"])

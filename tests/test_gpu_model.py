@@ -3,9 +3,9 @@ the reference's Model::forward (oracle/model_ref.py).
 
 A 2-layer Llama-shaped model (dim 512, 8 query / 2 kv heads of 64, FFN 1024,
 vocab 1000, Q4_K_M mix) decodes greedily; every step's logits must be within
-relative L2 2e-3 of the reference's for the same tokens (the quantized GEMVs
-use 16-bit activations; errors compound over the layers), and the greedy
-tokens must agree wherever the reference's top-2 margin is clear.
+relative L2 5e-4 of the reference's for the same tokens (LOGIT_TOL: the
+per-projection errors of the GEMV path compound over the layers), and the
+greedy tokens must agree wherever the reference's top-2 margin is clear.
 """
 import numpy as np
 import pytest
@@ -16,7 +16,7 @@ from swq.model import LlamaConfig, LlamaDecoder, rope_freqs
 
 pytestmark = pytest.mark.gpu
 
-LOGIT_TOL = 2e-3
+LOGIT_TOL = 5e-4
 
 
 def _weights(cfg, seed):

@@ -19,7 +19,7 @@ import swq.model as M
 from swq import synth
 from test_gpu_model import _small, _weights
 
-OPS = ("embed", "rmsnorm", "add_rmsnorm", "gemm_act", "rope_kv", "attention_decode", "silu_mul", "argmax",
+OPS = ("embed", "rmsnorm", "add_rmsnorm", "gemm_act_ws", "rope_kv", "attention_decode", "silu_mul", "argmax",
        "qkv_bias_norm", "decode_advance", "rope_kv_prefill", "attention_prefill", "add", "dequant")
 
 
@@ -39,6 +39,7 @@ def calls(monkeypatch):
 
     for name in OPS:
         monkeypatch.setattr(M, name, recorder(name))
+    monkeypatch.setattr(M, "gemm_workspace_bytes", lambda *a: 0)
     monkeypatch.setattr(torch.cuda, "Stream", lambda device=None: _Stream())
     monkeypatch.setattr(torch.cuda, "stream", lambda s: contextlib.nullcontext())
     monkeypatch.setattr(torch.cuda, "current_stream", lambda device=None: _Stream())
@@ -47,7 +48,7 @@ def calls(monkeypatch):
 
 def _gemms(log):
     """(type, weight tensor, M, N, K) of every projection, in order."""
-    return [(a[0], a[1], a[4], a[5], a[6]) for name, a, _ in log if name == "gemm_act"]
+    return [(a[0], a[1], a[4], a[5], a[6]) for name, a, _ in log if name == "gemm_act_ws"]
 
 
 def _mixed_cfg():

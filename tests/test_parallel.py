@@ -127,9 +127,10 @@ def _decoder_worker(rank, world, port):
 
     _init(rank, world, port)
     try:
-        for name in ("embed", "rmsnorm", "add_rmsnorm", "gemm_act", "rope_kv", "attention_decode", "silu_mul",
+        for name in ("embed", "rmsnorm", "add_rmsnorm", "gemm_act_ws", "rope_kv", "attention_decode", "silu_mul",
                      "argmax", "decode_advance", "rope_kv_prefill", "attention_prefill", "add", "qkv_bias_norm"):
             setattr(M, name, lambda *a, **k: None)
+        M.gemm_workspace_bytes = lambda *a: 0
         torch.cuda.Stream = lambda device=None: _S()
         torch.cuda.stream = lambda st: contextlib.nullcontext()
         cfg = _small()
