@@ -325,7 +325,14 @@ enum {
     /* GEMV CTAs per SM (0, the default: automatic; 1..4 forces it).  More
      * than one puts more consumer warps on each SM, each CTA with its share
      * of the SM's shared memory. */
-    SWQ_OPT_GEMV_CTAS_PER_SM = 8
+    SWQ_OPT_GEMV_CTAS_PER_SM = 8,
+    /* 1 (default): the GEMV kernel keeps the activations in fp32, as the
+     * reference does: each quant value becomes an exact float and the dot
+     * products are fp32 fused multiply-adds (up to 4 activation rows whose
+     * fp32 copy fits the kernel's shared memory; others take the 16-bit
+     * form).  0: activations rounded to 16-bit fixed point per 32-element
+     * block and integer dot products (dp2a), the earlier form. */
+    SWQ_OPT_GEMV_FP32_ACT = 9
 };
 swq_status swq_set_option(int option, int value);
 int swq_get_option(int option);

@@ -35,6 +35,7 @@ std::atomic<int> g_opt_tc_min_m{5};
 std::atomic<int> g_opt_gemv_smem_kb{0};
 std::atomic<int> g_opt_gemv_stage_kb{0};
 std::atomic<int> g_opt_gemv_ctas{0};
+std::atomic<int> g_opt_gemv_fp32{1};
 
 swq_status fail(swq_status s, const std::string& msg) {
     g_last_error = msg;
@@ -99,7 +100,7 @@ int gemv_group_rows(int type, int K, int max_m) {
     const size_t budget = 120 * 1024;
     for (int g : {8, 4, 2, 1}) {
         if (g > max_m && g != 1) continue;
-        if (swq::gemv_smem_x_bytes(type, g, K) <= budget) return g;
+        if (swq::gemv_smem_x_bytes(type, g, K, g_opt_gemv_fp32 != 0) <= budget) return g;
     }
     return 0;
 }
@@ -144,6 +145,7 @@ swq_status gemm_gemv_groups(int type, const void* W, const float* X, float* Y, i
         L.smem_kb = g_opt_gemv_smem_kb;
         L.stage_kb = g_opt_gemv_stage_kb;
         L.ctas_per_sm = g_opt_gemv_ctas;
+        L.xf = g_opt_gemv_fp32;
         cudaError_t e = swq::gemv_launch(L, s);
         if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
     }
@@ -215,6 +217,10 @@ swq_status swq_set_option(int option, int value) {
             if (value < 0 || value > 4) return fail(SWQ_ERR_BAD_ARG, "GEMV CTAs per SM must be 0..4");
             g_opt_gemv_ctas = value;
             return SWQ_OK;
+        case SWQ_OPT_GEMV_FP32_ACT:
+            if (value != 0 && value != 1) return fail(SWQ_ERR_BAD_ARG, "option value must be 0 or 1");
+            g_opt_gemv_fp32 = value;
+            return SWQ_OK;
         default:
             return fail(SWQ_ERR_BAD_ARG, "unknown option " + std::to_string(option));
     }
@@ -230,6 +236,7 @@ int swq_get_option(int option) {
         case SWQ_OPT_GEMV_SMEM_KB: return g_opt_gemv_smem_kb;
         case SWQ_OPT_GEMV_STAGE_KB: return g_opt_gemv_stage_kb;
         case SWQ_OPT_GEMV_CTAS_PER_SM: return g_opt_gemv_ctas;
+        case SWQ_OPT_GEMV_FP32_ACT: return g_opt_gemv_fp32;
         default: return -1;
     }
 }

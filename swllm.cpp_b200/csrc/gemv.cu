@@ -150,6 +150,219 @@ struct Cfg {
     static constexpr int THREADS = (NCW + 1) * 32;
 };
 
+// ---------------------------------------------------------------------------
+// fp32 activations (the default): x stays fp32 as in the reference, every
+// quant byte becomes an exact float, the products are exact in the FMA and only
+// the fp32 accumulation rounds -- as in cpu_matmul_transposed_* (src/tensor.h:
+// 570-1025), which rounds each product as well.
+//
+// Layout per activation row: units in groups of 32; a group holds NW chunk
+// planes (32 lanes x 16 B: the 4 fp32 activations of one decoded word of each
+// unit), then, for formats with a min (Q2_K, Q4_K, Q5_K), PARTS planes of the
+// part sums sum(x) (32 x 4 B).  A lane's loads are base + compile-time offsets
+// and a warp's never share a bank.
+// ---------------------------------------------------------------------------
+template <int T>
+struct XLayF {
+    using F = Fmt<T>;
+    static constexpr int NW = F::UE / 4;                           // chunks (words) per unit
+    static constexpr int WPP = NW / F::PARTS;                      // words per part
+    static constexpr int MPL = F::MIN ? F::PARTS : 0;              // meta planes
+    static constexpr int GB = 32 * (16 * NW + 4 * MPL);            // bytes per group
+    static constexpr int META = 32 * 16 * NW;                      // offset of the meta planes
+    __host__ __device__ static int row_bytes(int K) { return ((K / F::UE + 31) / 32) * GB; }
+    __device__ static uint32_t chunk_off(int u) { return (u >> 5) * GB + (u & 31) * 16; }
+    __device__ static uint32_t meta_off(int u) { return (u >> 5) * GB + META + (u & 31) * 4; }
+};
+
+// Quant byte b -> float (b - z), exact: the byte is placed in the low mantissa
+// of 2^23 (one byte permute), then 2^23 + z is subtracted (one packed add for
+// two elements).  Bytes 0, 1 of word w -> lo, bytes 2, 3 -> hi.
+__device__ __forceinline__ void word_to_f2(uint32_t w, float2 bias, float2& lo, float2& hi) {
+    lo = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650)),
+                                __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7651))), bias);
+    hi = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7652)),
+                                __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7653))), bias);
+}
+
+// Zero point of part pt in the units of its bytes (signed bytes are read as
+// byte ^ 0x80, i.e. value + 128).
+template <int T>
+__device__ __forceinline__ float2 part_bias(int pt) {
+    using F = Fmt<T>;
+    const float z = 8388608.0f + static_cast<float>(F::QSIGNED ? 128 : F::ioff(pt));
+    return make_float2(-z, -z);
+}
+
+template <int T, int MT>
+__device__ __forceinline__ void unit_dotf(const uint8_t* blk, int c, int u, const uint8_t* xs, int xstride,
+                                          float (&acc)[MT]) {
+    using F = Fmt<T>;
+    using XL = XLayF<T>;
+    constexpr int NW = XL::NW, WPP = XL::WPP;
+    uint32_t q[NW];
+    float wd[F::PARTS], wm[F::PARTS];
+    F::decode(blk, c, q, wd, wm);
+    const uint32_t co = XL::chunk_off(u);
+#pragma unroll
+    for (int pt = 0; pt < F::PARTS; ++pt) {
+        const float2 bias = part_bias<T>(pt);
+        float2 S[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) S[m] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < WPP; ++i) {
+            float2 lo, hi;
+            word_to_f2(F::QSIGNED ? (q[pt * WPP + i] ^ 0x80808080u) : q[pt * WPP + i], bias, lo, hi);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const float4 xv = *reinterpret_cast<const float4*>(xs + m * xstride + co + (pt * WPP + i) * 512);
+                S[m] = __ffma2_rn(make_float2(xv.x, xv.y), lo, S[m]);
+                S[m] = __ffma2_rn(make_float2(xv.z, xv.w), hi, S[m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            float t = wd[pt] * (S[m].x + S[m].y);
+            if (F::MIN)
+                t = fmaf(-wm[pt], *reinterpret_cast<const float*>(xs + m * xstride + XL::meta_off(u) + pt * 128), t);
+            acc[m] += t;
+        }
+    }
+}
+
+// The same unit position in two rows, sharing every activation load.
+template <int T, int MT>
+__device__ __forceinline__ void unit_dotf2(const uint8_t* blkA, const uint8_t* blkB, int c, int u, const uint8_t* xs,
+                                           int xstride, float (&accA)[MT], float (&accB)[MT]) {
+    using F = Fmt<T>;
+    using XL = XLayF<T>;
+    constexpr int NW = XL::NW, WPP = XL::WPP;
+    uint32_t qa[NW], qb[NW];
+    float wda[F::PARTS], wma[F::PARTS], wdb[F::PARTS], wmb[F::PARTS];
+    F::decode(blkA, c, qa, wda, wma);
+    F::decode(blkB, c, qb, wdb, wmb);
+    const uint32_t co = XL::chunk_off(u);
+#pragma unroll
+    for (int pt = 0; pt < F::PARTS; ++pt) {
+        const float2 bias = part_bias<T>(pt);
+        float2 SA[MT], SB[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) SA[m] = SB[m] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < WPP; ++i) {
+            float2 alo, ahi, blo, bhi;
+            word_to_f2(F::QSIGNED ? (qa[pt * WPP + i] ^ 0x80808080u) : qa[pt * WPP + i], bias, alo, ahi);
+            word_to_f2(F::QSIGNED ? (qb[pt * WPP + i] ^ 0x80808080u) : qb[pt * WPP + i], bias, blo, bhi);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const float4 xv = *reinterpret_cast<const float4*>(xs + m * xstride + co + (pt * WPP + i) * 512);
+                const float2 x01 = make_float2(xv.x, xv.y), x23 = make_float2(xv.z, xv.w);
+                SA[m] = __ffma2_rn(x01, alo, SA[m]);
+                SB[m] = __ffma2_rn(x01, blo, SB[m]);
+                SA[m] = __ffma2_rn(x23, ahi, SA[m]);
+                SB[m] = __ffma2_rn(x23, bhi, SB[m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            float ta = wda[pt] * (SA[m].x + SA[m].y);
+            float tb = wdb[pt] * (SB[m].x + SB[m].y);
+            if (F::MIN) {
+                const float I = *reinterpret_cast<const float*>(xs + m * xstride + XL::meta_off(u) + pt * 128);
+                ta = fmaf(-wma[pt], I, ta);
+                tb = fmaf(-wmb[pt], I, tb);
+            }
+            accA[m] += ta;
+            accB[m] += tb;
+        }
+    }
+}
+
+// 4 consecutive floats (one float4 load when VEC)
+__device__ __forceinline__ void load4(const float* p, float (&v)[4], bool vec) {
+    if (vec) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __ldg(p + i);
+    }
+}
+
+// Activation rows -> the fp32 layout, with the prologue (RMSNORM: (x + r) * w,
+// the squares of x + r summed per row into sqm; SWIGLU: silu(g) * u).  Item =
+// 4 consecutive elements of one row = one chunk; PE/4 consecutive items (one
+// part) sum their elements by shuffles for the meta plane.
+template <int T, int MT>
+__device__ __forceinline__ void prep_xf(const GemvParams& p, uint8_t* xq, int ctid, int nct, float (&sqm)[MT]) {
+    using F = Fmt<T>;
+    using XL = XLayF<T>;
+    const bool refcpu = p.refcpu != 0;
+    const bool rms = p.act == ACT_RMSNORM;
+    const int ipr = p.K / 4;  // items per row
+    const int items = MT * ipr;
+    constexpr int GL = F::PE / 4;  // lanes of one part
+    for (int base = 0; base < items; base += nct) {
+        const int it = base + ctid;
+        const bool act = it < items;
+        const int mm = (MT == 1 || !act) ? 0 : it / ipr;
+        const int kk = act ? (it - mm * ipr) * 4 : 0;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (act && mm < p.M) {
+            const size_t xo = static_cast<size_t>(mm) * p.ld + kk;
+            load4(p.X + xo, v, p.x_vec);
+            if (p.act == ACT_SWIGLU) {
+                float g[4];
+                load4(p.X + xo + p.K, g, p.x_vec);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] = v[i] / (1.0f + expf(-v[i])) * g[i];
+            } else if (rms) {
+                const size_t ro = static_cast<size_t>(mm) * p.K + kk;
+                if (p.R) {
+                    float r[4];
+                    load4(p.R + ro, r, p.x_vec);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) v[i] += r[i];
+                }
+                if (p.sum_out && blockIdx.x == 0) {
+                    if (p.x_vec) *reinterpret_cast<float4*>(p.sum_out + ro) = make_float4(v[0], v[1], v[2], v[3]);
+                    else for (int i = 0; i < 4; ++i) p.sum_out[ro + i] = v[i];
+                }
+                float sq = 0.f, w[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sq = fmaf(v[i], v[i], sq);
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                    if (m == mm) sqm[m] += sq;
+                load4(p.normw + kk, w, p.x_vec);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] *= w[i];
+            }
+        }
+        float psum = 0.f;
+        if (F::MIN) {
+            psum = (v[0] + v[1]) + (v[2] + v[3]);
+#pragma unroll
+            for (int o = 1; o < GL; o <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+        }
+        if (act) {
+            const int kb = kk / F::QK, kq = kk - kb * F::QK;
+            int c, p0, j;
+            const int np = F::item_dest(kq & ~7, refcpu, c, p0, j);
+            const int wi = 2 * j + ((kq >> 2) & 1);  // word of the part
+            const int u = kb * F::UPB + c;
+            uint8_t* xrow = xq + static_cast<size_t>(mm) * p.xstride;
+            const float4 v4 = make_float4(v[0], v[1], v[2], v[3]);
+            for (int t = 0; t < np; ++t) {
+                *reinterpret_cast<float4*>(xrow + XL::chunk_off(u) + ((p0 + t) * XL::WPP + wi) * 512) = v4;
+                if (F::MIN && wi % GL == 0)
+                    *reinterpret_cast<float*>(xrow + XL::meta_off(u) + (p0 + t) * 128) = psum;
+            }
+        }
+    }
+}
+
 // One unit of one row: decode the quant bits, dot every part with every
 // activation row, add into acc.
 template <int T, int MT>
@@ -257,7 +470,7 @@ __device__ __forceinline__ int tmap_row0(int rg, int r_begin, int r_end, int RG)
     return (rg + RG > r_end && r_end - RG >= r_begin) ? r_end - RG : rg;
 }
 
-template <int T, int MT>
+template <int T, int MT, bool XF>
 __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
     gemv_kernel(const GemvParams p, const __grid_constant__ CUtensorMap tmap) {
     using F = Fmt<T>;
@@ -362,11 +575,14 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
 #pragma unroll
     for (int m = 0; m < MT; ++m) sqm[m] = 0.f;
 
-    // Activation prep: item = 8 consecutive elements of one row (one 16-byte
+    // Activation prep.  fp32 (XF): item = 4 consecutive elements (prep_xf).
+    // 16-bit fixed point: item = 8 consecutive elements of one row (one 16-byte
     // chunk of one unit part).  Four lanes hold one 32-element block (scale);
     // PE/8 lanes one part (integer sum).  Loads for two items per thread are
     // issued before any arithmetic.
-    {
+    if constexpr (XF) {
+        prep_xf<T, MT>(p, xq, ctid, NCT, sqm);
+    } else {
         const int ipr = p.K / 8;  // items per row (multiple of 4)
         const int items = MT * ipr;
         for (int base = 0; base < items; base += 2 * NCT) {
@@ -500,7 +716,8 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
                     const uint8_t* rowB = rowA + NCW * p.row_stride;
                     for (int uu = lane; uu < nu; uu += 32) {
                         const int kbl = uu / UPB, c = uu - kbl * UPB;
-                        unit_dot2<T, MT>(rowA + kbl * BB, rowB + kbl * BB, c, uu, xq, p.xstride, accA, accB);
+                        if constexpr (XF) unit_dotf2<T, MT>(rowA + kbl * BB, rowB + kbl * BB, c, uu, xq, p.xstride, accA, accB);
+                        else unit_dot2<T, MT>(rowA + kbl * BB, rowB + kbl * BB, c, uu, xq, p.xstride, accA, accB);
                     }
                     row_store<MT>(accA, lane, p.Y, p.M, p.N, rg + r0, rsc);
                     row_store<MT>(accB, lane, p.Y, p.M, p.N, rg + r0 + NCW, rsc);
@@ -508,7 +725,8 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
 #pragma unroll 2
                     for (int uu = lane; uu < nu; uu += 32) {
                         const int kbl = uu / UPB, c = uu - kbl * UPB;
-                        unit_dot<T, MT>(rowA + kbl * BB, c, uu, xq, p.xstride, accA);
+                        if constexpr (XF) unit_dotf<T, MT>(rowA + kbl * BB, c, uu, xq, p.xstride, accA);
+                        else unit_dot<T, MT>(rowA + kbl * BB, c, uu, xq, p.xstride, accA);
                     }
                     row_store<MT>(accA, lane, p.Y, p.M, p.N, rg + r0, rsc);
                 }
@@ -542,13 +760,17 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
             if (hasB) {
                 for (int uu = lane; uu < nu; uu += 32) {
                     const int kbl = uu / UPB, c = uu - kbl * UPB;
-                    unit_dot2<T, MT>(rowA + kbl * BB, rowB + kbl * BB, c, kb0 * UPB + uu, xq, p.xstride, accA, accB);
+                    if constexpr (XF)
+                        unit_dotf2<T, MT>(rowA + kbl * BB, rowB + kbl * BB, c, kb0 * UPB + uu, xq, p.xstride, accA, accB);
+                    else
+                        unit_dot2<T, MT>(rowA + kbl * BB, rowB + kbl * BB, c, kb0 * UPB + uu, xq, p.xstride, accA, accB);
                 }
             } else if (hasA) {
 #pragma unroll 2
                 for (int uu = lane; uu < nu; uu += 32) {
                     const int kbl = uu / UPB, c = uu - kbl * UPB;
-                    unit_dot<T, MT>(rowA + kbl * BB, c, kb0 * UPB + uu, xq, p.xstride, accA);
+                    if constexpr (XF) unit_dotf<T, MT>(rowA + kbl * BB, c, kb0 * UPB + uu, xq, p.xstride, accA);
+                    else unit_dot<T, MT>(rowA + kbl * BB, c, kb0 * UPB + uu, xq, p.xstride, accA);
                 }
             }
             __syncwarp();
@@ -571,8 +793,9 @@ __global__ void __launch_bounds__(Cfg<MT>::THREADS, 2)
 static inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 template <int T>
-static uint32_t x_area_bytes_t(int MT, int K) {
-    return static_cast<uint32_t>(MT) * static_cast<uint32_t>(XLay<T>::row_bytes(K));
+static uint32_t x_area_bytes_t(int MT, int K, bool xf) {
+    return static_cast<uint32_t>(MT) *
+           static_cast<uint32_t>(xf ? XLayF<T>::row_bytes(K) : XLay<T>::row_bytes(K));
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -592,7 +815,7 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int T, int MT>
+template <int T, int MT, bool XF>
 static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
     using F = Fmt<T>;
     constexpr int RGMAX = Cfg<MT>::RGMAX;
@@ -616,7 +839,7 @@ static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
     // float4 activation loads: every row start 16-byte aligned (K % 32 == 0)
     auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     p.x_vec = (al(L.X) && al(L.R) && al(L.normw) && al(L.sum_out) && p.ld % 4 == 0) ? 1 : 0;
-    p.xstride = XLay<T>::row_bytes(L.K);
+    p.xstride = XF ? XLayF<T>::row_bytes(L.K) : XLay<T>::row_bytes(L.K);
 
     const int per_sm = L.ctas_per_sm > 0 ? L.ctas_per_sm : 1;
     const int grid = std::max(1, std::min(L.num_sms * per_sm, L.N));
@@ -626,7 +849,7 @@ static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
     uint32_t off = 2 * 16 * 8 + 16;
     off = align_up(off, 128);
     p.off_xq = off;
-    off += x_area_bytes_t<T>(MT, L.K);
+    off += x_area_bytes_t<T>(MT, L.K, XF);
     off = align_up(off, 128);
     p.off_ring = off;
     // (1 KB stays free for the kernel's static shared memory)
@@ -731,7 +954,7 @@ static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
         p.stages = std::max(2, std::min({static_cast<int>(ring_cap / p.stage_bytes), 8, need}));
     }
     const uint32_t smem = off + static_cast<uint32_t>(p.stages) * p.stage_bytes;
-    auto kern = gemv_kernel<T, MT>;
+    auto kern = gemv_kernel<T, MT, XF>;
     // The attribute is per device: raise it once to the opt-in maximum.
     static thread_local int set_dev = -1;
     int dev = -1;
@@ -756,23 +979,39 @@ static cudaError_t launch_t(const GemvLaunch& L, cudaStream_t stream) {
     return cudaLaunchKernelEx(&cfg, kern, p, tmap);
 }
 
+// fp32 activations (L.xf) for up to 4 rows when they fit the budget below;
+// else (or with L.xf = 0) 16-bit fixed-point activations.
+constexpr uint32_t kXfMaxBytes = 120u * 1024u;
+
 template <int T>
 static cudaError_t launch_fmt(const GemvLaunch& L, cudaStream_t s) {
-    if (L.M <= 1) return launch_t<T, 1>(L, s);
-    if (L.M <= 2) return launch_t<T, 2>(L, s);
-    if (L.M <= 4) return launch_t<T, 4>(L, s);
-    return launch_t<T, 8>(L, s);
+    const int mt = L.M <= 1 ? 1 : L.M <= 2 ? 2 : L.M <= 4 ? 4 : 8;
+    if (L.xf && mt <= 4 && x_area_bytes_t<T>(mt, L.K, true) <= kXfMaxBytes) {
+        if (mt == 1) return launch_t<T, 1, true>(L, s);
+        if (mt == 2) return launch_t<T, 2, true>(L, s);
+        return launch_t<T, 4, true>(L, s);
+    }
+    if (mt == 1) return launch_t<T, 1, false>(L, s);
+    if (mt == 2) return launch_t<T, 2, false>(L, s);
+    if (mt == 4) return launch_t<T, 4, false>(L, s);
+    return launch_t<T, 8, false>(L, s);
 }
 
-size_t gemv_smem_x_bytes(int type, int MT, int K) {
+template <int T>
+static size_t smem_x_bytes_fmt(int MT, int K, bool xf) {
+    if (xf && MT <= 4 && x_area_bytes_t<T>(MT, K, true) <= kXfMaxBytes) return x_area_bytes_t<T>(MT, K, true);
+    return x_area_bytes_t<T>(MT, K, false);
+}
+
+size_t gemv_smem_x_bytes(int type, int MT, int K, bool xf) {
     switch (type) {
-        case Q4_0: return x_area_bytes_t<Q4_0>(MT, K);
-        case Q8_0: return x_area_bytes_t<Q8_0>(MT, K);
-        case Q2_K: return x_area_bytes_t<Q2_K>(MT, K);
-        case Q3_K: return x_area_bytes_t<Q3_K>(MT, K);
-        case Q4_K: return x_area_bytes_t<Q4_K>(MT, K);
-        case Q5_K: return x_area_bytes_t<Q5_K>(MT, K);
-        case Q6_K: return x_area_bytes_t<Q6_K>(MT, K);
+        case Q4_0: return smem_x_bytes_fmt<Q4_0>(MT, K, xf);
+        case Q8_0: return smem_x_bytes_fmt<Q8_0>(MT, K, xf);
+        case Q2_K: return smem_x_bytes_fmt<Q2_K>(MT, K, xf);
+        case Q3_K: return smem_x_bytes_fmt<Q3_K>(MT, K, xf);
+        case Q4_K: return smem_x_bytes_fmt<Q4_K>(MT, K, xf);
+        case Q5_K: return smem_x_bytes_fmt<Q5_K>(MT, K, xf);
+        case Q6_K: return smem_x_bytes_fmt<Q6_K>(MT, K, xf);
         default: return 0;
     }
 }
@@ -915,7 +1154,7 @@ template <int T, int MT>
 static cudaError_t launch_grouped_gemv_t(const GroupedGemvParams& p0, int smem_optin, cudaStream_t s) {
     GroupedGemvParams p = p0;
     p.xstride = XLay<T>::row_bytes(p.K);
-    const size_t smem = static_cast<size_t>(MT) * p.xstride;
+    const size_t smem = static_cast<size_t>(MT) * p.xstride;  // 16-bit fixed-point activations
     if (smem > static_cast<size_t>(smem_optin)) return cudaErrorInvalidConfiguration;
     auto kern = grouped_gemv_kernel<T, MT>;
     if (smem > 48 * 1024) {

@@ -33,6 +33,7 @@ struct GemvLaunch {
     int smem_kb;   // CTA shared-memory budget in KB (0: automatic)
     int stage_kb;  // largest weight stage in KB (0: 96)
     int ctas_per_sm;  // 0: automatic
+    int xf = 1;       // fp32 activations (else 16-bit fixed point)
     // activation prologue (ACT_*); ld = X row stride in elements (0: K, SWIGLU: 2K)
     int act = ACT_NONE;
     const float* R = nullptr;
@@ -55,7 +56,7 @@ cudaError_t grouped_gemv_launch(int type, const void* const* wptrs, const int* o
                                 int n_experts, int rows_total, int N, int K, int refcpu, int smem_optin,
                                 cudaStream_t s);
 // Shared-memory bytes of the per-CTA activation prep for padded row count MT.
-size_t gemv_smem_x_bytes(int type, int MT, int K);
+size_t gemv_smem_x_bytes(int type, int MT, int K, bool xf);
 
 // Bit-exact dequantization of nblocks whole blocks.
 cudaError_t dequant_launch(int type, const void* src, float* dst, int64_t nblocks, int num_sms,

@@ -95,6 +95,63 @@ def fast_random_blocks(type_id: int, N: int, K: int, seed: int = 0,
     return blk.reshape(N, nb * bb)
 
 
+def _k4_unpack(s: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """[..., 12] packed K-quant scale bytes -> (scales, mins) [..., 8]
+    (get_scale_min_k4, src/tensor.h:218-227)."""
+    s = s.astype(np.int32)
+    sc = np.empty(s.shape[:-1] + (8,), np.int32)
+    mn = np.empty_like(sc)
+    for j in range(4):
+        sc[..., j] = s[..., j] & 63
+        mn[..., j] = s[..., j + 4] & 63
+        sc[..., j + 4] = (s[..., j + 8] & 15) | ((s[..., j] >> 6) << 4)
+        mn[..., j + 4] = (s[..., j + 8] >> 4) | ((s[..., j + 4] >> 6) << 4)
+    return sc, mn
+
+
+def _k4_pack(sc: np.ndarray, mn: np.ndarray) -> np.ndarray:
+    out = np.empty(sc.shape[:-1] + (12,), np.int32)
+    for j in range(4):
+        out[..., j] = (sc[..., j] & 63) | ((sc[..., j + 4] >> 4) << 6)
+        out[..., j + 4] = (mn[..., j] & 63) | ((mn[..., j + 4] >> 4) << 6)
+        out[..., j + 8] = (sc[..., j + 4] & 15) | ((mn[..., j + 4] & 15) << 4)
+    return out.astype(np.uint8)
+
+
+def centred_blocks(type_id: int, N: int, K: int, seed: int = 0, d_scale: float = 2e-3) -> np.ndarray:
+    """random_blocks with the mins of the formats that have them (Q2_K, Q4_K,
+    Q5_K) chosen as a quantizer chooses them: each sub-block's values centred
+    on zero (dmin per block, min codes = round(mean of d * scale * q / dmin)).
+    The other formats are centred by construction (zero point in the middle of
+    the code range) and come back as random_blocks.  Benchmark-distribution
+    blocks (independent uniform min codes) give every Q4_K weight a mean of
+    about +0.45, and a random model built of them amplifies rounding by orders
+    of magnitude; a quantized real model does not."""
+    blk = random_blocks(type_id, N, K, seed, d_scale=d_scale)
+    if type_id not in (Q2_K, Q4_K, Q5_K):
+        return blk
+    qk, bb, d_off, m_off = LAYOUT[type_id]
+    b = blk.reshape(N, K // qk, bb)
+    d = b[..., d_off:d_off + 2].copy().view(np.float16)[..., 0].astype(np.float64)
+    if type_id == Q2_K:
+        sc = (b[..., :16] & 15).astype(np.int32)
+        target = 1.5 * d[..., None] * sc                       # mean of d * sc * q, q uniform 0..3
+        dmin = (target.max(axis=-1) / 15.0).astype(np.float16)
+        dm = dmin.astype(np.float64)[..., None]
+        mn = np.where(dm > 0, np.clip(np.rint(target / np.where(dm > 0, dm, 1.0)), 0, 15), 0).astype(np.int32)
+        b[..., :16] = (sc | (mn << 4)).astype(np.uint8)
+    else:
+        sc, _ = _k4_unpack(b[..., 4:16])
+        qmean = 7.5 if type_id == Q4_K else 15.5
+        target = qmean * d[..., None] * sc
+        dmin = (target.max(axis=-1) / 63.0).astype(np.float16)
+        dm = dmin.astype(np.float64)[..., None]
+        mn = np.where(dm > 0, np.clip(np.rint(target / np.where(dm > 0, dm, 1.0)), 0, 63), 0).astype(np.int32)
+        b[..., 4:16] = _k4_pack(sc, mn)
+    b[..., m_off:m_off + 2] = dmin[..., None].view(np.uint8)
+    return b.reshape(N, -1)
+
+
 def random_activations(M: int, K: int, seed: int = 1) -> np.ndarray:
     rng = np.random.default_rng(seed)
     return rng.standard_normal((M, K), dtype=np.float32)
