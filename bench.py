@@ -49,15 +49,19 @@ METRIC = "Q4_K GEMV achieved HBM GB/s (% peak); decode tok/s at 1/2/4/8 B200"
 DECODE_DEADLINE_S = 420  # all decode measurements of the default run (about 60 s on one GPU)
 N_ROWS, K_COLS, M_ROWS = 4096, 4096, 1
 COPIES = 64
+REPLAYS = 128       # graph replays per step: a step is REPLAYS x COPIES GEMVs
+GEMV_STREAMS = 2    # streams the COPIES independent GEMVs of a graph alternate over
+REF_STEP_GEMVS = 64  # GEMVs per step of the reference arm
 Q4_K = 12
 BLOCK_BYTES = 144
 W_BYTES = N_ROWS * (K_COLS // 256) * BLOCK_BYTES              # 9,437,184
 ALG_BYTES = W_BYTES + 4 * K_COLS * M_ROWS + 4 * N_ROWS * M_ROWS  # 9,469,952 per GEMV
 WORKLOAD = (f"Q4_K GEMV N={N_ROWS} K={K_COLS} M={M_ROWS}, {COPIES} rotating weight copies "
             f"({COPIES * W_BYTES / 1e6:.0f} MB)")
-# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_kernel<Q4_K,1> launch
-# of this workload, from one ncu capture (profiles/gemv_q4k_4096x4096.md).
-NCU_TRAFFIC_PER_LAUNCH = 9_496_832
+# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_kernel<Q4_K,1,true>
+# launch of this workload, from one ncu capture (profiles/gemv_q4k_4096x4096.md);
+# None until that capture exists.
+NCU_TRAFFIC_PER_LAUNCH = None
 
 
 _T0 = time.time()
@@ -132,6 +136,17 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+class _NoClock:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        pass
+
+    def summary(self) -> dict:
+        return {}
+
+
 # ---------------------------------------------------------------- CPU arm
 def cpu_model() -> str:
     try:
@@ -144,10 +159,12 @@ def cpu_model() -> str:
     return "unknown"
 
 
-def cpu_gemv_timing(seconds: float, max_steps: int | None = None, copies: int = 16, threads: int = 0) -> dict:
-    """The reference CPU routine on all host cores (or `threads`), one
-    4096x4096 Q4_K GEMV per step, rotating over `copies` weight matrices
-    (151 MB, beyond the LLC)."""
+def cpu_gemv_timing(seconds: float, min_steps: int = 1, copies: int = 16, threads: int = 0, warmup: int = 1,
+                    per_step: int = 1) -> dict:
+    """The reference CPU routine on all host cores (or `threads`): steps of
+    `per_step` Q4_K 4096x4096 GEMVs rotating over `copies` weight matrices
+    (151 MB, beyond the LLC), after `warmup` untimed GEMVs; at least
+    `min_steps` steps and at least `seconds` of timed work."""
     import numpy as np
 
     import oracle
@@ -161,22 +178,26 @@ def cpu_gemv_timing(seconds: float, max_steps: int | None = None, copies: int = 
     else:
         kind = "port"
         oracle.set_threads(cores)
-        fn = lambda w, x: oracle.gemv(Q4_K, w, x, N_ROWS, K_COLS, format_order=False)  # noqa: E731
+        fn = lambda w, x: oracle.gemv(Q4_K, w, x, N_ROWS, K_COLS)  # noqa: E731
     ws = [synth.random_blocks(Q4_K, N_ROWS, K_COLS, seed=1000 + i) for i in range(copies)]
     x = synth.random_activations(1, K_COLS, seed=7)[0]
-    fn(ws[0], x)  # warm-up
-    n = 0
+    for i in range(max(1, warmup)):
+        fn(ws[i % copies], x)
+    n = steps = 0
     t0 = time.perf_counter()
     while True:
-        fn(ws[n % copies], x)
-        n += 1
+        for _ in range(per_step):
+            fn(ws[n % copies], x)
+            n += 1
+        steps += 1
         el = time.perf_counter() - t0
-        if el >= seconds or (max_steps is not None and n >= max_steps):
+        if el >= seconds and steps >= min_steps:
             break
     gbs = n * ALG_BYTES / el / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
-            "sample": f"{n} Q4_K GEMVs N={N_ROWS} K={K_COLS} M=1 over {copies} weight copies, "
-                      f"{el:.1f} s, {cores} OpenMP threads", "seconds": round(el, 2), "steps": n}
+            "sample": f"{n} Q4_K GEMVs N={N_ROWS} K={K_COLS} M=1 over {copies} weight copies "
+                      f"({steps} steps of {per_step}), {el:.1f} s, {cores} OpenMP threads, after "
+                      f"{max(1, warmup)} warm-up GEMVs", "seconds": round(el, 2), "steps": steps, "gemvs": n}
 
 
 def write_llama_gguf(path, cfg, seed: int = 0) -> int:
@@ -289,13 +310,14 @@ def ref_decode_timing(cfg, seconds: float = 20.0, max_tokens: int = 8, workdir: 
 def run_reference(args, rank: int) -> None:
     if rank != 0:
         return
-    budget = 60.0  # seconds of CPU work for the whole --steps run
-    r = cpu_gemv_timing(seconds=budget, max_steps=max(1, args.steps))
-    one = cpu_gemv_timing(seconds=5.0, max_steps=max(1, args.steps), copies=4, threads=1)
+    # steps of 64 GEMVs (one graph's worth of the GPU arm), --steps of them
+    # and at least 10 s of timed CPU work, after --warmup warm-up GEMVs
+    r = cpu_gemv_timing(seconds=10.0, min_steps=max(1, args.steps), warmup=args.warmup, per_step=REF_STEP_GEMVS)
+    one = cpu_gemv_timing(seconds=5.0, copies=4, threads=1, warmup=1, per_step=1)
     import oracle
     (oracle.ref_set_threads if oracle.ref_available() else oracle.set_threads)(oracle.host_cores())
     line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "GB/s",
-            "n_gpus": args.gpus, "steps": r["steps"], "warmup": args.warmup,
+            "n_gpus": args.gpus, "steps": r["steps"], "warmup": args.warmup, "steps_requested": args.steps,
             "ms_per_step": round(1e3 * r["seconds"] / r["steps"], 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"Q4_K GEMV N={N_ROWS} K={K_COLS} M=1 (reference CPU path)",
@@ -347,52 +369,80 @@ def run_swq(args, rank: int, world: int) -> None:
     d_x = torch.from_numpy(x_host).to(dev)
     d_ys = [torch.empty(N_ROWS, dtype=torch.float32, device=dev) for _ in range(COPIES)]
 
-    stream = torch.cuda.Stream(device=dev)
     torch.cuda.synchronize()
 
-    def step():
-        for i in range(COPIES):
-            swq.gemv(Q4_K, d_ws[i], d_x, d_ys[i], N_ROWS, K_COLS, stream=stream)
+    def capture(nstreams: int):
+        """One CUDA graph of the COPIES GEMVs, launch i on stream i % nstreams:
+        the graph holds no edge between GEMVs of different streams (they are
+        independent: same x, their own W and y), so their kernels may run at
+        the same time; on one stream each waits for its predecessor
+        (programmatic dependent launch: its weights stream in early, x is
+        read after the predecessor completes)."""
+        streams = [torch.cuda.Stream(device=dev) for _ in range(nstreams)]
+        main = streams[0]
 
-    with torch.cuda.stream(stream):
-        step()  # eager warm-up: attributes set, kernels loaded
-    swq.check(stream)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step()
-    with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup)):
-            graph.replay()
-    stream.synchronize()
+        def issue():
+            fork = torch.cuda.Event()
+            fork.record(main)
+            for st in streams[1:]:
+                st.wait_event(fork)
+            for i in range(COPIES):
+                st = streams[i % nstreams]
+                swq.gemv(Q4_K, d_ws[i], d_x, d_ys[i], N_ROWS, K_COLS, stream=st)
+            for st in streams[1:]:
+                join = torch.cuda.Event()
+                join.record(st)
+                main.wait_event(join)
+
+        with torch.cuda.stream(main):
+            issue()  # eager warm-up: attributes set, kernels loaded
+        swq.check(main)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=main):
+            issue()
+        return g, main
+
+    def time_steps(g, st, steps: int, warmup: int, clocks: bool):
+        with torch.cuda.stream(st):
+            for _ in range(warmup * REPLAYS):
+                g.replay()
+        st.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(gpu_uuid) if clocks else _NoClock() as clk:
+            with torch.cuda.stream(st):
+                ev0.record(st)
+                for _ in range(steps * REPLAYS):
+                    g.replay()
+                ev1.record(st)
+            ev1.synchronize()
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        swq.check(st)
+        if dist:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        return ms, clk.summary()
 
     peak, peak_kind = load_peaks()
     gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
     gpu_uuid = gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}"
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    log(f"gemv: timing {args.steps} steps")
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(gpu_uuid) as clk:
-        with torch.cuda.stream(stream):
-            ev0.record(stream)
-            for _ in range(args.steps):
-                graph.replay()
-            ev1.record(stream)
-        ev1.synchronize()
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    swq.check(stream)
-    if dist:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
-    launches = args.steps * COPIES
+    graph, stream = capture(GEMV_STREAMS)
+    graph1, stream1 = capture(1)
+    log(f"gemv: timing {args.steps} steps of {REPLAYS} x {COPIES} GEMVs on {GEMV_STREAMS} streams")
+    ms, clocks = time_steps(graph, stream, args.steps, max(3, args.warmup), clocks=True)
+    chain_steps = max(1, min(args.steps, 10))
+    ms1, _ = time_steps(graph1, stream1, chain_steps, 3, clocks=False)
+    launches = args.steps * REPLAYS * COPIES
     total_bytes = launches * ALG_BYTES * world
     value = total_bytes / (ms * 1e-3) / 1e9
     per_launch_s = ms * 1e-3 / launches
     achieved = ALG_BYTES / per_launch_s / 1e9
+    chain_launch_s = ms1 * 1e-3 / (chain_steps * REPLAYS * COPIES)
 
     # The host-buffer path below must reproduce the device result of the last copy.
     y_last = d_ys[-1].cpu().numpy()
@@ -431,17 +481,25 @@ def run_swq(args, rank: int, world: int) -> None:
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int32", "data": "synthetic",
+            "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "format": "Q4_K", "N": N_ROWS, "K": K_COLS, "M": M_ROWS,
-                       "copies": COPIES, "bytes_per_gemv": ALG_BYTES,
+                       "copies": COPIES, "gemvs_per_step": REPLAYS * COPIES, "bytes_per_gemv": ALG_BYTES,
+                       "issue": f"{COPIES} independent GEMVs (same x, own W and y) per graph, alternating over "
+                                f"{GEMV_STREAMS} streams; consecutive GEMVs of one stream are programmatic "
+                                f"dependents (weights prefetched, x read after the predecessor completes)",
                        "l2": "inputs larger than L2 (rotating weights)",
-                       "arith": "Q4_K nibbles x 16-bit fixed-point x (dp2a, int32), fp32 scales",
+                       "arith": "fp32 activations; Q4_K nibbles converted exactly to fp32; fp32 FMA (f32x2), "
+                                "fp32 scales",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": NCU_TRAFFIC_PER_LAUNCH,
-                         "kernel": "swq::gemv_kernel<Q4_K,1>", "alg_bytes_per_launch": ALG_BYTES,
-                         "us_per_launch": round(per_launch_s * 1e6, 3)},
+                         "kernel": "swq::gemv_kernel<Q4_K,1,true>", "alg_bytes_per_launch": ALG_BYTES,
+                         "us_per_launch": round(per_launch_s * 1e6, 3),
+                         "chain": {"us_per_launch": round(chain_launch_s * 1e6, 3),
+                                   "achieved": round(ALG_BYTES / chain_launch_s / 1e9, 1),
+                                   "frac": round(ALG_BYTES / chain_launch_s / 1e9 / peak, 4),
+                                   "note": "the same GEMVs on one stream: each waits for its predecessor"}},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": COPIES * 4 * K_COLS * M_ROWS,
@@ -449,11 +507,11 @@ def run_swq(args, rank: int, world: int) -> None:
                     "api": "swq_ctx_matmul_transposed_q (host fp32 x/out, resident weights)",
                     "steps": e2e_steps},
             "gpu_launches": launches,
-            "clocks": clk.summary(),
+            "clocks": clocks,
             "decode": None,
             "decode_70b": None,
         }
-    del graph
+    del graph, graph1
 
     # The decode measurements run under a deadline: if one does not finish
     # (a collective that never completes), rank 0 prints the line with what
@@ -471,9 +529,12 @@ def run_swq(args, rank: int, world: int) -> None:
     timer = threading.Timer(DECODE_DEADLINE_S, _deadline)
     timer.daemon = True
     timer.start()
+    if world == 1 and args.sweep:
+        log("gemv: done; config-1 format x batch sweep")
+        line["sweep"] = run_sweep()
     if args.decode:
         log("gemv: done; decode next")
-        decode = run_decode(rank, world, steps=128)
+        decode = run_decode(rank, world, steps=256)
         if line is not None:
             line["decode"] = decode
         decode_tp = run_decode_tp(rank, world)
@@ -526,13 +587,28 @@ def run_prefill(rank: int, prompt: int = 512, reps: int = 3, warmup: int = 1, se
 # How the decode measurements build their context: "synthetic" (random K/V in
 # the cache, Decoder.fill_kv) or "prefill" (LlamaDecoder.prefill of uniform
 # random prompt tokens, timed on its own and reported as prefill_ms).
-DECODE_CONTEXT = "synthetic"
+DECODE_CONTEXT = "prefill"
 
 
-def _build_context(dec, n: int, seed: int) -> dict:
-    """Positions 0..n-1 of every sequence, then the decoder stands at position n."""
+def _build_context(dec, n: int, seed: int, share_from=None) -> dict:
+    """Positions 0..n-1 of every sequence, then the decoder stands at position n.
+    share_from: a one-row decoder of the same model that prefilled the prompt;
+    every row of `dec` continues from its cache (one prompt shared by the
+    batch: its K/V rows copied, no second prefill)."""
     import numpy as np
     import torch
+    if share_from is not None:
+        src = share_from
+        with torch.cuda.stream(dec.stream):
+            dec.stream.wait_stream(src.stream)
+            dec.kcache[:, :, :n].copy_(src.kcache[:, :1, :n].expand(-1, dec.rows, -1, -1))
+            dec.vcache[:, :, :n].copy_(src.vcache[:, :1, :n].expand(-1, dec.rows, -1, -1))
+            dec.tokens.fill_(int(src.history[0, 0].item()))
+            dec.history[0].fill_(int(src.history[0, 0].item()))
+            dec.pos.fill_(n)
+            dec.step_no.fill_(1)
+        dec.steps_issued = 1
+        return {"context": f"the {n}-token prompt prefilled at batch 1, its K/V shared by the {dec.rows} rows"}
     if DECODE_CONTEXT == "prefill":
         toks = np.random.default_rng(seed).integers(0, dec.cfg.vocab, size=(dec.rows, n)).tolist()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -617,9 +693,10 @@ def run_decode_tp(rank: int, world: int, batches=(1, 8, 32), context: int = 2048
     64/8 heads of 128, FFN 28672, vocab 128256, Q4_K_M mix, synthetic weights
     generated on the device), tensor-parallel over all ranks (column-sharded
     q/k/v and gate/up, row-sharded o and down with an NCCL all-reduce each,
-    vocab-sharded LM head with an all-gather), after a synthetic context of
-    `context` tokens.  One rank: the whole model on one GPU.  tok/s = tokens
-    of the whole job per second (max time over ranks)."""
+    vocab-sharded LM head with an all-gather), after a `context`-token prefill
+    of uniform random token ids (batch 1, timed on its own; the larger batches
+    share that prompt's K/V).  One rank: the whole model on one GPU.  tok/s =
+    tokens of the whole job per second (max time over ranks)."""
     import torch
 
     from swq.model import LlamaConfig, LlamaDecoder
@@ -646,7 +723,9 @@ def run_decode_tp(rank: int, world: int, batches=(1, 8, 32), context: int = 2048
         import swq
         swq.check(dec.stream)  # a collective that timed out fails here, not in the timed loop
         log(f"decode70b: tp={world} batch {B}: captured")
-        ctx = _build_context(dec, context, seed=13)  # the same prompt on every rank
+        # the same prompt on every rank; batches above 1 share the batch-1 prefill
+        ctx = _build_context(dec, context, seed=13,
+                             share_from=base if (dec is not base and DECODE_CONTEXT == "prefill") else None)
         dec.generate(warmup)
         dec.stream.synchronize()
         swq.check(dec.stream)
@@ -675,6 +754,90 @@ def run_decode_tp(rank: int, world: int, batches=(1, 8, 32), context: int = 2048
     base.graph = None
     del base
     torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------- config-1 sweep
+SWEEP_FORMATS = ("Q4_0", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K")
+SWEEP_MS = (1, 8, 64, 512)
+
+
+def run_sweep(N: int = 14336, K: int = 4096, launches: int = 40, cpu_seconds: float = 1.0) -> dict:
+    """Quant-format x batch sweep on the Llama-3-8B FFN up-projection shape:
+    Y[M x N] = X[M x K] . W^T for every format and M in SWEEP_MS, through
+    swq_gemm (the fused GEMV kernel for M < 5, the tensor-core GEMM above),
+    CUDA-event timed over `launches` calls that rotate over weight copies
+    larger than 4 x L2 together.  Roofline per point: HBM (weight + X + Y
+    bytes) and tensor (2 M N K flops), whichever bounds it.  Beside each, the
+    reference's CPU routine on all host cores: one matmul_transposed_q per
+    activation row (it has no batched path), its per-row time measured on a
+    bounded sample and multiplied by M."""
+    import torch
+
+    import oracle
+    import swq
+    from swq import synth
+    from swq.model import synthetic_blocks
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    hbm, hbm_kind = load_peaks()
+    tc, tc_kind = load_tensor_peak()
+    g = torch.Generator(device=dev)
+    g.manual_seed(41)
+    cores = oracle.host_cores()
+    use_ref = oracle.ref_available()
+    (oracle.ref_set_threads if use_ref else oracle.set_threads)(cores)
+    out = {"shape": f"N={N} K={K}", "launches_per_point": launches,
+           "peaks": {"hbm_GBps": hbm, "hbm_kind": hbm_kind, "bf16_TFLOPs": tc, "tensor_kind": tc_kind},
+           "cpu": {"kind": "reference" if use_ref else "port", "cores": cores,
+                   "sample": f"matmul_transposed_q on {cores} threads, about {cpu_seconds:.1f} s per format; "
+                             "M > 1 is M such calls"},
+           "points": []}
+    for name in SWEEP_FORMATS:
+        t = TYPE_IDS[name]
+        wbytes = synth.matrix_bytes(t, N, K)
+        copies = max(2, -(-4 * 126_000_000 // wbytes))
+        ws = [synthetic_blocks(t, N, K, g, dev) for _ in range(copies)]
+        # the reference's per-row time: one host matrix, rows of X cycled
+        hw = synth.fast_random_blocks(t, N, K, seed=90 + t)
+        hx = synth.random_activations(4, K, seed=91)
+        fn = (lambda w, x: oracle.ref_gemv(t, w, x, N, K)) if use_ref else \
+             (lambda w, x: oracle.gemv(t, w, x, N, K))
+        fn(hw, hx[0])
+        n, t0 = 0, time.perf_counter()
+        while True:
+            fn(hw, hx[n % 4])
+            n += 1
+            if time.perf_counter() - t0 >= cpu_seconds:
+                break
+        cpu_row_s = (time.perf_counter() - t0) / n
+        for M in SWEEP_MS:
+            X = torch.randn((M, K), device=dev, generator=g)
+            Y = torch.empty((M, N), device=dev)
+            for i in range(3):
+                swq.gemm(t, ws[i % copies], X, Y, M, N, K)
+            swq.check()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(launches):
+                swq.gemm(t, ws[i % copies], X, Y, M, N, K)
+            e1.record()
+            e1.synchronize()
+            swq.check()
+            sec = e0.elapsed_time(e1) * 1e-3 / launches
+            nbytes = wbytes + 4 * M * K + 4 * M * N
+            flops = 2.0 * M * N * K
+            gbs, tfs = nbytes / sec / 1e9, flops / sec / 1e12
+            tc_path = M >= swq.get_option(swq.OPT_TENSOR_CORE_MIN_M)
+            t_roof = max(nbytes / (hbm * 1e9), flops / (tc * 1e12))
+            out["points"].append({
+                "format": name, "M": M, "us": round(sec * 1e6, 2), "GBps": round(gbs, 1), "TFLOPs": round(tfs, 2),
+                "path": "tensor-core GEMM (fp16 operands, fp32 accumulate)" if tc_path else "GEMV (fp32)",
+                "bound": "tensor" if flops / (tc * 1e12) > nbytes / (hbm * 1e9) else "hbm",
+                "roofline_frac": round(t_roof / sec, 4),
+                "cpu_ms": round(cpu_row_s * M * 1e3, 3), "speedup_vs_cpu": round(cpu_row_s * M / sec, 1)})
+        del ws
+        torch.cuda.empty_cache()
     return out
 
 
@@ -916,7 +1079,8 @@ def run_gemm(args, rank: int, world: int) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--steps", type=int, default=20,
+                    help="timed steps (headline: a step is 128 replays of the 64-GEMV graph)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["swq", "reference"], default="swq")
     ap.add_argument("--workload", choices=["gemv", "gemm", "decode", "decode70b", "moe", "prefill", "prefill70b"],
@@ -932,11 +1096,13 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU sample length (0: skip)")
     ap.add_argument("--collective", choices=["peer", "nccl"], default="peer",
                     help="decode70b: sums of the row-parallel projections")
+    ap.add_argument("--no-sweep", dest="sweep", action="store_false",
+                    help="skip the quant-format x batch sweep (N=14336, K=4096) of the default one-GPU run")
     ap.add_argument("--no-decode", dest="decode", action="store_false",
                     help="skip the Llama-3-8B decode tok/s measurement of the default run")
     ap.add_argument("--gguf", default=None, help="--workload decode: decode this GGUF model file instead of "
                                                   "the synthetic Llama-3-8B-shaped one")
-    ap.add_argument("--decode-context", choices=["synthetic", "prefill"], default="synthetic",
+    ap.add_argument("--decode-context", choices=["synthetic", "prefill"], default="prefill",
                     help="decode measurements: context as random K/V (synthetic) or a batched prefill of "
                          "random prompt tokens (prefill, also timed)")
     args = ap.parse_args()

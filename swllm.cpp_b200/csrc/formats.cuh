@@ -56,6 +56,23 @@ __device__ __forceinline__ void scale_min_k4_unit(int c, int t, uint32_t s0, uin
     m = hi ? ((a2 >> 4) | ((a1 >> 6) << 4)) : (a1 & 63u);
 }
 
+// get_scale_min_k4 for sub-blocks 2c and 2c + 1 of a unit, as floats: all 8
+// 6-bit scales and mins of the block are assembled bytewise from the 12-byte
+// field (s0, s1, s2) in a few word operations, and each selected byte becomes
+// an exact float through the low mantissa of 2^23.
+__device__ __forceinline__ void scale_min_k4_pair(int c, uint32_t s0, uint32_t s1, uint32_t s2, float& sc0,
+                                                  float& m0, float& sc1, float& m1) {
+    const uint32_t scl = s0 & 0x3F3F3F3Fu, mnl = s1 & 0x3F3F3F3Fu;  // sub-blocks 0..3
+    const uint32_t sch = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);  // 4..7
+    const uint32_t mnh = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
+    const uint32_t SC = c < 2 ? scl : sch, MN = c < 2 ? mnl : mnh;
+    const uint32_t sel0 = 0x7650u + ((2 * c) & 3), sel1 = sel0 + 1;
+    sc0 = __uint_as_float(__byte_perm(SC, 0x4B000000u, sel0)) - 8388608.0f;
+    sc1 = __uint_as_float(__byte_perm(SC, 0x4B000000u, sel1)) - 8388608.0f;
+    m0 = __uint_as_float(__byte_perm(MN, 0x4B000000u, sel0)) - 8388608.0f;
+    m1 = __uint_as_float(__byte_perm(MN, 0x4B000000u, sel1)) - 8388608.0f;
+}
+
 // Q3_K signed scales, src/tensor.h:286-304: word w (0..3) of the unpacked
 // 16 scales, each word reduced by 0x20202020 as a whole (byte borrows kept).
 __device__ __forceinline__ uint32_t q3k_scale_word(int w, uint32_t t0, uint32_t t1, uint32_t t2) {
@@ -319,13 +336,12 @@ struct Fmt<Q4_K> {
             q[8 + i] = w[i] & 0xF0F0F0F0u;
         }
         const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hd.x));
-        uint32_t sc0, m0, sc1, m1;
-        scale_min_k4_unit(c, 0, hd.y, hd.z, hd.w, sc0, m0);
-        scale_min_k4_unit(c, 1, hd.y, hd.z, hd.w, sc1, m1);
-        wd[0] = dm.x * static_cast<float>(sc0);
-        wm[0] = dm.y * static_cast<float>(m0);
-        wd[1] = dm.x * static_cast<float>(sc1) * 0.0625f;
-        wm[1] = dm.y * static_cast<float>(m1);
+        float sc0, m0, sc1, m1;
+        scale_min_k4_pair(c, hd.y, hd.z, hd.w, sc0, m0, sc1, m1);
+        wd[0] = dm.x * sc0;
+        wm[0] = dm.y * m0;
+        wd[1] = dm.x * sc1 * 0.0625f;
+        wm[1] = dm.y * m1;
     }
 };
 
@@ -378,13 +394,12 @@ struct Fmt<Q5_K> {
             q[8 + i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | ((hb & 0x02020202u) << 3);
         }
         const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hd.x));
-        uint32_t sc0, m0, sc1, m1;
-        scale_min_k4_unit(c, 0, hd.y, hd.z, hd.w, sc0, m0);
-        scale_min_k4_unit(c, 1, hd.y, hd.z, hd.w, sc1, m1);
-        wd[0] = dm.x * static_cast<float>(sc0);
-        wm[0] = dm.y * static_cast<float>(m0);
-        wd[1] = dm.x * static_cast<float>(sc1);
-        wm[1] = dm.y * static_cast<float>(m1);
+        float sc0, m0, sc1, m1;
+        scale_min_k4_pair(c, hd.y, hd.z, hd.w, sc0, m0, sc1, m1);
+        wd[0] = dm.x * sc0;
+        wm[0] = dm.y * m0;
+        wd[1] = dm.x * sc1;
+        wm[1] = dm.y * m1;
     }
 };
 

@@ -43,16 +43,23 @@ def test_reference_decode_timing_runs(tmp_path):
 
 
 def test_cpu_gemv_timing_threads():
+    """At least min_steps steps of per_step GEMVs and at least `seconds`,
+    after the warm-up GEMVs; the steps that ran are reported."""
     import bench
-    r = bench.cpu_gemv_timing(seconds=0.2, max_steps=2, copies=2, threads=1)
+    r = bench.cpu_gemv_timing(seconds=0.05, min_steps=3, copies=2, threads=1, warmup=2, per_step=2)
     assert r["cores"] == 1 and r["value"] > 0 and "1 OpenMP threads" in r["sample"]
+    assert r["steps"] >= 3 and r["gemvs"] == 2 * r["steps"] and r["seconds"] >= 0.05
+    assert "after 2 warm-up GEMVs" in r["sample"]
     assert isinstance(bench.cpu_model(), str)
 
 
-def test_decode_context_synthetic_is_the_kv_fill():
-    """The default decode context: the same tokens and random K/V fill the
-    decode measurements always used."""
+def test_decode_context_synthetic_is_the_kv_fill(monkeypatch):
+    """The synthetic decode context (--decode-context synthetic): the same
+    tokens and random K/V fill as the decode measurements used before the
+    prefill context became the default."""
     import bench
+    assert bench.DECODE_CONTEXT == "prefill"
+    monkeypatch.setattr(bench, "DECODE_CONTEXT", "synthetic")
 
     class Dec:
         rows = 3
@@ -64,7 +71,6 @@ def test_decode_context_synthetic_is_the_kv_fill():
         def fill_kv(self, n):
             self.filled = n
 
-    assert bench.DECODE_CONTEXT == "synthetic"
     d = Dec()
     out = bench._build_context(d, 512, seed=1)
     assert d.reset_args == ([1, 8, 15], 0) and d.filled == 512
