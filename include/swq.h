@@ -332,7 +332,15 @@ enum {
      * fp32 copy fits the kernel's shared memory; others take the 16-bit
      * form).  0: activations rounded to 16-bit fixed point per 32-element
      * block and integer dot products (dp2a), the earlier form. */
-    SWQ_OPT_GEMV_FP32_ACT = 9
+    SWQ_OPT_GEMV_FP32_ACT = 9,
+    /* Single-row GEMVs whose sub-block dot products are computed exactly in
+     * integers on the tensor cores: quant values are exact small integers, x
+     * is held per 16- or 32-element sub-block as a 30-bit fixed-point number
+     * (four 8-bit limbs), the sub-block results are scaled and summed in
+     * fp32.  K a multiple of 256 up to 16384 (Q6_K: of 2048).  1 (default):
+     * Q6_K, where it is the faster form on B200; 2: Q4_K as well; 0: neither
+     * (the fp32 form of SWQ_OPT_GEMV_FP32_ACT). */
+    SWQ_OPT_GEMV_INT_MMA = 10
 };
 swq_status swq_set_option(int option, int value);
 int swq_get_option(int option);

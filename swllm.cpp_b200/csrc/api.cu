@@ -36,6 +36,7 @@ std::atomic<int> g_opt_gemv_smem_kb{0};
 std::atomic<int> g_opt_gemv_stage_kb{0};
 std::atomic<int> g_opt_gemv_ctas{0};
 std::atomic<int> g_opt_gemv_fp32{1};
+std::atomic<int> g_opt_gemv_imma{1};
 
 swq_status fail(swq_status s, const std::string& msg) {
     g_last_error = msg;
@@ -146,6 +147,7 @@ swq_status gemm_gemv_groups(int type, const void* W, const float* X, float* Y, i
         L.stage_kb = g_opt_gemv_stage_kb;
         L.ctas_per_sm = g_opt_gemv_ctas;
         L.xf = g_opt_gemv_fp32;
+        L.imma = g_opt_gemv_imma;
         cudaError_t e = swq::gemv_launch(L, s);
         if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
     }
@@ -221,6 +223,10 @@ swq_status swq_set_option(int option, int value) {
             if (value != 0 && value != 1) return fail(SWQ_ERR_BAD_ARG, "option value must be 0 or 1");
             g_opt_gemv_fp32 = value;
             return SWQ_OK;
+        case SWQ_OPT_GEMV_INT_MMA:
+            if (value < 0 || value > 2) return fail(SWQ_ERR_BAD_ARG, "option value must be 0, 1 or 2");
+            g_opt_gemv_imma = value;
+            return SWQ_OK;
         default:
             return fail(SWQ_ERR_BAD_ARG, "unknown option " + std::to_string(option));
     }
@@ -237,6 +243,7 @@ int swq_get_option(int option) {
         case SWQ_OPT_GEMV_STAGE_KB: return g_opt_gemv_stage_kb;
         case SWQ_OPT_GEMV_CTAS_PER_SM: return g_opt_gemv_ctas;
         case SWQ_OPT_GEMV_FP32_ACT: return g_opt_gemv_fp32;
+        case SWQ_OPT_GEMV_INT_MMA: return g_opt_gemv_imma;
         default: return -1;
     }
 }

@@ -34,6 +34,7 @@ struct GemvLaunch {
     int stage_kb;  // largest weight stage in KB (0: 96)
     int ctas_per_sm;  // 0: automatic
     int xf = 1;       // fp32 activations (else 16-bit fixed point)
+    int imma = 1;     // M = 1: exact integer dot products on the tensor cores (1: Q6_K, 2: Q4_K too)
     // activation prologue (ACT_*); ld = X row stride in elements (0: K, SWIGLU: 2K)
     int act = ACT_NONE;
     const float* R = nullptr;
@@ -45,6 +46,10 @@ struct GemvLaunch {
 
 // Fused dequant + GEMV for M <= 8 activation rows.
 cudaError_t gemv_launch(const GemvLaunch& L, cudaStream_t s);
+// The single-row form with integer tensor-core dot products (gemv_imma.cu):
+// whether it takes this launch, and the launch.
+bool gemv_imma_supported(const GemvLaunch& L);
+cudaError_t gemv_imma_launch(const GemvLaunch& L, cudaStream_t s);
 // Device status bit of an input a kernel skipped because it was misaligned
 // (DEV_BAD_ALIGN in the device code).
 constexpr unsigned kStatusBadAlign = 32u;

@@ -29,6 +29,7 @@ OPT_GEMV_SMEM_KB = 6
 OPT_GEMV_STAGE_KB = 7
 OPT_GEMV_CTAS_PER_SM = 8
 OPT_GEMV_FP32_ACT = 9
+OPT_GEMV_INT_MMA = 10
 
 GEMM_NOALLOC_MAX_X_ELEMS = 8388608  # SWQ_GEMM_NOALLOC_MAX_X_ELEMS
 

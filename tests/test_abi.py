@@ -124,6 +124,11 @@ def test_options():
     swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 0)
     assert swq.get_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER) == 0
     swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 1)
+    assert swq.get_option(swq.OPT_GEMV_FP32_ACT) == 1
+    assert swq.get_option(swq.OPT_GEMV_INT_MMA) == 1
+    for opt, bad in ((swq.OPT_GEMV_FP32_ACT, 2), (swq.OPT_GEMV_INT_MMA, 3), (swq.OPT_GEMV_INT_MMA, -1)):
+        with pytest.raises(swq.SwqError):
+            swq.set_option(opt, bad)
     with pytest.raises(swq.SwqError) as ei:
         swq.set_option(swq.OPT_GEMV_MAX_M, 9)
     assert ei.value.status is Status.BAD_ARG

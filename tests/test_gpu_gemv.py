@@ -293,3 +293,51 @@ def test_ring_options(cuda, oracle_mod, smem_kb, stage_kb, ctas, fmt, N, K):
         swq.set_option(swq.OPT_GEMV_STAGE_KB, 0)
         swq.set_option(swq.OPT_GEMV_CTAS_PER_SM, 0)
     assert rel_l2(got, oracle_mod.gemm(t, blocks, X, 1, N, K)) <= REL_L2_TOL
+
+
+@pytest.mark.parametrize("fp32,int_mma", [(1, 0), (1, 1), (1, 2), (0, 0)],
+                         ids=["fp32", "fp32+intmma-q6k", "fp32+intmma-all", "int16"])
+@pytest.mark.parametrize("fmt,N,K", [("Q4_K", 300, 4096), ("Q6_K", 333, 4096), ("Q6_K", 64, 14336),
+                                     ("Q4_K", 37, 1024), ("Q4_K", 1, 256), ("Q6_K", 17, 2048)])
+def test_gemv_forms(cuda, oracle_mod, fp32, int_mma, fmt, N, K):
+    """Every single-row form against the oracle: fp32 activations with and
+    without the integer tensor-core dot products, and 16-bit fixed-point
+    activations; rows not a multiple of the 16-row tile, K below and above a
+    chunk, K that the tensor-core form does not take (Q6_K 1024 is not a
+    multiple of 2048: the fp32 form serves it)."""
+    t = synth.IDS[fmt]
+    blocks = synth.random_blocks(t, N, K, seed=900 + N)
+    X = synth.random_activations(1, K, seed=901)
+    swq.set_option(swq.OPT_GEMV_FP32_ACT, fp32)
+    swq.set_option(swq.OPT_GEMV_INT_MMA, int_mma)
+    try:
+        got = _gemm_gpu(cuda, t, blocks, X, N, K)
+    finally:
+        swq.set_option(swq.OPT_GEMV_FP32_ACT, 1)
+        swq.set_option(swq.OPT_GEMV_INT_MMA, 1)
+    want = oracle_mod.gemm(t, blocks, X, 1, N, K)
+    tol = 1e-5 if fp32 else REL_L2_TOL  # fp32 forms: rounding of fp32 sums only
+    assert rel_l2(got, want) <= tol
+
+
+@pytest.mark.parametrize("int_mma", [1, 2])
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K"])
+def test_int_mma_dynamic_range(cuda, oracle_mod, int_mma, fmt):
+    """Activations over twelve decades (each 16/32-element part gets its own
+    fixed-point scale), a part of zeros and a part of subnormals: the integer
+    tensor-core form stays at fp32 accuracy."""
+    t = synth.IDS[fmt]
+    N, K = 96, 4096
+    blocks = synth.random_blocks(t, N, K, seed=950)
+    rng = np.random.default_rng(951)
+    x = (rng.standard_normal(K) * 10.0 ** rng.uniform(-6, 6, K)).astype(np.float32)
+    x[64:96] = 0.0
+    x[128:144] = np.float32(1e-40)
+    X = x.reshape(1, K)
+    swq.set_option(swq.OPT_GEMV_INT_MMA, int_mma)
+    try:
+        got = _gemm_gpu(cuda, t, blocks, X, N, K)
+    finally:
+        swq.set_option(swq.OPT_GEMV_INT_MMA, 1)
+    want = oracle_mod.gemm(t, blocks, X, 1, N, K)
+    assert rel_l2(got, want) <= 1e-5
