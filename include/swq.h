@@ -186,6 +186,25 @@ swq_status swq_grouped_gemm(int ggml_type, const void* const* W_experts, const i
                             const float* X_sorted, float* Y, int n_experts, int total_rows,
                             int N, int K, swq_stream_t stream);
 
+/* ---- Grouped expert matmul for a known expected load ---------------------
+ *
+ * No counterpart in the reference (no MoE path).  swq_grouped_gemm /
+ * swq_grouped_gemv with the kernel picked from mean_rows, the expected rows
+ * per expert (for a MoE layer T * k / n_experts, known on the host before the
+ * routing runs on the device), where total_rows only bounds the rows (e.g. the
+ * capacity that swq_ep_received reports):
+ *   mean_rows <= 4: the grouped GEMV (expert matrices 16-byte aligned), each
+ *     expert's rows taken in passes of 4, 2 or 1 by its own row count, read
+ *     on the device;
+ *   else: the tensor-core grouped GEMM with its token tile from mean_rows;
+ *     rows of X at or past expert_offsets[n_experts] are not read.
+ * expert_offsets must be non-decreasing (as swq_moe_sort and swq_ep_received
+ * give them).  A row's result does not depend on the other rows.
+ * n_experts <= 4095. */
+swq_status swq_grouped_matmul(int ggml_type, const void* const* W_experts, const int* expert_offsets,
+                              const float* X_sorted, float* Y, int n_experts, int total_rows, int N, int K,
+                              int mean_rows, swq_stream_t stream);
+
 /* ---- GEMM with a fused activation prologue --------------------------------
  *
  * No counterpart in the reference: its decode step runs RMSNorm
@@ -371,13 +390,104 @@ swq_status swq_check(swq_stream_t stream);
  *      A wait that gives up (a peer that never arrives) records
  *      SWQ_ERR_TIMEOUT for swq_check.
  *   4. swq_allreduce_destroy once no call is in flight on any rank.
+ * After a timeout the ranks' epoch counters disagree (a rank that skipped a
+ * call is one behind); swq_allreduce_reset brings the group back:
+ *   a. every rank: wait until none of its sums is in flight (swq_check on the
+ *      streams that ran them), then a host barrier over the group;
+ *   b. every rank: swq_allreduce_reset(ar, stream) -- zeroes this rank's own
+ *      flag words and epoch counters and synchronizes `stream`;
+ *   c. a second host barrier; the next matched call then sums exactly.
+ * Skipping barrier (c) lets a fast rank read a slow rank's stale flags.
  * At most 8 ranks. */
 #define SWQ_ALLREDUCE_HANDLE_BYTES 64
 typedef struct swq_allreduce swq_allreduce;
 swq_status swq_allreduce_create(size_t max_elems, int rank, int world, swq_allreduce** out, void* handle_out);
 swq_status swq_allreduce_open(swq_allreduce* ar, const void* handles);
 swq_status swq_allreduce_sum(swq_allreduce* ar, float* data, size_t n, swq_stream_t stream);
+swq_status swq_allreduce_reset(swq_allreduce* ar, swq_stream_t stream);
 swq_status swq_allreduce_destroy(swq_allreduce* ar);
+
+/* ---- MoE routing, token sort and combine ---------------------------------
+ *
+ * No counterpart in the reference: it has no MoE forward (its FFN is dense,
+ * src/model.h:520-528; the GGUF expert tensor names appear only at
+ * src/hf_loader.h:474-493).  These run the routing around the grouped expert
+ * GEMMs on the device, with no count going back to the host (so a whole MoE
+ * layer can be captured in a CUDA graph).  All buffers are device memory.
+ *
+ * swq_moe_router: logits[t][e] = router_w[e] . X[t] (fp32, router_w E x H,
+ *   X T x H), then per token the k largest logits in descending order (ties:
+ *   the lower expert id first; NaN ranks as -inf) into topk_ids [T][k], and
+ *   topk_w [T][k] = softmax over those k logits (exp(l_j - l_0) / sum_i
+ *   exp(l_i - l_0), the sum left to right).  logits [T][E] is written too.
+ *   E <= SWQ_MOE_MAX_EXPERTS, k <= min(E, SWQ_MOE_MAX_TOPK); one token row
+ *   (H floats) must fit the shared memory of a CTA.
+ * swq_moe_sort: the P = T*k pairs p = t*k + j of topk_ids, stably sorted by
+ *   expert: expert_offsets [n_experts + 1] (expert e's rows are
+ *   expert_offsets[e] .. expert_offsets[e+1]-1), sorted_pairs [P] (the pair of
+ *   each row) and pair_rows [P] (the row of each pair).  A pair whose id is
+ *   outside [0, n_experts) gets row -1 and no row, and swq_check then returns
+ *   SWQ_ERR_BAD_ARG.
+ * swq_moe_gather: X_sorted[r] = X[sorted_pairs[r] / k] for the rows
+ *   r < expert_offsets[n_experts] (H floats each): the input of
+ *   swq_grouped_gemm / swq_grouped_gemv.
+ * swq_moe_combine: Y[t] = (accumulate ? Y[t] : 0) + sum_j topk_w[t][j] *
+ *   Y_sorted[pair_rows[t*k + j]], one fused multiply-add per slot in the
+ *   order j = 0 .. k-1 (rows -1 add nothing). */
+#define SWQ_MOE_MAX_EXPERTS 1024
+#define SWQ_MOE_MAX_TOPK 32
+swq_status swq_moe_router(const float* router_w, const float* X, int T, int E, int H, int k, float* logits,
+                          int* topk_ids, float* topk_w, swq_stream_t stream);
+swq_status swq_moe_sort(const int* topk_ids, int P, int n_experts, int* expert_offsets, int* sorted_pairs,
+                        int* pair_rows, swq_stream_t stream);
+swq_status swq_moe_gather(const float* X, const int* sorted_pairs, const int* expert_offsets, int n_experts, int P,
+                          int k, int H, float* X_sorted, swq_stream_t stream);
+swq_status swq_moe_combine(const float* Y_sorted, const int* pair_rows, const float* topk_w, int T, int k, int H,
+                           float* Y, int accumulate, swq_stream_t stream);
+
+/* ---- Expert-parallel dispatch and combine over peer memory ---------------
+ *
+ * No counterpart in the reference (see above).  The experts of a MoE layer
+ * are sharded over the `world` GPUs of a group (one process per GPU; rank r
+ * owns experts r*E/world .. (r+1)*E/world - 1).  Each rank's token rows
+ * travel to the ranks that own their experts by peer stores over NVLink
+ * (CUDA IPC), with the per-expert counts exchanged on the device, so nothing
+ * returns to the host; every wait is bounded (1 s) and records
+ * SWQ_ERR_TIMEOUT for swq_check.
+ *   1. swq_ep_create on every rank (device current): at most max_tokens tokens
+ *      per call, top_k slots each, n_experts (a multiple of world), hidden H.
+ *      handle_out receives SWQ_EP_HANDLE_BYTES bytes.  Device memory:
+ *      (world + 1) * max_tokens * top_k rows of H floats, plus small tables.
+ *   2. Exchange the handles, then swq_ep_open with all of them in rank order.
+ *   3. Per MoE layer, on every rank, in the same order:
+ *      swq_ep_dispatch(X [T][H], topk_ids [T][k] global expert ids, T);
+ *      swq_ep_received gives the rows this rank received (X_recv, capacity
+ *      rows of H floats) and their device expert offsets (E/world + 1 ints,
+ *      this rank's experts in order; rows beyond the last offset are
+ *      unused): the input of swq_grouped_gemm / swq_grouped_gemv with
+ *      total_rows = capacity;
+ *      swq_ep_combine(Y_recv, topk_w, Y): Y_recv holds the expert outputs of
+ *      the received rows (capacity x H, same row order); Y [T][H] receives
+ *      (accumulate ? Y : 0) + sum_j topk_w[t][j] * output of pair (t, j), one
+ *      fused multiply-add per slot in the order j = 0 .. k-1.
+ *   4. After a timeout: every rank waits until none of its calls is in
+ *      flight, meets the others at a host barrier, calls swq_ep_reset, and
+ *      meets them again (as for swq_allreduce_reset).
+ *   5. swq_ep_destroy once no call is in flight on any rank.
+ * With world = 1 the same calls run on one GPU without IPC peers.  At most
+ * SWQ_EP_MAX_RANKS ranks. */
+#define SWQ_EP_MAX_RANKS 8
+#define SWQ_EP_HANDLE_BYTES 64
+typedef struct swq_ep swq_ep;
+swq_status swq_ep_create(int max_tokens, int top_k, int n_experts, int hidden, int rank, int world, swq_ep** out,
+                         void* handle_out);
+swq_status swq_ep_open(swq_ep* ep, const void* handles);
+swq_status swq_ep_dispatch(swq_ep* ep, const float* X, const int* topk_ids, int T, swq_stream_t stream);
+swq_status swq_ep_received(const swq_ep* ep, float** X_recv, const int** expert_offsets, int* capacity);
+swq_status swq_ep_combine(swq_ep* ep, const float* Y_recv, const float* topk_w, float* Y, int accumulate,
+                          swq_stream_t stream);
+swq_status swq_ep_reset(swq_ep* ep, swq_stream_t stream);
+swq_status swq_ep_destroy(swq_ep* ep);
 
 /* ---- Host-buffer entry point (the reference's calling convention) --------
  *

@@ -90,6 +90,12 @@ def oracle_lib() -> ctypes.CDLL:
         lib.oracle_q3k_scales.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         lib.oracle_get_scale_min_k4.argtypes = [ctypes.c_int, ctypes.c_void_p,
                                                 ctypes.c_void_p, ctypes.c_void_p]
+        vp, i32 = ctypes.c_void_p, ctypes.c_int
+        lib.oracle_moe_router_logits.argtypes = [vp, vp, i32, i32, i32, vp]
+        lib.oracle_moe_topk_softmax.argtypes = [vp, i32, i32, i32, vp, vp]
+        lib.oracle_moe_sort.restype = ctypes.c_int
+        lib.oracle_moe_sort.argtypes = [vp, i32, i32, vp, vp, vp]
+        lib.oracle_moe_combine.argtypes = [vp, vp, vp, i32, i32, i32, vp, i32]
         _oracle = lib
     return _oracle
 
@@ -227,3 +233,72 @@ def host_cores() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:  # pragma: no cover
         return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------- MoE routing
+# The reference has no MoE forward; moe_oracle.c states the routing as libswq
+# defines it (parity for routing is unpinned by the reference).
+
+def moe_router_logits(W: np.ndarray, X: np.ndarray) -> np.ndarray:
+    """logits [T, E] in float64 of the fp32 router W [E, H] on X [T, H]."""
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    T, H = X.shape
+    E = W.shape[0]
+    out = np.empty((T, E), dtype=np.float64)
+    oracle_lib().oracle_moe_router_logits(_ptr(W), _ptr(X), T, E, H, _ptr(out))
+    return out
+
+
+def moe_topk_softmax(logits: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """(ids [T, k] int32, weights [T, k] float32) from fp32 logits [T, E]."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    T, E = logits.shape
+    ids = np.empty((T, k), dtype=np.int32)
+    w = np.empty((T, k), dtype=np.float32)
+    oracle_lib().oracle_moe_topk_softmax(_ptr(logits), T, E, k, _ptr(ids), _ptr(w))
+    return ids, w
+
+
+def moe_sort(ids: np.ndarray, n_experts: int) -> tuple[np.ndarray, np.ndarray, np.ndarray, int]:
+    """(offsets [E+1], sorted [rows], prow [P], pairs left out) of the pairs ids (any shape)."""
+    flat = np.ascontiguousarray(ids, dtype=np.int32).reshape(-1)
+    P = flat.size
+    offsets = np.empty(n_experts + 1, dtype=np.int32)
+    sorted_ = np.full(max(P, 1), -1, dtype=np.int32)
+    prow = np.empty(max(P, 1), dtype=np.int32)
+    bad = oracle_lib().oracle_moe_sort(_ptr(flat), P, n_experts, _ptr(offsets), _ptr(sorted_), _ptr(prow))
+    return offsets, sorted_[:offsets[-1]], prow[:P], int(bad)
+
+
+def moe_combine(Ys: np.ndarray, prow: np.ndarray, w: np.ndarray, T: int, k: int, H: int,
+                Y0: np.ndarray | None = None) -> np.ndarray:
+    """Y [T, H] = (Y0 or 0) + sum_j w[t, j] * Ys[prow[t*k + j]] with one fmaf per slot."""
+    Ys = np.ascontiguousarray(Ys, dtype=np.float32)
+    prow = np.ascontiguousarray(prow, dtype=np.int32).reshape(-1)
+    w = np.ascontiguousarray(w, dtype=np.float32).reshape(-1)
+    Y = np.zeros((T, H), dtype=np.float32) if Y0 is None else np.array(Y0, dtype=np.float32, copy=True)
+    oracle_lib().oracle_moe_combine(_ptr(Ys), _ptr(prow), _ptr(w), T, k, H, _ptr(Y), 0 if Y0 is None else 1)
+    return Y
+
+
+def ep_layout(ids_per_rank: list, n_experts: int, world: int) -> list[dict]:
+    """Expert-parallel placement of every rank's pairs (ids_per_rank[s] is
+    rank s's [T_s, k] global expert ids): for each rank d, its local expert
+    offsets `loff` and the (source, slot) of each received row, where slot is
+    the pair's position in its source's stable sort by expert.  Rows of a
+    local expert come from source 0, 1, ... in turn, each source's pairs in
+    pair order."""
+    el = n_experts // world
+    sorts = [moe_sort(ids, n_experts) for ids in ids_per_rank]
+    out = []
+    for d in range(world):
+        loff = [0]
+        tags = []
+        for le in range(el):
+            e = d * el + le
+            for s, (offs, _, _, _) in enumerate(sorts):
+                tags.extend((s, i) for i in range(offs[e], offs[e + 1]))
+            loff.append(len(tags))
+        out.append({"loff": np.array(loff, dtype=np.int32), "tags": tags})
+    return out

@@ -17,6 +17,7 @@
 
 #include "../../include/swq.h"
 #include "allreduce.h"
+#include "moe.h"
 #include "decode.h"
 #include "prefill.h"
 #include "qkv_extras.h"
@@ -441,6 +442,36 @@ swq_status swq_grouped_gemv(int type, const void* const* W_experts, const int* e
     return SWQ_OK;
 }
 
+swq_status swq_grouped_matmul(int type, const void* const* W_experts, const int* expert_offsets, const float* X_sorted,
+                              float* Y, int n_experts, int total_rows, int N, int K, int mean_rows,
+                              swq_stream_t stream) {
+    TypeInfo ti;
+    if (!type_info(type, &ti)) return fail(SWQ_ERR_BAD_TYPE, "type " + std::to_string(type) + " is not on this path");
+    if (n_experts < 0 || total_rows < 0 || N < 0 || K < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative size");
+    if (K % ti.qk != 0)
+        return fail(SWQ_ERR_BAD_SHAPE, "K=" + std::to_string(K) + " is not a multiple of " + std::to_string(ti.qk));
+    if (n_experts > 4095) return fail(SWQ_ERR_BAD_SHAPE, "n_experts above 4095");
+    if (n_experts == 0 || total_rows == 0 || N == 0) return SWQ_OK;
+    if (!W_experts || !expert_offsets || !X_sorted || !Y) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (K == 0) {
+        cudaError_t e = cudaMemsetAsync(Y, 0, sizeof(float) * static_cast<size_t>(total_rows) * N, s);
+        return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
+    }
+    cudaError_t e;
+    if (mean_rows <= 4)
+        e = swq::grouped_gemv_launch(type, W_experts, expert_offsets, X_sorted, Y, n_experts, total_rows, N, K,
+                                     g_opt_q2k_refcpu, dev.smem_per_block_optin, s, true);
+    else
+        e = swq::gemm_tc_grouped_launch(type, W_experts, expert_offsets, X_sorted, Y, n_experts, total_rows, N, K,
+                                        g_opt_q2k_refcpu, dev.num_sms, s, mean_rows, expert_offsets + n_experts);
+    if (e != cudaSuccess) return cuda_fail(e, "grouped matmul launch");
+    return SWQ_OK;
+}
+
 // ---- decode step -------------------------------------------------------------
 
 static swq_status launch_status(cudaError_t e, const char* what) {
@@ -668,12 +699,20 @@ swq_status swq_check(swq_stream_t stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
-    unsigned a = 0, b = 0, c = 0, d = 0;
+    unsigned a = 0, b = 0, c = 0, d = 0, m = 0;
     if ((e = swq::status_fetch_gemv(&a, s)) != cudaSuccess ||
         (e = swq::status_fetch_dequant(&b, s)) != cudaSuccess ||
         (e = swq::status_fetch_gemm_tc(&c, s)) != cudaSuccess ||
-        (e = swq::status_fetch_allreduce(&d, s)) != cudaSuccess)
+        (e = swq::status_fetch_allreduce(&d, s)) != cudaSuccess ||
+        (e = swq::status_fetch_moe(&m, s)) != cudaSuccess)
         return cuda_fail(e, "status fetch");
+    if (m & swq::kStatusBadId) {
+        char buf[128];
+        std::snprintf(buf, sizeof(buf), "an expert id outside [0, n_experts) was left out of the MoE sort "
+                                        "(status moe=%#x)", m);
+        return fail(SWQ_ERR_BAD_ARG, buf);
+    }
+    d |= m;
     if ((a | b | c | d) & swq::kStatusBadAlign) {
         char buf[160];
         std::snprintf(buf, sizeof(buf),
@@ -776,6 +815,19 @@ swq_status swq_allreduce_sum(swq_allreduce* ar, float* data, size_t n, swq_strea
                          "all-reduce launch");
 }
 
+swq_status swq_allreduce_reset(swq_allreduce* ar, swq_stream_t stream) {
+    if (!ar) return fail(SWQ_ERR_NULL_PTR, "null all-reduce");
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != ar->device) return fail(SWQ_ERR_BAD_ARG, "current device is not the all-reduce's device");
+    // Only this rank's own flag words and epoch counters: every rank resets its
+    // own, so after the caller's second barrier all ranks count from epoch 0.
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(ar->own, 0, swq::ar_header_bytes(), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "all-reduce reset");
+}
+
 swq_status swq_allreduce_destroy(swq_allreduce* ar) {
     if (!ar) return SWQ_OK;
     int cur = -1;
@@ -787,6 +839,209 @@ swq_status swq_allreduce_destroy(swq_allreduce* ar) {
     if (ar->own) cudaFree(ar->own);
     if (cur >= 0) cudaSetDevice(cur);
     delete ar;
+    return SWQ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// MoE routing, sort and combine; expert-parallel dispatch over peer memory.
+// ---------------------------------------------------------------------------
+
+static swq_status moe_shape_check(int T, int E, int k) {
+    if (T < 0 || E < 1 || k < 1) return fail(SWQ_ERR_BAD_SHAPE, "need T >= 0, n_experts >= 1, k >= 1");
+    if (E > SWQ_MOE_MAX_EXPERTS) return fail(SWQ_ERR_BAD_SHAPE, "more than SWQ_MOE_MAX_EXPERTS experts");
+    if (k > SWQ_MOE_MAX_TOPK || k > E) return fail(SWQ_ERR_BAD_SHAPE, "k above SWQ_MOE_MAX_TOPK or n_experts");
+    return SWQ_OK;
+}
+
+swq_status swq_moe_router(const float* router_w, const float* X, int T, int E, int H, int k, float* logits,
+                          int* topk_ids, float* topk_w, swq_stream_t stream) {
+    swq_status st = moe_shape_check(T, E, k);
+    if (st != SWQ_OK) return st;
+    if (H < 1) return fail(SWQ_ERR_BAD_SHAPE, "hidden size must be positive");
+    if (T == 0) return SWQ_OK;
+    if (!router_w || !X || !logits || !topk_ids || !topk_w) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    swq::DeviceInfo dev;
+    if ((st = current_device(&dev)) != SWQ_OK) return st;
+    if (static_cast<size_t>(H) * sizeof(float) > static_cast<size_t>(dev.smem_per_block_optin))
+        return fail(SWQ_ERR_BAD_SHAPE, "hidden size too large for one token row in shared memory");
+    return launch_status(swq::moe_router_launch(router_w, X, logits, T, E, H, k, topk_ids, topk_w,
+                                                dev.smem_per_block_optin, reinterpret_cast<cudaStream_t>(stream)),
+                         "MoE router launch");
+}
+
+swq_status swq_moe_sort(const int* topk_ids, int P, int n_experts, int* expert_offsets, int* sorted_pairs,
+                        int* pair_rows, swq_stream_t stream) {
+    if (P < 0 || n_experts < 1) return fail(SWQ_ERR_BAD_SHAPE, "need P >= 0 and n_experts >= 1");
+    if (n_experts > SWQ_MOE_MAX_EXPERTS) return fail(SWQ_ERR_BAD_SHAPE, "more than SWQ_MOE_MAX_EXPERTS experts");
+    if (!expert_offsets || (P > 0 && (!topk_ids || !sorted_pairs || !pair_rows)))
+        return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::moe_sort_launch(topk_ids, P, n_experts, expert_offsets, sorted_pairs, pair_rows,
+                                              reinterpret_cast<cudaStream_t>(stream)),
+                         "MoE sort launch");
+}
+
+swq_status swq_moe_gather(const float* X, const int* sorted_pairs, const int* expert_offsets, int n_experts, int P,
+                          int k, int H, float* X_sorted, swq_stream_t stream) {
+    if (P < 0 || n_experts < 1 || k < 1 || H < 1) return fail(SWQ_ERR_BAD_SHAPE, "bad size");
+    if (P == 0) return SWQ_OK;
+    if (!X || !sorted_pairs || !expert_offsets || !X_sorted) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::moe_gather_launch(X, sorted_pairs, expert_offsets, n_experts, P, k, H, X_sorted,
+                                                dev.num_sms, reinterpret_cast<cudaStream_t>(stream)),
+                         "MoE gather launch");
+}
+
+swq_status swq_moe_combine(const float* Y_sorted, const int* pair_rows, const float* topk_w, int T, int k, int H,
+                           float* Y, int accumulate, swq_stream_t stream) {
+    if (T < 0 || k < 1 || H < 1) return fail(SWQ_ERR_BAD_SHAPE, "bad size");
+    if (T == 0) return SWQ_OK;
+    if (!Y_sorted || !pair_rows || !topk_w || !Y) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::moe_combine_launch(Y_sorted, pair_rows, topk_w, T, k, H, Y, accumulate ? 1 : 0,
+                                                 dev.num_sms, reinterpret_cast<cudaStream_t>(stream)),
+                         "MoE combine launch");
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == SWQ_EP_HANDLE_BYTES, "IPC handle size");
+
+struct swq_ep {
+    int device = -1;
+    int rank = 0;
+    swq::EpShape shape{};
+    void* own = nullptr;
+    void* peer[SWQ_EP_MAX_RANKS] = {};
+    swq::EpView bufs[SWQ_EP_MAX_RANKS] = {};
+    bool opened = false;
+};
+
+swq_status swq_ep_create(int max_tokens, int top_k, int n_experts, int hidden, int rank, int world, swq_ep** out,
+                         void* handle_out) {
+    if (!out || !handle_out) return fail(SWQ_ERR_NULL_PTR, "null output pointer");
+    *out = nullptr;
+    if (world < 1 || world > SWQ_EP_MAX_RANKS || rank < 0 || rank >= world)
+        return fail(SWQ_ERR_BAD_ARG, "rank/world outside 0 <= rank < world <= SWQ_EP_MAX_RANKS");
+    swq_status st = moe_shape_check(max_tokens, n_experts, top_k);
+    if (st != SWQ_OK) return st;
+    if (max_tokens < 1 || hidden < 1) return fail(SWQ_ERR_BAD_SHAPE, "max_tokens and hidden must be positive");
+    if (n_experts % world) return fail(SWQ_ERR_BAD_SHAPE, "n_experts must split evenly over the ranks");
+    if (static_cast<int64_t>(max_tokens) * top_k * world > (1 << 30))
+        return fail(SWQ_ERR_BAD_SHAPE, "max_tokens * top_k * world above 2^30 rows");
+    swq::DeviceInfo dev;
+    if ((st = current_device(&dev)) != SWQ_OK) return st;
+    auto* ep = new swq_ep();
+    ep->device = dev.device;
+    ep->rank = rank;
+    ep->shape = swq::EpShape{max_tokens, top_k, n_experts, hidden, world};
+    const size_t bytes = swq::ep_buffer_bytes(ep->shape);
+    cudaError_t e = cudaMalloc(&ep->own, bytes);
+    if (e == cudaSuccess) e = cudaMemset(ep->own, 0, swq::ep_header_bytes());  // flags, epoch, meta start at 0
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, ep->own);
+    if (e != cudaSuccess) {
+        if (ep->own) cudaFree(ep->own);
+        delete ep;
+        return cuda_fail(e, "expert-parallel buffer");
+    }
+    std::memcpy(handle_out, &h, sizeof(h));
+    ep->bufs[rank] = swq::ep_view(ep->own, ep->shape);
+    if (world == 1) ep->opened = true;
+    *out = ep;
+    return SWQ_OK;
+}
+
+swq_status swq_ep_open(swq_ep* ep, const void* handles) {
+    if (!ep || !handles) return fail(SWQ_ERR_NULL_PTR, "null expert-parallel object or handles");
+    if (ep->opened && ep->shape.world > 1) return fail(SWQ_ERR_BAD_ARG, "peers already opened");
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != ep->device) return fail(SWQ_ERR_BAD_ARG, "current device is not the expert-parallel object's device");
+    for (int r = 0; r < ep->shape.world; ++r) {
+        if (r == ep->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + static_cast<size_t>(r) * SWQ_EP_HANDLE_BYTES,
+                    sizeof(h));
+        cudaError_t e = cudaIpcOpenMemHandle(&ep->peer[r], h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; ++q)
+                if (ep->peer[q]) {
+                    cudaIpcCloseMemHandle(ep->peer[q]);
+                    ep->peer[q] = nullptr;
+                }
+            return cuda_fail(e, "cudaIpcOpenMemHandle");
+        }
+        ep->bufs[r] = swq::ep_view(ep->peer[r], ep->shape);
+    }
+    ep->opened = true;
+    return SWQ_OK;
+}
+
+static swq_status ep_ready(const swq_ep* ep) {
+    if (!ep) return fail(SWQ_ERR_NULL_PTR, "null expert-parallel object");
+    if (!ep->opened) return fail(SWQ_ERR_BAD_ARG, "swq_ep_open has not run");
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != ep->device) return fail(SWQ_ERR_BAD_ARG, "current device is not the expert-parallel object's device");
+    return SWQ_OK;
+}
+
+swq_status swq_ep_dispatch(swq_ep* ep, const float* X, const int* topk_ids, int T, swq_stream_t stream) {
+    swq_status st = ep_ready(ep);
+    if (st != SWQ_OK) return st;
+    if (T < 0 || T > ep->shape.max_tokens) return fail(SWQ_ERR_BAD_SHAPE, "T outside 0 .. max_tokens");
+    if (T > 0 && (!X || !topk_ids)) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    return launch_status(swq::ep_dispatch_launch(ep->bufs, ep->rank, ep->shape, topk_ids, X, T,
+                                                 reinterpret_cast<cudaStream_t>(stream)),
+                         "expert-parallel dispatch launch");
+}
+
+swq_status swq_ep_received(const swq_ep* ep, float** X_recv, const int** expert_offsets, int* capacity) {
+    if (!ep || !X_recv || !expert_offsets || !capacity) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    *X_recv = ep->bufs[ep->rank].rbuf;
+    *expert_offsets = ep->bufs[ep->rank].loff;
+    *capacity = ep->shape.max_tokens * ep->shape.k * ep->shape.world;
+    return SWQ_OK;
+}
+
+swq_status swq_ep_combine(swq_ep* ep, const float* Y_recv, const float* topk_w, float* Y, int accumulate,
+                          swq_stream_t stream) {
+    swq_status st = ep_ready(ep);
+    if (st != SWQ_OK) return st;
+    if (!Y_recv || !topk_w || !Y) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    return launch_status(swq::ep_combine_launch(ep->bufs, ep->rank, ep->shape, Y_recv, topk_w, Y,
+                                                accumulate ? 1 : 0, reinterpret_cast<cudaStream_t>(stream)),
+                         "expert-parallel combine launch");
+}
+
+swq_status swq_ep_reset(swq_ep* ep, swq_stream_t stream) {
+    if (!ep) return fail(SWQ_ERR_NULL_PTR, "null expert-parallel object");
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != ep->device) return fail(SWQ_ERR_BAD_ARG, "current device is not the expert-parallel object's device");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(ep->own, 0, swq::ep_header_bytes(), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "expert-parallel reset");
+}
+
+swq_status swq_ep_destroy(swq_ep* ep) {
+    if (!ep) return SWQ_OK;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    cudaSetDevice(ep->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < ep->shape.world; ++r)
+        if (ep->peer[r]) cudaIpcCloseMemHandle(ep->peer[r]);
+    if (ep->own) cudaFree(ep->own);
+    if (cur >= 0) cudaSetDevice(cur);
+    delete ep;
     return SWQ_OK;
 }
 

@@ -1055,7 +1055,8 @@ __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__
     // split-K tile counters of the GEMM that follows start at zero
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncount; i += gridDim.x * blockDim.x) tcount[i] = 0u;
     const int ld = act.ld > 0 ? act.ld : K;
-    for (int row = blockIdx.x; row < M; row += gridDim.x) {
+    const int Mr = act.rows_dev ? min(M, max(0, *act.rows_dev)) : M;
+    for (int row = blockIdx.x; row < Mr; row += gridDim.x) {
         const float* xr = X + static_cast<int64_t>(row) * ld;
         const float* rr = act.R ? act.R + static_cast<int64_t>(row) * K : nullptr;
         float* so = act.sum_out ? act.sum_out + static_cast<int64_t>(row) * K : nullptr;
@@ -1324,8 +1325,8 @@ static cudaError_t launch_tc_bn(const void* W, const __half* Xh, const float* rs
 // Grouped: the token tile follows the mean rows per expert.
 template <int T>
 static cudaError_t launch_tc_grouped(const ExpertSet& ex, const __half* Xh, const float* rs, float* Y, int rows,
-                                     int N, int K, int num_sms, cudaStream_t s) {
-    const int mean = (rows + ex.n_experts - 1) / ex.n_experts;
+                                     int N, int K, int num_sms, cudaStream_t s, int mean_rows) {
+    const int mean = mean_rows > 0 ? mean_rows : (rows + ex.n_experts - 1) / ex.n_experts;
     if (mean <= 64) return launch_tc<T, 64, false, true>(nullptr, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
     if (mean <= 128) return launch_tc<T, 128, false, true>(nullptr, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
     return launch_tc<T, 256, false, true>(nullptr, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
@@ -1472,7 +1473,8 @@ cudaError_t gemm_tc_launch_ws(int type, const void* W, const float* X, float* Y,
 }
 
 cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
-                                   int n_experts, int rows, int N, int K, int refcpu, int num_sms, cudaStream_t s) {
+                                   int n_experts, int rows, int N, int K, int refcpu, int num_sms, cudaStream_t s,
+                                   int mean_rows, const int* live_rows) {
     if (tc::tc_fmt(type).qk == 0 || K % 32 != 0 || encode_fn2() == nullptr) return cudaErrorNotSupported;
     const int64_t n = static_cast<int64_t>(rows) * K;
     cudaMemPool_t pool = nullptr;
@@ -1483,18 +1485,20 @@ cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int
     if (e != cudaSuccess) return e;
     float* rs = reinterpret_cast<float*>(Xh + n);
     const int q2ref = (type == Q2_K && refcpu) ? 1 : 0;
-    e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, rows, K, num_sms, s, nullptr, 0, ActArgs{}, q2ref)
-                            : launch_x_to_f16<false>(X, Xh, rs, rows, K, num_sms, s, nullptr, 0, ActArgs{}, q2ref);
+    ActArgs act;
+    act.rows_dev = live_rows;
+    e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, rows, K, num_sms, s, nullptr, 0, act, q2ref)
+                            : launch_x_to_f16<false>(X, Xh, rs, rows, K, num_sms, s, nullptr, 0, act, q2ref);
     if (e == cudaSuccess) {
         const ExpertSet ex{reinterpret_cast<const uint8_t* const*>(wptrs), offsets, n_experts};
         switch (type) {
-            case Q4_0: e = launch_tc_grouped<Q4_0>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
-            case Q8_0: e = launch_tc_grouped<Q8_0>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
-            case Q2_K: e = launch_tc_grouped<Q2_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
-            case Q3_K: e = launch_tc_grouped<Q3_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
-            case Q4_K: e = launch_tc_grouped<Q4_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
-            case Q5_K: e = launch_tc_grouped<Q5_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
-            case Q6_K: e = launch_tc_grouped<Q6_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s); break;
+            case Q4_0: e = launch_tc_grouped<Q4_0>(ex, Xh, rs, Y, rows, N, K, num_sms, s, mean_rows); break;
+            case Q8_0: e = launch_tc_grouped<Q8_0>(ex, Xh, rs, Y, rows, N, K, num_sms, s, mean_rows); break;
+            case Q2_K: e = launch_tc_grouped<Q2_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s, mean_rows); break;
+            case Q3_K: e = launch_tc_grouped<Q3_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s, mean_rows); break;
+            case Q4_K: e = launch_tc_grouped<Q4_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s, mean_rows); break;
+            case Q5_K: e = launch_tc_grouped<Q5_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s, mean_rows); break;
+            case Q6_K: e = launch_tc_grouped<Q6_K>(ex, Xh, rs, Y, rows, N, K, num_sms, s, mean_rows); break;
             default: e = cudaErrorInvalidValue;
         }
     }

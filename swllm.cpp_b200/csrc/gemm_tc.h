@@ -17,6 +17,7 @@ struct ActArgs {
     float eps = 0.f;
     float* sum_out = nullptr;
     int ld = 0;  // X row stride in elements (0: K)
+    const int* rows_dev = nullptr;  // device row count: rows at or past it are not converted
 };
 
 // True when the tcgen05 GEMM serves this problem.
@@ -37,8 +38,11 @@ cudaError_t gemm_tc_launch_ws(int type, const void* W, const float* X, float* Y,
 // (rows x K) by the GGUF matrix wptrs[e] (N x K) into the same rows of Y.
 // wptrs and offsets are device arrays of n_experts and n_experts + 1 entries.
 // refcpu: Q2_K in the reference CPU routine's activation order.
+// mean_rows > 0 picks the token tile (else rows / n_experts); live_rows, when
+// given, is a device count past which X is not read (offsets non-decreasing).
 cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
-                                   int n_experts, int rows, int N, int K, int refcpu, int num_sms, cudaStream_t s);
+                                   int n_experts, int rows, int N, int K, int refcpu, int num_sms, cudaStream_t s,
+                                   int mean_rows = 0, const int* live_rows = nullptr);
 cudaError_t status_fetch_gemm_tc(unsigned* out, cudaStream_t s);
 
 // SWQ_OPT_EARLY_WEIGHT_PREFETCH for the tensor-core GEMM: 1 lets its weight

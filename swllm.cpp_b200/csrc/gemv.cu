@@ -1051,7 +1051,7 @@ struct GroupedGemvParams {
     const int* offsets;
     const float* X;
     float* Y;
-    int n_experts, rows_total, N, K, nb, row_bytes, xstride, refcpu, x_vec;
+    int n_experts, rows_total, N, K, nb, row_bytes, xstride, refcpu, x_vec, adaptive;
 };
 
 constexpr int GG_WARPS = 8;
@@ -1113,9 +1113,35 @@ __device__ void prep_x_rows(const float* X, int K, int rows, uint8_t* xq, int xs
     }
 }
 
+// One pass over `mrows` (<= MTP) activation rows of expert matrix W.
+template <int T, int MTP>
+__device__ __forceinline__ void grouped_pass(const GroupedGemvParams& p, const uint8_t* W, int m0, int mrows, int r0,
+                                             int r1, uint8_t* xq) {
+    using F = Fmt<T>;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nu = p.nb * F::UPB;
+    prep_x_rows<T, MTP>(p.X + static_cast<size_t>(m0) * p.K, p.K, mrows, xq, p.xstride, p.refcpu != 0,
+                        p.x_vec != 0, threadIdx.x, GG_WARPS * 32);
+    __syncthreads();
+    for (int row = r0 + warp; row < r1; row += GG_WARPS) {
+        float acc[MTP];
+#pragma unroll
+        for (int m = 0; m < MTP; ++m) acc[m] = 0.f;
+        const uint8_t* wr = W + static_cast<size_t>(row) * p.row_bytes;
+        for (int uu = lane; uu < nu; uu += 32) {
+            const int kbl = uu / F::UPB, c = uu - kbl * F::UPB;
+            unit_dot<T, MTP>(wr + kbl * F::BB, c, uu, xq, p.xstride, acc);
+        }
+        row_store<MTP>(acc, lane, p.Y + static_cast<size_t>(m0) * p.N, mrows, p.N, row, nullptr);
+    }
+    __syncthreads();  // the next pass overwrites xq
+}
+
+// MT rows per pass; with p.adaptive (MT = 4) each expert's rows are taken in
+// passes of 4, 2 or 1 by how many remain, so an expert with one row costs one
+// row's work.  A row's result does not depend on the pass it is in.
 template <int T, int MT>
 __global__ void __launch_bounds__(GG_WARPS * 32) grouped_gemv_kernel(const GroupedGemvParams p) {
-    using F = Fmt<T>;
     extern __shared__ __align__(128) uint8_t xq[];
     pdl_wait_primary();  // X and the offsets may come from the previous kernels
     const int e = blockIdx.y;
@@ -1129,25 +1155,20 @@ __global__ void __launch_bounds__(GG_WARPS * 32) grouped_gemv_kernel(const Group
         if (threadIdx.x == 0) atomicOr(&g_swq_dev_status, DEV_BAD_ALIGN);
         return;
     }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nu = p.nb * F::UPB;
-    for (int m0 = a; m0 < b; m0 += MT) {
-        const int mrows = min(MT, b - m0);
-        prep_x_rows<T, MT>(p.X + static_cast<size_t>(m0) * p.K, p.K, mrows, xq, p.xstride, p.refcpu != 0,
-                           p.x_vec != 0, threadIdx.x, GG_WARPS * 32);
-        __syncthreads();
-        for (int row = r0 + warp; row < r1; row += GG_WARPS) {
-            float acc[MT];
-#pragma unroll
-            for (int m = 0; m < MT; ++m) acc[m] = 0.f;
-            const uint8_t* wr = W + static_cast<size_t>(row) * p.row_bytes;
-            for (int uu = lane; uu < nu; uu += 32) {
-                const int kbl = uu / F::UPB, c = uu - kbl * F::UPB;
-                unit_dot<T, MT>(wr + kbl * F::BB, c, uu, xq, p.xstride, acc);
+    for (int m0 = a; m0 < b;) {
+        const int rem = b - m0;
+        if (MT == 4 && p.adaptive && rem < 3) {
+            if (rem == 2) {
+                grouped_pass<T, 2>(p, W, m0, 2, r0, r1, xq);
+                m0 += 2;
+            } else {
+                grouped_pass<T, 1>(p, W, m0, 1, r0, r1, xq);
+                m0 += 1;
             }
-            row_store<MT>(acc, lane, p.Y + static_cast<size_t>(m0) * p.N, mrows, p.N, row, nullptr);
+        } else {
+            grouped_pass<T, MT>(p, W, m0, min(MT, rem), r0, r1, xq);
+            m0 += MT;
         }
-        __syncthreads();  // the next group's rows overwrite xq
     }
 }
 
@@ -1176,7 +1197,7 @@ static cudaError_t launch_grouped_gemv_fmt(const GroupedGemvParams& p, int mt, i
 
 cudaError_t grouped_gemv_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
                                 int n_experts, int rows_total, int N, int K, int refcpu, int smem_optin,
-                                cudaStream_t s) {
+                                cudaStream_t s, bool adaptive) {
     GroupedGemvParams p{};
     p.wptrs = reinterpret_cast<const uint8_t* const*>(wptrs);
     p.offsets = offsets;
@@ -1188,8 +1209,10 @@ cudaError_t grouped_gemv_launch(int type, const void* const* wptrs, const int* o
     p.K = K;
     p.refcpu = refcpu;
     p.x_vec = (reinterpret_cast<uintptr_t>(X) & 15u) == 0 ? 1 : 0;
-    // activation rows per pass: the mean rows per expert (1, 2 or 4)
-    const int mt = (rows_total + n_experts - 1) / n_experts;
+    // activation rows per pass: the mean rows per expert (1, 2 or 4), or 4
+    // with the pass size chosen per expert on the device
+    p.adaptive = adaptive ? 1 : 0;
+    const int mt = adaptive ? 4 : (rows_total + n_experts - 1) / n_experts;
     switch (type) {
         case Q4_0: p.nb = K / Fmt<Q4_0>::QK; p.row_bytes = p.nb * Fmt<Q4_0>::BB; return launch_grouped_gemv_fmt<Q4_0>(p, mt, smem_optin, s);
         case Q8_0: p.nb = K / Fmt<Q8_0>::QK; p.row_bytes = p.nb * Fmt<Q8_0>::BB; return launch_grouped_gemv_fmt<Q8_0>(p, mt, smem_optin, s);

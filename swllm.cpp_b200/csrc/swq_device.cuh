@@ -13,7 +13,8 @@ enum : int { Q4_0 = 2, Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_
 // Read and cleared by swq_check().
 enum : unsigned { DEV_TIMEOUT_FULL = 1u, DEV_TIMEOUT_EMPTY = 2u, DEV_TIMEOUT_DRAIN = 4u,
                   DEV_TIMEOUT_MMA = 8u, DEV_TIMEOUT_PEER = 16u,
-                  DEV_BAD_ALIGN = 32u };  // not a wait: an input the kernel skipped
+                  DEV_BAD_ALIGN = 32u,    // not a wait: an input the kernel skipped
+                  DEV_BAD_ID = 64u };     // not a wait: an expert id out of range
 // One word per translation unit (no relocatable device code); each unit
 // exports a host accessor through SWQ_DEFINE_STATUS_FETCH.
 static __device__ unsigned g_swq_dev_status = 0;

@@ -67,6 +67,27 @@ class PeerAllReduce:
             stream = torch.cuda.current_stream(self.device)
         _raise(lib().swq_allreduce_sum(self._ar, _ptr(t), t.numel(), _stream(stream)))
 
+    def reset(self, stream=None, group=None) -> None:
+        """Bring the group back after a sum timed out (swq_check raised
+        SwqError with SWQ_ERR_TIMEOUT on some rank): every rank calls reset()
+        between steps.  Waits until no kernel of this rank is in flight
+        (every wait is bounded, so this ends), meets the other ranks at a host
+        barrier, zeroes this rank's flag words and epoch counters, and meets
+        them again so that no rank publishes a new epoch while a peer still
+        shows its old flags.  `group` is the process group for the two
+        barriers (default: the one the handles were exchanged over); a gloo
+        group keeps them off the GPU."""
+        import torch
+        import torch.distributed as dist
+        g = self.group if group is None else group
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=g)
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        with torch.cuda.device(self.device):
+            _raise(lib().swq_allreduce_reset(self._ar, _stream(stream)))
+        dist.barrier(group=g)
+
     def close(self) -> None:
         if self._ar:
             lib().swq_allreduce_destroy(self._ar)

@@ -86,6 +86,18 @@ def lib() -> ctypes.CDLL:
         "swq_gemm_act_ws": (i32, [i32, vp, vp, vp, i32, i32, i32, ctypes.POINTER(ActArgs), vp, sz, vp]),
         "swq_grouped_gemm": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "swq_grouped_gemv": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
+        "swq_grouped_matmul": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+        "swq_moe_router": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp]),
+        "swq_moe_sort": (i32, [vp, i32, i32, vp, vp, vp, vp]),
+        "swq_moe_gather": (i32, [vp, vp, vp, i32, i32, i32, i32, vp, vp]),
+        "swq_moe_combine": (i32, [vp, vp, vp, i32, i32, i32, vp, i32, vp]),
+        "swq_ep_create": (i32, [i32, i32, i32, i32, i32, i32, ctypes.POINTER(vp), vp]),
+        "swq_ep_open": (i32, [vp, vp]),
+        "swq_ep_dispatch": (i32, [vp, vp, vp, i32, vp]),
+        "swq_ep_received": (i32, [vp, ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.POINTER(i32)]),
+        "swq_ep_combine": (i32, [vp, vp, vp, vp, i32, vp]),
+        "swq_ep_reset": (i32, [vp, vp]),
+        "swq_ep_destroy": (i32, [vp]),
         "swq_rmsnorm": (i32, [vp, vp, vp, i32, ctypes.c_float, i32, vp]),
         "swq_add_rmsnorm": (i32, [vp, vp, vp, vp, i32, ctypes.c_float, i32, vp]),
         "swq_rope_kv": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, vp]),
@@ -107,6 +119,7 @@ def lib() -> ctypes.CDLL:
         "swq_allreduce_create": (i32, [sz, i32, i32, ctypes.POINTER(vp), vp]),
         "swq_allreduce_open": (i32, [vp, vp]),
         "swq_allreduce_sum": (i32, [vp, vp, sz, vp]),
+        "swq_allreduce_reset": (i32, [vp, vp]),
         "swq_allreduce_destroy": (i32, [vp]),
         "swq_ctx_create": (i32, [i32, ctypes.POINTER(vp)]),
         "swq_ctx_destroy": (i32, [vp]),
@@ -203,6 +216,39 @@ def grouped_gemm(type_id: int, w_ptrs, offsets, X, Y, n_experts: int, total_rows
     addresses; offsets: device int32 tensor of n_experts + 1 row offsets."""
     _raise(lib().swq_grouped_gemm(type_id, _ptr(w_ptrs), _ptr(offsets), _ptr(X), _ptr(Y), n_experts, total_rows,
                                   N, K, _stream(stream)))
+
+
+def grouped_matmul(type_id: int, w_ptrs, offsets, X, Y, n_experts: int, total_rows: int, N: int, K: int,
+                   mean_rows: int, stream=None) -> None:
+    """Grouped expert product with the kernel picked from mean_rows, the
+    expected rows per expert (swq_grouped_matmul); total_rows bounds the rows."""
+    _raise(lib().swq_grouped_matmul(type_id, _ptr(w_ptrs), _ptr(offsets), _ptr(X), _ptr(Y), n_experts, total_rows,
+                                    N, K, mean_rows, _stream(stream)))
+
+
+def moe_router(router_w, X, T: int, E: int, H: int, k: int, logits, ids, w, stream=None) -> None:
+    """fp32 router GEMV into logits [T, E], top-k ids [T, k] (int32) and the
+    softmax over those k logits w [T, k] (swq_moe_router)."""
+    _raise(lib().swq_moe_router(_ptr(router_w), _ptr(X), T, E, H, k, _ptr(logits), _ptr(ids), _ptr(w),
+                                _stream(stream)))
+
+
+def moe_sort(ids, P: int, n_experts: int, offsets, sorted_pairs, pair_rows, stream=None) -> None:
+    """Stable sort of P (token, slot) pairs by expert (swq_moe_sort)."""
+    _raise(lib().swq_moe_sort(_ptr(ids), P, n_experts, _ptr(offsets), _ptr(sorted_pairs), _ptr(pair_rows),
+                              _stream(stream)))
+
+
+def moe_gather(X, sorted_pairs, offsets, n_experts: int, P: int, k: int, H: int, X_sorted, stream=None) -> None:
+    """X_sorted[r] = X[sorted_pairs[r] // k] for the sorted rows (swq_moe_gather)."""
+    _raise(lib().swq_moe_gather(_ptr(X), _ptr(sorted_pairs), _ptr(offsets), n_experts, P, k, H, _ptr(X_sorted),
+                                _stream(stream)))
+
+
+def moe_combine(Y_sorted, pair_rows, w, T: int, k: int, H: int, Y, accumulate: bool = False, stream=None) -> None:
+    """Y[t] (+)= sum_j w[t, j] * Y_sorted[pair_rows[t*k + j]] (swq_moe_combine)."""
+    _raise(lib().swq_moe_combine(_ptr(Y_sorted), _ptr(pair_rows), _ptr(w), T, k, H, _ptr(Y), 1 if accumulate else 0,
+                                 _stream(stream)))
 
 
 ACT_NONE, ACT_RMSNORM, ACT_SWIGLU = 0, 1, 2

@@ -30,6 +30,7 @@ from typing import Callable, Sequence
 import numpy as np
 
 from .lib import gemm as _swq_gemm, grouped_gemm as _swq_grouped_gemm, grouped_gemv as _swq_grouped_gemv
+from .lib import grouped_matmul as _swq_grouped_matmul
 from .synth import block_geometry
 
 
@@ -142,6 +143,7 @@ class _GroupedCUDA:
     def __init__(self, device, gemv_rows: int = 4):
         self.device = device
         self.gemv_rows = gemv_rows
+        self.mean_rows = 0  # expected rows per expert, set by the caller (0: rows / experts)
 
     def table(self, weights: Sequence):
         import torch
@@ -149,6 +151,9 @@ class _GroupedCUDA:
 
     def __call__(self, type_id, weights, table, offsets, X, Y, N, K):
         rows, E = X.shape[0], len(weights)
+        if self.mean_rows > 0:  # the same kernel on every rank, whatever its share of the rows
+            _swq_grouped_matmul(type_id, table, offsets, X, Y, E, rows, N, K, self.mean_rows)
+            return
         fn = _swq_grouped_gemv if rows <= self.gemv_rows * E else _swq_grouped_gemm
         fn(type_id, table, offsets, X, Y, E, rows, N, K)
 
@@ -220,6 +225,8 @@ class ExpertParallelMoE:
         import torch
         import torch.distributed as dist
         T, k = topk_ids.shape
+        if hasattr(self.grouped, "mean_rows"):
+            self.grouped.mean_rows = max(1, -(-T * k // self.E))
         eid = topk_ids.reshape(-1).long()                       # pair p = t*k + j
         owner = torch.div(eid, self.el, rounding_mode="floor")
         order = torch.argsort(owner, stable=True)                # send order

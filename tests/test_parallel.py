@@ -204,3 +204,48 @@ def test_decoder_shards_reassemble():
         cols = [_shard(b, t, N, K, None, (r * K // 2, (r + 1) * K // 2)) for r in range(2)]
         assert np.array_equal(np.concatenate(cols, axis=1), b.reshape(N, -1))
         assert np.array_equal(cols[1], split_k(b, t, N, K, 1, 2)[0])
+
+
+# ------------------------------------------- peer all-reduce recovery (host)
+def _reset_worker(rank, world, port, path):
+    """PeerAllReduce.reset's host ordering with the device calls faked: no
+    rank may zero its flags before every rank has stopped its kernels
+    (first barrier), and no rank may return -- and so launch the next sum --
+    before every rank has zeroed them (second barrier).  Rank 1 arrives late."""
+    import contextlib
+    import time
+    from swq import comm
+    _init(rank, world, port)
+    try:
+        log = {}
+
+        class FakeLib:
+            def swq_allreduce_reset(self, ar, stream):
+                log["reset"] = time.time()
+                return 0
+
+        comm.lib = lambda: FakeLib()
+        comm._stream = lambda s: None
+        torch.cuda.synchronize = lambda device=None: log.setdefault("sync", time.time())
+        torch.cuda.device = lambda device: contextlib.nullcontext()
+        ar = object.__new__(comm.PeerAllReduce)
+        ar.group, ar.device, ar._ar = None, None, object()
+        if rank == 1:
+            time.sleep(0.5)
+        log["enter"] = time.time()
+        ar.reset(stream=object())
+        log["return"] = time.time()
+        np.save(f"{path}.{rank}.npy", np.array([log["enter"], log["sync"], log["reset"], log["return"]]))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_allreduce_reset_barriers(tmp_path):
+    path = str(tmp_path / "reset")
+    mp.spawn(_reset_worker, args=(2, _free_port(), path), nprocs=2, join=True)
+    enter, sync, reset, ret = np.stack([np.load(f"{path}.{r}.npy") for r in range(2)]).T
+    assert np.all(sync <= reset)                 # own kernels done before zeroing
+    assert reset.min() >= sync.max()             # nobody zeroes before everyone stopped
+    assert ret.min() >= reset.max()              # nobody resumes before everyone zeroed
+    assert reset[0] >= enter[1]                  # the early rank waited for the late one
