@@ -204,6 +204,15 @@ swq_status swq_grouped_gemm(int ggml_type, const void* const* W_experts, const i
 swq_status swq_grouped_matmul(int ggml_type, const void* const* W_experts, const int* expert_offsets,
                               const float* X_sorted, float* Y, int n_experts, int total_rows, int N, int K,
                               int mean_rows, swq_stream_t stream);
+/* swq_grouped_matmul with the experts stacked in one tensor, the layout of a
+ * GGUF expert tensor (ffn_{gate,up,down}_exps, [n_experts][N][K] blocks):
+ * expert e's matrix is rows e*N .. e*N+N-1 of the n_experts*N x K matrix at
+ * W_all.  The tensor-core form then loads each weight stage with one
+ * tensor-map copy (W_all 16-byte aligned and row bytes a multiple of 16; else
+ * one copy per row). */
+swq_status swq_grouped_matmul_stacked(int ggml_type, const void* W_all, const int* expert_offsets,
+                                      const float* X_sorted, float* Y, int n_experts, int total_rows, int N, int K,
+                                      int mean_rows, swq_stream_t stream);
 
 /* ---- GEMM with a fused activation prologue --------------------------------
  *

@@ -442,9 +442,9 @@ swq_status swq_grouped_gemv(int type, const void* const* W_experts, const int* e
     return SWQ_OK;
 }
 
-swq_status swq_grouped_matmul(int type, const void* const* W_experts, const int* expert_offsets, const float* X_sorted,
-                              float* Y, int n_experts, int total_rows, int N, int K, int mean_rows,
-                              swq_stream_t stream) {
+static swq_status grouped_matmul_impl(int type, const void* const* W_experts, const void* W_all,
+                                      const int* expert_offsets, const float* X_sorted, float* Y, int n_experts,
+                                      int total_rows, int N, int K, int mean_rows, swq_stream_t stream) {
     TypeInfo ti;
     if (!type_info(type, &ti)) return fail(SWQ_ERR_BAD_TYPE, "type " + std::to_string(type) + " is not on this path");
     if (n_experts < 0 || total_rows < 0 || N < 0 || K < 0) return fail(SWQ_ERR_BAD_SHAPE, "negative size");
@@ -452,7 +452,8 @@ swq_status swq_grouped_matmul(int type, const void* const* W_experts, const int*
         return fail(SWQ_ERR_BAD_SHAPE, "K=" + std::to_string(K) + " is not a multiple of " + std::to_string(ti.qk));
     if (n_experts > 4095) return fail(SWQ_ERR_BAD_SHAPE, "n_experts above 4095");
     if (n_experts == 0 || total_rows == 0 || N == 0) return SWQ_OK;
-    if (!W_experts || !expert_offsets || !X_sorted || !Y) return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
+    if ((!W_experts && !W_all) || !expert_offsets || !X_sorted || !Y)
+        return fail(SWQ_ERR_NULL_PTR, "null pointer argument");
     swq::DeviceInfo dev;
     swq_status st = current_device(&dev);
     if (st != SWQ_OK) return st;
@@ -464,12 +465,29 @@ swq_status swq_grouped_matmul(int type, const void* const* W_experts, const int*
     cudaError_t e;
     if (mean_rows <= 4)
         e = swq::grouped_gemv_launch(type, W_experts, expert_offsets, X_sorted, Y, n_experts, total_rows, N, K,
-                                     g_opt_q2k_refcpu, dev.smem_per_block_optin, s, true);
+                                     g_opt_q2k_refcpu, dev.smem_per_block_optin, s, true, W_all);
     else
         e = swq::gemm_tc_grouped_launch(type, W_experts, expert_offsets, X_sorted, Y, n_experts, total_rows, N, K,
-                                        g_opt_q2k_refcpu, dev.num_sms, s, mean_rows, expert_offsets + n_experts);
+                                        g_opt_q2k_refcpu, dev.num_sms, s, mean_rows, expert_offsets + n_experts,
+                                        W_all);
     if (e != cudaSuccess) return cuda_fail(e, "grouped matmul launch");
     return SWQ_OK;
+}
+
+swq_status swq_grouped_matmul(int type, const void* const* W_experts, const int* expert_offsets, const float* X_sorted,
+                              float* Y, int n_experts, int total_rows, int N, int K, int mean_rows,
+                              swq_stream_t stream) {
+    if (!W_experts) return fail(SWQ_ERR_NULL_PTR, "null expert table");
+    return grouped_matmul_impl(type, W_experts, nullptr, expert_offsets, X_sorted, Y, n_experts, total_rows, N, K,
+                               mean_rows, stream);
+}
+
+swq_status swq_grouped_matmul_stacked(int type, const void* W_all, const int* expert_offsets, const float* X_sorted,
+                                      float* Y, int n_experts, int total_rows, int N, int K, int mean_rows,
+                                      swq_stream_t stream) {
+    if (!W_all) return fail(SWQ_ERR_NULL_PTR, "null expert tensor");
+    return grouped_matmul_impl(type, nullptr, W_all, expert_offsets, X_sorted, Y, n_experts, total_rows, N, K,
+                               mean_rows, stream);
 }
 
 // ---- decode step -------------------------------------------------------------

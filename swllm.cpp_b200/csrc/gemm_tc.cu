@@ -517,6 +517,7 @@ struct Params {
     const int* offsets;
     int n_experts;
     int rows_total;
+    int stacked;  // grouped: expert e's matrix is rows e*N .. e*N+N-1 of W (wptrs unused)
     int early;  // the W producer may read weights before the previous kernel completes
     // split-K (dense only): each output tile is computed as ksplit work units
     // of gps W stages each; unit u = tile * ksplit + split.  With ksplit > 1
@@ -534,6 +535,7 @@ struct Params {
 struct TileRef {
     const uint8_t* W;
     int m0, m_end, nt;
+    int e;  // grouped: the expert
 };
 
 __device__ __forceinline__ int clamp_off(const Params& p, int e) { return min(max(p.offsets[e], 0), p.rows_total); }
@@ -549,6 +551,7 @@ __device__ __forceinline__ TileRef tile_ref(const Params& p, const int* tpre, in
         r.m0 = (tile / p.n_ntiles) * BN;
         r.m_end = p.M;
         r.W = p.W;
+        r.e = 0;
     } else {
         int lo = 0, hi = p.n_experts;  // last e with tpre[e] <= tile (empty experts share values)
         while (hi - lo > 1) {
@@ -560,7 +563,8 @@ __device__ __forceinline__ TileRef tile_ref(const Params& p, const int* tpre, in
         r.nt = local % p.n_ntiles;
         r.m0 = a + (local / p.n_ntiles) * BN;
         r.m_end = b;
-        r.W = p.wptrs[lo];
+        r.W = p.stacked ? p.W + static_cast<size_t>(lo) * p.N * p.row_bytes : p.wptrs[lo];
+        r.e = lo;
     }
     return r;
 }
@@ -781,10 +785,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 const uint32_t dst = smem_u32(w_st + js * WSTAGE);
                 const size_t goff = static_cast<size_t>(g) * F.gbytes;
-                if (!G && !p.rows_mode) {
+                if (!p.rows_mode) {
+                    // one tensor-map box per stage; stacked experts are rows of one map
                     if (lane == 0) {
                         mbar_arrive_expect_tx(&wfull[js], static_cast<uint32_t>(WSTAGE));
-                        tma_load_2d(dst, &wmap, static_cast<int>((goff & ~size_t(15)) >> 1), row0, &wfull[js]);
+                        tma_load_2d(dst, &wmap, static_cast<int>((goff & ~size_t(15)) >> 1),
+                                    G ? tr.e * p.N + row0 : row0, &wfull[js]);
                     }
                 } else {
                     // Rows lane, lane + 32, lane + 64, lane + 96 of the tile: copy
@@ -1161,6 +1167,7 @@ struct ExpertSet {
     const uint8_t* const* wptrs;
     const int* offsets;
     int n_experts;
+    const uint8_t* w_all = nullptr;  // stacked experts (wptrs unused)
 };
 
 // M is the number of X rows (grouped: all experts' rows together).
@@ -1214,7 +1221,9 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, const float* rowsc
     p.ksteps = (K + tc::BK - 1) / tc::BK;
     p.ngroups = (K + tc::KG - 1) / tc::KG;
     const uintptr_t w = reinterpret_cast<uintptr_t>(W);
-    const size_t wbytes = static_cast<size_t>(N) * p.row_bytes;
+    const bool stacked = G && ex->w_all != nullptr;
+    const int wrows = stacked ? ex->n_experts * N : N;  // rows of the weight tensor map
+    const size_t wbytes = static_cast<size_t>(wrows) * p.row_bytes;
     p.w_lo = reinterpret_cast<const uint8_t*>(w & ~uintptr_t(15));
     p.w_hi = reinterpret_cast<const uint8_t*>((w + wbytes + 15) & ~uintptr_t(15));
     size_t extra = 0;
@@ -1229,6 +1238,7 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, const float* rowsc
         p.offsets = ex->offsets;
         p.n_experts = ex->n_experts;
         p.rows_total = M;
+        p.stacked = stacked ? 1 : 0;
         extra = static_cast<size_t>(ex->n_experts + 1) * sizeof(int);
         // each expert adds at most one partial token tile
         max_tiles = static_cast<int>(std::min<int64_t>(
@@ -1239,7 +1249,7 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, const float* rowsc
     // (and always for grouped launches, whose expert weights are separate
     // allocations) one bulk copy per row from the 16-byte boundary at or below
     // the row's data.
-    bool tmap = !G && (w % 16 == 0) && (p.row_bytes % 16 == 0);
+    bool tmap = (!G || stacked) && (w % 16 == 0) && (p.row_bytes % 16 == 0);
     for (int attempt = 0; attempt < 2; ++attempt) {
         const bool offs = !tmap || (F.gbytes % 16 != 0);  // data may start up to 15 bytes into a smem row
         int wp = (F.gbytes + (offs ? 15 : 0) + 15) / 16 * 16;
@@ -1265,7 +1275,7 @@ static cudaError_t launch_tc(const void* W, const __half* Xh, const float* rowsc
         CUtensorMap wmap;
         std::memset(&wmap, 0, sizeof(wmap));
         if (tmap) {
-            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.row_bytes / 2), static_cast<cuuint64_t>(N)};
+            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.row_bytes / 2), static_cast<cuuint64_t>(wrows)};
             const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.row_bytes)};
             const cuuint32_t box[2] = {static_cast<cuuint32_t>(wp / 2), static_cast<cuuint32_t>(tc::BM)};
             const cuuint32_t estr[2] = {1, 1};
@@ -1322,14 +1332,28 @@ static cudaError_t launch_tc_bn(const void* W, const __half* Xh, const float* rs
     return launch_tc<T, 256, A4, false>(W, Xh, rs, Y, M, N, K, num_sms, s, nullptr, sk);
 }
 
-// Grouped: the token tile follows the mean rows per expert.
+// Grouped: the token tile follows the mean rows per expert.  Stacked experts
+// (one tensor, expert e at rows e*N ..) load each W stage with one tensor-map
+// box; separate expert matrices with one bulk copy per row.
+template <int T, bool A4>
+static cudaError_t launch_tc_grouped_a(const ExpertSet& ex, const __half* Xh, const float* rs, float* Y, int rows,
+                                       int N, int K, int num_sms, cudaStream_t s, int mean) {
+    const void* W = ex.w_all;
+    if (mean <= 64) return launch_tc<T, 64, A4, true>(W, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
+    if (mean <= 128) return launch_tc<T, 128, A4, true>(W, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
+    return launch_tc<T, 256, A4, true>(W, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
+}
+
 template <int T>
 static cudaError_t launch_tc_grouped(const ExpertSet& ex, const __half* Xh, const float* rs, float* Y, int rows,
                                      int N, int K, int num_sms, cudaStream_t s, int mean_rows) {
     const int mean = mean_rows > 0 ? mean_rows : (rows + ex.n_experts - 1) / ex.n_experts;
-    if (mean <= 64) return launch_tc<T, 64, false, true>(nullptr, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
-    if (mean <= 128) return launch_tc<T, 128, false, true>(nullptr, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
-    return launch_tc<T, 256, false, true>(nullptr, Xh, rs, Y, rows, N, K, num_sms, s, &ex);
+    // Q4_K, Q5_K and Q2_K keep every field of a block 4-byte aligned when W is.
+    if constexpr (T == Q4_K || T == Q5_K || T == Q2_K) {
+        if (ex.w_all != nullptr && reinterpret_cast<uintptr_t>(ex.w_all) % 4 == 0)
+            return launch_tc_grouped_a<T, true>(ex, Xh, rs, Y, rows, N, K, num_sms, s, mean);
+    }
+    return launch_tc_grouped_a<T, false>(ex, Xh, rs, Y, rows, N, K, num_sms, s, mean);
 }
 
 template <int T>
@@ -1474,7 +1498,7 @@ cudaError_t gemm_tc_launch_ws(int type, const void* W, const float* X, float* Y,
 
 cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
                                    int n_experts, int rows, int N, int K, int refcpu, int num_sms, cudaStream_t s,
-                                   int mean_rows, const int* live_rows) {
+                                   int mean_rows, const int* live_rows, const void* w_all) {
     if (tc::tc_fmt(type).qk == 0 || K % 32 != 0 || encode_fn2() == nullptr) return cudaErrorNotSupported;
     const int64_t n = static_cast<int64_t>(rows) * K;
     cudaMemPool_t pool = nullptr;
@@ -1490,7 +1514,8 @@ cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int
     e = tc::tc_fmt(type).f2 ? launch_x_to_f16<true>(X, Xh, rs, rows, K, num_sms, s, nullptr, 0, act, q2ref)
                             : launch_x_to_f16<false>(X, Xh, rs, rows, K, num_sms, s, nullptr, 0, act, q2ref);
     if (e == cudaSuccess) {
-        const ExpertSet ex{reinterpret_cast<const uint8_t* const*>(wptrs), offsets, n_experts};
+        const ExpertSet ex{reinterpret_cast<const uint8_t* const*>(wptrs), offsets, n_experts,
+                           static_cast<const uint8_t*>(w_all)};
         switch (type) {
             case Q4_0: e = launch_tc_grouped<Q4_0>(ex, Xh, rs, Y, rows, N, K, num_sms, s, mean_rows); break;
             case Q8_0: e = launch_tc_grouped<Q8_0>(ex, Xh, rs, Y, rows, N, K, num_sms, s, mean_rows); break;

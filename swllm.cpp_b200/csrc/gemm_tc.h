@@ -40,9 +40,11 @@ cudaError_t gemm_tc_launch_ws(int type, const void* W, const float* X, float* Y,
 // refcpu: Q2_K in the reference CPU routine's activation order.
 // mean_rows > 0 picks the token tile (else rows / n_experts); live_rows, when
 // given, is a device count past which X is not read (offsets non-decreasing).
+// w_all != nullptr: stacked experts, expert e is rows e*N .. e*N+N-1 of the
+// n_experts*N x K matrix at w_all (wptrs unused).
 cudaError_t gemm_tc_grouped_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
                                    int n_experts, int rows, int N, int K, int refcpu, int num_sms, cudaStream_t s,
-                                   int mean_rows = 0, const int* live_rows = nullptr);
+                                   int mean_rows = 0, const int* live_rows = nullptr, const void* w_all = nullptr);
 cudaError_t status_fetch_gemm_tc(unsigned* out, cudaStream_t s);
 
 // SWQ_OPT_EARLY_WEIGHT_PREFETCH for the tensor-core GEMM: 1 lets its weight

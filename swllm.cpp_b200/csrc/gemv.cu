@@ -1052,6 +1052,7 @@ struct GroupedGemvParams {
     const float* X;
     float* Y;
     int n_experts, rows_total, N, K, nb, row_bytes, xstride, refcpu, x_vec, adaptive;
+    const uint8_t* w_all;  // stacked experts: expert e at w_all + e * N * row_bytes (wptrs unused)
 };
 
 constexpr int GG_WARPS = 8;
@@ -1150,7 +1151,7 @@ __global__ void __launch_bounds__(GG_WARPS * 32) grouped_gemv_kernel(const Group
     const int r0 = blockIdx.x * GG_ROWS;
     if (b <= a || r0 >= p.N) return;
     const int r1 = min(p.N, r0 + GG_ROWS);
-    const uint8_t* W = p.wptrs[e];
+    const uint8_t* W = p.w_all ? p.w_all + static_cast<size_t>(e) * p.N * p.row_bytes : p.wptrs[e];
     if (reinterpret_cast<uintptr_t>(W) & 15u) {
         if (threadIdx.x == 0) atomicOr(&g_swq_dev_status, DEV_BAD_ALIGN);
         return;
@@ -1197,8 +1198,9 @@ static cudaError_t launch_grouped_gemv_fmt(const GroupedGemvParams& p, int mt, i
 
 cudaError_t grouped_gemv_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
                                 int n_experts, int rows_total, int N, int K, int refcpu, int smem_optin,
-                                cudaStream_t s, bool adaptive) {
+                                cudaStream_t s, bool adaptive, const void* w_all) {
     GroupedGemvParams p{};
+    p.w_all = static_cast<const uint8_t*>(w_all);
     p.wptrs = reinterpret_cast<const uint8_t* const*>(wptrs);
     p.offsets = offsets;
     p.X = X;

@@ -58,10 +58,11 @@ constexpr unsigned kStatusBadAlign = 32u;
 // offsets[e+1]-1 of X by its GGUF matrix wptrs[e] (device arrays); every expert
 // matrix 16-byte aligned (a misaligned one is skipped and flagged).
 // adaptive: rows per pass chosen per expert on the device (4, 2 or 1) instead
-// of from the mean rows_total / n_experts.
+// of from the mean rows_total / n_experts.  w_all: stacked experts (expert e
+// at w_all + e * N * row bytes; wptrs unused).
 cudaError_t grouped_gemv_launch(int type, const void* const* wptrs, const int* offsets, const float* X, float* Y,
                                 int n_experts, int rows_total, int N, int K, int refcpu, int smem_optin,
-                                cudaStream_t s, bool adaptive = false);
+                                cudaStream_t s, bool adaptive = false, const void* w_all = nullptr);
 // Shared-memory bytes of the per-CTA activation prep for padded row count MT.
 size_t gemv_smem_x_bytes(int type, int MT, int K, bool xf);
 

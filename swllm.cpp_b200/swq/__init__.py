@@ -28,7 +28,7 @@ from .lib import (  # noqa: F401
     add, add_rmsnorm, argmax, attention_decode, attention_prefill, attention_workspace_bytes, decode_advance, embed,
     qkv_bias_norm, rmsnorm, rope_kv, rope_kv_prefill, silu_mul,
     GEMM_NOALLOC_MAX_X_ELEMS, SwqError, Status, block_size, build, check, dequant, exported_symbols, gemm,
-    gemm_act, gemm_act_ws, gemm_noalloc, gemm_workspace_bytes, gemv, grouped_gemm, grouped_gemv, grouped_matmul,
+    gemm_act, gemm_act_ws, gemm_noalloc, gemm_workspace_bytes, gemv, grouped_gemm, grouped_gemv, grouped_matmul, grouped_matmul_stacked,
     moe_combine, moe_gather, moe_router, moe_sort,
     get_option, header_symbols, lib, lib_path, set_option, type_size,
 )

@@ -87,6 +87,7 @@ def lib() -> ctypes.CDLL:
         "swq_grouped_gemm": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "swq_grouped_gemv": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "swq_grouped_matmul": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+        "swq_grouped_matmul_stacked": (i32, [i32, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
         "swq_moe_router": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp]),
         "swq_moe_sort": (i32, [vp, i32, i32, vp, vp, vp, vp]),
         "swq_moe_gather": (i32, [vp, vp, vp, i32, i32, i32, i32, vp, vp]),
@@ -224,6 +225,13 @@ def grouped_matmul(type_id: int, w_ptrs, offsets, X, Y, n_experts: int, total_ro
     expected rows per expert (swq_grouped_matmul); total_rows bounds the rows."""
     _raise(lib().swq_grouped_matmul(type_id, _ptr(w_ptrs), _ptr(offsets), _ptr(X), _ptr(Y), n_experts, total_rows,
                                     N, K, mean_rows, _stream(stream)))
+
+
+def grouped_matmul_stacked(type_id: int, W_all, offsets, X, Y, n_experts: int, total_rows: int, N: int, K: int,
+                           mean_rows: int, stream=None) -> None:
+    """grouped_matmul with expert e at rows e*N .. of one stacked tensor W_all."""
+    _raise(lib().swq_grouped_matmul_stacked(type_id, _ptr(W_all), _ptr(offsets), _ptr(X), _ptr(Y), n_experts,
+                                            total_rows, N, K, mean_rows, _stream(stream)))
 
 
 def moe_router(router_w, X, T: int, E: int, H: int, k: int, logits, ids, w, stream=None) -> None:

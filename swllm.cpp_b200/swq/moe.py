@@ -8,9 +8,9 @@ host synchronisation:
 
   router GEMV (fp32) + top-k + softmax over the k      swq_moe_router
   rows to the ranks that own their experts             swq_ep_dispatch
-  gate|up of every routed row, grouped by expert        swq_grouped_matmul
+  gate|up of every routed row, grouped by expert        swq_grouped_matmul_stacked
   silu(gate) * up                                       swq_silu_mul
-  down, grouped by expert                               swq_grouped_matmul
+  down, grouped by expert                               swq_grouped_matmul_stacked
   weighted sum back in token order (+ shared expert)    swq_ep_combine
 
 `ExpertParallel` owns the peer-memory buffers of the dispatch and combine
@@ -26,7 +26,7 @@ from typing import Sequence
 
 import numpy as np
 
-from .lib import _ptr, _raise, _stream, grouped_matmul, lib, moe_router, silu_mul
+from .lib import _ptr, _raise, _stream, grouped_matmul, grouped_matmul_stacked, lib, moe_router, silu_mul
 
 HANDLE_BYTES = 64
 
@@ -122,46 +122,33 @@ class MoEFFN:
       others may be None).  types: GGML types of gate, up, down.
     router_w: [n_experts, H] fp32 (replicated on every rank).
     shared: optional (gate, up, down) of a shared expert of intermediate size
-      F_sh (types `shared_types`), computed on every rank for its own tokens
-      and added to the routed sum.
+      shared_F (types `shared_types`), computed on every rank for its own
+      tokens and added to the routed sum.
     max_tokens: the most tokens one call takes (buffers are sized for it).
+    scratch_from: another MoEFFN of the same shape whose dispatch buffers and
+      activations this one reuses (the layers of a decoder run one at a time).
     Call: y = ffn(x [T, H] fp32 device tensor) -> [T, H]; no host sync."""
 
-    def __init__(self, experts: Sequence, types: tuple[int, int, int], H: int, F: int, router_w, top_k: int,
-                 max_tokens: int, group=None, device=None, shared=None, shared_types=None, shared_F: int = 0):
+    def __init__(self, experts: Sequence | None, types: tuple[int, int, int], H: int, F: int, router_w, top_k: int,
+                 max_tokens: int, group=None, device=None, shared=None, shared_types=None, shared_F: int = 0,
+                 scratch_from: "MoEFFN | None" = None, n_experts: int = 0, device_blocks=None):
         import torch
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.rank, self.world = _group_rank_world(group)
-        self.E, self.H, self.F, self.k, self.types = len(experts), int(H), int(F), int(top_k), tuple(types)
+        self.E = len(experts) if experts is not None else int(n_experts)
+        self.H, self.F, self.k, self.types = int(H), int(F), int(top_k), tuple(types)
         if self.E % self.world:
             raise ValueError(f"{self.E} experts do not split over {self.world} ranks")
         self.el = self.E // self.world
         self.e0 = self.rank * self.el
         self.max_tokens = int(max_tokens)
         dev = self.device
-        own = experts[self.e0:self.e0 + self.el]
-        self.fused = types[0] == types[1]
-        if self.fused:  # gate rows then up rows: one [2F x H] matrix per expert
-            self.gu = [torch.cat([_to_dev(g, dev), _to_dev(u, dev)]) for g, u, _ in own]
-            self.gu_tab = torch.tensor([t.data_ptr() for t in self.gu], dtype=torch.int64, device=dev)
+        if device_blocks is not None:
+            self._weights_from_device(*device_blocks)
         else:
-            self.g = [_to_dev(g, dev) for g, _, _ in own]
-            self.u = [_to_dev(u, dev) for _, u, _ in own]
-            self.g_tab = torch.tensor([t.data_ptr() for t in self.g], dtype=torch.int64, device=dev)
-            self.u_tab = torch.tensor([t.data_ptr() for t in self.u], dtype=torch.int64, device=dev)
-        self.d = [_to_dev(d, dev) for _, _, d in own]
-        self.d_tab = torch.tensor([t.data_ptr() for t in self.d], dtype=torch.int64, device=dev)
+            self._weights_from_experts(experts[self.e0:self.e0 + self.el])
         rw = router_w if isinstance(router_w, torch.Tensor) else torch.from_numpy(np.asarray(router_w, np.float32))
         self.router_w = rw.to(device=dev, dtype=torch.float32).contiguous()
-        self.ep = ExpertParallel(self.max_tokens, self.k, self.E, self.H, group=group, device=dev)
-        cap = self.ep.capacity
-        self.logits = torch.empty(self.max_tokens, self.E, device=dev)
-        self.ids = torch.zeros(self.max_tokens, self.k, dtype=torch.int32, device=dev)
-        self.w = torch.zeros(self.max_tokens, self.k, device=dev)
-        self.gu_out = torch.empty(cap, 2 * self.F, device=dev)
-        self.h = torch.empty(cap, self.F, device=dev)
-        self.y_recv = torch.empty(cap, self.H, device=dev)
-        self.y = torch.empty(self.max_tokens, self.H, device=dev)
         self.shared = None
         if shared is not None:
             st = tuple(shared_types or types)
@@ -173,54 +160,135 @@ class MoEFFN:
                 self.sh_gu_w = torch.cat([sg, su])
             else:
                 self.sh_g, self.sh_u = sg, su
-                self.sh_h = torch.empty(self.max_tokens, self.shared_F, device=dev)
             self.sh_d = sd
-            self.sh_gu = torch.empty(self.max_tokens, 2 * self.shared_F, device=dev)
+        self._alloc(scratch_from, group)
+
+    def _weights_from_experts(self, own) -> None:
+        """Stack this rank's experts into one tensor per projection (the GGUF
+        expert-tensor layout) when every expert matrix keeps a 16-byte
+        boundary there; else one allocation per expert with a pointer table."""
+        import torch
+        from .synth import row_bytes
+        dev = self.device
+        self.fused = self.types[0] == self.types[1]
+        gu_sz = (2 if self.fused else 1) * self.F * row_bytes(self.types[0], self.H)
+        d_sz = self.H * row_bytes(self.types[2], self.F)
+        u_sz = self.F * row_bytes(self.types[1], self.H)
+        self.stacked = gu_sz % 16 == 0 and d_sz % 16 == 0 and (self.fused or u_sz % 16 == 0)
+        if self.fused:  # gate rows then up rows: one [2F x H] matrix per expert
+            gu = [torch.cat([_to_dev(g, dev), _to_dev(u, dev)]) for g, u, _ in own]
+            parts = {"gu": gu}
+        else:
+            parts = {"g": [_to_dev(g, dev) for g, _, _ in own], "u": [_to_dev(u, dev) for _, u, _ in own]}
+        parts["d"] = [_to_dev(d, dev) for _, _, d in own]
+        for name, mats in parts.items():
+            if self.stacked:
+                setattr(self, name + "_all", torch.cat(mats))
+            else:
+                setattr(self, name, mats)
+                setattr(self, name + "_tab", torch.tensor([t.data_ptr() for t in mats], dtype=torch.int64,
+                                                          device=dev))
+
+    def _weights_from_device(self, gu_all, d_all) -> None:
+        """gu_all: this rank's experts' fused gate|up matrices back to back
+        (el x [2F x H] GGUF rows, one device uint8 tensor); d_all: their down
+        matrices (el x [H x F])."""
+        from .synth import row_bytes
+        if self.types[0] != self.types[1]:
+            raise ValueError("device blocks hold fused gate|up matrices: gate and up need one type")
+        self.fused, self.stacked = True, True
+        gu_sz = 2 * self.F * row_bytes(self.types[0], self.H)
+        d_sz = self.H * row_bytes(self.types[2], self.F)
+        if gu_all.numel() != self.el * gu_sz or d_all.numel() != self.el * d_sz:
+            raise ValueError("device blocks do not hold el experts of this shape")
+        if gu_sz % 16 or d_sz % 16:
+            raise ValueError("stacked expert matrices must keep 16-byte boundaries")
+        self.gu_all, self.d_all = gu_all, d_all
+
+    def _gmm(self, name: str, type_id: int, offs, X, Y, rows: int, N: int, K: int, mean: int, stream) -> None:
+        if self.stacked:
+            grouped_matmul_stacked(type_id, getattr(self, name + "_all"), offs, X, Y, self.el, rows, N, K, mean,
+                                   stream=stream)
+        else:
+            grouped_matmul(type_id, getattr(self, name + "_tab"), offs, X, Y, self.el, rows, N, K, mean,
+                           stream=stream)
+
+    def _alloc(self, other: "MoEFFN | None", group) -> None:
+        import torch
+        dev = self.device
+        Fs = self.shared_F if self.shared else 0
+        if other is not None:
+            same = (other.E, other.H, other.F, other.k, other.max_tokens, other.world, Fs) == \
+                   (self.E, self.H, self.F, self.k, self.max_tokens, self.world, other.shared_F if other.shared else 0)
+            if not same:
+                raise ValueError("scratch_from needs a MoEFFN of the same shape")
+            for name in ("ep", "logits", "ids", "w", "gu_out", "h", "y_recv", "y", "sh_gu", "sh_h"):
+                setattr(self, name, getattr(other, name, None))
+            return
+        self.ep = ExpertParallel(self.max_tokens, self.k, self.E, self.H, group=group, device=dev)
+        cap = self.ep.capacity
+        self.logits = torch.empty(self.max_tokens, self.E, device=dev)
+        self.ids = torch.zeros(self.max_tokens, self.k, dtype=torch.int32, device=dev)
+        self.w = torch.zeros(self.max_tokens, self.k, device=dev)
+        self.gu_out = torch.empty(cap, 2 * self.F, device=dev)
+        self.h = torch.empty(cap, self.F, device=dev)
+        self.y_recv = torch.empty(cap, self.H, device=dev)
+        self.y = torch.empty(self.max_tokens, self.H, device=dev)
+        self.sh_gu = torch.empty(self.max_tokens, 2 * Fs, device=dev) if Fs else None
+        self.sh_h = torch.empty(self.max_tokens, Fs, device=dev) if Fs else None
 
     def route(self, x, T: int, stream=None) -> None:
         moe_router(self.router_w, x, T, self.E, self.H, self.k, self.logits, self.ids, self.w, stream=stream)
 
-    def _shared_ffn(self, x, T: int, stream) -> None:
+    def _shared_ffn(self, x, T: int, y, stream) -> None:
         """y[:T] = the shared expert's SwiGLU FFN of x (written, not added)."""
         from .lib import ACT_SWIGLU, gemm, gemm_act
         Fs, H = self.shared_F, self.H
         if self.sh_fused:
             gemm(self.shared_types[0], self.sh_gu_w, x, self.sh_gu, T, 2 * Fs, H, stream=stream)
-            gemm_act(self.shared_types[2], self.sh_d, self.sh_gu, self.y, T, H, Fs, kind=ACT_SWIGLU, ld=2 * Fs,
+            gemm_act(self.shared_types[2], self.sh_d, self.sh_gu, y, T, H, Fs, kind=ACT_SWIGLU, ld=2 * Fs,
                      stream=stream)
         else:
             gemm(self.shared_types[0], self.sh_g, x, self.sh_h, T, Fs, H, stream=stream)
             gemm(self.shared_types[1], self.sh_u, x, self.sh_gu, T, Fs, H, stream=stream)
             silu_mul(self.sh_h, self.sh_h, self.sh_gu, Fs, rows=T, ld=Fs, stream=stream)
-            gemm(self.shared_types[2], self.sh_d, self.sh_h, self.y, T, H, Fs, stream=stream)
+            gemm(self.shared_types[2], self.sh_d, self.sh_h, y, T, H, Fs, stream=stream)
 
-    def __call__(self, x, T: int | None = None, ids=None, w=None, stream=None):
-        """y [T, H] for x [T, H] (fp32, device).  ids/w override the router
-        (int32 [T, k] global expert ids and fp32 [T, k] weights)."""
+    def experts(self, T: int, peer_tokens: int | None = None, stream=None) -> None:
+        """The grouped expert FFN on the rows this rank received (after
+        ep.dispatch) into y_recv.  peer_tokens: the most tokens any rank
+        dispatched in this call (default max_tokens), bounding the rows."""
+        F, H = self.F, self.H
+        mean = max(1, math.ceil(T * self.k / self.E))
+        pt = self.max_tokens if peer_tokens is None else int(peer_tokens)
+        rows = min(self.ep.capacity, self.world * pt * self.k)
+        xr, offs = self.ep.recv_ptr, self.ep.offsets_ptr
+        if self.fused:
+            self._gmm("gu", self.types[0], offs, xr, self.gu_out, rows, 2 * F, H, mean, stream)
+            silu_mul(self.h, self.gu_out, self.gu_out.data_ptr() + 4 * F, F, rows=rows, ld=2 * F, stream=stream)
+        else:
+            self._gmm("g", self.types[0], offs, xr, self.h, rows, F, H, mean, stream)
+            self._gmm("u", self.types[1], offs, xr, self.gu_out, rows, F, H, mean, stream)
+            silu_mul(self.h, self.h, self.gu_out, F, rows=rows, ld=F, stream=stream)
+        self._gmm("d", self.types[2], offs, self.h, self.y_recv, rows, H, F, mean, stream)
+
+    def __call__(self, x, T: int | None = None, ids=None, w=None, out=None, peer_tokens: int | None = None,
+                 stream=None):
+        """y [T, H] for x [T, H] (fp32, device), into `out` when given.
+        ids/w override the router (int32 [T, k] global expert ids and fp32
+        [T, k] weights)."""
         T = int(x.shape[0]) if T is None else int(T)
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens above max_tokens={self.max_tokens}")
         if ids is None:
             self.route(x, T, stream)
             ids, w = self.ids, self.w
-        mean = max(1, math.ceil(T * self.k / self.E))
-        cap, F, H = self.ep.capacity, self.F, self.H
+        y = self.y if out is None else out
         self.ep.dispatch(x, ids, T, stream=stream)
-        xr, offs = self.ep.recv_ptr, self.ep.offsets_ptr
-        if self.fused:
-            grouped_matmul(self.types[0], self.gu_tab, offs, xr, self.gu_out, self.el, cap, 2 * F, H, mean,
-                           stream=stream)
-            silu_mul(self.h, self.gu_out, self.gu_out.data_ptr() + 4 * F, F, rows=cap, ld=2 * F, stream=stream)
-        else:
-            grouped_matmul(self.types[0], self.g_tab, offs, xr, self.h, self.el, cap, F, H, mean, stream=stream)
-            grouped_matmul(self.types[1], self.u_tab, offs, xr, self.gu_out, self.el, cap, F, H, mean,
-                           stream=stream)
-            silu_mul(self.h, self.h, self.gu_out, F, rows=cap, ld=F, stream=stream)
-        grouped_matmul(self.types[2], self.d_tab, offs, self.h, self.y_recv, self.el, cap, H, F, mean,
-                       stream=stream)
+        self.experts(T, peer_tokens, stream=stream)
         acc = False
         if self.shared is not None:
-            self._shared_ffn(x, T, stream)
+            self._shared_ffn(x, T, y, stream)
             acc = True
-        self.ep.combine(self.y_recv, w, self.y, accumulate=acc, stream=stream)
-        return self.y[:T]
+        self.ep.combine(self.y_recv, w, y, accumulate=acc, stream=stream)
+        return y[:T]

@@ -331,3 +331,28 @@ def test_moe_ffn_graph(cuda):
     assert torch.equal(moe.y[:T], eager)
     del graph
     moe.ep.close()
+
+
+@pytest.mark.parametrize("t,N,mean", [(synth.Q4_K, 512, 1), (synth.Q4_K, 300, 32), (synth.Q6_K, 256, 32),
+                                      (synth.Q4_0, 384, 40)])
+def test_grouped_matmul_stacked(cuda, t, N, mean):
+    """Experts stacked in one tensor (expert e at rows e*N ..) give the same
+    bits as the same matrices behind a pointer table, in both forms (for the
+    tensor-core form: one tensor-map box per stage against one copy per row;
+    a ragged N reads past an expert's last row and must mask it)."""
+    import swq
+    E, K = 5, 2048
+    Ws = [synth.random_blocks(t, N, K, seed=800 + e) for e in range(E)]
+    W_all = torch.from_numpy(np.concatenate([w.reshape(-1) for w in Ws])).cuda()
+    dW = [torch.from_numpy(w.reshape(-1)).cuda() for w in Ws]
+    tab = torch.tensor([d.data_ptr() for d in dW], dtype=torch.int64, device="cuda")
+    counts = [mean, 0, 2 * mean + 1, mean + 5, 3]
+    offs = torch.tensor(np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)).cuda()
+    R = int(sum(counts))
+    X = torch.from_numpy(synth.random_activations(R, K, seed=81)).cuda()
+    Y1 = torch.empty(R, N, device="cuda")
+    Y2 = torch.empty(R, N, device="cuda")
+    swq.grouped_matmul(t, tab, offs, X, Y1, E, R, N, K, mean)
+    swq.grouped_matmul_stacked(t, W_all, offs, X, Y2, E, R, N, K, mean)
+    swq.check()
+    assert torch.equal(Y1, Y2)
