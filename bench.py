@@ -511,6 +511,7 @@ def run_swq(args, rank: int, world: int) -> None:
             "decode": None,
             "decode_70b": None,
             "moe": None,
+            "moe_decode": None,
         }
     del graph, graph1
 
@@ -546,6 +547,10 @@ def run_swq(args, rank: int, world: int) -> None:
         moe = run_moe(rank, world)
         if line is not None:
             line["moe"] = moe
+        log("gemv: MoE decoder next")
+        moe_dec = run_decode_moe(rank, world)
+        if line is not None:
+            line["moe_decode"] = moe_dec
     timer.cancel()
     if dist:
         dist.barrier()
@@ -690,6 +695,71 @@ def run_decode(rank: int, world: int, batches=(1, 16), prefill: int = 512, steps
         if dec is not first:
             del dec
             torch.cuda.empty_cache()
+    return out
+
+
+def run_decode_moe(rank: int, world: int, B: int = 32, prefill: int = 1024, steps: int = 64,
+                   warmup: int = 4) -> dict:
+    """The MoE decoder (40 layers, hidden 2048, 16/4 heads of 128, 256 experts
+    of 512 top-8 + a shared expert of 512, Q4_K experts, vocab 151936,
+    synthetic weights generated on the device), experts sharded over the
+    ranks and each rank decoding its own rows with the whole attention: a
+    `prefill`-token prompt prefilled at batch 1 (timed), then `B` rows sharing
+    its K/V decode `steps` graph-replayed greedy steps.  tok/s of all ranks
+    (max time over ranks)."""
+    import numpy as np
+    import torch
+
+    from swq.model import LlamaConfig, LlamaDecoder
+
+    cfg = LlamaConfig.moe_40l(max_seq=prefill + steps + warmup + 8)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    grp = dist.group.WORLD if dist else None
+    log(f"decode_moe: building (experts over {world} ranks)")
+    one = LlamaDecoder(cfg, rows=1, seed=3, ep_group=grp, moe_max_tokens=prefill)
+    toks = [((np.arange(prefill) * 7919 + 13 * rank) % cfg.vocab).tolist()]
+    one.prefill(toks)  # warm-up of the prefill path (same calls on every rank)
+    one.stream.synchronize()
+    if dist:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(one.stream)
+    one.prefill(toks)
+    ev1.record(one.stream)
+    ev1.synchronize()
+    pf_ms = ev0.elapsed_time(ev1)
+    dec = LlamaDecoder(cfg, rows=B, weights_from=one)
+    dec.reset(list(range(B)), 0)
+    dec.capture()
+    ctx = _build_context(dec, prefill, seed=5, share_from=one)
+    dec.generate(warmup)
+    dec.stream.synchronize()
+    if dist:
+        dist.barrier()
+    ev0.record(dec.stream)
+    dec.generate(steps)
+    ev1.record(dec.stream)
+    ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms, pf_ms], dtype=torch.float64, device=dec.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, pf_ms = float(t[0].item()), float(t[1].item())
+    import swq
+    swq.check(dec.stream)
+    ok = bool(torch.isfinite(dec.logits).all().item())
+    out = {"model": "MoE decoder: 40 layers, hidden 2048, 16/4 heads of 128, 256 experts x 512 top-8 + shared 512, "
+                    "Q4_K experts, vocab 151936, synthetic weights", "expert_parallel": world,
+           "prefill": {"tokens_per_rank": prefill, "ms": round(pf_ms, 2),
+                       "tok_s": round(world * prefill / (pf_ms * 1e-3), 1)},
+           "decode": {"batch_per_rank": B, "steps": steps, "ms_per_step": round(ms / steps, 3),
+                      "tok_s": round(world * B * steps / (ms * 1e-3), 1), "finite_logits": ok, **ctx}}
+    dec.graph = None
+    del dec, one
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
     return out
 
 
@@ -1157,6 +1227,8 @@ def main() -> None:
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                     device_id=torch.device("cuda", local))
         d = run_moe(rank, world, steps=args.steps if args.steps != ap.get_default("steps") else 20)
+        if args.decode:
+            d["decoder"] = run_decode_moe(rank, world)
         if rank == 0:
             lay = d.get("decode_32", {}).get("layer", {})
             print(json.dumps({"metric": "MoE layer tok/s (decode batch 32 per GPU, 256 experts top-8, Q4_K)",

@@ -136,6 +136,9 @@ class RefLlama:
                 att[h * hd:(h + 1) * hd] = (p @ vs).astype(F32)
             x = (x + matmul(t["wo"], L["wo"], att, c.dim, q_dim)).astype(F32)
             xb = rmsnorm(x, L["ffn_norm"], c.eps)
+            if "router" in L:
+                x = (x + self._moe(L, t, xb)).astype(F32)
+                continue
             g = matmul(t["w_gate"], L["w_gate"], xb, c.ffn, c.dim)
             u = matmul(t["w_up"], L["w_up"], xb, c.ffn, c.dim)
             with np.errstate(over="ignore"):  # exp(-g) = inf for very negative g: silu -> -0, as expf
@@ -143,3 +146,34 @@ class RefLlama:
             x = (x + matmul(t["w_down"], L["w_down"], hmid, c.dim, c.ffn)).astype(F32)
         x = rmsnorm(x, W["output_norm"], c.eps)
         return matmul(c.types["output"], W["output"], x, c.vocab, c.dim)
+
+    def _swiglu(self, tg, gb, tu, ub, td, db, xb, f):
+        c = self.cfg
+        g = matmul(tg, gb, xb, f, c.dim)
+        u = matmul(tu, ub, xb, f, c.dim)
+        with np.errstate(over="ignore"):
+            h = (g / (F32(1.0) + np.exp(-g)) * u).astype(F32)
+        return matmul(td, db, h, c.dim, f)
+
+    def _moe(self, L, t, xb):
+        """MoE FFN (no counterpart in the reference, whose FFN is dense): fp32
+        router logits, the top_k experts with softmax weights over their
+        logits (oracle/moe_oracle.c), each a SwiGLU FFN, summed in slot order
+        onto the shared expert's output."""
+        from . import moe_router_logits, moe_topk_softmax
+        c = self.cfg
+        E, F, Fs = c.n_experts, c.expert_ffn, c.shared_ffn
+        logits = moe_router_logits(L["router"], xb[None]).astype(F32)
+        ids, w = moe_topk_softmax(logits, c.top_k)
+        self.last_ids = ids[0]
+        y = np.zeros(c.dim, F32)
+        if Fs:
+            y = self._swiglu(t["w_gate_shexp"], L["w_gate_shexp"], t["w_up_shexp"], L["w_up_shexp"],
+                             t["w_down_shexp"], L["w_down_shexp"], xb, Fs).astype(F32)
+        parts = {nm: np.asarray(L[nm]).reshape(E, -1) for nm in ("w_gate_exps", "w_up_exps", "w_down_exps")}
+        for j in range(c.top_k):
+            e = int(ids[0, j])
+            out = self._swiglu(t["w_gate_exps"], parts["w_gate_exps"][e], t["w_up_exps"], parts["w_up_exps"][e],
+                               t["w_down_exps"], parts["w_down_exps"][e], xb, F)
+            y = (y + w[0, j] * out).astype(F32)
+        return y

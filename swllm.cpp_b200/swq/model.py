@@ -61,12 +61,35 @@ class LlamaConfig:
     # layers (a GGUF Q4_K_M file keeps attn_v / ffn_down in Q6_K on some
     # layers only); None: every layer has `types`
     layer_types: tuple | None = None
+    # mixture of experts (0: the dense FFN above): n_experts routed experts of
+    # intermediate expert_ffn, top_k per token (softmax over the k router
+    # logits), plus a shared expert of shared_ffn (0: none); expert types in
+    # types["w_{gate,up,down}_exps"] and types["w_{gate,up,down}_shexp"]
+    n_experts: int = 0
+    top_k: int = 0
+    expert_ffn: int = 0
+    shared_ffn: int = 0
 
     @classmethod
     def llama3_70b(cls, **kw) -> "LlamaConfig":
         """Llama-3-70B shape: 80 layers, hidden 8192, 64 query / 8 kv heads of
         128, FFN 28672, vocab 128256."""
         return cls(n_layers=80, dim=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn=28672, vocab=128256, **kw)
+
+    @classmethod
+    def moe_40l(cls, **kw) -> "LlamaConfig":
+        """The MoE decoder shape: 40 layers, hidden 2048, 16 query / 4 kv heads
+        of 128, 256 routed experts of intermediate 512 with top-8 routing and
+        one shared expert of 512 (experts in Q4_K), vocab 151936."""
+        types = {"wq": Q4_K, "wk": Q4_K, "wv": Q6_K, "wo": Q4_K, "output": Q6_K,
+                 "w_gate_exps": Q4_K, "w_up_exps": Q4_K, "w_down_exps": Q4_K,
+                 "w_gate_shexp": Q4_K, "w_up_shexp": Q4_K, "w_down_shexp": Q4_K}
+        return cls(n_layers=40, dim=2048, n_heads=16, n_kv_heads=4, head_dim=128, ffn=512, vocab=151936,
+                   theta=1e6, types=types, n_experts=256, top_k=8, expert_ffn=512, shared_ffn=512, **kw)
+
+    @property
+    def is_moe(self) -> bool:
+        return self.n_experts > 0
 
     @property
     def q_dim(self) -> int:
@@ -77,22 +100,42 @@ class LlamaConfig:
         return self.n_kv_heads * self.head_dim
 
     def shapes(self) -> dict:
-        """name -> (N rows, K columns) of every quantized matrix of a layer."""
-        return {"wq": (self.q_dim, self.dim), "wk": (self.kv_dim, self.dim), "wv": (self.kv_dim, self.dim),
-                "wo": (self.dim, self.q_dim), "w_gate": (self.ffn, self.dim), "w_up": (self.ffn, self.dim),
-                "w_down": (self.dim, self.ffn)}
+        """name -> (N rows, K columns) of every quantized matrix of a layer
+        (for a MoE layer: the attention matrices; the experts are moe_shapes)."""
+        att = {"wq": (self.q_dim, self.dim), "wk": (self.kv_dim, self.dim), "wv": (self.kv_dim, self.dim),
+               "wo": (self.dim, self.q_dim)}
+        if self.is_moe:
+            return att
+        return dict(att, w_gate=(self.ffn, self.dim), w_up=(self.ffn, self.dim), w_down=(self.dim, self.ffn))
+
+    def moe_shapes(self) -> dict:
+        """name -> (N rows, K columns) of one expert's matrices (routed, then shared)."""
+        F, Fs, H = self.expert_ffn, self.shared_ffn, self.dim
+        return {"w_gate_exps": (F, H), "w_up_exps": (F, H), "w_down_exps": (H, F),
+                "w_gate_shexp": (Fs, H), "w_up_shexp": (Fs, H), "w_down_shexp": (H, Fs)}
 
     def layer_type_map(self, layer: int) -> dict:
-        """GGML type of each of layer `layer`'s seven matrices."""
+        """GGML type of each of layer `layer`'s matrices."""
         if self.layer_types:
             return self.layer_types[layer]
-        return {k: self.types[k] for k in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down")}
+        names = list(self.shapes()) + (list(self.moe_shapes()) if self.is_moe else [])
+        return {k: self.types[k] for k in names}
 
     def weight_bytes_per_token(self) -> int:
-        """Quantized weight bytes one decode step reads (all layers + LM head)."""
+        """Quantized weight bytes one decode step reads (all layers + LM head;
+        for a MoE model the attention, shared experts and LM head, without the
+        routed experts, whose share depends on the routing)."""
         per_layer = [sum(n * row_bytes(self.layer_type_map(li)[k], kk) for k, (n, kk) in self.shapes().items())
                      for li in range(self.n_layers)]
+        if self.is_moe and self.shared_ffn:
+            per_layer = [b + sum(n * row_bytes(self.types[k], kk) for k, (n, kk) in self.moe_shapes().items()
+                                 if k.endswith("shexp")) for b in per_layer]
         return sum(per_layer) + self.vocab * row_bytes(self.types["output"], self.dim)
+
+    def expert_bytes(self) -> int:
+        """Bytes of one routed expert's three matrices."""
+        return sum(n * row_bytes(self.types[k], kk) for k, (n, kk) in self.moe_shapes().items()
+                   if k.endswith("exps"))
 
 
 def rope_freqs(cfg: LlamaConfig) -> np.ndarray:
@@ -150,7 +193,7 @@ def _shard(host, type_id: int, N: int, K: int, rows: tuple[int, int] | None, col
 class LlamaDecoder:
     def __init__(self, cfg: LlamaConfig, rows: int = 1, device="cuda", seed: int = 0, weights: dict | None = None,
                  max_steps: int = 4096, group=None, weights_from: "LlamaDecoder | None" = None,
-                 collective: str = "peer", fuse: tuple | str = "auto"):
+                 collective: str = "peer", fuse: tuple | str = "auto", ep_group=None, moe_max_tokens: int = 0):
         """weights: None for synthetic weights, else host arrays: 'token_embd'
         [vocab, dim] fp32 (or (GGML type, blocks)), 'output_norm' [dim], 'output'
         blocks, and per layer 'layers'[l] with 'attn_norm', 'ffn_norm' [dim]
@@ -168,11 +211,25 @@ class LlamaDecoder:
         the tensor-core GEMM serves them (one CTA per row converts the
         activations), nothing on the GEMV path (every GEMV CTA would repeat
         the whole row's transform; measured slower), SwiGLU never (slower on
-        both paths)."""
+        both paths).
+
+        A MoE config (cfg.n_experts > 0) runs each layer's FFN as swq.moe.MoEFFN:
+        routed experts (expert-parallel over ep_group: every rank decodes its
+        own rows with the whole attention, and the experts are sharded), plus
+        the shared expert.  Host weights of a MoE layer: 'router' [n_experts,
+        dim] fp32 and the blocks of w_{gate,up,down}_exps (the experts stacked,
+        expert e at rows e*N ..) and w_{gate,up,down}_shexp.  moe_max_tokens:
+        rows per MoE call (prefill runs in chunks of it; default max(rows,
+        512)); every rank of ep_group must make the same calls (same rows and
+        prompt lengths)."""
         import torch
         from .parallel import _world
         self.cfg, self.rows, self.device = cfg, rows, torch.device(device)
         self.group = group
+        if cfg.is_moe and group is not None:
+            raise ValueError("a MoE decoder runs its attention per rank: shard the experts with ep_group")
+        self.ep_group = ep_group
+        self.moe_max_tokens = int(moe_max_tokens) or max(rows, 512)
         self.rank, self.world = _world(group) if group is not None else (0, 1)
         G, r = self.world, self.rank
         for what, n in (("query heads", cfg.n_heads), ("kv heads", cfg.n_kv_heads), ("ffn", cfg.ffn),
@@ -207,8 +264,11 @@ class LlamaDecoder:
         if weights_from is not None:
             if weights_from.cfg != cfg or weights_from.world != G:
                 raise ValueError("weights_from must have the same config and group size")
-            for name in ("token_embd", "output_norm", "output", "fuse_gate_up", "fuse_qk", "layers", "freqs"):
-                setattr(self, name, getattr(weights_from, name))
+            for name in ("token_embd", "output_norm", "output", "fuse_gate_up", "fuse_qk", "layers", "freqs",
+                         "moe_base"):
+                setattr(self, name, getattr(weights_from, name, None))
+            if self.moe_base is not None:
+                self.moe_max_tokens = self.moe_base.max_tokens
         else:
             self._load_weights(cfg, W, weights, blocks, g, f32)
         self._alloc_state(cfg, rows, max_steps, f32)
@@ -216,7 +276,9 @@ class LlamaDecoder:
             raise ValueError(f"collective must be 'peer' or 'nccl', not {collective!r}")
         self.collective = collective
         if fuse == "auto":
-            fuse = ("rmsnorm",) if rows >= get_option(OPT_TENSOR_CORE_MIN_M) else ()
+            fuse = ("rmsnorm",) if rows >= get_option(OPT_TENSOR_CORE_MIN_M) and not cfg.is_moe else ()
+        if cfg.is_moe and fuse:
+            raise ValueError("a MoE decoder runs its norms as their own pass (fuse=())")
         if not set(fuse) <= {"rmsnorm", "swiglu"}:
             raise ValueError(f"fuse takes 'rmsnorm' and 'swiglu', not {fuse!r}")
         self.fuse = tuple(fuse)
@@ -263,7 +325,7 @@ class LlamaDecoder:
                             else 1.0 + 0.01 * torch.randn(cfg.dim, generator=g, **f32))
         self.output = blocks("output", cfg.vocab, cfg.dim, W.get("output"), t["output"])
         lts = [cfg.layer_type_map(layer) for layer in range(cfg.n_layers)]
-        self.fuse_gate_up = all(lt["w_gate"] == lt["w_up"] for lt in lts)
+        self.fuse_gate_up = all(lt.get("w_gate") == lt.get("w_up") for lt in lts)
         self.fuse_qk = all(lt["wq"] == lt["wk"] for lt in lts)
         self.layers = []
         for layer, lt in enumerate(lts):
@@ -284,12 +346,56 @@ class LlamaDecoder:
             for name in ("q_norm", "k_norm"):
                 if lw.get(name) is not None:
                     L[name] = _upload(np.ascontiguousarray(lw[name], np.float32), dev)
-            if lt["w_gate"] == lt["w_up"]:  # rows of gate then rows of up: one GEMV
+            if cfg.is_moe:
+                L["moe"] = self._moe_layer(cfg, lt, lw if weights else None, layer)
+            elif lt["w_gate"] == lt["w_up"]:  # rows of gate then rows of up: one GEMV
                 L["w_gate_up"] = torch.cat([L.pop("w_gate"), L.pop("w_up")])
             if lt["wq"] == lt["wk"]:  # rows of q then rows of k
                 L["w_qk"] = torch.cat([L.pop("wq"), L.pop("wk")])
             self.layers.append(L)
         self.freqs = torch.from_numpy(rope_freqs(cfg)).to(dev)
+
+    def _moe_layer(self, cfg, lt, lw, layer):
+        """The MoE FFN of one layer: host weights (lw) or synthetic blocks
+        generated on the device (this rank's experts from a rank-dependent
+        seed; the router and the shared expert the same on every rank)."""
+        import torch
+        from .moe import MoEFFN, _group_rank_world
+        from .synth import row_bytes
+        dev, H, F, E, k = self.device, cfg.dim, cfg.expert_ffn, cfg.n_experts, cfg.top_k
+        types = (lt["w_gate_exps"], lt["w_up_exps"], lt["w_down_exps"])
+        stypes = (lt["w_gate_shexp"], lt["w_up_shexp"], lt["w_down_shexp"]) if cfg.shared_ffn else None
+        base = getattr(self, "moe_base", None)
+        kw = dict(group=self.ep_group, device=dev, scratch_from=base, shared_types=stypes, shared_F=cfg.shared_ffn)
+        if lw is not None:
+            def split(name, n, kk):
+                b = np.asarray(lw[name]).reshape(E, n * row_bytes(lt[name], kk))
+                return [b[e] for e in range(E)]
+            gs, us, ds = (split(nm, *cfg.moe_shapes()[nm]) for nm in ("w_gate_exps", "w_up_exps", "w_down_exps"))
+            shared = tuple(np.asarray(lw[nm]) for nm in ("w_gate_shexp", "w_up_shexp", "w_down_shexp")) \
+                if cfg.shared_ffn else None
+            moe = MoEFFN(list(zip(gs, us, ds)), types, H, F, np.asarray(lw["router"], np.float32), k,
+                         self.moe_max_tokens, shared=shared, **kw)
+        else:
+            ep_rank, ep_world = _group_rank_world(self.ep_group) if self.ep_group is not None else (0, 1)
+            el = E // ep_world
+            ge = torch.Generator(device=dev)
+            ge.manual_seed(7919 * (layer + 1) + 104729 * ep_rank)
+            gu_all = synthetic_blocks(types[0], el * 2 * F, H, ge, dev)
+            d_all = synthetic_blocks(types[2], el * H, F, ge, dev)
+            gr = torch.Generator(device=dev)
+            gr.manual_seed(15485863 + layer)
+            router = torch.randn(E, H, generator=gr, device=dev) * 0.02
+            shared = None
+            if cfg.shared_ffn:
+                Fs = cfg.shared_ffn
+                shared = (synthetic_blocks(stypes[0], Fs, H, gr, dev), synthetic_blocks(stypes[1], Fs, H, gr, dev),
+                          synthetic_blocks(stypes[2], H, Fs, gr, dev))
+            moe = MoEFFN(None, types, H, F, router, k, self.moe_max_tokens, shared=shared, n_experts=E,
+                         device_blocks=(gu_all, d_all), **kw)
+        if base is None:
+            self.moe_base = moe
+        return moe
 
     def _alloc_state(self, cfg, rows, max_steps, f32):
         import torch
@@ -404,14 +510,18 @@ class LlamaDecoder:
             else:
                 add_rmsnorm(xb, x, d, L["ffn_norm"], c.dim, c.eps, B, stream=s)  # x += o; xb = norm(x)
                 src, a_in, a_g = xb, {}, {}
-            if "w_gate_up" in L:
+            if "moe" in L:  # routed experts + shared expert of norm(x) into d
+                L["moe"](xb, B, out=d, peer_tokens=B, stream=s)
+            elif "w_gate_up" in L:
                 gemm(t["w_gate"], L["w_gate_up"], src, self.gu, B, 2 * ffn, c.dim, stream=s, **a_g)
             else:
                 gemm(t["w_gate"], L["w_gate"], src, self.h, B, ffn, c.dim, stream=s, **a_g)
                 self.gu[:, :ffn].copy_(self.h)
                 gemm(t["w_up"], L["w_up"], src, self.h, B, ffn, c.dim, stream=s, **a_in)
                 self.gu[:, ffn:].copy_(self.h)
-            if fuse_glu:
+            if "moe" in L:
+                pass
+            elif fuse_glu:
                 gemm(t["w_down"], L["w_down"], self.gu, d, B, c.dim, ffn, stream=s, kind=ACT_SWIGLU, ld=2 * ffn)
             else:
                 silu_mul(self.h, self.gu, self.gu[:, ffn:], ffn, B, 2 * ffn, stream=s)
@@ -504,15 +614,21 @@ class LlamaDecoder:
                 if tp:
                     self._nccl_all_reduce(d)
                 add_rmsnorm(xn, x, d, L["ffn_norm"], c.dim, c.eps, M, stream=s)  # x += o; xn = norm(x)
-                if "w_gate_up" in L:
-                    gemm(t["w_gate"], L["w_gate_up"], xn, gu, M, 2 * ffn, c.dim, s)
+                if "moe" in L:  # in chunks of moe_max_tokens rows, the same on every rank
+                    ch = self.moe_max_tokens
+                    for r0 in range(0, M, ch):
+                        r1 = min(M, r0 + ch)
+                        L["moe"](xn[r0:r1], r1 - r0, out=d[r0:r1], peer_tokens=r1 - r0, stream=s)
                 else:
-                    gemm(t["w_gate"], L["w_gate"], xn, h, M, ffn, c.dim, s)
-                    gu[:, :ffn].copy_(h)
-                    gemm(t["w_up"], L["w_up"], xn, h, M, ffn, c.dim, s)
-                    gu[:, ffn:].copy_(h)
-                silu_mul(h, gu, gu[:, ffn:], ffn, M, 2 * ffn, stream=s)
-                gemm(t["w_down"], L["w_down"], h, d, M, c.dim, ffn, s)
+                    if "w_gate_up" in L:
+                        gemm(t["w_gate"], L["w_gate_up"], xn, gu, M, 2 * ffn, c.dim, s)
+                    else:
+                        gemm(t["w_gate"], L["w_gate"], xn, h, M, ffn, c.dim, s)
+                        gu[:, :ffn].copy_(h)
+                        gemm(t["w_up"], L["w_up"], xn, h, M, ffn, c.dim, s)
+                        gu[:, ffn:].copy_(h)
+                    silu_mul(h, gu, gu[:, ffn:], ffn, M, 2 * ffn, stream=s)
+                    gemm(t["w_down"], L["w_down"], h, d, M, c.dim, ffn, s)
                 if tp:
                     self._nccl_all_reduce(d)
                 if li + 1 < len(self.layers):

@@ -32,18 +32,18 @@ HANDLE_BYTES = 64
 
 
 def _group_rank_world(group):
-    try:
-        import torch.distributed as dist
-        if dist.is_available() and dist.is_initialized():
-            return dist.get_rank(group), dist.get_world_size(group)
-    except Exception:  # noqa: BLE001 -- no torch.distributed
-        pass
-    return 0, 1
+    """(rank, size) of `group`; None is this process alone, whatever process
+    groups exist."""
+    if group is None:
+        return 0, 1
+    import torch.distributed as dist
+    return dist.get_rank(group), dist.get_world_size(group)
 
 
 class ExpertParallel:
     """swq_ep_* of this rank: at most max_tokens tokens per call, top_k slots
-    each, n_experts split evenly over the group, hidden size H."""
+    each, n_experts split evenly over `group` (None: this process alone),
+    hidden size H."""
 
     def __init__(self, max_tokens: int, top_k: int, n_experts: int, hidden: int, group=None, device=None):
         import torch
@@ -115,7 +115,8 @@ def _to_dev(a, device):
 
 
 class MoEFFN:
-    """SwiGLU mixture-of-experts FFN, experts sharded over `group`.
+    """SwiGLU mixture-of-experts FFN, experts sharded over `group` (None: all
+    experts in this process).
 
     experts: n_experts triples (gate [F x H], up [F x H], down [H x F]) of GGUF
       block arrays (numpy or torch uint8); only this rank's are read (the

@@ -273,7 +273,8 @@ def _ep_rank(rank, world, port, path):
             T = Ts[rank]
             x, experts, router = _ep_inputs(rank, T)
             moe = MoEFFN([e if (i // (EP_E // world)) == rank else None for i, e in enumerate(experts)],
-                         (swq.Q4_K, swq.Q4_K, swq.Q6_K), EP_H, EP_F, router, EP_K, max_tokens=64)
+                         (swq.Q4_K, swq.Q4_K, swq.Q6_K), EP_H, EP_F, router, EP_K, max_tokens=64,
+                         group=dist.group.WORLD)
             xd = torch.from_numpy(x).cuda()
             for rep in range(2):
                 dist.barrier()  # launch within the 50 ms bound of each other

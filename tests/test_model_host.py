@@ -277,3 +277,55 @@ def test_tensor_parallel_bias_slices(calls, monkeypatch, tmp_path, rank):
     for li, L in enumerate(dec.layers):
         for key, n in (("bq", dec.q_dim), ("bk", dec.kv_dim), ("bv", dec.kv_dim)):
             assert np.array_equal(L[key].numpy(), W["layers"][li][key][rank * n:(rank + 1) * n])
+
+
+# ---------------------------------------------------------------- MoE decoder wiring
+class _FakeMoE:
+    """Records MoEFFN construction and calls (no device work)."""
+    made = []
+
+    def __init__(self, experts, types, H, F, router_w, top_k, max_tokens, **kw):
+        self.args = dict(experts=experts, types=types, H=H, F=F, router=router_w, k=top_k, max_tokens=max_tokens, **kw)
+        self.max_tokens = max_tokens
+        self.calls = []
+        _FakeMoE.made.append(self)
+
+    def __call__(self, x, T, out=None, peer_tokens=None, stream=None):
+        self.calls.append((x, T, out, peer_tokens))
+
+
+def test_moe_decoder_wiring(calls, monkeypatch):
+    import swq.moe
+    from test_gpu_moe_model import _cfg, _weights
+    _FakeMoE.made = []
+    monkeypatch.setattr(swq.moe, "MoEFFN", _FakeMoE)
+    cfg = _cfg()
+    W = _weights(cfg, seed=2)
+    dec = M.LlamaDecoder(cfg, rows=3, device="cpu", weights=W, moe_max_tokens=4)
+    assert len(_FakeMoE.made) == cfg.n_layers
+    first = _FakeMoE.made[0]
+    for li, m in enumerate(_FakeMoE.made):
+        a = m.args
+        assert a["k"] == cfg.top_k and a["F"] == cfg.expert_ffn and a["max_tokens"] == 4
+        assert a["scratch_from"] is (None if li == 0 else first)  # one set of buffers for all layers
+        assert a["group"] is None and a["shared_F"] == cfg.shared_ffn
+        assert len(a["experts"]) == cfg.n_experts
+        np.testing.assert_array_equal(a["router"], W["layers"][li]["router"])
+        e3 = np.asarray(W["layers"][li]["w_down_exps"]).reshape(cfg.n_experts, -1)[3]
+        assert np.array_equal(a["experts"][3][2], e3)
+    dec.step()
+    g = _gemms(calls)
+    # per layer: q|k, v, o -- no dense FFN projection -- then the LM head
+    assert len(g) == 3 * cfg.n_layers + 1
+    for li, m in enumerate(_FakeMoE.made):
+        assert len(m.calls) == 1
+        x, T, out, pt = m.calls[0]
+        assert T == 3 and pt == 3 and out is dec.xb and x is dec.xn
+    # prefill: rows x P = 3 x 3 = 9 rows in MoE calls of at most 4 rows
+    for m in _FakeMoE.made:
+        m.calls.clear()
+    dec.prefill([[1, 2, 3], [4, 5, 6], [7, 8, 9]])
+    for m in _FakeMoE.made:
+        assert [c[1] for c in m.calls] == [4, 4, 1] and [c[3] for c in m.calls] == [4, 4, 1]
+    with pytest.raises(ValueError):
+        M.LlamaDecoder(cfg, rows=1, device="cpu", weights=W, group=object())
