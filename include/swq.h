@@ -352,7 +352,9 @@ enum {
     SWQ_OPT_GEMV_STAGE_KB = 7,
     /* GEMV CTAs per SM (0, the default: automatic; 1..4 forces it).  More
      * than one puts more consumer warps on each SM, each CTA with its share
-     * of the SM's shared memory. */
+     * of the SM's shared memory (the Q4_K tensor-core form runs 3 or 4 with
+     * CTAs of 8 consumer warps instead of 16: more independent GEMVs in
+     * flight at once, a longer single GEMV). */
     SWQ_OPT_GEMV_CTAS_PER_SM = 8,
     /* 1 (default): the GEMV kernel keeps the activations in fp32, as the
      * reference does: each quant value becomes an exact float and the dot
@@ -363,11 +365,13 @@ enum {
     SWQ_OPT_GEMV_FP32_ACT = 9,
     /* Single-row GEMVs whose sub-block dot products are computed exactly in
      * integers on the tensor cores: quant values are exact small integers, x
-     * is held per 16- or 32-element sub-block as a 30-bit fixed-point number
-     * (four 8-bit limbs), the sub-block results are scaled and summed in
-     * fp32.  K a multiple of 256 up to 16384 (Q6_K: of 2048).  1 (default):
-     * Q6_K, where it is the faster form on B200; 2: Q4_K as well; 0: neither
-     * (the fp32 form of SWQ_OPT_GEMV_FP32_ACT). */
+     * is held as a 30-bit fixed-point number (four 8-bit limbs), the integer
+     * sums are scaled and summed in fp32.  1: Q6_K (fixed point per 16-element
+     * sub-block, K a multiple of 2048 up to 16384); 2 (default): Q4_K as well
+     * (fixed point per 256-element super-block, the 6-bit sub-block scales
+     * applied in integers, one conversion per super-block; K a multiple of 512
+     * up to 8192, activation prologues included); 0: neither (the fp32 form
+     * of SWQ_OPT_GEMV_FP32_ACT). */
     SWQ_OPT_GEMV_INT_MMA = 10
 };
 swq_status swq_set_option(int option, int value);

@@ -37,7 +37,7 @@ std::atomic<int> g_opt_gemv_smem_kb{0};
 std::atomic<int> g_opt_gemv_stage_kb{0};
 std::atomic<int> g_opt_gemv_ctas{0};
 std::atomic<int> g_opt_gemv_fp32{1};
-std::atomic<int> g_opt_gemv_imma{1};
+std::atomic<int> g_opt_gemv_imma{2};
 
 swq_status fail(swq_status s, const std::string& msg) {
     g_last_error = msg;
@@ -717,13 +717,16 @@ swq_status swq_check(swq_stream_t stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
-    unsigned a = 0, b = 0, c = 0, d = 0, m = 0;
+    unsigned a = 0, b = 0, c = 0, d = 0, m = 0, a2 = 0, a3 = 0;
     if ((e = swq::status_fetch_gemv(&a, s)) != cudaSuccess ||
+        (e = swq::status_fetch_gemv_imma(&a2, s)) != cudaSuccess ||
+        (e = swq::status_fetch_gemv_q4k(&a3, s)) != cudaSuccess ||
         (e = swq::status_fetch_dequant(&b, s)) != cudaSuccess ||
         (e = swq::status_fetch_gemm_tc(&c, s)) != cudaSuccess ||
         (e = swq::status_fetch_allreduce(&d, s)) != cudaSuccess ||
         (e = swq::status_fetch_moe(&m, s)) != cudaSuccess)
         return cuda_fail(e, "status fetch");
+    a |= a2 | a3;
     if (m & swq::kStatusBadId) {
         char buf[128];
         std::snprintf(buf, sizeof(buf), "an expert id outside [0, n_experts) was left out of the MoE sort "

@@ -596,4 +596,6 @@ cudaError_t gemv_imma_launch(const GemvLaunch& L, cudaStream_t s) {
     }
 }
 
+SWQ_DEFINE_STATUS_FETCH(gemv_imma)
+
 }  // namespace swq

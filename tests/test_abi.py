@@ -125,7 +125,7 @@ def test_options():
     assert swq.get_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER) == 0
     swq.set_option(swq.OPT_Q2K_REFERENCE_CPU_ORDER, 1)
     assert swq.get_option(swq.OPT_GEMV_FP32_ACT) == 1
-    assert swq.get_option(swq.OPT_GEMV_INT_MMA) == 1
+    assert swq.get_option(swq.OPT_GEMV_INT_MMA) == 2
     for opt, bad in ((swq.OPT_GEMV_FP32_ACT, 2), (swq.OPT_GEMV_INT_MMA, 3), (swq.OPT_GEMV_INT_MMA, -1)):
         with pytest.raises(swq.SwqError):
             swq.set_option(opt, bad)

@@ -314,7 +314,7 @@ def test_gemv_forms(cuda, oracle_mod, fp32, int_mma, fmt, N, K):
         got = _gemm_gpu(cuda, t, blocks, X, N, K)
     finally:
         swq.set_option(swq.OPT_GEMV_FP32_ACT, 1)
-        swq.set_option(swq.OPT_GEMV_INT_MMA, 1)
+        swq.set_option(swq.OPT_GEMV_INT_MMA, 2)
     want = oracle_mod.gemm(t, blocks, X, 1, N, K)
     tol = 1e-5 if fp32 else REL_L2_TOL  # fp32 forms: rounding of fp32 sums only
     assert rel_l2(got, want) <= tol
@@ -338,6 +338,6 @@ def test_int_mma_dynamic_range(cuda, oracle_mod, int_mma, fmt):
     try:
         got = _gemm_gpu(cuda, t, blocks, X, N, K)
     finally:
-        swq.set_option(swq.OPT_GEMV_INT_MMA, 1)
+        swq.set_option(swq.OPT_GEMV_INT_MMA, 2)
     want = oracle_mod.gemm(t, blocks, X, 1, N, K)
     assert rel_l2(got, want) <= 1e-5
