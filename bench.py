@@ -38,7 +38,14 @@ import statistics
 import subprocess
 import sys
 import time
-from pathlib import Path
+
+# The result is the one JSON line on stdout; NCCL's log (its "NCCL version"
+# banner included) goes to stderr instead.  A level or file chosen by the
+# caller stands.
+os.environ.setdefault("NCCL_DEBUG", "WARN")
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
+from pathlib import Path  # noqa: E402
 
 REPO = Path(__file__).resolve().parent
 for _p in (str(REPO), str(REPO / "swllm.cpp_b200")):

@@ -18,8 +18,10 @@ ffn_down and the output matrix, Q4_K elsewhere).
 
 Tensor parallelism (one process per GPU, `group` of G ranks): rank r keeps
 query heads [r H/G, (r+1) H/G) and kv heads [r Hkv/G, ...) -- the rows of
-wq, wk, wv -- the same rows of gate and up, columns [r ffn/G, ...) of
-w_down, columns [r H hd/G, ...) of wo, and rows [r V/G, ...) of the LM head.
+wq, wk, wv -- its FFN columns (ffn_split: ffn/G each, or whole 16-byte
+row units when ffn/G columns of w_down are not) as rows of gate and up and
+columns of w_down, columns [r H hd/G, ...) of wo, and rows [r V/G, ...) of the
+LM head.
 Attention is local to the rank's heads; the o and down projections give
 partial sums that one all-reduce each completes; the rank's slice of the
 logits is all-gathered before the argmax.  Every collective is issued on the
@@ -29,6 +31,7 @@ checked against the same model on one rank.
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -179,6 +182,45 @@ def _upload(host: np.ndarray, device):
         return torch.from_numpy(host).to(device)
 
 
+def _align_elems(type_id: int) -> int:
+    """Fewest whole blocks, in elements, whose bytes are a multiple of 16."""
+    qk, bb = LAYOUT[type_id][:2]
+    return (16 // math.gcd(bb, 16)) * qk
+
+
+def ffn_split(cfg: LlamaConfig, world: int) -> list[tuple[int, int]]:
+    """FFN columns [f0, f0 + n) of each tensor-parallel rank: the rows of its
+    gate/up shard and the columns of its w_down shard.
+
+    Even (ffn / world each) when every rank's w_down rows then start on a
+    16-byte boundary, so that the GEMV and GEMM stream them with bulk copies.
+    Otherwise (e.g. Q6_K w_down of the 70B shape over 4 or 8 ranks: 28672 / 8
+    = 3584 columns = 2940 bytes per row) the FFN is split into whole alignment
+    units -- the fewest blocks whose bytes are a multiple of 16, for every
+    layer's w_down type -- as evenly as they go, the first ranks taking one
+    more (28672 over 8: six ranks of 4096, two of 2048).  Falls back to the even
+    split when there are fewer units than ranks."""
+    even = [(r * (cfg.ffn // world), cfg.ffn // world) for r in range(world)]
+    if world == 1 or cfg.is_moe:
+        return even
+    unit = 1
+    for layer in range(cfg.n_layers):
+        a = _align_elems(cfg.layer_type_map(layer)["w_down"])
+        unit = unit * a // math.gcd(unit, a)
+    if (cfg.ffn // world) % unit == 0 or cfg.ffn % unit:
+        return even
+    units = cfg.ffn // unit
+    base, extra = divmod(units, world)
+    if base == 0:
+        return even
+    out, f0 = [], 0
+    for r in range(world):
+        n = (base + (1 if r < extra else 0)) * unit
+        out.append((f0, n))
+        f0 += n
+    return out
+
+
 def _shard(host, type_id: int, N: int, K: int, rows: tuple[int, int] | None, cols: tuple[int, int] | None):
     """Rows [r0, r1) or columns [k0, k1) (whole blocks) of an N x K block matrix."""
     qk, bb = LAYOUT[type_id][:2]
@@ -238,23 +280,26 @@ class LlamaDecoder:
                 raise ValueError(f"{what}={n} does not split over {G} ranks")
         self.nh, self.nkv = cfg.n_heads // G, cfg.n_kv_heads // G
         self.q_dim, self.kv_dim = self.nh * cfg.head_dim, self.nkv * cfg.head_dim
-        self.ffn, self.vocab = cfg.ffn // G, cfg.vocab // G
+        self.ffn_off, self.ffn = ffn_split(cfg, G)[r]
+        self.vocab = cfg.vocab // G
         dev = self.device
         g = torch.Generator(device=dev)
         g.manual_seed(seed + 1000003 * r)
         f32 = dict(dtype=torch.float32, device=dev)
         # local (rows, K) of every matrix, and the slice of the whole matrix it is
-        row_part = {"wq": self.q_dim, "wk": self.kv_dim, "wv": self.kv_dim, "w_gate": self.ffn, "w_up": self.ffn,
-                    "output": self.vocab}
-        col_part = {"wo": self.q_dim, "w_down": self.ffn}
+        # this rank's rows (column-parallel) or columns (row-parallel): (first, count)
+        row_part = {"wq": (r * self.q_dim, self.q_dim), "wk": (r * self.kv_dim, self.kv_dim),
+                    "wv": (r * self.kv_dim, self.kv_dim), "w_gate": (self.ffn_off, self.ffn),
+                    "w_up": (self.ffn_off, self.ffn), "output": (r * self.vocab, self.vocab)}
+        col_part = {"wo": (r * self.q_dim, self.q_dim), "w_down": (self.ffn_off, self.ffn)}
 
         def blocks(name, N, K, host, type_id):
             if name in row_part:
-                n = row_part[name]
-                Nl, Kl, rs, cs = n, K, (r * n, (r + 1) * n), None
+                f, n = row_part[name]
+                Nl, Kl, rs, cs = n, K, (f, f + n), None
             else:
-                k = col_part[name]
-                Nl, Kl, rs, cs = N, k, None, (r * k, (r + 1) * k)
+                f, k = col_part[name]
+                Nl, Kl, rs, cs = N, k, None, (f, f + k)
             if host is not None:
                 part = _shard(host, type_id, N, K, rs, cs) if G > 1 else np.ascontiguousarray(host)
                 return _upload(part.reshape(-1), dev)

@@ -329,3 +329,55 @@ def test_moe_decoder_wiring(calls, monkeypatch):
         assert [c[1] for c in m.calls] == [4, 4, 1] and [c[3] for c in m.calls] == [4, 4, 1]
     with pytest.raises(ValueError):
         M.LlamaDecoder(cfg, rows=1, device="cpu", weights=W, group=object())
+
+
+def test_ffn_split_keeps_down_rows_aligned():
+    """The 70B shape's Q6_K w_down over 4 and 8 ranks: ffn / G columns are
+    2940 or 5880 bytes per row, not a multiple of 16, so the FFN is split in
+    units of 8 Q6_K blocks (2048 columns); over 2 ranks the even split is
+    already aligned and stays."""
+    cfg = M.LlamaConfig.llama3_70b()
+    assert M.ffn_split(cfg, 2) == [(0, 14336), (14336, 14336)]
+    assert M.ffn_split(cfg, 4) == [(0, 8192), (8192, 8192), (16384, 6144), (22528, 6144)]
+    s8 = M.ffn_split(cfg, 8)
+    assert [n for _, n in s8] == [4096] * 6 + [2048] * 2
+    for G in (1, 2, 4, 8):
+        parts = M.ffn_split(cfg, G)
+        assert parts[0][0] == 0 and sum(n for _, n in parts) == cfg.ffn
+        assert all(a + n == b for (a, n), (b, _) in zip(parts, parts[1:]))
+        for _, n in parts:
+            assert (n // 256 * 210) % 16 == 0
+    # every layer's w_down type counts: Q4_K (512) with Q6_K (2048) -> 2048
+    small = M.LlamaConfig(n_layers=2, dim=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=3 * 2048,
+                          types=dict(M.LlamaConfig().types, w_down=synth.Q4_K))
+    assert M.ffn_split(small, 4) == [(r * 1536, 1536) for r in range(4)]  # 1536 / 256 * 144 = 864 = 54 * 16
+
+
+@pytest.mark.parametrize("rank", [0, 3])
+def test_tensor_parallel_uneven_ffn_shards(calls, monkeypatch, rank):
+    """An FFN of 14336 with a Q6_K w_down over 4 ranks: 3584 columns are not
+    a whole 16-byte row unit, so the ranks take 4096, 4096, 4096 and 2048
+    columns; rank r keeps exactly those gate/up rows and w_down columns and
+    sizes its activation buffers to them."""
+    import swq.parallel as P
+    monkeypatch.setattr(P, "_world", lambda group: (rank, 4))
+    cfg = M.LlamaConfig(n_layers=1, dim=256, n_heads=4, n_kv_heads=4, head_dim=64, ffn=14336, vocab=400,
+                        max_seq=16)
+    W = _weights_for(cfg, 11)
+    dec = M.LlamaDecoder(cfg, rows=1, device="cpu", weights=W, group=object(), collective="nccl")
+    f0, n = [(0, 4096), (4096, 4096), (8192, 4096), (12288, 2048)][rank]
+    assert (dec.ffn_off, dec.ffn) == (f0, n)
+    L, lt = dec.layers[0], cfg.layer_type_map(0)
+    qk, bb = synth.block_geometry(lt["w_down"])
+    down = W["layers"][0]["w_down"].reshape(cfg.dim, cfg.ffn // qk, bb)[:, f0 // qk:(f0 + n) // qk]
+    assert np.array_equal(L["w_down"].numpy(), down.reshape(-1))
+    qk, bb = synth.block_geometry(lt["w_gate"])
+    gate = W["layers"][0]["w_gate"].reshape(cfg.ffn, -1)[f0:f0 + n]
+    up = W["layers"][0]["w_up"].reshape(cfg.ffn, -1)[f0:f0 + n]
+    if "w_gate_up" in L:
+        ng = n * synth.row_bytes(lt["w_gate"], cfg.dim)
+        assert np.array_equal(L["w_gate_up"][:ng].numpy(), gate.reshape(-1))
+        assert np.array_equal(L["w_gate_up"][ng:].numpy(), up.reshape(-1))
+    else:
+        assert np.array_equal(L["w_gate"].numpy(), gate.reshape(-1))
+    assert tuple(dec.h.shape) == (1, n) and tuple(dec.gu.shape) == (1, 2 * n)
