@@ -39,11 +39,6 @@ import subprocess
 import sys
 import time
 
-# The result is the one JSON line on stdout; NCCL's log (its "NCCL version"
-# banner included) goes to stderr instead.  A level or file chosen by the
-# caller stands.
-os.environ.setdefault("NCCL_DEBUG", "WARN")
-os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 from pathlib import Path  # noqa: E402
 
@@ -76,6 +71,26 @@ _T0 = time.time()
 
 def log(*a):
     print(f"[{time.time() - _T0:7.1f}s]", *a, file=sys.stderr, flush=True)
+
+
+# The result is the one JSON line on stdout.  Libraries write to stdout too
+# (NCCL's "NCCL version" banner at its default log level), so main() moves
+# file descriptor 1 onto stderr and keeps the original stdout for emit().
+_RESULT_OUT = None
+
+
+def _claim_stdout() -> None:
+    global _RESULT_OUT
+    if _RESULT_OUT is None:
+        sys.stdout.flush()
+        _RESULT_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    """Print the result line on the original stdout."""
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    print(json.dumps(line), file=out, flush=True)
 
 
 def load_peaks() -> tuple[float, str]:
@@ -347,7 +362,7 @@ def run_reference(args, rank: int) -> None:
             "note": "the reference's Model::forward decodes one sequence per call (src/main.cpp), so a batch "
                     "of B sequences takes B calls: its tok/s is the same at every batch size",
             "batches": {"1": dec}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------- GPU arm
@@ -531,7 +546,7 @@ def run_swq(args, rank: int, world: int) -> None:
     def _deadline():
         if line is not None:
             line["decode_timeout"] = f"decode measurements did not finish within {DECODE_DEADLINE_S} s"
-            print(json.dumps(line), flush=True)
+            emit(line)
         log("decode deadline reached; exiting")
         os._exit(0 if line is not None or rank != 0 else 1)
 
@@ -563,7 +578,7 @@ def run_swq(args, rank: int, world: int) -> None:
         dist.barrier()
         dist.destroy_process_group()
     if line is not None:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 # ---------------------------------------------------------------- prefill workload
@@ -1178,7 +1193,7 @@ def run_gemm(args, rank: int, world: int) -> None:
         "clocks": clk.summary(),
         "weight_GBps": round(wbytes / per_call_s / 1e9, 1),
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main() -> None:
@@ -1213,6 +1228,7 @@ def main() -> None:
                     help="decode measurements: context as random K/V (synthetic) or a batched prefill of "
                          "random prompt tokens (prefill, also timed)")
     args = ap.parse_args()
+    _claim_stdout()
     global DECODE_CONTEXT
     DECODE_CONTEXT = args.decode_context
     rank = int(os.environ.get("RANK", "0"))
@@ -1238,10 +1254,9 @@ def main() -> None:
             d["decoder"] = run_decode_moe(rank, world)
         if rank == 0:
             lay = d.get("decode_32", {}).get("layer", {})
-            print(json.dumps({"metric": "MoE layer tok/s (decode batch 32 per GPU, 256 experts top-8, Q4_K)",
-                              "value": lay.get("tok_s"), "unit": "tok/s", "n_gpus": world,
-                              "higher_is_better": True, "scaling": "weak", "data": "synthetic", "moe": d}),
-                  flush=True)
+            emit({"metric": "MoE layer tok/s (decode batch 32 per GPU, 256 experts top-8, Q4_K)",
+                  "value": lay.get("tok_s"), "unit": "tok/s", "n_gpus": world,
+                  "higher_is_better": True, "scaling": "weak", "data": "synthetic", "moe": d})
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
@@ -1254,9 +1269,9 @@ def main() -> None:
         if rank != 0:
             return
         d = run_prefill(rank, prompt=args.M, seventy=args.workload == "prefill70b")
-        print(json.dumps({"metric": f"prefill tok/s ({d['model']}, {args.M}-token prompt)", "value": d["tok_s"],
-                          "unit": "tok/s", "n_gpus": 1, "higher_is_better": True, "data": "synthetic",
-                          "prefill": d}), flush=True)
+        emit({"metric": f"prefill tok/s ({d['model']}, {args.M}-token prompt)", "value": d["tok_s"],
+              "unit": "tok/s", "n_gpus": 1, "higher_is_better": True, "data": "synthetic",
+              "prefill": d})
         return
     if args.workload in ("decode", "decode70b"):
         import torch
@@ -1279,9 +1294,9 @@ def main() -> None:
             name, scaling = f"decode tok/s (Llama-3-70B Q4_K_M, batch 1, tensor-parallel x{world})", "strong"
         if rank == 0:
             b1 = d["batches"]["1"]
-            print(json.dumps({"metric": name, "value": b1["tok_s"],
-                              "unit": "tok/s", "n_gpus": world, "higher_is_better": True, "scaling": scaling,
-                              "data": "synthetic", "decode": d}), flush=True)
+            emit({"metric": name, "value": b1["tok_s"],
+                  "unit": "tok/s", "n_gpus": world, "higher_is_better": True, "scaling": scaling,
+                  "data": "synthetic", "decode": d})
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
