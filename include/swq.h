@@ -366,12 +366,13 @@ enum {
     /* Single-row GEMVs whose sub-block dot products are computed exactly in
      * integers on the tensor cores: quant values are exact small integers, x
      * is held as a 30-bit fixed-point number (four 8-bit limbs), the integer
-     * sums are scaled and summed in fp32.  1: Q6_K (fixed point per 16-element
-     * sub-block, K a multiple of 2048 up to 16384); 2 (default): Q4_K as well
-     * (fixed point per 256-element super-block, the 6-bit sub-block scales
-     * applied in integers, one conversion per super-block; K a multiple of 512
-     * up to 8192, activation prologues included); 0: neither (the fp32 form
-     * of SWQ_OPT_GEMV_FP32_ACT). */
+     * sums are scaled and summed in fp32.  2 (default): Q4_K and Q6_K with x
+     * in fixed point per 256-element super-block and the sub-block scales
+     * applied in integers, one conversion per super-block (Q4_K: K a multiple
+     * of 512 up to 8192; Q6_K: of 2048 up to 16384; activation prologues
+     * included); 1: Q6_K only, in the earlier form (fixed point per
+     * 16-element sub-block, one conversion per sub-block); 0: neither (the
+     * fp32 form of SWQ_OPT_GEMV_FP32_ACT). */
     SWQ_OPT_GEMV_INT_MMA = 10
 };
 swq_status swq_set_option(int option, int value);

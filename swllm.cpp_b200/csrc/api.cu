@@ -720,7 +720,7 @@ swq_status swq_check(swq_stream_t stream) {
     unsigned a = 0, b = 0, c = 0, d = 0, m = 0, a2 = 0, a3 = 0;
     if ((e = swq::status_fetch_gemv(&a, s)) != cudaSuccess ||
         (e = swq::status_fetch_gemv_imma(&a2, s)) != cudaSuccess ||
-        (e = swq::status_fetch_gemv_q4k(&a3, s)) != cudaSuccess ||
+        (e = swq::status_fetch_gemv_kq(&a3, s)) != cudaSuccess ||
         (e = swq::status_fetch_dequant(&b, s)) != cudaSuccess ||
         (e = swq::status_fetch_gemm_tc(&c, s)) != cudaSuccess ||
         (e = swq::status_fetch_allreduce(&d, s)) != cudaSuccess ||

@@ -1017,7 +1017,7 @@ size_t gemv_smem_x_bytes(int type, int MT, int K, bool xf) {
 }
 
 cudaError_t gemv_launch(const GemvLaunch& L, cudaStream_t s) {
-    if (L.imma >= 2 && gemv_q4k_supported(L)) return gemv_q4k_launch(L, s);
+    if (L.imma >= 2 && gemv_kq_supported(L)) return gemv_kq_launch(L, s);
     if (L.imma && gemv_imma_supported(L)) return gemv_imma_launch(L, s);
     switch (L.type) {
         case Q4_0: return launch_fmt<Q4_0>(L, s);

@@ -50,10 +50,10 @@ cudaError_t gemv_launch(const GemvLaunch& L, cudaStream_t s);
 // whether it takes this launch, and the launch.
 bool gemv_imma_supported(const GemvLaunch& L);
 cudaError_t gemv_imma_launch(const GemvLaunch& L, cudaStream_t s);
-// The single-row Q4_K form with integer tensor-core sub-block sums and one
-// conversion per super-block (gemv_q4k.cu; SWQ_OPT_GEMV_INT_MMA >= 2).
-bool gemv_q4k_supported(const GemvLaunch& L);
-cudaError_t gemv_q4k_launch(const GemvLaunch& L, cudaStream_t s);
+// The single-row Q4_K / Q6_K form with integer tensor-core sub-block sums and
+// one conversion per super-block (gemv_kq.cu; SWQ_OPT_GEMV_INT_MMA >= 2).
+bool gemv_kq_supported(const GemvLaunch& L);
+cudaError_t gemv_kq_launch(const GemvLaunch& L, cudaStream_t s);
 // Device status bit of an input a kernel skipped because it was misaligned
 // (DEV_BAD_ALIGN in the device code).
 constexpr unsigned kStatusBadAlign = 32u;
@@ -78,6 +78,6 @@ cudaError_t dequant_launch(int type, const void* src, float* dst, int64_t nblock
 cudaError_t status_fetch_gemv(unsigned* out, cudaStream_t s);
 cudaError_t status_fetch_dequant(unsigned* out, cudaStream_t s);
 cudaError_t status_fetch_gemv_imma(unsigned* out, cudaStream_t s);
-cudaError_t status_fetch_gemv_q4k(unsigned* out, cudaStream_t s);
+cudaError_t status_fetch_gemv_kq(unsigned* out, cudaStream_t s);
 
 }  // namespace swq
