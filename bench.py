@@ -60,10 +60,11 @@ W_BYTES = N_ROWS * (K_COLS // 256) * BLOCK_BYTES              # 9,437,184
 ALG_BYTES = W_BYTES + 4 * K_COLS * M_ROWS + 4 * N_ROWS * M_ROWS  # 9,469,952 per GEMV
 WORKLOAD = (f"Q4_K GEMV N={N_ROWS} K={K_COLS} M={M_ROWS}, {COPIES} rotating weight copies "
             f"({COPIES * W_BYTES / 1e6:.0f} MB)")
-# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_kernel<Q4_K,1,true>
-# launch of this workload, from one ncu capture (profiles/gemv_q4k_4096x4096.md);
-# None until that capture exists.
-NCU_TRAFFIC_PER_LAUNCH = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_kq_kernel<Q4_K, 16>
+# launch of this workload: the mean of three launches of one ncu capture
+# (profiles/gemv_kq_q4k_4096x4096.md: 9,487,104 / 9,486,080 / 9,490,944 read,
+# 0 written).
+NCU_TRAFFIC_PER_LAUNCH = 9488043
 
 
 _T0 = time.time()
@@ -91,6 +92,13 @@ def emit(line: dict) -> None:
     """Print the result line on the original stdout."""
     out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
     print(json.dumps(line), file=out, flush=True)
+
+
+def _gemv_form(fmt: str, M: int) -> str:
+    """The GEMV kernel the library picks for `fmt` at M rows (default options)."""
+    if M == 1 and fmt in ("Q4_K", "Q6_K"):
+        return f"swq::kq::gemv_kq_kernel<{fmt}> (30-bit fixed-point x, exact integer sub-block sums)"
+    return f"swq::gemv_kernel<{fmt},M> (fp32 x, fp32 FMA)"
 
 
 def load_peaks() -> tuple[float, str]:
@@ -510,13 +518,14 @@ def run_swq(args, rank: int, world: int) -> None:
                                 f"{GEMV_STREAMS} streams; consecutive GEMVs of one stream are programmatic "
                                 f"dependents (weights prefetched, x read after the predecessor completes)",
                        "l2": "inputs larger than L2 (rotating weights)",
-                       "arith": "fp32 activations; Q4_K nibbles converted exactly to fp32; fp32 FMA (f32x2), "
-                                "fp32 scales",
+                       "arith": "fp32 activations as 30-bit fixed point per 256-element super-block (4 int8 "
+                                "limbs); exact integer sub-block products (mma.sync u8 x s8 -> s32) scaled by the "
+                                "6-bit scales in int32; one fp32 conversion per super-block, fp32 sums",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": NCU_TRAFFIC_PER_LAUNCH,
-                         "kernel": "swq::gemv_kernel<Q4_K,1,true>", "alg_bytes_per_launch": ALG_BYTES,
+                         "kernel": "swq::kq::gemv_kq_kernel<Q4_K,16>", "alg_bytes_per_launch": ALG_BYTES,
                          "us_per_launch": round(per_launch_s * 1e6, 3),
                          "chain": {"us_per_launch": round(chain_launch_s * 1e6, 3),
                                    "achieved": round(ALG_BYTES / chain_launch_s / 1e9, 1),
@@ -930,7 +939,7 @@ def run_sweep(N: int = 14336, K: int = 4096, launches: int = 40, cpu_seconds: fl
             t_roof = max(nbytes / (hbm * 1e9), flops / (tc * 1e12))
             out["points"].append({
                 "format": name, "M": M, "us": round(sec * 1e6, 2), "GBps": round(gbs, 1), "TFLOPs": round(tfs, 2),
-                "path": "tensor-core GEMM (fp16 operands, fp32 accumulate)" if tc_path else "GEMV (fp32)",
+                "path": "tensor-core GEMM (fp16 operands, fp32 accumulate)" if tc_path else _gemv_form(name, M),
                 "bound": "tensor" if flops / (tc * 1e12) > nbytes / (hbm * 1e9) else "hbm",
                 "roofline_frac": round(t_roof / sec, 4),
                 "cpu_ms": round(cpu_row_s * M * 1e3, 3), "speedup_vs_cpu": round(cpu_row_s * M / sec, 1)})
@@ -1183,7 +1192,7 @@ def run_gemm(args, rank: int, world: int) -> None:
                       "us_per_call": round(per_call_s * 1e6, 2)} if tc_path else
                      {"bound": "hbm", "achieved": round(wbytes / per_call_s / 1e9, 1), "peak": hbm_peak,
                       "unit": "GB/s", "frac": round(wbytes / per_call_s / 1e9 / hbm_peak, 4),
-                      "peak_kind": hbm_kind, "traffic": None, "kernel": f"swq::gemv_kernel<{args.format},M>",
+                      "peak_kind": hbm_kind, "traffic": None, "kernel": _gemv_form(args.format, M),
                       "us_per_call": round(per_call_s * 1e6, 2)}),
         "cpu_baseline": cpu_gemm_timing(t, M, args.cpu_seconds, N, K) if world == 1 else None,
         "e2e": {"value": round(flops * e2e_steps / e2e_s / 1e12, 2), "unit": "TFLOP/s",
