@@ -118,6 +118,29 @@ swq_status swq_rope_kv(float* q, const float* k, const float* v, float* k_cache,
 swq_status swq_qkv_bias_norm(float* q, float* k, float* v, const float* bq, const float* bk, const float* bv,
                               const float* q_norm, const float* k_norm, int q_dim, int kv_dim, int head_dim,
                               float eps, int rows, int ldq, int ldk, int ldv, swq_stream_t stream);
+/* One decode step of a GatedDeltaNet (linear attention) layer after its
+ * projections: the reference's Qwen3.5 branch of Model::forward from the
+ * q/k/v, gate, beta, alpha and dt projections to the input of the output
+ * projection (src/model.h:421-504).  Per row r:
+ *   v = causal depthwise conv1d of the value channels over conv_width steps
+ *       (the history conv_state[r][d][0..conv_width) shifts left, v enters
+ *       last; conv_w [value_dim][conv_width]; NULL conv_w: v unchanged);
+ *   per value head h (key head h mod n_k_heads, k_hd = key_head_dim,
+ *   v_hd = value_head_dim): decay = exp(-exp(ssm_a[h]) * sigmoid(alpha[h])
+ *   * sigmoid(dt[h])), beta = sigmoid(beta[h]) (NULL alpha / dt / ssm_a /
+ *   beta: the factor is 1); pred = S^T k; S = decay S + beta k (v - pred)^T;
+ *   y = S^T q with S = state[r][h] [k_hd][v_hd];
+ *   y = rmsnorm(y over the head, eps 1e-5) * norm_w (NULL: no norm);
+ *   y *= sigmoid(z) (NULL z: sigmoid(0), as the reference gates without the
+ *   projection).
+ * qkv rows (stride ld_qkv, 0: packed) hold q [n_k*k_hd], k [n_k*k_hd],
+ * v [n_v*v_hd]; z [rows][n_v*v_hd]; beta, alpha, dt [rows][n_v]; y
+ * [rows][n_v*v_hd].  The state and conv history are updated in place (zero
+ * them to start a sequence).  value_head_dim <= 1024. */
+swq_status swq_gdn_step(const float* qkv, int ld_qkv, const float* z, const float* beta, const float* alpha,
+                        const float* dt, const float* ssm_a, const float* conv_w, const float* norm_w, float* state,
+                        float* conv_state, float* y, int rows, int n_k_heads, int n_v_heads, int key_head_dim,
+                        int value_head_dim, int conv_width, swq_stream_t stream);
 /* Prefill: no counterpart in the reference, which runs a prompt as one
  * Model::forward per token (src/main.cpp:284-287).  The prompt's seq_len
  * tokens of num_seqs sequences are the rows m = s*seq_len + p of q / k / v /

@@ -80,6 +80,58 @@ def rope_neox(vec: np.ndarray, head_dim: int, pos: int, freqs: np.ndarray) -> np
     return out
 
 
+def sigmoid(x) -> np.float32:
+    with np.errstate(over="ignore"):
+        return F32(F32(1.0) / (F32(1.0) + np.exp(F32(-x), dtype=F32)))
+
+
+def gdn_step(qkv, z, beta, alpha, dt, ssm_a, conv_w, norm_w, S, conv, n_k, n_v, k_hd, v_hd, cw):
+    """One GatedDeltaNet step after the projections, the loops of
+    src/model.h:421-504 in fp32 (one row; S [n_v, k_hd, v_hd] and conv
+    [value_dim, cw] updated in place).  z, beta, alpha, dt, ssm_a, conv_w,
+    norm_w may be None, as the reference's missing tensors."""
+    key_dim, value_dim = n_k * k_hd, n_v * v_hd
+    q, k, v = qkv[:key_dim], qkv[key_dim:2 * key_dim], qkv[2 * key_dim:2 * key_dim + value_dim].astype(F32)
+    if conv_w is not None and cw > 0:
+        conv[:, :cw - 1] = conv[:, 1:].copy()
+        conv[:, cw - 1] = v
+        out = np.zeros(value_dim, F32)
+        for w in range(cw):  # sequential sum over the taps, channel by channel
+            out = (out + (conv_w[:, w] * conv[:, w]).astype(F32)).astype(F32)
+        v = out
+    y = np.zeros(value_dim, F32)
+    for h in range(n_v):
+        kh = h % n_k
+        qh, khv = q[kh * k_hd:(kh + 1) * k_hd].astype(F32), k[kh * k_hd:(kh + 1) * k_hd].astype(F32)
+        vh = v[h * v_hd:(h + 1) * v_hd]
+        base = np.exp(F32(ssm_a[h]), dtype=F32) if ssm_a is not None else F32(1.0)
+        ag = sigmoid(alpha[h]) if alpha is not None else F32(1.0)
+        log_decay = F32(-base * ag)
+        if dt is not None:
+            log_decay = F32(log_decay * sigmoid(dt[h]))
+        decay = np.exp(log_decay, dtype=F32)
+        b = sigmoid(beta[h]) if beta is not None else F32(1.0)
+        Sh = S[h]
+        pred = np.zeros(v_hd, F32)
+        for i in range(k_hd):  # sum over i in order, as the reference's loop
+            pred = (pred + (Sh[i] * khv[i]).astype(F32)).astype(F32)
+        delta = (vh - pred).astype(F32)
+        for i in range(k_hd):
+            Sh[i] = ((decay * Sh[i]).astype(F32) + ((b * khv[i]).astype(F32) * delta).astype(F32)).astype(F32)
+        yh = np.zeros(v_hd, F32)
+        for i in range(k_hd):
+            yh = (yh + (Sh[i] * qh[i]).astype(F32)).astype(F32)
+        if norm_w is not None:
+            ss = F32(0.0)
+            for val in yh:
+                ss = F32(ss + val * val)
+            ss = F32(1.0) / np.sqrt(F32(ss / F32(v_hd) + F32(1e-5)))
+            yh = (yh * ss * norm_w[h * v_hd:(h + 1) * v_hd]).astype(F32)
+        y[h * v_hd:(h + 1) * v_hd] = yh
+    zz = z if z is not None else np.zeros(value_dim, F32)
+    return np.array([F32(y[d] * sigmoid(zz[d])) for d in range(value_dim)], F32)
+
+
 def softmax(x: np.ndarray) -> np.ndarray:
     m = x.max()
     e = np.exp((x - m).astype(F32)).astype(F32)
@@ -101,6 +153,10 @@ class RefLlama:
         self.cfg, self.W, self.freqs = cfg, weights, freqs.astype(F32)
         self.kc = np.zeros((cfg.n_layers, max_seq, cfg.n_kv_heads * cfg.head_dim), F32)
         self.vc = np.zeros_like(self.kc)
+        lin = getattr(cfg, "linear_layers", ())
+        if lin:  # GatedDeltaNet state per linear layer (LinearAttentionState, src/model.h:131-166)
+            self.S = np.zeros((len(lin), cfg.lin_n_v, cfg.lin_k_hd, cfg.lin_v_hd), F32)
+            self.conv = np.zeros((len(lin), cfg.lin_value_dim, max(1, cfg.lin_conv)), F32)
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         c, W = self.cfg, self.W
@@ -110,6 +166,10 @@ class RefLlama:
         for li, L in enumerate(W["layers"]):
             t = c.layer_type_map(li) if hasattr(c, "layer_type_map") else c.types
             xb = rmsnorm(x, L["attn_norm"], c.eps)
+            if li in getattr(c, "linear_layers", ()):
+                x = (x + self._gdn(li, L, t, xb)).astype(F32)
+                x = self._ffn(L, t, x)
+                continue
             q = matmul(t["wq"], L["wq"], xb, q_dim, c.dim)
             k = matmul(t["wk"], L["wk"], xb, kv_dim, c.dim)
             v = matmul(t["wv"], L["wv"], xb, kv_dim, c.dim)
@@ -135,17 +195,36 @@ class RefLlama:
                 p = softmax((ks @ qh).astype(F32) / np.sqrt(F32(hd)))
                 att[h * hd:(h + 1) * hd] = (p @ vs).astype(F32)
             x = (x + matmul(t["wo"], L["wo"], att, c.dim, q_dim)).astype(F32)
-            xb = rmsnorm(x, L["ffn_norm"], c.eps)
-            if "router" in L:
-                x = (x + self._moe(L, t, xb)).astype(F32)
-                continue
-            g = matmul(t["w_gate"], L["w_gate"], xb, c.ffn, c.dim)
-            u = matmul(t["w_up"], L["w_up"], xb, c.ffn, c.dim)
-            with np.errstate(over="ignore"):  # exp(-g) = inf for very negative g: silu -> -0, as expf
-                hmid = (g / (F32(1.0) + np.exp(-g)) * u).astype(F32)
-            x = (x + matmul(t["w_down"], L["w_down"], hmid, c.dim, c.ffn)).astype(F32)
+            x = self._ffn(L, t, x)
         x = rmsnorm(x, W["output_norm"], c.eps)
         return matmul(c.types["output"], W["output"], x, c.vocab, c.dim)
+
+    def _ffn(self, L, t, x):
+        """x + FFN(rmsnorm(x, ffn_norm)): dense SwiGLU (src/model.h:519-541) or MoE."""
+        c = self.cfg
+        xb = rmsnorm(x, L["ffn_norm"], c.eps)
+        if "router" in L:
+            return (x + self._moe(L, t, xb)).astype(F32)
+        g = matmul(t["w_gate"], L["w_gate"], xb, c.ffn, c.dim)
+        u = matmul(t["w_up"], L["w_up"], xb, c.ffn, c.dim)
+        with np.errstate(over="ignore"):  # exp(-g) = inf for very negative g: silu -> -0, as expf
+            hmid = (g / (F32(1.0) + np.exp(-g)) * u).astype(F32)
+        return (x + matmul(t["w_down"], L["w_down"], hmid, c.dim, c.ffn)).astype(F32)
+
+    def _gdn(self, li, L, t, xb):
+        """A GatedDeltaNet layer's output projection input and output
+        (src/model.h:369-513): projections of xb, gdn_step, ssm_out."""
+        c = self.cfg
+        kd, vd, nv, H = c.lin_key_dim, c.lin_value_dim, c.lin_n_v, c.dim
+        qkv = matmul(t["w_qkv"], L["w_qkv"], xb, 2 * kd + vd, H)
+        proj = {k: matmul(t[k], L[k], xb, n, H) if k in L else None
+                for k, n in (("w_z", vd), ("w_beta", nv), ("w_alpha", nv), ("w_dt", nv))}
+        j = c.linear_layers.index(li)
+        conv = L.get("conv1d")
+        y = gdn_step(qkv, proj["w_z"], proj["w_beta"], proj["w_alpha"], proj["w_dt"], L.get("ssm_a"),
+                     None if conv is None else np.asarray(conv, F32).reshape(vd, c.lin_conv), L.get("ssm_norm"),
+                     self.S[j], self.conv[j], c.lin_n_k, nv, c.lin_k_hd, c.lin_v_hd, c.lin_conv)
+        return matmul(t["w_ssm_out"], L["w_ssm_out"], y, H, vd)
 
     def _swiglu(self, tg, gb, tu, ub, td, db, xb, f):
         c = self.cfg

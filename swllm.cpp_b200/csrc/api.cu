@@ -22,6 +22,7 @@
 #include "prefill.h"
 #include "qkv_extras.h"
 #include "gemm_tc.h"
+#include "gdn.h"
 #include "gemv.h"
 
 namespace {
@@ -559,6 +560,30 @@ swq_status swq_qkv_bias_norm(float* q, float* k, float* v, const float* bq, cons
     return launch_status(swq::qkv_extras_launch(q, k, v, bq, bk, bv, q_norm, k_norm, q_dim, kv_dim, head_dim, eps,
                                                 rows, ldq, ldk, ldv, reinterpret_cast<cudaStream_t>(stream)),
                          "q/k/v extras launch");
+}
+
+swq_status swq_gdn_step(const float* qkv, int ld_qkv, const float* z, const float* beta, const float* alpha,
+                        const float* dt, const float* ssm_a, const float* conv_w, const float* norm_w, float* state,
+                        float* conv_state, float* y, int rows, int n_k_heads, int n_v_heads, int key_head_dim,
+                        int value_head_dim, int conv_width, swq_stream_t stream) {
+    if (rows < 0 || n_k_heads <= 0 || n_v_heads <= 0 || key_head_dim <= 0 || value_head_dim <= 0 ||
+        conv_width < 0)
+        return fail(SWQ_ERR_BAD_SHAPE, "gdn step: non-positive head count or size");
+    if (value_head_dim > swq::gdn_max_head_dim() || key_head_dim > 16384)
+        return fail(SWQ_ERR_BAD_SHAPE, "gdn step: head dimension above the kernel's limit (value 1024, key 16384)");
+    const long long qkv_dim = 2LL * n_k_heads * key_head_dim + 1LL * n_v_heads * value_head_dim;
+    if (ld_qkv == 0) ld_qkv = static_cast<int>(qkv_dim);
+    if (ld_qkv < qkv_dim) return fail(SWQ_ERR_BAD_SHAPE, "gdn step: q/k/v row stride below its size");
+    if (rows == 0) return SWQ_OK;
+    if (!qkv || !state || !y || (conv_w && conv_width > 0 && !conv_state))
+        return fail(SWQ_ERR_NULL_PTR, "gdn step: null q/k/v, state, output or conv history");
+    swq::DeviceInfo dev;
+    swq_status st = current_device(&dev);
+    if (st != SWQ_OK) return st;
+    return launch_status(swq::gdn_step_launch(qkv, ld_qkv, z, beta, alpha, dt, ssm_a, conv_w, norm_w, state,
+                                              conv_state, y, rows, n_k_heads, n_v_heads, key_head_dim,
+                                              value_head_dim, conv_width, reinterpret_cast<cudaStream_t>(stream)),
+                         "gdn step launch");
 }
 
 // ---- prefill (rows m = s * seq_len + p: token p of sequence s at pos0 + p) ----

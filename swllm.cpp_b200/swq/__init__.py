@@ -26,6 +26,7 @@ from .lib import (  # noqa: F401
     OPT_TENSOR_CORE_MIN_M, OPT_GEMV_SMEM_KB, OPT_GEMV_STAGE_KB, OPT_GEMV_CTAS_PER_SM, OPT_GEMV_FP32_ACT, OPT_GEMV_INT_MMA,
     ACT_NONE, ACT_RMSNORM, ACT_SWIGLU,
     add, add_rmsnorm, argmax, attention_decode, attention_prefill, attention_workspace_bytes, decode_advance, embed,
+    gdn_step,
     qkv_bias_norm, rmsnorm, rope_kv, rope_kv_prefill, silu_mul,
     GEMM_NOALLOC_MAX_X_ELEMS, SwqError, Status, block_size, build, check, dequant, exported_symbols, gemm,
     gemm_act, gemm_act_ws, gemm_noalloc, gemm_workspace_bytes, gemv, grouped_gemm, grouped_gemv, grouped_matmul, grouped_matmul_stacked,

@@ -367,9 +367,13 @@ NEOX_ARCHS = ("qwen2", "qwen3", "qwen2moe", "qwen35", "qwen35moe", "starcoder2",
               "stablelm", "codeshell")
 _MATRICES = {"wq": "attn_q", "wk": "attn_k", "wv": "attn_v", "wo": "attn_output", "w_gate": "ffn_gate",
              "w_up": "ffn_up", "w_down": "ffn_down"}
-# tensors of layer kinds LlamaDecoder does not run (GatedDeltaNet layers of
-# hybrid models), src/model.h:783-800
-_UNSUPPORTED = ("attn_qkv.weight", "ssm_out.weight")
+# GatedDeltaNet layers of hybrid (Qwen3.5) files, src/model.h:795-807: name in
+# the weights dict -> GGUF stem of the projections (attn_qkv and ssm_out
+# required, the others optional as the reference's), and of the F32 vectors
+_LINEAR_MATRICES = {"w_qkv": "attn_qkv", "w_z": "attn_gate", "w_beta": "ssm_beta", "w_alpha": "ssm_alpha",
+                    "w_dt": "ssm_dt", "w_ssm_out": "ssm_out"}
+_LINEAR_VECTORS = {"ssm_a": "ssm_a", "conv1d": "ssm_conv1d.weight", "ssm_norm": "ssm_norm.weight"}
+_FFN = ("w_gate", "w_up", "w_down")
 # optional per-layer tensors the decoder applies after the q/k/v projections
 # (src/model.h:291-318, loaded at :822-837): name in the weights dict -> GGUF stem
 _EXTRAS = {"bq": "attn_q.bias", "bk": "attn_k.bias", "bv": "attn_v.bias", "q_norm": "attn_q_norm.weight",
@@ -392,8 +396,8 @@ def llama_config(g: GGUFFile, context_override: int = 0):
     heads = g.get_i64(f"{arch}.attention.head_count", 0)
     if hidden == 0 or layers == 0 or heads == 0:
         raise GGUFError(f"incomplete model config (hidden={hidden}, layers={layers}, heads={heads})")
-    if arch in ("qwen35", "qwen35moe"):
-        raise GGUFError(f"architecture '{arch}' has GatedDeltaNet layers; the decoder runs dense attention only")
+    if arch == "qwen35moe":
+        raise GGUFError(f"architecture '{arch}': hybrid MoE files are not supported by the decoder")
     vocab = g.get_i64(f"{arch}.vocab_size", g.get_i64("tokenizer.ggml.tokens", 0))
     if vocab == 0:
         tok = g.metadata.get("tokenizer.ggml.tokens")
@@ -409,22 +413,45 @@ def llama_config(g: GGUFFile, context_override: int = 0):
         max_seq = context_override
     elif context_override == 0 and max_seq > 8192:
         max_seq = 4096
-    for li in range(layers):
-        for suffix in _UNSUPPORTED:
-            if f"blk.{li}.{suffix}" in g.tensors:
-                raise GGUFError(f"blk.{li}.{suffix}: this layer kind is not supported by the decoder")
+    # hybrid files: layer kinds from {arch}.attention.layer_types (0 full, 1
+    # linear attention) and the GatedDeltaNet sizes with the reference's
+    # defaults (src/model.h:637-678, :911-921)
+    linear = ()
+    lin = {}
+    if arch == "qwen35":
+        kinds = g.metadata.get(f"{arch}.attention.layer_types")
+        kinds = [int(e.value) for e in kinds.value] if kinds is not None and kinds.type == ARRAY else []
+        linear = tuple(li for li, k in enumerate(kinds[:layers]) if k != 0)
+        n_kv = g.get_i64(f"{arch}.attention.head_count_kv", heads)
+        lin = dict(lin_k_hd=g.get_i64(f"{arch}.attention.linear_key_length", 0) or head_dim,
+                   lin_v_hd=g.get_i64(f"{arch}.attention.linear_value_length", 0) or head_dim,
+                   lin_n_k=g.get_i64(f"{arch}.attention.linear_head_count_kv", 0) or heads,
+                   lin_n_v=g.get_i64(f"{arch}.attention.linear_head_count", 0) or n_kv,
+                   lin_conv=g.get_i64(f"{arch}.ssm.conv_kernel", 0) or 4)
     layer_types = []
     for li in range(layers):
         lt = {}
-        for key, stem in _MATRICES.items():
+        if li in linear:
+            for key, stem in _LINEAR_MATRICES.items():
+                name = f"blk.{li}.{stem}.weight"
+                if name in g.tensors:
+                    lt[key] = g.tensors[name].type
+                elif key in ("w_qkv", "w_ssm_out"):
+                    raise GGUFError(f"tensor '{name}' not found (GatedDeltaNet layer {li})")
+            stems = {k: _MATRICES[k] for k in _FFN}
+        else:
+            stems = _MATRICES
+        for key, stem in stems.items():
             name = f"blk.{li}.{stem}.weight"
             if name not in g.tensors:
                 raise GGUFError(f"tensor '{name}' not found")
             lt[key] = g.tensors[name].type
         layer_types.append(lt)
     out_name = "output.weight" if "output.weight" in g.tensors else "token_embd.weight"
-    types = dict(layer_types[0], output=g.tensors[out_name].type)
-    for name, t in [(f"blk.{li}.{_MATRICES[k]}.weight", t) for li, lt in enumerate(layer_types)
+    full = [lt for li, lt in enumerate(layer_types) if li not in linear]
+    types = dict(full[0] if full else layer_types[0], output=g.tensors[out_name].type)
+    stem_of = dict(_MATRICES, **_LINEAR_MATRICES)
+    for name, t in [(f"blk.{li}.{stem_of[k]}.weight", t) for li, lt in enumerate(layer_types)
                     for k, t in lt.items()] + [(out_name, types["output"])]:
         if t not in QUANT_TYPES:
             raise GGUFError(f"tensor '{name}' has GGML type {t}; libswq multiplies "
@@ -436,7 +463,8 @@ def llama_config(g: GGUFFile, context_override: int = 0):
                        eps=float(np.float32(g.get_f64(f"{arch}.attention.layer_norm_rms_epsilon", 1e-5))),
                        theta=float(np.float32(g.get_f64(f"{arch}.rope.freq_base", 10000.0))),
                        rope_neox=arch in NEOX_ARCHS, max_seq=max_seq, types=types,
-                       layer_types=None if uniform else tuple(layer_types))
+                       layer_types=None if uniform and not linear else tuple(layer_types),
+                       linear_layers=linear, **lin)
 
 
 def llama_weights(g: GGUFFile, cfg) -> dict:
@@ -486,6 +514,21 @@ def llama_weights(g: GGUFFile, cfg) -> dict:
         if ffn_norm not in g.tensors and f"blk.{li}.post_attention_norm.weight" in g.tensors:
             ffn_norm = f"blk.{li}.post_attention_norm.weight"
         L = {"attn_norm": vec(f"blk.{li}.attn_norm.weight", cfg.dim), "ffn_norm": vec(ffn_norm, cfg.dim)}
+        if li in cfg.linear_layers:
+            lt = cfg.layer_type_map(li)
+            for key, (N, K) in cfg.layer_shapes(li).items():
+                if key in lt:
+                    name = f"blk.{li}.{dict(_MATRICES, **_LINEAR_MATRICES)[key]}.weight"
+                    check_shape(name, N, K)
+                    L[key] = g.blocks(name)
+            for key, stem in _LINEAR_VECTORS.items():
+                name = f"blk.{li}.{stem}"
+                if name in g.tensors:
+                    n = {"ssm_a": cfg.lin_n_v, "conv1d": cfg.lin_value_dim * cfg.lin_conv,
+                         "ssm_norm": cfg.lin_value_dim}[key]
+                    L[key] = vec(name, n)
+            layers.append(L)
+            continue
         for key, (N, K) in cfg.shapes().items():
             name = f"blk.{li}.{_MATRICES[key]}.weight"
             check_shape(name, N, K)

@@ -109,6 +109,7 @@ def lib() -> ctypes.CDLL:
         "swq_attention_prefill": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, vp]),
         "swq_qkv_bias_norm": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, ctypes.c_float, i32, i32, i32,
                                     i32, vp]),
+        "swq_gdn_step": (i32, [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
         "swq_silu_mul": (i32, [vp, vp, vp, i32, i32, i32, vp]),
         "swq_add": (i32, [vp, vp, i64, vp]),
         "swq_embed": (i32, [vp, vp, vp, i32, i32, i32, vp]),
@@ -365,6 +366,18 @@ def qkv_bias_norm(q, k, v, bq, bk, bv, q_norm, k_norm, q_dim: int, kv_dim: int, 
     """q/k/v bias adds, then per-head RMSNorm of q and k (any vector may be None)."""
     _raise(lib().swq_qkv_bias_norm(_ptr(q), _ptr(k), _ptr(v), _ptr(bq), _ptr(bk), _ptr(bv), _ptr(q_norm),
                                    _ptr(k_norm), q_dim, kv_dim, head_dim, eps, rows, ldq, ldk, ldv, _stream(stream)))
+
+
+def gdn_step(qkv, z, beta, alpha, dt, ssm_a, conv_w, norm_w, state, conv_state, y, rows: int, n_k_heads: int,
+             n_v_heads: int, key_head_dim: int, value_head_dim: int, conv_width: int, ld_qkv: int = 0,
+             stream=None) -> None:
+    """One GatedDeltaNet decode step after the projections (swq_gdn_step):
+    conv1d of v, the gated delta-rule update of `state` and its read-out,
+    per-head RMSNorm, sigmoid(z) gate, into y.  z, beta, alpha, dt, ssm_a,
+    conv_w, norm_w may be None."""
+    _raise(lib().swq_gdn_step(_ptr(qkv), ld_qkv, _ptr(z), _ptr(beta), _ptr(alpha), _ptr(dt), _ptr(ssm_a),
+                              _ptr(conv_w), _ptr(norm_w), _ptr(state), _ptr(conv_state), _ptr(y), rows, n_k_heads,
+                              n_v_heads, key_head_dim, value_head_dim, conv_width, _stream(stream)))
 
 
 def silu_mul(out, gate, up, n: int, rows: int = 1, ld: int | None = None, stream=None) -> None:

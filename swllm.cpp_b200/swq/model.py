@@ -37,7 +37,7 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import lib as _lib_mod  # noqa: F401  (module import for the ctypes table)
-from .lib import (ACT_NONE, ACT_RMSNORM, ACT_SWIGLU, OPT_TENSOR_CORE_MIN_M, add, argmax, add_rmsnorm,
+from .lib import (ACT_NONE, ACT_RMSNORM, ACT_SWIGLU, OPT_TENSOR_CORE_MIN_M, add, argmax, add_rmsnorm, gdn_step,
                   attention_decode, attention_prefill, attention_workspace_bytes, decode_advance, dequant, embed,
                   gemm_act_ws, gemm_workspace_bytes, get_option, qkv_bias_norm, rmsnorm, rope_kv, rope_kv_prefill,
                   silu_mul)
@@ -72,6 +72,16 @@ class LlamaConfig:
     top_k: int = 0
     expert_ffn: int = 0
     shared_ffn: int = 0
+    # GatedDeltaNet (linear attention) layers of a hybrid model (Qwen3.5,
+    # src/model.h:369-513): their indices, key / value heads and head dims,
+    # conv1d width; their matrices (w_qkv, w_z, w_beta, w_alpha, w_dt,
+    # w_ssm_out, then the FFN) come from layer_types
+    linear_layers: tuple = ()
+    lin_n_k: int = 0
+    lin_n_v: int = 0
+    lin_k_hd: int = 0
+    lin_v_hd: int = 0
+    lin_conv: int = 0
 
     @classmethod
     def llama3_70b(cls, **kw) -> "LlamaConfig":
@@ -93,6 +103,29 @@ class LlamaConfig:
     @property
     def is_moe(self) -> bool:
         return self.n_experts > 0
+
+    @property
+    def is_hybrid(self) -> bool:
+        return len(self.linear_layers) > 0
+
+    @property
+    def lin_key_dim(self) -> int:
+        return self.lin_n_k * self.lin_k_hd
+
+    @property
+    def lin_value_dim(self) -> int:
+        return self.lin_n_v * self.lin_v_hd
+
+    def layer_shapes(self, layer: int) -> dict:
+        """name -> (N, K) of every quantized matrix layer `layer` may have: a
+        GatedDeltaNet layer's projections (w_z, w_beta, w_alpha, w_dt are
+        optional) and FFN, else shapes()."""
+        if layer not in self.linear_layers:
+            return self.shapes()
+        kd, vd, nv, H = self.lin_key_dim, self.lin_value_dim, self.lin_n_v, self.dim
+        return {"w_qkv": (2 * kd + vd, H), "w_z": (vd, H), "w_beta": (nv, H), "w_alpha": (nv, H),
+                "w_dt": (nv, H), "w_ssm_out": (H, vd),
+                "w_gate": (self.ffn, H), "w_up": (self.ffn, H), "w_down": (H, self.ffn)}
 
     @property
     def q_dim(self) -> int:
@@ -128,7 +161,8 @@ class LlamaConfig:
         """Quantized weight bytes one decode step reads (all layers + LM head;
         for a MoE model the attention, shared experts and LM head, without the
         routed experts, whose share depends on the routing)."""
-        per_layer = [sum(n * row_bytes(self.layer_type_map(li)[k], kk) for k, (n, kk) in self.shapes().items())
+        per_layer = [sum(n * row_bytes(self.layer_type_map(li)[k], kk) for k, (n, kk) in
+                         self.layer_shapes(li).items() if k in self.layer_type_map(li))
                      for li in range(self.n_layers)]
         if self.is_moe and self.shared_ffn:
             per_layer = [b + sum(n * row_bytes(self.types[k], kk) for k, (n, kk) in self.moe_shapes().items()
@@ -270,6 +304,8 @@ class LlamaDecoder:
         self.group = group
         if cfg.is_moe and group is not None:
             raise ValueError("a MoE decoder runs its attention per rank: shard the experts with ep_group")
+        if cfg.is_hybrid and (group is not None or cfg.is_moe or weights is None):
+            raise ValueError("a hybrid (GatedDeltaNet) decoder runs on one GPU, dense, from given weights")
         self.ep_group = ep_group
         self.moe_max_tokens = int(moe_max_tokens) or max(rows, 512)
         self.rank, self.world = _world(group) if group is not None else (0, 1)
@@ -321,9 +357,10 @@ class LlamaDecoder:
             raise ValueError(f"collective must be 'peer' or 'nccl', not {collective!r}")
         self.collective = collective
         if fuse == "auto":
-            fuse = ("rmsnorm",) if rows >= get_option(OPT_TENSOR_CORE_MIN_M) and not cfg.is_moe else ()
-        if cfg.is_moe and fuse:
-            raise ValueError("a MoE decoder runs its norms as their own pass (fuse=())")
+            fuse = ("rmsnorm",) if rows >= get_option(OPT_TENSOR_CORE_MIN_M) and not (cfg.is_moe or cfg.is_hybrid) \
+                else ()
+        if (cfg.is_moe or cfg.is_hybrid) and fuse:
+            raise ValueError("a MoE or hybrid decoder runs its norms as their own pass (fuse=())")
         if not set(fuse) <= {"rmsnorm", "swiglu"}:
             raise ValueError(f"fuse takes 'rmsnorm' and 'swiglu', not {fuse!r}")
         self.fuse = tuple(fuse)
@@ -371,7 +408,7 @@ class LlamaDecoder:
         self.output = blocks("output", cfg.vocab, cfg.dim, W.get("output"), t["output"])
         lts = [cfg.layer_type_map(layer) for layer in range(cfg.n_layers)]
         self.fuse_gate_up = all(lt.get("w_gate") == lt.get("w_up") for lt in lts)
-        self.fuse_qk = all(lt["wq"] == lt["wk"] for lt in lts)
+        self.fuse_qk = all(lt.get("wq") == lt.get("wk") for lt in lts)
         self.layers = []
         for layer, lt in enumerate(lts):
             lw = W["layers"][layer] if weights else {}
@@ -379,6 +416,10 @@ class LlamaDecoder:
             for name in ("attn_norm", "ffn_norm"):
                 L[name] = (_upload(np.ascontiguousarray(lw[name], np.float32), dev) if weights
                            else 1.0 + 0.01 * torch.randn(cfg.dim, generator=g, **f32))
+            if layer in cfg.linear_layers:
+                self._load_linear_layer(cfg, L, lt, lw)
+                self.layers.append(L)
+                continue
             for name, (N, K) in cfg.shapes().items():
                 L[name] = blocks(name, N, K, lw.get(name), lt[name])
             # optional q/k/v biases and q/k head norms (Qwen-style files,
@@ -399,6 +440,22 @@ class LlamaDecoder:
                 L["w_qk"] = torch.cat([L.pop("wq"), L.pop("wk")])
             self.layers.append(L)
         self.freqs = torch.from_numpy(rope_freqs(cfg)).to(dev)
+
+    def _load_linear_layer(self, cfg, L, lt, lw) -> None:
+        """A GatedDeltaNet layer's projections (whole matrices: the hybrid
+        decoder runs on one GPU), its F32 vectors (ssm_a [n_v], conv1d
+        [value_dim, conv], ssm_norm [value_dim], each optional as the
+        reference's tensors are) and its dense FFN."""
+        import torch
+        dev = self.device
+        for name in ("w_qkv", "w_z", "w_beta", "w_alpha", "w_dt", "w_ssm_out", "w_gate", "w_up", "w_down"):
+            if name in lt:
+                L[name] = _upload(np.ascontiguousarray(lw[name]).reshape(-1), dev)
+        for name in ("ssm_a", "conv1d", "ssm_norm"):
+            if lw.get(name) is not None:
+                L[name] = _upload(np.ascontiguousarray(lw[name], np.float32).reshape(-1), dev)
+        if lt["w_gate"] == lt["w_up"]:
+            L["w_gate_up"] = torch.cat([L.pop("w_gate"), L.pop("w_up")])
 
     def _moe_layer(self, cfg, lt, lw, layer):
         """The MoE FFN of one layer: host weights (lw) or synthetic blocks
@@ -465,6 +522,15 @@ class LlamaDecoder:
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.step_no = torch.zeros(1, dtype=torch.int32, device=dev)
         self.history = torch.zeros((max_steps, B), dtype=torch.int32, device=dev)
+        if cfg.is_hybrid:
+            kd, vd, nv = cfg.lin_key_dim, cfg.lin_value_dim, cfg.lin_n_v
+            self.gdn_qkv = torch.zeros((B, 2 * kd + vd), **f32)
+            self.gdn_z = torch.zeros((B, vd), **f32)
+            self.gdn_gates = torch.zeros((3, B, nv), **f32)  # beta, alpha, dt projections
+            self.gdn_y = torch.zeros((B, vd), **f32)
+            nlin = len(cfg.linear_layers)
+            self.gdn_state = torch.zeros((nlin, B, nv, cfg.lin_k_hd, cfg.lin_v_hd), **f32)
+            self.gdn_conv = torch.zeros((nlin, B, vd, max(1, cfg.lin_conv)), **f32)
         self.ws_bytes = attention_workspace_bytes(self.nh, self.nkv, cfg.head_dim, B, cfg.max_seq)
         self.ws = torch.zeros(max(1, self.ws_bytes // 4), **f32)  # zero-filled, as the kernel expects
         self.gemm_ws, self.gemm_ws_bytes = None, 0  # tensor-core GEMM scratch, grown on first need
@@ -523,29 +589,32 @@ class LlamaDecoder:
         pending = None  # fused: d to add to the residual before the next norm
         for li, L in enumerate(self.layers):
             t = L["types"]
-            # q, k, v of norm(x) (fused: x2 = x + pending first)
-            if fuse_rms:
-                src, a_in = x, dict(kind=ACT_RMSNORM, residual=pending, norm_w=L["attn_norm"])
-                a_qk = dict(a_in, sum_out=x2)
+            if li in c.linear_layers:  # GatedDeltaNet: norm(x) -> d (fuse=() for hybrid models)
+                self._gdn_layer(li, L, xb, d)
             else:
-                src, a_in, a_qk = xb, {}, {}
-            if "w_qk" in L:
-                gemm(t["wq"], L["w_qk"], src, self.qk, B, ld, c.dim, stream=s, **a_qk)
-            else:
-                gemm(t["wq"], L["wq"], src, self.att, B, qd, c.dim, stream=s, **a_qk)
-                q[:, :qd].copy_(self.att)
-                gemm(t["wk"], L["wk"], src, self.v, B, kvd, c.dim, stream=s, **a_in)
-                k.copy_(self.v)
-            gemm(t["wv"], L["wv"], src, self.v, B, kvd, c.dim, stream=s, **a_in)
-            if _EXTRAS.intersection(L):
-                qkv_bias_norm(q, k, self.v, L.get("bq"), L.get("bk"), L.get("bv"), L.get("q_norm"), L.get("k_norm"),
-                              qd, kvd, c.head_dim, c.eps, B, ldq=ld, ldk=ld, ldv=kvd, stream=s)
-            kc, vc = self.kcache[li], self.vcache[li]
-            rope_kv(q, k, self.v, kc, vc, self.pos, self.freqs, qd, kvd, c.head_dim, c.head_dim,
-                    c.rope_neox, B, c.max_seq, ldq=ld, ldk=ld, stream=s)
-            attention_decode(self.att, q, kc, vc, self.pos, self.ws, self.ws_bytes, self.nh, self.nkv,
-                             c.head_dim, B, c.max_seq, ldq=ld, stream=s)
-            gemm(t["wo"], L["wo"], self.att, d, B, c.dim, qd, stream=s)
+                # q, k, v of norm(x) (fused: x2 = x + pending first)
+                if fuse_rms:
+                    src, a_in = x, dict(kind=ACT_RMSNORM, residual=pending, norm_w=L["attn_norm"])
+                    a_qk = dict(a_in, sum_out=x2)
+                else:
+                    src, a_in, a_qk = xb, {}, {}
+                if "w_qk" in L:
+                    gemm(t["wq"], L["w_qk"], src, self.qk, B, ld, c.dim, stream=s, **a_qk)
+                else:
+                    gemm(t["wq"], L["wq"], src, self.att, B, qd, c.dim, stream=s, **a_qk)
+                    q[:, :qd].copy_(self.att)
+                    gemm(t["wk"], L["wk"], src, self.v, B, kvd, c.dim, stream=s, **a_in)
+                    k.copy_(self.v)
+                gemm(t["wv"], L["wv"], src, self.v, B, kvd, c.dim, stream=s, **a_in)
+                if _EXTRAS.intersection(L):
+                    qkv_bias_norm(q, k, self.v, L.get("bq"), L.get("bk"), L.get("bv"), L.get("q_norm"),
+                                  L.get("k_norm"), qd, kvd, c.head_dim, c.eps, B, ldq=ld, ldk=ld, ldv=kvd, stream=s)
+                kc, vc = self.kcache[li], self.vcache[li]
+                rope_kv(q, k, self.v, kc, vc, self.pos, self.freqs, qd, kvd, c.head_dim, c.head_dim,
+                        c.rope_neox, B, c.max_seq, ldq=ld, ldk=ld, stream=s)
+                attention_decode(self.att, q, kc, vc, self.pos, self.ws, self.ws_bytes, self.nh, self.nkv,
+                                 c.head_dim, B, c.max_seq, ldq=ld, stream=s)
+                gemm(t["wo"], L["wo"], self.att, d, B, c.dim, qd, stream=s)
             if tp:
                 self.all_reduce(d)
             # gate, up of norm(residual + o)
@@ -593,6 +662,28 @@ class LlamaDecoder:
             argmax(self.logits, c.vocab, B, self.tokens, self.history, self.step_no, stream=s)
             decode_advance(self.pos, self.step_no, stream=s)
 
+    def _gdn_layer(self, li: int, L: dict, xb, d) -> None:
+        """A GatedDeltaNet layer of the step (src/model.h:369-513): the q/k/v,
+        gate, beta, alpha and dt projections of norm(x) = xb, swq_gdn_step
+        (conv1d, gated delta rule, head norm, gate), the ssm_out projection
+        into d."""
+        c, B, s, t = self.cfg, self.rows, self.stream, L["types"]
+        kd, vd, nv = c.lin_key_dim, c.lin_value_dim, c.lin_n_v
+        gemm = self._gemm
+        gemm(t["w_qkv"], L["w_qkv"], xb, self.gdn_qkv, B, 2 * kd + vd, c.dim, stream=s)
+        if "w_z" in L:
+            gemm(t["w_z"], L["w_z"], xb, self.gdn_z, B, vd, c.dim, stream=s)
+        gates = []
+        for i, name in enumerate(("w_beta", "w_alpha", "w_dt")):
+            if name in L:
+                gemm(t[name], L[name], xb, self.gdn_gates[i], B, nv, c.dim, stream=s)
+            gates.append(self.gdn_gates[i] if name in L else None)
+        j = c.linear_layers.index(li)
+        gdn_step(self.gdn_qkv, self.gdn_z if "w_z" in L else None, gates[0], gates[1], gates[2], L.get("ssm_a"),
+                 L.get("conv1d"), L.get("ssm_norm"), self.gdn_state[j], self.gdn_conv[j], self.gdn_y, B,
+                 c.lin_n_k, nv, c.lin_k_hd, c.lin_v_hd, c.lin_conv if "conv1d" in L else 0, stream=s)
+        gemm(t["w_ssm_out"], L["w_ssm_out"], self.gdn_y, d, B, c.dim, vd, stream=s)
+
     def prefill(self, prompts, pos0: int = 0, all_logits: bool = False):
         """Batched prefill: the prompt tokens of every sequence through the whole
         model at once -- M = rows x P activation rows, every projection one
@@ -609,6 +700,9 @@ class LlamaDecoder:
         logits of every prompt position, [rows, P, vocab] (one process)."""
         import torch
         c, B, s = self.cfg, self.rows, self.stream
+        if c.is_hybrid:
+            raise NotImplementedError("batched prefill of GatedDeltaNet layers (a sequential recurrence) is not "
+                                      "built; run the prompt through step() one position at a time")
         toks = np.asarray(prompts, dtype=np.int32)
         if toks.ndim != 2 or toks.shape[0] != B or toks.shape[1] < 1:
             raise ValueError(f"prompts must be {B} lists of at least one token, got shape {toks.shape}")
@@ -715,12 +809,17 @@ class LlamaDecoder:
             self.step()
 
     def reset(self, tokens, pos: int = 0) -> None:
-        """Set the current tokens and position (ordered on the decode stream)."""
+        """Set the current tokens and position (ordered on the decode stream).
+        Position 0 starts new sequences: the GatedDeltaNet layers' recurrent
+        state and conv history are zeroed, as Model::reset does."""
         import torch
         with torch.cuda.stream(self.stream):
             self.tokens.copy_(torch.as_tensor(np.asarray(tokens, np.int32)).to(self.device))
             self.pos.fill_(pos)
             self.step_no.fill_(0)
+            if pos == 0 and self.cfg.is_hybrid:
+                self.gdn_state.zero_()
+                self.gdn_conv.zero_()
         self.steps_issued = 0
 
     def generate(self, n: int) -> None:

@@ -17,6 +17,13 @@ its SHA-256 and the reference's logits are stored (tests/golden/).
           (src/model.h:629-634).
 * "bias": "qwen2" with q/k/v biases (src/model.h:291-294).
 * "qknorm": "qwen3" with per-head q/k RMSNorm weights (src/model.h:296-318).
+* "hybrid": "qwen35" (neox RoPE) whose layer 0 is a GatedDeltaNet layer
+          (qwen35.attention.layer_types = [1, 0]; 2 key heads and 4 value
+          heads of 32, conv width 4; attn_qkv, attn_gate, ssm_beta,
+          ssm_alpha, ssm_dt, ssm_out projections, F32 ssm_a, ssm_conv1d,
+          ssm_norm) and layer 1 full attention (src/model.h:369-513).  Its
+          attn_qkv scales are small: the reference applies the delta rule to
+          unnormalised keys, which diverges once beta |k|^2 > 2.
 """
 from __future__ import annotations
 
@@ -31,6 +38,8 @@ from swq import synth
 TOKENS = [7, 123, 45, 299, 0, 200]   # teacher-forced tokens at positions 0..5
 
 SHAPE = dict(layers=2, hidden=256, heads=4, kv_heads=2, ffn=512, vocab=300, context=32)
+# GatedDeltaNet layers of the "hybrid" variant
+LINEAR = dict(n_k=2, n_v=4, k_hd=32, v_hd=32, conv=4)
 _STEMS = {"wq": "attn_q", "wk": "attn_k", "wv": "attn_v", "wo": "attn_output", "w_gate": "ffn_gate",
           "w_up": "ffn_up", "w_down": "ffn_down"}
 
@@ -51,7 +60,14 @@ VARIANTS = {
     "qknorm": dict(
         arch="qwen3", alignment=32, embd=G.F32, output=G.Q6_K, vocab_key=True, qk_norm=True,
         layers=[dict(wq=G.Q4_K, wk=G.Q4_K, wv=G.Q6_K, wo=G.Q4_K, w_gate=G.Q4_K, w_up=G.Q4_K, w_down=G.Q6_K)] * 2),
+    "hybrid": dict(
+        arch="qwen35", alignment=32, embd=G.F32, output=G.Q6_K, vocab_key=True, linear=(0,),
+        layers=[dict(w_qkv=G.Q4_K, w_z=G.Q8_0, w_beta=G.Q8_0, w_alpha=G.Q8_0, w_dt=G.Q8_0, w_ssm_out=G.Q8_0,
+                     w_gate=G.Q4_K, w_up=G.Q4_K, w_down=G.Q6_K),
+                dict(wq=G.Q4_K, wk=G.Q4_K, wv=G.Q6_K, wo=G.Q4_K, w_gate=G.Q4_K, w_up=G.Q4_K, w_down=G.Q6_K)]),
 }
+_LINEAR_STEMS = {"w_qkv": "attn_qkv", "w_z": "attn_gate", "w_beta": "ssm_beta", "w_alpha": "ssm_alpha",
+                 "w_dt": "ssm_dt", "w_ssm_out": "ssm_out"}
 
 
 def _shapes(s):
@@ -61,11 +77,20 @@ def _shapes(s):
             "w_gate": (s["ffn"], s["hidden"]), "w_up": (s["ffn"], s["hidden"]), "w_down": (s["hidden"], s["ffn"])}
 
 
+def _linear_shapes(s):
+    L = LINEAR
+    key, val = L["n_k"] * L["k_hd"], L["n_v"] * L["v_hd"]
+    return {"w_qkv": (2 * key + val, s["hidden"]), "w_z": (val, s["hidden"]), "w_beta": (L["n_v"], s["hidden"]),
+            "w_alpha": (L["n_v"], s["hidden"]), "w_dt": (L["n_v"], s["hidden"]), "w_ssm_out": (s["hidden"], val),
+            "w_gate": (s["ffn"], s["hidden"]), "w_up": (s["ffn"], s["hidden"]), "w_down": (s["hidden"], s["ffn"])}
+
+
 def write(path: Path, variant: str) -> Path:
     """Write the variant's GGUF file at path."""
     v, s = VARIANTS[variant], SHAPE
     a = v.get("arch", "llama")
-    rng = np.random.default_rng({"mix": 11, "tied": 12, "neox": 13, "bias": 14, "qknorm": 15}[variant])
+    rng = np.random.default_rng({"mix": 11, "tied": 12, "neox": 13, "bias": 14, "qknorm": 15,
+                                 "hybrid": 16}[variant])
     meta = {
         "general.architecture": a,
         "general.name": f"tiny-{variant}",
@@ -84,13 +109,22 @@ def write(path: Path, variant: str) -> Path:
     }
     if v["vocab_key"]:
         meta[f"{a}.vocab_size"] = s["vocab"]
+    linear = v.get("linear", ())
+    if linear:
+        meta[f"{a}.attention.layer_types"] = [1 if li in linear else 0 for li in range(s["layers"])]
+        meta[f"{a}.attention.linear_key_length"] = LINEAR["k_hd"]
+        meta[f"{a}.attention.linear_value_length"] = LINEAR["v_hd"]
+        meta[f"{a}.attention.linear_head_count_kv"] = LINEAR["n_k"]
+        meta[f"{a}.attention.linear_head_count"] = LINEAR["n_v"]
+        meta[f"{a}.ssm.conv_kernel"] = LINEAR["conv"]
     tensors = []
 
     def norm(name):
         tensors.append((name, G.F32, (s["hidden"],), (1 + 0.01 * rng.standard_normal(s["hidden"])).astype(np.float32)))
 
-    def mat(name, t, N, K, seed):
-        tensors.append((name, t, (K, N), synth.random_blocks(t, N, K, seed=seed)))
+    def mat(name, t, N, K, seed, scale=1.0):
+        tensors.append((name, t, (K, N), synth.random_blocks(t, N, K, seed=seed, d_scale=2e-3 * scale,
+                                                             dmin_scale=1e-3 * scale)))
 
     if v["embd"] == G.F32:
         tensors.append(("token_embd.weight", G.F32, (s["hidden"], s["vocab"]),
@@ -103,6 +137,20 @@ def write(path: Path, variant: str) -> Path:
     for li, lt in enumerate(v["layers"]):
         norm(f"blk.{li}.attn_norm.weight")
         norm(f"blk.{li}.ffn_norm.weight")
+        if li in linear:
+            for j, (key, (N, K)) in enumerate(_linear_shapes(s).items()):
+                stem = _LINEAR_STEMS.get(key) or _STEMS[key]
+                # q/k/v small enough that the delta rule, which the reference
+                # runs on unnormalised keys, stays stable (beta |k|^2 < 2)
+                mat(f"blk.{li}.{stem}.weight", lt[key], N, K, 1000 + 10 * li + j,
+                    scale=0.0075 if key == "w_qkv" else 1.0)
+            nv, val, cw = LINEAR["n_v"], LINEAR["n_v"] * LINEAR["v_hd"], LINEAR["conv"]
+            tensors.append((f"blk.{li}.ssm_a", G.F32, (nv,), (0.5 * rng.standard_normal(nv)).astype(np.float32)))
+            tensors.append((f"blk.{li}.ssm_conv1d.weight", G.F32, (cw, val),
+                            (0.5 * rng.standard_normal((val, cw))).astype(np.float32)))
+            tensors.append((f"blk.{li}.ssm_norm.weight", G.F32, (val,),
+                            (1 + 0.1 * rng.standard_normal(val)).astype(np.float32)))
+            continue
         for j, (key, (N, K)) in enumerate(_shapes(s).items()):
             mat(f"blk.{li}.{_STEMS[key]}.weight", lt[key], N, K, 1000 + 10 * li + j)
         hd = s["hidden"] // s["heads"]

@@ -218,10 +218,8 @@ def files_with(tmp_path, changes: dict, drop=(), extra_tensors=(), retype=None):
 
 
 def test_unsupported_models_rejected(tmp_path):
-    gdn = ("blk.0.attn_qkv.weight", G.F32, (256,), np.zeros(256, np.float32))  # a GatedDeltaNet layer
-    for kw in (dict(changes={"general.architecture": "qwen35"}),
+    for kw in (dict(changes={"general.architecture": "qwen35moe"}),
                dict(changes={"llama.rope.dimension_count": 32}),
-               dict(changes={}, extra_tensors=[gdn]),
                dict(changes={}, drop=("blk.1.ffn_up.weight",)),
                dict(changes={}, retype=("blk.0.attn_q.weight", G.F16)),
                dict(changes={"llama.block_count": 0})):
@@ -229,6 +227,19 @@ def test_unsupported_models_rejected(tmp_path):
         with pytest.raises(G.GGUFError):
             cfg = G.llama_config(G.GGUFFile(p))
             G.llama_weights(G.GGUFFile(p), cfg)
+
+
+def test_hybrid_file_without_its_linear_projections_rejected(tmp_path):
+    """A GatedDeltaNet layer needs attn_qkv and ssm_out (the reference runs
+    such a layer as an identity residual, src/model.h:508; the decoder
+    refuses the file instead)."""
+    src = G.GGUFFile(LG.write(tmp_path / "h.gguf", "hybrid"))
+    for drop in ("blk.0.attn_qkv.weight", "blk.0.ssm_out.weight"):
+        tensors = [(n, i.type, i.dims[:i.n_dims], src.get_tensor_data(n)) for n, i in src.tensors.items() if n != drop]
+        p = tmp_path / f"d{len(list(tmp_path.iterdir()))}.gguf"
+        G.write_gguf(p, dict(src.metadata), tensors, alignment=src.alignment)
+        with pytest.raises(G.GGUFError):
+            G.llama_config(G.GGUFFile(p))
 
 
 def test_neox_architectures(tmp_path):

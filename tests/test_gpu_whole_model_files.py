@@ -26,12 +26,13 @@ from test_gpu_model import LOGIT_TOL, _teacher_forced
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("variant", ["mix", "tied", "neox", "bias", "qknorm"])
+@pytest.mark.parametrize("variant", ["mix", "tied", "neox", "bias", "qknorm", "hybrid"])
 def test_gguf_model_matches_reference_logits(cuda, tmp_path, variant):
     """LlamaDecoder.from_gguf on a tiny GGUF file -- "mix": all seven formats,
     a different type mix per layer, F32 embedding table; "tied": a Q8_0
-    embedding table that is also the LM head -- teacher-forced, against the
-    logits the reference's own Model::forward gave for the same file
+    embedding table that is also the LM head; "hybrid": a GatedDeltaNet layer
+    then a full-attention layer -- teacher-forced, against the logits the
+    reference's own Model::forward gave for the same file
     (tests/golden/golden_llama_<variant>.npz)."""
     import llama_gguf as LG
     from conftest import GOLDEN
