@@ -130,6 +130,162 @@ __global__ void __launch_bounds__(PF_WARPS * 32) attention_prefill_kernel(
     for (int i = 0; i < PER; ++i) oh[i] = acc[i] * inv_l;
 }
 
+
+// Causal attention for a whole prompt, tiled (the form used for head_dim 64
+// and 128): CTA = (64 query rows of one sequence, query head h), 256 threads.
+// Q rows live in shared memory; key/value positions 0 .. the tile's last
+// query position stream through in tiles of 64.  Thread (ty, tx), ty =
+// t / 16, tx = t % 16, owns scores S[ty + 16 i][tx + 16 j] (i, j < 4) of a
+// tile and output rows ty + 16 i, dims 4 tx .. 4 tx + 3 (+ 64 for head_dim
+// 128).  Online softmax per row (the 16 threads of a row are 16 lanes of one
+// warp: max and sum by shuffles), masked causally (key t <= the row's
+// position).  fp32 throughout, like the reference's loops
+// (src/model.h:329-361); the sums run in another order.
+template <int HD>
+__global__ void __launch_bounds__(256) attention_prefill_tiled(
+    float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ kcache,
+    const float* __restrict__ vcache, int pos0, int seq_len, int num_heads, int num_kv_heads, int max_seq, int ldq,
+    int ldo) {
+    constexpr int BM = 64, BN = 64, KS = HD + 4;  // K rows padded: 16 consecutive rows hit distinct banks
+    constexpr int DPT = HD / 16;                  // output dims per thread (4 or 8)
+    extern __shared__ float psm[];
+    float* Qs = psm;             // [BM][HD]
+    float* Ks = Qs + BM * HD;    // [BN][KS]
+    float* Vs = Ks + BN * KS;    // [BN][HD]
+    float* Ps = Vs + BN * HD;    // [BM][BN + 1]
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    // heavier (later) query tiles first: the causal work grows with the tile
+    const int qt = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
+    const int p0 = qt * BM;
+    const int nrow = min(BM, seq_len - p0);
+    const int kvh = h / (num_heads / num_kv_heads);
+    const int kv_dim = num_kv_heads * HD;
+    const size_t m0 = static_cast<size_t>(seq) * seq_len + p0;
+    for (int i = tid; i < BM * HD / 4; i += 256) {
+        const int r = i / (HD / 4), c = (i % (HD / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < nrow) {
+            const float* src = q + (m0 + r) * ldq + h * HD + c;
+            v = make_float4(src[0], src[1], src[2], src[3]);
+        }
+        *reinterpret_cast<float4*>(Qs + r * HD + c) = v;
+    }
+    const float* kb = kcache + static_cast<size_t>(seq) * max_seq * kv_dim + kvh * HD;
+    const float* vb = vcache + static_cast<size_t>(seq) * max_seq * kv_dim + kvh * HD;
+    const float sqrt_hd = sqrtf(static_cast<float>(HD));
+    float mrow[4], lrow[4], acc[4][DPT];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        mrow[i] = -INFINITY;
+        lrow[i] = 0.f;
+#pragma unroll
+        for (int d = 0; d < DPT; ++d) acc[i][d] = 0.f;
+    }
+    const int last = pos0 + p0 + nrow - 1;  // last key position any row of the tile sees
+    for (int t0 = 0; t0 <= last; t0 += BN) {
+        __syncthreads();  // the previous tile's K, V, P are consumed
+        for (int i = tid; i < BN * HD / 4; i += 256) {
+            const int r = i / (HD / 4), c = (i % (HD / 4)) * 4;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (t0 + r <= last) {
+                const float* ks = kb + static_cast<size_t>(t0 + r) * kv_dim + c;
+                const float* vs = vb + static_cast<size_t>(t0 + r) * kv_dim + c;
+                kv = make_float4(ks[0], ks[1], ks[2], ks[3]);
+                vv = make_float4(vs[0], vs[1], vs[2], vs[3]);
+            }
+            *reinterpret_cast<float4*>(Ks + r * KS + c) = kv;
+            *reinterpret_cast<float4*>(Vs + r * HD + c) = vv;
+        }
+        __syncthreads();
+        float sc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < HD; d += 4) {
+            float4 qa[4], ka[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qa[i] = *reinterpret_cast<const float4*>(Qs + (ty + 16 * i) * HD + d);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ka[j] = *reinterpret_cast<const float4*>(Ks + (tx + 16 * j) * KS + d);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float s = sc[i][j];
+                    s = fmaf(qa[i].x, ka[j].x, s);
+                    s = fmaf(qa[i].y, ka[j].y, s);
+                    s = fmaf(qa[i].z, ka[j].z, s);
+                    s = fmaf(qa[i].w, ka[j].w, s);
+                    sc[i][j] = s;
+                }
+        }
+        // mask, online softmax per row, P into shared memory
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = ty + 16 * i;
+            const int qpos = pos0 + p0 + r;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int t = t0 + tx + 16 * j;
+                sc[i][j] = (r < nrow && t <= qpos) ? sc[i][j] / sqrt_hd : -INFINITY;
+                mx = fmaxf(mx, sc[i][j]);
+            }
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float mnew = fmaxf(mrow[i], mx);
+            // rows with nothing unmasked yet keep m = -inf: scale 1, p = 0
+            const float corr = mnew == -INFINITY ? 1.f : expf(mrow[i] - mnew);
+            float ps = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float pv = mnew == -INFINITY ? 0.f : expf(sc[i][j] - mnew);
+                Ps[r * (BN + 1) + tx + 16 * j] = pv;
+                ps += pv;
+            }
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+            lrow[i] = lrow[i] * corr + ps;
+            mrow[i] = mnew;
+#pragma unroll
+            for (int dd = 0; dd < DPT; ++dd) acc[i][dd] *= corr;
+        }
+        __syncthreads();
+        // O += P V
+        const int kmax = min(BN, last - t0 + 1);
+        for (int kk = 0; kk < kmax; ++kk) {
+            const float4 v0 = *reinterpret_cast<const float4*>(Vs + kk * HD + 4 * tx);
+            float4 v1 = v0;
+            if constexpr (DPT == 8) v1 = *reinterpret_cast<const float4*>(Vs + kk * HD + 64 + 4 * tx);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float pv = Ps[(ty + 16 * i) * (BN + 1) + kk];
+                acc[i][0] = fmaf(pv, v0.x, acc[i][0]);
+                acc[i][1] = fmaf(pv, v0.y, acc[i][1]);
+                acc[i][2] = fmaf(pv, v0.z, acc[i][2]);
+                acc[i][3] = fmaf(pv, v0.w, acc[i][3]);
+                if constexpr (DPT == 8) {
+                    acc[i][4] = fmaf(pv, v1.x, acc[i][4]);
+                    acc[i][5] = fmaf(pv, v1.y, acc[i][5]);
+                    acc[i][6] = fmaf(pv, v1.z, acc[i][6]);
+                    acc[i][7] = fmaf(pv, v1.w, acc[i][7]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = ty + 16 * i;
+        if (r >= nrow) continue;
+        float* o = out + (m0 + r) * ldo + h * HD;
+        const float inv = 1.f / lrow[i];
+#pragma unroll
+        for (int dd = 0; dd < DPT; ++dd) o[(dd < 4 ? 4 * tx : 64 + 4 * tx - 4) + dd] = acc[i][dd] * inv;
+    }
+}
+
 }  // namespace
 
 cudaError_t rope_kv_prefill_launch(float* q, const float* k, const float* v, float* kcache, float* vcache, int pos0,
@@ -147,6 +303,28 @@ cudaError_t rope_kv_prefill_launch(float* q, const float* k, const float* v, flo
 cudaError_t attention_prefill_launch(float* out, const float* q, const float* kcache, const float* vcache, int pos0,
                                      int seq_len, int rows, int num_heads, int num_kv_heads, int head_dim,
                                      int max_seq, int ldq, int ldo, cudaStream_t s) {
+    if ((head_dim == 64 || head_dim == 128) && seq_len > 0 && rows % seq_len == 0 && (ldq % 4) == 0 &&
+        (reinterpret_cast<uintptr_t>(q) & 15u) == 0 && (num_kv_heads * head_dim) % 4 == 0) {
+        const int nseq = rows / seq_len;
+        const dim3 grid((seq_len + 63) / 64, num_heads, nseq);
+        if (nseq > 65535 || num_heads > 65535) return cudaErrorInvalidConfiguration;
+        const size_t smem = (64 * head_dim + 64 * (head_dim + 4) + 64 * head_dim + 64 * 65) * sizeof(float);
+        cudaError_t e;
+        if (head_dim == 128) {
+            e = cudaFuncSetAttribute(attention_prefill_tiled<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+            attention_prefill_tiled<128><<<grid, 256, smem, s>>>(out, q, kcache, vcache, pos0, seq_len, num_heads,
+                                                                  num_kv_heads, max_seq, ldq, ldo);
+        } else {
+            e = cudaFuncSetAttribute(attention_prefill_tiled<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+            attention_prefill_tiled<64><<<grid, 256, smem, s>>>(out, q, kcache, vcache, pos0, seq_len, num_heads,
+                                                                 num_kv_heads, max_seq, ldq, ldo);
+        }
+        return cudaGetLastError();
+    }
     const long long warps = static_cast<long long>(rows) * num_heads;
     const long long blocks = (warps + PF_WARPS - 1) / PF_WARPS;
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;

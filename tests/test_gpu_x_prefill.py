@@ -41,7 +41,11 @@ def _attention_ref(q, kc, vc, pos0, P, S, H, Hkv, hd):
 
 
 @pytest.mark.parametrize("S,P,pos0,H,Hkv,hd", [(1, 9, 0, 8, 2, 64), (3, 5, 4, 8, 8, 128), (2, 17, 11, 4, 1, 128),
-                                                (1, 40, 0, 2, 2, 256), (2, 3, 0, 4, 2, 32)])
+                                                (1, 40, 0, 2, 2, 256), (2, 3, 0, 4, 2, 32),
+                                                # tiled kernel: several query and key tiles, a
+                                                # tile boundary, a context before the prompt
+                                                (1, 200, 70, 8, 2, 128), (2, 130, 0, 4, 4, 64),
+                                                (1, 64, 0, 2, 1, 128), (1, 65, 63, 4, 2, 64)])
 def test_attention_prefill_matches_numpy(cuda, S, P, pos0, H, Hkv, hd):
     torch = cuda
     import swq
