@@ -342,14 +342,31 @@ __global__ void __launch_bounds__(AttCfg<MUL, PER>::THREADS) attn_kernel(
 // out[r, i] = silu(gate[r*ld + i]) * up[r*ld + i], silu(x) = x / (1 + exp(-x))
 // (src/tensor.h:1050-1064); out is rows x n, row-major.
 __global__ void silu_mul_kernel(float* __restrict__ out, const float* __restrict__ gate, const float* __restrict__ up,
-                                int n, int rows, int ld) {
+                                int n, int rows, int ld, int vec) {
     pdl_wait_primary();
-    const int64_t total = static_cast<int64_t>(n) * rows;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t r = i / n, c = i - r * n;
-        const float g = gate[r * ld + c];
-        out[i] = g / (1.0f + expf(-g)) * up[r * ld + c];
+    // rows over grid y, columns over grid x; 4 columns per thread when every
+    // row of the three arrays starts 16-byte aligned
+    for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+        const float* g = gate + static_cast<size_t>(r) * ld;
+        const float* u = up + static_cast<size_t>(r) * ld;
+        float* o = out + static_cast<size_t>(r) * n;
+        if (vec) {
+            for (int c = 4 * (blockIdx.x * blockDim.x + threadIdx.x); c < n; c += 4 * gridDim.x * blockDim.x) {
+                const float4 gv = *reinterpret_cast<const float4*>(g + c);
+                const float4 uv = *reinterpret_cast<const float4*>(u + c);
+                float4 ov;
+                ov.x = gv.x / (1.0f + expf(-gv.x)) * uv.x;
+                ov.y = gv.y / (1.0f + expf(-gv.y)) * uv.y;
+                ov.z = gv.z / (1.0f + expf(-gv.z)) * uv.z;
+                ov.w = gv.w / (1.0f + expf(-gv.w)) * uv.w;
+                *reinterpret_cast<float4*>(o + c) = ov;
+            }
+        } else {
+            for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < n; c += gridDim.x * blockDim.x) {
+                const float gv = g[c];
+                o[c] = gv / (1.0f + expf(-gv)) * u[c];
+            }
+        }
     }
 }
 
@@ -540,8 +557,15 @@ cudaError_t attention_launch(float* out, const float* q, const float* kcache, co
 
 cudaError_t silu_mul_launch(float* out, const float* gate, const float* up, int n, int rows, int ld, int num_sms,
                             cudaStream_t s) {
-    ERR_RET(launch_pdl(silu_mul_kernel, dim3(grid_for(static_cast<int64_t>(n) * rows, num_sms)), dim3(256), s, out,
-                       gate, up, n, rows, ld));
+    const int vec = (n % 4 == 0 && ld % 4 == 0 && ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(gate) |
+                                                    reinterpret_cast<uintptr_t>(up)) & 15u) == 0) ? 1 : 0;
+    const int per = vec ? 4 * 256 : 256;
+    int gx = (n + per - 1) / per;
+    int gy = std::min(rows, 65535);
+    // about four CTAs per SM in all, at least one column block per row
+    const int want = std::max(1, 4 * num_sms / std::max(1, gy));
+    gx = std::max(1, std::min(gx, want));
+    ERR_RET(launch_pdl(silu_mul_kernel, dim3(gx, gy), dim3(256), s, out, gate, up, n, rows, ld, vec));
     return cudaGetLastError();
 }
 
