@@ -396,7 +396,26 @@ enum {
      * included); 1: Q6_K only, in the earlier form (fixed point per
      * 16-element sub-block, one conversion per sub-block); 0: neither (the
      * fp32 form of SWQ_OPT_GEMV_FP32_ACT). */
-    SWQ_OPT_GEMV_INT_MMA = 10
+    SWQ_OPT_GEMV_INT_MMA = 10,
+    /* Largest M served by the batched K-quant GEMV: Q4_K and Q6_K with
+     * 2 <= M <= this value (at most 32; K a multiple of 256, Q6_K of 2048)
+     * read each weight once for all rows; per row, x is split into two fp16
+     * parts relative to each 256-element super-block's largest element (22
+     * bits), every product with a quant value is exact on the tensor cores
+     * and the sums are fp32.  It takes precedence over the tensor-core GEMM
+     * and the CUDA-core GEMV for those calls.  Default 16 (from 17 rows on,
+     * the tensor-core GEMM is faster on large matrices); 0 or 1 turns it
+     * off.  Its
+     * scratch comes from the workspace (swq_gemm_act_ws /
+     * swq_gemm_workspace_bytes) or libswq's stream-ordered pool; calls with
+     * SWQ_GEMM_NOALLOC keep the tensor-core GEMM. */
+    SWQ_OPT_GEMV_BATCH_MAX_M = 11,
+    /* Tuning of the batched K-quant GEMV: shared-memory KB of the activation
+     * table of one K split (8..160, default 72; K is split so that a split's
+     * table fits), and consumer warps per 16-row tile (0 = automatic, or 1,
+     * 2, 4, 8, 16). */
+    SWQ_OPT_GEMV_BATCH_TABLE_KB = 12,
+    SWQ_OPT_GEMV_BATCH_GROUP = 13
 };
 swq_status swq_set_option(int option, int value);
 int swq_get_option(int option);

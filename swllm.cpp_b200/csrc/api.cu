@@ -24,6 +24,7 @@
 #include "gemm_tc.h"
 #include "gdn.h"
 #include "gemv.h"
+#include "gemv_kqm.h"
 
 namespace {
 
@@ -39,6 +40,9 @@ std::atomic<int> g_opt_gemv_stage_kb{0};
 std::atomic<int> g_opt_gemv_ctas{0};
 std::atomic<int> g_opt_gemv_fp32{1};
 std::atomic<int> g_opt_gemv_imma{2};
+std::atomic<int> g_opt_kqm_max_m{16};
+std::atomic<int> g_opt_kqm_table_kb{72};
+std::atomic<int> g_opt_kqm_group{0};
 
 swq_status fail(swq_status s, const std::string& msg) {
     g_last_error = msg;
@@ -117,6 +121,38 @@ swq_status check_gemm_args(int type, const void* W, const float* X, const float*
     if (M == 0 || N == 0 || K == 0) return SWQ_OK;
     if (!W || !X || !Y) return fail(SWQ_ERR_NULL_PTR, "null W, X or Y");
     return SWQ_OK;
+}
+
+// The batched K-quant GEMV (2 <= M <= SWQ_OPT_GEMV_BATCH_MAX_M rows of Q4_K or
+// Q6_K) takes this call.
+bool kqm_takes(int type, const void* W, int M, int N, int K, const swq::DeviceInfo& dev) {
+    return g_opt_kqm_max_m >= 2 &&
+           swq::gemv_kqm_supported(type, W, M, N, K, g_opt_kqm_max_m, dev.num_sms, dev.smem_per_block_optin);
+}
+
+// Batched K-quant GEMV with its scratch from the caller (ws) or, when ws is
+// null, from libswq's stream-ordered pool.
+swq_status kqm_run(int type, const void* W, const float* X, float* Y, int M, int N, int K, const swq::ActArgs& act,
+                   const swq::DeviceInfo& dev, cudaStream_t s, void* ws = nullptr, size_t ws_bytes = 0) {
+    const size_t need = swq::gemv_kqm_workspace_bytes(type, M, N, K, dev.num_sms, dev.smem_per_block_optin);
+    if (ws != nullptr) {
+        if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0)
+            return fail(SWQ_ERR_BAD_ARG, "workspace not 256-byte aligned");
+        if (ws_bytes < need)
+            return fail(SWQ_ERR_BAD_ARG, "workspace of " + std::to_string(ws_bytes) + " bytes, this call needs " +
+                                             std::to_string(need));
+        cudaError_t e = swq::gemv_kqm_launch(type, W, X, Y, M, N, K, act, g_opt_early_prefetch, dev.num_sms,
+                                             dev.smem_per_block_optin, ws, ws_bytes, s);
+        return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "batched K-quant GEMV launch (caller workspace)");
+    }
+    void* buf = nullptr;
+    cudaError_t e = swq::scratch_alloc(&buf, need, s);
+    if (e != cudaSuccess) return cuda_fail(e, "batched K-quant GEMV scratch");
+    e = swq::gemv_kqm_launch(type, W, X, Y, M, N, K, act, g_opt_early_prefetch, dev.num_sms, dev.smem_per_block_optin,
+                             buf, need, s);
+    cudaError_t e2 = swq::scratch_free(buf, s);
+    if (e != cudaSuccess) return cuda_fail(e, "batched K-quant GEMV launch");
+    return e2 == cudaSuccess ? SWQ_OK : cuda_fail(e2, "batched K-quant GEMV scratch free");
 }
 
 // Y = X . W^T through the GEMV kernel, groups of up to max_m rows of X.
@@ -229,6 +265,21 @@ swq_status swq_set_option(int option, int value) {
             if (value < 0 || value > 2) return fail(SWQ_ERR_BAD_ARG, "option value must be 0, 1 or 2");
             g_opt_gemv_imma = value;
             return SWQ_OK;
+        case SWQ_OPT_GEMV_BATCH_MAX_M:
+            if (value < 0) return fail(SWQ_ERR_BAD_ARG, "option value must be >= 0");
+            g_opt_kqm_max_m = value;
+            return SWQ_OK;
+        case SWQ_OPT_GEMV_BATCH_TABLE_KB:
+            if (value < 8 || value > 160) return fail(SWQ_ERR_BAD_ARG, "option value must be 8..160");
+            g_opt_kqm_table_kb = value;
+            swq::gemv_kqm_tune(g_opt_kqm_table_kb, g_opt_kqm_group);
+            return SWQ_OK;
+        case SWQ_OPT_GEMV_BATCH_GROUP:
+            if (value != 0 && value != 1 && value != 2 && value != 4 && value != 8 && value != 16)
+                return fail(SWQ_ERR_BAD_ARG, "option value must be 0, 1, 2, 4, 8 or 16");
+            g_opt_kqm_group = value;
+            swq::gemv_kqm_tune(g_opt_kqm_table_kb, g_opt_kqm_group);
+            return SWQ_OK;
         default:
             return fail(SWQ_ERR_BAD_ARG, "unknown option " + std::to_string(option));
     }
@@ -246,6 +297,9 @@ int swq_get_option(int option) {
         case SWQ_OPT_GEMV_CTAS_PER_SM: return g_opt_gemv_ctas;
         case SWQ_OPT_GEMV_FP32_ACT: return g_opt_gemv_fp32;
         case SWQ_OPT_GEMV_INT_MMA: return g_opt_gemv_imma;
+        case SWQ_OPT_GEMV_BATCH_MAX_M: return g_opt_kqm_max_m;
+        case SWQ_OPT_GEMV_BATCH_TABLE_KB: return g_opt_kqm_table_kb;
+        case SWQ_OPT_GEMV_BATCH_GROUP: return g_opt_kqm_group;
         default: return -1;
     }
 }
@@ -279,6 +333,7 @@ swq_status swq_gemm(int type, const void* W, const float* X, float* Y, int M, in
         return e == cudaSuccess ? SWQ_OK : cuda_fail(e, "cudaMemsetAsync");
     }
     const int max_m = g_opt_gemv_max_m;
+    if (kqm_takes(type, W, M, N, K, dev)) return kqm_run(type, W, X, Y, M, N, K, swq::ActArgs{}, dev, s);
     if (M >= g_opt_tc_min_m && g_opt_gemm_tc &&
         swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
         cudaError_t e = swq::gemm_tc_launch(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms, s);
@@ -323,6 +378,7 @@ swq_status swq_gemm_act(int type, const void* W, const float* X, float* Y, int M
     if ((st = current_device(&dev)) != SWQ_OK) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (K == 0) return fail(SWQ_ERR_BAD_SHAPE, "swq_gemm_act needs K > 0");
+    if (!noalloc && kqm_takes(type, W, M, N, K, dev)) return kqm_run(type, W, X, Y, M, N, K, a, dev, s);
     if (M >= g_opt_tc_min_m && g_opt_gemm_tc && swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
         cudaError_t e = noalloc ? swq::gemm_tc_launch_noalloc(type, W, X, Y, M, N, K, g_opt_q2k_refcpu, dev.num_sms,
                                                               s, a)
@@ -336,9 +392,12 @@ swq_status swq_gemm_act(int type, const void* W, const float* X, float* Y, int M
 size_t swq_gemm_workspace_bytes(int type, int M, int N, int K) {
     TypeInfo ti;
     if (!type_info(type, &ti) || M <= 0 || N <= 0 || K <= 0 || K % ti.qk != 0) return 0;
-    if (M < g_opt_tc_min_m || !g_opt_gemm_tc) return 0;  // the GEMV kernel needs no scratch
     swq::DeviceInfo dev;
     if (current_device(&dev) != SWQ_OK) return 0;
+    // the batched K-quant GEMV (W's alignment is checked again at the call)
+    if (kqm_takes(type, reinterpret_cast<const void*>(256), M, N, K, dev))
+        return swq::gemv_kqm_workspace_bytes(type, M, N, K, dev.num_sms, dev.smem_per_block_optin);
+    if (M < g_opt_tc_min_m || !g_opt_gemm_tc) return 0;  // the GEMV kernel needs no scratch
     return swq::gemm_tc_workspace_bytes(M, N, K, dev.num_sms);
 }
 
@@ -353,6 +412,10 @@ swq_status swq_gemm_act_ws(int type, const void* W, const float* X, float* Y, in
     swq::DeviceInfo dev;
     if ((st = current_device(&dev)) != SWQ_OK) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (kqm_takes(type, W, M, N, K, dev)) {
+        if (!workspace) return fail(SWQ_ERR_NULL_PTR, "swq_gemm_act_ws: this call needs a workspace");
+        return kqm_run(type, W, X, Y, M, N, K, a, dev, s, workspace, workspace_bytes);
+    }
     if (M >= g_opt_tc_min_m && g_opt_gemm_tc && swq::gemm_tc_supported(type, W, M, N, K, g_opt_q2k_refcpu)) {
         const size_t need = swq::gemm_tc_workspace_bytes(M, N, K, dev.num_sms);
         if (!workspace) return fail(SWQ_ERR_NULL_PTR, "swq_gemm_act_ws: this call needs a workspace");
@@ -742,16 +805,17 @@ swq_status swq_check(swq_stream_t stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
-    unsigned a = 0, b = 0, c = 0, d = 0, m = 0, a2 = 0, a3 = 0;
+    unsigned a = 0, b = 0, c = 0, d = 0, m = 0, a2 = 0, a3 = 0, a4 = 0;
     if ((e = swq::status_fetch_gemv(&a, s)) != cudaSuccess ||
         (e = swq::status_fetch_gemv_imma(&a2, s)) != cudaSuccess ||
         (e = swq::status_fetch_gemv_kq(&a3, s)) != cudaSuccess ||
+        (e = swq::status_fetch_gemv_kqm(&a4, s)) != cudaSuccess ||
         (e = swq::status_fetch_dequant(&b, s)) != cudaSuccess ||
         (e = swq::status_fetch_gemm_tc(&c, s)) != cudaSuccess ||
         (e = swq::status_fetch_allreduce(&d, s)) != cudaSuccess ||
         (e = swq::status_fetch_moe(&m, s)) != cudaSuccess)
         return cuda_fail(e, "status fetch");
-    a |= a2 | a3;
+    a |= a2 | a3 | a4;
     if (m & swq::kStatusBadId) {
         char buf[128];
         std::snprintf(buf, sizeof(buf), "an expert id outside [0, n_experts) was left out of the MoE sort "

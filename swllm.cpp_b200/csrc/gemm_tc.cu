@@ -1459,6 +1459,15 @@ static cudaError_t scratch_pool(cudaMemPool_t* out) {
     return cudaSuccess;
 }
 
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t s) {
+    cudaMemPool_t pool = nullptr;
+    cudaError_t e = scratch_pool(&pool);
+    if (e != cudaSuccess) return e;
+    return cudaMallocFromPoolAsync(p, bytes, pool, s);
+}
+
+cudaError_t scratch_free(void* p, cudaStream_t s) { return cudaFreeAsync(p, s); }
+
 cudaError_t gemm_tc_launch(int type, const void* W, const float* X, float* Y, int M, int N, int K, int refcpu,
                            int num_sms, cudaStream_t s, const ActArgs& act) {
     if (!gemm_tc_supported(type, W, M, N, K, refcpu)) return cudaErrorNotSupported;

@@ -20,6 +20,10 @@ struct ActArgs {
     const int* rows_dev = nullptr;  // device row count: rows at or past it are not converted
 };
 
+// Stream-ordered scratch from libswq's pool on the current device (kept for
+// the next call once freed).
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t s);
+cudaError_t scratch_free(void* p, cudaStream_t s);
 // True when the tcgen05 GEMM serves this problem.
 bool gemm_tc_supported(int type, const void* W, int M, int N, int K, int refcpu);
 // Y[M x N] = X[M x K] . W[N x K]^T on tensor cores.

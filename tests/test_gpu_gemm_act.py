@@ -94,17 +94,20 @@ def test_bad_prologue_arguments(cuda):
         swq.gemm_act(swq.Q4_K, w, x, y, 1, 4, 256, kind=swq.ACT_SWIGLU, ld=300)  # ld < 2K
 
 
-@pytest.mark.parametrize("fmt,M,N,K", [("Q4_K", 40, 640, 2048), ("Q6_K", 300, 1000, 4096), ("Q4_K", 3, 512, 1024)])
+@pytest.mark.parametrize("fmt,M,N,K", [("Q4_K", 40, 640, 2048), ("Q6_K", 300, 1000, 4096), ("Q4_K", 3, 512, 1024),
+                                       ("Q5_K", 3, 512, 1024), ("Q6_K", 12, 1000, 2048)])
 def test_caller_workspace_matches_pool(cuda, fmt, M, N, K):
     """swq_gemm_act_ws with a workspace of exactly swq_gemm_workspace_bytes:
     the same kernels and split plan as the pool form, so the same bits (the
-    GEMV rows, M <= 4, need no workspace at all)."""
+    CUDA-core GEMV rows, M <= 4 of the other formats, need no workspace; the
+    batched K-quant GEMV needs one for its activation table)."""
     torch = cuda
     t = synth.IDS[fmt]
     d_w = torch.from_numpy(synth.random_blocks(t, N, K, seed=7300 + M).reshape(-1)).cuda()
     d_x = torch.from_numpy(synth.random_activations(M, K, seed=7301)).cuda()
     need = swq.gemm_workspace_bytes(t, M, N, K)
-    assert (need == 0) == (M < swq.get_option(swq.OPT_TENSOR_CORE_MIN_M))
+    batched = fmt in ("Q4_K", "Q6_K") and 2 <= M <= swq.get_option(swq.OPT_GEMV_BATCH_MAX_M)
+    assert (need == 0) == (not batched and M < swq.get_option(swq.OPT_TENSOR_CORE_MIN_M))
     ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
     y1, y2 = torch.empty((M, N), device="cuda"), torch.full((M, N), float("nan"), device="cuda")
     swq.gemm(t, d_w, d_x, y1, M, N, K)

@@ -75,7 +75,10 @@ def test_greedy_decode_matches_reference(cuda, graph):
 
 
 def test_batch_rows_are_independent(cuda):
-    """Four sequences in step equal four single-sequence runs."""
+    """Four sequences in step equal four single-sequence runs: the same tokens,
+    logits within 1e-4 (four rows run the batched K-quant GEMV, x split into
+    two fp16 parts per super-block; one row the integer single-row form; each
+    is within 1e-5 of the reference per projection)."""
     torch = cuda
     cfg = _small()
     W = _weights(cfg, seed=8)
@@ -92,7 +95,7 @@ def test_batch_rows_are_independent(cuda):
         one.generate(4)
         one.stream.synchronize()
         assert np.array_equal(one.history[:4, 0].cpu().numpy(), both[:, r])
-        assert rel_l2(one.logits[0].cpu().numpy(), logits4[r]) <= 1e-5
+        assert rel_l2(one.logits[0].cpu().numpy(), logits4[r]) <= 1e-4
 
 
 def test_synthetic_weights_decode_runs(cuda):
