@@ -52,7 +52,8 @@ DECODE_DEADLINE_S = 540  # decode and MoE measurements of the default run (about
 N_ROWS, K_COLS, M_ROWS = 4096, 4096, 1
 COPIES = 64
 REPLAYS = 128       # graph replays per step: a step is REPLAYS x COPIES GEMVs
-GEMV_STREAMS = 2    # streams the COPIES independent GEMVs of a graph alternate over
+GEMV_STREAMS = 4    # streams the COPIES independent GEMVs of a graph alternate over
+GEMV_CTAS_PER_SM = 3  # SWQ_OPT_GEMV_CTAS_PER_SM for them: three GEMVs (CTAs of 8 warps) on each SM at once
 REF_STEP_GEMVS = 64  # GEMVs per step of the reference arm
 Q4_K = 12
 BLOCK_BYTES = 144
@@ -60,11 +61,11 @@ W_BYTES = N_ROWS * (K_COLS // 256) * BLOCK_BYTES              # 9,437,184
 ALG_BYTES = W_BYTES + 4 * K_COLS * M_ROWS + 4 * N_ROWS * M_ROWS  # 9,469,952 per GEMV
 WORKLOAD = (f"Q4_K GEMV N={N_ROWS} K={K_COLS} M={M_ROWS}, {COPIES} rotating weight copies "
             f"({COPIES * W_BYTES / 1e6:.0f} MB)")
-# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_kq_kernel<Q4_K, 16>
-# launch of this workload: the mean of three launches of one ncu capture
-# (profiles/gemv_kq_q4k_4096x4096.md: 9,487,104 / 9,486,080 / 9,490,944 read,
-# 0 written).
-NCU_TRAFFIC_PER_LAUNCH = 9488043
+# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_kq_kernel<Q4_K, 8>
+# launch of this workload (the launch shape of the timed graph): the mean of
+# three launches of one ncu capture (profiles/gemv_kq_q4k_4096x4096.md:
+# 9,492,992 / 9,491,968 / 9,496,576 read, 0 written).
+NCU_TRAFFIC_PER_LAUNCH = 9493845
 
 
 _T0 = time.time()
@@ -401,7 +402,7 @@ def run_swq(args, rank: int, world: int) -> None:
 
     torch.cuda.synchronize()
 
-    def capture(nstreams: int):
+    def capture(nstreams: int, ctas: int = 0):
         """One CUDA graph of the COPIES GEMVs, launch i on stream i % nstreams:
         the graph holds no edge between GEMVs of different streams (they are
         independent: same x, their own W and y), so their kernels may run at
@@ -424,12 +425,15 @@ def run_swq(args, rank: int, world: int) -> None:
                 join.record(st)
                 main.wait_event(join)
 
+        old = swq.get_option(swq.OPT_GEMV_CTAS_PER_SM)
+        swq.set_option(swq.OPT_GEMV_CTAS_PER_SM, ctas)  # read at launch: the graph keeps this launch shape
         with torch.cuda.stream(main):
             issue()  # eager warm-up: attributes set, kernels loaded
         swq.check(main)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=main):
             issue()
+        swq.set_option(swq.OPT_GEMV_CTAS_PER_SM, old)
         return g, main
 
     def time_steps(g, st, steps: int, warmup: int, clocks: bool):
@@ -461,7 +465,7 @@ def run_swq(args, rank: int, world: int) -> None:
     peak, peak_kind = load_peaks()
     gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
     gpu_uuid = gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}"
-    graph, stream = capture(GEMV_STREAMS)
+    graph, stream = capture(GEMV_STREAMS, GEMV_CTAS_PER_SM)
     graph1, stream1 = capture(1)
     log(f"gemv: timing {args.steps} steps of {REPLAYS} x {COPIES} GEMVs on {GEMV_STREAMS} streams")
     ms, clocks = time_steps(graph, stream, args.steps, max(3, args.warmup), clocks=True)
@@ -515,8 +519,10 @@ def run_swq(args, rank: int, world: int) -> None:
             "config": {"workload": WORKLOAD, "format": "Q4_K", "N": N_ROWS, "K": K_COLS, "M": M_ROWS,
                        "copies": COPIES, "gemvs_per_step": REPLAYS * COPIES, "bytes_per_gemv": ALG_BYTES,
                        "issue": f"{COPIES} independent GEMVs (same x, own W and y) per graph, alternating over "
-                                f"{GEMV_STREAMS} streams; consecutive GEMVs of one stream are programmatic "
-                                f"dependents (weights prefetched, x read after the predecessor completes)",
+                                f"{GEMV_STREAMS} streams, SWQ_OPT_GEMV_CTAS_PER_SM={GEMV_CTAS_PER_SM} (a CTA of 8 "
+                                f"consumer warps per SM and GEMV, three GEMVs per SM at once); consecutive GEMVs of "
+                                f"one stream are programmatic dependents (weights prefetched, x read after the "
+                                f"predecessor completes)",
                        "l2": "inputs larger than L2 (rotating weights)",
                        "arith": "fp32 activations as 30-bit fixed point per 256-element super-block (4 int8 "
                                 "limbs); exact integer sub-block products (mma.sync u8 x s8 -> s32) scaled by the "
@@ -525,12 +531,13 @@ def run_swq(args, rank: int, world: int) -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": NCU_TRAFFIC_PER_LAUNCH,
-                         "kernel": "swq::kq::gemv_kq_kernel<Q4_K,16>", "alg_bytes_per_launch": ALG_BYTES,
+                         "kernel": "swq::kq::gemv_kq_kernel<Q4_K,8>", "alg_bytes_per_launch": ALG_BYTES,
                          "us_per_launch": round(per_launch_s * 1e6, 3),
                          "chain": {"us_per_launch": round(chain_launch_s * 1e6, 3),
                                    "achieved": round(ALG_BYTES / chain_launch_s / 1e9, 1),
                                    "frac": round(ALG_BYTES / chain_launch_s / 1e9 / peak, 4),
-                                   "note": "the same GEMVs on one stream: each waits for its predecessor"}},
+                                   "note": "the same GEMVs on one stream, default launch shape (two CTAs of "
+                                           "16 consumer warps per SM): each waits for its predecessor"}},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": COPIES * 4 * K_COLS * M_ROWS,
