@@ -43,6 +43,7 @@ std::atomic<int> g_opt_gemv_imma{2};
 std::atomic<int> g_opt_kqm_max_m{16};
 std::atomic<int> g_opt_kqm_table_kb{72};
 std::atomic<int> g_opt_kqm_group{0};
+std::atomic<int> g_opt_attn_form{2};
 
 swq_status fail(swq_status s, const std::string& msg) {
     g_last_error = msg;
@@ -280,6 +281,10 @@ swq_status swq_set_option(int option, int value) {
             g_opt_kqm_group = value;
             swq::gemv_kqm_tune(g_opt_kqm_table_kb, g_opt_kqm_group);
             return SWQ_OK;
+        case SWQ_OPT_PREFILL_ATTENTION:
+            if (value < 0 || value > 2) return fail(SWQ_ERR_BAD_ARG, "option value must be 0, 1 or 2");
+            g_opt_attn_form = value;
+            return SWQ_OK;
         default:
             return fail(SWQ_ERR_BAD_ARG, "unknown option " + std::to_string(option));
     }
@@ -300,6 +305,7 @@ int swq_get_option(int option) {
         case SWQ_OPT_GEMV_BATCH_MAX_M: return g_opt_kqm_max_m;
         case SWQ_OPT_GEMV_BATCH_TABLE_KB: return g_opt_kqm_table_kb;
         case SWQ_OPT_GEMV_BATCH_GROUP: return g_opt_kqm_group;
+        case SWQ_OPT_PREFILL_ATTENTION: return g_opt_attn_form;
         default: return -1;
     }
 }
@@ -704,7 +710,7 @@ swq_status swq_attention_prefill(float* out, const float* q, const float* k_cach
     if (st != SWQ_OK) return st;
     return launch_status(swq::attention_prefill_launch(out, q, k_cache, v_cache, pos0, seq_len, rows, num_heads,
                                                        num_kv_heads, head_dim, max_seq, ldq, ldo,
-                                                       reinterpret_cast<cudaStream_t>(stream)),
+                                                       reinterpret_cast<cudaStream_t>(stream), g_opt_attn_form),
                          "prefill attention launch");
 }
 

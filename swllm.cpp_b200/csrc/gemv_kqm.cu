@@ -735,12 +735,29 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) gemv_kqm_kernel(const Param
     named_bar_sync(1, NT);
     if (!*last_flag) return;
     __threadfence();
-    const int rows = r_end - r_begin;
-    for (int e = threadIdx.x; e < p.M * rows; e += NT) {
-        const int m = e / rows, row = r_begin + e % rows;
-        float v = 0.f;
-        for (int s = 0; s < p.S; ++s) v += __ldcg(p.part + (static_cast<size_t>(s) * MB + m) * p.N + row);
-        p.Y[static_cast<size_t>(m) * p.ldy + row] = v * s_rs[m];
+    // four outputs per thread and pass, all their partials requested before
+    // the first store (the loads of one pass are independent)
+    const int rows = r_end - r_begin, total = p.M * rows;
+    for (int e0 = threadIdx.x; e0 < total; e0 += 4 * NT) {
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        size_t off[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = min(e0 + u * NT, total - 1);
+            off[u] = static_cast<size_t>(e / rows) * p.N + r_begin + e % rows;
+        }
+        for (int s = 0; s < p.S; ++s) {
+            const float* ps = p.part + static_cast<size_t>(s) * MB * p.N;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] += __ldcg(ps + off[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = e0 + u * NT;
+            if (e >= total) break;
+            const int m = e / rows, row = r_begin + e % rows;
+            p.Y[static_cast<size_t>(m) * p.ldy + row] = v[u] * s_rs[m];
+        }
     }
     if (threadIdx.x == 0) p.cnt[gi] = 0u;
 }

@@ -11,12 +11,14 @@
 // [S*P x n] buffer; row m is position pos0 + p of sequence s.
 //
 // KV cache layout as in decode.cu: [sequence s][position t][kv_dim] per layer.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 
 #include <cstdint>
 
 #include "prefill.h"
+#include "swq_device.cuh"
 
 namespace swq {
 
@@ -286,6 +288,279 @@ __global__ void __launch_bounds__(256) attention_prefill_tiled(
     }
 }
 
+
+// Causal attention for a whole prompt on the tensor cores (head_dim 64 and
+// 128): CTA = (64 query rows of one sequence, query head h), 4 warps of 16
+// rows; key/value positions stream through shared memory in tiles of 64.
+//
+// Operands are fp16 pairs: a row x of Q or K is scaled by 2^(13 - E) (E: its
+// largest binary exponent) and split x = h + l (h = fp16 of the scaled
+// value, l = fp16 of the rest: 22 bits relative to the row's largest
+// element); S = Q K^T takes h.h + h.l + l.h on m16n8k16 MMAs with fp32
+// accumulation, then the row scales 2^(E - 13) and 1 / sqrt(head_dim) in
+// fp32.  P = exp(S - m) (online softmax per row in fp32) and V are split the
+// same way (V unscaled, except rows past 2^15 in magnitude, scaled down by a
+// power of two that P takes back) for O += P V.  Every product is exact; the
+// dropped l.l terms sit 2^-22 below the kept ones.  The reference's loops
+// (src/model.h:329-361) round every product and sum in fp32 instead.
+//
+// Fragments: Q (A) and K (B of S) as 32-bit shared loads (rows padded to
+// HD + 8 halves: the 8 rows x 4 pairs of a fragment hit 32 distinct banks);
+// P (A of O) straight from the S accumulators; V (B of O) by ldmatrix.trans
+// from its row-major tile.
+namespace amma {
+
+__device__ __forceinline__ uint32_t lds32(const __half* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const __half* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ uint32_t h2(float a, float b) {
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Split a and b into fp16 h (returned) and l (lo).
+__device__ __forceinline__ uint32_t split2(float a, float b, uint32_t& lo) {
+    const __half2 hv = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(hv);
+    lo = h2(a - hf.x, b - hf.y);
+    return *reinterpret_cast<const uint32_t*>(&hv);
+}
+
+// One row of HD fp32 values (src; null = zeros), 8 lanes (sub = lane & 7) of
+// HD / 8 each, into h / l rows of shared memory.  SCALE_TO_TOP: scaled to
+// below 2^13, *aux = 2^(E - 13) (NaN for a non-finite row); else unscaled
+// unless the row reaches 2^15 (then scaled down, *aux = the factor back).
+template <int HD, bool SCALE_TO_TOP>
+__device__ __forceinline__ void stage_row(const float* src, __half* dh, __half* dl, float* aux, int sub) {
+    constexpr int PER = HD / 8;
+    float v[PER];
+    if (src) {
+#pragma unroll
+        for (int i = 0; i < PER; i += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(src + sub * PER + i);
+            v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) v[i] = 0.f;
+    }
+    float mx = 0.f;
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        mx = fmaxf(mx, fabsf(v[i]));
+        bad |= !(fabsf(v[i]) <= 3.402823466e38f);
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        bad |= __shfl_xor_sync(0xffffffffu, bad ? 1 : 0, o) != 0;
+    }
+    const int E = max(((__float_as_int(mx) >> 23) & 0xFF) - 126, -100);  // mx < 2^E
+    float up, back;
+    if (SCALE_TO_TOP) {
+        up = __int_as_float((127 + 13 - E) << 23);
+        back = __int_as_float((127 + E - 13) << 23);
+    } else {
+        const int k = max(E - 15, 0);
+        up = __int_as_float((127 - k) << 23);
+        back = __int_as_float((127 + k) << 23);
+    }
+    if (bad) {
+        up = 0.f;
+        back = __int_as_float(0x7fc00000);
+    }
+    uint32_t H[PER / 2], L[PER / 2];
+#pragma unroll
+    for (int i = 0; i < PER; i += 2) H[i / 2] = split2(v[i] * up, v[i + 1] * up, L[i / 2]);
+#pragma unroll
+    for (int i = 0; i < PER / 2; i += 2) {
+        *reinterpret_cast<uint2*>(dh + sub * PER + 2 * i) = make_uint2(H[i], H[i + 1]);
+        *reinterpret_cast<uint2*>(dl + sub * PER + 2 * i) = make_uint2(L[i], L[i + 1]);
+    }
+    if (sub == 0) *aux = back;
+}
+
+}  // namespace amma
+
+template <int HD>
+__global__ void __launch_bounds__(128, 2) attention_prefill_mma(
+    float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ kcache,
+    const float* __restrict__ vcache, int pos0, int seq_len, int num_heads, int num_kv_heads, int max_seq, int ldq,
+    int ldo) {
+    using namespace amma;
+    constexpr int BM = 64, BN = 64, ST = HD + 8;  // row stride in halves
+    constexpr int NB = BN / 8, ND = HD / 8, KS = HD / 16;
+    extern __shared__ __align__(16) uint8_t amsm[];
+    __half* Qh = reinterpret_cast<__half*>(amsm);
+    __half* Ql = Qh + BM * ST;
+    __half* Kh = Ql + BM * ST;
+    __half* Kl = Kh + BN * ST;
+    __half* Vh = Kl + BN * ST;
+    __half* Vl = Vh + BN * ST;
+    float* qinv = reinterpret_cast<float*>(Vl + BN * ST);
+    float* kinv = qinv + BM;
+    float* vmul = kinv + BN;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int sub = lane & 7, rsub = lane >> 3;  // staging: 4 rows per warp pass, 8 lanes a row
+    // heavier (later) query tiles first: the causal work grows with the tile
+    const int qt = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
+    const int p0 = qt * BM;
+    const int nrow = min(BM, seq_len - p0);
+    const int kvh = h / (num_heads / num_kv_heads);
+    const int kv_dim = num_kv_heads * HD;
+    const size_t m0 = static_cast<size_t>(seq) * seq_len + p0;
+    for (int r = 4 * warp + rsub; r < BM; r += 16)
+        stage_row<HD, true>(r < nrow ? q + (m0 + r) * ldq + h * HD : nullptr, Qh + r * ST, Ql + r * ST, qinv + r,
+                            sub);
+    const float* kb = kcache + static_cast<size_t>(seq) * max_seq * kv_dim + kvh * HD;
+    const float* vb = vcache + static_cast<size_t>(seq) * max_seq * kv_dim + kvh * HD;
+    const float rsqrt_hd = 1.0f / sqrtf(static_cast<float>(HD));
+    const int r0 = 16 * warp + g, r1 = r0 + 8;  // this lane's two query rows in the tile
+    const int qpos0 = pos0 + p0 + r0, qpos1 = pos0 + p0 + r1;
+    const bool live0 = r0 < nrow, live1 = r1 < nrow;
+    float O[ND][4];
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd) O[nd][0] = O[nd][1] = O[nd][2] = O[nd][3] = 0.f;
+    float m_0 = -INFINITY, m_1 = -INFINITY, l_0 = 0.f, l_1 = 0.f;
+    const int last = pos0 + p0 + nrow - 1;  // last key position any row of the tile sees
+    for (int t0 = 0; t0 <= last; t0 += BN) {
+        __syncthreads();  // the previous tile's K and V are consumed (and Q staged)
+        for (int r = 4 * warp + rsub; r < BN; r += 16) {
+            const bool in = t0 + r <= last;
+            stage_row<HD, true>(in ? kb + static_cast<size_t>(t0 + r) * kv_dim : nullptr, Kh + r * ST, Kl + r * ST,
+                                kinv + r, sub);
+            stage_row<HD, false>(in ? vb + static_cast<size_t>(t0 + r) * kv_dim : nullptr, Vh + r * ST, Vl + r * ST,
+                                 vmul + r, sub);
+        }
+        __syncthreads();
+        // S = Q K^T for this warp's 16 rows x 64 keys
+        float S[NB][4];
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) S[nb][0] = S[nb][1] = S[nb][2] = S[nb][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            const int c = ks * 16 + 2 * t;
+            uint32_t ah[4], al[4];
+            ah[0] = lds32(Qh + r0 * ST + c);
+            ah[1] = lds32(Qh + r1 * ST + c);
+            ah[2] = lds32(Qh + r0 * ST + c + 8);
+            ah[3] = lds32(Qh + r1 * ST + c + 8);
+            al[0] = lds32(Ql + r0 * ST + c);
+            al[1] = lds32(Ql + r1 * ST + c);
+            al[2] = lds32(Ql + r0 * ST + c + 8);
+            al[3] = lds32(Ql + r1 * ST + c + 8);
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) {
+                const __half* kh = Kh + (nb * 8 + g) * ST + c;
+                const __half* kl = Kl + (nb * 8 + g) * ST + c;
+                const uint32_t bh0 = lds32(kh), bh1 = lds32(kh + 8), bl0 = lds32(kl), bl1 = lds32(kl + 8);
+                mma16816(S[nb], ah, bh0, bh1);
+                mma16816(S[nb], ah, bl0, bl1);
+                mma16816(S[nb], al, bh0, bh1);
+            }
+        }
+        // scores, causal mask, online softmax (rows r0, r1: the 4 lanes t of a row)
+        const float qs0 = qinv[r0] * rsqrt_hd, qs1 = qinv[r1] * rsqrt_hd;
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const int j = nb * 8 + 2 * t + c, key = t0 + j;
+                const float ki = kinv[j];
+                S[nb][c] = (live0 && key <= qpos0) ? S[nb][c] * ki * qs0 : -INFINITY;
+                S[nb][2 + c] = (live1 && key <= qpos1) ? S[nb][2 + c] * ki * qs1 : -INFINITY;
+                mx0 = fmaxf(mx0, S[nb][c]);
+                mx1 = fmaxf(mx1, S[nb][2 + c]);
+            }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m_0, mx0), mn1 = fmaxf(m_1, mx1);
+        // rows with nothing unmasked yet keep m = -inf: scale 1, p = 0
+        const float corr0 = mn0 == -INFINITY ? 1.f : expf(m_0 - mn0);
+        const float corr1 = mn1 == -INFINITY ? 1.f : expf(m_1 - mn1);
+        float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                S[nb][c] = mn0 == -INFINITY ? 0.f : expf(S[nb][c] - mn0);
+                S[nb][2 + c] = mn1 == -INFINITY ? 0.f : expf(S[nb][2 + c] - mn1);
+                ps0 += S[nb][c];
+                ps1 += S[nb][2 + c];
+            }
+        }
+        ps0 += __shfl_xor_sync(0xffffffffu, ps0, 1);
+        ps0 += __shfl_xor_sync(0xffffffffu, ps0, 2);
+        ps1 += __shfl_xor_sync(0xffffffffu, ps1, 1);
+        ps1 += __shfl_xor_sync(0xffffffffu, ps1, 2);
+        l_0 = l_0 * corr0 + ps0;
+        l_1 = l_1 * corr1 + ps1;
+        m_0 = mn0;
+        m_1 = mn1;
+#pragma unroll
+        for (int nd = 0; nd < ND; ++nd) {
+            O[nd][0] *= corr0;
+            O[nd][1] *= corr0;
+            O[nd][2] *= corr1;
+            O[nd][3] *= corr1;
+        }
+        // O += P V, 16 keys per k-step (n-blocks 2kk and 2kk + 1 of S)
+#pragma unroll
+        for (int kk = 0; kk < NB / 2; ++kk) {
+            const float va0 = vmul[kk * 16 + 2 * t], va1 = vmul[kk * 16 + 2 * t + 1];
+            const float vb0 = vmul[kk * 16 + 8 + 2 * t], vb1 = vmul[kk * 16 + 8 + 2 * t + 1];
+            uint32_t ph[4], pl[4];
+            ph[0] = split2(S[2 * kk][0] * va0, S[2 * kk][1] * va1, pl[0]);
+            ph[1] = split2(S[2 * kk][2] * va0, S[2 * kk][3] * va1, pl[1]);
+            ph[2] = split2(S[2 * kk + 1][0] * vb0, S[2 * kk + 1][1] * vb1, pl[2]);
+            ph[3] = split2(S[2 * kk + 1][2] * vb0, S[2 * kk + 1][3] * vb1, pl[3]);
+            // ldmatrix.trans rows: keys kk*16 + (lane / 8 % 2) * 8 + lane % 8, dims 8 (nd + lane / 16)
+            const int vrow = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+            for (int nd = 0; nd < ND; nd += 2) {
+                const int vcol = 8 * (nd + (lane >> 4));
+                uint32_t bh[4], bl[4];
+                ldsm_x4_t(bh, Vh + vrow * ST + vcol);
+                ldsm_x4_t(bl, Vl + vrow * ST + vcol);
+                mma16816(O[nd], ph, bh[0], bh[1]);
+                mma16816(O[nd], ph, bl[0], bl[1]);
+                mma16816(O[nd], pl, bh[0], bh[1]);
+                mma16816(O[nd + 1], ph, bh[2], bh[3]);
+                mma16816(O[nd + 1], ph, bl[2], bl[3]);
+                mma16816(O[nd + 1], pl, bh[2], bh[3]);
+            }
+        }
+    }
+    const float inv0 = 1.f / l_0, inv1 = 1.f / l_1;
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd) {
+        const int d = nd * 8 + 2 * t;
+        if (live0)
+            *reinterpret_cast<float2*>(out + (m0 + r0) * ldo + h * HD + d) =
+                make_float2(O[nd][0] * inv0, O[nd][1] * inv0);
+        if (live1)
+            *reinterpret_cast<float2*>(out + (m0 + r1) * ldo + h * HD + d) =
+                make_float2(O[nd][2] * inv1, O[nd][3] * inv1);
+    }
+}
+
 }  // namespace
 
 cudaError_t rope_kv_prefill_launch(float* q, const float* k, const float* v, float* kcache, float* vcache, int pos0,
@@ -302,8 +577,32 @@ cudaError_t rope_kv_prefill_launch(float* q, const float* k, const float* v, flo
 
 cudaError_t attention_prefill_launch(float* out, const float* q, const float* kcache, const float* vcache, int pos0,
                                      int seq_len, int rows, int num_heads, int num_kv_heads, int head_dim,
-                                     int max_seq, int ldq, int ldo, cudaStream_t s) {
-    if ((head_dim == 64 || head_dim == 128) && seq_len > 0 && rows % seq_len == 0 && (ldq % 4) == 0 &&
+                                     int max_seq, int ldq, int ldo, cudaStream_t s, int form) {
+    const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (form >= 2 && (head_dim == 64 || head_dim == 128) && seq_len > 0 && rows % seq_len == 0 && (ldq % 4) == 0 &&
+        (ldo % 2) == 0 && a16(q) && a16(kcache) && a16(vcache) && (reinterpret_cast<uintptr_t>(out) & 7u) == 0 &&
+        (num_kv_heads * head_dim) % 4 == 0) {
+        const int nseq = rows / seq_len;
+        const dim3 grid((seq_len + 63) / 64, num_heads, nseq);
+        if (nseq > 65535 || num_heads > 65535) return cudaErrorInvalidConfiguration;
+        const size_t smem = 6 * 64 * (head_dim + 8) * sizeof(__half) + 3 * 64 * sizeof(float);
+        cudaError_t e;
+        if (head_dim == 128) {
+            e = cudaFuncSetAttribute(attention_prefill_mma<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+            attention_prefill_mma<128><<<grid, 128, smem, s>>>(out, q, kcache, vcache, pos0, seq_len, num_heads,
+                                                                num_kv_heads, max_seq, ldq, ldo);
+        } else {
+            e = cudaFuncSetAttribute(attention_prefill_mma<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+            attention_prefill_mma<64><<<grid, 128, smem, s>>>(out, q, kcache, vcache, pos0, seq_len, num_heads,
+                                                               num_kv_heads, max_seq, ldq, ldo);
+        }
+        return cudaGetLastError();
+    }
+    if (form >= 1 && (head_dim == 64 || head_dim == 128) && seq_len > 0 && rows % seq_len == 0 && (ldq % 4) == 0 &&
         (reinterpret_cast<uintptr_t>(q) & 15u) == 0 && (num_kv_heads * head_dim) % 4 == 0) {
         const int nseq = rows / seq_len;
         const dim3 grid((seq_len + 63) / 64, num_heads, nseq);

@@ -24,7 +24,7 @@ from .lib import (  # noqa: F401
     Q2_K, Q3_K, Q4_0, Q4_K, Q5_K, Q6_K, Q8_0, TYPES, TYPE_NAMES,
     OPT_EARLY_WEIGHT_PREFETCH, OPT_GEMV_MAX_M, OPT_Q2K_REFERENCE_CPU_ORDER, OPT_TENSOR_CORE_GEMM,
     OPT_TENSOR_CORE_MIN_M, OPT_GEMV_SMEM_KB, OPT_GEMV_STAGE_KB, OPT_GEMV_CTAS_PER_SM, OPT_GEMV_FP32_ACT, OPT_GEMV_INT_MMA,
-    OPT_GEMV_BATCH_MAX_M, OPT_GEMV_BATCH_TABLE_KB, OPT_GEMV_BATCH_GROUP,
+    OPT_GEMV_BATCH_MAX_M, OPT_GEMV_BATCH_TABLE_KB, OPT_GEMV_BATCH_GROUP, OPT_PREFILL_ATTENTION,
     ACT_NONE, ACT_RMSNORM, ACT_SWIGLU,
     add, add_rmsnorm, argmax, attention_decode, attention_prefill, attention_workspace_bytes, decode_advance, embed,
     gdn_step,

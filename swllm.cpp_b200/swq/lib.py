@@ -33,6 +33,7 @@ OPT_GEMV_INT_MMA = 10
 OPT_GEMV_BATCH_MAX_M = 11
 OPT_GEMV_BATCH_TABLE_KB = 12
 OPT_GEMV_BATCH_GROUP = 13
+OPT_PREFILL_ATTENTION = 14
 
 GEMM_NOALLOC_MAX_X_ELEMS = 8388608  # SWQ_GEMM_NOALLOC_MAX_X_ELEMS
 
