@@ -99,7 +99,15 @@ def _gemv_form(fmt: str, M: int) -> str:
     """The GEMV kernel the library picks for `fmt` at M rows (default options)."""
     if M == 1 and fmt in ("Q4_K", "Q6_K"):
         return f"swq::kq::gemv_kq_kernel<{fmt}> (30-bit fixed-point x, exact integer sub-block sums)"
+    if fmt in ("Q4_K", "Q6_K") and 2 <= M <= 16:
+        return (f"swq::kqm::gemv_kqm_kernel<{fmt}> (x as fp16 pairs per super-block, exact products, "
+                f"fp32 sums)")
     return f"swq::gemv_kernel<{fmt},M> (fp32 x, fp32 FMA)"
+
+
+def _batched_path(fmt: str, M: int) -> bool:
+    """True where the batched K-quant GEMV serves M rows (default options)."""
+    return fmt in ("Q4_K", "Q6_K") and 2 <= M <= 16
 
 
 def load_peaks() -> tuple[float, str]:
@@ -942,7 +950,7 @@ def run_sweep(N: int = 14336, K: int = 4096, launches: int = 40, cpu_seconds: fl
             nbytes = wbytes + 4 * M * K + 4 * M * N
             flops = 2.0 * M * N * K
             gbs, tfs = nbytes / sec / 1e9, flops / sec / 1e12
-            tc_path = M >= swq.get_option(swq.OPT_TENSOR_CORE_MIN_M)
+            tc_path = M >= swq.get_option(swq.OPT_TENSOR_CORE_MIN_M) and not _batched_path(name, M)
             t_roof = max(nbytes / (hbm * 1e9), flops / (tc * 1e12))
             out["points"].append({
                 "format": name, "M": M, "us": round(sec * 1e6, 2), "GBps": round(gbs, 1), "TFLOPs": round(tfs, 2),
@@ -1168,7 +1176,7 @@ def run_gemm(args, rank: int, world: int) -> None:
     value = flops * world / per_call_s / 1e12
     peak, peak_kind = load_tensor_peak()
     hbm_peak, hbm_kind = load_peaks()
-    tc_path = M >= swq.get_option(swq.OPT_TENSOR_CORE_MIN_M)
+    tc_path = M >= swq.get_option(swq.OPT_TENSOR_CORE_MIN_M) and not _batched_path(args.format, M)
 
     # End to end through the host-buffer API: host X in, host Y out.
     comp = swq.Compute(device=local)
