@@ -185,6 +185,33 @@ def test_fused_known_answers(cuda):
         np.testing.assert_allclose(got, want, rtol=1e-3, atol=case["tol"])
 
 
+@pytest.mark.parametrize("fmt,M", [("Q4_K", 1), ("Q6_K", 1), ("Q4_K", 4), ("Q6_K", 12), ("Q4_K", 40), ("Q5_K", 1)])
+def test_host_buffer_repeated_calls(cuda, oracle_mod, fmt, M):
+    """The host-buffer context over many calls in a row: new activations each
+    time and two weights in turn, a larger shape in between (the staging
+    buffers grow), an eviction, then the same shapes again -- every result the
+    oracle's, on each path (integer GEMV, batched GEMV, tensor-core GEMM,
+    CUDA-core GEMV)."""
+    t = synth.IDS[fmt]
+    N, K = 700, 4096
+    ws = [swq.QuantWeight(synth.random_blocks(t, N, K, seed=20 + i), t) for i in range(2)]
+    tol = REL_L2_TOL if M < 17 else 1e-3
+    with swq.Compute() as c:
+        for rnd in range(2):
+            for i in range(5):
+                X = synth.random_activations(M, K, seed=100 * rnd + i)
+                Y = np.zeros((M, N), np.float32)
+                w = ws[i % 2]
+                c.matmul_q_batched(Y, X, w, M, N, K)
+                assert rel_l2(Y, oracle_mod.gemm(t, w.data, X, M, N, K)) <= tol, (rnd, i)
+            big = swq.QuantWeight(synth.random_blocks(t, 2 * N, 2 * K, seed=30 + rnd), t)
+            X = synth.random_activations(M + 1, 2 * K, seed=7 + rnd)
+            Y = np.zeros((M + 1, 2 * N), np.float32)
+            c.matmul_q_batched(Y, X, big, M + 1, 2 * N, 2 * K)
+            assert rel_l2(Y, oracle_mod.gemm(t, big.data, X, M + 1, 2 * N, 2 * K)) <= tol
+            c.evict(ws[0])
+
+
 def test_host_buffer_compute_api(cuda, oracle_mod):
     """Compute.matmul_transposed_q with host arrays, the reference's calling
     convention (src/tensor.h:1212): weights uploaded once and kept resident."""
