@@ -684,6 +684,40 @@ class LlamaDecoder:
                  c.lin_n_k, nv, c.lin_k_hd, c.lin_v_hd, c.lin_conv if "conv1d" in L else 0, stream=s)
         gemm(t["w_ssm_out"], L["w_ssm_out"], self.gdn_y, d, B, c.dim, vd, stream=s)
 
+    def _gdn_prefill(self, li: int, L: dict, xn, d, P: int) -> None:
+        """A GatedDeltaNet layer of a prefill: its projections as M = rows x P
+        row GEMMs, then the recurrence one prompt position at a time (swq_gdn_step
+        on the rows' position p: the reference's Model::forward per token,
+        src/model.h:369-513), the ssm_out projection of all positions into d."""
+        import torch
+        c, B, s, t = self.cfg, self.rows, self.stream, L["types"]
+        kd, vd, nv = c.lin_key_dim, c.lin_value_dim, c.lin_n_v
+        M, gemm, dev = B * P, self._gemm, self.device
+        f32 = dict(dtype=torch.float32, device=dev)
+        qkv = torch.empty((M, 2 * kd + vd), **f32)
+        gemm(t["w_qkv"], L["w_qkv"], xn, qkv, M, 2 * kd + vd, c.dim, s)
+        z = None
+        if "w_z" in L:
+            z = torch.empty((M, vd), **f32)
+            gemm(t["w_z"], L["w_z"], xn, z, M, vd, c.dim, s)
+        gates = []
+        for name in ("w_beta", "w_alpha", "w_dt"):
+            g = None
+            if name in L:
+                g = torch.empty((M, nv), **f32)
+                gemm(t[name], L[name], xn, g, M, nv, c.dim, s)
+            gates.append(g)
+        y = torch.empty((M, vd), **f32)
+        j = c.linear_layers.index(li)
+        at_p = lambda a, p: None if a is None else a.view(B, P, -1)[:, p].contiguous()  # noqa: E731
+        for p in range(P):
+            gdn_step(at_p(qkv, p), at_p(z, p), at_p(gates[0], p), at_p(gates[1], p), at_p(gates[2], p),
+                     L.get("ssm_a"), L.get("conv1d"), L.get("ssm_norm"), self.gdn_state[j], self.gdn_conv[j],
+                     self.gdn_y, B, c.lin_n_k, nv, c.lin_k_hd, c.lin_v_hd, c.lin_conv if "conv1d" in L else 0,
+                     stream=s)
+            y.view(B, P, vd)[:, p].copy_(self.gdn_y)
+        gemm(t["w_ssm_out"], L["w_ssm_out"], y, d, M, c.dim, vd, s)
+
     def prefill(self, prompts, pos0: int = 0, all_logits: bool = False):
         """Batched prefill: the prompt tokens of every sequence through the whole
         model at once -- M = rows x P activation rows, every projection one
@@ -700,9 +734,6 @@ class LlamaDecoder:
         logits of every prompt position, [rows, P, vocab] (one process)."""
         import torch
         c, B, s = self.cfg, self.rows, self.stream
-        if c.is_hybrid:
-            raise NotImplementedError("batched prefill of GatedDeltaNet layers (a sequential recurrence) is not "
-                                      "built; run the prompt through step() one position at a time")
         toks = np.asarray(prompts, dtype=np.int32)
         if toks.ndim != 2 or toks.shape[0] != B or toks.shape[1] < 1:
             raise ValueError(f"prompts must be {B} lists of at least one token, got shape {toks.shape}")
@@ -731,27 +762,33 @@ class LlamaDecoder:
                 r1 = min(M, r0 + 65535)
                 embed(x[r0:r1], self.token_embd, tok_d[r0:r1], c.dim, c.vocab, r1 - r0, stream=s)
             rmsnorm(xn, x, self.layers[0]["attn_norm"], c.dim, c.eps, M, stream=s)
+            if c.is_hybrid and pos0 == 0:  # new sequences: the recurrences start from zero
+                self.gdn_state.zero_()
+                self.gdn_conv.zero_()
             for li, L in enumerate(self.layers):
                 t = L["types"]
-                if "w_qk" in L:
-                    gemm(t["wq"], L["w_qk"], xn, qk, M, ld, c.dim, s)
+                if li in c.linear_layers:  # GatedDeltaNet: norm(x) -> d
+                    self._gdn_prefill(li, L, xn, d, P)
                 else:
-                    gemm(t["wq"], L["wq"], xn, att, M, qd, c.dim, s)
-                    qk[:, :qd].copy_(att)
-                    gemm(t["wk"], L["wk"], xn, v, M, kvd, c.dim, s)
-                    qk[:, qd:].copy_(v)
-                gemm(t["wv"], L["wv"], xn, v, M, kvd, c.dim, s)
-                if _EXTRAS.intersection(L):
-                    qkv_bias_norm(qk, qk[:, qd:], v, L.get("bq"), L.get("bk"), L.get("bv"), L.get("q_norm"),
-                                  L.get("k_norm"), qd, kvd, hd, c.eps, M, ldq=ld, ldk=ld, ldv=kvd, stream=s)
-                kc, vc = self.kcache[li], self.vcache[li]
-                rope_kv_prefill(qk, qk[:, qd:], v, kc, vc, pos0, P, self.freqs, qd, kvd, hd, hd, c.rope_neox, B,
-                                c.max_seq, ldq=ld, ldk=ld, ldv=kvd, stream=s)
-                attention_prefill(att, qk, kc, vc, pos0, P, self.nh, self.nkv, hd, B, c.max_seq, ldq=ld, ldo=qd,
-                                  stream=s)
-                gemm(t["wo"], L["wo"], att, d, M, c.dim, qd, s)
-                if tp:
-                    self._nccl_all_reduce(d)
+                    if "w_qk" in L:
+                        gemm(t["wq"], L["w_qk"], xn, qk, M, ld, c.dim, s)
+                    else:
+                        gemm(t["wq"], L["wq"], xn, att, M, qd, c.dim, s)
+                        qk[:, :qd].copy_(att)
+                        gemm(t["wk"], L["wk"], xn, v, M, kvd, c.dim, s)
+                        qk[:, qd:].copy_(v)
+                    gemm(t["wv"], L["wv"], xn, v, M, kvd, c.dim, s)
+                    if _EXTRAS.intersection(L):
+                        qkv_bias_norm(qk, qk[:, qd:], v, L.get("bq"), L.get("bk"), L.get("bv"), L.get("q_norm"),
+                                      L.get("k_norm"), qd, kvd, hd, c.eps, M, ldq=ld, ldk=ld, ldv=kvd, stream=s)
+                    kc, vc = self.kcache[li], self.vcache[li]
+                    rope_kv_prefill(qk, qk[:, qd:], v, kc, vc, pos0, P, self.freqs, qd, kvd, hd, hd, c.rope_neox,
+                                    B, c.max_seq, ldq=ld, ldk=ld, ldv=kvd, stream=s)
+                    attention_prefill(att, qk, kc, vc, pos0, P, self.nh, self.nkv, hd, B, c.max_seq, ldq=ld,
+                                      ldo=qd, stream=s)
+                    gemm(t["wo"], L["wo"], att, d, M, c.dim, qd, s)
+                    if tp:
+                        self._nccl_all_reduce(d)
                 add_rmsnorm(xn, x, d, L["ffn_norm"], c.dim, c.eps, M, stream=s)  # x += o; xn = norm(x)
                 if "moe" in L:  # in chunks of moe_max_tokens rows, the same on every rank
                     ch = self.moe_max_tokens

@@ -162,11 +162,12 @@ def test_prefill_logits_match_reference(cuda, rows, P):
         assert hist[1, r] == int(np.argmax(after[r]))
 
 
-@pytest.mark.parametrize("variant", ["mix", "tied", "neox", "bias", "qknorm"])
+@pytest.mark.parametrize("variant", ["mix", "tied", "neox", "bias", "qknorm", "hybrid"])
 def test_gguf_prefill_matches_reference_logits(cuda, tmp_path, variant):
-    """A GGUF file's prompt in one prefill (6 rows: the tensor-core GEMMs)
-    against the logits of the reference's own Model::forward run token by
-    token on the same file (tests/golden/golden_llama_<variant>.npz)."""
+    """A GGUF file's prompt in one prefill against the logits of the
+    reference's own Model::forward run token by token on the same file
+    (tests/golden/golden_llama_<variant>.npz); "hybrid": a GatedDeltaNet
+    layer, its recurrence one prompt position at a time."""
     import llama_gguf as LG
     from conftest import GOLDEN
     gold = np.load(GOLDEN / f"golden_llama_{variant}.npz")

@@ -20,7 +20,7 @@ from swq import synth
 from test_gpu_model import _small, _weights
 
 OPS = ("embed", "rmsnorm", "add_rmsnorm", "gemm_act_ws", "rope_kv", "attention_decode", "silu_mul", "argmax",
-       "qkv_bias_norm", "decode_advance", "rope_kv_prefill", "attention_prefill", "add", "dequant")
+       "qkv_bias_norm", "decode_advance", "rope_kv_prefill", "attention_prefill", "add", "dequant", "gdn_step")
 
 
 class _Stream:
@@ -155,6 +155,29 @@ def test_from_gguf_wiring(calls, tmp_path):
     v = LG.VARIANTS["mix"]["layers"]
     assert types == [v[0]["wq"], v[0]["wv"], v[0]["wo"], v[0]["w_gate"], v[0]["w_down"],
                      v[1]["wq"], v[1]["wv"], v[1]["wo"], v[1]["w_gate"], v[1]["w_down"], synth.Q6_K]
+
+
+def test_hybrid_prefill_wiring(calls, tmp_path):
+    """A hybrid file's prefill: the GatedDeltaNet layer's projections once over
+    all rows x P positions, its recurrence (swq_gdn_step) once per position on
+    that position's rows, in order, from a zeroed state; the attention layer
+    through the prefill kernels."""
+    dec = M.LlamaDecoder.from_gguf(LG.write(tmp_path / "h.gguf", "hybrid"), device="cpu", rows=2)
+    c = dec.cfg
+    dec.gdn_state.fill_(1.0)
+    dec.gdn_conv.fill_(1.0)
+    calls.clear()
+    P = 4
+    dec.prefill([[1, 2, 3, 4], [5, 6, 7, 8]])
+    assert float(dec.gdn_state.abs().sum()) == 0.0 and float(dec.gdn_conv.abs().sum()) == 0.0
+    steps = [a for name, a, _ in calls if name == "gdn_step"]
+    assert len(steps) == P * len(c.linear_layers)
+    for a in steps:
+        assert a[0].shape == (2, 2 * c.lin_key_dim + c.lin_value_dim) and a[11] == 2  # one position, both rows
+    g = _gemms(calls)
+    assert (g[0][2], g[0][3]) == (2 * P, 2 * c.lin_key_dim + c.lin_value_dim)  # w_qkv over all positions
+    assert sum(1 for name, _, _ in calls if name == "attention_prefill") == c.n_layers - len(c.linear_layers)
+    assert int(dec.pos.item()) == P
 
 
 @pytest.mark.parametrize("rank", [0, 1])
