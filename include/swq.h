@@ -417,10 +417,13 @@ enum {
     SWQ_OPT_GEMV_BATCH_TABLE_KB = 12,
     SWQ_OPT_GEMV_BATCH_GROUP = 13,
     /* Causal attention of swq_attention_prefill for head_dim 64 and 128:
-     * 2 (default) on the tensor cores, q, k, v and the softmax weights as
+     * 3 (default) on the tensor cores, q, k, v and the softmax weights as
      * pairs of fp16 numbers (22 bits relative to each q / k row's largest
-     * element; exact products, fp32 sums); 1 the fp32 tiled CUDA-core form;
-     * 0 one warp per row and head (the form other head dims use). */
+     * element; exact products, fp32 sums), the context's K/V converted once
+     * per call into scratch from libswq's stream-ordered pool; 2 the same
+     * arithmetic converting each K/V tile in every query tile (no scratch);
+     * 1 the fp32 tiled CUDA-core form; 0 one warp per row and head (the form
+     * other head dims use). */
     SWQ_OPT_PREFILL_ATTENTION = 14
 };
 swq_status swq_set_option(int option, int value);

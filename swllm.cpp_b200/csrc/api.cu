@@ -43,7 +43,7 @@ std::atomic<int> g_opt_gemv_imma{2};
 std::atomic<int> g_opt_kqm_max_m{16};
 std::atomic<int> g_opt_kqm_table_kb{72};
 std::atomic<int> g_opt_kqm_group{0};
-std::atomic<int> g_opt_attn_form{2};
+std::atomic<int> g_opt_attn_form{3};
 
 swq_status fail(swq_status s, const std::string& msg) {
     g_last_error = msg;
@@ -282,7 +282,7 @@ swq_status swq_set_option(int option, int value) {
             swq::gemv_kqm_tune(g_opt_kqm_table_kb, g_opt_kqm_group);
             return SWQ_OK;
         case SWQ_OPT_PREFILL_ATTENTION:
-            if (value < 0 || value > 2) return fail(SWQ_ERR_BAD_ARG, "option value must be 0, 1 or 2");
+            if (value < 0 || value > 3) return fail(SWQ_ERR_BAD_ARG, "option value must be 0, 1, 2 or 3");
             g_opt_attn_form = value;
             return SWQ_OK;
         default:

@@ -17,6 +17,7 @@
 
 #include <cstdint>
 
+#include "gemm_tc.h"  // scratch_alloc / scratch_free
 #include "prefill.h"
 #include "swq_device.cuh"
 
@@ -385,12 +386,29 @@ __device__ __forceinline__ void stage_row(const float* src, __half* dh, __half* 
     uint32_t H[PER / 2], L[PER / 2];
 #pragma unroll
     for (int i = 0; i < PER; i += 2) H[i / 2] = split2(v[i] * up, v[i + 1] * up, L[i / 2]);
+    if (dh == nullptr) return;  // a row past the end (the shuffles above need all 8 lanes)
 #pragma unroll
     for (int i = 0; i < PER / 2; i += 2) {
         *reinterpret_cast<uint2*>(dh + sub * PER + 2 * i) = make_uint2(H[i], H[i + 1]);
         *reinterpret_cast<uint2*>(dl + sub * PER + 2 * i) = make_uint2(L[i], L[i + 1]);
     }
     if (sub == 0) *aux = back;
+}
+
+// 16 bytes global -> shared, asynchronous; src_bytes 0 fills zeros (a row past
+// the context) and reads nothing.
+__device__ __forceinline__ void cp16(void* dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp8(void* dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 }  // namespace amma
@@ -561,6 +579,214 @@ __global__ void __launch_bounds__(128, 2) attention_prefill_mma(
     }
 }
 
+
+// The K and V rows of every sequence's context as fp16 pairs, once per layer:
+// row record [k h | k l | v h | v l] (HD halves each) per (sequence, KV head,
+// position), scales [(kinv, vmul)] per row -- what attention_prefill_mma's
+// staging computes for every query tile, computed once for all of them.
+// One warp per 4 rows (8 lanes a row).
+template <int HD>
+__global__ void __launch_bounds__(256) kv_pairs_kernel(const float* __restrict__ kcache,
+                                                       const float* __restrict__ vcache, __half* __restrict__ pairs,
+                                                       float* __restrict__ scales, int n_ctx, int num_kv_heads,
+                                                       int max_seq, long long total) {
+    using namespace amma;
+    const int lane = threadIdx.x & 31, sub = lane & 7;
+    const long long row = (static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * 4 + (lane >> 3);
+    const bool live = row < total;
+    const long long r = live ? row : 0;
+    const int t = static_cast<int>(r % n_ctx);
+    const long long sh = r / n_ctx;  // sequence * num_kv_heads + kv head
+    const int kvh = static_cast<int>(sh % num_kv_heads);
+    const long long seq = sh / num_kv_heads;
+    const size_t off = (static_cast<size_t>(seq) * max_seq + t) * (static_cast<size_t>(num_kv_heads) * HD) +
+                       static_cast<size_t>(kvh) * HD;
+    __half* rec = pairs + static_cast<size_t>(r) * 4 * HD;
+    stage_row<HD, true>(kcache + off, live ? rec : nullptr, rec + HD, scales + 2 * r, sub);
+    stage_row<HD, false>(vcache + off, live ? rec + 2 * HD : nullptr, rec + 3 * HD, scales + 2 * r + 1, sub);
+}
+
+// attention_prefill_mma's arithmetic on the pairs of kv_pairs_kernel: 32-key
+// tiles, copied asynchronously into two shared-memory stages (the next tile
+// lands while this one is computed), no conversion in the loop.
+template <int HD>
+__global__ void __launch_bounds__(128, 2) attention_prefill_pairs(
+    float* __restrict__ out, const float* __restrict__ q, const __half* __restrict__ pairs,
+    const float* __restrict__ scales, int pos0, int seq_len, int num_heads, int num_kv_heads, int n_ctx, int ldq,
+    int ldo) {
+    using namespace amma;
+    constexpr int BM = 64, BN = 32, ST = HD + 8;  // row stride in halves
+    constexpr int NB = BN / 8, ND = HD / 8, KS = HD / 16, CH = HD / 8;  // CH: 16-byte chunks of a row part
+    constexpr int STAGE = 4 * BN * ST;                                   // halves of one stage (k h, k l, v h, v l)
+    extern __shared__ __align__(16) uint8_t apsm[];
+    __half* Qh = reinterpret_cast<__half*>(apsm);
+    __half* Ql = Qh + BM * ST;
+    __half* KV = Ql + BM * ST;                                      // [stage][part][BN][ST]
+    float* qinv = reinterpret_cast<float*>(KV + 2 * STAGE);          // [BM]
+    float* scl = qinv + BM;                                          // [stage][BN][2]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int sub = lane & 7, rsub = lane >> 3;
+    const int qt = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
+    const int p0 = qt * BM;
+    const int nrow = min(BM, seq_len - p0);
+    const int kvh = h / (num_heads / num_kv_heads);
+    const size_t m0 = static_cast<size_t>(seq) * seq_len + p0;
+    const long long base = (static_cast<long long>(seq) * num_kv_heads + kvh) * n_ctx;  // first pair row
+    const int last = pos0 + p0 + nrow - 1;  // last key position any row of the tile sees
+    const int ntile = last / BN + 1;
+    auto load = [&](int tile, int stage) {
+        const int t0 = tile * BN;
+        __half* dst = KV + stage * STAGE;
+        for (int c = threadIdx.x; c < BN * 4 * CH; c += 128) {
+            const int r = c / (4 * CH), part = (c / CH) % 4, o = c % CH;
+            const bool in = t0 + r < n_ctx;
+            const __half* src = pairs + (static_cast<size_t>(base + (in ? t0 + r : 0)) * 4 + part) * HD + o * 8;
+            cp16(dst + (part * BN + r) * ST + o * 8, src, in ? 16 : 0);
+        }
+        if (threadIdx.x < BN) {
+            const int r = threadIdx.x;
+            const bool in = t0 + r < n_ctx;
+            cp8(scl + stage * 2 * BN + 2 * r, scales + 2 * (base + (in ? t0 + r : 0)), in ? 8 : 0);
+        }
+        cp_commit();
+    };
+    load(0, 0);
+    for (int r = 4 * warp + rsub; r < BM; r += 16)
+        stage_row<HD, true>(r < nrow ? q + (m0 + r) * ldq + h * HD : nullptr, Qh + r * ST, Ql + r * ST, qinv + r,
+                            sub);
+    const float rsqrt_hd = 1.0f / sqrtf(static_cast<float>(HD));
+    const int r0 = 16 * warp + g, r1 = r0 + 8;
+    const int qpos0 = pos0 + p0 + r0, qpos1 = pos0 + p0 + r1;
+    const bool live0 = r0 < nrow, live1 = r1 < nrow;
+    float O[ND][4];
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd) O[nd][0] = O[nd][1] = O[nd][2] = O[nd][3] = 0.f;
+    float m_0 = -INFINITY, m_1 = -INFINITY, l_0 = 0.f, l_1 = 0.f;
+    for (int tile = 0; tile < ntile; ++tile) {
+        const int stage = tile & 1, t0 = tile * BN;
+        if (tile + 1 < ntile) {
+            load(tile + 1, stage ^ 1);
+            cp_wait<1>();  // this tile's group has landed
+        } else {
+            cp_wait<0>();
+        }
+        __syncthreads();
+        const __half* Kh = KV + stage * STAGE;
+        const __half* Kl = Kh + BN * ST;
+        const __half* Vh = Kl + BN * ST;
+        const __half* Vl = Vh + BN * ST;
+        const float* sc = scl + stage * 2 * BN;
+        float S[NB][4];
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) S[nb][0] = S[nb][1] = S[nb][2] = S[nb][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            const int c = ks * 16 + 2 * t;
+            uint32_t ah[4], al[4];
+            ah[0] = lds32(Qh + r0 * ST + c);
+            ah[1] = lds32(Qh + r1 * ST + c);
+            ah[2] = lds32(Qh + r0 * ST + c + 8);
+            ah[3] = lds32(Qh + r1 * ST + c + 8);
+            al[0] = lds32(Ql + r0 * ST + c);
+            al[1] = lds32(Ql + r1 * ST + c);
+            al[2] = lds32(Ql + r0 * ST + c + 8);
+            al[3] = lds32(Ql + r1 * ST + c + 8);
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) {
+                const __half* kh = Kh + (nb * 8 + g) * ST + c;
+                const __half* kl = Kl + (nb * 8 + g) * ST + c;
+                const uint32_t bh0 = lds32(kh), bh1 = lds32(kh + 8), bl0 = lds32(kl), bl1 = lds32(kl + 8);
+                mma16816(S[nb], ah, bh0, bh1);
+                mma16816(S[nb], ah, bl0, bl1);
+                mma16816(S[nb], al, bh0, bh1);
+            }
+        }
+        const float qs0 = qinv[r0] * rsqrt_hd, qs1 = qinv[r1] * rsqrt_hd;
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const int j = nb * 8 + 2 * t + c, key = t0 + j;
+                const float ki = sc[2 * j];
+                S[nb][c] = (live0 && key <= qpos0) ? S[nb][c] * ki * qs0 : -INFINITY;
+                S[nb][2 + c] = (live1 && key <= qpos1) ? S[nb][2 + c] * ki * qs1 : -INFINITY;
+                mx0 = fmaxf(mx0, S[nb][c]);
+                mx1 = fmaxf(mx1, S[nb][2 + c]);
+            }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m_0, mx0), mn1 = fmaxf(m_1, mx1);
+        const float corr0 = mn0 == -INFINITY ? 1.f : expf(m_0 - mn0);
+        const float corr1 = mn1 == -INFINITY ? 1.f : expf(m_1 - mn1);
+        float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                S[nb][c] = mn0 == -INFINITY ? 0.f : expf(S[nb][c] - mn0);
+                S[nb][2 + c] = mn1 == -INFINITY ? 0.f : expf(S[nb][2 + c] - mn1);
+                ps0 += S[nb][c];
+                ps1 += S[nb][2 + c];
+            }
+        }
+        ps0 += __shfl_xor_sync(0xffffffffu, ps0, 1);
+        ps0 += __shfl_xor_sync(0xffffffffu, ps0, 2);
+        ps1 += __shfl_xor_sync(0xffffffffu, ps1, 1);
+        ps1 += __shfl_xor_sync(0xffffffffu, ps1, 2);
+        l_0 = l_0 * corr0 + ps0;
+        l_1 = l_1 * corr1 + ps1;
+        m_0 = mn0;
+        m_1 = mn1;
+#pragma unroll
+        for (int nd = 0; nd < ND; ++nd) {
+            O[nd][0] *= corr0;
+            O[nd][1] *= corr0;
+            O[nd][2] *= corr1;
+            O[nd][3] *= corr1;
+        }
+#pragma unroll
+        for (int kk = 0; kk < NB / 2; ++kk) {
+            const float va0 = sc[2 * (kk * 16 + 2 * t) + 1], va1 = sc[2 * (kk * 16 + 2 * t + 1) + 1];
+            const float vb0 = sc[2 * (kk * 16 + 8 + 2 * t) + 1], vb1 = sc[2 * (kk * 16 + 8 + 2 * t + 1) + 1];
+            uint32_t ph[4], pl[4];
+            ph[0] = split2(S[2 * kk][0] * va0, S[2 * kk][1] * va1, pl[0]);
+            ph[1] = split2(S[2 * kk][2] * va0, S[2 * kk][3] * va1, pl[1]);
+            ph[2] = split2(S[2 * kk + 1][0] * vb0, S[2 * kk + 1][1] * vb1, pl[2]);
+            ph[3] = split2(S[2 * kk + 1][2] * vb0, S[2 * kk + 1][3] * vb1, pl[3]);
+            const int vrow = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+            for (int nd = 0; nd < ND; nd += 2) {
+                const int vcol = 8 * (nd + (lane >> 4));
+                uint32_t bh[4], bl[4];
+                ldsm_x4_t(bh, Vh + vrow * ST + vcol);
+                ldsm_x4_t(bl, Vl + vrow * ST + vcol);
+                mma16816(O[nd], ph, bh[0], bh[1]);
+                mma16816(O[nd], ph, bl[0], bl[1]);
+                mma16816(O[nd], pl, bh[0], bh[1]);
+                mma16816(O[nd + 1], ph, bh[2], bh[3]);
+                mma16816(O[nd + 1], ph, bl[2], bl[3]);
+                mma16816(O[nd + 1], pl, bh[2], bh[3]);
+            }
+        }
+        __syncthreads();  // this stage is read out: the load after next may overwrite it
+    }
+    const float inv0 = 1.f / l_0, inv1 = 1.f / l_1;
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd) {
+        const int d = nd * 8 + 2 * t;
+        if (live0)
+            *reinterpret_cast<float2*>(out + (m0 + r0) * ldo + h * HD + d) =
+                make_float2(O[nd][0] * inv0, O[nd][1] * inv0);
+        if (live1)
+            *reinterpret_cast<float2*>(out + (m0 + r1) * ldo + h * HD + d) =
+                make_float2(O[nd][2] * inv1, O[nd][3] * inv1);
+    }
+}
+
 }  // namespace
 
 cudaError_t rope_kv_prefill_launch(float* q, const float* k, const float* v, float* kcache, float* vcache, int pos0,
@@ -579,9 +805,50 @@ cudaError_t attention_prefill_launch(float* out, const float* q, const float* kc
                                      int seq_len, int rows, int num_heads, int num_kv_heads, int head_dim,
                                      int max_seq, int ldq, int ldo, cudaStream_t s, int form) {
     const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-    if (form >= 2 && (head_dim == 64 || head_dim == 128) && seq_len > 0 && rows % seq_len == 0 && (ldq % 4) == 0 &&
-        (ldo % 2) == 0 && a16(q) && a16(kcache) && a16(vcache) && (reinterpret_cast<uintptr_t>(out) & 7u) == 0 &&
-        (num_kv_heads * head_dim) % 4 == 0) {
+    const bool mma_ok = (head_dim == 64 || head_dim == 128) && seq_len > 0 && rows % seq_len == 0 &&
+                        (ldq % 4) == 0 && (ldo % 2) == 0 && a16(q) && a16(kcache) && a16(vcache) &&
+                        (reinterpret_cast<uintptr_t>(out) & 7u) == 0 && (num_kv_heads * head_dim) % 4 == 0;
+    if (form >= 3 && mma_ok) {
+        // K/V as fp16 pairs once for the layer (stream-ordered scratch), then
+        // the double-buffered tensor-core attention over them
+        const int nseq = rows / seq_len;
+        const int n_ctx = pos0 + seq_len;
+        const dim3 grid((seq_len + 63) / 64, num_heads, nseq);
+        if (nseq > 65535 || num_heads > 65535) return cudaErrorInvalidConfiguration;
+        const long long total = static_cast<long long>(nseq) * num_kv_heads * n_ctx;
+        const size_t pair_bytes = (static_cast<size_t>(total) * 4 * head_dim * sizeof(__half) + 255) / 256 * 256;
+        const size_t bytes = pair_bytes + static_cast<size_t>(total) * 2 * sizeof(float);
+        const long long blocks = (total + 31) / 32;
+        if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+        void* buf = nullptr;
+        cudaError_t e = scratch_alloc(&buf, bytes, s);
+        if (e != cudaSuccess) return e;
+        __half* pairs = static_cast<__half*>(buf);
+        float* scales = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + pair_bytes);
+        const int ST = head_dim + 8;
+        const size_t smem = (2 * 64 * ST + 2 * 4 * 32 * ST) * sizeof(__half) + (64 + 2 * 2 * 32) * sizeof(float);
+        if (head_dim == 128) {
+            kv_pairs_kernel<128><<<static_cast<unsigned>(blocks), 256, 0, s>>>(kcache, vcache, pairs, scales, n_ctx,
+                                                                                num_kv_heads, max_seq, total);
+            e = cudaFuncSetAttribute(attention_prefill_pairs<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem));
+            if (e == cudaSuccess)
+                attention_prefill_pairs<128><<<grid, 128, smem, s>>>(out, q, pairs, scales, pos0, seq_len, num_heads,
+                                                                      num_kv_heads, n_ctx, ldq, ldo);
+        } else {
+            kv_pairs_kernel<64><<<static_cast<unsigned>(blocks), 256, 0, s>>>(kcache, vcache, pairs, scales, n_ctx,
+                                                                               num_kv_heads, max_seq, total);
+            e = cudaFuncSetAttribute(attention_prefill_pairs<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem));
+            if (e == cudaSuccess)
+                attention_prefill_pairs<64><<<grid, 128, smem, s>>>(out, q, pairs, scales, pos0, seq_len, num_heads,
+                                                                     num_kv_heads, n_ctx, ldq, ldo);
+        }
+        if (e == cudaSuccess) e = cudaGetLastError();
+        const cudaError_t e2 = scratch_free(buf, s);
+        return e != cudaSuccess ? e : e2;
+    }
+    if (form >= 2 && mma_ok) {
         const int nseq = rows / seq_len;
         const dim3 grid((seq_len + 63) / 64, num_heads, nseq);
         if (nseq > 65535 || num_heads > 65535) return cudaErrorInvalidConfiguration;

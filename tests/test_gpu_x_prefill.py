@@ -46,10 +46,10 @@ def _attention_ref(q, kc, vc, pos0, P, S, H, Hkv, hd):
                                                 # tile boundary, a context before the prompt
                                                 (1, 200, 70, 8, 2, 128), (2, 130, 0, 4, 4, 64),
                                                 (1, 64, 0, 2, 1, 128), (1, 65, 63, 4, 2, 64)])
-@pytest.mark.parametrize("form", [2, 1, 0], ids=["tensor-core", "tiled-fp32", "warp-per-row"])
+@pytest.mark.parametrize("form", [3, 2, 1, 0], ids=["tensor-core-pairs", "tensor-core", "tiled-fp32", "warp-per-row"])
 def test_attention_prefill_matches_numpy(cuda, S, P, pos0, H, Hkv, hd, form):
     """Every form of the causal attention (SWQ_OPT_PREFILL_ATTENTION) against
-    float64; the tensor-core form keeps 22-bit operand pairs, within 1e-5."""
+    float64; the tensor-core forms keep 22-bit operand pairs, within 1e-5."""
     torch = cuda
     import swq
     max_seq = pos0 + P + 3
@@ -70,8 +70,9 @@ def test_attention_prefill_matches_numpy(cuda, S, P, pos0, H, Hkv, hd, form):
     assert rel_l2(d_out.cpu().numpy(), want) <= ATT_TOL
 
 
+@pytest.mark.parametrize("form", [3, 2])
 @pytest.mark.parametrize("hd", [64, 128])
-def test_attention_prefill_tensor_core_dynamic_range(cuda, hd):
+def test_attention_prefill_tensor_core_dynamic_range(cuda, hd, form):
     """Tensor-core form: rows of q and k over many decades (each row its own
     scale), tiny and large values (v up to 1e6: scaled down below fp16's
     range, the softmax weights take the factor back), a non-finite q row
@@ -88,9 +89,14 @@ def test_attention_prefill_tensor_core_dynamic_range(cuda, hd):
         np.float32)
     q[7, :hd] = np.inf
     d_out = torch.full((S * P, H * hd), float("nan"), device="cuda")
-    swq.attention_prefill(d_out, torch.from_numpy(q).cuda(), torch.from_numpy(kc).cuda(),
-                          torch.from_numpy(vc).cuda(), pos0, P, H, Hkv, hd, S, max_seq)
-    swq.check()
+    old = swq.get_option(swq.OPT_PREFILL_ATTENTION)
+    swq.set_option(swq.OPT_PREFILL_ATTENTION, form)
+    try:
+        swq.attention_prefill(d_out, torch.from_numpy(q).cuda(), torch.from_numpy(kc).cuda(),
+                              torch.from_numpy(vc).cuda(), pos0, P, H, Hkv, hd, S, max_seq)
+        swq.check()
+    finally:
+        swq.set_option(swq.OPT_PREFILL_ATTENTION, old)
     got = d_out.cpu().numpy()
     assert not np.isfinite(got[7, :hd]).any()
     q[7, :hd] = 0.0
