@@ -136,6 +136,25 @@ TC_LOGIT_TOL = 5e-2
 TOKS = [11, 500, 7]
 
 
+@pytest.mark.parametrize("rows,fuse", [(6, ()), (16, ()), (6, ("rmsnorm", "swiglu"))])
+def test_batched_decode_at_fp32_accuracy(cuda, rows, fuse):
+    """Batched decode (6 and 16 rows) of a 4-layer Q4_K_M model whose every
+    projection the batched K-quant GEMV serves (K a multiple of 2048, so the
+    Q6_K rows qualify too): teacher-forced logits of every row within
+    LOGIT_TOL of the CPU restatement, the bound of the single-row fp32 path --
+    not the tensor-core path's fp16 bound."""
+    from oracle.model_ref import RefLlama
+    cfg = LlamaConfig(n_layers=4, dim=2048, n_heads=16, n_kv_heads=4, head_dim=128, ffn=2048, vocab=1000,
+                      max_seq=16)
+    W = _weights(cfg, seed=21)
+    got = _teacher_forced(LlamaDecoder(cfg, rows=rows, weights=W, fuse=fuse), rows, TOKS)
+    for r in range(0, rows, 5):
+        ref = RefLlama(cfg, W, rope_freqs(cfg), cfg.max_seq)
+        for pos, tok in enumerate(TOKS):
+            want = ref.forward(tok + r, pos)
+            assert rel_l2(got[pos, r], want) <= LOGIT_TOL, (r, pos, rel_l2(got[pos, r], want))
+
+
 @pytest.mark.parametrize("fuse", [(), ("rmsnorm",), ("swiglu",), ("rmsnorm", "swiglu")])
 @pytest.mark.parametrize("rows", [1, 6])
 def test_decode_paths_match_reference(cuda, rows, fuse):
