@@ -1195,7 +1195,11 @@ def run_gemm(args, rank: int, world: int) -> None:
         "metric": f"dequant-GEMM TFLOP/s (N={N} K={K})", "value": round(value, 1),
         "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
+        "vs_baseline": None,
+        "dtype": ("f16 operands, f32 accumulate" if tc_path else
+                  "f32 (x as fp16 pairs per super-block, exact products, fp32 sums)"
+                  if _batched_path(args.format, M) else "f32"),
+        "data": "synthetic",
         "config": {"workload": f"{args.format} dequant-GEMM M={M} N={N} K={K}, {copies} rotating weight copies",
                    "format": args.format, "M": M, "N": N, "K": K, "copies": copies,
                    "l2": "inputs larger than L2 (rotating weights)"},
