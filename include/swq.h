@@ -411,9 +411,10 @@ enum {
      * SWQ_GEMM_NOALLOC keep the tensor-core GEMM. */
     SWQ_OPT_GEMV_BATCH_MAX_M = 11,
     /* Tuning of the batched K-quant GEMV: shared-memory KB of the activation
-     * table of one K split (8..160, default 72; K is split so that a split's
-     * table fits), and consumer warps per 16-row tile (0 = automatic, or 1,
-     * 2, 4, 8, 16). */
+     * table of one K split (8..160, or 0 = automatic, the default: 72, or
+     * 144 for 9..16 rows on matrices that give every CTA 8 or more 16-row
+     * tiles; K is split so that a split's table fits), and consumer warps per
+     * 16-row tile (0 = automatic, or 1, 2, 4, 8, 16). */
     SWQ_OPT_GEMV_BATCH_TABLE_KB = 12,
     SWQ_OPT_GEMV_BATCH_GROUP = 13,
     /* Causal attention of swq_attention_prefill for head_dim 64 and 128:

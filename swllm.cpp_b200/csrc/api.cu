@@ -41,7 +41,7 @@ std::atomic<int> g_opt_gemv_ctas{0};
 std::atomic<int> g_opt_gemv_fp32{1};
 std::atomic<int> g_opt_gemv_imma{2};
 std::atomic<int> g_opt_kqm_max_m{16};
-std::atomic<int> g_opt_kqm_table_kb{72};
+std::atomic<int> g_opt_kqm_table_kb{0};
 std::atomic<int> g_opt_kqm_group{0};
 std::atomic<int> g_opt_attn_form{3};
 
@@ -271,7 +271,8 @@ swq_status swq_set_option(int option, int value) {
             g_opt_kqm_max_m = value;
             return SWQ_OK;
         case SWQ_OPT_GEMV_BATCH_TABLE_KB:
-            if (value < 8 || value > 160) return fail(SWQ_ERR_BAD_ARG, "option value must be 8..160");
+            if (value != 0 && (value < 8 || value > 160))
+                return fail(SWQ_ERR_BAD_ARG, "option value must be 0 or 8..160");
             g_opt_kqm_table_kb = value;
             swq::gemv_kqm_tune(g_opt_kqm_table_kb, g_opt_kqm_group);
             return SWQ_OK;

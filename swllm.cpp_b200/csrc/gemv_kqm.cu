@@ -804,9 +804,35 @@ int ncb_for(int M) {
     return 0;
 }
 
-std::atomic<int> g_table_kb{72};  // shared-memory table of one split (SWQ_OPT_GEMV_BATCH_TABLE_KB)
-std::atomic<int> g_group{0};      // consumer warps per tile (SWQ_OPT_GEMV_BATCH_GROUP, 0: automatic)
+std::atomic<int> g_table_kb{0};  // KB of one split's table (SWQ_OPT_GEMV_BATCH_TABLE_KB, 0: automatic)
+std::atomic<int> g_group{0};     // consumer warps per tile (SWQ_OPT_GEMV_BATCH_GROUP, 0: automatic)
 constexpr size_t kSplitPartialLimit = 16u << 20;  // partials of CTA-parallel splits (stay in L2)
+
+// K split and CTA layout for a table of at most table_kb KB per split.
+struct KqmSplit {
+    int kbs, S, SC, G, tiles_cta;
+    size_t part_bytes;
+};
+
+KqmSplit split_for(int table_kb, size_t rec, int nb, int N, int MB, int num_sms) {
+    KqmSplit q{};
+    const int kbs_max = std::max<int>(1, static_cast<int>(static_cast<size_t>(table_kb) * 1024 / rec));
+    const int S0 = (nb + kbs_max - 1) / kbs_max;
+    q.kbs = (nb + S0 - 1) / S0;
+    q.S = (nb + q.kbs - 1) / q.kbs;  // no empty split
+    const int tiles = (N + kqm::TR - 1) / kqm::TR;
+    q.part_bytes = static_cast<size_t>(q.S) * MB * N * sizeof(float);
+    if (q.S > 1 && q.part_bytes <= kSplitPartialLimit && num_sms / q.S >= 1) {
+        q.SC = q.S;
+        q.G = std::max(1, std::min(tiles, num_sms / q.S));
+    } else {
+        q.SC = 1;
+        q.G = std::max(1, std::min(tiles, num_sms));
+    }
+    const int rows_cta = (N + q.G - 1) / q.G;
+    q.tiles_cta = (rows_cta + kqm::TR - 1) / kqm::TR;
+    return q;
+}
 
 struct KqmPlan {
     kqm::Params p;
@@ -815,7 +841,7 @@ struct KqmPlan {
     size_t off_tab = 0, off_rsq = 0, off_part = 0, off_cnt = 0, ws_bytes = 0;
 };
 
-bool plan_kqm(int type, int M, int N, int K, int num_sms, int smem_optin, KqmPlan& P) {
+bool plan_kqm_at(int type, int M, int N, int K, int num_sms, int smem_optin, int table_kb, KqmPlan& P) {
     using namespace kqm;
     const int BB = type == Q4_K ? 144 : 210;
     Params& p = P.p;
@@ -830,19 +856,12 @@ bool plan_kqm(int type, int M, int N, int K, int num_sms, int smem_optin, KqmPla
     p.nb = K / 256;
     p.M = M;
     p.ldy = N;
-    const int kbs_max = std::max<int>(1, static_cast<int>(static_cast<size_t>(g_table_kb.load()) * 1024 / rec));
-    const int S0 = (p.nb + kbs_max - 1) / kbs_max;
-    p.kbs = (p.nb + S0 - 1) / S0;
-    p.S = (p.nb + p.kbs - 1) / p.kbs;  // no empty split
-    const int tiles = (N + TR - 1) / TR;
-    const size_t part_bytes = static_cast<size_t>(p.S) * MB * N * sizeof(float);
-    if (p.S > 1 && part_bytes <= kSplitPartialLimit && num_sms / p.S >= 1) {
-        p.SC = p.S;
-        p.G = std::max(1, std::min(tiles, num_sms / p.S));
-    } else {
-        p.SC = 1;
-        p.G = std::max(1, std::min(tiles, num_sms));
-    }
+    const KqmSplit q = split_for(table_kb, rec, p.nb, N, MB, num_sms);
+    p.kbs = q.kbs;
+    p.S = q.S;
+    p.SC = q.SC;
+    p.G = q.G;
+    const size_t part_bytes = q.part_bytes;
     P.grid = p.G * p.SC;
     p.KC = std::min(p.kbs, 8);
     const int nch_max = (p.kbs + p.KC - 1) / p.KC;
@@ -856,14 +875,18 @@ bool plan_kqm(int type, int M, int N, int K, int num_sms, int smem_optin, KqmPla
     // ring holds at least one tile's stages per group: a wait then never
     // reaches a slot more than one lap ahead (an mbarrier parity wait cannot
     // tell that lap from the previous one).
+    // Automatically: at least two tiles per group (a group neither idles nor
+    // ends on a lone last tile), at least two warps per group, at most the
+    // split's super-blocks (B200: the 8-row LM head 128256 x 4096 Q6_K takes
+    // 150 us with groups of 4 warps, 176 us with 8).
     int gw = 1;
-    while (gw * 2 <= std::min(P.NCW, p.kbs)) gw *= 2;
+    while (gw < P.NCW && gw * q.tiles_cta < 2 * P.NCW) gw *= 2;
+    gw = std::max(gw, 2);
+    while (gw > 1 && gw > p.kbs) gw /= 2;
     if (g_group.load() > 0) gw = std::min(g_group.load(), P.NCW);
     while ((gw > 1 && P.NCW / gw > 8) || P.NCW % gw != 0) gw *= 2;
     const uint32_t budget = static_cast<uint32_t>(smem_optin) - 1024u;
-    const int rows_cta = (N + p.G - 1) / p.G;
-    const int tiles_cta = (rows_cta + TR - 1) / TR;
-    const int need = tiles_cta * nch_max * (p.SC == 1 ? p.S : 1);
+    const int need = q.tiles_cta * nch_max * (p.SC == 1 ? p.S : 1);
     uint32_t off = 0;
     for (;; gw *= 2) {
         off = static_cast<uint32_t>(2 * MAX_STAGES * 8 + 16);
@@ -898,6 +921,22 @@ bool plan_kqm(int type, int M, int N, int K, int num_sms, int smem_optin, KqmPla
     ws = align_up(ws + static_cast<size_t>(p.G) * sizeof(unsigned), 256);
     P.ws_bytes = ws;
     return true;
+}
+
+// Table size: the tuned value, else 72 KB (8 super-blocks per split for up
+// to 8 rows, 4 for 16), or 144 KB for 9..16 rows where each CTA still gets 8
+// tiles or more (8 super-blocks per split: half the splits and per-tile sums;
+// on B200 gate+up 28672 x 4096 at 16 rows 57.8 -> 48.2 us; slower on small
+// matrices, whose CTAs then hold few tiles).
+bool plan_kqm(int type, int M, int N, int K, int num_sms, int smem_optin, KqmPlan& P) {
+    if (g_table_kb.load() > 0) return plan_kqm_at(type, M, N, K, num_sms, smem_optin, g_table_kb.load(), P);
+    if (ncb_for(M) == 2 && K > 0 && K % 256 == 0 && N > 0) {
+        const size_t rec = static_cast<size_t>(kqm::REC_UNIT) * 2;
+        if (split_for(144, rec, K / 256, N, 16, num_sms).tiles_cta >= 8 &&
+            plan_kqm_at(type, M, N, K, num_sms, smem_optin, 144, P))
+            return true;
+    }
+    return plan_kqm_at(type, M, N, K, num_sms, smem_optin, 72, P);
 }
 
 bool kqm_shape_ok(int type, const void* W, int M, int N, int K, int max_m) {

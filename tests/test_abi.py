@@ -132,6 +132,17 @@ def test_options():
     with pytest.raises(swq.SwqError) as ei:
         swq.set_option(swq.OPT_GEMV_MAX_M, 9)
     assert ei.value.status is Status.BAD_ARG
+    # batched K-quant GEMV: up to 16 rows; table size and tile groups automatic
+    assert swq.get_option(swq.OPT_GEMV_BATCH_MAX_M) == 16
+    assert swq.get_option(swq.OPT_GEMV_BATCH_TABLE_KB) == 0
+    assert swq.get_option(swq.OPT_GEMV_BATCH_GROUP) == 0
+    swq.set_option(swq.OPT_GEMV_BATCH_TABLE_KB, 144)
+    assert swq.get_option(swq.OPT_GEMV_BATCH_TABLE_KB) == 144
+    swq.set_option(swq.OPT_GEMV_BATCH_TABLE_KB, 0)
+    for opt, bad in ((swq.OPT_GEMV_BATCH_TABLE_KB, 7), (swq.OPT_GEMV_BATCH_TABLE_KB, 161),
+                     (swq.OPT_GEMV_BATCH_GROUP, 3), (swq.OPT_GEMV_BATCH_GROUP, 32)):
+        with pytest.raises(swq.SwqError):
+            swq.set_option(opt, bad)
     with pytest.raises(swq.SwqError):
         swq.set_option(99, 0)
     assert swq.get_option(99) == -1

@@ -78,10 +78,12 @@ def test_kqm_shapes(cuda, oracle_mod, fmt, M, N, K):
 
 
 @pytest.mark.parametrize("fmt,M,N,K", [("Q4_K", 32, 20000, 4096), ("Q6_K", 16, 40000, 4096),
-                                       ("Q4_K", 16, 2048, 28672), ("Q6_K", 4, 1000, 16384)])
+                                       ("Q4_K", 16, 2048, 28672), ("Q6_K", 4, 1000, 16384),
+                                       ("Q4_K", 12, 9000, 4096)])
 def test_kqm_large(cuda, oracle_mod, fmt, M, N, K):
     """Partials too large for L2 (one CTA runs every split of its rows, adding
-    into Y in split order), and long rows split over many CTAs."""
+    into Y in split order), and long rows split over many CTAs; at 9..16 rows
+    the automatic plan takes the 144 KB table on all but the first shape."""
     t = synth.IDS[fmt]
     blocks = synth.random_blocks(t, N, K, seed=N + K)
     X = synth.random_activations(M, K, seed=M * 7)
@@ -91,7 +93,7 @@ def test_kqm_large(cuda, oracle_mod, fmt, M, N, K):
 
 
 @pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K"])
-@pytest.mark.parametrize("table_kb,group", [(72, 1), (36, 0), (36, 2), (18, 1), (144, 4), (9, 0)])
+@pytest.mark.parametrize("table_kb,group", [(0, 0), (72, 1), (36, 0), (36, 2), (18, 1), (144, 4), (9, 0)])
 @pytest.mark.parametrize("M,N,K", [(8, 3000, 4096), (16, 1000, 14336), (32, 700, 8192), (2, 24000, 2048)])
 def test_kqm_tuning_plans(cuda, oracle_mod, fmt, table_kb, group, M, N, K):
     """Every table size and tile group gives the oracle's rows, also where a
