@@ -1,7 +1,7 @@
 /*
  * swq_oracle.c -- CPU restatement of swllm.cpp's quantized-weight path.
  *
- * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA library
+ * TEST INFRASTRUCTURE ONLY.  This file is the oracle for the CUDA library
  * (libswq): only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
  * reference arm may load it.  The product path never calls it and there is no
  * CPU fallback built on it.
