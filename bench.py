@@ -495,9 +495,8 @@ def run_swq(args, rank: int, world: int) -> None:
     # site would make them: raw host pointers held by the caller, one call per
     # GEMV (the Python mirror's per-call argument checks and pointer lookups,
     # about 3 us of a 36 us call on a B200 host, are not part of the drop-in).
-    # The warm-up runs through the
-    # mirror on the same arrays, so the weights are resident under the same
-    # host addresses.
+    # The warm-up runs through the mirror on the same arrays, so the weights
+    # are resident under the same host addresses.
     from swq.lib import _raise, lib as swq_lib
     e2e_steps = max(1, min(args.steps, 200))
     comp = swq.Compute(device=local)
