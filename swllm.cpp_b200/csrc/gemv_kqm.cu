@@ -22,8 +22,9 @@
 //           exceed fp16's exact integers)
 // Every product is exact; the MMA sums 16 products at a time in fp32.  Error
 // sources: the 22-bit split of x relative to the super-block's largest
-// element, the MMA's and the epilogue's fp32 sums -- the reference rounds
-// every product and addition instead.
+// element (fewer bits for blocks below 2^-117, see prep_kernel), the MMA's
+// and the epilogue's fp32 sums -- the reference rounds every product and
+// addition instead.
 //
 // Two launches:
 //   prep_kernel   X -> the B-fragment table: per super-block and k-step of 16
@@ -304,8 +305,11 @@ __global__ void __launch_bounds__(256) prep_kernel(const PrepParams p) {
     nonfinite = __any_sync(0xffffffffu, nonfinite);
     // E: mx < 2^E; the scaled values stay below 2^14 (fp16 max 65504), the
     // scaled sums of 32 times 2^-5 too.  E >= -100 keeps the scale factors
-    // normal floats (a super-block whose largest element is below 2^-101
-    // keeps fewer bits, far under fp32's resolution of any sum it joins).
+    // normal floats: a super-block whose largest element is below 2^-117
+    // keeps fewer than 22 bits (its low part turns fp16-subnormal).  Beside
+    // blocks of normal magnitude that is far under fp32's resolution of the
+    // row's sums; a row made only of such blocks loses relative accuracy
+    // (about 1e-4 at fp32's smallest normals, 1e-2 for subnormal rows).
     const int E = max(((__float_as_int(mx) >> 23) & 0xFF) - 126, -100);
     const float up_s = nonfinite ? 0.f : __int_as_float((127 + 14 - E) << 23);
     float u[8];
