@@ -1,6 +1,7 @@
-"""The arithmetic of the batched K-quant GEMV (gemv_kqm.cu), restated in numpy
-on the CPU, against the oracle restatement of cpu_matmul_transposed_q4_k /
-_q6_k (src/tensor.h:769-856).
+"""The arithmetic of the Q4_K / Q6_K GEMV kernels, restated in numpy on the
+CPU, against the oracle restatement of cpu_matmul_transposed_q4_k / _q6_k
+(src/tensor.h:769-856): the batched K-quant GEMV (gemv_kqm.cu, 2..32 rows)
+first, the single-row integer GEMV (gemv_kq.cu) at the end.
 
 The kernel holds each activation row per 256-element super-block as
 x 2^(14 - E) = h + l, two fp16 numbers (E: the block's largest binary
@@ -234,3 +235,82 @@ def test_rows_below_the_block_floor(oracle_mod, fmt):
         err = rel_l2(emulate(t, blocks, X, N, K)[0], exact[0])
         assert err <= bound, (scale, err)
         assert rel_l2(ref[0], exact[0]) <= 1e-5
+
+
+# ---------------------------------------------------------------------------
+# Single-row integer GEMV (gemv_kq.cu): per 256-element super-block,
+# Z = round(x 2^(30 - E)) (E: the block's largest binary exponent, E >= -96)
+# split into int8 limbs; the sub-block sums S_j = sum q_k Z_k are exact
+# integers, scaled by 2^(E - 30) once per super-block; the sums X_j of x for
+# the Q4_K mins and the Q6_K offset are fp32 sums in the kernel's tree.  The
+# emulation keeps the integers exact and sums the rest in float64.
+
+def kq_split_row(x: np.ndarray, nb: int, t: int):
+    x = np.asarray(x, F32).reshape(nb, 256)
+    mx = np.abs(x).max(axis=1).astype(F32)
+    E = np.maximum(((mx.view(np.int32) >> 23) & 0xFF) - 126, -96)
+    Z = np.rint((x * np.ldexp(F32(1), 30 - E).astype(F32)[:, None]).astype(F32).astype(F64)).astype(np.int64)
+    if t == Q4_K:  # sub-blocks of 32: four lanes of 8, (l0 + l1) + (l2 + l3)
+        v = x.reshape(nb, 8, 4, 8)
+        lane = ((v[..., 0] + v[..., 1]) + (v[..., 2] + v[..., 3])) + ((v[..., 4] + v[..., 5]) + (v[..., 6] + v[..., 7]))
+        Xj = ((lane[..., 0] + lane[..., 1]) + (lane[..., 2] + lane[..., 3])).astype(F32)
+    else:  # sub-blocks of 16: two lanes of 8
+        v = x.reshape(nb, 16, 2, 8)
+        lane = ((v[..., 0] + v[..., 1]) + (v[..., 2] + v[..., 3])) + ((v[..., 4] + v[..., 5]) + (v[..., 6] + v[..., 7]))
+        Xj = (lane[..., 0] + lane[..., 1]).astype(F32)
+    return Z, Xj, np.ldexp(1.0, E - 30)
+
+
+def emulate_kq(t, blocks, x, N, K) -> np.ndarray:
+    """y[N] of the single-row kernel's representation (exact integer sums)."""
+    nb = K // 256
+    Z, Xj, xe = kq_split_row(x, nb, t)
+    if t == Q4_K:
+        d, dmin, sc, mn, q = q4k_parts(blocks, N, K)
+        S = (q.astype(np.int64) * Z[None]).reshape(N, nb, 8, 32).sum(axis=3)
+        I = (sc.astype(np.int64) * S).sum(axis=2)
+        mins = (mn * Xj[None].astype(F64)).sum(axis=2)
+        return (d.astype(F64) * I.astype(F64) * xe[None] - dmin.astype(F64) * mins).sum(axis=1)
+    d, sc, qm = q6k_parts(blocks, N, K)
+    S = ((qm + 32).astype(np.int64) * Z[None]).reshape(N, nb, 16, 16).sum(axis=3)
+    I = (sc.astype(np.int64) * S).sum(axis=2)
+    off = 32.0 * (sc * Xj[None].astype(F64)).sum(axis=2)
+    return (d.astype(F64) * (I.astype(F64) * xe[None] - off)).sum(axis=1)
+
+
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K"])
+@pytest.mark.parametrize("N,K", [(256, 4096), (128, 14336)])
+def test_single_row_representation(oracle_mod, fmt, N, K):
+    """30-bit fixed point per super-block with exact integer sums: about 1e-8
+    (Q4_K) to 1e-7 (Q6_K) from the exact sum of the reference's fp32 weights,
+    an order of magnitude under the reference's own fp32 loop."""
+    t = synth.IDS[fmt]
+    blocks = synth.random_blocks(t, N, K, seed=N + 2 * K)
+    x = synth.random_activations(1, K, seed=K + 1)[0]
+    exact = dequant_f32(t, blocks, N, K).astype(F64) @ x.astype(F64)
+    ref = np.asarray(oracle_mod.gemv(t, blocks, x, N, K))
+    emu = emulate_kq(t, blocks, x, N, K)
+    assert rel_l2(emu, exact) <= REPR_TOL
+    assert rel_l2(emu, ref) <= GPU_TOL
+
+
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K"])
+def test_single_row_below_the_block_floor(oracle_mod, fmt):
+    """E >= -96 keeps the single-row kernel's scale factors normal fp32
+    numbers, so a super-block whose largest element is below 2^-97 (about
+    6e-30) keeps fewer than 30 bits.  Beside blocks of normal magnitude that is
+    far under the row's fp32 resolution; a whole row that small loses accuracy:
+    nothing at 1e-29, about 1e-6 at 1e-32, about 1e-3 at 1e-35, and most of
+    the value at fp32's smallest normals (1e-38), where the reference's own
+    fp32 loop stays near 1e-6.  Activations of a model never sit there."""
+    t = synth.IDS[fmt]
+    N, K = 128, 4096
+    blocks = synth.random_blocks(t, N, K, seed=3)
+    W = dequant_f32(t, blocks, N, K).astype(F64)
+    base = synth.random_activations(1, K, seed=4)[0].astype(F32)
+    for scale, lo, hi in ((1e-29, 0.0, REPR_TOL), (1e-32, 0.0, 3e-6), (1e-35, 1e-4, 3e-3), (1e-38, 0.1, 1.0)):
+        x = (base * F32(scale)).astype(F32)
+        exact = W @ x.astype(F64)
+        err = rel_l2(emulate_kq(t, blocks, x, N, K), exact)
+        assert lo <= err <= hi, (scale, err)
+        assert rel_l2(np.asarray(oracle_mod.gemv(t, blocks, x, N, K)), exact) <= 1e-5
