@@ -420,7 +420,8 @@ enum {
     /* Causal attention of swq_attention_prefill for head_dim 64 and 128:
      * 3 (default) on the tensor cores, q, k, v and the softmax weights as
      * pairs of fp16 numbers (22 bits relative to each q / k row's largest
-     * element; exact products, fp32 sums), the context's K/V converted once
+     * element; v unscaled, so values far below 1 keep fewer bits: about
+     * 1.7e-8 / |v| relative; exact products, fp32 sums), the context's K/V converted once
      * per call into scratch from libswq's stream-ordered pool; 2 the same
      * arithmetic converting each K/V tile in every query tile (no scratch);
      * 1 the fp32 tiled CUDA-core form; 0 one warp per row and head (the form
