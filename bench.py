@@ -1268,6 +1268,9 @@ def main() -> None:
                     help="skip the Llama-3-8B decode tok/s measurement of the default run")
     ap.add_argument("--gguf", default=None, help="--workload decode: decode this GGUF model file instead of "
                                                   "the synthetic Llama-3-8B-shaped one")
+    ap.add_argument("--prefill-attention", type=int, choices=[0, 1, 2, 3], default=None,
+                    help="--workload prefill|prefill70b: SWQ_OPT_PREFILL_ATTENTION for the run (default: the "
+                         "library's, 3)")
     ap.add_argument("--decode-context", choices=["synthetic", "prefill"], default="prefill",
                     help="decode measurements: context as random K/V (synthetic) or a batched prefill of "
                          "random prompt tokens (prefill, also timed)")
@@ -1312,6 +1315,9 @@ def main() -> None:
             log("prefill runs on one GPU; other ranks exit")
         if rank != 0:
             return
+        if args.prefill_attention is not None:
+            import swq
+            swq.set_option(swq.OPT_PREFILL_ATTENTION, args.prefill_attention)
         d = run_prefill(rank, prompt=args.M, seventy=args.workload == "prefill70b")
         emit({"metric": f"prefill tok/s ({d['model']}, {args.M}-token prompt)", "value": d["tok_s"],
               "unit": "tok/s", "n_gpus": 1, "higher_is_better": True, "data": "synthetic",
